@@ -1,0 +1,343 @@
+// attention.cuh — variable-length multi-head self-attention over packed
+// sequences (cu_seqlens), restating native/model.go:646-739 (attendHead,
+// rotateHalf, softmaxScaled) for every head and sequence at once.
+//
+// The reference materialises a seq×padSeq(seq) score matrix per head; here
+// scores never leave the SM. Queries, keys and values are read straight from
+// the fused [T, 3h] qkv buffer (q columns head·hd, k columns h + head·hd,
+// v columns 2h + head·hd, model.go:660-662). NeoX rotary embedding
+// (model.go:674-685) is applied to q and k while they are staged, from the
+// f32 cos/sin tables built like precomputeRoPE (model.go:306-318).
+//
+// Two kernels:
+//   attn_flash_kernel  64 query rows × one head per CTA, 64-key tiles,
+//                      bf16 m16n8k16 tensor-core MMAs with f32 accumulation
+//                      and online softmax (head_dim 32 or 64).
+//   attn_rowq_kernel   one warp per (query, head): lanes split the keys,
+//                      f32 math, warp merge. Serves CLS-pooled last layers
+//                      (one query per sequence, model.go:403-410) and any
+//                      head_dim the flash kernel does not cover.
+#pragma once
+
+#include "common.cuh"
+
+namespace futon {
+
+struct AttnTile {
+  int seq;  // sequence index within the micro-batch
+  int q0;   // first query position of the tile
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
+                                          const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+
+// Stages rows [r0, r0+64) of one head's q or k (with RoPE) or v into shared
+// memory as bf16, zero-filling rows at or past L. src points at row 0 of the
+// sequence for this head's columns; ld is the qkv row stride.
+template <int HD, bool ROPE>
+__device__ __forceinline__ void stage_rows(__nv_bfloat16* dst, int lds, const __nv_bfloat16* src,
+                                           int ld, int r0, int L, const float* rcos,
+                                           const float* rsin) {
+  constexpr int kRows = 64;
+  if constexpr (ROPE) {
+    constexpr int kHalf = HD / 2;
+    constexpr int kChunks = kHalf / 8;  // 8 rotation pairs per work item
+    for (int w = threadIdx.x; w < kRows * kChunks; w += blockDim.x) {
+      const int r = w / kChunks, c = (w % kChunks) * 8;
+      const int pos = r0 + r;
+      uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+      if (pos < L) {
+        const __nv_bfloat16* p = src + (size_t)pos * ld;
+        uint4 x1 = *reinterpret_cast<const uint4*>(p + c);
+        uint4 x2 = *reinterpret_cast<const uint4*>(p + c + kHalf);
+        const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(&x1);
+        const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&x2);
+        const float* cr = rcos + (size_t)pos * kHalf + c;
+        const float* sr = rsin + (size_t)pos * kHalf + c;
+        float y1[8], y2[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float v1 = __bfloat162float(a[i]), v2 = __bfloat162float(b[i]);
+          float cc = cr[i], ss = sr[i];
+          y1[i] = v1 * cc - v2 * ss;
+          y2[i] = v2 * cc + v1 * ss;
+        }
+        lo = make_uint4(pack_bf16(y1[0], y1[1]), pack_bf16(y1[2], y1[3]), pack_bf16(y1[4], y1[5]),
+                        pack_bf16(y1[6], y1[7]));
+        hi = make_uint4(pack_bf16(y2[0], y2[1]), pack_bf16(y2[2], y2[3]), pack_bf16(y2[4], y2[5]),
+                        pack_bf16(y2[6], y2[7]));
+      }
+      *reinterpret_cast<uint4*>(dst + r * lds + c) = lo;
+      *reinterpret_cast<uint4*>(dst + r * lds + c + kHalf) = hi;
+    }
+  } else {
+    constexpr int kChunks = HD / 8;
+    for (int w = threadIdx.x; w < kRows * kChunks; w += blockDim.x) {
+      const int r = w / kChunks, c = (w % kChunks) * 8;
+      const int pos = r0 + r;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (pos < L) v = *reinterpret_cast<const uint4*>(src + (size_t)pos * ld + c);
+      *reinterpret_cast<uint4*>(dst + r * lds + c) = v;
+    }
+  }
+}
+
+template <typename T> __device__ __forceinline__ void store2(T* dst, float a, float b);
+template <> __device__ __forceinline__ void store2<float>(float* dst, float a, float b) {
+  *reinterpret_cast<float2*>(dst) = make_float2(a, b);
+}
+template <> __device__ __forceinline__ void store2<__nv_bfloat16>(__nv_bfloat16* dst, float a,
+                                                                  float b) {
+  *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(a, b);
+}
+
+// grid = (num_tiles, num_heads), block = 128 (4 warps × 16 query rows).
+template <int HD, bool ROPE, typename OutT>
+__global__ void __launch_bounds__(128)
+    attn_flash_kernel(const __nv_bfloat16* __restrict__ qkv, int hidden,
+                      const int* __restrict__ cu_seqlens, const AttnTile* __restrict__ tiles,
+                      const float* __restrict__ rcos, const float* __restrict__ rsin,
+                      float scale_log2, OutT* __restrict__ out, int ldo) {
+  constexpr int kBQ = 64, kBK = 64, kLds = HD + 8;
+  __shared__ __align__(16) __nv_bfloat16 sQ[kBQ * kLds];
+  __shared__ __align__(16) __nv_bfloat16 sK[kBK * kLds];
+  __shared__ __align__(16) __nv_bfloat16 sV[kBK * kLds];
+
+  const AttnTile tile = tiles[blockIdx.x];
+  const int head = blockIdx.y;
+  const int s0 = cu_seqlens[tile.seq];
+  const int L = cu_seqlens[tile.seq + 1] - s0;
+  const int ld = 3 * hidden;
+  const __nv_bfloat16* qg = qkv + (size_t)s0 * ld + head * HD;
+  const __nv_bfloat16* kg = qg + hidden;
+  const __nv_bfloat16* vg = qg + 2 * hidden;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  stage_rows<HD, ROPE>(sQ, kLds, qg, ld, tile.q0, L, rcos, rsin);
+  __syncthreads();
+
+  uint32_t qf[HD / 16][4];
+#pragma unroll
+  for (int kc = 0; kc < HD / 16; ++kc)
+    ldsm_x4(qf[kc], smem_u32(&sQ[(warp * 16 + (lane & 15)) * kLds + kc * 16 + (lane >> 4) * 8]));
+
+  float o[HD / 8][4];
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+
+  for (int kv0 = 0; kv0 < L; kv0 += kBK) {
+    __syncthreads();
+    stage_rows<HD, ROPE>(sK, kLds, kg, ld, kv0, L, rcos, rsin);
+    stage_rows<HD, false>(sV, kLds, vg, ld, kv0, L, nullptr, nullptr);
+    __syncthreads();
+
+    float s[kBK / 8][4];
+#pragma unroll
+    for (int nb = 0; nb < kBK / 8; ++nb) {
+      s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+#pragma unroll
+      for (int kc = 0; kc < HD / 16; ++kc) {
+        uint32_t kf[2];
+        ldsm_x2(kf, smem_u32(&sK[(nb * 8 + (lane & 7)) * kLds + kc * 16 + ((lane >> 3) & 1) * 8]));
+        mma_16816(s[nb], qf[kc], kf);
+      }
+    }
+    // Scale into the log2 domain and mask keys past the sequence end.
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < kBK / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = kv0 + nb * 8 + (lane & 3) * 2 + (e & 1);
+        float v = (key < L) ? s[nb][e] * scale_log2 : -INFINITY;
+        s[nb][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    }
+    float alpha[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const float m_new = fmaxf(m_run[r], mx[r]);
+      alpha[r] = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - m_new);
+      m_run[r] = m_new;
+      l_run[r] *= alpha[r];
+    }
+#pragma unroll
+    for (int nb = 0; nb < kBK / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p = exp2f(s[nb][e] - m_run[e >> 1]);
+        s[nb][e] = p;
+        l_run[e >> 1] += p;
+      }
+    }
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; ++nd) {
+      o[nd][0] *= alpha[0];
+      o[nd][1] *= alpha[0];
+      o[nd][2] *= alpha[1];
+      o[nd][3] *= alpha[1];
+    }
+#pragma unroll
+    for (int kc = 0; kc < kBK / 16; ++kc) {
+      uint32_t pf[4];
+      pf[0] = pack_bf16(s[2 * kc][0], s[2 * kc][1]);
+      pf[1] = pack_bf16(s[2 * kc][2], s[2 * kc][3]);
+      pf[2] = pack_bf16(s[2 * kc + 1][0], s[2 * kc + 1][1]);
+      pf[3] = pack_bf16(s[2 * kc + 1][2], s[2 * kc + 1][3]);
+#pragma unroll
+      for (int nd = 0; nd < HD / 8; ++nd) {
+        uint32_t vf[2];
+        ldsm_x2_t(vf, smem_u32(&sV[(kc * 16 + (lane & 15)) * kLds + nd * 8]));
+        mma_16816(o[nd], pf, vf);
+      }
+    }
+  }
+
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+  }
+  const float inv0 = 1.f / l_run[0], inv1 = 1.f / l_run[1];
+  const int qr0 = tile.q0 + warp * 16 + (lane >> 2);
+  const int qr1 = qr0 + 8;
+#pragma unroll
+  for (int nd = 0; nd < HD / 8; ++nd) {
+    const int col = head * HD + nd * 8 + (lane & 3) * 2;
+    if (qr0 < L) store2<OutT>(out + (size_t)(s0 + qr0) * ldo + col, o[nd][0] * inv0, o[nd][1] * inv0);
+    if (qr1 < L) store2<OutT>(out + (size_t)(s0 + qr1) * ldo + col, o[nd][2] * inv1, o[nd][3] * inv1);
+  }
+}
+
+// Index of the sequence holding packed row `row` (cu is non-decreasing).
+__device__ __forceinline__ int find_seq(const int* cu, int nseq, int row) {
+  int lo = 0, hi = nseq;  // invariant: cu[lo] <= row < cu[hi]
+  while (hi - lo > 1) {
+    int mid = (lo + hi) >> 1;
+    if (cu[mid] <= row) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// One warp per (query, head). cls_mode = 0: query i is packed row i (all
+// tokens); output row i. cls_mode = 1: query i is the first token of
+// sequence i; output row i of a compact [nseq, ldo] buffer.
+template <int HD, typename OutT>
+__global__ void __launch_bounds__(256)
+    attn_rowq_kernel(const __nv_bfloat16* __restrict__ qkv, int hidden, int num_heads,
+                     const int* __restrict__ cu_seqlens, int nseq, int nq, int cls_mode,
+                     const float* __restrict__ rcos, const float* __restrict__ rsin, int rope,
+                     float scale_log2, OutT* __restrict__ out, int ldo) {
+  const int gw = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  const int qi = gw / num_heads, head = gw % num_heads;
+  if (qi >= nq) return;
+  int seq, qrow;
+  if (cls_mode) {
+    seq = qi;
+    qrow = cu_seqlens[qi];
+  } else {
+    qrow = qi;
+    seq = find_seq(cu_seqlens, nseq, qi);
+  }
+  const int s0 = cu_seqlens[seq];
+  const int L = cu_seqlens[seq + 1] - s0;
+  const int qpos = qrow - s0;
+  const int ld = 3 * hidden;
+  constexpr int kHalf = HD / 2;
+
+  float q[HD];
+  {
+    const __nv_bfloat16* p = qkv + (size_t)qrow * ld + head * HD;
+#pragma unroll
+    for (int d = 0; d < HD; ++d) q[d] = __bfloat162float(p[d]);
+    if (rope) {
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) {
+        float c = rcos[(size_t)qpos * kHalf + i], s = rsin[(size_t)qpos * kHalf + i];
+        float x1 = q[i], x2 = q[i + kHalf];
+        q[i] = x1 * c - x2 * s;
+        q[i + kHalf] = x2 * c + x1 * s;
+      }
+    }
+  }
+  float m = -INFINITY, l = 0.f;
+  float o[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) o[d] = 0.f;
+  for (int j = lane; j < L; j += 32) {
+    const __nv_bfloat16* kp = qkv + (size_t)(s0 + j) * ld + hidden + head * HD;
+    const __nv_bfloat16* vp = kp + hidden;
+    float k[HD];
+#pragma unroll
+    for (int d = 0; d < HD; ++d) k[d] = __bfloat162float(kp[d]);
+    if (rope) {
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) {
+        float c = rcos[(size_t)j * kHalf + i], s = rsin[(size_t)j * kHalf + i];
+        float x1 = k[i], x2 = k[i + kHalf];
+        k[i] = x1 * c - x2 * s;
+        k[i + kHalf] = x2 * c + x1 * s;
+      }
+    }
+    float sc = 0.f;
+#pragma unroll
+    for (int d = 0; d < HD; ++d) sc += q[d] * k[d];
+    sc *= scale_log2;
+    const float m_new = fmaxf(m, sc);
+    const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
+    const float p = exp2f(sc - m_new);
+    l = l * alpha + p;
+#pragma unroll
+    for (int d = 0; d < HD; ++d) o[d] = o[d] * alpha + p * __bfloat162float(vp[d]);
+    m = m_new;
+  }
+  const float mw = warp_max(m);
+  const float a = (m == -INFINITY) ? 0.f : exp2f(m - mw);
+  const float lw = warp_sum(l * a);
+  const float inv = 1.f / lw;
+  OutT* dst = out + (size_t)(cls_mode ? qi : qrow) * ldo + head * HD;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    const float v = warp_sum(o[d] * a);
+    if (lane == (d & 31)) {
+      if constexpr (sizeof(OutT) == 4) dst[d] = v * inv;
+      else dst[d] = __float2bfloat16_rn(v * inv);
+    }
+  }
+}
+
+}  // namespace futon

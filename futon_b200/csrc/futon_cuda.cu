@@ -1,0 +1,1141 @@
+// futon_cuda.cu — libfuton_cuda: model upload, forward orchestration and the
+// C ABI declared in include/futon_cuda.h.
+//
+// Data layout in HBM, per device (one full replica per GPU):
+//   embeddings: word [vocab, h] f32, position [max_seq, h] f32 (absolute
+//     packs), token-type row 0 [h] f32, embedding LayerNorm γ/β f32;
+//   per layer: qkv W [3h, h], out W [h, h], fc1 W [inter, h] (or fc1‖gate
+//     interleaved [2·inter, h] for SwiGLU), fc2 W [h, inter] — bf16, K-major
+//     (the pack's nn.Linear layout), or int8 + per-row f32 scales on the Q8
+//     path; biases and LayerNorm parameters f32;
+//   rotary cos/sin tables [max_trained, hd/2] f32 (RoPE packs).
+// Activations of one micro-batch of T packed tokens: x [T, h] f32 (residual
+// stream), xb [T, h] bf16 (GEMM operand), qkv [T, 3h] bf16, attn [T, h],
+// ffn [T, inter], tmp [T, h] f32 (pre-LayerNorm sums), int8 copies on Q8.
+//
+// One forward = embed+LN, then per layer: qkv GEMM, attention, out GEMM with
+// residual, LN, fc1 GEMM with GELU or SwiGLU, fc2 GEMM with residual, LN;
+// then one pooling kernel. The last layer of a CLS-pooled pack runs its
+// query-side work on the CLS rows only (native/model.go:403-410).
+#include "../../include/futon_cuda.h"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm_launch.cuh"
+#include "rowops.cuh"
+
+using namespace futon;
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+int set_err(char* err, size_t errlen, int code, const char* fmt, ...) {
+  if (err && errlen) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, errlen, fmt, ap);
+    va_end(ap);
+  }
+  return code;
+}
+
+#define CU_TRY(call)                                                                     \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return set_err(err, errlen, e_ == cudaErrorMemoryAllocation ? FUTON_ENOMEM : FUTON_ECUDA, \
+                     "native: cuda %s (%s:%d)", cudaGetErrorString(e_), __FILE__, __LINE__); \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// Tensor maps (TMA descriptors)
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major [rows, cols] operand (bf16 or int8) read in 128-byte-wide,
+// box_rows-high swizzled tiles. Rows and columns past the extent read as 0.
+bool make_operand_map(CUtensorMap* map, const void* base, bool s8, uint64_t rows, uint64_t cols,
+                      uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const uint32_t esz = s8 ? 1 : 2;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * esz};
+  cuuint32_t box[2] = {128u / esz, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, s8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// N tile for a GEMM with N output columns: the widest of 256/192/128 that
+// divides N, else 64 (partial last tile, masked in the epilogue).
+int pick_bn(int n) {
+  if (n % 256 == 0) return 256;
+  if (n % 192 == 0) return 192;
+  if (n % 128 == 0) return 128;
+  return 64;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ---------------------------------------------------------------------------
+// Model state
+// ---------------------------------------------------------------------------
+struct GemmWeight {
+  void* w = nullptr;        // bf16 [n, k] or int8 [n, k]
+  float* scale = nullptr;   // int8 only: [n]
+  float* bias = nullptr;    // [n] or null
+  int n = 0, k = 0, bn = 64;
+  CUtensorMap map;
+};
+
+struct LayerDev {
+  GemmWeight qkv, out, fc1, fc2;  // fc1 is fc1‖gate interleaved for SwiGLU
+  float *n1w, *n1b, *n2w, *n2b;
+};
+
+struct Workspace {
+  size_t tokens = 0;  // capacity
+  void* base = nullptr;
+  float* x;
+  bf16* xb;
+  bf16* qkv;
+  void* attn;        // bf16 (float path) or f32 (q8 path)
+  void* ffn;         // bf16 or f32
+  float* tmp;
+  float* xc;         // CLS rows of the residual stream
+  int8_t *xq, *attnq, *ffnq;
+  float *xs, *attns, *ffns;
+};
+
+struct DevCtx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  std::vector<void*> allocs;
+  float *word = nullptr, *pos = nullptr, *type0 = nullptr, *embw = nullptr, *embb = nullptr;
+  float *rcos = nullptr, *rsin = nullptr;
+  std::vector<LayerDev> layers;
+  int* err_word = nullptr;
+  Workspace ws;
+  // call-scoped buffers
+  int* d_ids = nullptr;
+  size_t d_ids_cap = 0;
+  int* d_meta = nullptr;
+  size_t d_meta_cap = 0;
+  float* d_out = nullptr;
+  size_t d_out_cap = 0;
+  int* h_meta = nullptr;  // pinned
+  size_t h_meta_cap = 0;
+  int* h_ids = nullptr;   // pinned
+  size_t h_ids_cap = 0;
+  float* h_out = nullptr; // pinned
+  size_t h_out_cap = 0;
+  cudaEvent_t meta_evt = nullptr;
+  std::atomic<long long> launches{0};
+
+  ~DevCtx() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    for (void* p : allocs) cudaFree(p);
+    if (ws.base) cudaFree(ws.base);
+    if (d_ids) cudaFree(d_ids);
+    if (d_meta) cudaFree(d_meta);
+    if (d_out) cudaFree(d_out);
+    if (h_meta) cudaFreeHost(h_meta);
+    if (h_ids) cudaFreeHost(h_ids);
+    if (h_out) cudaFreeHost(h_out);
+    if (meta_evt) cudaEventDestroy(meta_evt);
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+}  // namespace
+
+struct futon_model {
+  futon_cfg cfg;
+  int q8 = 0;
+  int head_dim = 0;
+  int eff_max = 0;
+  int swiglu_half = 0;
+  std::vector<std::unique_ptr<DevCtx>> devs;
+};
+
+namespace {
+
+constexpr int kTokenBudget = 131072;  // tokens per micro-batch
+
+int effective_max(const futon_cfg& c) {
+  if (c.max_trained_positions > 0 && c.max_trained_positions < c.max_seq_len)
+    return c.max_trained_positions;
+  return c.max_seq_len;
+}
+
+// ---- tensor lookup -------------------------------------------------------
+struct HostTensor {
+  const futon_tensor* t = nullptr;
+  std::vector<float> f32;  // converted copy for F16 inputs
+  const float* data() const { return t->dtype == FUTON_DTYPE_F32 ? (const float*)t->data : f32.data(); }
+};
+
+float f16_to_f32(uint16_t h) {
+  // Exact binary16 → binary32 conversion.
+  uint32_t sign = (uint32_t)(h >> 15) << 31, exp = (h >> 10) & 0x1f, man = h & 0x3ff, bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {
+      int e = -1;
+      do { man <<= 1; ++e; } while (!(man & 0x400));
+      bits = sign | (uint32_t)(127 - 15 - e) << 23 | (man & 0x3ff) << 13;
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7f800000u | man << 13;
+  } else {
+    bits = sign | (exp + 127 - 15) << 23 | man << 13;
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+struct TensorSet {
+  std::map<std::string, HostTensor> byname;
+  std::map<std::string, bool> used;
+};
+
+int need(TensorSet& ts, const std::string& name, std::vector<int64_t> shape, bool optional,
+         const float** out, char* err, size_t errlen) {
+  *out = nullptr;
+  auto it = ts.byname.find(name);
+  if (it == ts.byname.end()) {
+    if (optional) return FUTON_OK;
+    return set_err(err, errlen, FUTON_EINVAL, "native: missing tensor %s", name.c_str());
+  }
+  const futon_tensor* t = it->second.t;
+  if (t->ndim != (int)shape.size())
+    return set_err(err, errlen, FUTON_EINVAL, "native: tensor %s rank %d, want %d", name.c_str(),
+                   t->ndim, (int)shape.size());
+  for (size_t i = 0; i < shape.size(); ++i)
+    if (t->shape[i] != shape[i])
+      return set_err(err, errlen, FUTON_EINVAL, "native: tensor %s dim %zu is %lld, want %lld",
+                     name.c_str(), i, (long long)t->shape[i], (long long)shape[i]);
+  ts.used[name] = true;
+  *out = it->second.data();
+  return FUTON_OK;
+}
+
+// ---- device uploads ------------------------------------------------------
+template <typename T>
+int dev_alloc(DevCtx& d, T** p, size_t count, char* err, size_t errlen) {
+  void* v = nullptr;
+  CU_TRY(cudaMalloc(&v, std::max<size_t>(count * sizeof(T), 16)));
+  d.allocs.push_back(v);
+  *p = static_cast<T*>(v);
+  return FUTON_OK;
+}
+
+int upload_f32(DevCtx& d, float** dst, const float* src, size_t count, char* err, size_t errlen) {
+  if (!src) { *dst = nullptr; return FUTON_OK; }
+  int rc = dev_alloc(d, dst, count, err, errlen);
+  if (rc) return rc;
+  CU_TRY(cudaMemcpy(*dst, src, count * sizeof(float), cudaMemcpyHostToDevice));
+  return FUTON_OK;
+}
+
+// Uploads a GEMM weight (optionally two interleaved halves for SwiGLU) as
+// bf16 or int8 + per-row scales, builds its bias and its TMA descriptor.
+int upload_gemm(DevCtx& d, GemmWeight& g, const float* w1, const float* b1, const float* w2,
+                const float* b2, int n1, int k, int half, bool q8, float* staging, char* err,
+                size_t errlen) {
+  const int n = w2 ? 2 * n1 : n1;
+  g.n = n;
+  g.k = k;
+  // Stage the f32 matrix on the device (interleaving fc1/gate blocks of `half` rows).
+  if (!w2) {
+    CU_TRY(cudaMemcpy(staging, w1, (size_t)n * k * sizeof(float), cudaMemcpyHostToDevice));
+  } else {
+    for (int j = 0; j * half < n1; ++j) {
+      CU_TRY(cudaMemcpy(staging + (size_t)(2 * j) * half * k, w1 + (size_t)j * half * k,
+                        (size_t)half * k * sizeof(float), cudaMemcpyHostToDevice));
+      CU_TRY(cudaMemcpy(staging + (size_t)(2 * j + 1) * half * k, w2 + (size_t)j * half * k,
+                        (size_t)half * k * sizeof(float), cudaMemcpyHostToDevice));
+    }
+  }
+  int rc;
+  if (q8) {
+    int8_t* q = nullptr;
+    if ((rc = dev_alloc(d, &q, (size_t)n * k, err, errlen))) return rc;
+    if ((rc = dev_alloc(d, &g.scale, (size_t)n, err, errlen))) return rc;
+    quant_rows_kernel<<<std::min(4096, (n + 7) / 8), 256, 0, d.stream>>>(staging, n, k, q, g.scale);
+    g.w = q;
+  } else {
+    bf16* w = nullptr;
+    if ((rc = dev_alloc(d, &w, (size_t)n * k, err, errlen))) return rc;
+    f32_to_bf16_kernel<<<1024, 256, 0, d.stream>>>(staging, (size_t)n * k, w);
+    g.w = w;
+  }
+  CU_TRY(cudaGetLastError());
+  CU_TRY(cudaStreamSynchronize(d.stream));
+  // Bias (interleaved like the weight for SwiGLU; an absent half is zero).
+  if (b1 || b2) {
+    std::vector<float> hb((size_t)n, 0.0f);
+    if (!w2) {
+      memcpy(hb.data(), b1, sizeof(float) * n);
+    } else {
+      for (int j = 0; j * half < n1; ++j)
+        for (int r = 0; r < half; ++r) {
+          if (b1) hb[(size_t)2 * j * half + r] = b1[(size_t)j * half + r];
+          if (b2) hb[(size_t)(2 * j + 1) * half + r] = b2[(size_t)j * half + r];
+        }
+    }
+    if ((rc = upload_f32(d, &g.bias, hb.data(), (size_t)n, err, errlen))) return rc;
+  }
+  g.bn = w2 ? 2 * half : pick_bn(n);
+  if (!make_operand_map(&g.map, g.w, q8, (uint64_t)n, (uint64_t)k, (uint32_t)g.bn))
+    return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed for a weight");
+  return FUTON_OK;
+}
+
+// ---- workspace -----------------------------------------------------------
+int ensure_workspace(const futon_model& m, DevCtx& d, size_t tokens, char* err, size_t errlen) {
+  if (d.ws.tokens >= tokens) return FUTON_OK;
+  if (d.ws.base) {
+    CU_TRY(cudaDeviceSynchronize());  // callers may have queued work on their own stream
+    cudaFree(d.ws.base);
+    d.ws.base = nullptr;
+    d.ws.tokens = 0;
+  }
+  const size_t T = tokens, h = m.cfg.hidden_size, I = m.cfg.intermediate_size;
+  const bool q8 = m.q8 != 0;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+  const size_t o_x = take(T * h * 4), o_xb = take(T * h * 2), o_qkv = take(T * 3 * h * 2);
+  const size_t o_attn = take(T * h * (q8 ? 4 : 2)), o_ffn = take(T * I * (q8 ? 4 : 2));
+  const size_t o_tmp = take(T * h * 4), o_xc = take(T * h * 4);
+  size_t o_xq = 0, o_aq = 0, o_fq = 0, o_xs = 0, o_as = 0, o_fs = 0;
+  if (q8) {
+    o_xq = take(T * h); o_aq = take(T * h); o_fq = take(T * I);
+    o_xs = take(T * 4); o_as = take(T * 4); o_fs = take(T * 4);
+  }
+  void* base = nullptr;
+  CU_TRY(cudaMalloc(&base, off));
+  uint8_t* b = static_cast<uint8_t*>(base);
+  Workspace& w = d.ws;
+  w.base = base;
+  w.tokens = tokens;
+  w.x = (float*)(b + o_x);
+  w.xb = (bf16*)(b + o_xb);
+  w.qkv = (bf16*)(b + o_qkv);
+  w.attn = b + o_attn;
+  w.ffn = b + o_ffn;
+  w.tmp = (float*)(b + o_tmp);
+  w.xc = (float*)(b + o_xc);
+  w.xq = q8 ? (int8_t*)(b + o_xq) : nullptr;
+  w.attnq = q8 ? (int8_t*)(b + o_aq) : nullptr;
+  w.ffnq = q8 ? (int8_t*)(b + o_fq) : nullptr;
+  w.xs = q8 ? (float*)(b + o_xs) : nullptr;
+  w.attns = q8 ? (float*)(b + o_as) : nullptr;
+  w.ffns = q8 ? (float*)(b + o_fs) : nullptr;
+  return FUTON_OK;
+}
+
+template <typename T>
+int ensure_dev(T** p, size_t* cap, size_t count, char* err, size_t errlen) {
+  if (*cap >= count) return FUTON_OK;
+  if (*p) {
+    CU_TRY(cudaDeviceSynchronize());
+    cudaFree(*p);
+  }
+  *p = nullptr;
+  *cap = 0;
+  size_t n = std::max<size_t>(count, 1024);
+  CU_TRY(cudaMalloc((void**)p, n * sizeof(T)));
+  *cap = n;
+  return FUTON_OK;
+}
+template <typename T>
+int ensure_host(T** p, size_t* cap, size_t count, char* err, size_t errlen) {
+  if (*cap >= count) return FUTON_OK;
+  if (*p) {
+    CU_TRY(cudaDeviceSynchronize());
+    cudaFreeHost(*p);
+  }
+  *p = nullptr;
+  *cap = 0;
+  size_t n = std::max<size_t>(count, 1024);
+  CU_TRY(cudaMallocHost((void**)p, n * sizeof(T)));
+  *cap = n;
+  return FUTON_OK;
+}
+
+// ---- GEMM helper ---------------------------------------------------------
+int run_gemm(DevCtx& d, const void* A, bool s8, const float* a_scale, int M, const GemmWeight& w,
+             int epi, bool out_f32, void* out, int ldo, const float* resid, int ldr,
+             cudaStream_t st, char* err, size_t errlen) {
+  if (M == 0) return FUTON_OK;
+  CUtensorMap ta;
+  if (!make_operand_map(&ta, A, s8, (uint64_t)M, (uint64_t)w.k, 128))
+    return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (activation)");
+  GemmLaunch g;
+  g.ta = &ta;
+  g.tw = &w.map;
+  g.M = M;
+  g.N = w.n;
+  g.K = w.k;
+  g.bn = w.bn;
+  g.epi = epi;
+  g.out_f32 = out_f32;
+  g.ep.out = out;
+  g.ep.ldo = ldo;
+  g.ep.bias = w.bias;
+  g.ep.resid = resid;
+  g.ep.ldr = ldr;
+  g.ep.a_scale = a_scale;
+  g.ep.w_scale = w.scale;
+  g.err = d.err_word;
+  g.num_sms = d.num_sms;
+  g.stream = st;
+  cudaError_t e = s8 ? launch_gemm_s8(g) : launch_gemm_bf16(g);
+  if (e != cudaSuccess)
+    return set_err(err, errlen, FUTON_ECUDA, "native: gemm launch: %s", cudaGetErrorString(e));
+  d.launches.fetch_add(1, std::memory_order_relaxed);
+  return FUTON_OK;
+}
+
+inline int grid_rows(int rows, int per_block, int sms) {
+  long g = (rows + per_block - 1) / per_block;
+  long cap = (long)sms * 16;
+  return (int)std::max<long>(1, std::min(g, cap));
+}
+
+// ---- attention dispatch --------------------------------------------------
+template <typename OutT>
+int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* cu,
+                  const AttnTile* tiles, int ntiles, bool cls_only, OutT* out,
+                  cudaStream_t st, char* err, size_t errlen) {
+  const int h = m.cfg.hidden_size, H = m.cfg.num_heads, hd = m.head_dim;
+  const bool rope = m.cfg.position_encoding == FUTON_POS_ROPE;
+  const float scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
+  if (!cls_only && (hd == 32 || hd == 64) && ntiles > 0) {
+    dim3 grid(ntiles, H);
+    if (hd == 32) {
+      if (rope) attn_flash_kernel<32, true, OutT><<<grid, 128, 0, st>>>(d.ws.qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+      else attn_flash_kernel<32, false, OutT><<<grid, 128, 0, st>>>(d.ws.qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+    } else {
+      if (rope) attn_flash_kernel<64, true, OutT><<<grid, 128, 0, st>>>(d.ws.qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+      else attn_flash_kernel<64, false, OutT><<<grid, 128, 0, st>>>(d.ws.qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+    }
+  } else {
+    const int nq = cls_only ? nseq : T;
+    const long warps = (long)nq * H;
+    const int blocks = (int)((warps * 32 + 255) / 256);
+    if (blocks == 0) return FUTON_OK;
+#define FUTON_ROWQ(HD_)                                                                    \
+  attn_rowq_kernel<HD_, OutT><<<blocks, 256, 0, st>>>(d.ws.qkv, h, H, cu, nseq, nq,        \
+                                                     cls_only ? 1 : 0, d.rcos, d.rsin,     \
+                                                     rope ? 1 : 0, scale_log2, out, h)
+    switch (hd) {
+      case 8: FUTON_ROWQ(8); break;
+      case 16: FUTON_ROWQ(16); break;
+      case 32: FUTON_ROWQ(32); break;
+      case 64: FUTON_ROWQ(64); break;
+      case 128: FUTON_ROWQ(128); break;
+      default: return set_err(err, errlen, FUTON_EINVAL, "native: unsupported head_dim %d", hd);
+    }
+#undef FUTON_ROWQ
+  }
+  CU_TRY(cudaGetLastError());
+  d.launches.fetch_add(1, std::memory_order_relaxed);
+  return FUTON_OK;
+}
+
+// ---- one micro-batch -----------------------------------------------------
+// ids: device [T]; cu: device [nseq+1] (local offsets); tiles: device.
+int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, int nseq, int T,
+               const AttnTile* tiles, int ntiles, int out_dim, float* out, cudaStream_t st,
+               volatile const int* cancel, char* err, size_t errlen) {
+  const futon_cfg& c = m.cfg;
+  const int h = c.hidden_size, I = c.intermediate_size;
+  const bool q8 = m.q8 != 0, cls = c.pooling == FUTON_POOL_CLS;
+  const float eps = (float)c.layer_norm_eps;
+  Workspace& w = d.ws;
+  int rc;
+
+  embed_ln_kernel<<<grid_rows(T, 8, d.num_sms), 256, 0, st>>>(
+      ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0, d.pos, d.embw, d.embb, eps, w.x, w.xb, w.xq, w.xs);
+  CU_TRY(cudaGetLastError());
+  d.launches.fetch_add(1, std::memory_order_relaxed);
+
+  for (int li = 0; li < c.num_layers; ++li) {
+    if (cancel && *cancel)
+      return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
+    const LayerDev& L = d.layers[li];
+    const bool last_cls = cls && li == c.num_layers - 1;
+    const int rows = last_cls ? nseq : T;
+
+    // qkv = x·Wqkvᵀ + b → bf16 [T, 3h]
+    if ((rc = run_gemm(d, q8 ? (const void*)w.xq : w.xb, q8, w.xs, T, L.qkv, kEpiStore, false,
+                       w.qkv, 3 * h, nullptr, 0, st, err, errlen)))
+      return rc;
+
+    // attention → attn [rows, h]
+    if (q8) rc = run_attention<float>(m, d, T, nseq, cu, tiles, ntiles, last_cls, (float*)w.attn, st, err, errlen);
+    else rc = run_attention<bf16>(m, d, T, nseq, cu, tiles, ntiles, last_cls, (bf16*)w.attn, st, err, errlen);
+    if (rc) return rc;
+
+    const float* resid = w.x;
+    if (last_cls) {
+      gather_rows_kernel<<<grid_rows(nseq * (h / 4), 256, d.num_sms), 256, 0, st>>>(
+          w.x, cu, nseq, h, w.xc, nullptr);
+      CU_TRY(cudaGetLastError());
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+      resid = w.xc;
+    }
+
+    // out projection + residual → tmp f32, then LN1 → x, xb (, xq)
+    const void* a_out = w.attn;
+    const float* a_out_s = nullptr;
+    if (q8) {
+      quant_rows_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>((const float*)w.attn, rows, h, w.attnq, w.attns);
+      CU_TRY(cudaGetLastError());
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+      a_out = w.attnq;
+      a_out_s = w.attns;
+    }
+    if ((rc = run_gemm(d, a_out, q8, a_out_s, rows, L.out, kEpiResid, true, w.tmp, h, resid, h, st,
+                       err, errlen)))
+      return rc;
+    layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(w.tmp, rows, h, L.n1w, L.n1b,
+                                                                   eps, w.x, w.xb, w.xq, w.xs);
+    CU_TRY(cudaGetLastError());
+    d.launches.fetch_add(1, std::memory_order_relaxed);
+
+    if (cancel && *cancel)
+      return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
+
+    // FFN
+    const int epi = c.activation == FUTON_ACT_SWIGLU ? kEpiSwiglu : kEpiGelu;
+    if ((rc = run_gemm(d, q8 ? (const void*)w.xq : w.xb, q8, w.xs, rows, L.fc1, epi, q8, w.ffn, I,
+                       nullptr, 0, st, err, errlen)))
+      return rc;
+    const void* a_fc2 = w.ffn;
+    const float* a_fc2_s = nullptr;
+    if (q8) {
+      quant_rows_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>((const float*)w.ffn, rows, I, w.ffnq, w.ffns);
+      CU_TRY(cudaGetLastError());
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+      a_fc2 = w.ffnq;
+      a_fc2_s = w.ffns;
+    }
+    if ((rc = run_gemm(d, a_fc2, q8, a_fc2_s, rows, L.fc2, kEpiResid, true, w.tmp, h, w.x, h, st,
+                       err, errlen)))
+      return rc;
+    layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(w.tmp, rows, h, L.n2w, L.n2b,
+                                                                   eps, w.x, w.xb, w.xq, w.xs);
+    CU_TRY(cudaGetLastError());
+    d.launches.fetch_add(1, std::memory_order_relaxed);
+  }
+
+  const int mat_ln = c.matryoshka_layernorm ? 1 : 0;
+  pool_kernel<<<nseq, 256, h * sizeof(float), st>>>(w.x, cu, h, cls ? 0 : 1, out_dim, mat_ln,
+                                                    c.normalize ? 1 : 0, out);
+  CU_TRY(cudaGetLastError());
+  d.launches.fetch_add(1, std::memory_order_relaxed);
+  return FUTON_OK;
+}
+
+// ---- call planning -------------------------------------------------------
+struct MicroBatch {
+  int s0, s1;   // sequences [s0, s1)
+  int t0, t1;   // tokens [t0, t1)
+  size_t cu_off, tile_off;  // int offsets into the meta buffer
+  int ntiles;
+};
+
+int validate_input(const futon_model& m, const int32_t* cu, int nseq, int out_dim, char* err,
+                   size_t errlen) {
+  const futon_cfg& c = m.cfg;
+  if (nseq < 0) return set_err(err, errlen, FUTON_EINVAL, "native: negative sequence count");
+  if (out_dim < 0 || out_dim > c.hidden_size)
+    return set_err(err, errlen, FUTON_EINVAL, "native: requested dim %d outside [1,%d]", out_dim,
+                   c.hidden_size);
+  if (out_dim != 0 && out_dim != c.hidden_size && !c.matryoshka)
+    return set_err(err, errlen, FUTON_EINVAL,
+                   "native: pack does not support matryoshka truncation to %d", out_dim);
+  if (nseq > 0 && cu[0] != 0)
+    return set_err(err, errlen, FUTON_EINVAL, "native: cu_seqlens[0] must be 0");
+  for (int s = 0; s < nseq; ++s) {
+    const int L = cu[s + 1] - cu[s];
+    if (L <= 0) return set_err(err, errlen, FUTON_EINVAL, "native: batch item %d: empty token sequence", s);
+    if (L > m.eff_max)
+      return set_err(err, errlen, FUTON_EINVAL,
+                     "native: batch item %d: sequence length %d exceeds effective max_seq_len %d", s,
+                     L, m.eff_max);
+  }
+  return FUTON_OK;
+}
+
+int check_ids(const futon_model& m, const int32_t* ids, const int32_t* cu, int nseq, char* err,
+              size_t errlen) {
+  const int V = m.cfg.vocab_size;
+  for (int s = 0; s < nseq; ++s)
+    for (int t = cu[s]; t < cu[s + 1]; ++t)
+      if (ids[t] < 0 || ids[t] >= V)
+        return set_err(err, errlen, FUTON_EINVAL, "native: batch item %d: token id %d outside vocab of %d",
+                       s, ids[t], V);
+  return FUTON_OK;
+}
+
+// Plans micro-batches, fills the pinned meta buffer, uploads it (one copy).
+int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, std::vector<MicroBatch>& mbs,
+                    cudaStream_t st, char* err, size_t errlen) {
+  mbs.clear();
+  size_t meta = 0;
+  for (int s = 0; s < nseq;) {
+    MicroBatch mb;
+    mb.s0 = s;
+    mb.t0 = cu[s];
+    int ntiles = 0;
+    while (s < nseq && (s == mb.s0 || cu[s + 1] - mb.t0 <= kTokenBudget)) {
+      ntiles += (cu[s + 1] - cu[s] + 63) / 64;
+      ++s;
+    }
+    mb.s1 = s;
+    mb.t1 = cu[s];
+    mb.ntiles = ntiles;
+    mb.cu_off = meta;
+    meta += align_up((size_t)(mb.s1 - mb.s0 + 1), 4);
+    mb.tile_off = meta;
+    meta += align_up((size_t)ntiles * 2, 4);
+    mbs.push_back(mb);
+  }
+  if (mbs.empty()) return FUTON_OK;
+  // The pinned staging may still feed the previous call's upload.
+  CU_TRY(cudaEventSynchronize(d.meta_evt));
+  int rc;
+  if ((rc = ensure_host(&d.h_meta, &d.h_meta_cap, meta, err, errlen))) return rc;
+  if ((rc = ensure_dev(&d.d_meta, &d.d_meta_cap, meta, err, errlen))) return rc;
+  for (const MicroBatch& mb : mbs) {
+    int* hc = d.h_meta + mb.cu_off;
+    for (int s = mb.s0; s <= mb.s1; ++s) hc[s - mb.s0] = cu[s] - mb.t0;
+    AttnTile* ht = reinterpret_cast<AttnTile*>(d.h_meta + mb.tile_off);
+    int k = 0;
+    for (int s = mb.s0; s < mb.s1; ++s)
+      for (int q0 = 0; q0 < cu[s + 1] - cu[s]; q0 += 64) ht[k++] = AttnTile{s - mb.s0, q0};
+  }
+  CU_TRY(cudaMemcpyAsync(d.d_meta, d.h_meta, meta * sizeof(int), cudaMemcpyHostToDevice, st));
+  CU_TRY(cudaEventRecord(d.meta_evt, st));
+  return FUTON_OK;
+}
+
+int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* cu, int nseq,
+             int out_dim, float* d_out, cudaStream_t st, volatile const int* cancel, char* err,
+             size_t errlen) {
+  std::vector<MicroBatch> mbs;
+  int rc;
+  if ((rc = plan_and_upload(d, cu, nseq, mbs, st, err, errlen))) return rc;
+  size_t max_t = 0;
+  for (const MicroBatch& mb : mbs) max_t = std::max<size_t>(max_t, (size_t)(mb.t1 - mb.t0));
+  if ((rc = ensure_workspace(m, d, max_t, err, errlen))) return rc;
+  const int dim = out_dim ? out_dim : m.cfg.hidden_size;
+  for (const MicroBatch& mb : mbs) {
+    if (cancel && *cancel)
+      return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
+    if ((rc = forward_mb(m, d, d_ids + mb.t0, d.d_meta + mb.cu_off, mb.s1 - mb.s0, mb.t1 - mb.t0,
+                         reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
+                         out_dim, d_out + (size_t)mb.s0 * dim, st, cancel, err, errlen)))
+      return rc;
+  }
+  return FUTON_OK;
+}
+
+int read_device_error(DevCtx& d, char* err, size_t errlen) {
+  int code = 0;
+  CU_TRY(cudaMemcpy(&code, d.err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    CU_TRY(cudaMemset(d.err_word, 0, sizeof(int)));
+    return set_err(err, errlen, code == kDevBadInput ? FUTON_EINVAL : FUTON_EDEVICE,
+                   code == kDevBadInput ? "native: token id outside vocab (device-side check)"
+                                        : "native: device-side error %d (a bounded pipeline wait expired)",
+                   code);
+  }
+  return FUTON_OK;
+}
+
+// Host-buffer encode on one device (blocking).
+int encode_host(futon_model* m, DevCtx& d, const int32_t* ids, const int32_t* cu, int nseq,
+                int out_dim, float* out, volatile const int* cancel, char* err, size_t errlen) {
+  std::lock_guard<std::mutex> lock(d.mu);
+  CU_TRY(cudaSetDevice(d.device));
+  if (nseq == 0) return FUTON_OK;
+  const size_t T = (size_t)cu[nseq];
+  const int dim = out_dim ? out_dim : m->cfg.hidden_size;
+  int rc;
+  if ((rc = ensure_host(&d.h_ids, &d.h_ids_cap, T, err, errlen))) return rc;
+  if ((rc = ensure_dev(&d.d_ids, &d.d_ids_cap, T, err, errlen))) return rc;
+  if ((rc = ensure_host(&d.h_out, &d.h_out_cap, (size_t)nseq * dim, err, errlen))) return rc;
+  if ((rc = ensure_dev(&d.d_out, &d.d_out_cap, (size_t)nseq * dim, err, errlen))) return rc;
+  memcpy(d.h_ids, ids, T * sizeof(int));
+  CU_TRY(cudaMemcpyAsync(d.d_ids, d.h_ids, T * sizeof(int), cudaMemcpyHostToDevice, d.stream));
+  rc = run_call(*m, d, d.d_ids, cu, nseq, out_dim, d.d_out, d.stream, cancel, err, errlen);
+  if (rc) {
+    cudaStreamSynchronize(d.stream);  // leave nothing in flight
+    return rc;
+  }
+  CU_TRY(cudaMemcpyAsync(d.h_out, d.d_out, (size_t)nseq * dim * sizeof(float),
+                         cudaMemcpyDeviceToHost, d.stream));
+  CU_TRY(cudaStreamSynchronize(d.stream));
+  if ((rc = read_device_error(d, err, errlen))) return rc;
+  memcpy(out, d.h_out, (size_t)nseq * dim * sizeof(float));
+  return FUTON_OK;
+}
+
+// ---- kernel-seam context (per CUDA device) ------------------------------
+struct SeamCtx {
+  std::mutex mu;
+  void* scratch = nullptr;
+  size_t cap = 0;
+  int* err_word = nullptr;
+  int num_sms = 148;
+  bool init = false;
+};
+SeamCtx g_seam[64];
+
+int seam_begin(int dev, size_t bytes, SeamCtx** out, char* err, size_t errlen) {
+  if (dev < 0 || dev >= 64) return set_err(err, errlen, FUTON_EINVAL, "native: bad device %d", dev);
+  SeamCtx& s = g_seam[dev];
+  CU_TRY(cudaSetDevice(dev));
+  if (!s.init) {
+    CU_TRY(cudaMalloc(&s.err_word, sizeof(int)));
+    CU_TRY(cudaMemset(s.err_word, 0, sizeof(int)));
+    CU_TRY(cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev));
+    s.init = true;
+  }
+  if (s.cap < bytes) {
+    CU_TRY(cudaDeviceSynchronize());
+    if (s.scratch) cudaFree(s.scratch);
+    s.scratch = nullptr;
+    s.cap = 0;
+    CU_TRY(cudaMalloc(&s.scratch, bytes));
+    s.cap = bytes;
+  }
+  *out = &s;
+  return FUTON_OK;
+}
+
+int seam_finish(SeamCtx& s, cudaStream_t st, char* err, size_t errlen) {
+  CU_TRY(cudaStreamSynchronize(st));
+  int code = 0;
+  CU_TRY(cudaMemcpy(&code, s.err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code) {
+    CU_TRY(cudaMemset(s.err_word, 0, sizeof(int)));
+    return set_err(err, errlen, FUTON_EDEVICE, "native: device-side error %d", code);
+  }
+  return FUTON_OK;
+}
+
+int seam_gemm(SeamCtx& s, const void* A, bool s8, const float* a_scale, int m, const void* W,
+              const float* w_scale, int n, int k, const float* bias, float* dst, cudaStream_t st,
+              char* err, size_t errlen) {
+  CUtensorMap ta, tw;
+  const int bn = pick_bn(n);
+  if (!make_operand_map(&ta, A, s8, (uint64_t)m, (uint64_t)k, 128) ||
+      !make_operand_map(&tw, W, s8, (uint64_t)n, (uint64_t)k, (uint32_t)bn))
+    return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed");
+  GemmLaunch g;
+  g.ta = &ta;
+  g.tw = &tw;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.bn = bn;
+  g.epi = kEpiStore;
+  g.out_f32 = true;
+  g.ep.out = dst;
+  g.ep.ldo = n;
+  g.ep.bias = bias;
+  g.ep.resid = nullptr;
+  g.ep.ldr = 0;
+  g.ep.a_scale = a_scale;
+  g.ep.w_scale = w_scale;
+  g.err = s.err_word;
+  g.num_sms = s.num_sms;
+  g.stream = st;
+  cudaError_t e = s8 ? launch_gemm_s8(g) : launch_gemm_bf16(g);
+  if (e != cudaSuccess)
+    return set_err(err, errlen, FUTON_ECUDA, "native: gemm launch: %s", cudaGetErrorString(e));
+  return FUTON_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int futon_cuda_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, int ntensors,
+                            const int* devices, int ndev, int q8, futon_model** out, char* err,
+                            size_t errlen) {
+  if (!cfg || !out || (ntensors > 0 && !tensors))
+    return set_err(err, errlen, FUTON_EINVAL, "native: null argument");
+  *out = nullptr;
+  const futon_cfg& c = *cfg;
+  const int h = c.hidden_size, I = c.intermediate_size, H = c.num_heads;
+  if (h <= 0 || c.num_layers <= 0 || H <= 0 || I <= 0 || c.vocab_size <= 0 || c.max_seq_len <= 2)
+    return set_err(err, errlen, FUTON_EINVAL, "native: non-positive architecture dimension");
+  if (h % H != 0)
+    return set_err(err, errlen, FUTON_EINVAL, "native: hidden_size %d not divisible by num_heads %d", h, H);
+  const int hd = h / H;
+  if (h % 8 || I % 8 || h > 1024)
+    return set_err(err, errlen, FUTON_EINVAL,
+                   "native: hidden_size and intermediate_size must be multiples of 8 (hidden ≤ 1024)");
+  if (q8 && (h % 16 || I % 16))
+    return set_err(err, errlen, FUTON_EINVAL, "native: the int8 path needs K multiples of 16");
+  if (hd != 8 && hd != 16 && hd != 32 && hd != 64 && hd != 128)
+    return set_err(err, errlen, FUTON_EINVAL, "native: unsupported head_dim %d", hd);
+  const bool rope = c.position_encoding == FUTON_POS_ROPE, swiglu = c.activation == FUTON_ACT_SWIGLU;
+  if (rope && !(c.rope_theta > 0))
+    return set_err(err, errlen, FUTON_EINVAL, "native: rope position encoding requires rope_theta > 0");
+  int half = 0;
+  if (swiglu) {
+    half = (I % 128 == 0) ? 128 : (I % 64 == 0) ? 64 : (I % 32 == 0) ? 32 : 0;
+    if (!half)
+      return set_err(err, errlen, FUTON_EINVAL, "native: swiglu needs intermediate_size %% 32 == 0");
+  }
+  if (!devices || ndev <= 0) return set_err(err, errlen, FUTON_EINVAL, "native: no devices");
+  int visible = futon_cuda_device_count();
+  for (int i = 0; i < ndev; ++i)
+    if (devices[i] < 0 || devices[i] >= visible)
+      return set_err(err, errlen, FUTON_EINVAL, "native: device %d not visible (%d devices)",
+                     devices[i], visible);
+
+  // ---- tensor set (newModel, model.go:134-263) ----
+  TensorSet ts;
+  for (int i = 0; i < ntensors; ++i) {
+    const futon_tensor& t = tensors[i];
+    if (!t.name || !t.data)
+      return set_err(err, errlen, FUTON_EINVAL, "native: tensor %d has no name or data", i);
+    if (t.dtype != FUTON_DTYPE_F32 && t.dtype != FUTON_DTYPE_F16)
+      return set_err(err, errlen, FUTON_EINVAL, "native: tensor %s has unsupported dtype", t.name);
+    if (t.ndim < 1 || t.ndim > 4)
+      return set_err(err, errlen, FUTON_EINVAL, "native: tensor %s has rank %d", t.name, t.ndim);
+    HostTensor ht;
+    ht.t = &t;
+    if (t.dtype == FUTON_DTYPE_F16) {
+      size_t n = 1;
+      for (int k = 0; k < t.ndim; ++k) n *= (size_t)t.shape[k];
+      ht.f32.resize(n);
+      const uint16_t* src = (const uint16_t*)t.data;
+      for (size_t k = 0; k < n; ++k) ht.f32[k] = f16_to_f32(src[k]);
+    }
+    if (ts.byname.count(t.name))
+      return set_err(err, errlen, FUTON_EINVAL, "native: duplicate tensor %s", t.name);
+    ts.byname.emplace(t.name, std::move(ht));
+  }
+  int rc;
+  const float *word, *pos = nullptr, *type = nullptr, *embw, *embb;
+  if ((rc = need(ts, "embeddings.word", {c.vocab_size, h}, false, &word, err, errlen))) return rc;
+  if (!rope && (rc = need(ts, "embeddings.position", {c.max_seq_len, h}, false, &pos, err, errlen))) return rc;
+  if (c.type_vocab_size > 0 &&
+      (rc = need(ts, "embeddings.token_type", {c.type_vocab_size, h}, false, &type, err, errlen)))
+    return rc;
+  if ((rc = need(ts, "embeddings.norm.weight", {h}, false, &embw, err, errlen))) return rc;
+  if ((rc = need(ts, "embeddings.norm.bias", {h}, false, &embb, err, errlen))) return rc;
+  struct LW {
+    const float *qkvw, *qkvb, *outw, *outb, *n1w, *n1b, *fc1w, *fc1b, *gatew, *gateb, *fc2w, *fc2b,
+        *n2w, *n2b;
+  };
+  std::vector<LW> lw(c.num_layers);
+  for (int i = 0; i < c.num_layers; ++i) {
+    auto p = [&](const char* s) { return "layers." + std::to_string(i) + "." + s; };
+    LW& l = lw[i];
+    l.gatew = l.gateb = nullptr;
+    if ((rc = need(ts, p("attn.qkv.weight"), {3 * h, h}, false, &l.qkvw, err, errlen))) return rc;
+    if ((rc = need(ts, p("attn.qkv.bias"), {3 * h}, true, &l.qkvb, err, errlen))) return rc;
+    if ((rc = need(ts, p("attn.out.weight"), {h, h}, false, &l.outw, err, errlen))) return rc;
+    if ((rc = need(ts, p("attn.out.bias"), {h}, true, &l.outb, err, errlen))) return rc;
+    if ((rc = need(ts, p("norm1.weight"), {h}, false, &l.n1w, err, errlen))) return rc;
+    if ((rc = need(ts, p("norm1.bias"), {h}, false, &l.n1b, err, errlen))) return rc;
+    if ((rc = need(ts, p("mlp.fc1.weight"), {I, h}, false, &l.fc1w, err, errlen))) return rc;
+    if ((rc = need(ts, p("mlp.fc1.bias"), {I}, true, &l.fc1b, err, errlen))) return rc;
+    if (swiglu) {
+      if ((rc = need(ts, p("mlp.gate.weight"), {I, h}, false, &l.gatew, err, errlen))) return rc;
+      if ((rc = need(ts, p("mlp.gate.bias"), {I}, true, &l.gateb, err, errlen))) return rc;
+    }
+    if ((rc = need(ts, p("mlp.fc2.weight"), {h, I}, false, &l.fc2w, err, errlen))) return rc;
+    if ((rc = need(ts, p("mlp.fc2.bias"), {h}, true, &l.fc2b, err, errlen))) return rc;
+    if ((rc = need(ts, p("norm2.weight"), {h}, false, &l.n2w, err, errlen))) return rc;
+    if ((rc = need(ts, p("norm2.bias"), {h}, false, &l.n2b, err, errlen))) return rc;
+  }
+  for (auto& kv : ts.byname)
+    if (!ts.used.count(kv.first))
+      return set_err(err, errlen, FUTON_EINVAL,
+                     "native: unexpected tensor %s (pack/config mismatch)", kv.first.c_str());
+
+  auto model = std::make_unique<futon_model>();
+  model->cfg = c;
+  model->q8 = q8 ? 1 : 0;
+  model->head_dim = hd;
+  model->eff_max = effective_max(c);
+  model->swiglu_half = half;
+
+  // RoPE tables (precomputeRoPE, model.go:306-318): f64 angles, f32 storage.
+  std::vector<float> rc_tab, rs_tab;
+  if (rope) {
+    const int ms = model->eff_max, hh = hd / 2;
+    rc_tab.resize((size_t)ms * hh);
+    rs_tab.resize((size_t)ms * hh);
+    for (int t = 0; t < ms; ++t)
+      for (int i = 0; i < hh; ++i) {
+        const double freq = 1.0 / std::pow(c.rope_theta, (double)(2 * i) / (double)hd);
+        const double ang = (double)t * freq;
+        rc_tab[(size_t)t * hh + i] = (float)std::cos(ang);
+        rs_tab[(size_t)t * hh + i] = (float)std::sin(ang);
+      }
+  }
+
+  const size_t max_mat = std::max<size_t>((size_t)3 * h * h, (size_t)2 * I * h);
+  for (int di = 0; di < ndev; ++di) {
+    auto d = std::make_unique<DevCtx>();
+    d->device = devices[di];
+    CU_TRY(cudaSetDevice(d->device));
+    CU_TRY(cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, d->device));
+    CU_TRY(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+    CU_TRY(cudaEventCreateWithFlags(&d->meta_evt, cudaEventDisableTiming));
+    CU_TRY(cudaEventRecord(d->meta_evt, d->stream));
+    if ((rc = dev_alloc(*d, &d->err_word, 1, err, errlen))) return rc;
+    CU_TRY(cudaMemset(d->err_word, 0, sizeof(int)));
+    if ((rc = upload_f32(*d, &d->word, word, (size_t)c.vocab_size * h, err, errlen))) return rc;
+    if ((rc = upload_f32(*d, &d->pos, pos, pos ? (size_t)c.max_seq_len * h : 0, err, errlen))) return rc;
+    if ((rc = upload_f32(*d, &d->type0, type, type ? (size_t)h : 0, err, errlen))) return rc;
+    if ((rc = upload_f32(*d, &d->embw, embw, h, err, errlen))) return rc;
+    if ((rc = upload_f32(*d, &d->embb, embb, h, err, errlen))) return rc;
+    if (rope) {
+      if ((rc = upload_f32(*d, &d->rcos, rc_tab.data(), rc_tab.size(), err, errlen))) return rc;
+      if ((rc = upload_f32(*d, &d->rsin, rs_tab.data(), rs_tab.size(), err, errlen))) return rc;
+    }
+    float* staging = nullptr;
+    CU_TRY(cudaMalloc(&staging, max_mat * sizeof(float)));
+    d->layers.resize(c.num_layers);
+    for (int i = 0; i < c.num_layers && rc == FUTON_OK; ++i) {
+      const LW& l = lw[i];
+      LayerDev& L = d->layers[i];
+      if ((rc = upload_gemm(*d, L.qkv, l.qkvw, l.qkvb, nullptr, nullptr, 3 * h, h, 0, q8, staging, err, errlen))) break;
+      if ((rc = upload_gemm(*d, L.out, l.outw, l.outb, nullptr, nullptr, h, h, 0, q8, staging, err, errlen))) break;
+      if (swiglu) rc = upload_gemm(*d, L.fc1, l.fc1w, l.fc1b, l.gatew, l.gateb, I, h, half, q8, staging, err, errlen);
+      else rc = upload_gemm(*d, L.fc1, l.fc1w, l.fc1b, nullptr, nullptr, I, h, 0, q8, staging, err, errlen);
+      if (rc) break;
+      if ((rc = upload_gemm(*d, L.fc2, l.fc2w, l.fc2b, nullptr, nullptr, h, I, 0, q8, staging, err, errlen))) break;
+      if ((rc = upload_f32(*d, &L.n1w, l.n1w, h, err, errlen))) break;
+      if ((rc = upload_f32(*d, &L.n1b, l.n1b, h, err, errlen))) break;
+      if ((rc = upload_f32(*d, &L.n2w, l.n2w, h, err, errlen))) break;
+      if ((rc = upload_f32(*d, &L.n2b, l.n2b, h, err, errlen))) break;
+    }
+    cudaFree(staging);
+    if (rc) return rc;
+    CU_TRY(cudaStreamSynchronize(d->stream));
+    model->devs.push_back(std::move(d));
+  }
+  *out = model.release();
+  return FUTON_OK;
+}
+
+void futon_cuda_model_destroy(futon_model* model) {
+  if (!model) return;
+  delete model;
+}
+
+int futon_cuda_encode(futon_model* model, int device, const int32_t* ids,
+                      const int32_t* cu_seqlens, int nseq, int out_dim, float* out,
+                      volatile const int* cancel, char* err, size_t errlen) {
+  if (!model) return set_err(err, errlen, FUTON_EINVAL, "native: null model");
+  if (device < 0 || device >= (int)model->devs.size())
+    return set_err(err, errlen, FUTON_EINVAL, "native: device index %d out of range", device);
+  if (nseq > 0 && (!ids || !cu_seqlens || !out))
+    return set_err(err, errlen, FUTON_EINVAL, "native: null buffer");
+  int rc;
+  if ((rc = validate_input(*model, cu_seqlens, nseq, out_dim, err, errlen))) return rc;
+  if ((rc = check_ids(*model, ids, cu_seqlens, nseq, err, errlen))) return rc;
+  if (cancel && *cancel) return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
+  return encode_host(model, *model->devs[device], ids, cu_seqlens, nseq, out_dim, out, cancel, err,
+                     errlen);
+}
+
+int futon_cuda_encode_batch(futon_model* model, const int32_t* ids, const int32_t* cu_seqlens,
+                            int nseq, int out_dim, float* out, volatile const int* cancel,
+                            char* err, size_t errlen) {
+  if (!model) return set_err(err, errlen, FUTON_EINVAL, "native: null model");
+  if (nseq > 0 && (!ids || !cu_seqlens || !out))
+    return set_err(err, errlen, FUTON_EINVAL, "native: null buffer");
+  int rc;
+  if ((rc = validate_input(*model, cu_seqlens, nseq, out_dim, err, errlen))) return rc;
+  if ((rc = check_ids(*model, ids, cu_seqlens, nseq, err, errlen))) return rc;
+  if (cancel && *cancel) return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
+  const int ndev = (int)model->devs.size();
+  const int dim = out_dim ? out_dim : model->cfg.hidden_size;
+  if (nseq == 0) return FUTON_OK;
+  // Contiguous shards balanced by estimated cost: GEMM work ∝ L, attention ∝ L².
+  const double h = model->cfg.hidden_size;
+  std::vector<double> cost(nseq + 1, 0.0);
+  for (int s = 0; s < nseq; ++s) {
+    const double L = cu_seqlens[s + 1] - cu_seqlens[s];
+    cost[s + 1] = cost[s] + L * (12.0 * h + 2.0 * L);
+  }
+  std::vector<int> cut(ndev + 1, nseq);
+  cut[0] = 0;
+  for (int k = 1; k < ndev; ++k) {
+    const double target = cost[nseq] * k / ndev;
+    cut[k] = (int)(std::lower_bound(cost.begin(), cost.end(), target) - cost.begin());
+    cut[k] = std::max(cut[k - 1], std::min(cut[k], nseq));
+  }
+  std::vector<int> rcs(ndev, FUTON_OK);
+  std::vector<std::string> msgs(ndev);
+  std::vector<std::thread> threads;
+  for (int k = 0; k < ndev; ++k) {
+    threads.emplace_back([&, k] {
+      const int s0 = cut[k], s1 = cut[k + 1];
+      if (s1 <= s0) return;
+      std::vector<int32_t> cu(s1 - s0 + 1);
+      for (int s = s0; s <= s1; ++s) cu[s - s0] = cu_seqlens[s] - cu_seqlens[s0];
+      char e[512] = {0};
+      rcs[k] = encode_host(model, *model->devs[k], ids + cu_seqlens[s0], cu.data(), s1 - s0,
+                           out_dim, out + (size_t)s0 * dim, cancel, e, sizeof e);
+      msgs[k] = e;
+    });
+  }
+  for (auto& t : threads) t.join();
+  for (int k = 0; k < ndev; ++k)
+    if (rcs[k] != FUTON_OK) return set_err(err, errlen, rcs[k], "%s", msgs[k].c_str());
+  return FUTON_OK;
+}
+
+int futon_cuda_encode_device(futon_model* model, int device, const int32_t* d_ids,
+                             const int32_t* cu_seqlens, int nseq, int out_dim, float* d_out,
+                             void* stream, char* err, size_t errlen) {
+  if (!model) return set_err(err, errlen, FUTON_EINVAL, "native: null model");
+  if (device < 0 || device >= (int)model->devs.size())
+    return set_err(err, errlen, FUTON_EINVAL, "native: device index %d out of range", device);
+  int rc;
+  if ((rc = validate_input(*model, cu_seqlens, nseq, out_dim, err, errlen))) return rc;
+  DevCtx& d = *model->devs[device];
+  std::lock_guard<std::mutex> lock(d.mu);
+  CU_TRY(cudaSetDevice(d.device));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : d.stream;
+  return run_call(*model, d, (const int*)d_ids, cu_seqlens, nseq, out_dim, d_out, st, nullptr, err,
+                  errlen);
+}
+
+int futon_cuda_sync(futon_model* model, int device, void* stream, char* err, size_t errlen) {
+  if (!model) return set_err(err, errlen, FUTON_EINVAL, "native: null model");
+  if (device < 0 || device >= (int)model->devs.size())
+    return set_err(err, errlen, FUTON_EINVAL, "native: device index %d out of range", device);
+  DevCtx& d = *model->devs[device];
+  std::lock_guard<std::mutex> lock(d.mu);
+  CU_TRY(cudaSetDevice(d.device));
+  if (stream) CU_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  CU_TRY(cudaStreamSynchronize(d.stream));
+  return read_device_error(d, err, errlen);
+}
+
+long long futon_cuda_launch_count(futon_model* model, int device) {
+  if (!model || device < 0 || device >= (int)model->devs.size()) return -1;
+  return model->devs[device]->launches.load();
+}
+
+int futon_cuda_matmul_t(int cuda_device, float* dst, const float* a, const float* b, int m, int n,
+                        int k, const float* bias, void* stream, char* err, size_t errlen) {
+  if (m < 0 || n <= 0 || k <= 0 || k % 8)
+    return set_err(err, errlen, FUTON_EINVAL, "native: matmul shape m=%d n=%d k=%d (k %% 8 == 0)", m, n, k);
+  if (m == 0) return FUTON_OK;
+  const size_t abytes = align_up((size_t)m * k * 2, 256), bbytes = align_up((size_t)n * k * 2, 256);
+  SeamCtx* s;
+  int rc;
+  if ((rc = seam_begin(cuda_device, abytes + bbytes, &s, err, errlen))) return rc;
+  std::lock_guard<std::mutex> lock(s->mu);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bf16* ab = (bf16*)s->scratch;
+  bf16* bb = (bf16*)((uint8_t*)s->scratch + abytes);
+  f32_to_bf16_kernel<<<1024, 256, 0, st>>>(a, (size_t)m * k, ab);
+  f32_to_bf16_kernel<<<1024, 256, 0, st>>>(b, (size_t)n * k, bb);
+  CU_TRY(cudaGetLastError());
+  if ((rc = seam_gemm(*s, ab, false, nullptr, m, bb, nullptr, n, k, bias, dst, st, err, errlen))) return rc;
+  return seam_finish(*s, st, err, errlen);
+}
+
+int futon_cuda_matmul_t_q8(int cuda_device, float* dst, const float* a, const int8_t* qb,
+                           const float* scales, int m, int n, int k, const float* bias,
+                           void* stream, char* err, size_t errlen) {
+  if (m < 0 || n <= 0 || k <= 0 || k % 16)
+    return set_err(err, errlen, FUTON_EINVAL, "native: q8 matmul shape m=%d n=%d k=%d (k %% 16 == 0)", m, n, k);
+  if (m == 0) return FUTON_OK;
+  const size_t qbytes = align_up((size_t)m * k, 256), sbytes = align_up((size_t)m * 4, 256);
+  SeamCtx* s;
+  int rc;
+  if ((rc = seam_begin(cuda_device, qbytes + sbytes, &s, err, errlen))) return rc;
+  std::lock_guard<std::mutex> lock(s->mu);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int8_t* qa = (int8_t*)s->scratch;
+  float* sa = (float*)((uint8_t*)s->scratch + qbytes);
+  quant_rows_kernel<<<grid_rows(m, 8, s->num_sms), 256, 0, st>>>(a, m, k, qa, sa);
+  CU_TRY(cudaGetLastError());
+  if ((rc = seam_gemm(*s, qa, true, sa, m, qb, scales, n, k, bias, dst, st, err, errlen))) return rc;
+  return seam_finish(*s, st, err, errlen);
+}
+
+int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, const float* src,
+                                int rows, int k, void* stream, char* err, size_t errlen) {
+  if (rows < 0 || k <= 0 || k % 4)
+    return set_err(err, errlen, FUTON_EINVAL, "native: quantize shape rows=%d k=%d (k %% 4 == 0)", rows, k);
+  if (rows == 0) return FUTON_OK;
+  SeamCtx* s;
+  int rc;
+  if ((rc = seam_begin(cuda_device, 256, &s, err, errlen))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  quant_rows_kernel<<<grid_rows(rows, 8, s->num_sms), 256, 0, st>>>(src, rows, k, dst, scales);
+  CU_TRY(cudaGetLastError());
+  return seam_finish(*s, st, err, errlen);
+}
+
+}  // extern "C"

@@ -1,0 +1,6 @@
+// gemm_bf16.cu — bf16 × bf16 → f32 tcgen05 GEMM instantiations.
+#include "gemm_launch.cuh"
+
+namespace futon {
+cudaError_t launch_gemm_bf16(const GemmLaunch& g) { return launch_gemm_any<false>(g); }
+}  // namespace futon

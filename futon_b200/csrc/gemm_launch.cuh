@@ -1,0 +1,87 @@
+// gemm_launch.cuh — host-side launch of the tcgen05 GEMM instantiations.
+#pragma once
+
+#include <atomic>
+
+#include "gemm_tc.cuh"
+
+namespace futon {
+
+struct GemmLaunch {
+  const CUtensorMap* ta;  // A [M, K] (bf16 or s8), box 128 × 128 bytes
+  const CUtensorMap* tw;  // W [N, K], box bn × 128 bytes
+  int M, N, K;
+  int bn;                 // 64, 128, 192 or 256
+  int epi;                // EpiKind
+  bool out_f32;           // output element type: f32 (true) or bf16
+  EpiParams ep;
+  int* err;               // device error word
+  int num_sms;
+  cudaStream_t stream;
+};
+
+// Defined in gemm_bf16.cu / gemm_s8.cu.
+cudaError_t launch_gemm_bf16(const GemmLaunch& g);
+cudaError_t launch_gemm_s8(const GemmLaunch& g);
+
+template <int BN, int EPI, bool S8, typename OutT>
+cudaError_t launch_gemm_inst(const GemmLaunch& g) {
+  using C = GemmCfg<BN, S8>;
+  auto kern = gemm_tc_kernel<BN, EPI, S8, OutT>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<uint64_t> attr_done{0};  // one bit per device
+  if (!(attr_done.load() & (1ull << (dev & 63)))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_done.fetch_or(1ull << (dev & 63));
+  }
+  const long tiles = (long)((g.M + C::kBM - 1) / C::kBM) * ((g.N + BN - 1) / BN);
+  if (tiles == 0) return cudaSuccess;
+  const int grid = (int)(tiles < g.num_sms ? tiles : g.num_sms);
+  kern<<<grid, C::kThreads, C::kSmemBytes, g.stream>>>(*g.ta, *g.tw, g.M, g.N, g.K, g.ep, g.err);
+  return cudaGetLastError();
+}
+
+template <bool S8, int BN>
+cudaError_t launch_gemm_bn(const GemmLaunch& g) {
+  using Bf = __nv_bfloat16;
+  if constexpr (!S8) {
+    switch (g.epi) {
+      case kEpiStore:
+        return g.out_f32 ? launch_gemm_inst<BN, kEpiStore, false, float>(g)
+                         : launch_gemm_inst<BN, kEpiStore, false, Bf>(g);
+      case kEpiGelu: return launch_gemm_inst<BN, kEpiGelu, false, Bf>(g);
+      case kEpiSwiglu:
+        if constexpr (BN != 192) return launch_gemm_inst<BN, kEpiSwiglu, false, Bf>(g);
+        else return cudaErrorInvalidValue;
+      case kEpiResid: return launch_gemm_inst<BN, kEpiResid, false, float>(g);
+    }
+  } else {
+    switch (g.epi) {
+      case kEpiStore:
+        return g.out_f32 ? launch_gemm_inst<BN, kEpiStore, true, float>(g)
+                         : launch_gemm_inst<BN, kEpiStore, true, Bf>(g);
+      case kEpiGelu: return launch_gemm_inst<BN, kEpiGelu, true, float>(g);
+      case kEpiSwiglu:
+        if constexpr (BN != 192) return launch_gemm_inst<BN, kEpiSwiglu, true, float>(g);
+        else return cudaErrorInvalidValue;
+      case kEpiResid: return launch_gemm_inst<BN, kEpiResid, true, float>(g);
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <bool S8>
+cudaError_t launch_gemm_any(const GemmLaunch& g) {
+  switch (g.bn) {
+    case 64: return launch_gemm_bn<S8, 64>(g);
+    case 128: return launch_gemm_bn<S8, 128>(g);
+    case 192: return launch_gemm_bn<S8, 192>(g);
+    case 256: return launch_gemm_bn<S8, 256>(g);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace futon

@@ -1,0 +1,341 @@
+// gemm_tc.cuh — tcgen05 tensor-core GEMM for sm_100a with fused epilogues.
+//
+// Computes the Kernel.MatMulT contract of futon (native/kernel.go:26-36):
+//     D[m, n] = Σ_k A[m, k] · W[n, k]  (+ bias[n])
+// with A row-major [M, K] (activations) and W row-major [N, K] (nn.Linear
+// layout, exactly how pack weights are stored), then applies one of the
+// layer epilogues of native/model.go:550-635 before the single store:
+//   kEpiStore   D + bias                               (qkv projection)
+//   kEpiGelu    gelu(D + bias)                         (fc1, model.go:610-616)
+//   kEpiSwiglu  (D_fc1 + b1) * silu(D_gate + b2)       (fc1‖gate, model.go:617-627)
+//   kEpiResid   (D + bias) + residual                  (out / fc2 before LayerNorm)
+// and, for the int8 path (native/quant.go:99-137), the exact rescale
+//   float32(sum_s32) * (scale_a[m] * scale_w[n]) + bias[n].
+//
+// Structure: one persistent CTA per SM, 6 warps.
+//   warp 0     TMA producer: 128-byte-swizzled K-major tiles of A (128 rows)
+//              and W (BN rows) into a STAGES-deep shared-memory ring.
+//   warp 1     allocates tensor memory; lane 0 issues tcgen05.mma
+//              (M=128, N=BN, K=16 bf16 / 32 s8 per instruction) into one of
+//              two TMEM accumulators and commits completion to mbarriers.
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator lane quarter the warp
+//              owns (one output row per thread), fused math, global store.
+// The two accumulators let the epilogue of tile i overlap the MMAs of tile
+// i+1. Tiles are visited n-fastest so CTAs running together share A tiles
+// through L2; the weights (≤ 19 MB) stay L2-resident.
+#pragma once
+
+#include "common.cuh"
+#include "mathf32.cuh"
+
+namespace futon {
+
+enum EpiKind : int { kEpiStore = 0, kEpiGelu = 1, kEpiSwiglu = 2, kEpiResid = 3 };
+
+struct EpiParams {
+  void* out;             // bf16 or f32 output, row stride ldo elements
+  int ldo;
+  const float* bias;     // [N] (interleaved like W for kEpiSwiglu) or null
+  const float* resid;    // kEpiResid: f32 [M, ldr]
+  int ldr;
+  const float* a_scale;  // int8 path: per-row activation scales [M]
+  const float* w_scale;  // int8 path: per-row weight scales [N]
+};
+
+template <int BN, bool S8>
+struct GemmCfg {
+  static constexpr int kBM = 128;
+  static constexpr int kRowBytes = 128;                       // one swizzle row
+  static constexpr int kBK = S8 ? 128 : 64;                   // elements per k-block
+  static constexpr int kABytes = kBM * kRowBytes;
+  static constexpr int kBBytes = BN * kRowBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (BN == 256) ? 4 : (BN == 192) ? 5 : (BN == 128) ? 6 : 8;
+  static constexpr uint32_t kAccStride = (BN <= 64) ? 64 : (BN <= 128) ? 128 : 256;
+  static constexpr uint32_t kTmemCols = 2 * kAccStride;       // power of two, ≤ 512
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kThreads = 192;
+};
+
+template <typename T> __device__ __forceinline__ void store32(T* dst, const float (&v)[32]);
+
+template <> __device__ __forceinline__ void store32<float>(float* dst, const float (&v)[32]) {
+  float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+template <> __device__ __forceinline__ void store32<__nv_bfloat16>(__nv_bfloat16* dst,
+                                                                   const float (&v)[32]) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 p = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+      w[j] = *reinterpret_cast<uint32_t*>(&p);
+    }
+    d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <typename T> __device__ __forceinline__ void store1(T* dst, float v);
+template <> __device__ __forceinline__ void store1<float>(float* dst, float v) { *dst = v; }
+template <> __device__ __forceinline__ void store1<__nv_bfloat16>(__nv_bfloat16* dst, float v) {
+  *dst = __float2bfloat16_rn(v);
+}
+
+// Accumulator word → f32 value before the activation: f32 sum + bias, or the
+// int8 rescale float32(sum) * (sA * sW) + bias (quant.go:132-135).
+template <bool S8>
+__device__ __forceinline__ float acc_value(uint32_t u, float a_s, const EpiParams& ep, int col) {
+  float v;
+  if constexpr (S8) {
+    v = fmul((float)(int32_t)u, fmul(a_s, ep.w_scale[col]));
+  } else {
+    v = __uint_as_float(u);
+  }
+  if (ep.bias) v = fadd(v, ep.bias[col]);
+  return v;
+}
+
+// One tile's epilogue for one thread (= one output row).
+template <int BN, int EPI, bool S8, typename OutT>
+__device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int N, int nb,
+                                             const EpiParams& ep) {
+  const bool row_ok = row < M;
+  const float a_s = (S8 && row_ok) ? ep.a_scale[row] : 0.0f;
+  OutT* out = reinterpret_cast<OutT*>(ep.out);
+  if constexpr (EPI == kEpiSwiglu) {
+    constexpr int kHalf = BN / 2;
+    const int wcol0 = nb * BN;            // interleaved weight/bias column of this tile
+    const int ocol0 = nb * kHalf;         // output column of this tile
+    const bool full = (nb + 1) * BN <= N;
+#pragma unroll 1
+    for (int c = 0; c < kHalf; c += 32) {
+      uint32_t u[32], g[32];
+      tmem_ld32(taddr + c, u);
+      tmem_ld32(taddr + kHalf + c, g);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        int wc = wcol0 + c + i;
+        bool ok = full || (wc + kHalf < N);
+        float h = ok ? acc_value<S8>(u[i], a_s, ep, wc) : 0.0f;
+        float gg = ok ? acc_value<S8>(g[i], a_s, ep, wc + kHalf) : 0.0f;
+        v[i] = fmul(h, fmul(gg, sigmoid_f32(gg)));
+      }
+      if (row_ok) {
+        OutT* dst = out + (size_t)row * ep.ldo + ocol0 + c;
+        if (full) {
+          store32<OutT>(dst, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (wcol0 + c + i + kHalf < N) store1<OutT>(dst + i, v[i]);
+        }
+      }
+    }
+  } else {
+    const int col0 = nb * BN;
+    const bool full = col0 + BN <= N;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t u[32];
+      tmem_ld32(taddr + c, u);
+      tmem_ld_wait();
+      const int col = col0 + c;
+      float v[32];
+      if (full || col + 32 <= N) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = acc_value<S8>(u[i], a_s, ep, col + i);
+          if constexpr (EPI == kEpiGelu) x = gelu_f32(x);
+          if constexpr (EPI == kEpiResid) {
+            if (row_ok) x = fadd(x, ep.resid[(size_t)row * ep.ldr + col + i]);
+          }
+          v[i] = x;
+        }
+        if (row_ok) store32<OutT>(out + (size_t)row * ep.ldo + col, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (col + i < N && row_ok) {
+            float x = acc_value<S8>(u[i], a_s, ep, col + i);
+            if constexpr (EPI == kEpiGelu) x = gelu_f32(x);
+            if constexpr (EPI == kEpiResid) x = fadd(x, ep.resid[(size_t)row * ep.ldr + col + i]);
+            store1<OutT>(out + (size_t)row * ep.ldo + col + i, x);
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int BN, int EPI, bool S8, typename OutT>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   int M, int N, int K, EpiParams ep, int* err) {
+  using C = GemmCfg<BN, S8>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full_bar = bars;                       // [kStages] TMA → MMA
+  uint64_t* empty_bar = bars + C::kStages;         // [kStages] MMA → TMA
+  uint64_t* accf_bar = bars + 2 * C::kStages;      // [2] MMA → epilogue
+  uint64_t* acce_bar = accf_bar + 2;               // [2] epilogue → MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + C::kBM - 1) / C::kBM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_k = (K + C::kBK - 1) / C::kBK;
+  const int num_tiles = num_m * num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&accf_bar[a]), 1);
+      mbar_init(smem_u32(&acce_bar[a]), 4);  // one arrive per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int mb = tile / num_n, nb = tile % num_n;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u, err, kDevTimeoutSmemEmpty,
+                                 abort_flag))
+            goto producer_done;
+          uint8_t* sa = smem + stage * C::kStageBytes;
+          uint8_t* sb = sa + C::kABytes;
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          tma_load_2d(smem_u32(sa), &tmA, fb, kb * C::kBK, mb * C::kBM);
+          tma_load_2d(smem_u32(sb), &tmW, fb, kb * C::kBK, nb * BN);
+          ++issued;
+          if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+    producer_done:
+      // Drain: make sure this thread's own copies have landed before exit.
+      {
+        int n = issued < C::kStages ? issued : C::kStages;
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < n; ++i) {
+          if (--s < 0) { s = C::kStages - 1; ph ^= 1u; }
+          uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(smem_u32(&full_bar[s]), ph)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = make_idesc(S8 ? 2u : 1u, 1u, 128u, (uint32_t)BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+        if (!mbar_wait_bounded(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, err, kDevTimeoutAccEmpty,
+                               abort_flag))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::kAccStride;
+        bool ok = true;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&full_bar[stage]), phase, err, kDevTimeoutTmaFull,
+                                 abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* sa = smem + stage * C::kStageBytes;
+          const uint64_t adesc = smem_desc_k_sw128(smem_u32(sa));
+          const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sa + C::kABytes));
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            // +32 bytes along K inside the 128-byte swizzle row (encoded >> 4).
+            const uint64_t koff = (uint64_t)(ks * 2);
+            if constexpr (S8)
+              mma_s8(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
+            else
+              mma_bf16(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
+          }
+          mma_commit(smem_u32(&empty_bar[stage]));
+          if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+        }
+        mma_commit(smem_u32(&accf_bar[acc]));
+        if (!ok) break;
+      }
+      // Drain: wait (bounded) for the last committed MMAs before TMEM is freed.
+      if (it > 0) {
+        const int acc = (it - 1) & 1;
+        const uint32_t acc_phase = (uint32_t)((it - 1) >> 1) & 1u;
+        uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(smem_u32(&accf_bar[acc]), acc_phase)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 ----------------
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+      if (!mbar_wait_bounded(smem_u32(&accf_bar[acc]), acc_phase, err, kDevTimeoutAccFull,
+                             abort_flag))
+        break;
+      tc_fence_after();
+      const int mb = tile / num_n, nb = tile % num_n;
+      const int row = mb * C::kBM + quarter * 32 + lane;
+      const uint32_t taddr = tmem_base + acc * C::kAccStride + ((uint32_t)(quarter * 32) << 16);
+      epilogue_row<BN, EPI, S8, OutT>(taddr, row, M, N, nb, ep);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+}  // namespace futon

@@ -1,0 +1,76 @@
+// mathf32.cuh — device versions of futon's float32 transcendentals.
+//
+// Restates native/mathf32.go:40-124 (futon, MIT): expF32 is Cephes' single-
+// precision exp (range reduction k·ln2 + r, minimax polynomial, scale by
+// 2^k); erfcPos is the Numerical Recipes erfcc Chebyshev fit; geluF32 is the
+// exact-erf GELU evaluated through erfc; sigmoidF32 is 1/(1+e^-x) with the
+// reference's clamps. Every multiply and add is a separately rounded f32 op
+// (__fmul_rn / __fadd_rn), the evaluation the Go source has on amd64, so the
+// device activations equal the CPU oracle's bit for bit.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace futon {
+
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+
+constexpr float kExpOverflowF32 = 88.72283f;   // ln(MaxFloat32)
+constexpr float kExpUnderflowF32 = -87.33654f; // ln(2^-126)
+constexpr float kExpClampLo = -104.0f;
+
+__device__ __forceinline__ float exp_f32(float x) {
+  if (x < kExpUnderflowF32) return 0.0f;
+  float kf = fsub(fadd(fmul(x, 1.4426950408889634f), 12582912.0f), 12582912.0f);
+  int32_t k = (int32_t)kf;
+  float r = fsub(x, fmul(kf, 0.693145751953125f));
+  r = fsub(r, fmul(kf, 1.428606820309417e-06f));
+  float p = 1.9875691500e-4f;
+  p = fadd(fmul(p, r), 1.3981999507e-3f);
+  p = fadd(fmul(p, r), 8.3334519073e-3f);
+  p = fadd(fmul(p, r), 4.1665795894e-2f);
+  p = fadd(fmul(p, r), 1.6666665459e-1f);
+  p = fadd(fmul(p, r), 5.0000001201e-1f);
+  p = fadd(fmul(fadd(fmul(p, r), 1.0f), r), 1.0f);
+  int32_t e = k + 127;
+  if (e <= 0) return 0.0f;
+  if (e >= 255) return fmul(fmul(p, __int_as_float((e - 1) << 23)), 2.0f);
+  return fmul(p, __int_as_float(e << 23));
+}
+
+__device__ __forceinline__ float erfc_pos_f32(float a) {
+  float t = __fdiv_rn(1.0f, fadd(1.0f, fmul(0.5f, a)));
+  float p = 0.17087277f;
+  p = fsub(fmul(p, t), 0.82215223f);
+  p = fadd(fmul(p, t), 1.48851587f);
+  p = fsub(fmul(p, t), 1.13520398f);
+  p = fadd(fmul(p, t), 0.27886807f);
+  p = fsub(fmul(p, t), 0.18628806f);
+  p = fadd(fmul(p, t), 0.09678418f);
+  p = fadd(fmul(p, t), 0.37409196f);
+  p = fadd(fmul(p, t), 1.00002368f);
+  p = fsub(fmul(p, t), 1.26551223f);
+  float e = fsub(p, fmul(a, a));
+  if (e < kExpClampLo) e = kExpClampLo;
+  return fmul(t, exp_f32(e));
+}
+
+__device__ __forceinline__ float gelu_f32(float x) {
+  float a = fmul(x, 0.7071067811865476f);
+  if (a < 0) a = -a;
+  float c = erfc_pos_f32(a);
+  if (x < 0) return fmul(fmul(0.5f, x), c);
+  return fmul(fmul(0.5f, x), fsub(2.0f, c));
+}
+
+__device__ __forceinline__ float sigmoid_f32(float x) {
+  float e = -x;
+  if (e < kExpClampLo) e = kExpClampLo;
+  if (e > kExpOverflowF32) return 0.0f;
+  return __fdiv_rn(1.0f, fadd(1.0f, exp_f32(e)));
+}
+
+}  // namespace futon

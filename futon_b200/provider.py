@@ -1,0 +1,292 @@
+"""Python mirror of futon's native Provider over libfuton_cuda.
+
+Same names, argument meaning and error behaviour as the Go surface
+(native/provider.go:36-290, native/model.go:112-457):
+
+  Model.load(pack_dir)            LoadModel: manifest + config + tensors,
+                                  uploaded once per device (one replica each)
+  Model.encode_tokens(ids, dim)   EncodeTokens for one sequence
+  Model.encode_packed(ids, cu)    many sequences in one call (packed, no padding)
+  Provider(Options(...))          New: pack load + Dimensions validation
+  Provider.embed_ids / embed_batch_ids / dimensions / model_name /
+  is_available / close
+
+Text tokenisation stays with the caller (the reference keeps its WordPiece
+tokenizer in Go on the host); these entry points take token ids.
+Errors carry the reference's "native:" messages; a raised cancel flag
+surfaces as CanceledError. There is no CPU path: every forward runs the
+CUDA kernels in libfuton_cuda.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+import threading
+from typing import Dict, Iterable, List, Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import CanceledError, FutonError
+from .pack import (ACT_SWIGLU, POOL_MEAN, POS_ROPE, PackConfig, PackError, load_pack)
+
+NATIVE_MODEL_NAME_PREFIX = "native/"
+ENV_NATIVE_Q8 = "FUTON_NATIVE_Q8"
+
+
+class CancelFlag:
+    """A cancellation flag the library polls between micro-batches and layers
+    (the GPU counterpart of the reference's context checkpoints)."""
+
+    def __init__(self) -> None:
+        self._v = C.c_int(0)
+
+    def cancel(self) -> None:
+        self._v.value = 1
+
+    def is_set(self) -> bool:
+        return self._v.value != 0
+
+    @property
+    def ptr(self) -> int:
+        return C.addressof(self._v)
+
+
+def _cfg_struct(cfg: PackConfig) -> _lib.FutonCfg:
+    c = _lib.FutonCfg()
+    c.hidden_size = cfg.hidden_size
+    c.num_layers = cfg.num_layers
+    c.num_heads = cfg.num_heads
+    c.intermediate_size = cfg.intermediate_size
+    c.vocab_size = cfg.vocab_size
+    c.type_vocab_size = cfg.type_vocab_size
+    c.max_seq_len = cfg.max_seq_len
+    c.max_trained_positions = cfg.max_trained_positions
+    c.layer_norm_eps = cfg.layer_norm_eps
+    c.position_encoding = _lib.POS_ROPE if cfg.position_encoding == POS_ROPE else _lib.POS_ABSOLUTE
+    c.rope_theta = cfg.rope_theta
+    c.activation = _lib.ACT_SWIGLU if cfg.activation == ACT_SWIGLU else _lib.ACT_GELU
+    c.pooling = _lib.POOL_MEAN if cfg.pooling == POOL_MEAN else _lib.POOL_CLS
+    c.normalize = 1 if cfg.normalize else 0
+    c.matryoshka = 1 if cfg.matryoshka is not None else 0
+    c.matryoshka_layernorm = 1 if (cfg.matryoshka is not None and cfg.matryoshka.layernorm) else 0
+    return c
+
+
+def pack_ids(seqs: Sequence[Sequence[int]]) -> tuple:
+    """Packs id sequences into (ids int32 [Σ L], cu_seqlens int32 [n+1])."""
+    lens = np.fromiter((len(s) for s in seqs), dtype=np.int64, count=len(seqs))
+    cu = np.zeros(len(seqs) + 1, dtype=np.int32)
+    np.cumsum(lens, out=cu[1:])
+    ids = (np.concatenate([np.asarray(s, dtype=np.int32) for s in seqs])
+           if len(seqs) else np.zeros(0, dtype=np.int32))
+    return np.ascontiguousarray(ids, dtype=np.int32), cu
+
+
+class Model:
+    """A pack uploaded to one or more GPUs (LoadModel + newModel)."""
+
+    def __init__(self, cfg: PackConfig, tensors: Dict[str, np.ndarray],
+                 devices: Optional[Sequence[int]] = None, q8: Optional[bool] = None):
+        cfg.validate()
+        if q8 is None:
+            q8 = _lib.env_flag(ENV_NATIVE_Q8)
+        ndev = _lib.device_count()
+        if devices is None:
+            devices = list(range(ndev))
+        devices = list(devices)
+        if not devices:
+            raise FutonError(_lib.FUTON_EINVAL, "native: no CUDA device visible")
+        self.cfg = cfg
+        self.q8 = bool(q8)
+        self.devices = devices
+        keep = []
+        arr = (_lib.FutonTensor * max(1, len(tensors)))()
+        for i, name in enumerate(sorted(tensors)):
+            t = tensors[name]
+            if t.dtype == np.float16:
+                dt = _lib.DTYPE_F16
+            else:
+                t = np.ascontiguousarray(t, dtype=np.float32)
+                dt = _lib.DTYPE_F32
+            t = np.ascontiguousarray(t)
+            keep.append(t)
+            if t.ndim < 1 or t.ndim > 4:
+                raise PackError(f"pack {cfg.model_id}: tensor {name!r} rank {t.ndim}")
+            arr[i].name = name.encode()
+            arr[i].dtype = dt
+            arr[i].ndim = t.ndim
+            for k, s in enumerate(t.shape):
+                arr[i].shape[k] = s
+            arr[i].data = t.ctypes.data
+        devs = (C.c_int * len(devices))(*devices)
+        handle = C.c_void_p()
+        cs = _cfg_struct(cfg)
+        _lib.call("futon_cuda_model_create", C.byref(cs), arr, len(tensors), devs, len(devices),
+                  1 if self.q8 else 0, C.byref(handle))
+        self._h = handle
+        self._closed = False
+        self._mu = threading.Lock()
+
+    @classmethod
+    def load(cls, pack_dir, devices=None, q8=None) -> "Model":
+        p = load_pack(pack_dir, keep_f16=True)
+        return cls(p.cfg, p.tensors, devices=devices, q8=q8)
+
+    # -- lifecycle --------------------------------------------------------
+    def close(self) -> None:
+        with self._mu:
+            if not self._closed and self._h:
+                _lib.lib().futon_cuda_model_destroy(self._h)
+            self._closed = True
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self) -> C.c_void_p:
+        if self._closed:
+            raise FutonError(_lib.FUTON_EINVAL, "native: model is closed")
+        return self._h
+
+    def effective_max_seq_len(self) -> int:
+        return self.cfg.effective_max_seq_len()
+
+    def out_width(self, out_dim: int) -> int:
+        return out_dim if out_dim else self.cfg.hidden_size
+
+    # -- forward ----------------------------------------------------------
+    def encode_packed(self, ids: np.ndarray, cu_seqlens: np.ndarray, out_dim: int = 0,
+                      device: int = 0, cancel: Optional[CancelFlag] = None) -> np.ndarray:
+        """[nseq, dim] vectors for packed sequences on device index `device`."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        nseq = len(cu) - 1
+        out = np.empty((max(nseq, 0), self.out_width(out_dim)), dtype=np.float32)
+        _lib.call("futon_cuda_encode", self.handle, device, ids.ctypes.data, cu.ctypes.data, nseq,
+                  out_dim, out.ctypes.data, cancel.ptr if cancel else None)
+        return out
+
+    def encode_batch(self, ids: np.ndarray, cu_seqlens: np.ndarray, out_dim: int = 0,
+                     cancel: Optional[CancelFlag] = None) -> np.ndarray:
+        """Data-parallel over every device of the model (EmbedBatch's engine)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        nseq = len(cu) - 1
+        out = np.empty((max(nseq, 0), self.out_width(out_dim)), dtype=np.float32)
+        _lib.call("futon_cuda_encode_batch", self.handle, ids.ctypes.data, cu.ctypes.data, nseq,
+                  out_dim, out.ctypes.data, cancel.ptr if cancel else None)
+        return out
+
+    def encode_tokens(self, ids: Sequence[int], out_dim: int = 0, device: int = 0,
+                      cancel: Optional[CancelFlag] = None) -> np.ndarray:
+        """EncodeTokens (model.go:335-457) for one id sequence."""
+        ids = np.asarray(ids, dtype=np.int64)
+        if ids.size == 0:
+            raise FutonError(_lib.FUTON_EINVAL, "native: empty token sequence")
+        if ids.min() < np.iinfo(np.int32).min or ids.max() > np.iinfo(np.int32).max:
+            raise FutonError(_lib.FUTON_EINVAL, "native: token id outside vocab")
+        cu = np.array([0, ids.size], dtype=np.int32)
+        return self.encode_packed(ids.astype(np.int32), cu, out_dim, device, cancel)[0]
+
+    def encode_device(self, d_ids: int, cu_seqlens: np.ndarray, out_dim: int, d_out: int,
+                      device: int = 0, stream: Optional[int] = None) -> None:
+        """Queues a forward over ids already in HBM (returns without waiting)."""
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        _lib.call("futon_cuda_encode_device", self.handle, device, C.c_void_p(d_ids),
+                  cu.ctypes.data, len(cu) - 1, out_dim, C.c_void_p(d_out),
+                  C.c_void_p(stream) if stream else None)
+
+    def sync(self, device: int = 0, stream: Optional[int] = None) -> None:
+        _lib.call("futon_cuda_sync", self.handle, device, C.c_void_p(stream) if stream else None)
+
+    def launch_count(self, device: int = 0) -> int:
+        return int(_lib.lib().futon_cuda_launch_count(self.handle, device))
+
+
+@dataclasses.dataclass
+class Options:
+    """native.Options (provider.go:55-65) plus the GPU selection."""
+
+    pack_dir: str = ""
+    dimensions: int = 0
+    devices: Optional[List[int]] = None  # None = every visible GPU
+    q8: Optional[bool] = None            # None = FUTON_NATIVE_Q8 == "1"
+
+
+class Provider:
+    """native.Provider over the B200 engine (provider.go:36-290)."""
+
+    def __init__(self, opts: Options):
+        if not opts.pack_dir:
+            raise FutonError(_lib.FUTON_EINVAL,
+                             "native: PackDir is required (no downloading in this phase)")
+        self.model = Model.load(opts.pack_dir, devices=opts.devices, q8=opts.q8)
+        cfg = self.model.cfg
+        dims = opts.dimensions or cfg.hidden_size
+        if dims != cfg.hidden_size:
+            if cfg.matryoshka is None:
+                self.model.close()
+                raise FutonError(_lib.FUTON_EINVAL, f"native: pack {cfg.model_id} does not "
+                                 f"support truncation to {dims} dimensions")
+            if dims < 1 or dims > cfg.hidden_size:
+                self.model.close()
+                raise FutonError(_lib.FUTON_EINVAL,
+                                 f"native: dimensions {dims} outside [1,{cfg.hidden_size}]")
+        self._dims = dims
+        self._mu = threading.Lock()
+        self._closed = False
+
+    def _check_open(self) -> None:
+        with self._mu:
+            if self._closed:
+                raise FutonError(_lib.FUTON_EINVAL, "native: provider is closed")
+
+    def _clamp(self, ids: Sequence[int]) -> List[int]:
+        return list(ids)
+
+    def embed_ids(self, ids: Sequence[int], cancel: Optional[CancelFlag] = None) -> np.ndarray:
+        """Embed for pre-tokenised input (provider.go:115-121)."""
+        self._check_open()
+        return self.model.encode_tokens(ids, self._dims, cancel=cancel)
+
+    def embed_batch_ids(self, batch: Sequence[Sequence[int]],
+                        cancel: Optional[CancelFlag] = None) -> np.ndarray:
+        """EmbedBatch (provider.go:152-202): index-aligned [n, dims] vectors,
+        sharded across every GPU; the first error fails the batch."""
+        self._check_open()
+        if len(batch) == 0:
+            return np.zeros((0, self._dims), dtype=np.float32)
+        for i, s in enumerate(batch):
+            if len(s) == 0:
+                raise FutonError(_lib.FUTON_EINVAL,
+                                 f"native: batch item {i}: native: empty token sequence")
+        ids, cu = pack_ids(batch)
+        return self.model.encode_batch(ids, cu, self._dims, cancel=cancel)
+
+    def dimensions(self) -> int:
+        return self._dims
+
+    def model_name(self) -> str:
+        """Engine-qualified pack id (provider.go:261-264)."""
+        return NATIVE_MODEL_NAME_PREFIX + self.model.cfg.model_id
+
+    def is_available(self) -> bool:
+        with self._mu:
+            return not self._closed
+
+    def close(self) -> None:
+        with self._mu:
+            if self._closed:
+                return
+            self._closed = True
+        self.model.close()
+
+
+def new(opts: Options) -> Provider:
+    """native.New."""
+    return Provider(opts)

@@ -1,0 +1,57 @@
+"""Shared fixtures for the futon_b200 test suite.
+
+Markers: `gpu` tests need a CUDA device and call libfuton_cuda through its
+C ABI; everything else runs on the CPU (oracle, pack host logic, ABI
+loading, gloo multi-process planning).
+"""
+from __future__ import annotations
+
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+GOLDEN = ROOT / "tests" / "golden" / "toy"
+
+# Reference gates (native/model_test.go:19-22) for the CPU oracle, and the
+# north-star gate for the bf16 tensor-core path.
+TOY_COSINE_MIN = 0.99999
+TOY_ABS_TOL = 2e-4
+GPU_COSINE_MIN = 0.9999
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and libfuton_cuda")
+
+
+def cosine(a, b) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def row_cosines(a, b) -> np.ndarray:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1))
+
+
+@pytest.fixture(scope="session")
+def toy_expected():
+    return json.loads((GOLDEN / "expected.json").read_text())
+
+
+@pytest.fixture(scope="session")
+def gpu():
+    """Asserts a CUDA device and the built library are present (no skip: a
+    GPU test that cannot reach the kernels must fail loudly)."""
+    import futon_b200
+    n = futon_b200.device_count()
+    assert n > 0, "no CUDA device visible to libfuton_cuda"
+    return n

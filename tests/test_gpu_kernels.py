@@ -1,0 +1,94 @@
+"""GPU unit parity for the kernel seam (Kernel.MatMulT, MatMulTQ8,
+quantizeRowQ8) through the C ABI, mirroring native/kernel_test.go and
+native/quant_test.go."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from futon_b200 import _lib
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def naive_matmul_t(a, b, bias):
+    out = a.astype(np.float64) @ b.astype(np.float64).T
+    if bias is not None:
+        out += bias.astype(np.float64)
+    return out
+
+
+# bf16 operands (8-bit mantissa): |err| ≤ 2·2^-9·Σ|a||b| per element, and
+# f32 accumulation noise below that; the test bounds by 1e-2 relative to the
+# magnitude sum.
+@pytest.mark.parametrize("m,n,k", [(1, 8, 8), (3, 4, 16), (7, 16, 32), (13, 29, 64),
+                                   (128, 128, 128), (130, 200, 384), (257, 1152, 384),
+                                   (300, 384, 1536), (64, 6144, 768)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_matmul_t(gpu, m, n, k, with_bias):
+    import torch
+    rng = np.random.default_rng(m * 1000 + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((n, k)).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32) if with_bias else None
+    da, db = _dev(a), _dev(b)
+    dbias = _dev(bias) if with_bias else None
+    dout = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    _lib.call("futon_cuda_matmul_t", 0, dout.data_ptr(), da.data_ptr(), db.data_ptr(), m, n, k,
+              dbias.data_ptr() if with_bias else None, None)
+    got = dout.cpu().numpy().astype(np.float64)
+    want = naive_matmul_t(a, b, bias)
+    mag = np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64).T
+    assert np.all(np.abs(got - want) <= 1e-2 * mag + 1e-5), np.abs(got - want).max()
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 16), (2, 3, 32), (5, 9, 64), (13, 29, 128),
+                                   (200, 384, 384), (129, 256, 1536), (300, 2304, 768)])
+def test_matmul_t_q8_bit_exact(gpu, m, n, k):
+    """Q8 GEMM equals the reference scheme bit for bit: same activation
+    codes, exact s32 dots, float32(sum)·(sA·sB) + bias (quant.go:99-137)."""
+    import torch
+    rng = np.random.default_rng(17 + m + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    w = rng.standard_normal((n, k)).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    qb, sb = O.quantize_rows_q8(w)
+    want = O.matmul_t_q8(a, qb, sb, bias)
+    dout = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    _lib.call("futon_cuda_matmul_t_q8", 0, dout.data_ptr(), _dev(a).data_ptr(),
+              _dev(qb).data_ptr(), _dev(sb).data_ptr(), m, n, k, _dev(bias).data_ptr(), None)
+    got = dout.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.abs(got - want).max()
+
+
+@pytest.mark.parametrize("rows,k", [(1, 4), (3, 257 * 4), (100, 384), (64, 3072)])
+def test_quantize_rows_bit_exact(gpu, rows, k):
+    import torch
+    rng = np.random.default_rng(rows + k)
+    x = rng.standard_normal((rows, k)).astype(np.float32)
+    x[0, :] = 0.0  # all-zero row: scale 0, zero codes
+    if rows > 2:
+        x[1, :4] = [0.5, -0.5, 1.5, -2.5]  # halfway cases
+    qw, sw = O.quantize_rows_q8(x)
+    dq = torch.empty((rows, k), dtype=torch.int8, device="cuda")
+    ds = torch.empty(rows, dtype=torch.float32, device="cuda")
+    _lib.call("futon_cuda_quantize_rows_q8", 0, dq.data_ptr(), ds.data_ptr(), _dev(x).data_ptr(),
+              rows, k, None)
+    assert np.array_equal(dq.cpu().numpy(), qw)
+    assert np.array_equal(ds.cpu().numpy().view(np.uint32), sw.view(np.uint32))
+    assert (dq.cpu().numpy() != -128).all()
+
+
+def test_seam_rejects_bad_shapes(gpu):
+    with pytest.raises(_lib.FutonError):
+        _lib.call("futon_cuda_matmul_t", 0, None, None, None, 4, 4, 7, None, None)
+    with pytest.raises(_lib.FutonError):
+        _lib.call("futon_cuda_matmul_t_q8", 0, None, None, None, None, 4, 4, 8, None, None)

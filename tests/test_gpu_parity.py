@@ -1,0 +1,247 @@
+"""GPU parity: libfuton_cuda (through its C ABI) against the CPU oracle, the
+reference's golden vectors and the pinned torch restatement.
+
+Gate for the bf16 tensor-core path: per-vector cosine ≥ 0.9999 against the
+reference algorithm and unit-norm outputs (|‖v‖ − 1| ≤ 1e-5).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, GPU_COSINE_MIN, cosine, row_cosines
+from futon_b200 import CancelFlag, CanceledError, FutonError, Model, synth
+from futon_b200.pack import load_pack
+from oracle.oracle import GEMM_AVX2, GEMM_GO, OracleModel, has_avx2
+
+pytestmark = pytest.mark.gpu
+NORM_TOL = 1e-5
+_models = {}
+
+
+def oracle_mode():
+    return GEMM_AVX2 if has_avx2() else GEMM_GO
+
+
+def synth_model(arch: str, q8: bool = False):
+    key = (arch, q8)
+    if key not in _models:
+        cfg = synth.arch(arch)
+        w = synth.make_weights(cfg)
+        _models[key] = (cfg, w, Model(cfg, w, devices=[0], q8=q8))
+    return _models[key]
+
+
+def assert_parity(got, want, label, cos_min=GPU_COSINE_MIN):
+    cs = row_cosines(got, want)
+    norms = np.linalg.norm(got, axis=1)
+    assert cs.min() >= cos_min, f"{label}: min cosine {cs.min():.7f} < {cos_min} (mean {cs.mean():.7f})"
+    assert np.abs(norms - 1).max() <= NORM_TOL, f"{label}: norm off by {np.abs(norms - 1).max():.2e}"
+    return cs
+
+
+# ---------------------------------------------------------------------------
+# Reference golden vectors (native/testdata/toy/expected.json)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("pack", ["toy-absolute-gelu", "toy-rope-swiglu"])
+def test_toy_golden(gpu, toy_expected, pack):
+    p = load_pack(GOLDEN / pack)
+    m = Model(p.cfg, p.tensors, devices=[0], q8=False)
+    pexp = toy_expected["packs"][pack]
+    worst = 1.0
+    for c in pexp["forward_cases"]:
+        got = m.encode_tokens(c["ids"])
+        want = np.asarray(c["vector"], np.float32)
+        worst = min(worst, cosine(got, want))
+        assert cosine(got, want) >= GPU_COSINE_MIN, (pack, len(c["ids"]), cosine(got, want))
+        assert np.abs(got - want).max() <= 5e-3
+    for c in pexp.get("matryoshka_cases", []):
+        got = m.encode_tokens(c["ids"], c["dim"])
+        assert got.shape == (c["dim"],)
+        assert cosine(got, np.asarray(c["vector"], np.float32)) >= GPU_COSINE_MIN
+    for c in pexp.get("text_cases", []):
+        got = m.encode_tokens(c["ids"])
+        assert cosine(got, np.asarray(c["vector"], np.float32)) >= GPU_COSINE_MIN
+    m.close()
+
+
+def test_toy_golden_packed(gpu, toy_expected):
+    """All forward cases of a pack in ONE packed call match the goldens."""
+    for pack in ("toy-absolute-gelu", "toy-rope-swiglu"):
+        p = load_pack(GOLDEN / pack)
+        m = Model(p.cfg, p.tensors, devices=[0])
+        cases = toy_expected["packs"][pack]["forward_cases"]
+        from futon_b200 import pack_ids
+        ids, cu = pack_ids([c["ids"] for c in cases])
+        got = m.encode_packed(ids, cu)
+        want = np.stack([np.asarray(c["vector"], np.float32) for c in cases])
+        assert_parity(got, want, pack)
+        m.close()
+
+
+# ---------------------------------------------------------------------------
+# Benchmark configurations vs the oracle
+# ---------------------------------------------------------------------------
+def test_c0_full_vs_oracle(gpu):
+    cfg, w, m = synth_model("bge")
+    ids, cu = synth.make_inputs("c0")
+    got = m.encode_packed(ids, cu)
+    want = OracleModel(cfg, w, gemm=oracle_mode()).encode_batch(ids, cu)
+    cs = assert_parity(got, want, "c0")
+    print(f"c0 min cos {cs.min():.7f} mean {cs.mean():.7f}")
+
+
+def test_c1_subset_vs_oracle(gpu):
+    cfg, w, m = synth_model("minilm6")
+    ids, cu = synth.make_inputs("c1", nseq=32)
+    got = m.encode_packed(ids, cu)
+    want = OracleModel(cfg, w, gemm=oracle_mode()).encode_batch(ids, cu)
+    assert_parity(got, want, "c1")
+
+
+@pytest.mark.parametrize("dim", [768, 256, 64])
+def test_c2_subset_vs_oracle(gpu, dim):
+    cfg, w, m = synth_model("nomic")
+    ids, cu = synth.make_inputs("c2", nseq=6)
+    got = m.encode_packed(ids, cu, out_dim=dim)
+    assert got.shape == (6, dim)
+    want = OracleModel(cfg, w, gemm=oracle_mode()).encode_batch(ids, cu, out_dim=dim)
+    assert_parity(got, want, f"c2/{dim}")
+
+
+@pytest.mark.parametrize("q8", [False, True])
+def test_c3_short_vs_oracle(gpu, q8):
+    """arctic shape (RoPE, SwiGLU, CLS) at L=256 against the oracle, both
+    the f32-weight path and the Q8 path (oracle requantises like model.go)."""
+    cfg, w, m = synth_model("arctic", q8=q8)
+    rng = np.random.default_rng(5)
+    lens = [256, 200]
+    seqs = [np.concatenate([[101], rng.integers(1000, cfg.vocab_size, L - 2), [102]]) for L in lens]
+    from futon_b200 import pack_ids
+    ids, cu = pack_ids(seqs)
+    got = m.encode_packed(ids, cu)
+    want = OracleModel(cfg, w, q8=q8, gemm=oracle_mode()).encode_batch(ids, cu)
+    assert_parity(got, want, f"c3 q8={q8}")
+
+
+def test_c4_subset_vs_oracle(gpu):
+    cfg, w, m = synth_model("bge")
+    ids, cu = synth.make_inputs("c4", nseq=96)
+    got = m.encode_packed(ids, cu)
+    want = OracleModel(cfg, w, gemm=oracle_mode()).encode_batch(ids, cu)
+    assert_parity(got, want, "c4-subset")
+
+
+# ---------------------------------------------------------------------------
+# Full-size: c3 at L=2048 vs the pinned torch restatement (fp32 on the GPU)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("q8", [False, True])
+def test_c3_full_vs_torch(gpu, q8):
+    import torch
+    from torch_ref import TorchRef
+    torch.backends.cuda.matmul.allow_tf32 = False
+    cfg, w, m = synth_model("arctic", q8=q8)
+    ids, cu = synth.make_inputs("c3")
+    got = m.encode_packed(ids, cu)
+    ref = TorchRef(cfg, w, device="cuda", q8=q8)
+    want = ref.encode_packed(ids, cu)
+    del ref
+    torch.cuda.empty_cache()
+    assert_parity(got, want, f"c3-full q8={q8}")
+
+
+# ---------------------------------------------------------------------------
+# Invariants: batch ≡ single, determinism, device-resident entry point
+# ---------------------------------------------------------------------------
+def test_batch_matches_single_bitwise(gpu):
+    """Packing never perturbs a sequence (no padding, no cross-sequence
+    reduction): each vector of a packed call equals its single-sequence call."""
+    cfg, w, m = synth_model("bge")
+    ids, cu = synth.make_inputs("c4", nseq=40, seed=3)
+    batch = m.encode_packed(ids, cu)
+    for i in range(len(cu) - 1):
+        single = m.encode_tokens(ids[cu[i]:cu[i + 1]])
+        assert np.array_equal(single, batch[i]), f"sequence {i} differs"
+
+
+def test_deterministic_runs(gpu):
+    cfg, w, m = synth_model("nomic")
+    ids, cu = synth.make_inputs("c2", nseq=8, seed=4)
+    a = m.encode_packed(ids, cu, out_dim=256)
+    b = m.encode_packed(ids, cu, out_dim=256)
+    assert np.array_equal(a, b)
+
+
+def test_encode_device_matches_host(gpu):
+    import torch
+    cfg, w, m = synth_model("bge")
+    ids, cu = synth.make_inputs("c4", nseq=300, seed=7)
+    host = m.encode_packed(ids, cu)
+    d_ids = torch.from_numpy(ids).cuda()
+    d_out = torch.empty((len(cu) - 1, cfg.hidden_size), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    m.encode_device(d_ids.data_ptr(), cu, 0, d_out.data_ptr(),
+                    stream=torch.cuda.current_stream().cuda_stream)
+    m.sync(stream=torch.cuda.current_stream().cuda_stream)
+    assert np.array_equal(d_out.cpu().numpy(), host)
+    assert m.launch_count() > 0
+
+
+def test_micro_batching_large_call(gpu):
+    """A call larger than one micro-batch (131,072 tokens) splits without
+    changing any vector."""
+    cfg, w, m = synth_model("bge")
+    ids, cu = synth.make_inputs("c4", nseq=2000, seed=9)
+    big = np.concatenate([ids] * 1)
+    full = m.encode_packed(big, cu)
+    # re-encode a slice that crosses no boundary and compare
+    sub = m.encode_packed(ids[cu[100]:cu[140]], cu[100:141] - cu[100])
+    assert np.array_equal(full[100:140], sub)
+    n = np.linalg.norm(full, axis=1)
+    assert np.abs(n - 1).max() <= NORM_TOL
+
+
+# ---------------------------------------------------------------------------
+# Rejects and cancellation (model_test.go:416-471, 203-244)
+# ---------------------------------------------------------------------------
+def test_rejects(gpu):
+    p = load_pack(GOLDEN / "toy-absolute-gelu")
+    m = Model(p.cfg, p.tensors, devices=[0])
+    with pytest.raises(FutonError, match="empty"):
+        m.encode_tokens([])
+    with pytest.raises(FutonError, match="outside vocab"):
+        m.encode_tokens([2, 999, 3])
+    with pytest.raises(FutonError, match="exceeds effective max_seq_len"):
+        m.encode_tokens([5] * (p.cfg.max_seq_len + 1))
+    with pytest.raises(FutonError, match="matryoshka"):
+        m.encode_tokens([2, 3], 16)
+    with pytest.raises(FutonError, match="outside"):
+        m.encode_tokens([2, 3], p.cfg.hidden_size + 1)
+    with pytest.raises(FutonError, match="empty"):
+        m.encode_packed(np.array([2, 3], np.int32), np.array([0, 2, 2], np.int32))
+    m.close()
+
+
+def test_cancellation(gpu):
+    cfg, w, m = synth_model("bge")
+    ids, cu = synth.make_inputs("c0")
+    flag = CancelFlag()
+    flag.cancel()
+    with pytest.raises(CanceledError):
+        m.encode_packed(ids, cu, cancel=flag)
+    # The model stays usable after a canceled call.
+    out = m.encode_packed(ids, cu)
+    assert np.abs(np.linalg.norm(out, axis=1) - 1).max() <= NORM_TOL
+
+
+def test_trained_context_clamp(gpu):
+    """Sequences past max_trained_positions are refused (config.go:111-116)."""
+    import copy
+    p = load_pack(GOLDEN / "toy-rope-swiglu")
+    cfg = copy.deepcopy(p.cfg)
+    cfg.max_trained_positions = 16
+    m = Model(cfg, p.tensors, devices=[0])
+    m.encode_tokens([5] * 16)
+    with pytest.raises(FutonError, match="exceeds effective max_seq_len 16"):
+        m.encode_tokens([5] * 17)
+    m.close()
