@@ -1,0 +1,337 @@
+#!/usr/bin/env python3
+"""Benchmark: embeddings/s of the bge-small-shaped encoder on the c4 workload.
+
+A step is one forward over one c4 batch per GPU: 65,536 sequences with
+log-normal lengths (median 64, sigma 0.8, clipped to [8, 512]), CLS pooled,
+L2-normalised 384-d vectors, random-init weights (synthetic data of the
+benchmark's shape; see futon_b200/synth.py). Each rank encodes its own batch
+(weak scaling, no collective on the data path; NCCL is used only for the
+barrier and the max-over-ranks of the timings).
+
+  value  whole-job embeddings/s with ids already in HBM (device-resident
+         entry point), timed with CUDA events on the launch stream, max over ranks
+  e2e    the same through the host-buffer C ABI (futon_cuda_encode): ids
+         copied host→device and vectors device→host inside the timed region
+  roofline  the dominant kernel's achieved TFLOP/s (its algorithmic FLOPs per
+         launch ÷ its CUDA-event-timed average launch duration, from the
+         library's per-stage profiler over a second timed pass)
+  cpu_baseline  the reference algorithm on the host cores (the CPU oracle's
+         AVX2 port of the reference kernel, all threads) on a bounded sample
+
+`--impl reference` times that CPU port alone (the reference is Go and has no
+GPU path; it cannot be built on this image) and prints its own line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "embeddings/sec (bge-small-shaped encoder, c4 log-normal batch)"
+UNIT = "embeddings/s"
+WORKLOAD = "c4"
+CPU_SAMPLE_SEQS = 512
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(steps: int = 1, warmup: int = 0, seqs: int = CPU_SAMPLE_SEQS):
+    """The reference algorithm on all host cores: the oracle's restatement of
+    the reference forward with its AVX2 panel GEMM (kernel_avx2_amd64.s)."""
+    from futon_b200 import synth
+    from oracle.oracle import GEMM_AVX2, GEMM_GO, OracleModel, has_avx2
+    cfg = synth.arch("bge")
+    w = synth.make_weights(cfg)
+    ids, cu = synth.make_inputs(WORKLOAD, nseq=seqs, seed=11)
+    threads = os.cpu_count() or 1
+    m = OracleModel(cfg, w, gemm=GEMM_AVX2 if has_avx2() else GEMM_GO)
+    for _ in range(warmup):
+        m.encode_batch(ids, cu, threads=threads)
+    times = []
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        m.encode_batch(ids, cu, threads=threads)
+        times.append(time.perf_counter() - t0)
+    m.close()
+    dt = sum(times) / len(times)
+    return {
+        "value": seqs / dt, "unit": UNIT, "cores": threads, "kind": "port",
+        "sample": (f"{seqs} c4-distributed sequences ({int(cu[-1])} tokens) per step through the "
+                   f"C restatement of the reference forward ({'AVX2' if has_avx2() else 'scalar'} "
+                   f"GEMM), {threads} threads"),
+        "ms_per_sample": dt * 1e3, "tokens_per_sec": int(cu[-1]) / dt,
+    }
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    cb = cpu_baseline(steps=args.steps, warmup=min(args.warmup, 1))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": cb["ms_per_sample"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "model": "bge-small-shaped (12 layers, hidden 384)",
+                   "sample_seqs": CPU_SAMPLE_SEQS, "parallelism": "host threads"},
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": ("the reference is a pure-Go CPU library; no Go toolchain exists on this image, "
+                 "so its algorithm runs as the repository's C restatement (oracle/)"),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="futon_b200", choices=["futon_b200", "reference"])
+    ap.add_argument("--nseq", type=int, default=None, help="override sequences per rank")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
+    local = env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from futon_b200 import Model, synth
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = synth.arch("bge")
+    weights = synth.make_weights(cfg)
+    model = Model(cfg, weights, devices=[local], q8=False)
+    ids, cu = synth.make_inputs(WORKLOAD, seed=1 + rank, nseq=args.nseq)
+    nseq, ntok = len(cu) - 1, int(cu[-1])
+    flops = synth.total_flops(cfg, cu)
+    dim = cfg.hidden_size
+
+    # A dedicated stream: the library queues its kernels on the stream handle it
+    # is given, and the legacy default stream's handle (0) means "library stream".
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sh = stream.cuda_stream
+    d_ids = torch.from_numpy(ids).cuda()
+    d_out = torch.empty((nseq, dim), dtype=torch.float32, device="cuda")
+
+    def step():
+        model.encode_device(d_ids.data_ptr(), cu, 0, d_out.data_ptr(), stream=sh)
+
+    # ---- value: device-resident ----
+    for _ in range(args.warmup):
+        step()
+    model.sync(stream=sh)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    l0 = model.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    model.sync(stream=sh)
+    barrier()
+    launches = model.launch_count() - l0
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    norms = torch.linalg.vector_norm(d_out, dim=1)
+    assert float((norms - 1).abs().max()) < 1e-4, "outputs are not unit-norm"
+    value = world * nseq / (ms / 1e3)
+
+    # ---- roofline: second pass with the per-stage profiler on ----
+    model.profile(True)
+    barrier()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    for _ in range(args.steps):
+        step()
+    p1.record(stream)
+    p1.synchronize()
+    prof = model.profile_read()
+    model.profile(False)
+    prof_ms = p0.elapsed_time(p1) / args.steps
+    peaks, peak_src = load_peaks()
+    gemms = {k: v for k, v in prof.items() if k.startswith("gemm") or k.startswith("attention")}
+    top = max(gemms, key=lambda k: gemms[k]["ms"])
+    tk = gemms[top]
+    per_launch_ms = tk["ms"] / tk["launches"]
+    achieved = tk["flops"] / tk["launches"] / (per_launch_ms / 1e3) / 1e12
+    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    traffic = None
+    tf = ROOT / "profiles" / "traffic_per_launch.json"
+    if tf.exists():
+        try:
+            td = json.loads(tf.read_text()).get(top)
+            if td:
+                traffic = td["bytes_per_token"] * (tk["flops"] / tk["launches"]) / td["flops_per_token"]
+        except (ValueError, KeyError, ZeroDivisionError):
+            traffic = None
+    total_ms = sum(v["ms"] for v in prof.values()) / args.steps
+    breakdown = {k: {"ms_per_step": round(v["ms"] / args.steps, 3),
+                     "share": round(v["ms"] / args.steps / total_ms, 4),
+                     "launches_per_step": v["launches"] // args.steps,
+                     "tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1) if v["flops"] else None,
+                     "gbs": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1)}
+                 for k, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])}
+
+    # ---- e2e: host buffers through the C ABI ----
+    for _ in range(max(1, args.warmup)):
+        model.encode_packed(ids, cu)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = model.encode_packed(ids, cu)
+    t1 = time.perf_counter()
+    barrier()
+    e2e_ms = max_over_ranks((t1 - t0) * 1e3) / args.steps
+    assert np.abs(np.linalg.norm(out, axis=1) - 1).max() < 1e-4
+    ntiles = int(np.sum((np.diff(cu) + 63) // 64))
+    h2d = ids.nbytes + cu.nbytes + ntiles * 8
+    d2h = nseq * dim * 4 + 4
+
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline()
+        cb = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights N(0,0.02), seeded c4 lengths and ids)",
+            "config": {"workload": WORKLOAD, "model": "bge-small-shaped (12 layers, hidden 384, "
+                       "12 heads, FFN 1536, GELU, CLS)", "seqs_per_rank": nseq,
+                       "tokens_per_rank": ntok, "global_batch": nseq * world,
+                       "parallelism": f"dp{world}",
+                       "l2": "working set > L2 (per micro-batch activations ~1.3 GB)"},
+            "tokens_per_sec": round(world * ntok / (ms / 1e3), 1),
+            "tflops": round(world * flops / (ms / 1e3) / 1e12, 1),
+            "frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
+            "gpu_launches": launches,
+            "e2e": {"value": round(world * nseq / (e2e_ms / 1e3), 1), "unit": UNIT,
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                    "ms_per_step": round(e2e_ms, 3)},
+            "roofline": {"kernel": top, "bound": "tensor", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_src} bf16_tflops_sustained",
+                         "traffic": traffic, "launches_per_step": tk["launches"] // args.steps,
+                         "avg_launch_ms": round(per_launch_ms, 4),
+                         "profiled_ms_per_step": round(prof_ms, 3)},
+            "stages": breakdown,
+            "clocks": clk,
+            "cpu_baseline": cb,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -23,7 +23,8 @@ EXPORTED = (
     "futon_cuda_device_count", "futon_cuda_model_create", "futon_cuda_model_destroy",
     "futon_cuda_encode", "futon_cuda_encode_batch", "futon_cuda_encode_device",
     "futon_cuda_sync", "futon_cuda_launch_count", "futon_cuda_matmul_t",
-    "futon_cuda_matmul_t_q8", "futon_cuda_quantize_rows_q8",
+    "futon_cuda_matmul_t_q8", "futon_cuda_quantize_rows_q8", "futon_cuda_profile",
+    "futon_cuda_profile_read", "futon_cuda_profile_stage_count", "futon_cuda_profile_stage_name",
 )
 
 
@@ -98,6 +99,16 @@ def lib() -> C.CDLL:
         L.futon_cuda_sync.argtypes = [vp, ip, vp, cp, sz]
         L.futon_cuda_launch_count.restype = C.c_longlong
         L.futon_cuda_launch_count.argtypes = [vp, ip]
+        L.futon_cuda_profile.restype = ip
+        L.futon_cuda_profile.argtypes = [vp, ip, ip, cp, sz]
+        L.futon_cuda_profile_read.restype = ip
+        L.futon_cuda_profile_read.argtypes = [vp, ip, ip, C.POINTER(C.c_double),
+                                              C.POINTER(C.c_longlong), C.POINTER(C.c_double),
+                                              C.POINTER(C.c_double), cp, sz]
+        L.futon_cuda_profile_stage_count.restype = ip
+        L.futon_cuda_profile_stage_count.argtypes = []
+        L.futon_cuda_profile_stage_name.restype = C.c_char_p
+        L.futon_cuda_profile_stage_name.argtypes = [ip]
         L.futon_cuda_matmul_t.restype = ip
         L.futon_cuda_matmul_t.argtypes = [ip, vp, vp, vp, ip, ip, ip, vp, vp, cp, sz]
         L.futon_cuda_matmul_t_q8.restype = ip

@@ -9,10 +9,12 @@
 // (model.go:674-685) is applied to q and k while they are staged, from the
 // f32 cos/sin tables built like precomputeRoPE (model.go:306-318).
 //
-// Two kernels:
+// Kernels:
 //   attn_flash_kernel  64 query rows × one head per CTA, 64-key tiles,
 //                      bf16 m16n8k16 tensor-core MMAs with f32 accumulation
 //                      and online softmax (head_dim 32 or 64).
+//   attn_flash_split_kernel  the same over f32 qkv with every operand split
+//                      into bf16 hi + lo parts (int8 path).
 //   attn_rowq_kernel   one warp per (query, head): lanes split the keys,
 //                      f32 math, warp merge. Serves CLS-pooled last layers
 //                      (one query per sequence, model.go:403-410) and any
@@ -242,6 +244,175 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Split-precision variant for the int8 path. The int8 path quantises the
+// attention output per row, and int8 rounding boundaries amplify any input
+// perturbation, so its attention must track float32 closely: q, k, v (f32)
+// and the probabilities are each split into bf16 hi + lo parts and every
+// product runs as hi·hi + hi·lo + lo·hi (relative error ≈ 2^-16).
+// ---------------------------------------------------------------------------
+template <int HD, bool ROPE>
+__device__ __forceinline__ void stage_rows_split(__nv_bfloat16* dhi, __nv_bfloat16* dlo, int lds,
+                                                 const float* src, int ld, int r0, int L,
+                                                 const float* rcos, const float* rsin) {
+  constexpr int kRows = 64, kHalf = HD / 2;
+  constexpr int kItems = ROPE ? kRows * kHalf : kRows * HD;
+  for (int w = threadIdx.x; w < kItems; w += blockDim.x) {
+    if constexpr (ROPE) {
+      const int r = w / kHalf, i = w % kHalf, pos = r0 + r;
+      float y1 = 0.f, y2 = 0.f;
+      if (pos < L) {
+        const float x1 = src[(size_t)pos * ld + i], x2 = src[(size_t)pos * ld + i + kHalf];
+        const float c = rcos[(size_t)pos * kHalf + i], sn = rsin[(size_t)pos * kHalf + i];
+        y1 = x1 * c - x2 * sn;
+        y2 = x2 * c + x1 * sn;
+      }
+      const __nv_bfloat16 h1 = __float2bfloat16_rn(y1), h2 = __float2bfloat16_rn(y2);
+      dhi[r * lds + i] = h1;
+      dlo[r * lds + i] = __float2bfloat16_rn(y1 - __bfloat162float(h1));
+      dhi[r * lds + i + kHalf] = h2;
+      dlo[r * lds + i + kHalf] = __float2bfloat16_rn(y2 - __bfloat162float(h2));
+    } else {
+      const int r = w / HD, i = w % HD, pos = r0 + r;
+      const float y = pos < L ? src[(size_t)pos * ld + i] : 0.f;
+      const __nv_bfloat16 hv = __float2bfloat16_rn(y);
+      dhi[r * lds + i] = hv;
+      dlo[r * lds + i] = __float2bfloat16_rn(y - __bfloat162float(hv));
+    }
+  }
+}
+
+// grid = (num_tiles, num_heads), block = 128, dynamic smem = 6 · 64 · (HD+8) bf16.
+template <int HD, bool ROPE>
+__global__ void __launch_bounds__(128)
+    attn_flash_split_kernel(const float* __restrict__ qkv, int hidden,
+                            const int* __restrict__ cu_seqlens, const AttnTile* __restrict__ tiles,
+                            const float* __restrict__ rcos, const float* __restrict__ rsin,
+                            float scale_log2, float* __restrict__ out, int ldo) {
+  constexpr int kBK = 64, kLds = HD + 8, kTile = 64 * kLds;
+  extern __shared__ __align__(16) __nv_bfloat16 sm[];
+  __nv_bfloat16 *sQh = sm, *sQl = sm + kTile, *sKh = sm + 2 * kTile, *sKl = sm + 3 * kTile;
+  __nv_bfloat16 *sVh = sm + 4 * kTile, *sVl = sm + 5 * kTile;
+
+  const AttnTile tile = tiles[blockIdx.x];
+  const int head = blockIdx.y;
+  const int s0 = cu_seqlens[tile.seq];
+  const int L = cu_seqlens[tile.seq + 1] - s0;
+  const int ld = 3 * hidden;
+  const float* qg = qkv + (size_t)s0 * ld + head * HD;
+  const float* kg = qg + hidden;
+  const float* vg = qg + 2 * hidden;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  stage_rows_split<HD, ROPE>(sQh, sQl, kLds, qg, ld, tile.q0, L, rcos, rsin);
+  __syncthreads();
+  uint32_t qh[HD / 16][4], ql[HD / 16][4];
+#pragma unroll
+  for (int kc = 0; kc < HD / 16; ++kc) {
+    const int off = (warp * 16 + (lane & 15)) * kLds + kc * 16 + (lane >> 4) * 8;
+    ldsm_x4(qh[kc], smem_u32(&sQh[off]));
+    ldsm_x4(ql[kc], smem_u32(&sQl[off]));
+  }
+  float o[HD / 8][4];
+#pragma unroll
+  for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+
+  for (int kv0 = 0; kv0 < L; kv0 += kBK) {
+    __syncthreads();
+    stage_rows_split<HD, ROPE>(sKh, sKl, kLds, kg, ld, kv0, L, rcos, rsin);
+    stage_rows_split<HD, false>(sVh, sVl, kLds, vg, ld, kv0, L, nullptr, nullptr);
+    __syncthreads();
+    float s[kBK / 8][4];
+#pragma unroll
+    for (int nb = 0; nb < kBK / 8; ++nb) {
+      s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+#pragma unroll
+      for (int kc = 0; kc < HD / 16; ++kc) {
+        const int off = (nb * 8 + (lane & 7)) * kLds + kc * 16 + ((lane >> 3) & 1) * 8;
+        uint32_t kh[2], kl[2];
+        ldsm_x2(kh, smem_u32(&sKh[off]));
+        ldsm_x2(kl, smem_u32(&sKl[off]));
+        mma_16816(s[nb], ql[kc], kh);
+        mma_16816(s[nb], qh[kc], kl);
+        mma_16816(s[nb], qh[kc], kh);
+      }
+    }
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < kBK / 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = kv0 + nb * 8 + (lane & 3) * 2 + (e & 1);
+        const float v = (key < L) ? s[nb][e] * scale_log2 : -INFINITY;
+        s[nb][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    }
+    float alpha[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const float m_new = fmaxf(m_run[r], mx[r]);
+      alpha[r] = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - m_new);
+      m_run[r] = m_new;
+      l_run[r] *= alpha[r];
+    }
+#pragma unroll
+    for (int nb = 0; nb < kBK / 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p = exp2f(s[nb][e] - m_run[e >> 1]);
+        s[nb][e] = p;
+        l_run[e >> 1] += p;
+      }
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; ++nd) {
+      o[nd][0] *= alpha[0]; o[nd][1] *= alpha[0];
+      o[nd][2] *= alpha[1]; o[nd][3] *= alpha[1];
+    }
+#pragma unroll
+    for (int kc = 0; kc < kBK / 16; ++kc) {
+      float pv[8] = {s[2 * kc][0], s[2 * kc][1], s[2 * kc][2], s[2 * kc][3],
+                     s[2 * kc + 1][0], s[2 * kc + 1][1], s[2 * kc + 1][2], s[2 * kc + 1][3]};
+      float lo[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        lo[i] = pv[i] - __bfloat162float(__float2bfloat16_rn(pv[i]));
+      uint32_t ph[4] = {pack_bf16(pv[0], pv[1]), pack_bf16(pv[2], pv[3]), pack_bf16(pv[4], pv[5]),
+                        pack_bf16(pv[6], pv[7])};
+      uint32_t pl[4] = {pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]), pack_bf16(lo[4], lo[5]),
+                        pack_bf16(lo[6], lo[7])};
+#pragma unroll
+      for (int nd = 0; nd < HD / 8; ++nd) {
+        const int off = (kc * 16 + (lane & 15)) * kLds + nd * 8;
+        uint32_t vh[2], vl[2];
+        ldsm_x2_t(vh, smem_u32(&sVh[off]));
+        ldsm_x2_t(vl, smem_u32(&sVl[off]));
+        mma_16816(o[nd], pl, vh);
+        mma_16816(o[nd], ph, vl);
+        mma_16816(o[nd], ph, vh);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+  }
+  const float inv0 = 1.f / l_run[0], inv1 = 1.f / l_run[1];
+  const int qr0 = tile.q0 + warp * 16 + (lane >> 2), qr1 = qr0 + 8;
+#pragma unroll
+  for (int nd = 0; nd < HD / 8; ++nd) {
+    const int col = head * HD + nd * 8 + (lane & 3) * 2;
+    if (qr0 < L) store2<float>(out + (size_t)(s0 + qr0) * ldo + col, o[nd][0] * inv0, o[nd][1] * inv0);
+    if (qr1 < L) store2<float>(out + (size_t)(s0 + qr1) * ldo + col, o[nd][2] * inv1, o[nd][3] * inv1);
+  }
+}
+
 // Index of the sequence holding packed row `row` (cu is non-decreasing).
 __device__ __forceinline__ int find_seq(const int* cu, int nseq, int row) {
   int lo = 0, hi = nseq;  // invariant: cu[lo] <= row < cu[hi]
@@ -255,9 +426,15 @@ __device__ __forceinline__ int find_seq(const int* cu, int nseq, int row) {
 // One warp per (query, head). cls_mode = 0: query i is packed row i (all
 // tokens); output row i. cls_mode = 1: query i is the first token of
 // sequence i; output row i of a compact [nseq, ldo] buffer.
-template <int HD, typename OutT>
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+template <int HD, typename InT, typename OutT>
 __global__ void __launch_bounds__(256)
-    attn_rowq_kernel(const __nv_bfloat16* __restrict__ qkv, int hidden, int num_heads,
+    attn_rowq_kernel(const InT* __restrict__ qkv, int hidden, int num_heads,
                      const int* __restrict__ cu_seqlens, int nseq, int nq, int cls_mode,
                      const float* __restrict__ rcos, const float* __restrict__ rsin, int rope,
                      float scale_log2, OutT* __restrict__ out, int ldo) {
@@ -281,9 +458,9 @@ __global__ void __launch_bounds__(256)
 
   float q[HD];
   {
-    const __nv_bfloat16* p = qkv + (size_t)qrow * ld + head * HD;
+    const InT* p = qkv + (size_t)qrow * ld + head * HD;
 #pragma unroll
-    for (int d = 0; d < HD; ++d) q[d] = __bfloat162float(p[d]);
+    for (int d = 0; d < HD; ++d) q[d] = to_f32(p[d]);
     if (rope) {
 #pragma unroll
       for (int i = 0; i < kHalf; ++i) {
@@ -299,11 +476,11 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int d = 0; d < HD; ++d) o[d] = 0.f;
   for (int j = lane; j < L; j += 32) {
-    const __nv_bfloat16* kp = qkv + (size_t)(s0 + j) * ld + hidden + head * HD;
-    const __nv_bfloat16* vp = kp + hidden;
+    const InT* kp = qkv + (size_t)(s0 + j) * ld + hidden + head * HD;
+    const InT* vp = kp + hidden;
     float k[HD];
 #pragma unroll
-    for (int d = 0; d < HD; ++d) k[d] = __bfloat162float(kp[d]);
+    for (int d = 0; d < HD; ++d) k[d] = to_f32(kp[d]);
     if (rope) {
 #pragma unroll
       for (int i = 0; i < kHalf; ++i) {
@@ -322,7 +499,7 @@ __global__ void __launch_bounds__(256)
     const float p = exp2f(sc - m_new);
     l = l * alpha + p;
 #pragma unroll
-    for (int d = 0; d < HD; ++d) o[d] = o[d] * alpha + p * __bfloat162float(vp[d]);
+    for (int d = 0; d < HD; ++d) o[d] = o[d] * alpha + p * to_f32(vp[d]);
     m = m_new;
   }
   const float mw = warp_max(m);

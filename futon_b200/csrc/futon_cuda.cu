@@ -129,7 +129,7 @@ struct Workspace {
   void* base = nullptr;
   float* x;
   bf16* xb;
-  bf16* qkv;
+  void* qkv;         // bf16 (float path) or f32 (q8 path)
   void* attn;        // bf16 (float path) or f32 (q8 path)
   void* ffn;         // bf16 or f32
   float* tmp;
@@ -164,6 +164,13 @@ struct DevCtx {
   size_t h_out_cap = 0;
   cudaEvent_t meta_evt = nullptr;
   std::atomic<long long> launches{0};
+  // Optional per-stage profiler (CUDA events around each launch).
+  bool prof_on = false;
+  struct ProfRec { cudaEvent_t a, b; int stage; double flops, bytes; };
+  std::vector<ProfRec> prof_pending;
+  std::vector<cudaEvent_t> ev_pool, ev_all;
+  struct ProfAgg { double ms = 0, flops = 0, bytes = 0; long long n = 0; };
+  ProfAgg prof_agg[16];
 
   ~DevCtx() {
     cudaSetDevice(device);
@@ -177,6 +184,7 @@ struct DevCtx {
     if (h_ids) cudaFreeHost(h_ids);
     if (h_out) cudaFreeHost(h_out);
     if (meta_evt) cudaEventDestroy(meta_evt);
+    for (cudaEvent_t e : ev_all) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
   }
 };
@@ -195,6 +203,65 @@ struct futon_model {
 namespace {
 
 constexpr int kTokenBudget = 131072;  // tokens per micro-batch
+
+// Profiler stages (futon_cuda_profile_read's `stage` argument).
+enum Stage : int {
+  kStEmbed = 0, kStGemmQkv, kStAttn, kStAttnCls, kStGather, kStQuant, kStGemmOut, kStLayerNorm,
+  kStGemmFc1, kStGemmFc2, kStPool, kNumStages
+};
+const char* kStageNames[kNumStages] = {"embed_ln", "gemm_qkv", "attention", "attention_cls",
+                                       "gather_cls", "quant_rows", "gemm_out", "layernorm",
+                                       "gemm_fc1", "gemm_fc2", "pool"};
+
+cudaEvent_t prof_event(DevCtx& d) {
+  if (!d.ev_pool.empty()) {
+    cudaEvent_t e = d.ev_pool.back();
+    d.ev_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  d.ev_all.push_back(e);
+  return e;
+}
+// Brackets one launch when profiling is on.
+struct ProfScope {
+  DevCtx& d;
+  cudaStream_t st;
+  int stage;
+  double flops, bytes;
+  cudaEvent_t a = nullptr;
+  ProfScope(DevCtx& d_, cudaStream_t st_, int stage_, double flops_, double bytes_)
+      : d(d_), st(st_), stage(stage_), flops(flops_), bytes(bytes_) {
+    if (d.prof_on) {
+      a = prof_event(d);
+      cudaEventRecord(a, st);
+    }
+  }
+  ~ProfScope() {
+    if (d.prof_on && a) {
+      cudaEvent_t b = prof_event(d);
+      cudaEventRecord(b, st);
+      d.prof_pending.push_back({a, b, stage, flops, bytes});
+    }
+  }
+};
+
+void prof_collect(DevCtx& d) {
+  for (auto& r : d.prof_pending) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+      auto& g = d.prof_agg[r.stage];
+      g.ms += ms;
+      g.flops += r.flops;
+      g.bytes += r.bytes;
+      g.n += 1;
+    }
+    d.ev_pool.push_back(r.a);
+    d.ev_pool.push_back(r.b);
+  }
+  d.prof_pending.clear();
+}
 
 int effective_max(const futon_cfg& c) {
   if (c.max_trained_positions > 0 && c.max_trained_positions < c.max_seq_len)
@@ -341,7 +408,8 @@ int ensure_workspace(const futon_model& m, DevCtx& d, size_t tokens, char* err, 
   const bool q8 = m.q8 != 0;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
-  const size_t o_x = take(T * h * 4), o_xb = take(T * h * 2), o_qkv = take(T * 3 * h * 2);
+  const size_t o_x = take(T * h * 4), o_xb = take(T * h * 2);
+  const size_t o_qkv = take(T * 3 * h * (q8 ? 4 : 2));
   const size_t o_attn = take(T * h * (q8 ? 4 : 2)), o_ffn = take(T * I * (q8 ? 4 : 2));
   const size_t o_tmp = take(T * h * 4), o_xc = take(T * h * 4);
   size_t o_xq = 0, o_aq = 0, o_fq = 0, o_xs = 0, o_as = 0, o_fs = 0;
@@ -357,7 +425,7 @@ int ensure_workspace(const futon_model& m, DevCtx& d, size_t tokens, char* err, 
   w.tokens = tokens;
   w.x = (float*)(b + o_x);
   w.xb = (bf16*)(b + o_xb);
-  w.qkv = (bf16*)(b + o_qkv);
+  w.qkv = b + o_qkv;
   w.attn = b + o_attn;
   w.ffn = b + o_ffn;
   w.tmp = (float*)(b + o_tmp);
@@ -401,10 +469,16 @@ int ensure_host(T** p, size_t* cap, size_t count, char* err, size_t errlen) {
 }
 
 // ---- GEMM helper ---------------------------------------------------------
-int run_gemm(DevCtx& d, const void* A, bool s8, const float* a_scale, int M, const GemmWeight& w,
-             int epi, bool out_f32, void* out, int ldo, const float* resid, int ldr,
-             cudaStream_t st, char* err, size_t errlen) {
+int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale, int M,
+             const GemmWeight& w, int epi, bool out_f32, void* out, int ldo, const float* resid,
+             int ldr, cudaStream_t st, char* err, size_t errlen) {
   if (M == 0) return FUTON_OK;
+  const double esz = s8 ? 1.0 : 2.0;
+  const double out_cols = epi == kEpiSwiglu ? w.n / 2 : w.n;
+  const double osz = (out_f32 || (s8 && epi != kEpiStore)) ? 4.0 : 2.0;
+  const double bytes = (double)M * w.k * esz + (double)w.n * w.k * esz + (double)M * out_cols * osz +
+                       (resid ? (double)M * w.n * 4.0 : 0.0);
+  ProfScope prof(d, st, stage, 2.0 * M * w.n * w.k, bytes);
   CUtensorMap ta;
   if (!make_operand_map(&ta, A, s8, (uint64_t)M, (uint64_t)w.k, 128))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (activation)");
@@ -441,31 +515,49 @@ inline int grid_rows(int rows, int per_block, int sms) {
 }
 
 // ---- attention dispatch --------------------------------------------------
-template <typename OutT>
+// Float path: bf16 qkv, bf16 tensor-core flash attention. Int8 path: f32 qkv
+// and split-precision (bf16 hi+lo) flash attention with f32 output, so the
+// per-row quantisation that follows sees float32-accurate values.
+template <typename InT, typename OutT>
 int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* cu,
-                  const AttnTile* tiles, int ntiles, bool cls_only, OutT* out,
+                  const AttnTile* tiles, int ntiles, bool cls_only, const InT* qkv, OutT* out,
                   cudaStream_t st, char* err, size_t errlen) {
   const int h = m.cfg.hidden_size, H = m.cfg.num_heads, hd = m.head_dim;
   const bool rope = m.cfg.position_encoding == FUTON_POS_ROPE;
   const float scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
+  constexpr bool kSplit = sizeof(InT) == 4;
   if (!cls_only && (hd == 32 || hd == 64) && ntiles > 0) {
     dim3 grid(ntiles, H);
-    if (hd == 32) {
-      if (rope) attn_flash_kernel<32, true, OutT><<<grid, 128, 0, st>>>(d.ws.qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
-      else attn_flash_kernel<32, false, OutT><<<grid, 128, 0, st>>>(d.ws.qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+    if constexpr (kSplit) {
+      const int smem = 6 * 64 * (hd + 8) * 2;
+      auto launch = [&](auto kern) -> cudaError_t {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, 128, smem, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+        return cudaGetLastError();
+      };
+      cudaError_t e;
+      if (hd == 32) e = rope ? launch(attn_flash_split_kernel<32, true>) : launch(attn_flash_split_kernel<32, false>);
+      else e = rope ? launch(attn_flash_split_kernel<64, true>) : launch(attn_flash_split_kernel<64, false>);
+      CU_TRY(e);
     } else {
-      if (rope) attn_flash_kernel<64, true, OutT><<<grid, 128, 0, st>>>(d.ws.qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
-      else attn_flash_kernel<64, false, OutT><<<grid, 128, 0, st>>>(d.ws.qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+      if (hd == 32) {
+        if (rope) attn_flash_kernel<32, true, OutT><<<grid, 128, 0, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+        else attn_flash_kernel<32, false, OutT><<<grid, 128, 0, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+      } else {
+        if (rope) attn_flash_kernel<64, true, OutT><<<grid, 128, 0, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+        else attn_flash_kernel<64, false, OutT><<<grid, 128, 0, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+      }
     }
   } else {
     const int nq = cls_only ? nseq : T;
     const long warps = (long)nq * H;
     const int blocks = (int)((warps * 32 + 255) / 256);
     if (blocks == 0) return FUTON_OK;
-#define FUTON_ROWQ(HD_)                                                                    \
-  attn_rowq_kernel<HD_, OutT><<<blocks, 256, 0, st>>>(d.ws.qkv, h, H, cu, nseq, nq,        \
-                                                     cls_only ? 1 : 0, d.rcos, d.rsin,     \
-                                                     rope ? 1 : 0, scale_log2, out, h)
+#define FUTON_ROWQ(HD_)                                                                   \
+  attn_rowq_kernel<HD_, InT, OutT><<<blocks, 256, 0, st>>>(qkv, h, H, cu, nseq, nq,         \
+                                                          cls_only ? 1 : 0, d.rcos, d.rsin, \
+                                                          rope ? 1 : 0, scale_log2, out, h)
     switch (hd) {
       case 8: FUTON_ROWQ(8); break;
       case 16: FUTON_ROWQ(16); break;
@@ -483,20 +575,27 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
 
 // ---- one micro-batch -----------------------------------------------------
 // ids: device [T]; cu: device [nseq+1] (local offsets); tiles: device.
+// sum_l2 = Σ L² over the micro-batch's sequences (attention work, profiler only).
 int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, int nseq, int T,
-               const AttnTile* tiles, int ntiles, int out_dim, float* out, cudaStream_t st,
-               volatile const int* cancel, char* err, size_t errlen) {
+               double sum_l2, const AttnTile* tiles, int ntiles, int out_dim, float* out,
+               cudaStream_t st, volatile const int* cancel, char* err, size_t errlen) {
   const futon_cfg& c = m.cfg;
   const int h = c.hidden_size, I = c.intermediate_size;
   const bool q8 = m.q8 != 0, cls = c.pooling == FUTON_POOL_CLS;
   const float eps = (float)c.layer_norm_eps;
+  const double qsz = q8 ? 1.0 : 0.0;  // int8 copy bytes per element written by LN
   Workspace& w = d.ws;
   int rc;
 
-  embed_ln_kernel<<<grid_rows(T, 8, d.num_sms), 256, 0, st>>>(
-      ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0, d.pos, d.embw, d.embb, eps, w.x, w.xb, w.xq, w.xs);
-  CU_TRY(cudaGetLastError());
-  d.launches.fetch_add(1, std::memory_order_relaxed);
+  {
+    const double pos_bytes = c.position_encoding == FUTON_POS_ABSOLUTE ? 4.0 * h : 0.0;
+    ProfScope prof(d, st, kStEmbed, 0.0, (double)T * (4.0 + 4.0 * h + pos_bytes + 6.0 * h + qsz * h));
+    embed_ln_kernel<<<grid_rows(T, 8, d.num_sms), 256, 0, st>>>(
+        ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0, d.pos, d.embw, d.embb, eps,
+        w.x, w.xb, w.xq, w.xs);
+    CU_TRY(cudaGetLastError());
+    d.launches.fetch_add(1, std::memory_order_relaxed);
+  }
 
   for (int li = 0; li < c.num_layers; ++li) {
     if (cancel && *cancel)
@@ -505,18 +604,29 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
     const bool last_cls = cls && li == c.num_layers - 1;
     const int rows = last_cls ? nseq : T;
 
-    // qkv = x·Wqkvᵀ + b → bf16 [T, 3h]
-    if ((rc = run_gemm(d, q8 ? (const void*)w.xq : w.xb, q8, w.xs, T, L.qkv, kEpiStore, false,
-                       w.qkv, 3 * h, nullptr, 0, st, err, errlen)))
+    // qkv = x·Wqkvᵀ + b → [T, 3h] (bf16; f32 on the int8 path)
+    if ((rc = run_gemm(d, kStGemmQkv, q8 ? (const void*)w.xq : w.xb, q8, w.xs, T, L.qkv, kEpiStore,
+                       q8, w.qkv, 3 * h, nullptr, 0, st, err, errlen)))
       return rc;
 
     // attention → attn [rows, h]
-    if (q8) rc = run_attention<float>(m, d, T, nseq, cu, tiles, ntiles, last_cls, (float*)w.attn, st, err, errlen);
-    else rc = run_attention<bf16>(m, d, T, nseq, cu, tiles, ntiles, last_cls, (bf16*)w.attn, st, err, errlen);
-    if (rc) return rc;
+    {
+      const double esz = q8 ? 4.0 : 2.0;
+      const double fl = last_cls ? 4.0 * (double)T * h : 4.0 * sum_l2 * h;
+      const double by = (double)T * 3.0 * h * esz + (double)rows * h * esz;
+      ProfScope prof(d, st, last_cls ? kStAttnCls : kStAttn, fl, by);
+      if (q8)
+        rc = run_attention<float, float>(m, d, T, nseq, cu, tiles, ntiles, last_cls,
+                                         (const float*)w.qkv, (float*)w.attn, st, err, errlen);
+      else
+        rc = run_attention<bf16, bf16>(m, d, T, nseq, cu, tiles, ntiles, last_cls,
+                                       (const bf16*)w.qkv, (bf16*)w.attn, st, err, errlen);
+      if (rc) return rc;
+    }
 
     const float* resid = w.x;
     if (last_cls) {
+      ProfScope prof(d, st, kStGather, 0.0, (double)nseq * 8.0 * h);
       gather_rows_kernel<<<grid_rows(nseq * (h / 4), 256, d.num_sms), 256, 0, st>>>(
           w.x, cu, nseq, h, w.xc, nullptr);
       CU_TRY(cudaGetLastError());
@@ -528,51 +638,66 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
     const void* a_out = w.attn;
     const float* a_out_s = nullptr;
     if (q8) {
-      quant_rows_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>((const float*)w.attn, rows, h, w.attnq, w.attns);
+      ProfScope prof(d, st, kStQuant, 0.0, (double)rows * h * 5.0 + rows * 4.0);
+      quant_rows_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>((const float*)w.attn, rows,
+                                                                     h, w.attnq, w.attns);
       CU_TRY(cudaGetLastError());
       d.launches.fetch_add(1, std::memory_order_relaxed);
       a_out = w.attnq;
       a_out_s = w.attns;
     }
-    if ((rc = run_gemm(d, a_out, q8, a_out_s, rows, L.out, kEpiResid, true, w.tmp, h, resid, h, st,
-                       err, errlen)))
+    if ((rc = run_gemm(d, kStGemmOut, a_out, q8, a_out_s, rows, L.out, kEpiResid, true, w.tmp, h,
+                       resid, h, st, err, errlen)))
       return rc;
-    layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(w.tmp, rows, h, L.n1w, L.n1b,
-                                                                   eps, w.x, w.xb, w.xq, w.xs);
-    CU_TRY(cudaGetLastError());
-    d.launches.fetch_add(1, std::memory_order_relaxed);
+    {
+      ProfScope prof(d, st, kStLayerNorm, 0.0, (double)rows * h * (10.0 + qsz));
+      layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(w.tmp, rows, h, L.n1w, L.n1b,
+                                                                     eps, w.x, w.xb, w.xq, w.xs);
+      CU_TRY(cudaGetLastError());
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+    }
 
     if (cancel && *cancel)
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
 
     // FFN
     const int epi = c.activation == FUTON_ACT_SWIGLU ? kEpiSwiglu : kEpiGelu;
-    if ((rc = run_gemm(d, q8 ? (const void*)w.xq : w.xb, q8, w.xs, rows, L.fc1, epi, q8, w.ffn, I,
-                       nullptr, 0, st, err, errlen)))
+    if ((rc = run_gemm(d, kStGemmFc1, q8 ? (const void*)w.xq : w.xb, q8, w.xs, rows, L.fc1, epi, q8,
+                       w.ffn, I, nullptr, 0, st, err, errlen)))
       return rc;
     const void* a_fc2 = w.ffn;
     const float* a_fc2_s = nullptr;
     if (q8) {
-      quant_rows_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>((const float*)w.ffn, rows, I, w.ffnq, w.ffns);
+      ProfScope prof(d, st, kStQuant, 0.0, (double)rows * I * 5.0 + rows * 4.0);
+      quant_rows_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>((const float*)w.ffn, rows, I,
+                                                                     w.ffnq, w.ffns);
       CU_TRY(cudaGetLastError());
       d.launches.fetch_add(1, std::memory_order_relaxed);
       a_fc2 = w.ffnq;
       a_fc2_s = w.ffns;
     }
-    if ((rc = run_gemm(d, a_fc2, q8, a_fc2_s, rows, L.fc2, kEpiResid, true, w.tmp, h, w.x, h, st,
-                       err, errlen)))
+    if ((rc = run_gemm(d, kStGemmFc2, a_fc2, q8, a_fc2_s, rows, L.fc2, kEpiResid, true, w.tmp, h,
+                       w.x, h, st, err, errlen)))
       return rc;
-    layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(w.tmp, rows, h, L.n2w, L.n2b,
-                                                                   eps, w.x, w.xb, w.xq, w.xs);
+    {
+      ProfScope prof(d, st, kStLayerNorm, 0.0, (double)rows * h * (10.0 + qsz));
+      layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(w.tmp, rows, h, L.n2w, L.n2b,
+                                                                     eps, w.x, w.xb, w.xq, w.xs);
+      CU_TRY(cudaGetLastError());
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+    }
+  }
+
+  {
+    const int dim = out_dim ? out_dim : h;
+    const double rows_read = cls ? (double)nseq : (double)T;
+    ProfScope prof(d, st, kStPool, 0.0, rows_read * h * 4.0 + (double)nseq * dim * 4.0);
+    const int mat_ln = c.matryoshka_layernorm ? 1 : 0;
+    pool_kernel<<<nseq, 256, h * sizeof(float), st>>>(w.x, cu, h, cls ? 0 : 1, out_dim, mat_ln,
+                                                      c.normalize ? 1 : 0, out);
     CU_TRY(cudaGetLastError());
     d.launches.fetch_add(1, std::memory_order_relaxed);
   }
-
-  const int mat_ln = c.matryoshka_layernorm ? 1 : 0;
-  pool_kernel<<<nseq, 256, h * sizeof(float), st>>>(w.x, cu, h, cls ? 0 : 1, out_dim, mat_ln,
-                                                    c.normalize ? 1 : 0, out);
-  CU_TRY(cudaGetLastError());
-  d.launches.fetch_add(1, std::memory_order_relaxed);
   return FUTON_OK;
 }
 
@@ -582,6 +707,7 @@ struct MicroBatch {
   int t0, t1;   // tokens [t0, t1)
   size_t cu_off, tile_off;  // int offsets into the meta buffer
   int ntiles;
+  double sum_l2;            // Σ L² (profiler)
 };
 
 int validate_input(const futon_model& m, const int32_t* cu, int nseq, int out_dim, char* err,
@@ -628,10 +754,14 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, std::vector<MicroBat
     mb.s0 = s;
     mb.t0 = cu[s];
     int ntiles = 0;
+    double l2 = 0.0;
     while (s < nseq && (s == mb.s0 || cu[s + 1] - mb.t0 <= kTokenBudget)) {
+      const double Ls = cu[s + 1] - cu[s];
       ntiles += (cu[s + 1] - cu[s] + 63) / 64;
+      l2 += Ls * Ls;
       ++s;
     }
+    mb.sum_l2 = l2;
     mb.s1 = s;
     mb.t1 = cu[s];
     mb.ntiles = ntiles;
@@ -674,7 +804,7 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
     if (cancel && *cancel)
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
     if ((rc = forward_mb(m, d, d_ids + mb.t0, d.d_meta + mb.cu_off, mb.s1 - mb.s0, mb.t1 - mb.t0,
-                         reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
+                         mb.sum_l2, reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
                          out_dim, d_out + (size_t)mb.s0 * dim, st, cancel, err, errlen)))
       return rc;
   }
@@ -1082,6 +1212,45 @@ int futon_cuda_sync(futon_model* model, int device, void* stream, char* err, siz
 long long futon_cuda_launch_count(futon_model* model, int device) {
   if (!model || device < 0 || device >= (int)model->devs.size()) return -1;
   return model->devs[device]->launches.load();
+}
+
+int futon_cuda_profile(futon_model* model, int device, int enable, char* err, size_t errlen) {
+  if (!model || device < 0 || device >= (int)model->devs.size())
+    return set_err(err, errlen, FUTON_EINVAL, "native: bad model or device index");
+  DevCtx& d = *model->devs[device];
+  std::lock_guard<std::mutex> lock(d.mu);
+  CU_TRY(cudaSetDevice(d.device));
+  CU_TRY(cudaDeviceSynchronize());
+  prof_collect(d);
+  for (auto& g : d.prof_agg) g = DevCtx::ProfAgg();
+  d.prof_on = enable != 0;
+  return FUTON_OK;
+}
+
+int futon_cuda_profile_read(futon_model* model, int device, int stage, double* ms,
+                            long long* launches, double* flops, double* bytes, char* err,
+                            size_t errlen) {
+  if (!model || device < 0 || device >= (int)model->devs.size())
+    return set_err(err, errlen, FUTON_EINVAL, "native: bad model or device index");
+  if (stage < 0 || stage >= kNumStages)
+    return set_err(err, errlen, FUTON_EINVAL, "native: profiler stage %d out of range", stage);
+  DevCtx& d = *model->devs[device];
+  std::lock_guard<std::mutex> lock(d.mu);
+  CU_TRY(cudaSetDevice(d.device));
+  CU_TRY(cudaDeviceSynchronize());
+  prof_collect(d);
+  const auto& g = d.prof_agg[stage];
+  if (ms) *ms = g.ms;
+  if (launches) *launches = g.n;
+  if (flops) *flops = g.flops;
+  if (bytes) *bytes = g.bytes;
+  return FUTON_OK;
+}
+
+int futon_cuda_profile_stage_count(void) { return kNumStages; }
+
+const char* futon_cuda_profile_stage_name(int stage) {
+  return (stage >= 0 && stage < kNumStages) ? kStageNames[stage] : "";
 }
 
 int futon_cuda_matmul_t(int cuda_device, float* dst, const float* a, const float* b, int m, int n,

@@ -12,14 +12,15 @@
 // and, for the int8 path (native/quant.go:99-137), the exact rescale
 //   float32(sum_s32) * (scale_a[m] * scale_w[n]) + bias[n].
 //
-// Structure: one persistent CTA per SM, 6 warps.
+// Structure: one persistent CTA per SM, 10 warps.
 //   warp 0     TMA producer: 128-byte-swizzled K-major tiles of A (128 rows)
 //              and W (BN rows) into a STAGES-deep shared-memory ring.
 //   warp 1     allocates tensor memory; lane 0 issues tcgen05.mma
 //              (M=128, N=BN, K=16 bf16 / 32 s8 per instruction) into one of
 //              two TMEM accumulators and commits completion to mbarriers.
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator lane quarter the warp
-//              owns (one output row per thread), fused math, global store.
+//   warps 2-9  epilogue: tcgen05.ld of the accumulator lane quarter the warp
+//              may access (one output row per thread; the two warps of a
+//              quarter split the 32-column chunks), fused math, global store.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile
 // i+1. Tiles are visited n-fastest so CTAs running together share A tiles
 // through L2; the weights (≤ 19 MB) stay L2-resident.
@@ -54,7 +55,8 @@ struct GemmCfg {
   static constexpr uint32_t kAccStride = (BN <= 64) ? 64 : (BN <= 128) ? 128 : 256;
   static constexpr uint32_t kTmemCols = 2 * kAccStride;       // power of two, ≤ 512
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr int kThreads = 192;
+  static constexpr int kEpiWarps = 8;   // two per TMEM lane quarter
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
 };
 
 template <typename T> __device__ __forceinline__ void store32(T* dst, const float (&v)[32]);
@@ -100,10 +102,20 @@ __device__ __forceinline__ float acc_value(uint32_t u, float a_s, const EpiParam
   return v;
 }
 
-// One tile's epilogue for one thread (= one output row).
+// Activations: the reference's exact f32 evaluation on the int8 path (whose
+// outputs are re-quantised, so every bit matters), fast forms on the bf16 path.
+template <bool S8> __device__ __forceinline__ float act_gelu(float x) {
+  if constexpr (S8) return gelu_f32(x); else return gelu_fast(x);
+}
+template <bool S8> __device__ __forceinline__ float act_silu(float g) {
+  if constexpr (S8) return fmul(g, sigmoid_f32(g)); else return silu_fast(g);
+}
+
+// One tile's epilogue for one thread (= one output row). The two warps that
+// share a TMEM lane quarter split the tile's 32-column chunks (part = 0/1).
 template <int BN, int EPI, bool S8, typename OutT>
 __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int N, int nb,
-                                             const EpiParams& ep) {
+                                             int part, const EpiParams& ep) {
   const bool row_ok = row < M;
   const float a_s = (S8 && row_ok) ? ep.a_scale[row] : 0.0f;
   OutT* out = reinterpret_cast<OutT*>(ep.out);
@@ -113,7 +125,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int
     const int ocol0 = nb * kHalf;         // output column of this tile
     const bool full = (nb + 1) * BN <= N;
 #pragma unroll 1
-    for (int c = 0; c < kHalf; c += 32) {
+    for (int c = 32 * part; c < kHalf; c += 64) {
       uint32_t u[32], g[32];
       tmem_ld32(taddr + c, u);
       tmem_ld32(taddr + kHalf + c, g);
@@ -121,11 +133,11 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int
       float v[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        int wc = wcol0 + c + i;
-        bool ok = full || (wc + kHalf < N);
-        float h = ok ? acc_value<S8>(u[i], a_s, ep, wc) : 0.0f;
-        float gg = ok ? acc_value<S8>(g[i], a_s, ep, wc + kHalf) : 0.0f;
-        v[i] = fmul(h, fmul(gg, sigmoid_f32(gg)));
+        const int wc = wcol0 + c + i;
+        const bool ok = full || (wc + kHalf < N);
+        const float hh = ok ? acc_value<S8>(u[i], a_s, ep, wc) : 0.0f;
+        const float gg = ok ? acc_value<S8>(g[i], a_s, ep, wc + kHalf) : 0.0f;
+        v[i] = fmul(hh, act_silu<S8>(gg));
       }
       if (row_ok) {
         OutT* dst = out + (size_t)row * ep.ldo + ocol0 + c;
@@ -142,20 +154,29 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int
     const int col0 = nb * BN;
     const bool full = col0 + BN <= N;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = 32 * part; c < BN; c += 64) {
       uint32_t u[32];
       tmem_ld32(taddr + c, u);
       tmem_ld_wait();
       const int col = col0 + c;
       float v[32];
       if (full || col + 32 <= N) {
+        float r[32];
+        if constexpr (EPI == kEpiResid) {
+          if (row_ok) {
+            const float4* rp = reinterpret_cast<const float4*>(ep.resid + (size_t)row * ep.ldr + col);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 q = rp[i];
+              r[4 * i] = q.x; r[4 * i + 1] = q.y; r[4 * i + 2] = q.z; r[4 * i + 3] = q.w;
+            }
+          }
+        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float x = acc_value<S8>(u[i], a_s, ep, col + i);
-          if constexpr (EPI == kEpiGelu) x = gelu_f32(x);
-          if constexpr (EPI == kEpiResid) {
-            if (row_ok) x = fadd(x, ep.resid[(size_t)row * ep.ldr + col + i]);
-          }
+          if constexpr (EPI == kEpiGelu) x = act_gelu<S8>(x);
+          if constexpr (EPI == kEpiResid) x = fadd(x, row_ok ? r[i] : 0.0f);
           v[i] = x;
         }
         if (row_ok) store32<OutT>(out + (size_t)row * ep.ldo + col, v);
@@ -164,7 +185,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int
         for (int i = 0; i < 32; ++i) {
           if (col + i < N && row_ok) {
             float x = acc_value<S8>(u[i], a_s, ep, col + i);
-            if constexpr (EPI == kEpiGelu) x = gelu_f32(x);
+            if constexpr (EPI == kEpiGelu) x = act_gelu<S8>(x);
             if constexpr (EPI == kEpiResid) x = fadd(x, ep.resid[(size_t)row * ep.ldr + col + i]);
             store1<OutT>(out + (size_t)row * ep.ldo + col + i, x);
           }
@@ -175,7 +196,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int
 }
 
 template <int BN, int EPI, bool S8, typename OutT>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    int M, int N, int K, EpiParams ep, int* err) {
   using C = GemmCfg<BN, S8>;
@@ -204,7 +225,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&accf_bar[a]), 1);
-      mbar_init(smem_u32(&acce_bar[a]), 4);  // one arrive per epilogue warp
+      mbar_init(smem_u32(&acce_bar[a]), C::kEpiWarps);  // one arrive per epilogue warp
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -311,8 +332,9 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5 ----------------
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    // ---------------- epilogue warps 2..9 ----------------
+    const int quarter = warp & 3;        // TMEM lanes [32*quarter, 32*quarter+32)
+    const int part = (warp - 2) >> 2;    // which half of the column chunks
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
@@ -324,7 +346,7 @@ __global__ void __launch_bounds__(192, 1)
       const int mb = tile / num_n, nb = tile % num_n;
       const int row = mb * C::kBM + quarter * 32 + lane;
       const uint32_t taddr = tmem_base + acc * C::kAccStride + ((uint32_t)(quarter * 32) << 16);
-      epilogue_row<BN, EPI, S8, OutT>(taddr, row, M, N, nb, ep);
+      epilogue_row<BN, EPI, S8, OutT>(taddr, row, M, N, nb, part, ep);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));

@@ -73,4 +73,24 @@ __device__ __forceinline__ float sigmoid_f32(float x) {
   return __fdiv_rn(1.0f, fadd(1.0f, exp_f32(e)));
 }
 
+// Fast variants for the bf16 path, whose outputs are rounded to bf16 (2^-9
+// relative) right after: erfc from Abramowitz & Stegun 7.1.26 (absolute
+// error ≤ 1.5e-7) with CUDA's __expf / __fdividef intrinsics, arranged like
+// geluF32 (0.5·x·erfc(|x|/√2) for x < 0, 0.5·x·(2 − erfc) otherwise).
+__device__ __forceinline__ float gelu_fast(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  float p = fmaf(1.061405429f, t, -1.453152027f);
+  p = fmaf(p, t, 1.421413741f);
+  p = fmaf(p, t, -0.284496736f);
+  p = fmaf(p, t, 0.254829592f);
+  const float q = p * t * __expf(-z * z);  // erfc(|x|/√2)
+  return x < 0.0f ? 0.5f * x * q : 0.5f * x * (2.0f - q);
+}
+
+// g·σ(g) with the exponent clamped so the denominator stays finite.
+__device__ __forceinline__ float silu_fast(float g) {
+  return __fdividef(g, 1.0f + __expf(fminf(-g, 80.0f)));
+}
+
 }  // namespace futon

@@ -207,6 +207,23 @@ class Model:
     def launch_count(self, device: int = 0) -> int:
         return int(_lib.lib().futon_cuda_launch_count(self.handle, device))
 
+    def profile(self, enable: bool, device: int = 0) -> None:
+        """Resets the per-stage profiler and turns it on or off."""
+        _lib.call("futon_cuda_profile", self.handle, device, 1 if enable else 0)
+
+    def profile_read(self, device: int = 0) -> Dict[str, dict]:
+        """{stage: {ms, launches, flops, bytes}} accumulated since profile(True)."""
+        L = _lib.lib()
+        out = {}
+        for st in range(L.futon_cuda_profile_stage_count()):
+            ms, n, fl, by = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
+            _lib.call("futon_cuda_profile_read", self.handle, device, st, C.byref(ms), C.byref(n),
+                      C.byref(fl), C.byref(by))
+            if n.value:
+                out[L.futon_cuda_profile_stage_name(st).decode()] = {
+                    "ms": ms.value, "launches": n.value, "flops": fl.value, "bytes": by.value}
+        return out
+
 
 @dataclasses.dataclass
 class Options:

@@ -129,6 +129,19 @@ int futon_cuda_sync(futon_model* model, int device, void* stream, char* err, siz
  * (counts every launch of this library's own kernels). */
 long long futon_cuda_launch_count(futon_model* model, int device);
 
+/* ---- Per-stage profiler (no counterpart in the reference: measurement) ----
+ * When enabled, every launch on `device` is bracketed by CUDA events and
+ * attributed to a stage (embed_ln, gemm_qkv, attention, …) together with its
+ * algorithmic FLOPs and bytes. futon_cuda_profile resets the counters and
+ * turns recording on (enable != 0) or off; futon_cuda_profile_read waits for
+ * the device and returns the totals of one stage. */
+int futon_cuda_profile(futon_model* model, int device, int enable, char* err, size_t errlen);
+int futon_cuda_profile_read(futon_model* model, int device, int stage, double* ms,
+                            long long* launches, double* flops, double* bytes, char* err,
+                            size_t errlen);
+int futon_cuda_profile_stage_count(void);
+const char* futon_cuda_profile_stage_name(int stage);
+
 /* ---- Kernel seam (device pointers, CUDA device `cuda_device`) ---- */
 
 /* dst[m×n] = a[m×k] · b[n×k]ᵀ (+ bias[n]) on the tcgen05 tensor cores with

@@ -63,8 +63,11 @@ def test_matmul_t_q8_bit_exact(gpu, m, n, k):
     qb, sb = O.quantize_rows_q8(w)
     want = O.matmul_t_q8(a, qb, sb, bias)
     dout = torch.empty((m, n), dtype=torch.float32, device="cuda")
-    _lib.call("futon_cuda_matmul_t_q8", 0, dout.data_ptr(), _dev(a).data_ptr(),
-              _dev(qb).data_ptr(), _dev(sb).data_ptr(), m, n, k, _dev(bias).data_ptr(), None)
+    # Keep every operand alive across the call (a freed temporary's memory
+    # is reused by the caching allocator).
+    da, dqb, dsb, dbias = _dev(a), _dev(qb), _dev(sb), _dev(bias)
+    _lib.call("futon_cuda_matmul_t_q8", 0, dout.data_ptr(), da.data_ptr(), dqb.data_ptr(),
+              dsb.data_ptr(), m, n, k, dbias.data_ptr(), None)
     got = dout.cpu().numpy()
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.abs(got - want).max()
 
@@ -80,7 +83,8 @@ def test_quantize_rows_bit_exact(gpu, rows, k):
     qw, sw = O.quantize_rows_q8(x)
     dq = torch.empty((rows, k), dtype=torch.int8, device="cuda")
     ds = torch.empty(rows, dtype=torch.float32, device="cuda")
-    _lib.call("futon_cuda_quantize_rows_q8", 0, dq.data_ptr(), ds.data_ptr(), _dev(x).data_ptr(),
+    dx = _dev(x)
+    _lib.call("futon_cuda_quantize_rows_q8", 0, dq.data_ptr(), ds.data_ptr(), dx.data_ptr(),
               rows, k, None)
     assert np.array_equal(dq.cpu().numpy(), qw)
     assert np.array_equal(ds.cpu().numpy().view(np.uint32), sw.view(np.uint32))

@@ -35,6 +35,8 @@ def synth_model(arch: str, q8: bool = False):
 def assert_parity(got, want, label, cos_min=GPU_COSINE_MIN):
     cs = row_cosines(got, want)
     norms = np.linalg.norm(got, axis=1)
+    print(f"[parity] {label}: n={len(cs)} min cos {cs.min():.7f} mean {cs.mean():.7f} "
+          f"max |norm-1| {np.abs(norms - 1).max():.1e}")
     assert cs.min() >= cos_min, f"{label}: min cosine {cs.min():.7f} < {cos_min} (mean {cs.mean():.7f})"
     assert np.abs(norms - 1).max() <= NORM_TOL, f"{label}: norm off by {np.abs(norms - 1).max():.2e}"
     return cs
@@ -109,6 +111,17 @@ def test_c2_subset_vs_oracle(gpu, dim):
     assert_parity(got, want, f"c2/{dim}")
 
 
+# Q8 path gates. The reference's Q8 forward amplifies float32-rounding-level
+# differences through its 48 per-row quantisations (tests/study_q8_sensitivity.py:
+# 1e-7 relative noise on attention outputs alone moves it to cos ≈ 0.9999,
+# 1e-6 to ≈ 0.99986), so no implementation that is not bit-identical can sit
+# closer than ≈ 1.4e-4 to it. Gates: cos ≥ 0.9998 against the oracle's Q8
+# forward, and the reference's own Q8 acceptance rule — cos ≥ 0.999 against
+# the float path (native/quant.go:27-29).
+Q8_COSINE_MIN = 0.9998
+Q8_VS_FLOAT_MIN = 0.999
+
+
 @pytest.mark.parametrize("q8", [False, True])
 def test_c3_short_vs_oracle(gpu, q8):
     """arctic shape (RoPE, SwiGLU, CLS) at L=256 against the oracle, both
@@ -121,7 +134,10 @@ def test_c3_short_vs_oracle(gpu, q8):
     ids, cu = pack_ids(seqs)
     got = m.encode_packed(ids, cu)
     want = OracleModel(cfg, w, q8=q8, gemm=oracle_mode()).encode_batch(ids, cu)
-    assert_parity(got, want, f"c3 q8={q8}")
+    assert_parity(got, want, f"c3 q8={q8}", Q8_COSINE_MIN if q8 else GPU_COSINE_MIN)
+    if q8:
+        flt = OracleModel(cfg, w, q8=False, gemm=oracle_mode()).encode_batch(ids, cu)
+        assert_parity(got, flt, "c3 q8 vs float", Q8_VS_FLOAT_MIN)
 
 
 def test_c4_subset_vs_oracle(gpu):
@@ -147,7 +163,7 @@ def test_c3_full_vs_torch(gpu, q8):
     want = ref.encode_packed(ids, cu)
     del ref
     torch.cuda.empty_cache()
-    assert_parity(got, want, f"c3-full q8={q8}")
+    assert_parity(got, want, f"c3-full q8={q8}", Q8_COSINE_MIN if q8 else GPU_COSINE_MIN)
 
 
 # ---------------------------------------------------------------------------
@@ -180,9 +196,9 @@ def test_encode_device_matches_host(gpu):
     d_ids = torch.from_numpy(ids).cuda()
     d_out = torch.empty((len(cu) - 1, cfg.hidden_size), dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
-    m.encode_device(d_ids.data_ptr(), cu, 0, d_out.data_ptr(),
-                    stream=torch.cuda.current_stream().cuda_stream)
-    m.sync(stream=torch.cuda.current_stream().cuda_stream)
+    s = torch.cuda.Stream()
+    m.encode_device(d_ids.data_ptr(), cu, 0, d_out.data_ptr(), stream=s.cuda_stream)
+    m.sync(stream=s.cuda_stream)
     assert np.array_equal(d_out.cpu().numpy(), host)
     assert m.launch_count() > 0
 
