@@ -261,15 +261,17 @@ def main():
     per_launch_ms = tk["ms"] / tk["launches"]
     achieved = tk["flops"] / tk["launches"] / (per_launch_ms / 1e3) / 1e12
     peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
-    traffic = None
-    tf = ROOT / "profiles" / "traffic_per_launch.json"
+    # DRAM traffic of the dominant kernel from the committed ncu capture,
+    # scaled from bytes per token to this bench's average launch.
+    traffic, traffic_src = None, None
+    tf = ROOT / "profiles" / "traffic_per_launch.txt"
     if tf.exists():
-        try:
-            td = json.loads(tf.read_text()).get(top)
-            if td:
-                traffic = td["bytes_per_token"] * (tk["flops"] / tk["launches"]) / td["flops_per_token"]
-        except (ValueError, KeyError, ZeroDivisionError):
-            traffic = None
+        for ln in tf.read_text().splitlines():
+            f = ln.split()
+            if len(f) >= 4 and f[0] == top and not ln.startswith("#"):
+                tokens_per_launch = tk["flops"] / tk["launches"] / float(f[2])
+                traffic = round(float(f[1]) * tokens_per_launch)
+                traffic_src = f"profiles/{f[3]} (scaled per token)"
     total_ms = sum(v["ms"] for v in prof.values()) / args.steps
     breakdown = {k: {"ms_per_step": round(v["ms"] / args.steps, 3),
                      "share": round(v["ms"] / args.steps / total_ms, 4),
@@ -319,7 +321,8 @@ def main():
             "roofline": {"kernel": top, "bound": "tensor", "achieved": round(achieved, 1),
                          "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_src} bf16_tflops_sustained",
-                         "traffic": traffic, "launches_per_step": tk["launches"] // args.steps,
+                         "traffic": traffic, "traffic_source": traffic_src,
+                         "launches_per_step": tk["launches"] // args.steps,
                          "avg_launch_ms": round(per_launch_ms, 4),
                          "profiled_ms_per_step": round(prof_ms, 3)},
             "stages": breakdown,

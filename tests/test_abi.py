@@ -1,0 +1,72 @@
+"""The C-ABI library loads and exports every declared entry point; errors
+come back as codes and messages, never crashes (no GPU needed)."""
+from __future__ import annotations
+
+import ctypes as C
+import re
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, ROOT
+from futon_b200 import FutonError, Model, _lib
+from futon_b200.pack import load_pack
+
+
+def declared(header) -> set:
+    text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+    return set(re.findall(r"\b((?:futon|fo)_\w+)\s*\(", text))
+
+
+def test_header_symbols_exported():
+    names = declared(ROOT / "include" / "futon_cuda.h")
+    assert names == set(_lib.EXPORTED), names ^ set(_lib.EXPORTED)
+    lib = C.CDLL(str(_lib.LIB_PATH))
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_oracle_header_symbols_exported():
+    from oracle import oracle as O
+    names = declared(ROOT / "oracle" / "futon_oracle.h")
+    lib = C.CDLL(str(O.build()))
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_device_count_is_int():
+    assert isinstance(_lib.device_count(), int)
+
+
+def test_stage_names():
+    L = _lib.lib()
+    n = L.futon_cuda_profile_stage_count()
+    names = [L.futon_cuda_profile_stage_name(i).decode() for i in range(n)]
+    assert "gemm_fc1" in names and "attention" in names
+    assert L.futon_cuda_profile_stage_name(n) == b""
+
+
+def test_create_rejects_without_crashing():
+    """Bad configurations return FUTON_EINVAL with a message (no GPU needed:
+    validation runs before any device work)."""
+    p = load_pack(GOLDEN / "toy-absolute-gelu")
+    cfg = _lib.FutonCfg()
+    handle = C.c_void_p()
+    devs = (C.c_int * 1)(0)
+    with pytest.raises(FutonError, match="non-positive"):
+        _lib.call("futon_cuda_model_create", C.byref(cfg), None, 0, devs, 1, 0, C.byref(handle))
+    if _lib.device_count() == 0:
+        with pytest.raises(FutonError):
+            Model(p.cfg, p.tensors, devices=[0])
+
+
+def test_null_model_calls_return_errors():
+    ids = np.array([2, 3], np.int32)
+    cu = np.array([0, 2], np.int32)
+    out = np.zeros((1, 32), np.float32)
+    with pytest.raises(FutonError, match="null model"):
+        _lib.call("futon_cuda_encode", None, 0, ids.ctypes.data, cu.ctypes.data, 1, 0,
+                  out.ctypes.data, None)
+    with pytest.raises(FutonError, match="null model"):
+        _lib.call("futon_cuda_sync", None, 0, None)
+    assert _lib.lib().futon_cuda_launch_count(None, 0) == -1

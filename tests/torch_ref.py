@@ -40,7 +40,7 @@ class TorchRef:
     def __init__(self, cfg, tensors: Dict[str, np.ndarray], device="cpu", dtype=torch.float32,
                  q8: bool = False):
         self.cfg, self.dev, self.dt, self.q8 = cfg, torch.device(device), dtype, q8
-        self.t = {k: torch.as_tensor(np.asarray(v, dtype=np.float32)).to(self.dev, dtype)
+        self.t = {k: torch.as_tensor(np.array(v, dtype=np.float32)).to(self.dev, dtype)
                   for k, v in tensors.items()}
         self.qw = {}
         if q8:
