@@ -1308,3 +1308,109 @@ int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, con
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// Q8 GEMM without allocation
+//
+// For callers that may not allocate device memory once they are running: a
+// serving loop whose HBM is already reserved by another allocator (a PyTorch
+// caching allocator or an inference-server arena can hold all free memory),
+// or a latency-critical path that cannot afford cudaMalloc/cudaFree
+// (cudaFree synchronises the whole device). The quantised activations and
+// their scales go to a fixed array in this library's device image instead of
+// allocated scratch. The array (kNoAllocScratchBytes) is resident on every
+// GPU that loads the library, until the process exits.
+// ===========================================================================
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB
+__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+__device__ __align__(256) int g_noalloc_err;
+
+struct NoAllocDev {
+  bool ready = false;
+  uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch
+  int* err = nullptr;          // device address of g_noalloc_err
+  int num_sms = 148;
+};
+NoAllocDev g_noalloc[64];
+std::mutex g_noalloc_mu;
+
+// Resolves the device addresses of the static arrays on the current device
+// (host code must not use the arrays' names as device pointers).
+int noalloc_setup(int dev, NoAllocDev** out, char* err, size_t errlen) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDev& s = g_noalloc[dev];
+  if (!s.ready) {
+    void* p = nullptr;
+    CU_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    s.scratch = static_cast<uint8_t*>(p);
+    CU_TRY(cudaGetSymbolAddress(&p, g_noalloc_err));
+    s.err = static_cast<int*>(p);
+    CU_TRY(cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev));
+    s.ready = true;
+  }
+  *out = &s;
+  return FUTON_OK;
+}
+
+}  // namespace
+
+extern "C" int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const float* a,
+                                              const int8_t* qb, const float* scales, int m, int n,
+                                              int k, const float* bias, void* stream, char* err,
+                                              size_t errlen) {
+  if (cuda_device < 0 || cuda_device >= 64)
+    return set_err(err, errlen, FUTON_EINVAL, "native: bad device %d", cuda_device);
+  if (m < 0 || n <= 0 || k <= 0 || k % 16)
+    return set_err(err, errlen, FUTON_EINVAL,
+                   "native: q8 matmul shape m=%d n=%d k=%d (k %% 16 == 0)", m, n, k);
+  const size_t qbytes = align_up((size_t)m * k, 256), need = qbytes + (size_t)m * 4;
+  if (need > kNoAllocScratchBytes)
+    return set_err(err, errlen, FUTON_EINVAL,
+                   "native: q8 no-alloc scratch needs %zu bytes for m=%d k=%d; the fixed "
+                   "scratch holds %zu (m·k + 4·m, rounded)", need, m, k, kNoAllocScratchBytes);
+  if (m == 0) return FUTON_OK;
+  CU_TRY(cudaSetDevice(cuda_device));
+  NoAllocDev* s;
+  int rc;
+  if ((rc = noalloc_setup(cuda_device, &s, err, errlen))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int8_t* qa = reinterpret_cast<int8_t*>(s->scratch);
+  float* sa = reinterpret_cast<float*>(s->scratch + qbytes);
+  CU_TRY(cudaMemsetAsync(s->err, 0, sizeof(int), st));
+  quant_rows_kernel<<<grid_rows(m, 8, s->num_sms), 256, 0, st>>>(a, m, k, qa, sa);
+  CU_TRY(cudaGetLastError());
+  CUtensorMap ta, tw;
+  const int bn = pick_bn(n);
+  if (!make_operand_map(&ta, qa, true, (uint64_t)m, (uint64_t)k, 128) ||
+      !make_operand_map(&tw, qb, true, (uint64_t)n, (uint64_t)k, (uint32_t)bn))
+    return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed");
+  GemmLaunch g;
+  g.ta = &ta;
+  g.tw = &tw;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.bn = bn;
+  g.epi = kEpiStore;
+  g.out_f32 = true;
+  g.ep.out = dst;
+  g.ep.ldo = n;
+  g.ep.bias = bias;
+  g.ep.resid = nullptr;
+  g.ep.ldr = 0;
+  g.ep.a_scale = sa;
+  g.ep.w_scale = scales;
+  g.err = s->err;
+  g.num_sms = s->num_sms;
+  g.stream = st;
+  cudaError_t e = launch_gemm_s8(g);
+  if (e != cudaSuccess)
+    return set_err(err, errlen, FUTON_ECUDA, "native: gemm launch: %s", cudaGetErrorString(e));
+  CU_TRY(cudaStreamSynchronize(st));
+  int code = 0;
+  CU_TRY(cudaMemcpy(&code, s->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code) return set_err(err, errlen, FUTON_EDEVICE, "native: device-side error %d", code);
+  return FUTON_OK;
+}

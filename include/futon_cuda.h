@@ -161,6 +161,24 @@ int futon_cuda_matmul_t_q8(int cuda_device, float* dst, const float* a, const in
 int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, const float* src,
                                 int rows, int k, void* stream, char* err, size_t errlen);
 
+/* futon_cuda_matmul_t_q8 for callers that must not allocate device memory
+ * (no counterpart in the reference): a serving loop whose HBM another
+ * allocator already holds, or a latency-critical path where cudaMalloc or
+ * cudaFree (which synchronises the device) is not acceptable. Same inputs,
+ * outputs and bit-exact results as futon_cuda_matmul_t_q8, but the quantised
+ * activations and scales go to a fixed 4 MiB array in the library's device
+ * image (resident on every GPU that loads the library until exit), so
+ * m·k + 4·m bytes (each part rounded up to 256) must fit in 4 MiB; larger
+ * shapes are rejected with FUTON_EINVAL. The first call on a device resolves
+ * that array's device address; make it before any stream capture. The call
+ * allocates nothing, zeroes its device error word, and waits for its stream.
+ * All calls on a device share the one array: calls whose GPU work overlaps
+ * (other host threads, other streams) race and must be serialised by the
+ * caller. */
+int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const float* a, const int8_t* qb,
+                                   const float* scales, int m, int n, int k, const float* bias,
+                                   void* stream, char* err, size_t errlen);
+
 #ifdef __cplusplus
 }
 #endif
