@@ -9,16 +9,19 @@
 // (model.go:674-685) is applied to q and k while they are staged, from the
 // f32 cos/sin tables built like precomputeRoPE (model.go:306-318).
 //
+// q and k arrive rotated: NeoX RoPE (model.go:674-685) runs in the qkv GEMM
+// epilogue, on the f32 accumulator.
+//
 // Kernels:
-//   attn_flash_kernel  64 query rows × one head per CTA, 64-key tiles,
-//                      bf16 m16n8k16 tensor-core MMAs with f32 accumulation
-//                      and online softmax (head_dim 32 or 64).
-//   attn_flash_split_kernel  the same over f32 qkv with every operand split
-//                      into bf16 hi + lo parts (int8 path).
+//   attn_heads_kernel  one 64-query tile of one sequence per CTA, all heads
+//                      in turn, 64-key tiles staged by cp.async in a two-slot
+//                      ring, bf16 m16n8k16 tensor-core MMAs with f32
+//                      accumulation and online softmax (head_dim 32 or 64);
+//                      also the CLS-only last layer (model.go:403-410).
+//   attn_flash_split_kernel  int8 path: 64 queries × one head per CTA over
+//                      f32 qkv, every operand split into bf16 hi + lo parts.
 //   attn_rowq_kernel   one warp per (query, head): lanes split the keys,
-//                      f32 math, warp merge. Serves CLS-pooled last layers
-//                      (one query per sequence, model.go:403-410) and any
-//                      head_dim the flash kernel does not cover.
+//                      f32 math, warp merge (head dims other than 32/64).
 #pragma once
 
 #include "common.cuh"
@@ -58,57 +61,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&p);
 }
 
-// Stages rows [r0, r0+64) of one head's q or k (with RoPE) or v into shared
-// memory as bf16, zero-filling rows at or past L. src points at row 0 of the
-// sequence for this head's columns; ld is the qkv row stride.
-template <int HD, bool ROPE>
-__device__ __forceinline__ void stage_rows(__nv_bfloat16* dst, int lds, const __nv_bfloat16* src,
-                                           int ld, int r0, int L, const float* rcos,
-                                           const float* rsin) {
-  constexpr int kRows = 64;
-  if constexpr (ROPE) {
-    constexpr int kHalf = HD / 2;
-    constexpr int kChunks = kHalf / 8;  // 8 rotation pairs per work item
-    for (int w = threadIdx.x; w < kRows * kChunks; w += blockDim.x) {
-      const int r = w / kChunks, c = (w % kChunks) * 8;
-      const int pos = r0 + r;
-      uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-      if (pos < L) {
-        const __nv_bfloat16* p = src + (size_t)pos * ld;
-        uint4 x1 = *reinterpret_cast<const uint4*>(p + c);
-        uint4 x2 = *reinterpret_cast<const uint4*>(p + c + kHalf);
-        const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(&x1);
-        const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&x2);
-        const float* cr = rcos + (size_t)pos * kHalf + c;
-        const float* sr = rsin + (size_t)pos * kHalf + c;
-        float y1[8], y2[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float v1 = __bfloat162float(a[i]), v2 = __bfloat162float(b[i]);
-          float cc = cr[i], ss = sr[i];
-          y1[i] = v1 * cc - v2 * ss;
-          y2[i] = v2 * cc + v1 * ss;
-        }
-        lo = make_uint4(pack_bf16(y1[0], y1[1]), pack_bf16(y1[2], y1[3]), pack_bf16(y1[4], y1[5]),
-                        pack_bf16(y1[6], y1[7]));
-        hi = make_uint4(pack_bf16(y2[0], y2[1]), pack_bf16(y2[2], y2[3]), pack_bf16(y2[4], y2[5]),
-                        pack_bf16(y2[6], y2[7]));
-      }
-      *reinterpret_cast<uint4*>(dst + r * lds + c) = lo;
-      *reinterpret_cast<uint4*>(dst + r * lds + c + kHalf) = hi;
-    }
-  } else {
-    constexpr int kChunks = HD / 8;
-    for (int w = threadIdx.x; w < kRows * kChunks; w += blockDim.x) {
-      const int r = w / kChunks, c = (w % kChunks) * 8;
-      const int pos = r0 + r;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (pos < L) v = *reinterpret_cast<const uint4*>(src + (size_t)pos * ld + c);
-      *reinterpret_cast<uint4*>(dst + r * lds + c) = v;
-    }
-  }
-}
-
 template <typename T> __device__ __forceinline__ void store2(T* dst, float a, float b);
 template <> __device__ __forceinline__ void store2<float>(float* dst, float a, float b) {
   *reinterpret_cast<float2*>(dst) = make_float2(a, b);
@@ -116,132 +68,6 @@ template <> __device__ __forceinline__ void store2<float>(float* dst, float a, f
 template <> __device__ __forceinline__ void store2<__nv_bfloat16>(__nv_bfloat16* dst, float a,
                                                                   float b) {
   *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(a, b);
-}
-
-// grid = (num_tiles, num_heads), block = 128 (4 warps × 16 query rows).
-template <int HD, bool ROPE, typename OutT>
-__global__ void __launch_bounds__(128)
-    attn_flash_kernel(const __nv_bfloat16* __restrict__ qkv, int hidden,
-                      const int* __restrict__ cu_seqlens, const AttnTile* __restrict__ tiles,
-                      const float* __restrict__ rcos, const float* __restrict__ rsin,
-                      float scale_log2, OutT* __restrict__ out, int ldo) {
-  constexpr int kBQ = 64, kBK = 64, kLds = HD + 8;
-  __shared__ __align__(16) __nv_bfloat16 sQ[kBQ * kLds];
-  __shared__ __align__(16) __nv_bfloat16 sK[kBK * kLds];
-  __shared__ __align__(16) __nv_bfloat16 sV[kBK * kLds];
-
-  const AttnTile tile = tiles[blockIdx.x];
-  const int head = blockIdx.y;
-  const int s0 = cu_seqlens[tile.seq];
-  const int L = cu_seqlens[tile.seq + 1] - s0;
-  const int ld = 3 * hidden;
-  const __nv_bfloat16* qg = qkv + (size_t)s0 * ld + head * HD;
-  const __nv_bfloat16* kg = qg + hidden;
-  const __nv_bfloat16* vg = qg + 2 * hidden;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  stage_rows<HD, ROPE>(sQ, kLds, qg, ld, tile.q0, L, rcos, rsin);
-  __syncthreads();
-
-  uint32_t qf[HD / 16][4];
-#pragma unroll
-  for (int kc = 0; kc < HD / 16; ++kc)
-    ldsm_x4(qf[kc], smem_u32(&sQ[(warp * 16 + (lane & 15)) * kLds + kc * 16 + (lane >> 4) * 8]));
-
-  float o[HD / 8][4];
-#pragma unroll
-  for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY};
-  float l_run[2] = {0.f, 0.f};
-
-  for (int kv0 = 0; kv0 < L; kv0 += kBK) {
-    __syncthreads();
-    stage_rows<HD, ROPE>(sK, kLds, kg, ld, kv0, L, rcos, rsin);
-    stage_rows<HD, false>(sV, kLds, vg, ld, kv0, L, nullptr, nullptr);
-    __syncthreads();
-
-    float s[kBK / 8][4];
-#pragma unroll
-    for (int nb = 0; nb < kBK / 8; ++nb) {
-      s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
-#pragma unroll
-      for (int kc = 0; kc < HD / 16; ++kc) {
-        uint32_t kf[2];
-        ldsm_x2(kf, smem_u32(&sK[(nb * 8 + (lane & 7)) * kLds + kc * 16 + ((lane >> 3) & 1) * 8]));
-        mma_16816(s[nb], qf[kc], kf);
-      }
-    }
-    // Scale into the log2 domain and mask keys past the sequence end.
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int nb = 0; nb < kBK / 8; ++nb) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = kv0 + nb * 8 + (lane & 3) * 2 + (e & 1);
-        float v = (key < L) ? s[nb][e] * scale_log2 : -INFINITY;
-        s[nb][e] = v;
-        mx[e >> 1] = fmaxf(mx[e >> 1], v);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-    }
-    float alpha[2];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const float m_new = fmaxf(m_run[r], mx[r]);
-      alpha[r] = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - m_new);
-      m_run[r] = m_new;
-      l_run[r] *= alpha[r];
-    }
-#pragma unroll
-    for (int nb = 0; nb < kBK / 8; ++nb) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float p = exp2f(s[nb][e] - m_run[e >> 1]);
-        s[nb][e] = p;
-        l_run[e >> 1] += p;
-      }
-    }
-#pragma unroll
-    for (int nd = 0; nd < HD / 8; ++nd) {
-      o[nd][0] *= alpha[0];
-      o[nd][1] *= alpha[0];
-      o[nd][2] *= alpha[1];
-      o[nd][3] *= alpha[1];
-    }
-#pragma unroll
-    for (int kc = 0; kc < kBK / 16; ++kc) {
-      uint32_t pf[4];
-      pf[0] = pack_bf16(s[2 * kc][0], s[2 * kc][1]);
-      pf[1] = pack_bf16(s[2 * kc][2], s[2 * kc][3]);
-      pf[2] = pack_bf16(s[2 * kc + 1][0], s[2 * kc + 1][1]);
-      pf[3] = pack_bf16(s[2 * kc + 1][2], s[2 * kc + 1][3]);
-#pragma unroll
-      for (int nd = 0; nd < HD / 8; ++nd) {
-        uint32_t vf[2];
-        ldsm_x2_t(vf, smem_u32(&sV[(kc * 16 + (lane & 15)) * kLds + nd * 8]));
-        mma_16816(o[nd], pf, vf);
-      }
-    }
-  }
-
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
-  }
-  const float inv0 = 1.f / l_run[0], inv1 = 1.f / l_run[1];
-  const int qr0 = tile.q0 + warp * 16 + (lane >> 2);
-  const int qr1 = qr0 + 8;
-#pragma unroll
-  for (int nd = 0; nd < HD / 8; ++nd) {
-    const int col = head * HD + nd * 8 + (lane & 3) * 2;
-    if (qr0 < L) store2<OutT>(out + (size_t)(s0 + qr0) * ldo + col, o[nd][0] * inv0, o[nd][1] * inv0);
-    if (qr1 < L) store2<OutT>(out + (size_t)(s0 + qr1) * ldo + col, o[nd][2] * inv1, o[nd][3] * inv1);
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -410,6 +236,176 @@ __global__ void __launch_bounds__(128)
     const int col = head * HD + nd * 8 + (lane & 3) * 2;
     if (qr0 < L) store2<float>(out + (size_t)(s0 + qr0) * ldo + col, o[nd][0] * inv0, o[nd][1] * inv0);
     if (qr1 < L) store2<float>(out + (size_t)(s0 + qr1) * ldo + col, o[nd][2] * inv1, o[nd][3] * inv1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// attn_heads_kernel: one CTA per 64-query tile of one sequence, looping over
+// every head. q, k, v arrive pre-rotated (RoPE is applied in the qkv GEMM
+// epilogue). Per (head, 64-key tile) step the CTA stages q (first step of a
+// head), k and v with cp.async into a two-slot ring, so the next step's
+// loads overlap this step's tensor-core work. cls_mode: CTA s computes only
+// query row 0 of sequence s (the CLS-pruned last layer) into row s of out.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait1() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
+
+// 64 rows × HD bf16 of one head into shared memory (row stride HD + 8);
+// rows at or past `lim` are zero-filled without reading.
+template <int HD>
+__device__ __forceinline__ void stage_async(__nv_bfloat16* dst, const __nv_bfloat16* src, int ld,
+                                            int r0, int lim) {
+  constexpr int kChunks = HD / 8, kLds = HD + 8;
+  for (int w = threadIdx.x; w < 64 * kChunks; w += blockDim.x) {
+    const int r = w / kChunks, c = (w % kChunks) * 8;
+    const bool ok = r0 + r < lim;
+    cp_async16(smem_u32(dst + r * kLds + c), ok ? src + (size_t)(r0 + r) * ld + c : src, ok);
+  }
+}
+
+template <int HD>
+constexpr int attn_heads_smem_bytes() { return 6 * 64 * (HD + 8) * 2; }
+
+// grid = ntiles (or nseq in cls_mode), block = 128 (4 warps × 16 query rows).
+template <int HD, typename OutT>
+__global__ void __launch_bounds__(128, 4)
+    attn_heads_kernel(const __nv_bfloat16* __restrict__ qkv, int hidden, int num_heads,
+                      const int* __restrict__ cu_seqlens, const AttnTile* __restrict__ tiles,
+                      int cls_mode, float scale_log2, OutT* __restrict__ out, int ldo) {
+  constexpr int kLds = HD + 8, kTile = 64 * kLds;
+  extern __shared__ __align__(16) __nv_bfloat16 sm_heads[];
+  __nv_bfloat16* sQ = sm_heads;             // [2][kTile], slot = head parity
+  __nv_bfloat16* sK = sm_heads + 2 * kTile; // [2][kTile], slot = step parity
+  __nv_bfloat16* sV = sm_heads + 4 * kTile;
+
+  const AttnTile tile = cls_mode ? AttnTile{(int)blockIdx.x, 0} : tiles[blockIdx.x];
+  const int s0 = cu_seqlens[tile.seq];
+  const int L = cu_seqlens[tile.seq + 1] - s0;
+  const int qlim = cls_mode ? 1 : L;  // query positions < qlim are real
+  const int ld = 3 * hidden;
+  const __nv_bfloat16* base = qkv + (size_t)s0 * ld;
+  const int nkv = (L + 63) / 64;
+  const int nsteps = num_heads * nkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  auto issue = [&](int step) {
+    const int hh = step / nkv, j = step - hh * nkv, slot = step & 1;
+    if (j == 0) stage_async<HD>(sQ + (hh & 1) * kTile, base + hh * HD, ld, tile.q0, qlim);
+    stage_async<HD>(sK + slot * kTile, base + hidden + hh * HD, ld, j * 64, L);
+    stage_async<HD>(sV + slot * kTile, base + 2 * hidden + hh * HD, ld, j * 64, L);
+    cp_async_commit();
+  };
+
+  uint32_t qf[HD / 16][4];
+  float o[HD / 8][4];
+  float m_run[2], l_run[2];
+  issue(0);
+  for (int step = 0; step < nsteps; ++step) {
+    if (step + 1 < nsteps) issue(step + 1);
+    else cp_async_commit();  // empty group keeps wait_group(1) uniform
+    cp_async_wait1();
+    __syncthreads();
+    const int head = step / nkv, j = step - head * nkv, slot = step & 1;
+    const __nv_bfloat16* kS = sK + slot * kTile;
+    const __nv_bfloat16* vS = sV + slot * kTile;
+    if (j == 0) {
+      const __nv_bfloat16* qS = sQ + (head & 1) * kTile;
+#pragma unroll
+      for (int kc = 0; kc < HD / 16; ++kc)
+        ldsm_x4(qf[kc], smem_u32(&qS[(warp * 16 + (lane & 15)) * kLds + kc * 16 + (lane >> 4) * 8]));
+#pragma unroll
+      for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      m_run[0] = m_run[1] = -INFINITY;
+      l_run[0] = l_run[1] = 0.f;
+    }
+    const int kv0 = j * 64;
+    float sc[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+      sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+#pragma unroll
+      for (int kc = 0; kc < HD / 16; ++kc) {
+        uint32_t kf[2];
+        ldsm_x2(kf, smem_u32(&kS[(nb * 8 + (lane & 7)) * kLds + kc * 16 + ((lane >> 3) & 1) * 8]));
+        mma_16816(sc[nb], qf[kc], kf);
+      }
+    }
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = kv0 + nb * 8 + (lane & 3) * 2 + (e & 1);
+        const float v = (key < L) ? sc[nb][e] * scale_log2 : -INFINITY;
+        sc[nb][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    float alpha[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float m_new = fmaxf(m_run[r], mx[r]);
+      alpha[r] = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - m_new);
+      m_run[r] = m_new;
+      l_run[r] *= alpha[r];
+    }
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p = exp2f(sc[nb][e] - m_run[e >> 1]);
+        sc[nb][e] = p;
+        l_run[e >> 1] += p;
+      }
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; ++nd) {
+      o[nd][0] *= alpha[0]; o[nd][1] *= alpha[0];
+      o[nd][2] *= alpha[1]; o[nd][3] *= alpha[1];
+    }
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      uint32_t pf[4];
+      pf[0] = pack_bf16(sc[2 * kc][0], sc[2 * kc][1]);
+      pf[1] = pack_bf16(sc[2 * kc][2], sc[2 * kc][3]);
+      pf[2] = pack_bf16(sc[2 * kc + 1][0], sc[2 * kc + 1][1]);
+      pf[3] = pack_bf16(sc[2 * kc + 1][2], sc[2 * kc + 1][3]);
+#pragma unroll
+      for (int nd = 0; nd < HD / 8; ++nd) {
+        uint32_t vf[2];
+        ldsm_x2_t(vf, smem_u32(&vS[(kc * 16 + (lane & 15)) * kLds + nd * 8]));
+        mma_16816(o[nd], pf, vf);
+      }
+    }
+    if (j == nkv - 1) {
+      float lsum[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        lsum[r] = l_run[r];
+        lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 1);
+        lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 2);
+      }
+      const float inv0 = 1.f / lsum[0], inv1 = 1.f / lsum[1];
+      const int qr0 = tile.q0 + warp * 16 + (lane >> 2), qr1 = qr0 + 8;
+      const size_t orow0 = cls_mode ? (size_t)tile.seq : (size_t)(s0 + qr0);
+      const size_t orow1 = (size_t)(s0 + qr1);
+#pragma unroll
+      for (int nd = 0; nd < HD / 8; ++nd) {
+        const int col = head * HD + nd * 8 + (lane & 3) * 2;
+        if (qr0 < qlim) store2<OutT>(out + orow0 * ldo + col, o[nd][0] * inv0, o[nd][1] * inv0);
+        if (qr1 < qlim) store2<OutT>(out + orow1 * ldo + col, o[nd][2] * inv1, o[nd][3] * inv1);
+      }
+    }
+    __syncthreads();  // every warp is done with this slot before it is refilled
   }
 }
 

@@ -124,16 +124,21 @@ struct LayerDev {
   float *n1w, *n1b, *n2w, *n2b;
 };
 
+// Float path: the residual stream is xb (bf16), updated in place by the
+// fused residual + LayerNorm epilogues; xf receives the f32 final hidden
+// state for pooling. Int8 path: the residual stream is x (f32) plus its int8
+// codes xq/xs; xb is unused.
 struct Workspace {
   size_t tokens = 0;  // capacity
   void* base = nullptr;
-  float* x;
-  bf16* xb;
+  float* x;          // int8 path: residual stream (f32)
+  bf16* xb;          // float path: residual stream / GEMM operand (bf16)
+  float* xf;         // float path: final hidden rows (f32) for pooling
   void* qkv;         // bf16 (float path) or f32 (q8 path)
   void* attn;        // bf16 (float path) or f32 (q8 path)
   void* ffn;         // bf16 or f32
-  float* tmp;
-  float* xc;         // CLS rows of the residual stream
+  float* tmp;        // pre-LayerNorm sums when LayerNorm is not fused
+  void* xc;          // CLS rows of the residual stream (bf16 or f32)
   int8_t *xq, *attnq, *ffnq;
   float *xs, *attns, *ffns;
 };
@@ -194,6 +199,7 @@ struct DevCtx {
 struct futon_model {
   futon_cfg cfg;
   int q8 = 0;
+  bool fuse_ln = false;  // residual + LayerNorm fused into the out/fc2 GEMMs (hidden == 384)
   int head_dim = 0;
   int eff_max = 0;
   int swiglu_half = 0;
@@ -344,8 +350,8 @@ int upload_f32(DevCtx& d, float** dst, const float* src, size_t count, char* err
 // Uploads a GEMM weight (optionally two interleaved halves for SwiGLU) as
 // bf16 or int8 + per-row scales, builds its bias and its TMA descriptor.
 int upload_gemm(DevCtx& d, GemmWeight& g, const float* w1, const float* b1, const float* w2,
-                const float* b2, int n1, int k, int half, bool q8, float* staging, char* err,
-                size_t errlen) {
+                const float* b2, int n1, int k, int half, bool q8, bool full_row, float* staging,
+                char* err, size_t errlen) {
   const int n = w2 ? 2 * n1 : n1;
   g.n = n;
   g.k = k;
@@ -389,8 +395,9 @@ int upload_gemm(DevCtx& d, GemmWeight& g, const float* w1, const float* b1, cons
     }
     if ((rc = upload_f32(d, &g.bias, hb.data(), (size_t)n, err, errlen))) return rc;
   }
-  g.bn = w2 ? 2 * half : pick_bn(n);
-  if (!make_operand_map(&g.map, g.w, q8, (uint64_t)n, (uint64_t)k, (uint32_t)g.bn))
+  g.bn = w2 ? 2 * half : (full_row ? n : pick_bn(n));
+  const uint32_t box = g.bn <= 256 ? (uint32_t)g.bn : (uint32_t)g.bn / 2;
+  if (!make_operand_map(&g.map, g.w, q8, (uint64_t)n, (uint64_t)k, box))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed for a weight");
   return FUTON_OK;
 }
@@ -408,10 +415,11 @@ int ensure_workspace(const futon_model& m, DevCtx& d, size_t tokens, char* err, 
   const bool q8 = m.q8 != 0;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
-  const size_t o_x = take(T * h * 4), o_xb = take(T * h * 2);
+  const size_t o_x = q8 ? take(T * h * 4) : 0, o_xb = q8 ? 0 : take(T * h * 2);
+  const size_t o_xf = q8 ? 0 : take(T * h * 4);
   const size_t o_qkv = take(T * 3 * h * (q8 ? 4 : 2));
   const size_t o_attn = take(T * h * (q8 ? 4 : 2)), o_ffn = take(T * I * (q8 ? 4 : 2));
-  const size_t o_tmp = take(T * h * 4), o_xc = take(T * h * 4);
+  const size_t o_tmp = (q8 || !m.fuse_ln) ? take(T * h * 4) : 0, o_xc = take(T * h * (q8 ? 4 : 2));
   size_t o_xq = 0, o_aq = 0, o_fq = 0, o_xs = 0, o_as = 0, o_fs = 0;
   if (q8) {
     o_xq = take(T * h); o_aq = take(T * h); o_fq = take(T * I);
@@ -423,13 +431,14 @@ int ensure_workspace(const futon_model& m, DevCtx& d, size_t tokens, char* err, 
   Workspace& w = d.ws;
   w.base = base;
   w.tokens = tokens;
-  w.x = (float*)(b + o_x);
-  w.xb = (bf16*)(b + o_xb);
+  w.x = q8 ? (float*)(b + o_x) : nullptr;
+  w.xb = q8 ? nullptr : (bf16*)(b + o_xb);
+  w.xf = q8 ? nullptr : (float*)(b + o_xf);
   w.qkv = b + o_qkv;
   w.attn = b + o_attn;
   w.ffn = b + o_ffn;
-  w.tmp = (float*)(b + o_tmp);
-  w.xc = (float*)(b + o_xc);
+  w.tmp = (q8 || !m.fuse_ln) ? (float*)(b + o_tmp) : nullptr;
+  w.xc = b + o_xc;
   w.xq = q8 ? (int8_t*)(b + o_xq) : nullptr;
   w.attnq = q8 ? (int8_t*)(b + o_aq) : nullptr;
   w.ffnq = q8 ? (int8_t*)(b + o_fq) : nullptr;
@@ -469,15 +478,35 @@ int ensure_host(T** p, size_t* cap, size_t count, char* err, size_t errlen) {
 }
 
 // ---- GEMM helper ---------------------------------------------------------
+struct GemmOut {
+  int epi = kEpiStore;
+  bool out_f32 = false;
+  void* out = nullptr;
+  int ldo = 0;
+  const void* resid = nullptr;
+  int ldr = 0;
+  bool resid_bf16 = false;
+  const float* ln_w = nullptr;
+  const float* ln_b = nullptr;
+  float eps = 0.f;
+  float* out_f32_copy = nullptr;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int rope_hd = 0;
+  int rope_cols = 0;
+  const int* cu = nullptr;
+  int nseq = 0;
+};
+
 int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale, int M,
-             const GemmWeight& w, int epi, bool out_f32, void* out, int ldo, const float* resid,
-             int ldr, cudaStream_t st, char* err, size_t errlen) {
+             const GemmWeight& w, const GemmOut& o, cudaStream_t st, char* err, size_t errlen) {
   if (M == 0) return FUTON_OK;
   const double esz = s8 ? 1.0 : 2.0;
-  const double out_cols = epi == kEpiSwiglu ? w.n / 2 : w.n;
-  const double osz = (out_f32 || (s8 && epi != kEpiStore)) ? 4.0 : 2.0;
+  const double out_cols = o.epi == kEpiSwiglu ? w.n / 2 : w.n;
+  const double osz = (o.out_f32 || (s8 && o.epi != kEpiStore)) ? 4.0 : 2.0;
+  const double rsz = o.resid ? (o.resid_bf16 ? 2.0 : 4.0) : 0.0;
   const double bytes = (double)M * w.k * esz + (double)w.n * w.k * esz + (double)M * out_cols * osz +
-                       (resid ? (double)M * w.n * 4.0 : 0.0);
+                       (double)M * w.n * rsz + (o.out_f32_copy ? (double)M * w.n * 4.0 : 0.0);
   ProfScope prof(d, st, stage, 2.0 * M * w.n * w.k, bytes);
   CUtensorMap ta;
   if (!make_operand_map(&ta, A, s8, (uint64_t)M, (uint64_t)w.k, 128))
@@ -489,15 +518,26 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   g.N = w.n;
   g.K = w.k;
   g.bn = w.bn;
-  g.epi = epi;
-  g.out_f32 = out_f32;
-  g.ep.out = out;
-  g.ep.ldo = ldo;
+  g.epi = o.epi;
+  g.out_f32 = o.out_f32;
+  g.ep.out = o.out;
+  g.ep.ldo = o.ldo;
   g.ep.bias = w.bias;
-  g.ep.resid = resid;
-  g.ep.ldr = ldr;
+  g.ep.resid = o.resid;
+  g.ep.ldr = o.ldr;
+  g.ep.resid_bf16 = o.resid_bf16 ? 1 : 0;
   g.ep.a_scale = a_scale;
   g.ep.w_scale = w.scale;
+  g.ep.ln_w = o.ln_w;
+  g.ep.ln_b = o.ln_b;
+  g.ep.eps = o.eps;
+  g.ep.out_f32 = o.out_f32_copy;
+  g.ep.rope_cos = o.rope_cos;
+  g.ep.rope_sin = o.rope_sin;
+  g.ep.rope_hd = o.rope_hd;
+  g.ep.rope_cols = o.rope_cols;
+  g.ep.cu = o.cu;
+  g.ep.nseq = o.nseq;
   g.err = d.err_word;
   g.num_sms = d.num_sms;
   g.stream = st;
@@ -515,59 +555,66 @@ inline int grid_rows(int rows, int per_block, int sms) {
 }
 
 // ---- attention dispatch --------------------------------------------------
-// Float path: bf16 qkv, bf16 tensor-core flash attention. Int8 path: f32 qkv
-// and split-precision (bf16 hi+lo) flash attention with f32 output, so the
-// per-row quantisation that follows sees float32-accurate values.
+// q and k arrive already rotated (RoPE runs in the qkv GEMM epilogue).
+// Float path: bf16 qkv, attn_heads_kernel (all heads per CTA) for regular
+// and CLS-only layers. Int8 path: f32 qkv and split-precision attention, so
+// the per-row quantisation that follows sees float32-accurate values.
+// Head dims other than 32/64 use the per-query kernel.
 template <typename InT, typename OutT>
 int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* cu,
                   const AttnTile* tiles, int ntiles, bool cls_only, const InT* qkv, OutT* out,
                   cudaStream_t st, char* err, size_t errlen) {
   const int h = m.cfg.hidden_size, H = m.cfg.num_heads, hd = m.head_dim;
-  const bool rope = m.cfg.position_encoding == FUTON_POS_ROPE;
   const float scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
   constexpr bool kSplit = sizeof(InT) == 4;
-  if (!cls_only && (hd == 32 || hd == 64) && ntiles > 0) {
-    dim3 grid(ntiles, H);
-    if constexpr (kSplit) {
+  const bool tc_hd = hd == 32 || hd == 64;
+  if constexpr (!kSplit) {
+    if (tc_hd) {
+      const int grid = cls_only ? nseq : ntiles;
+      if (grid == 0) return FUTON_OK;
+      auto launch = [&](auto kern, int smem) -> cudaError_t {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, 128, smem, st>>>(qkv, h, H, cu, tiles, cls_only ? 1 : 0, scale_log2, out, h);
+        return cudaGetLastError();
+      };
+      CU_TRY(hd == 32 ? launch(attn_heads_kernel<32, OutT>, attn_heads_smem_bytes<32>())
+                      : launch(attn_heads_kernel<64, OutT>, attn_heads_smem_bytes<64>()));
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+      return FUTON_OK;
+    }
+  } else {
+    if (tc_hd && !cls_only && ntiles > 0) {
+      dim3 grid(ntiles, H);
       const int smem = 6 * 64 * (hd + 8) * 2;
       auto launch = [&](auto kern) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        kern<<<grid, 128, smem, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
+        kern<<<grid, 128, smem, st>>>(qkv, h, cu, tiles, nullptr, nullptr, scale_log2, out, h);
         return cudaGetLastError();
       };
-      cudaError_t e;
-      if (hd == 32) e = rope ? launch(attn_flash_split_kernel<32, true>) : launch(attn_flash_split_kernel<32, false>);
-      else e = rope ? launch(attn_flash_split_kernel<64, true>) : launch(attn_flash_split_kernel<64, false>);
-      CU_TRY(e);
-    } else {
-      if (hd == 32) {
-        if (rope) attn_flash_kernel<32, true, OutT><<<grid, 128, 0, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
-        else attn_flash_kernel<32, false, OutT><<<grid, 128, 0, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
-      } else {
-        if (rope) attn_flash_kernel<64, true, OutT><<<grid, 128, 0, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
-        else attn_flash_kernel<64, false, OutT><<<grid, 128, 0, st>>>(qkv, h, cu, tiles, d.rcos, d.rsin, scale_log2, out, h);
-      }
+      CU_TRY(hd == 32 ? launch(attn_flash_split_kernel<32, false>)
+                      : launch(attn_flash_split_kernel<64, false>));
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+      return FUTON_OK;
     }
-  } else {
-    const int nq = cls_only ? nseq : T;
-    const long warps = (long)nq * H;
-    const int blocks = (int)((warps * 32 + 255) / 256);
-    if (blocks == 0) return FUTON_OK;
+  }
+  const int nq = cls_only ? nseq : T;
+  const long warps = (long)nq * H;
+  const int blocks = (int)((warps * 32 + 255) / 256);
+  if (blocks == 0) return FUTON_OK;
 #define FUTON_ROWQ(HD_)                                                                   \
   attn_rowq_kernel<HD_, InT, OutT><<<blocks, 256, 0, st>>>(qkv, h, H, cu, nseq, nq,         \
-                                                          cls_only ? 1 : 0, d.rcos, d.rsin, \
-                                                          rope ? 1 : 0, scale_log2, out, h)
-    switch (hd) {
-      case 8: FUTON_ROWQ(8); break;
-      case 16: FUTON_ROWQ(16); break;
-      case 32: FUTON_ROWQ(32); break;
-      case 64: FUTON_ROWQ(64); break;
-      case 128: FUTON_ROWQ(128); break;
-      default: return set_err(err, errlen, FUTON_EINVAL, "native: unsupported head_dim %d", hd);
-    }
-#undef FUTON_ROWQ
+                                                          cls_only ? 1 : 0, nullptr, nullptr, \
+                                                          0, scale_log2, out, h)
+  switch (hd) {
+    case 8: FUTON_ROWQ(8); break;
+    case 16: FUTON_ROWQ(16); break;
+    case 32: FUTON_ROWQ(32); break;
+    case 64: FUTON_ROWQ(64); break;
+    default: return set_err(err, errlen, FUTON_EINVAL, "native: unsupported head_dim %d", hd);
   }
+#undef FUTON_ROWQ
   CU_TRY(cudaGetLastError());
   d.launches.fetch_add(1, std::memory_order_relaxed);
   return FUTON_OK;
@@ -583,13 +630,13 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
   const int h = c.hidden_size, I = c.intermediate_size;
   const bool q8 = m.q8 != 0, cls = c.pooling == FUTON_POOL_CLS;
   const float eps = (float)c.layer_norm_eps;
-  const double qsz = q8 ? 1.0 : 0.0;  // int8 copy bytes per element written by LN
   Workspace& w = d.ws;
   int rc;
 
   {
     const double pos_bytes = c.position_encoding == FUTON_POS_ABSOLUTE ? 4.0 * h : 0.0;
-    ProfScope prof(d, st, kStEmbed, 0.0, (double)T * (4.0 + 4.0 * h + pos_bytes + 6.0 * h + qsz * h));
+    const double out_bytes = q8 ? 5.0 * h : 2.0 * h;
+    ProfScope prof(d, st, kStEmbed, 0.0, (double)T * (4.0 + 4.0 * h + pos_bytes + out_bytes));
     embed_ln_kernel<<<grid_rows(T, 8, d.num_sms), 256, 0, st>>>(
         ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0, d.pos, d.embw, d.embb, eps,
         w.x, w.xb, w.xq, w.xs);
@@ -601,13 +648,29 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
     if (cancel && *cancel)
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
     const LayerDev& L = d.layers[li];
-    const bool last_cls = cls && li == c.num_layers - 1;
+    const bool last = li == c.num_layers - 1;
+    const bool last_cls = cls && last;
     const int rows = last_cls ? nseq : T;
 
     // qkv = x·Wqkvᵀ + b → [T, 3h] (bf16; f32 on the int8 path)
-    if ((rc = run_gemm(d, kStGemmQkv, q8 ? (const void*)w.xq : w.xb, q8, w.xs, T, L.qkv, kEpiStore,
-                       q8, w.qkv, 3 * h, nullptr, 0, st, err, errlen)))
-      return rc;
+    {
+      GemmOut o;
+      o.epi = kEpiStore;
+      o.out_f32 = q8;
+      o.out = w.qkv;
+      o.ldo = 3 * h;
+      if (c.position_encoding == FUTON_POS_ROPE) {
+        o.rope_cos = d.rcos;
+        o.rope_sin = d.rsin;
+        o.rope_hd = m.head_dim;
+        o.rope_cols = 2 * h;
+        o.cu = cu;
+        o.nseq = nseq;
+      }
+      if ((rc = run_gemm(d, kStGemmQkv, q8 ? (const void*)w.xq : w.xb, q8, w.xs, T, L.qkv, o, st,
+                         err, errlen)))
+        return rc;
+    }
 
     // attention → attn [rows, h]
     {
@@ -624,17 +687,56 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       if (rc) return rc;
     }
 
-    const float* resid = w.x;
+    // Residual stream rows for this layer's query side.
+    const void* resid = q8 ? (const void*)w.x : (const void*)w.xb;
     if (last_cls) {
-      ProfScope prof(d, st, kStGather, 0.0, (double)nseq * 8.0 * h);
-      gather_rows_kernel<<<grid_rows(nseq * (h / 4), 256, d.num_sms), 256, 0, st>>>(
-          w.x, cu, nseq, h, w.xc, nullptr);
+      const size_t esz = q8 ? 4 : 2;
+      ProfScope prof(d, st, kStGather, 0.0, (double)nseq * 2.0 * h * esz);
+      const int blocks = grid_rows((int)((size_t)nseq * h * esz / 16), 256, d.num_sms);
+      if (q8) gather_rows_kernel<float><<<blocks, 256, 0, st>>>(w.x, cu, nseq, h, (float*)w.xc);
+      else gather_rows_kernel<bf16><<<blocks, 256, 0, st>>>(w.xb, cu, nseq, h, (bf16*)w.xc);
       CU_TRY(cudaGetLastError());
       d.launches.fetch_add(1, std::memory_order_relaxed);
       resid = w.xc;
     }
 
-    // out projection + residual → tmp f32, then LN1 → x, xb (, xq)
+    // Residual block: out = LN(x + W·a + b), written over the residual stream.
+    auto resid_ln = [&](int stage, const void* A, const float* a_scale, const GemmWeight& W,
+                        const void* res, const float* lnw, const float* lnb,
+                        bool f32_copy) -> int {
+      GemmOut o;
+      if (m.fuse_ln) {
+        o.epi = kEpiResidLN;
+        o.out = w.xb;
+        o.ldo = h;
+        o.resid = res;
+        o.ldr = h;
+        o.resid_bf16 = true;
+        o.ln_w = lnw;
+        o.ln_b = lnb;
+        o.eps = eps;
+        o.out_f32_copy = f32_copy ? w.xf : nullptr;
+        return run_gemm(d, stage, A, q8, a_scale, rows, W, o, st, err, errlen);
+      }
+      o.epi = kEpiResid;
+      o.out_f32 = true;
+      o.out = w.tmp;
+      o.ldo = h;
+      o.resid = res;
+      o.ldr = h;
+      o.resid_bf16 = !q8;
+      int r2 = run_gemm(d, stage, A, q8, a_scale, rows, W, o, st, err, errlen);
+      if (r2) return r2;
+      ProfScope prof(d, st, kStLayerNorm, 0.0, (double)rows * h * (q8 ? 9.0 : (f32_copy ? 10.0 : 6.0)));
+      float* xo = q8 ? w.x : (f32_copy ? w.xf : nullptr);
+      layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(
+          w.tmp, rows, h, lnw, lnb, eps, xo, q8 ? nullptr : w.xb, w.xq, w.xs);
+      CU_TRY(cudaGetLastError());
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+      return FUTON_OK;
+    };
+
+    // out projection + residual + LN1
     const void* a_out = w.attn;
     const float* a_out_s = nullptr;
     if (q8) {
@@ -646,25 +748,22 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       a_out = w.attnq;
       a_out_s = w.attns;
     }
-    if ((rc = run_gemm(d, kStGemmOut, a_out, q8, a_out_s, rows, L.out, kEpiResid, true, w.tmp, h,
-                       resid, h, st, err, errlen)))
-      return rc;
-    {
-      ProfScope prof(d, st, kStLayerNorm, 0.0, (double)rows * h * (10.0 + qsz));
-      layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(w.tmp, rows, h, L.n1w, L.n1b,
-                                                                     eps, w.x, w.xb, w.xq, w.xs);
-      CU_TRY(cudaGetLastError());
-      d.launches.fetch_add(1, std::memory_order_relaxed);
-    }
+    if ((rc = resid_ln(kStGemmOut, a_out, a_out_s, L.out, resid, L.n1w, L.n1b, false))) return rc;
 
     if (cancel && *cancel)
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
 
     // FFN
-    const int epi = c.activation == FUTON_ACT_SWIGLU ? kEpiSwiglu : kEpiGelu;
-    if ((rc = run_gemm(d, kStGemmFc1, q8 ? (const void*)w.xq : w.xb, q8, w.xs, rows, L.fc1, epi, q8,
-                       w.ffn, I, nullptr, 0, st, err, errlen)))
-      return rc;
+    {
+      GemmOut o;
+      o.epi = c.activation == FUTON_ACT_SWIGLU ? kEpiSwiglu : kEpiGelu;
+      o.out_f32 = q8;
+      o.out = w.ffn;
+      o.ldo = I;
+      if ((rc = run_gemm(d, kStGemmFc1, q8 ? (const void*)w.xq : w.xb, q8, w.xs, rows, L.fc1, o, st,
+                         err, errlen)))
+        return rc;
+    }
     const void* a_fc2 = w.ffn;
     const float* a_fc2_s = nullptr;
     if (q8) {
@@ -676,16 +775,8 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       a_fc2 = w.ffnq;
       a_fc2_s = w.ffns;
     }
-    if ((rc = run_gemm(d, kStGemmFc2, a_fc2, q8, a_fc2_s, rows, L.fc2, kEpiResid, true, w.tmp, h,
-                       w.x, h, st, err, errlen)))
-      return rc;
-    {
-      ProfScope prof(d, st, kStLayerNorm, 0.0, (double)rows * h * (10.0 + qsz));
-      layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(w.tmp, rows, h, L.n2w, L.n2b,
-                                                                     eps, w.x, w.xb, w.xq, w.xs);
-      CU_TRY(cudaGetLastError());
-      d.launches.fetch_add(1, std::memory_order_relaxed);
-    }
+    const void* resid2 = q8 ? (const void*)w.x : (const void*)w.xb;
+    if ((rc = resid_ln(kStGemmFc2, a_fc2, a_fc2_s, L.fc2, resid2, L.n2w, L.n2b, last))) return rc;
   }
 
   {
@@ -693,8 +784,8 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
     const double rows_read = cls ? (double)nseq : (double)T;
     ProfScope prof(d, st, kStPool, 0.0, rows_read * h * 4.0 + (double)nseq * dim * 4.0);
     const int mat_ln = c.matryoshka_layernorm ? 1 : 0;
-    pool_kernel<<<nseq, 256, h * sizeof(float), st>>>(w.x, cu, h, cls ? 0 : 1, out_dim, mat_ln,
-                                                      c.normalize ? 1 : 0, out);
+    pool_kernel<<<nseq, 256, h * sizeof(float), st>>>(q8 ? w.x : w.xf, cu, h, cls ? 0 : 1, out_dim,
+                                                      mat_ln, c.normalize ? 1 : 0, out);
     CU_TRY(cudaGetLastError());
     d.launches.fetch_add(1, std::memory_order_relaxed);
   }
@@ -918,8 +1009,19 @@ int seam_gemm(SeamCtx& s, const void* A, bool s8, const float* a_scale, int m, c
   g.ep.bias = bias;
   g.ep.resid = nullptr;
   g.ep.ldr = 0;
+  g.ep.resid_bf16 = 0;
   g.ep.a_scale = a_scale;
   g.ep.w_scale = w_scale;
+  g.ep.ln_w = nullptr;
+  g.ep.ln_b = nullptr;
+  g.ep.eps = 0.f;
+  g.ep.out_f32 = nullptr;
+  g.ep.rope_cos = nullptr;
+  g.ep.rope_sin = nullptr;
+  g.ep.rope_hd = 0;
+  g.ep.rope_cols = 0;
+  g.ep.cu = nullptr;
+  g.ep.nseq = 0;
   g.err = s.err_word;
   g.num_sms = s.num_sms;
   g.stream = st;
@@ -963,7 +1065,7 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
                    "native: hidden_size and intermediate_size must be multiples of 8 (hidden ≤ 1024)");
   if (q8 && (h % 16 || I % 16))
     return set_err(err, errlen, FUTON_EINVAL, "native: the int8 path needs K multiples of 16");
-  if (hd != 8 && hd != 16 && hd != 32 && hd != 64 && hd != 128)
+  if (hd != 8 && hd != 16 && hd != 32 && hd != 64)
     return set_err(err, errlen, FUTON_EINVAL, "native: unsupported head_dim %d", hd);
   const bool rope = c.position_encoding == FUTON_POS_ROPE, swiglu = c.activation == FUTON_ACT_SWIGLU;
   if (rope && !(c.rope_theta > 0))
@@ -1050,6 +1152,7 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
   model->head_dim = hd;
   model->eff_max = effective_max(c);
   model->swiglu_half = half;
+  model->fuse_ln = !q8 && h == 384;
 
   // RoPE tables (precomputeRoPE, model.go:306-318): f64 angles, f32 storage.
   std::vector<float> rc_tab, rs_tab;
@@ -1092,12 +1195,13 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
     for (int i = 0; i < c.num_layers && rc == FUTON_OK; ++i) {
       const LW& l = lw[i];
       LayerDev& L = d->layers[i];
-      if ((rc = upload_gemm(*d, L.qkv, l.qkvw, l.qkvb, nullptr, nullptr, 3 * h, h, 0, q8, staging, err, errlen))) break;
-      if ((rc = upload_gemm(*d, L.out, l.outw, l.outb, nullptr, nullptr, h, h, 0, q8, staging, err, errlen))) break;
-      if (swiglu) rc = upload_gemm(*d, L.fc1, l.fc1w, l.fc1b, l.gatew, l.gateb, I, h, half, q8, staging, err, errlen);
-      else rc = upload_gemm(*d, L.fc1, l.fc1w, l.fc1b, nullptr, nullptr, I, h, 0, q8, staging, err, errlen);
+      const bool fr = model->fuse_ln;
+      if ((rc = upload_gemm(*d, L.qkv, l.qkvw, l.qkvb, nullptr, nullptr, 3 * h, h, 0, q8, false, staging, err, errlen))) break;
+      if ((rc = upload_gemm(*d, L.out, l.outw, l.outb, nullptr, nullptr, h, h, 0, q8, fr, staging, err, errlen))) break;
+      if (swiglu) rc = upload_gemm(*d, L.fc1, l.fc1w, l.fc1b, l.gatew, l.gateb, I, h, half, q8, false, staging, err, errlen);
+      else rc = upload_gemm(*d, L.fc1, l.fc1w, l.fc1b, nullptr, nullptr, I, h, 0, q8, false, staging, err, errlen);
       if (rc) break;
-      if ((rc = upload_gemm(*d, L.fc2, l.fc2w, l.fc2b, nullptr, nullptr, h, I, 0, q8, staging, err, errlen))) break;
+      if ((rc = upload_gemm(*d, L.fc2, l.fc2w, l.fc2b, nullptr, nullptr, h, I, 0, q8, fr, staging, err, errlen))) break;
       if ((rc = upload_f32(*d, &L.n1w, l.n1w, h, err, errlen))) break;
       if ((rc = upload_f32(*d, &L.n1b, l.n1b, h, err, errlen))) break;
       if ((rc = upload_f32(*d, &L.n2w, l.n2w, h, err, errlen))) break;
@@ -1400,8 +1504,19 @@ extern "C" int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const
   g.ep.bias = bias;
   g.ep.resid = nullptr;
   g.ep.ldr = 0;
+  g.ep.resid_bf16 = 0;
   g.ep.a_scale = sa;
   g.ep.w_scale = scales;
+  g.ep.ln_w = nullptr;
+  g.ep.ln_b = nullptr;
+  g.ep.eps = 0.f;
+  g.ep.out_f32 = nullptr;
+  g.ep.rope_cos = nullptr;
+  g.ep.rope_sin = nullptr;
+  g.ep.rope_hd = 0;
+  g.ep.rope_cols = 0;
+  g.ep.cu = nullptr;
+  g.ep.nseq = 0;
   g.err = s->err;
   g.num_sms = s->num_sms;
   g.stream = st;

@@ -47,7 +47,11 @@ cudaError_t launch_gemm_inst(const GemmLaunch& g) {
 template <bool S8, int BN>
 cudaError_t launch_gemm_bn(const GemmLaunch& g) {
   using Bf = __nv_bfloat16;
-  if constexpr (!S8) {
+  if constexpr (BN == 384) {
+    // Full-row tiles exist for the fused residual + LayerNorm epilogue only.
+    if (!S8 && g.epi == kEpiResidLN && g.N == 384) return launch_gemm_inst<384, kEpiResidLN, false, Bf>(g);
+    return cudaErrorInvalidValue;
+  } else if constexpr (!S8) {
     switch (g.epi) {
       case kEpiStore:
         return g.out_f32 ? launch_gemm_inst<BN, kEpiStore, false, float>(g)
@@ -80,6 +84,7 @@ cudaError_t launch_gemm_any(const GemmLaunch& g) {
     case 128: return launch_gemm_bn<S8, 128>(g);
     case 192: return launch_gemm_bn<S8, 192>(g);
     case 256: return launch_gemm_bn<S8, 256>(g);
+    case 384: return launch_gemm_bn<S8, 384>(g);
   }
   return cudaErrorInvalidValue;
 }

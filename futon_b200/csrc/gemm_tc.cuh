@@ -9,6 +9,8 @@
 //   kEpiGelu    gelu(D + bias)                         (fc1, model.go:610-616)
 //   kEpiSwiglu  (D_fc1 + b1) * silu(D_gate + b2)       (fc1‖gate, model.go:617-627)
 //   kEpiResid   (D + bias) + residual                  (out / fc2 before LayerNorm)
+//   kEpiResidLN LayerNorm((D + bias) + residual)       (out / fc2 + norm1 / norm2,
+//               full-row tiles: BN = N = hidden ≤ 384, model.go:596-599, 628-633)
 // and, for the int8 path (native/quant.go:99-137), the exact rescale
 //   float32(sum_s32) * (scale_a[m] * scale_w[n]) + bias[n].
 //
@@ -31,16 +33,30 @@
 
 namespace futon {
 
-enum EpiKind : int { kEpiStore = 0, kEpiGelu = 1, kEpiSwiglu = 2, kEpiResid = 3 };
+enum EpiKind : int { kEpiStore = 0, kEpiGelu = 1, kEpiSwiglu = 2, kEpiResid = 3, kEpiResidLN = 4 };
 
 struct EpiParams {
   void* out;             // bf16 or f32 output, row stride ldo elements
   int ldo;
   const float* bias;     // [N] (interleaved like W for kEpiSwiglu) or null
-  const float* resid;    // kEpiResid: f32 [M, ldr]
+  const void* resid;     // kEpiResid / kEpiResidLN: [M, ldr], f32 or bf16 (resid_bf16)
   int ldr;
+  int resid_bf16;
   const float* a_scale;  // int8 path: per-row activation scales [M]
   const float* w_scale;  // int8 path: per-row weight scales [N]
+  const float* ln_w;     // kEpiResidLN: LayerNorm γ, β [N], eps
+  const float* ln_b;
+  float eps;
+  float* out_f32;        // kEpiResidLN: optional f32 copy of the normalised rows
+  // kEpiStore on the qkv projection of a RoPE pack: NeoX rotation of the q
+  // and k columns (< rope_cols) per head of rope_hd, at each row's position
+  // in its sequence (cu_seqlens[nseq+1]), before the store (model.go:674-685).
+  const float* rope_cos;  // [positions, rope_hd/2]
+  const float* rope_sin;
+  int rope_hd;
+  int rope_cols;
+  const int* cu;
+  int nseq;
 };
 
 template <int BN, bool S8>
@@ -51,10 +67,15 @@ struct GemmCfg {
   static constexpr int kABytes = kBM * kRowBytes;
   static constexpr int kBBytes = BN * kRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN == 256) ? 4 : (BN == 192) ? 5 : (BN == 128) ? 6 : 8;
-  static constexpr uint32_t kAccStride = (BN <= 64) ? 64 : (BN <= 128) ? 128 : 256;
-  static constexpr uint32_t kTmemCols = 2 * kAccStride;       // power of two, ≤ 512
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kStages = (BN == 384) ? 3 : (BN == 256) ? 4 : (BN == 192) ? 5 : (BN == 128) ? 6 : 8;
+  static constexpr int kMmaN = BN <= 256 ? BN : BN / 2;       // N of one tcgen05.mma (≤ 256)
+  static constexpr int kNSplit = BN / kMmaN;                  // MMAs per k-step
+  static constexpr int kNumAcc = BN <= 256 ? 2 : 1;           // TMEM accumulators
+  static constexpr uint32_t kAccStride = (BN <= 64) ? 64 : (BN <= 128) ? 128 : (BN <= 256) ? 256 : 512;
+  static constexpr uint32_t kTmemCols = kNumAcc * kAccStride; // power of two, ≤ 512
+  static constexpr int kRedBytes = 2 * 128 * 16;              // LayerNorm partial sums
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kRedBytes;
   static constexpr int kEpiWarps = 8;   // two per TMEM lane quarter
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
 };
@@ -88,6 +109,59 @@ template <> __device__ __forceinline__ void store1<__nv_bfloat16>(__nv_bfloat16*
   *dst = __float2bfloat16_rn(v);
 }
 
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// 32 consecutive residual values of one row (f32 or bf16).
+__device__ __forceinline__ void load_resid32(const EpiParams& ep, int row, int col, float (&r)[32]) {
+  if (ep.resid_bf16) {
+    const uint4* rp = reinterpret_cast<const uint4*>(
+        reinterpret_cast<const __nv_bfloat16*>(ep.resid) + (size_t)row * ep.ldr + col);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 q = rp[i];
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
+        const float2 f = __bfloat1622float2(b2);
+        r[8 * i + 2 * j] = f.x;
+        r[8 * i + 2 * j + 1] = f.y;
+      }
+    }
+  } else {
+    const float4* rp =
+        reinterpret_cast<const float4*>(reinterpret_cast<const float*>(ep.resid) + (size_t)row * ep.ldr + col);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 q = rp[i];
+      r[4 * i] = q.x; r[4 * i + 1] = q.y; r[4 * i + 2] = q.z; r[4 * i + 3] = q.w;
+    }
+  }
+}
+
+__device__ __forceinline__ float load_resid1(const EpiParams& ep, int row, int col) {
+  if (ep.resid_bf16)
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ep.resid)[(size_t)row * ep.ldr + col]);
+  return reinterpret_cast<const float*>(ep.resid)[(size_t)row * ep.ldr + col];
+}
+
 // Accumulator word → f32 value before the activation: f32 sum + bias, or the
 // int8 rescale float32(sum) * (sA * sW) + bias (quant.go:132-135).
 template <bool S8>
@@ -109,6 +183,92 @@ template <bool S8> __device__ __forceinline__ float act_gelu(float x) {
 }
 template <bool S8> __device__ __forceinline__ float act_silu(float g) {
   if constexpr (S8) return fmul(g, sigmoid_f32(g)); else return silu_fast(g);
+}
+
+// Position of packed row `row` within its sequence (cu non-decreasing).
+__device__ __forceinline__ int seq_position(const int* cu, int nseq, int row) {
+  int lo = 0, hi = nseq;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (cu[mid] <= row) lo = mid; else hi = mid;
+  }
+  return row - cu[lo];
+}
+
+// Rotates the 32 values of one chunk in place: heads of hd ≤ 32 lie inside
+// the chunk (pairs i, i + hd/2 of each head).
+__device__ __forceinline__ void rope_in_chunk(float (&v)[32], int hd, const float* cr,
+                                              const float* sr) {
+  const int half = hd >> 1;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int t = i & (hd - 1);
+    if (t < half) {
+      const float c = cr[t], sn = sr[t];
+      const float x1 = v[i], x2 = v[i + half < 32 ? i + half : i];
+      v[i] = x1 * c - x2 * sn;
+      v[i + half < 32 ? i + half : i] = x2 * c + x1 * sn;
+    }
+  }
+}
+
+// kEpiStore with RoPE on q/k columns: each thread owns whole heads of its
+// row (the two warps of a lane quarter take alternate heads).
+template <int BN, bool S8, typename OutT>
+__device__ __forceinline__ void epilogue_qkv_rope(uint32_t taddr, int row, int M, int N, int nb,
+                                                  int part, const EpiParams& ep) {
+  const bool row_ok = row < M;
+  const float a_s = (S8 && row_ok) ? ep.a_scale[row] : 0.0f;
+  OutT* out = reinterpret_cast<OutT*>(ep.out);
+  const int hd = ep.rope_hd, half = hd >> 1;
+  const int pos = row_ok ? seq_position(ep.cu, ep.nseq, row) : 0;
+  const float* cr = ep.rope_cos + (size_t)pos * half;
+  const float* sr = ep.rope_sin + (size_t)pos * half;
+  const int col0 = nb * BN;
+  const int span = hd < 32 ? 32 : hd;         // columns handled as one unit
+#pragma unroll 1
+  for (int c = part * span; c < BN; c += 2 * span) {
+    const int col = col0 + c;
+    const bool rot = col < ep.rope_cols;
+    if (span == 32) {
+      uint32_t u[32];
+      tmem_ld32(taddr + c, u);
+      tmem_ld_wait();
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = acc_value<S8>(u[i], a_s, ep, col + i < N ? col + i : N - 1);
+      if (rot) rope_in_chunk(v, hd, cr, sr);
+      if (row_ok) {
+        if (col + 32 <= N) store32<OutT>(out + (size_t)row * ep.ldo + col, v);
+        else
+          for (int i = 0; i < 32; ++i)
+            if (col + i < N) store1<OutT>(out + (size_t)row * ep.ldo + col + i, v[i]);
+      }
+    } else {  // hd == 64: the head's halves are two 32-column chunks
+      uint32_t u[32], w[32];
+      tmem_ld32(taddr + c, u);
+      tmem_ld32(taddr + c + 32, w);
+      tmem_ld_wait();
+      float a[32], b[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        a[i] = acc_value<S8>(u[i], a_s, ep, col + i);
+        b[i] = acc_value<S8>(w[i], a_s, ep, col + 32 + i);
+      }
+      if (rot) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x1 = a[i], x2 = b[i], cc = cr[i], sn = sr[i];
+          a[i] = x1 * cc - x2 * sn;
+          b[i] = x2 * cc + x1 * sn;
+        }
+      }
+      if (row_ok) {
+        store32<OutT>(out + (size_t)row * ep.ldo + col, a);
+        store32<OutT>(out + (size_t)row * ep.ldo + col + 32, b);
+      }
+    }
+  }
 }
 
 // One tile's epilogue for one thread (= one output row). The two warps that
@@ -163,14 +323,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int
       if (full || col + 32 <= N) {
         float r[32];
         if constexpr (EPI == kEpiResid) {
-          if (row_ok) {
-            const float4* rp = reinterpret_cast<const float4*>(ep.resid + (size_t)row * ep.ldr + col);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 q = rp[i];
-              r[4 * i] = q.x; r[4 * i + 1] = q.y; r[4 * i + 2] = q.z; r[4 * i + 3] = q.w;
-            }
-          }
+          if (row_ok) load_resid32(ep, row, col, r);
         }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -186,11 +339,71 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int
           if (col + i < N && row_ok) {
             float x = acc_value<S8>(u[i], a_s, ep, col + i);
             if constexpr (EPI == kEpiGelu) x = act_gelu<S8>(x);
-            if constexpr (EPI == kEpiResid) x = fadd(x, ep.resid[(size_t)row * ep.ldr + col + i]);
+            if constexpr (EPI == kEpiResid) x = fadd(x, load_resid1(ep, row, col + i));
             store1<OutT>(out + (size_t)row * ep.ldo + col + i, x);
           }
         }
       }
+    }
+  }
+}
+
+// kEpiResidLN for one thread (= one row) and one column half (part): v =
+// (D + bias) + residual is written back over the accumulator, the row's
+// f64 Σv and Σv² are combined with the other half's through shared memory,
+// then y = (v − mean)·inv·γ + β goes out as bf16 (and f32 when asked), with
+// inv = float32(1/sqrt(var + eps)) as in layerNormRows (model.go:743-769).
+// Tiles span the whole row (N = BN), so the output may overwrite the
+// residual in place: each thread reads its residual before writing its row.
+template <int BN>
+__device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int M, int part,
+                                                  int quarter, int lane, const EpiParams& ep,
+                                                  double2* red) {
+  constexpr int kCols = BN / 2;
+  const bool row_ok = row < M;
+  const int c0 = part * kCols;
+  double s1 = 0.0, s2 = 0.0;
+#pragma unroll 1
+  for (int c = c0; c < c0 + kCols; c += 32) {
+    uint32_t u[32];
+    tmem_ld32(taddr + c, u);
+    float r[32];
+    if (row_ok) load_resid32(ep, row, c, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float v = __uint_as_float(u[i]);
+      if (ep.bias) v = fadd(v, ep.bias[c + i]);
+      v = fadd(v, row_ok ? r[i] : 0.0f);
+      u[i] = __float_as_uint(v);
+      s1 += (double)v;
+      s2 += (double)v * (double)v;
+    }
+    tmem_st32(taddr + c, u);
+  }
+  tmem_st_wait();
+  const int slot = quarter * 32 + lane;
+  red[part * 128 + slot] = make_double2(s1, s2);
+  named_bar_sync(1 + quarter, 64);
+  const double2 o = red[(1 - part) * 128 + slot];
+  const double mean = (s1 + o.x) / (double)BN;
+  double var = (s2 + o.y) / (double)BN - mean * mean;
+  var = var > 0.0 ? var : 0.0;
+  const float inv = (float)(1.0 / sqrt(var + (double)ep.eps));
+  const float mf = (float)mean;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out);
+#pragma unroll 1
+  for (int c = c0; c < c0 + kCols; c += 32) {
+    uint32_t u[32];
+    tmem_ld32(taddr + c, u);
+    tmem_ld_wait();
+    float y[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      y[i] = fadd(fmul(fmul(fsub(__uint_as_float(u[i]), mf), inv), ep.ln_w[c + i]), ep.ln_b[c + i]);
+    if (row_ok) {
+      store32<__nv_bfloat16>(out + (size_t)row * ep.ldo + c, y);
+      if (ep.out_f32) store32<float>(ep.out_f32 + (size_t)row * BN + c, y);
     }
   }
 }
@@ -206,10 +419,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
   uint64_t* full_bar = bars;                       // [kStages] TMA → MMA
   uint64_t* empty_bar = bars + C::kStages;         // [kStages] MMA → TMA
-  uint64_t* accf_bar = bars + 2 * C::kStages;      // [2] MMA → epilogue
-  uint64_t* acce_bar = accf_bar + 2;               // [2] epilogue → MMA
+  uint64_t* accf_bar = bars + 2 * C::kStages;      // [kNumAcc] MMA → epilogue
+  uint64_t* acce_bar = accf_bar + 2;               // [kNumAcc] epilogue → MMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  double2* red = reinterpret_cast<double2*>(smem + C::kStages * C::kStageBytes + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -260,7 +474,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
           const uint32_t fb = smem_u32(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, C::kStageBytes);
           tma_load_2d(smem_u32(sa), &tmA, fb, kb * C::kBK, mb * C::kBM);
-          tma_load_2d(smem_u32(sb), &tmW, fb, kb * C::kBK, nb * BN);
+#pragma unroll
+          for (int j = 0; j < C::kNSplit; ++j)
+            tma_load_2d(smem_u32(sb + j * C::kMmaN * C::kRowBytes), &tmW, fb, kb * C::kBK,
+                        nb * BN + j * C::kMmaN);
           ++issued;
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
         }
@@ -283,13 +500,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = make_idesc(S8 ? 2u : 1u, 1u, 128u, (uint32_t)BN);
+      constexpr uint32_t idesc = make_idesc(S8 ? 2u : 1u, 1u, 128u, (uint32_t)C::kMmaN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
-        const int acc = it & 1;
-        const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+        const int acc = it % C::kNumAcc;
+        const uint32_t acc_phase = (uint32_t)(it / C::kNumAcc) & 1u;
         if (!mbar_wait_bounded(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, err, kDevTimeoutAccEmpty,
                                abort_flag))
           break;
@@ -305,15 +522,20 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
           tc_fence_after();
           const uint8_t* sa = smem + stage * C::kStageBytes;
           const uint64_t adesc = smem_desc_k_sw128(smem_u32(sa));
-          const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sa + C::kABytes));
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            // +32 bytes along K inside the 128-byte swizzle row (encoded >> 4).
-            const uint64_t koff = (uint64_t)(ks * 2);
-            if constexpr (S8)
-              mma_s8(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
-            else
-              mma_bf16(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
+          for (int j = 0; j < C::kNSplit; ++j) {
+            const uint64_t bdesc =
+                smem_desc_k_sw128(smem_u32(sa + C::kABytes + j * C::kMmaN * C::kRowBytes));
+            const uint32_t dj = d_tmem + (uint32_t)(j * C::kMmaN);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              // +32 bytes along K inside the 128-byte swizzle row (encoded >> 4).
+              const uint64_t koff = (uint64_t)(ks * 2);
+              if constexpr (S8)
+                mma_s8(dj, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
+              else
+                mma_bf16(dj, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
+            }
           }
           mma_commit(smem_u32(&empty_bar[stage]));
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
@@ -323,8 +545,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
       }
       // Drain: wait (bounded) for the last committed MMAs before TMEM is freed.
       if (it > 0) {
-        const int acc = (it - 1) & 1;
-        const uint32_t acc_phase = (uint32_t)((it - 1) >> 1) & 1u;
+        const int acc = (it - 1) % C::kNumAcc;
+        const uint32_t acc_phase = (uint32_t)((it - 1) / C::kNumAcc) & 1u;
         uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(smem_u32(&accf_bar[acc]), acc_phase)) {
           if (globaltimer_ns() - t0 > kWaitLimitNs) break;
@@ -337,8 +559,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     const int part = (warp - 2) >> 2;    // which half of the column chunks
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
-      const int acc = it & 1;
-      const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+      const int acc = it % C::kNumAcc;
+      const uint32_t acc_phase = (uint32_t)(it / C::kNumAcc) & 1u;
       if (!mbar_wait_bounded(smem_u32(&accf_bar[acc]), acc_phase, err, kDevTimeoutAccFull,
                              abort_flag))
         break;
@@ -346,7 +568,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
       const int mb = tile / num_n, nb = tile % num_n;
       const int row = mb * C::kBM + quarter * 32 + lane;
       const uint32_t taddr = tmem_base + acc * C::kAccStride + ((uint32_t)(quarter * 32) << 16);
-      epilogue_row<BN, EPI, S8, OutT>(taddr, row, M, N, nb, part, ep);
+      if constexpr (EPI == kEpiResidLN) {
+        epilogue_resid_ln<BN>(taddr, row, M, part, quarter, lane, ep, red);
+      } else if constexpr (EPI == kEpiStore && BN <= 256) {
+        if (ep.rope_cos)
+          epilogue_qkv_rope<BN, S8, OutT>(taddr, row, M, N, nb, part, ep);
+        else
+          epilogue_row<BN, EPI, S8, OutT>(taddr, row, M, N, nb, part, ep);
+      } else {
+        epilogue_row<BN, EPI, S8, OutT>(taddr, row, M, N, nb, part, ep);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));

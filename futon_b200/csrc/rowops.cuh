@@ -102,11 +102,13 @@ __device__ __forceinline__ void warp_layernorm_store(float4 (&v)[kMaxRowVec], in
       y.z = fadd(fmul(fmul(fsub(v[j].z, mf), inv), g.z), be.z);
       y.w = fadd(fmul(fmul(fsub(v[j].w, mf), inv), g.w), be.w);
       v[j] = y;
-      reinterpret_cast<float4*>(xo)[c4] = y;
-      __nv_bfloat162 p0 = __floats2bfloat162_rn(y.x, y.y);
-      __nv_bfloat162 p1 = __floats2bfloat162_rn(y.z, y.w);
-      uint2 pk = make_uint2(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1));
-      reinterpret_cast<uint2*>(xbo)[c4] = pk;
+      if (xo) reinterpret_cast<float4*>(xo)[c4] = y;
+      if (xbo) {
+        __nv_bfloat162 p0 = __floats2bfloat162_rn(y.x, y.y);
+        __nv_bfloat162 p1 = __floats2bfloat162_rn(y.z, y.w);
+        uint2 pk = make_uint2(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1));
+        reinterpret_cast<uint2*>(xbo)[c4] = pk;
+      }
     }
   }
   if (xq) warp_quant_row(v, n4, lane, xq, xs);
@@ -160,8 +162,9 @@ __global__ void __launch_bounds__(256)
         v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
-    warp_layernorm_store(v, h, lane, w, b, eps, x + (size_t)t * h, xb + (size_t)t * h,
-                         xq ? xq + (size_t)t * h : nullptr, xq ? xs + t : nullptr);
+    warp_layernorm_store(v, h, lane, w, b, eps, x ? x + (size_t)t * h : nullptr,
+                         xb ? xb + (size_t)t * h : nullptr, xq ? xq + (size_t)t * h : nullptr,
+                         xq ? xs + t : nullptr);
   }
 }
 
@@ -181,8 +184,9 @@ __global__ void __launch_bounds__(256)
       const int c4 = lane + 32 * j;
       v[j] = c4 < n4 ? src[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    warp_layernorm_store(v, h, lane, w, b, eps, x + (size_t)r * h, xb + (size_t)r * h,
-                         xq ? xq + (size_t)r * h : nullptr, xq ? xs + r : nullptr);
+    warp_layernorm_store(v, h, lane, w, b, eps, x ? x + (size_t)r * h : nullptr,
+                         xb ? xb + (size_t)r * h : nullptr, xq ? xq + (size_t)r * h : nullptr,
+                         xq ? xs + r : nullptr);
   }
 }
 
@@ -221,23 +225,18 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Copies the CLS row (first token) of every sequence into a compact buffer.
-__global__ void gather_rows_kernel(const float* __restrict__ x, const int* __restrict__ cu,
-                                   int nseq, int h, float* __restrict__ xc,
-                                   __nv_bfloat16* __restrict__ xcb) {
-  const int n4 = h >> 2;
-  const size_t total = (size_t)nseq * n4;
+// Copies the CLS row (first token) of every sequence into a compact buffer
+// (f32 or bf16 rows; 16-byte vectors).
+template <typename T>
+__global__ void gather_rows_kernel(const T* __restrict__ x, const int* __restrict__ cu, int nseq,
+                                   int h, T* __restrict__ xc) {
+  const int nv = h * (int)sizeof(T) / 16;
+  const size_t total = (size_t)nseq * nv;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
        i += (size_t)gridDim.x * blockDim.x) {
-    const int s = (int)(i / n4), c4 = (int)(i % n4);
-    float4 v = reinterpret_cast<const float4*>(x + (size_t)cu[s] * h)[c4];
-    reinterpret_cast<float4*>(xc + (size_t)s * h)[c4] = v;
-    if (xcb) {
-      __nv_bfloat162 p0 = __floats2bfloat162_rn(v.x, v.y);
-      __nv_bfloat162 p1 = __floats2bfloat162_rn(v.z, v.w);
-      reinterpret_cast<uint2*>(xcb + (size_t)s * h)[c4] =
-          make_uint2(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1));
-    }
+    const int s = (int)(i / nv), c = (int)(i % nv);
+    reinterpret_cast<uint4*>(xc + (size_t)s * h)[c] =
+        reinterpret_cast<const uint4*>(x + (size_t)cu[s] * h)[c];
   }
 }
 
