@@ -275,7 +275,16 @@ __device__ __forceinline__ void stage_async(__nv_bfloat16* dst, const __nv_bfloa
 template <int HD>
 constexpr int attn_heads_smem_bytes() { return 6 * 64 * (HD + 8) * 2; }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // grid = ntiles (or nseq in cls_mode), block = 128 (4 warps × 16 query rows).
+// Work is skipped where a sequence ends: warps whose 16 query rows all lie
+// past the sequence idle, and only the 8-key blocks that hold keys are
+// multiplied (most benchmark sequences are shorter than one 64 × 64 tile).
 template <int HD, typename OutT>
 __global__ void __launch_bounds__(128, 4)
     attn_heads_kernel(const __nv_bfloat16* __restrict__ qkv, int hidden, int num_heads,
@@ -294,118 +303,150 @@ __global__ void __launch_bounds__(128, 4)
   const int ld = 3 * hidden;
   const __nv_bfloat16* base = qkv + (size_t)s0 * ld;
   const int nkv = (L + 63) / 64;
-  const int nsteps = num_heads * nkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool warp_active = tile.q0 + warp * 16 < qlim;
 
-  auto issue = [&](int step) {
-    const int hh = step / nkv, j = step - hh * nkv, slot = step & 1;
-    if (j == 0) stage_async<HD>(sQ + (hh & 1) * kTile, base + hh * HD, ld, tile.q0, qlim);
-    stage_async<HD>(sK + slot * kTile, base + hidden + hh * HD, ld, j * 64, L);
-    stage_async<HD>(sV + slot * kTile, base + 2 * hidden + hh * HD, ld, j * 64, L);
+  // Next (head, key tile) to stage; one commit group per step (possibly empty).
+  int nh = 0, nj = 0, issued = 0;
+  auto issue_next = [&]() {
+    if (nh < num_heads) {
+      const int slot = issued & 1;
+      if (nj == 0) stage_async<HD>(sQ + (nh & 1) * kTile, base + nh * HD, ld, tile.q0, qlim);
+      stage_async<HD>(sK + slot * kTile, base + hidden + nh * HD, ld, nj * 64, L);
+      stage_async<HD>(sV + slot * kTile, base + 2 * hidden + nh * HD, ld, nj * 64, L);
+      if (++nj == nkv) { nj = 0; ++nh; }
+      ++issued;
+    }
     cp_async_commit();
   };
+
+  // Per-thread ldmatrix offsets (elements).
+  const int q_off = (warp * 16 + (lane & 15)) * kLds + (lane >> 4) * 8;
+  const int k_off = (lane & 7) * kLds + ((lane >> 3) & 1) * 8;
+  const int v_off = (lane & 15) * kLds;
 
   uint32_t qf[HD / 16][4];
   float o[HD / 8][4];
   float m_run[2], l_run[2];
-  issue(0);
-  for (int step = 0; step < nsteps; ++step) {
-    if (step + 1 < nsteps) issue(step + 1);
-    else cp_async_commit();  // empty group keeps wait_group(1) uniform
-    cp_async_wait1();
-    __syncthreads();
-    const int head = step / nkv, j = step - head * nkv, slot = step & 1;
-    const __nv_bfloat16* kS = sK + slot * kTile;
-    const __nv_bfloat16* vS = sV + slot * kTile;
-    if (j == 0) {
-      const __nv_bfloat16* qS = sQ + (head & 1) * kTile;
+  issue_next();
+  int step = 0;
+  for (int head = 0; head < num_heads; ++head) {
+    for (int j = 0; j < nkv; ++j, ++step) {
+      issue_next();
+      cp_async_wait1();
+      __syncthreads();
+      const __nv_bfloat16* kS = sK + (step & 1) * kTile;
+      const __nv_bfloat16* vS = sV + (step & 1) * kTile;
+      if (warp_active) {
+        if (j == 0) {
+          const __nv_bfloat16* qS = sQ + (head & 1) * kTile;
 #pragma unroll
-      for (int kc = 0; kc < HD / 16; ++kc)
-        ldsm_x4(qf[kc], smem_u32(&qS[(warp * 16 + (lane & 15)) * kLds + kc * 16 + (lane >> 4) * 8]));
+          for (int kc = 0; kc < HD / 16; ++kc) ldsm_x4(qf[kc], smem_u32(&qS[q_off + kc * 16]));
 #pragma unroll
-      for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-      m_run[0] = m_run[1] = -INFINITY;
-      l_run[0] = l_run[1] = 0.f;
-    }
-    const int kv0 = j * 64;
-    float sc[8][4];
+          for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+          m_run[0] = m_run[1] = -INFINITY;
+          l_run[0] = l_run[1] = 0.f;
+        }
+        const int kv0 = j * 64;
+        const int nkeys = min(64, L - kv0);
+        const int nblk = (nkeys + 7) >> 3;  // 8-key blocks holding keys (warp-uniform)
+        float sc[8][4];
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+        for (int nb = 0; nb < 8; ++nb) {
+          sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+          if (nb < nblk) {
 #pragma unroll
-      for (int kc = 0; kc < HD / 16; ++kc) {
-        uint32_t kf[2];
-        ldsm_x2(kf, smem_u32(&kS[(nb * 8 + (lane & 7)) * kLds + kc * 16 + ((lane >> 3) & 1) * 8]));
-        mma_16816(sc[nb], qf[kc], kf);
+            for (int kc = 0; kc < HD / 16; ++kc) {
+              uint32_t kf[2];
+              ldsm_x2(kf, smem_u32(&kS[nb * 8 * kLds + k_off + kc * 16]));
+              mma_16816(sc[nb], qf[kc], kf);
+            }
+          }
+        }
+        // Mask keys past the end of a partial tile.
+        if (nkeys < 64) {
+#pragma unroll
+          for (int b = 0; b < 8; ++b)
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (b * 8 + (lane & 3) * 2 + (e & 1) >= nkeys) sc[b][e] = -INFINITY;
+        }
+        // Online softmax in raw score units; the scale folds into the exponent.
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int nb = 0; nb < 8; ++nb)
+          if (nb < nblk) {
+            mx[0] = fmaxf(mx[0], fmaxf(sc[nb][0], sc[nb][1]));
+            mx[1] = fmaxf(mx[1], fmaxf(sc[nb][2], sc[nb][3]));
+          }
+        float alpha[2], mscaled[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+          mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+          const float m_new = fmaxf(m_run[r], mx[r]);
+          alpha[r] = (m_run[r] == -INFINITY) ? 0.f : ex2_approx((m_run[r] - m_new) * scale_log2);
+          m_run[r] = m_new;
+          mscaled[r] = m_new * scale_log2;
+          l_run[r] *= alpha[r];
+        }
+#pragma unroll
+        for (int nb = 0; nb < 8; ++nb) {
+          if (nb < nblk) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float p = ex2_approx(fmaf(sc[nb][e], scale_log2, -mscaled[e >> 1]));
+              sc[nb][e] = p;
+              l_run[e >> 1] += p;
+            }
+          } else {
+            sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int nd = 0; nd < HD / 8; ++nd) {
+          o[nd][0] *= alpha[0]; o[nd][1] *= alpha[0];
+          o[nd][2] *= alpha[1]; o[nd][3] *= alpha[1];
+        }
+        const int nkc = (nblk + 1) >> 1;  // 16-key chunks for P·V
+#pragma unroll
+        for (int kc = 0; kc < 4; ++kc) {
+          if (kc < nkc) {
+            uint32_t pf[4];
+            pf[0] = pack_bf16(sc[2 * kc][0], sc[2 * kc][1]);
+            pf[1] = pack_bf16(sc[2 * kc][2], sc[2 * kc][3]);
+            pf[2] = pack_bf16(sc[2 * kc + 1][0], sc[2 * kc + 1][1]);
+            pf[3] = pack_bf16(sc[2 * kc + 1][2], sc[2 * kc + 1][3]);
+#pragma unroll
+            for (int nd = 0; nd < HD / 8; ++nd) {
+              uint32_t vf[2];
+              ldsm_x2_t(vf, smem_u32(&vS[kc * 16 * kLds + v_off + nd * 8]));
+              mma_16816(o[nd], pf, vf);
+            }
+          }
+        }
+        if (j == nkv - 1) {
+          float lsum[2];
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            lsum[r] = l_run[r];
+            lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 1);
+            lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 2);
+          }
+          const float inv0 = 1.f / lsum[0], inv1 = 1.f / lsum[1];
+          const int qr0 = tile.q0 + warp * 16 + (lane >> 2), qr1 = qr0 + 8;
+          const size_t orow0 = cls_mode ? (size_t)tile.seq : (size_t)(s0 + qr0);
+          const size_t orow1 = (size_t)(s0 + qr1);
+#pragma unroll
+          for (int nd = 0; nd < HD / 8; ++nd) {
+            const int col = head * HD + nd * 8 + (lane & 3) * 2;
+            if (qr0 < qlim) store2<OutT>(out + orow0 * ldo + col, o[nd][0] * inv0, o[nd][1] * inv0);
+            if (qr1 < qlim) store2<OutT>(out + orow1 * ldo + col, o[nd][2] * inv1, o[nd][3] * inv1);
+          }
+        }
       }
+      __syncthreads();  // every warp is done with this slot before it is refilled
     }
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = kv0 + nb * 8 + (lane & 3) * 2 + (e & 1);
-        const float v = (key < L) ? sc[nb][e] * scale_log2 : -INFINITY;
-        sc[nb][e] = v;
-        mx[e >> 1] = fmaxf(mx[e >> 1], v);
-      }
-    float alpha[2];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-      const float m_new = fmaxf(m_run[r], mx[r]);
-      alpha[r] = (m_run[r] == -INFINITY) ? 0.f : exp2f(m_run[r] - m_new);
-      m_run[r] = m_new;
-      l_run[r] *= alpha[r];
-    }
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float p = exp2f(sc[nb][e] - m_run[e >> 1]);
-        sc[nb][e] = p;
-        l_run[e >> 1] += p;
-      }
-#pragma unroll
-    for (int nd = 0; nd < HD / 8; ++nd) {
-      o[nd][0] *= alpha[0]; o[nd][1] *= alpha[0];
-      o[nd][2] *= alpha[1]; o[nd][3] *= alpha[1];
-    }
-#pragma unroll
-    for (int kc = 0; kc < 4; ++kc) {
-      uint32_t pf[4];
-      pf[0] = pack_bf16(sc[2 * kc][0], sc[2 * kc][1]);
-      pf[1] = pack_bf16(sc[2 * kc][2], sc[2 * kc][3]);
-      pf[2] = pack_bf16(sc[2 * kc + 1][0], sc[2 * kc + 1][1]);
-      pf[3] = pack_bf16(sc[2 * kc + 1][2], sc[2 * kc + 1][3]);
-#pragma unroll
-      for (int nd = 0; nd < HD / 8; ++nd) {
-        uint32_t vf[2];
-        ldsm_x2_t(vf, smem_u32(&vS[(kc * 16 + (lane & 15)) * kLds + nd * 8]));
-        mma_16816(o[nd], pf, vf);
-      }
-    }
-    if (j == nkv - 1) {
-      float lsum[2];
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        lsum[r] = l_run[r];
-        lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 1);
-        lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 2);
-      }
-      const float inv0 = 1.f / lsum[0], inv1 = 1.f / lsum[1];
-      const int qr0 = tile.q0 + warp * 16 + (lane >> 2), qr1 = qr0 + 8;
-      const size_t orow0 = cls_mode ? (size_t)tile.seq : (size_t)(s0 + qr0);
-      const size_t orow1 = (size_t)(s0 + qr1);
-#pragma unroll
-      for (int nd = 0; nd < HD / 8; ++nd) {
-        const int col = head * HD + nd * 8 + (lane & 3) * 2;
-        if (qr0 < qlim) store2<OutT>(out + orow0 * ldo + col, o[nd][0] * inv0, o[nd][1] * inv0);
-        if (qr1 < qlim) store2<OutT>(out + orow1 * ldo + col, o[nd][2] * inv1, o[nd][3] * inv1);
-      }
-    }
-    __syncthreads();  // every warp is done with this slot before it is refilled
   }
 }
 
