@@ -97,6 +97,21 @@ bool make_operand_map(CUtensorMap* map, const void* base, bool s8, uint64_t rows
   return r == CUDA_SUCCESS;
 }
 
+// bf16 [rows, cols] GEMM output (row stride ld) written by TMA tile stores:
+// 32 × 32 boxes with the 64-byte swizzle the epilogue staging uses.
+bool make_output_map(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // N tile for a GEMM with N output columns: the widest of 256/192/128 that
 // divides N, else 64 (partial last tile, masked in the epilogue).
 int pick_bn(int n) {
@@ -508,12 +523,20 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   const double bytes = (double)M * w.k * esz + (double)w.n * w.k * esz + (double)M * out_cols * osz +
                        (double)M * w.n * rsz + (o.out_f32_copy ? (double)M * w.n * 4.0 : 0.0);
   ProfScope prof(d, st, stage, 2.0 * M * w.n * w.k, bytes);
-  CUtensorMap ta;
+  CUtensorMap ta, to;
   if (!make_operand_map(&ta, A, s8, (uint64_t)M, (uint64_t)w.k, 128))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (activation)");
+  // bf16 outputs of every epilogue but the fused LayerNorm leave through TMA.
+  const bool bf16_out = !(o.out_f32 || (s8 && o.epi != kEpiStore)) && o.epi != kEpiResidLN;
+  if (bf16_out) {
+    const uint64_t ncols = o.epi == kEpiSwiglu ? (uint64_t)w.n / 2 : (uint64_t)w.n;
+    if (!make_output_map(&to, o.out, (uint64_t)M, ncols, (uint64_t)o.ldo))
+      return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (output)");
+  }
   GemmLaunch g;
   g.ta = &ta;
   g.tw = &w.map;
+  g.to = bf16_out ? &to : nullptr;
   g.M = M;
   g.N = w.n;
   g.K = w.k;
@@ -998,6 +1021,7 @@ int seam_gemm(SeamCtx& s, const void* A, bool s8, const float* a_scale, int m, c
   GemmLaunch g;
   g.ta = &ta;
   g.tw = &tw;
+  g.to = nullptr;
   g.M = m;
   g.N = n;
   g.K = k;
@@ -1493,6 +1517,7 @@ extern "C" int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const
   GemmLaunch g;
   g.ta = &ta;
   g.tw = &tw;
+  g.to = nullptr;
   g.M = m;
   g.N = n;
   g.K = k;

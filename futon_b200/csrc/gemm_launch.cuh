@@ -10,6 +10,7 @@ namespace futon {
 struct GemmLaunch {
   const CUtensorMap* ta;  // A [M, K] (bf16 or s8), box 128 × 128 bytes
   const CUtensorMap* tw;  // W [N, K], box bn × 128 bytes
+  const CUtensorMap* to;  // bf16 output [M, ncols], box 32 × 32, 64B swizzle (TMA-store epilogues)
   int M, N, K;
   int bn;                 // 64, 128, 192 or 256
   int epi;                // EpiKind
@@ -37,10 +38,13 @@ cudaError_t launch_gemm_inst(const GemmLaunch& g) {
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(1ull << (dev & 63));
   }
+  constexpr bool kTmaStore = sizeof(OutT) == 2 && EPI != kEpiResidLN;
+  if (kTmaStore && !g.to) return cudaErrorInvalidValue;  // bf16 outputs need an output map
   const long tiles = (long)((g.M + C::kBM - 1) / C::kBM) * ((g.N + BN - 1) / BN);
   if (tiles == 0) return cudaSuccess;
   const int grid = (int)(tiles < g.num_sms ? tiles : g.num_sms);
-  kern<<<grid, C::kThreads, C::kSmemBytes, g.stream>>>(*g.ta, *g.tw, g.M, g.N, g.K, g.ep, g.err);
+  kern<<<grid, C::kThreads, C::kSmemBytes, g.stream>>>(*g.ta, *g.tw, g.to ? *g.to : *g.ta, g.M,
+                                                       g.N, g.K, g.ep, g.err);
   return cudaGetLastError();
 }
 

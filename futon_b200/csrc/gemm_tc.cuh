@@ -5,7 +5,7 @@
 // with A row-major [M, K] (activations) and W row-major [N, K] (nn.Linear
 // layout, exactly how pack weights are stored), then applies one of the
 // layer epilogues of native/model.go:550-635 before the single store:
-//   kEpiStore   D + bias                               (qkv projection)
+//   kEpiStore   D + bias, optionally RoPE on q/k     (qkv projection)
 //   kEpiGelu    gelu(D + bias)                         (fc1, model.go:610-616)
 //   kEpiSwiglu  (D_fc1 + b1) * silu(D_gate + b2)       (fc1‖gate, model.go:617-627)
 //   kEpiResid   (D + bias) + residual                  (out / fc2 before LayerNorm)
@@ -18,11 +18,14 @@
 //   warp 0     TMA producer: 128-byte-swizzled K-major tiles of A (128 rows)
 //              and W (BN rows) into a STAGES-deep shared-memory ring.
 //   warp 1     allocates tensor memory; lane 0 issues tcgen05.mma
-//              (M=128, N=BN, K=16 bf16 / 32 s8 per instruction) into one of
+//              (M=128, N≤256, K=16 bf16 / 32 s8 per instruction) into one of
 //              two TMEM accumulators and commits completion to mbarriers.
 //   warps 2-9  epilogue: tcgen05.ld of the accumulator lane quarter the warp
 //              may access (one output row per thread; the two warps of a
-//              quarter split the 32-column chunks), fused math, global store.
+//              quarter split the 32-column chunks), fused math, then either
+//              a TMA tile store through a per-warp 64B-swizzled staging ring
+//              (bf16 outputs: full-sector writes, no per-thread stores) or
+//              direct vector stores (f32 outputs).
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile
 // i+1. Tiles are visited n-fastest so CTAs running together share A tiles
 // through L2; the weights (≤ 19 MB) stay L2-resident.
@@ -67,17 +70,20 @@ struct GemmCfg {
   static constexpr int kABytes = kBM * kRowBytes;
   static constexpr int kBBytes = BN * kRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN == 384) ? 3 : (BN == 256) ? 4 : (BN == 192) ? 5 : (BN == 128) ? 6 : 8;
+  static constexpr int kStages = (BN == 384) ? 3 : (BN >= 192) ? 4 : (BN == 128) ? 5 : 7;
   static constexpr int kMmaN = BN <= 256 ? BN : BN / 2;       // N of one tcgen05.mma (≤ 256)
   static constexpr int kNSplit = BN / kMmaN;                  // MMAs per k-step
   static constexpr int kNumAcc = BN <= 256 ? 2 : 1;           // TMEM accumulators
   static constexpr uint32_t kAccStride = (BN <= 64) ? 64 : (BN <= 128) ? 128 : (BN <= 256) ? 256 : 512;
   static constexpr uint32_t kTmemCols = kNumAcc * kAccStride; // power of two, ≤ 512
-  static constexpr int kRedBytes = 2 * 128 * 16;              // LayerNorm partial sums
-  static constexpr int kSmemBytes =
-      kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kRedBytes;
-  static constexpr int kEpiWarps = 8;   // two per TMEM lane quarter
+  static constexpr int kEpiWarps = 8;                         // two per TMEM lane quarter
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  // After the stage ring: barriers (256 B), then either the LayerNorm
+  // partial sums (2 × 128 double2) or the TMA-store staging (per epilogue
+  // warp two 32 × 64-byte buffers).
+  static constexpr int kStagingBytes = kEpiWarps * 2 * 2048;
+  static constexpr int kExtraOffset = kStages * kStageBytes + 1024;  // 1024-aligned
+  static constexpr int kSmemBytes = kExtraOffset + kStagingBytes + 1024 /*align*/;
 };
 
 template <typename T> __device__ __forceinline__ void store32(T* dst, const float (&v)[32]);
@@ -88,19 +94,21 @@ template <> __device__ __forceinline__ void store32<float>(float* dst, const flo
   for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
+__device__ __forceinline__ uint4 pack8_bf16(const float* v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+    w[j] = *reinterpret_cast<uint32_t*>(&p);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <> __device__ __forceinline__ void store32<__nv_bfloat16>(__nv_bfloat16* dst,
                                                                    const float (&v)[32]) {
   uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t w[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      __nv_bfloat162 p = __floats2bfloat162_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
-      w[j] = *reinterpret_cast<uint32_t*>(&p);
-    }
-    d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
-  }
+  for (int i = 0; i < 4; ++i) d4[i] = pack8_bf16(v + 8 * i);
 }
 
 template <typename T> __device__ __forceinline__ void store1(T* dst, float v);
@@ -127,6 +135,82 @@ __device__ __forceinline__ void tmem_st_wait() {
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+
+// ---- TMA tile store (shared → global), bulk-group completion ----------------
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Destination of one epilogue warp's 32 × 32 output chunks.
+// TmaSink (bf16 outputs): each lane writes its row's 64 bytes into a
+// 64B-swizzled staging buffer (16-byte chunk c of row r at c ^ ((r >> 1) & 3),
+// CU_TENSOR_MAP_SWIZZLE_64B), then lane 0 stores the 32-row box with TMA;
+// two buffers per warp alternate so the next chunk overlaps the store. The
+// tensor map clips rows ≥ M and columns ≥ N.
+struct TmaSink {
+  uint8_t* buf;              // 2 × 2048 bytes, 1024-aligned
+  const CUtensorMap* map;
+  int lane;
+  int count;
+  __device__ __forceinline__ void put(const float (&v)[32], int col, int row0) {
+    uint8_t* b = buf + (count & 1) * 2048;
+    if (lane == 0 && count >= 2) bulk_wait_read1();
+    __syncwarp();
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(b + lane * 64 + ((c ^ sw) << 4)) = pack8_bf16(v + 8 * c);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map, smem_u32(b), col, row0);
+      bulk_commit();
+    }
+    ++count;
+  }
+  __device__ __forceinline__ void drain() {
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+};
+
+// DirectSink (f32 outputs): per-thread vector stores with bounds checks.
+template <typename OutT>
+struct DirectSink {
+  OutT* out;
+  int ldo;
+  int row;
+  bool row_ok;
+  int ncols;
+  __device__ __forceinline__ void put(const float (&v)[32], int col, int /*row0*/) {
+    if (!row_ok) return;
+    OutT* dst = out + (size_t)row * ldo + col;
+    if (col + 32 <= ncols) {
+      store32<OutT>(dst, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < ncols) store1<OutT>(dst + i, v[i]);
+    }
+  }
+  __device__ __forceinline__ void drain() {}
+};
 
 // 32 consecutive residual values of one row (f32 or bf16).
 __device__ __forceinline__ void load_resid32(const EpiParams& ep, int row, int col, float (&r)[32]) {
@@ -156,24 +240,47 @@ __device__ __forceinline__ void load_resid32(const EpiParams& ep, int row, int c
   }
 }
 
-__device__ __forceinline__ float load_resid1(const EpiParams& ep, int row, int col) {
-  if (ep.resid_bf16)
-    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ep.resid)[(size_t)row * ep.ldr + col]);
-  return reinterpret_cast<const float*>(ep.resid)[(size_t)row * ep.ldr + col];
+// 32 consecutive entries of a per-column f32 vector (bias, scales), zero past
+// `limit` (16-byte vector loads on full chunks).
+__device__ __forceinline__ void load_col32(const float* p, int col, int limit, float (&r)[32]) {
+  if (!p) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = 0.0f;
+    return;
+  }
+  if (col + 32 <= limit) {
+    const float4* p4 = reinterpret_cast<const float4*>(p + col);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 q = p4[i];
+      r[4 * i] = q.x; r[4 * i + 1] = q.y; r[4 * i + 2] = q.z; r[4 * i + 3] = q.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = col + i < limit ? p[col + i] : 0.0f;
+  }
 }
 
-// Accumulator word → f32 value before the activation: f32 sum + bias, or the
-// int8 rescale float32(sum) * (sA * sW) + bias (quant.go:132-135).
+// Accumulator chunk → f32 values before the activation: f32 sum + bias, or
+// the int8 rescale float32(sum) * (sA * sW) + bias (quant.go:132-135).
 template <bool S8>
-__device__ __forceinline__ float acc_value(uint32_t u, float a_s, const EpiParams& ep, int col) {
-  float v;
+__device__ __forceinline__ void acc_values(const uint32_t (&u)[32], float a_s, const EpiParams& ep,
+                                           int col, int N, float (&v)[32]) {
+  float b[32];
+  load_col32(ep.bias, col, N, b);
   if constexpr (S8) {
-    v = fmul((float)(int32_t)u, fmul(a_s, ep.w_scale[col]));
+    float ws[32];
+    load_col32(ep.w_scale, col, N, ws);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = fmul((float)(int32_t)u[i], fmul(a_s, ws[i]));
   } else {
-    v = __uint_as_float(u);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]);
   }
-  if (ep.bias) v = fadd(v, ep.bias[col]);
-  return v;
+  if (ep.bias) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = fadd(v[i], b[i]);
+  }
 }
 
 // Activations: the reference's exact f32 evaluation on the int8 path (whose
@@ -195,155 +302,123 @@ __device__ __forceinline__ int seq_position(const int* cu, int nseq, int row) {
   return row - cu[lo];
 }
 
-// Rotates the 32 values of one chunk in place: heads of hd ≤ 32 lie inside
-// the chunk (pairs i, i + hd/2 of each head).
-__device__ __forceinline__ void rope_in_chunk(float (&v)[32], int hd, const float* cr,
-                                              const float* sr) {
-  const int half = hd >> 1;
+// Rotates the 32 values of one chunk in place: heads of HD ≤ 32 lie inside
+// the chunk (pairs i, i + HD/2 of each head).
+template <int HD>
+__device__ __forceinline__ void rope_in_chunk(float (&v)[32], const float* cr, const float* sr) {
+  constexpr int kHalf = HD / 2;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    const int t = i & (hd - 1);
-    if (t < half) {
-      const float c = cr[t], sn = sr[t];
-      const float x1 = v[i], x2 = v[i + half < 32 ? i + half : i];
+    if ((i % HD) < kHalf) {
+      const float c = cr[i % HD], sn = sr[i % HD];
+      const float x1 = v[i], x2 = v[i + kHalf];
       v[i] = x1 * c - x2 * sn;
-      v[i + half < 32 ? i + half : i] = x2 * c + x1 * sn;
+      v[i + kHalf] = x2 * c + x1 * sn;
     }
   }
 }
 
-// kEpiStore with RoPE on q/k columns: each thread owns whole heads of its
-// row (the two warps of a lane quarter take alternate heads).
-template <int BN, bool S8, typename OutT>
-__device__ __forceinline__ void epilogue_qkv_rope(uint32_t taddr, int row, int M, int N, int nb,
-                                                  int part, const EpiParams& ep) {
+// kEpiStore / kEpiGelu / kEpiSwiglu / kEpiResid for one thread (= one row).
+// The two warps sharing a TMEM lane quarter split the 32-column chunks
+// (part = 0/1; whole heads per thread when RoPE is on).
+template <int BN, int EPI, bool S8, typename Sink>
+__device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, int M, int N,
+                                             int nb, int part, const EpiParams& ep, Sink& sink) {
   const bool row_ok = row < M;
   const float a_s = (S8 && row_ok) ? ep.a_scale[row] : 0.0f;
-  OutT* out = reinterpret_cast<OutT*>(ep.out);
-  const int hd = ep.rope_hd, half = hd >> 1;
-  const int pos = row_ok ? seq_position(ep.cu, ep.nseq, row) : 0;
-  const float* cr = ep.rope_cos + (size_t)pos * half;
-  const float* sr = ep.rope_sin + (size_t)pos * half;
-  const int col0 = nb * BN;
-  const int span = hd < 32 ? 32 : hd;         // columns handled as one unit
-#pragma unroll 1
-  for (int c = part * span; c < BN; c += 2 * span) {
-    const int col = col0 + c;
-    const bool rot = col < ep.rope_cols;
-    if (span == 32) {
-      uint32_t u[32];
-      tmem_ld32(taddr + c, u);
-      tmem_ld_wait();
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = acc_value<S8>(u[i], a_s, ep, col + i < N ? col + i : N - 1);
-      if (rot) rope_in_chunk(v, hd, cr, sr);
-      if (row_ok) {
-        if (col + 32 <= N) store32<OutT>(out + (size_t)row * ep.ldo + col, v);
-        else
-          for (int i = 0; i < 32; ++i)
-            if (col + i < N) store1<OutT>(out + (size_t)row * ep.ldo + col + i, v[i]);
-      }
-    } else {  // hd == 64: the head's halves are two 32-column chunks
-      uint32_t u[32], w[32];
-      tmem_ld32(taddr + c, u);
-      tmem_ld32(taddr + c + 32, w);
-      tmem_ld_wait();
-      float a[32], b[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        a[i] = acc_value<S8>(u[i], a_s, ep, col + i);
-        b[i] = acc_value<S8>(w[i], a_s, ep, col + 32 + i);
-      }
-      if (rot) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float x1 = a[i], x2 = b[i], cc = cr[i], sn = sr[i];
-          a[i] = x1 * cc - x2 * sn;
-          b[i] = x2 * cc + x1 * sn;
-        }
-      }
-      if (row_ok) {
-        store32<OutT>(out + (size_t)row * ep.ldo + col, a);
-        store32<OutT>(out + (size_t)row * ep.ldo + col + 32, b);
-      }
-    }
-  }
-}
-
-// One tile's epilogue for one thread (= one output row). The two warps that
-// share a TMEM lane quarter split the tile's 32-column chunks (part = 0/1).
-template <int BN, int EPI, bool S8, typename OutT>
-__device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int M, int N, int nb,
-                                             int part, const EpiParams& ep) {
-  const bool row_ok = row < M;
-  const float a_s = (S8 && row_ok) ? ep.a_scale[row] : 0.0f;
-  OutT* out = reinterpret_cast<OutT*>(ep.out);
   if constexpr (EPI == kEpiSwiglu) {
     constexpr int kHalf = BN / 2;
     const int wcol0 = nb * BN;            // interleaved weight/bias column of this tile
     const int ocol0 = nb * kHalf;         // output column of this tile
-    const bool full = (nb + 1) * BN <= N;
 #pragma unroll 1
     for (int c = 32 * part; c < kHalf; c += 64) {
       uint32_t u[32], g[32];
       tmem_ld32(taddr + c, u);
       tmem_ld32(taddr + kHalf + c, g);
       tmem_ld_wait();
-      float v[32];
+      float hv[32], gv[32], v[32];
+      acc_values<S8>(u, a_s, ep, wcol0 + c, N, hv);
+      acc_values<S8>(g, a_s, ep, wcol0 + kHalf + c, N, gv);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int wc = wcol0 + c + i;
-        const bool ok = full || (wc + kHalf < N);
-        const float hh = ok ? acc_value<S8>(u[i], a_s, ep, wc) : 0.0f;
-        const float gg = ok ? acc_value<S8>(g[i], a_s, ep, wc + kHalf) : 0.0f;
-        v[i] = fmul(hh, act_silu<S8>(gg));
-      }
-      if (row_ok) {
-        OutT* dst = out + (size_t)row * ep.ldo + ocol0 + c;
-        if (full) {
-          store32<OutT>(dst, v);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (wcol0 + c + i + kHalf < N) store1<OutT>(dst + i, v[i]);
+      for (int i = 0; i < 32; ++i) v[i] = fmul(hv[i], act_silu<S8>(gv[i]));
+      sink.put(v, ocol0 + c, row0);
+    }
+  } else if constexpr (EPI == kEpiStore) {
+    const int col0 = nb * BN;
+    const bool rope = ep.rope_cos != nullptr;
+    const int hd = ep.rope_hd, half = hd >> 1;
+    const int pos = (rope && row_ok) ? seq_position(ep.cu, ep.nseq, row) : 0;
+    const float* cr = rope ? ep.rope_cos + (size_t)pos * half : nullptr;
+    const float* sr = rope ? ep.rope_sin + (size_t)pos * half : nullptr;
+    if (rope && hd == 64) {
+      // A head's two halves are two 32-column chunks: heads alternate by part.
+#pragma unroll 1
+      for (int c = 64 * part; c < BN; c += 128) {
+        float a[32], b[32];
+        {
+          uint32_t u[32];
+          tmem_ld32(taddr + c, u);
+          tmem_ld_wait();
+          acc_values<S8>(u, a_s, ep, col0 + c, N, a);
         }
+        {
+          uint32_t u[32];
+          tmem_ld32(taddr + c + 32, u);
+          tmem_ld_wait();
+          acc_values<S8>(u, a_s, ep, col0 + c + 32, N, b);
+        }
+        if (col0 + c < ep.rope_cols) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x1 = a[i], x2 = b[i], cc = cr[i], sn = sr[i];
+            a[i] = x1 * cc - x2 * sn;
+            b[i] = x2 * cc + x1 * sn;
+          }
+        }
+        sink.put(a, col0 + c, row0);
+        sink.put(b, col0 + c + 32, row0);
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 32 * part; c < BN; c += 64) {
+        uint32_t u[32];
+        tmem_ld32(taddr + c, u);
+        tmem_ld_wait();
+        float v[32];
+        acc_values<S8>(u, a_s, ep, col0 + c, N, v);
+        if (rope && col0 + c < ep.rope_cols) {
+          if (hd == 32) rope_in_chunk<32>(v, cr, sr);
+          else if (hd == 16) rope_in_chunk<16>(v, cr, sr);
+          else rope_in_chunk<8>(v, cr, sr);
+        }
+        sink.put(v, col0 + c, row0);
       }
     }
   } else {
     const int col0 = nb * BN;
-    const bool full = col0 + BN <= N;
 #pragma unroll 1
     for (int c = 32 * part; c < BN; c += 64) {
       uint32_t u[32];
       tmem_ld32(taddr + c, u);
-      tmem_ld_wait();
       const int col = col0 + c;
-      float v[32];
-      if (full || col + 32 <= N) {
-        float r[32];
-        if constexpr (EPI == kEpiResid) {
-          if (row_ok) load_resid32(ep, row, col, r);
-        }
+      float r[32];
+      if constexpr (EPI == kEpiResid) {
+        if (row_ok && col + 32 <= N) {
+          load_resid32(ep, row, col, r);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = acc_value<S8>(u[i], a_s, ep, col + i);
-          if constexpr (EPI == kEpiGelu) x = act_gelu<S8>(x);
-          if constexpr (EPI == kEpiResid) x = fadd(x, row_ok ? r[i] : 0.0f);
-          v[i] = x;
-        }
-        if (row_ok) store32<OutT>(out + (size_t)row * ep.ldo + col, v);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (col + i < N && row_ok) {
-            float x = acc_value<S8>(u[i], a_s, ep, col + i);
-            if constexpr (EPI == kEpiGelu) x = act_gelu<S8>(x);
-            if constexpr (EPI == kEpiResid) x = fadd(x, load_resid1(ep, row, col + i));
-            store1<OutT>(out + (size_t)row * ep.ldo + col + i, x);
-          }
+          for (int i = 0; i < 32; ++i) r[i] = 0.0f;
         }
       }
+      tmem_ld_wait();
+      float v[32];
+      acc_values<S8>(u, a_s, ep, col, N, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if constexpr (EPI == kEpiGelu) v[i] = act_gelu<S8>(v[i]);
+        if constexpr (EPI == kEpiResid) v[i] = fadd(v[i], r[i]);
+      }
+      sink.put(v, col, row0);
     }
   }
 }
@@ -367,14 +442,20 @@ __device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int M
   for (int c = c0; c < c0 + kCols; c += 32) {
     uint32_t u[32];
     tmem_ld32(taddr + c, u);
-    float r[32];
-    if (row_ok) load_resid32(ep, row, c, r);
+    float r[32], b[32];
+    if (row_ok) {
+      load_resid32(ep, row, c, r);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) r[i] = 0.0f;
+    }
+    load_col32(ep.bias, c, BN, b);
     tmem_ld_wait();
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       float v = __uint_as_float(u[i]);
-      if (ep.bias) v = fadd(v, ep.bias[c + i]);
-      v = fadd(v, row_ok ? r[i] : 0.0f);
+      if (ep.bias) v = fadd(v, b[i]);
+      v = fadd(v, r[i]);
       u[i] = __float_as_uint(v);
       s1 += (double)v;
       s2 += (double)v * (double)v;
@@ -396,11 +477,14 @@ __device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int M
   for (int c = c0; c < c0 + kCols; c += 32) {
     uint32_t u[32];
     tmem_ld32(taddr + c, u);
+    float g[32], be[32];
+    load_col32(ep.ln_w, c, BN, g);
+    load_col32(ep.ln_b, c, BN, be);
     tmem_ld_wait();
     float y[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i)
-      y[i] = fadd(fmul(fmul(fsub(__uint_as_float(u[i]), mf), inv), ep.ln_w[c + i]), ep.ln_b[c + i]);
+      y[i] = fadd(fmul(fmul(fsub(__uint_as_float(u[i]), mf), inv), g[i]), be[i]);
     if (row_ok) {
       store32<__nv_bfloat16>(out + (size_t)row * ep.ldo + c, y);
       if (ep.out_f32) store32<float>(ep.out_f32 + (size_t)row * BN + c, y);
@@ -411,8 +495,12 @@ __device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int M
 template <int BN, int EPI, bool S8, typename OutT>
 __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                   int M, int N, int K, EpiParams ep, int* err) {
+                   const __grid_constant__ CUtensorMap tmO, int M, int N, int K, EpiParams ep,
+                   int* err) {
   using C = GemmCfg<BN, S8>;
+  // bf16 outputs leave through TMA tile stores; f32 outputs and the fused
+  // LayerNorm epilogue store directly.
+  constexpr bool kTmaStore = sizeof(OutT) == 2 && EPI != kEpiResidLN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -423,7 +511,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   uint64_t* acce_bar = accf_bar + 2;               // [kNumAcc] epilogue → MMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  double2* red = reinterpret_cast<double2*>(smem + C::kStages * C::kStageBytes + 256);
+  uint8_t* extra = smem + C::kExtraOffset;         // LayerNorm sums or TMA-store staging
+  double2* red = reinterpret_cast<double2*>(extra);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -447,6 +536,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
+    if constexpr (kTmaStore) tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
@@ -557,6 +647,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     // ---------------- epilogue warps 2..9 ----------------
     const int quarter = warp & 3;        // TMEM lanes [32*quarter, 32*quarter+32)
     const int part = (warp - 2) >> 2;    // which half of the column chunks
+    TmaSink tsink{extra + (warp - 2) * 4096, &tmO, lane, 0};
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int acc = it % C::kNumAcc;
@@ -566,22 +657,23 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
         break;
       tc_fence_after();
       const int mb = tile / num_n, nb = tile % num_n;
-      const int row = mb * C::kBM + quarter * 32 + lane;
+      const int row0 = mb * C::kBM + quarter * 32;
+      const int row = row0 + lane;
       const uint32_t taddr = tmem_base + acc * C::kAccStride + ((uint32_t)(quarter * 32) << 16);
       if constexpr (EPI == kEpiResidLN) {
         epilogue_resid_ln<BN>(taddr, row, M, part, quarter, lane, ep, red);
-      } else if constexpr (EPI == kEpiStore && BN <= 256) {
-        if (ep.rope_cos)
-          epilogue_qkv_rope<BN, S8, OutT>(taddr, row, M, N, nb, part, ep);
-        else
-          epilogue_row<BN, EPI, S8, OutT>(taddr, row, M, N, nb, part, ep);
+      } else if constexpr (kTmaStore) {
+        epilogue_row<BN, EPI, S8>(taddr, row, row0, M, N, nb, part, ep, tsink);
       } else {
-        epilogue_row<BN, EPI, S8, OutT>(taddr, row, M, N, nb, part, ep);
+        DirectSink<OutT> dsink{reinterpret_cast<OutT*>(ep.out), ep.ldo, row, row < M,
+                               EPI == kEpiSwiglu ? N / 2 : N};
+        epilogue_row<BN, EPI, S8>(taddr, row, row0, M, N, nb, part, ep, dsink);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
     }
+    if constexpr (kTmaStore) tsink.drain();
   }
 
   __syncthreads();
