@@ -281,16 +281,132 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// One (head, key tile) step of one warp over its 16 query rows: S = Q Kᵀ on
+// the NBLK 8-key blocks that hold keys, masking (PARTIAL: keys ≥ nkeys in the
+// last block), online softmax with the scale folded into the exponent, and
+// O += P V. FIRST: the head's first key tile (no rescale of O).
+template <int HD, int NBLK, bool PARTIAL, bool FIRST>
+__device__ __forceinline__ void attn_step(const __nv_bfloat16* kS, const __nv_bfloat16* vS,
+                                          int k_off, int v_off, int lane, int nkeys,
+                                          float scale_log2, const uint32_t (&qf)[HD / 16][4],
+                                          float (&o)[HD / 8][4], float (&m_run)[2],
+                                          float (&l_run)[2]) {
+  constexpr int kLds = HD + 8;
+  float sc[NBLK][4];
+#pragma unroll
+  for (int nb = 0; nb < NBLK; ++nb) {
+    sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+#pragma unroll
+    for (int kc = 0; kc < HD / 16; ++kc) {
+      uint32_t kf[2];
+      ldsm_x2(kf, smem_u32(&kS[nb * 8 * kLds + k_off + kc * 16]));
+      mma_16816(sc[nb], qf[kc], kf);
+    }
+  }
+  if constexpr (PARTIAL) {
+    const int key0 = (NBLK - 1) * 8 + (lane & 3) * 2;
+    if (key0 >= nkeys) { sc[NBLK - 1][0] = -INFINITY; sc[NBLK - 1][2] = -INFINITY; }
+    if (key0 + 1 >= nkeys) { sc[NBLK - 1][1] = -INFINITY; sc[NBLK - 1][3] = -INFINITY; }
+  }
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int nb = 0; nb < NBLK; ++nb) {
+    mx0 = fmaxf(mx0, fmaxf(sc[nb][0], sc[nb][1]));
+    mx1 = fmaxf(mx1, fmaxf(sc[nb][2], sc[nb][3]));
+  }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  float ms0, ms1;
+  if constexpr (FIRST) {
+    m_run[0] = mx0;
+    m_run[1] = mx1;
+    l_run[0] = l_run[1] = 0.f;
+  } else {
+    const float n0 = fmaxf(m_run[0], mx0), n1 = fmaxf(m_run[1], mx1);
+    const float a0 = ex2_approx((m_run[0] - n0) * scale_log2);
+    const float a1 = ex2_approx((m_run[1] - n1) * scale_log2);
+    m_run[0] = n0;
+    m_run[1] = n1;
+    l_run[0] *= a0;
+    l_run[1] *= a1;
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; ++nd) {
+      o[nd][0] *= a0; o[nd][1] *= a0;
+      o[nd][2] *= a1; o[nd][3] *= a1;
+    }
+  }
+  ms0 = m_run[0] * scale_log2;
+  ms1 = m_run[1] * scale_log2;
+#pragma unroll
+  for (int nb = 0; nb < NBLK; ++nb) {
+    sc[nb][0] = ex2_approx(fmaf(sc[nb][0], scale_log2, -ms0));
+    sc[nb][1] = ex2_approx(fmaf(sc[nb][1], scale_log2, -ms0));
+    sc[nb][2] = ex2_approx(fmaf(sc[nb][2], scale_log2, -ms1));
+    sc[nb][3] = ex2_approx(fmaf(sc[nb][3], scale_log2, -ms1));
+    l_run[0] += sc[nb][0] + sc[nb][1];
+    l_run[1] += sc[nb][2] + sc[nb][3];
+  }
+  if constexpr (FIRST) {
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  }
+#pragma unroll
+  for (int kc = 0; kc < (NBLK + 1) / 2; ++kc) {
+    uint32_t pf[4];
+    pf[0] = pack_bf16(sc[2 * kc][0], sc[2 * kc][1]);
+    pf[1] = pack_bf16(sc[2 * kc][2], sc[2 * kc][3]);
+    if (2 * kc + 1 < NBLK) {
+      pf[2] = pack_bf16(sc[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][0], sc[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][1]);
+      pf[3] = pack_bf16(sc[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][2], sc[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][3]);
+    } else {
+      pf[2] = pf[3] = 0u;
+    }
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; ++nd) {
+      uint32_t vf[2];
+      ldsm_x2_t(vf, smem_u32(&vS[kc * 16 * kLds + v_off + nd * 8]));
+      mma_16816(o[nd], pf, vf);
+    }
+  }
+}
+
+template <int HD, bool FIRST>
+__device__ __forceinline__ void attn_step_dispatch(int nkeys, const __nv_bfloat16* kS,
+                                                   const __nv_bfloat16* vS, int k_off, int v_off,
+                                                   int lane, float scale_log2,
+                                                   const uint32_t (&qf)[HD / 16][4],
+                                                   float (&o)[HD / 8][4], float (&m)[2],
+                                                   float (&l)[2]) {
+  const int nblk = (nkeys + 7) >> 3;
+  const bool partial = (nkeys & 7) != 0;
+#define FUTON_STEP(NB)                                                                      \
+  case NB:                                                                                  \
+    if (partial)                                                                            \
+      attn_step<HD, NB, true, FIRST>(kS, vS, k_off, v_off, lane, nkeys, scale_log2, qf, o, m, l); \
+    else                                                                                    \
+      attn_step<HD, NB, false, FIRST>(kS, vS, k_off, v_off, lane, nkeys, scale_log2, qf, o, m, l); \
+    break;
+  switch (nblk) {
+    FUTON_STEP(1) FUTON_STEP(2) FUTON_STEP(3) FUTON_STEP(4)
+    FUTON_STEP(5) FUTON_STEP(6) FUTON_STEP(7) FUTON_STEP(8)
+  }
+#undef FUTON_STEP
+}
+
 // grid = ntiles (or nseq in cls_mode), block = 128 (4 warps × 16 query rows).
-// Work is skipped where a sequence ends: warps whose 16 query rows all lie
-// past the sequence idle, and only the 8-key blocks that hold keys are
-// multiplied (most benchmark sequences are shorter than one 64 × 64 tile).
+// Work stops where a sequence ends: warps whose 16 query rows all lie past
+// the sequence idle, and a step multiplies only the 8-key blocks that hold
+// keys (most benchmark sequences are shorter than one 64 × 64 tile).
 template <int HD, typename OutT>
 __global__ void __launch_bounds__(128, 4)
     attn_heads_kernel(const __nv_bfloat16* __restrict__ qkv, int hidden, int num_heads,
                       const int* __restrict__ cu_seqlens, const AttnTile* __restrict__ tiles,
                       int cls_mode, float scale_log2, OutT* __restrict__ out, int ldo) {
   constexpr int kLds = HD + 8, kTile = 64 * kLds;
+  constexpr int kChunks = HD / 8;                 // 16-byte chunks per row
+  constexpr int kPerThread = 64 * kChunks / 128;  // staged chunks per thread per matrix
   extern __shared__ __align__(16) __nv_bfloat16 sm_heads[];
   __nv_bfloat16* sQ = sm_heads;             // [2][kTile], slot = head parity
   __nv_bfloat16* sK = sm_heads + 2 * kTile; // [2][kTile], slot = step parity
@@ -306,14 +422,32 @@ __global__ void __launch_bounds__(128, 4)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool warp_active = tile.q0 + warp * 16 < qlim;
 
+  // This thread's staged (row, chunk) pairs: the same for every matrix/step.
+  int st_row[kPerThread], st_goff[kPerThread], st_soff[kPerThread];
+#pragma unroll
+  for (int i = 0; i < kPerThread; ++i) {
+    const int w = threadIdx.x + i * 128;
+    st_row[i] = w / kChunks;
+    st_goff[i] = st_row[i] * ld + (w % kChunks) * 8;
+    st_soff[i] = st_row[i] * kLds + (w % kChunks) * 8;
+  }
+  auto stage = [&](__nv_bfloat16* dst, const __nv_bfloat16* src, int r0, int lim) {
+    const __nv_bfloat16* g = src + (size_t)r0 * ld;
+#pragma unroll
+    for (int i = 0; i < kPerThread; ++i) {
+      const bool ok = r0 + st_row[i] < lim;
+      cp_async16(smem_u32(dst + st_soff[i]), ok ? g + st_goff[i] : src, ok);
+    }
+  };
+
   // Next (head, key tile) to stage; one commit group per step (possibly empty).
   int nh = 0, nj = 0, issued = 0;
   auto issue_next = [&]() {
     if (nh < num_heads) {
       const int slot = issued & 1;
-      if (nj == 0) stage_async<HD>(sQ + (nh & 1) * kTile, base + nh * HD, ld, tile.q0, qlim);
-      stage_async<HD>(sK + slot * kTile, base + hidden + nh * HD, ld, nj * 64, L);
-      stage_async<HD>(sV + slot * kTile, base + 2 * hidden + nh * HD, ld, nj * 64, L);
+      if (nj == 0) stage(sQ + (nh & 1) * kTile, base + nh * HD, tile.q0, qlim);
+      stage(sK + slot * kTile, base + hidden + nh * HD, nj * 64, L);
+      stage(sV + slot * kTile, base + 2 * hidden + nh * HD, nj * 64, L);
       if (++nj == nkv) { nj = 0; ++nh; }
       ++issued;
     }
@@ -335,105 +469,27 @@ __global__ void __launch_bounds__(128, 4)
       issue_next();
       cp_async_wait1();
       __syncthreads();
-      const __nv_bfloat16* kS = sK + (step & 1) * kTile;
-      const __nv_bfloat16* vS = sV + (step & 1) * kTile;
       if (warp_active) {
+        const __nv_bfloat16* kS = sK + (step & 1) * kTile;
+        const __nv_bfloat16* vS = sV + (step & 1) * kTile;
+        const int nkeys = min(64, L - j * 64);
         if (j == 0) {
           const __nv_bfloat16* qS = sQ + (head & 1) * kTile;
 #pragma unroll
           for (int kc = 0; kc < HD / 16; ++kc) ldsm_x4(qf[kc], smem_u32(&qS[q_off + kc * 16]));
-#pragma unroll
-          for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-          m_run[0] = m_run[1] = -INFINITY;
-          l_run[0] = l_run[1] = 0.f;
-        }
-        const int kv0 = j * 64;
-        const int nkeys = min(64, L - kv0);
-        const int nblk = (nkeys + 7) >> 3;  // 8-key blocks holding keys (warp-uniform)
-        float sc[8][4];
-#pragma unroll
-        for (int nb = 0; nb < 8; ++nb) {
-          sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
-          if (nb < nblk) {
-#pragma unroll
-            for (int kc = 0; kc < HD / 16; ++kc) {
-              uint32_t kf[2];
-              ldsm_x2(kf, smem_u32(&kS[nb * 8 * kLds + k_off + kc * 16]));
-              mma_16816(sc[nb], qf[kc], kf);
-            }
-          }
-        }
-        // Mask keys past the end of a partial tile.
-        if (nkeys < 64) {
-#pragma unroll
-          for (int b = 0; b < 8; ++b)
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (b * 8 + (lane & 3) * 2 + (e & 1) >= nkeys) sc[b][e] = -INFINITY;
-        }
-        // Online softmax in raw score units; the scale folds into the exponent.
-        float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-        for (int nb = 0; nb < 8; ++nb)
-          if (nb < nblk) {
-            mx[0] = fmaxf(mx[0], fmaxf(sc[nb][0], sc[nb][1]));
-            mx[1] = fmaxf(mx[1], fmaxf(sc[nb][2], sc[nb][3]));
-          }
-        float alpha[2], mscaled[2];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-          mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-          const float m_new = fmaxf(m_run[r], mx[r]);
-          alpha[r] = (m_run[r] == -INFINITY) ? 0.f : ex2_approx((m_run[r] - m_new) * scale_log2);
-          m_run[r] = m_new;
-          mscaled[r] = m_new * scale_log2;
-          l_run[r] *= alpha[r];
-        }
-#pragma unroll
-        for (int nb = 0; nb < 8; ++nb) {
-          if (nb < nblk) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float p = ex2_approx(fmaf(sc[nb][e], scale_log2, -mscaled[e >> 1]));
-              sc[nb][e] = p;
-              l_run[e >> 1] += p;
-            }
-          } else {
-            sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
-          }
-        }
-#pragma unroll
-        for (int nd = 0; nd < HD / 8; ++nd) {
-          o[nd][0] *= alpha[0]; o[nd][1] *= alpha[0];
-          o[nd][2] *= alpha[1]; o[nd][3] *= alpha[1];
-        }
-        const int nkc = (nblk + 1) >> 1;  // 16-key chunks for P·V
-#pragma unroll
-        for (int kc = 0; kc < 4; ++kc) {
-          if (kc < nkc) {
-            uint32_t pf[4];
-            pf[0] = pack_bf16(sc[2 * kc][0], sc[2 * kc][1]);
-            pf[1] = pack_bf16(sc[2 * kc][2], sc[2 * kc][3]);
-            pf[2] = pack_bf16(sc[2 * kc + 1][0], sc[2 * kc + 1][1]);
-            pf[3] = pack_bf16(sc[2 * kc + 1][2], sc[2 * kc + 1][3]);
-#pragma unroll
-            for (int nd = 0; nd < HD / 8; ++nd) {
-              uint32_t vf[2];
-              ldsm_x2_t(vf, smem_u32(&vS[kc * 16 * kLds + v_off + nd * 8]));
-              mma_16816(o[nd], pf, vf);
-            }
-          }
+          attn_step_dispatch<HD, true>(nkeys, kS, vS, k_off, v_off, lane, scale_log2, qf, o,
+                                       m_run, l_run);
+        } else {
+          attn_step_dispatch<HD, false>(nkeys, kS, vS, k_off, v_off, lane, scale_log2, qf, o,
+                                        m_run, l_run);
         }
         if (j == nkv - 1) {
-          float lsum[2];
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            lsum[r] = l_run[r];
-            lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 1);
-            lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 2);
-          }
-          const float inv0 = 1.f / lsum[0], inv1 = 1.f / lsum[1];
+          float l0 = l_run[0], l1 = l_run[1];
+          l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+          l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+          l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+          l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+          const float inv0 = 1.f / l0, inv1 = 1.f / l1;
           const int qr0 = tile.q0 + warp * 16 + (lane >> 2), qr1 = qr0 + 8;
           const size_t orow0 = cls_mode ? (size_t)tile.seq : (size_t)(s0 + qr0);
           const size_t orow1 = (size_t)(s0 + qr1);
