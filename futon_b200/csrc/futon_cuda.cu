@@ -526,8 +526,8 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   CUtensorMap ta, to;
   if (!make_operand_map(&ta, A, s8, (uint64_t)M, (uint64_t)w.k, 128))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (activation)");
-  // bf16 outputs of every epilogue but the fused LayerNorm leave through TMA.
-  const bool bf16_out = !(o.out_f32 || (s8 && o.epi != kEpiStore)) && o.epi != kEpiResidLN;
+  // bf16 outputs leave through TMA tile stores.
+  const bool bf16_out = o.epi == kEpiResidLN || !(o.out_f32 || (s8 && o.epi != kEpiStore));
   if (bf16_out) {
     const uint64_t ncols = o.epi == kEpiSwiglu ? (uint64_t)w.n / 2 : (uint64_t)w.n;
     if (!make_output_map(&to, o.out, (uint64_t)M, ncols, (uint64_t)o.ldo))

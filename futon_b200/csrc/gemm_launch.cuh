@@ -38,7 +38,7 @@ cudaError_t launch_gemm_inst(const GemmLaunch& g) {
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(1ull << (dev & 63));
   }
-  constexpr bool kTmaStore = sizeof(OutT) == 2 && EPI != kEpiResidLN;
+  constexpr bool kTmaStore = sizeof(OutT) == 2;
   if (kTmaStore && !g.to) return cudaErrorInvalidValue;  // bf16 outputs need an output map
   const long tiles = (long)((g.M + C::kBM - 1) / C::kBM) * ((g.N + BN - 1) / BN);
   if (tiles == 0) return cudaSuccess;

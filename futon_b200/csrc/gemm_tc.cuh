@@ -153,6 +153,9 @@ __device__ __forceinline__ void bulk_commit() {
 __device__ __forceinline__ void bulk_wait_read1() {
   asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
@@ -163,14 +166,17 @@ __device__ __forceinline__ void bulk_wait_all() {
 // CU_TENSOR_MAP_SWIZZLE_64B), then lane 0 stores the 32-row box with TMA;
 // two buffers per warp alternate so the next chunk overlaps the store. The
 // tensor map clips rows ≥ M and columns ≥ N.
+template <int NBUF>
 struct TmaSink {
-  uint8_t* buf;              // 2 × 2048 bytes, 1024-aligned
+  uint8_t* buf;              // NBUF × 2048 bytes, 1024-aligned
   const CUtensorMap* map;
   int lane;
   int count;
   __device__ __forceinline__ void put(const float (&v)[32], int col, int row0) {
-    uint8_t* b = buf + (count & 1) * 2048;
-    if (lane == 0 && count >= 2) bulk_wait_read1();
+    uint8_t* b = buf + (count % NBUF) * 2048;
+    if (lane == 0 && count >= NBUF) {
+      if constexpr (NBUF == 2) bulk_wait_read1(); else bulk_wait_read0();
+    }
     __syncwarp();
     const int sw = (lane >> 1) & 3;
 #pragma unroll
@@ -429,11 +435,13 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
 // then y = (v − mean)·inv·γ + β goes out as bf16 (and f32 when asked), with
 // inv = float32(1/sqrt(var + eps)) as in layerNormRows (model.go:743-769).
 // Tiles span the whole row (N = BN), so the output may overwrite the
-// residual in place: each thread reads its residual before writing its row.
-template <int BN>
-__device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int M, int part,
-                                                  int quarter, int lane, const EpiParams& ep,
-                                                  double2* red) {
+// residual in place: a warp reads its residual columns before it stores
+// them (TMA tile stores of the warp's 32-row slab), and the two warps of a
+// lane quarter own disjoint column halves.
+template <int BN, typename Sink>
+__device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int row0, int M,
+                                                  int part, int quarter, int lane,
+                                                  const EpiParams& ep, double2* red, Sink& sink) {
   constexpr int kCols = BN / 2;
   const bool row_ok = row < M;
   const int c0 = part * kCols;
@@ -472,7 +480,6 @@ __device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int M
   var = var > 0.0 ? var : 0.0;
   const float inv = (float)(1.0 / sqrt(var + (double)ep.eps));
   const float mf = (float)mean;
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(ep.out);
 #pragma unroll 1
   for (int c = c0; c < c0 + kCols; c += 32) {
     uint32_t u[32];
@@ -485,10 +492,8 @@ __device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int M
 #pragma unroll
     for (int i = 0; i < 32; ++i)
       y[i] = fadd(fmul(fmul(fsub(__uint_as_float(u[i]), mf), inv), g[i]), be[i]);
-    if (row_ok) {
-      store32<__nv_bfloat16>(out + (size_t)row * ep.ldo + c, y);
-      if (ep.out_f32) store32<float>(ep.out_f32 + (size_t)row * BN + c, y);
-    }
+    sink.put(y, c, row0);
+    if (row_ok && ep.out_f32) store32<float>(ep.out_f32 + (size_t)row * BN + c, y);
   }
 }
 
@@ -498,9 +503,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
                    const __grid_constant__ CUtensorMap tmO, int M, int N, int K, EpiParams ep,
                    int* err) {
   using C = GemmCfg<BN, S8>;
-  // bf16 outputs leave through TMA tile stores; f32 outputs and the fused
-  // LayerNorm epilogue store directly.
-  constexpr bool kTmaStore = sizeof(OutT) == 2 && EPI != kEpiResidLN;
+  // bf16 outputs leave through TMA tile stores; f32 outputs store directly.
+  constexpr bool kTmaStore = sizeof(OutT) == 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -511,7 +515,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   uint64_t* acce_bar = accf_bar + 2;               // [kNumAcc] epilogue → MMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint8_t* extra = smem + C::kExtraOffset;         // LayerNorm sums or TMA-store staging
+  // Extra region: LayerNorm kernels keep 4 KB of partial sums, then one
+  // 2 KB staging buffer per epilogue warp; other kernels two per warp.
+  uint8_t* extra = smem + C::kExtraOffset;
   double2* red = reinterpret_cast<double2*>(extra);
 
   const int warp = threadIdx.x >> 5;
@@ -647,7 +653,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     // ---------------- epilogue warps 2..9 ----------------
     const int quarter = warp & 3;        // TMEM lanes [32*quarter, 32*quarter+32)
     const int part = (warp - 2) >> 2;    // which half of the column chunks
-    TmaSink tsink{extra + (warp - 2) * 4096, &tmO, lane, 0};
+    TmaSink<2> tsink{extra + (warp - 2) * 4096, &tmO, lane, 0};
+    TmaSink<1> lsink{extra + 4096 + (warp - 2) * 2048, &tmO, lane, 0};
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int acc = it % C::kNumAcc;
@@ -661,7 +668,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
       const int row = row0 + lane;
       const uint32_t taddr = tmem_base + acc * C::kAccStride + ((uint32_t)(quarter * 32) << 16);
       if constexpr (EPI == kEpiResidLN) {
-        epilogue_resid_ln<BN>(taddr, row, M, part, quarter, lane, ep, red);
+        epilogue_resid_ln<BN>(taddr, row, row0, M, part, quarter, lane, ep, red, lsink);
       } else if constexpr (kTmaStore) {
         epilogue_row<BN, EPI, S8>(taddr, row, row0, M, N, nb, part, ep, tsink);
       } else {
@@ -673,7 +680,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
     }
-    if constexpr (kTmaStore) tsink.drain();
+    if constexpr (EPI == kEpiResidLN) lsink.drain();
+    else if constexpr (kTmaStore) tsink.drain();
   }
 
   __syncthreads();
