@@ -437,26 +437,62 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
 // Tiles span the whole row (N = BN), so the output may overwrite the
 // residual in place: a warp reads its residual columns before it stores
 // them (TMA tile stores of the warp's 32-row slab), and the two warps of a
-// lane quarter own disjoint column halves.
+// lane quarter own disjoint column halves. The bf16 residual is read two
+// chunks ahead; the first two loads are issued before the accumulator is
+// ready (ln_prefetch), so they overlap the tile's MMAs.
+struct LnResid {
+  uint4 buf[2][4];  // two chunks of 32 bf16
+};
+
+template <int BN>
+__device__ __forceinline__ void ln_load_chunk(const EpiParams& ep, int row, bool row_ok, int col,
+                                              uint4 (&dst)[4]) {
+  if (row_ok) {
+    const uint4* rp = reinterpret_cast<const uint4*>(
+        reinterpret_cast<const __nv_bfloat16*>(ep.resid) + (size_t)row * ep.ldr + col);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = rp[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <int BN>
+__device__ __forceinline__ void ln_prefetch(const EpiParams& ep, int row, int M, int part,
+                                            LnResid& rs) {
+  const int c0 = part * (BN / 2);
+  ln_load_chunk<BN>(ep, row, row < M, c0, rs.buf[0]);
+  ln_load_chunk<BN>(ep, row, row < M, c0 + 32, rs.buf[1]);
+}
+
 template <int BN, typename Sink>
 __device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int row0, int M,
                                                   int part, int quarter, int lane,
-                                                  const EpiParams& ep, double2* red, Sink& sink) {
-  constexpr int kCols = BN / 2;
+                                                  const EpiParams& ep, double2* red, Sink& sink,
+                                                  LnResid& rs) {
+  constexpr int kCols = BN / 2, kChunks = kCols / 32;
   const bool row_ok = row < M;
   const int c0 = part * kCols;
   double s1 = 0.0, s2 = 0.0;
-#pragma unroll 1
-  for (int c = c0; c < c0 + kCols; c += 32) {
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    const int c = c0 + 32 * k;
     uint32_t u[32];
     tmem_ld32(taddr + c, u);
     float r[32], b[32];
-    if (row_ok) {
-      load_resid32(ep, row, c, r);
-    } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) r[i] = 0.0f;
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t w[4] = {rs.buf[k & 1][i].x, rs.buf[k & 1][i].y, rs.buf[k & 1][i].z,
+                             rs.buf[k & 1][i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+        r[8 * i + 2 * j] = f.x;
+        r[8 * i + 2 * j + 1] = f.y;
+      }
     }
+    if (k + 2 < kChunks) ln_load_chunk<BN>(ep, row, row_ok, c + 64, rs.buf[k & 1]);
     load_col32(ep.bias, c, BN, b);
     tmem_ld_wait();
 #pragma unroll
@@ -659,16 +695,18 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int acc = it % C::kNumAcc;
       const uint32_t acc_phase = (uint32_t)(it / C::kNumAcc) & 1u;
+      const int mb = tile / num_n, nb = tile % num_n;
+      const int row0 = mb * C::kBM + quarter * 32;
+      const int row = row0 + lane;
+      LnResid rs;
+      if constexpr (EPI == kEpiResidLN) ln_prefetch<BN>(ep, row, M, part, rs);
       if (!mbar_wait_bounded(smem_u32(&accf_bar[acc]), acc_phase, err, kDevTimeoutAccFull,
                              abort_flag))
         break;
       tc_fence_after();
-      const int mb = tile / num_n, nb = tile % num_n;
-      const int row0 = mb * C::kBM + quarter * 32;
-      const int row = row0 + lane;
       const uint32_t taddr = tmem_base + acc * C::kAccStride + ((uint32_t)(quarter * 32) << 16);
       if constexpr (EPI == kEpiResidLN) {
-        epilogue_resid_ln<BN>(taddr, row, row0, M, part, quarter, lane, ep, red, lsink);
+        epilogue_resid_ln<BN>(taddr, row, row0, M, part, quarter, lane, ep, red, lsink, rs);
       } else if constexpr (kTmaStore) {
         epilogue_row<BN, EPI, S8>(taddr, row, row0, M, N, nb, part, ep, tsink);
       } else {

@@ -74,23 +74,38 @@ __device__ __forceinline__ float sigmoid_f32(float x) {
 }
 
 // Fast variants for the bf16 path, whose outputs are rounded to bf16 (2^-9
-// relative) right after: erfc from Abramowitz & Stegun 7.1.26 (absolute
-// error ≤ 1.5e-7) with CUDA's __expf / __fdividef intrinsics, arranged like
-// geluF32 (0.5·x·erfc(|x|/√2) for x < 0, 0.5·x·(2 − erfc) otherwise).
-__device__ __forceinline__ float gelu_fast(float x) {
-  const float z = fabsf(x) * 0.70710678118654752f;
-  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
-  float p = fmaf(1.061405429f, t, -1.453152027f);
-  p = fmaf(p, t, 1.421413741f);
-  p = fmaf(p, t, -0.284496736f);
-  p = fmaf(p, t, 0.254829592f);
-  const float q = p * t * __expf(-z * z);  // erfc(|x|/√2)
-  return x < 0.0f ? 0.5f * x * q : 0.5f * x * (2.0f - q);
+// relative) right after. GELU: erfc(z) = 1 / P(z)^16 with the degree-6
+// polynomial of Abramowitz & Stegun 7.1.28 (|error| ≤ 3e-7), one hardware
+// reciprocal and no exponential, arranged like geluF32 (0.5·x·erfc(|x|/√2)
+// for x < 0, x − 0.5·x·erfc otherwise); P^16 overflowing to +inf gives
+// erfc = 0, the correct limit. SiLU: g · 1/(1 + 2^(−g·log2 e)).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// g·σ(g) with the exponent clamped so the denominator stays finite.
+__device__ __forceinline__ float gelu_fast(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  float p = fmaf(0.0000430638f, z, 0.0002765672f);
+  p = fmaf(p, z, 0.0001520143f);
+  p = fmaf(p, z, 0.0092705272f);
+  p = fmaf(p, z, 0.0422820123f);
+  p = fmaf(p, z, 0.0705230784f);
+  p = fmaf(p, z, 1.0f);
+  const float p2 = p * p, p4 = p2 * p2, p8 = p4 * p4;
+  const float q = rcp_approx((p8 + p8) * p8);  // 0.5 · erfc(|x|/√2)
+  return x < 0.0f ? x * q : fmaf(-x, q, x);
+}
+
 __device__ __forceinline__ float silu_fast(float g) {
-  return __fdividef(g, 1.0f + __expf(fminf(-g, 80.0f)));
+  const float e = exp2_approx(fminf(-g, 80.0f) * 1.4426950408889634f);
+  return g * rcp_approx(1.0f + e);
 }
 
 }  // namespace futon
