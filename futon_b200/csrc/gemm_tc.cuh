@@ -419,10 +419,15 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
       tmem_ld_wait();
       float v[32];
       acc_values<S8>(u, a_s, ep, col, N, v);
+      if constexpr (EPI == kEpiGelu && !S8) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if constexpr (EPI == kEpiGelu) v[i] = act_gelu<S8>(v[i]);
-        if constexpr (EPI == kEpiResid) v[i] = fadd(v[i], r[i]);
+        for (int i = 0; i < 16; ++i) gelu_fast2(v[2 * i], v[2 * i + 1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if constexpr (EPI == kEpiGelu) v[i] = act_gelu<S8>(v[i]);
+          if constexpr (EPI == kEpiResid) v[i] = fadd(v[i], r[i]);
+        }
       }
       sink.put(v, col, row0);
     }
