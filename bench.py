@@ -17,6 +17,10 @@ barrier and the max-over-ranks of the timings).
          library's per-stage profiler over a second timed pass)
   cpu_baseline  the reference algorithm on the host cores (the CPU oracle's
          AVX2 port of the reference kernel, all threads) on a bounded sample
+  seq128 the throughput target's shape — 8,192 bge sequences of 128 tokens per
+         GPU, ids in HBM, CUDA events — with its fraction of the bf16 peak
+  p50_batch_latency  median over 50 calls of one c0 batch (32 sequences,
+         L ~ U[8, 128]) through the host-buffer C ABI, wall clock per call
 
 `--impl reference` times that CPU port alone (the reference is Go and has no
 GPU path; it cannot be built on this image) and prints its own line.
@@ -295,6 +299,45 @@ def main():
     h2d = ids.nbytes + cu.nbytes + ntiles * 8
     d2h = nseq * dim * 4 + 4
 
+    # ---- the target shape: bge at sequence length 128 ----
+    ids128, cu128 = synth.make_inputs("bge-seq128", seed=11 + rank)
+    n128 = len(cu128) - 1
+    flops128 = synth.total_flops(cfg, cu128)
+    d_ids128 = torch.from_numpy(ids128).cuda()
+    d_out128 = torch.empty((n128, dim), dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        model.encode_device(d_ids128.data_ptr(), cu128, 0, d_out128.data_ptr(), stream=sh)
+    barrier()
+    q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    q0.record(stream)
+    for _ in range(args.steps):
+        model.encode_device(d_ids128.data_ptr(), cu128, 0, d_out128.data_ptr(), stream=sh)
+    q1.record(stream)
+    q1.synchronize()
+    barrier()
+    ms128 = max_over_ranks(q0.elapsed_time(q1)) / args.steps
+    tf128 = flops128 / (ms128 / 1e3) / 1e12
+    seq128 = {"seqs_per_rank": n128, "seq_len": 128, "ms_per_step": round(ms128, 3),
+              "embeddings_per_sec": round(world * n128 / (ms128 / 1e3), 1),
+              "tokens_per_sec": round(world * int(cu128[-1]) / (ms128 / 1e3), 1),
+              "tflops_per_gpu": round(tf128, 1),
+              "frac_of_bf16_peak": round(tf128 / peaks["bf16_tflops"], 4),
+              "frac_of_bf16_peak_sustained": round(tf128 / peak, 4)}
+    del d_ids128, d_out128
+
+    # ---- p50 latency of one c0 batch through the host-buffer ABI ----
+    ids0, cu0 = synth.make_inputs("c0", seed=1 + rank)
+    for _ in range(5):
+        model.encode_packed(ids0, cu0)
+    lat = []
+    for _ in range(50):
+        t0 = time.perf_counter()
+        model.encode_packed(ids0, cu0)
+        lat.append((time.perf_counter() - t0) * 1e3)
+    p50 = max_over_ranks(statistics.median(lat))
+    latency = {"config": "c0: 32 bge sequences, L ~ U[8, 128], host buffers", "repeats": 50,
+               "p50_ms": round(p50, 3)}
+
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline()
@@ -326,6 +369,8 @@ def main():
                          "avg_launch_ms": round(per_launch_ms, 4),
                          "profiled_ms_per_step": round(prof_ms, 3)},
             "stages": breakdown,
+            "seq128": seq128,
+            "p50_batch_latency": latency,
             "clocks": clk,
             "cpu_baseline": cb,
         }

@@ -5,26 +5,27 @@
 // The reference materialises a seq×padSeq(seq) score matrix per head; here
 // scores never leave the SM. Queries, keys and values are read straight from
 // the fused [T, 3h] qkv buffer (q columns head·hd, k columns h + head·hd,
-// v columns 2h + head·hd, model.go:660-662). NeoX rotary embedding
-// (model.go:674-685) is applied to q and k while they are staged, from the
-// f32 cos/sin tables built like precomputeRoPE (model.go:306-318).
-//
-// q and k arrive rotated: NeoX RoPE (model.go:674-685) runs in the qkv GEMM
-// epilogue, on the f32 accumulator.
+// v columns 2h + head·hd, model.go:660-662). q and k arrive rotated: NeoX
+// RoPE (model.go:674-685) runs in the qkv GEMM epilogue, on the f32
+// accumulator.
 //
 // Kernels:
 //   attn_heads_kernel  one 64-query tile of one sequence per CTA, all heads
 //                      in turn, 64-key tiles staged by cp.async in a two-slot
-//                      ring, bf16 m16n8k16 tensor-core MMAs with f32
-//                      accumulation and online softmax (head_dim 32 or 64);
-//                      also the CLS-only last layer (model.go:403-410).
+//                      ring, m16n8k16 tensor-core MMAs with f32 accumulation
+//                      (Q·Kᵀ in bf16, P·V in f16 — v is stored as f16) and
+//                      online softmax (head_dim 32 or 64); also the CLS-only
+//                      last layer (model.go:403-410).
 //   attn_flash_split_kernel  int8 path: 64 queries × one head per CTA over
 //                      f32 qkv, every operand split into bf16 hi + lo parts.
 //   attn_rowq_kernel   one warp per (query, head): lanes split the keys,
 //                      f32 math, warp merge (head dims other than 32/64).
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
+#include "mathf32.cuh"
 
 namespace futon {
 
@@ -41,6 +42,11 @@ __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
 __device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
                : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
 __device__ __forceinline__ void ldsm_x2_t(uint32_t (&r)[2], uint32_t addr) {
@@ -281,26 +287,50 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+__device__ __forceinline__ void mma_16816_f16(float (&d)[4], const uint32_t (&a)[4],
+                                              const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// 2^lo, 2^hi as one f16x2 word (lo in the low half): the exponents are
+// rounded to f16 (relative error of the power ≤ 2^-11·|t|·ln 2, so at most
+// 2^-12 where the probability is above 1/2 and 2^-8 where it is below 2^-8)
+// and the powers come back in f16 — the A operand of the P·V MMA as is.
+__device__ __forceinline__ uint32_t ex2_f16x2(float lo, float hi) {
+  uint32_t t, r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(t) : "f"(hi), "f"(lo));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(t));
+  return r;
+}
+
 // One (head, key tile) step of one warp over its 16 query rows: S = Q Kᵀ on
 // the NBLK 8-key blocks that hold keys, masking (PARTIAL: keys ≥ nkeys in the
 // last block), online softmax with the scale folded into the exponent, and
-// O += P V. FIRST: the head's first key tile (no rescale of O).
+// O += P V with P and V in f16. The softmax denominators come out of the
+// same MMAs: a ninth (fifth) B block of ones sums each row of P exactly as
+// it is multiplied. FIRST: the head's first key tile (no rescale of O).
 template <int HD, int NBLK, bool PARTIAL, bool FIRST>
-__device__ __forceinline__ void attn_step(const __nv_bfloat16* kS, const __nv_bfloat16* vS,
+__device__ __forceinline__ void attn_step(const __nv_bfloat16* kS, const __half* vS,
                                           int k_off, int v_off, int lane, int nkeys,
                                           float scale_log2, const uint32_t (&qf)[HD / 16][4],
                                           float (&o)[HD / 8][4], float (&m_run)[2],
-                                          float (&l_run)[2]) {
+                                          float (&lsum)[4]) {
   constexpr int kLds = HD + 8;
   float sc[NBLK][4];
 #pragma unroll
   for (int nb = 0; nb < NBLK; ++nb) {
     sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
 #pragma unroll
-    for (int kc = 0; kc < HD / 16; ++kc) {
-      uint32_t kf[2];
-      ldsm_x2(kf, smem_u32(&kS[nb * 8 * kLds + k_off + kc * 16]));
-      mma_16816(sc[nb], qf[kc], kf);
+    for (int kc = 0; kc < HD / 16; kc += 2) {
+      uint32_t kf[4];
+      ldsm_x4(kf, smem_u32(&kS[nb * 8 * kLds + k_off + kc * 16]));
+      const uint32_t k0[2] = {kf[0], kf[1]}, k1[2] = {kf[2], kf[3]};
+      mma_16816(sc[nb], qf[kc], k0);
+      mma_16816(sc[nb], qf[kc + 1], k1);
     }
   }
   if constexpr (PARTIAL) {
@@ -318,67 +348,70 @@ __device__ __forceinline__ void attn_step(const __nv_bfloat16* kS, const __nv_bf
   mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-  float ms0, ms1;
   if constexpr (FIRST) {
     m_run[0] = mx0;
     m_run[1] = mx1;
-    l_run[0] = l_run[1] = 0.f;
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+    lsum[0] = lsum[1] = lsum[2] = lsum[3] = 0.f;
   } else {
     const float n0 = fmaxf(m_run[0], mx0), n1 = fmaxf(m_run[1], mx1);
     const float a0 = ex2_approx((m_run[0] - n0) * scale_log2);
     const float a1 = ex2_approx((m_run[1] - n1) * scale_log2);
     m_run[0] = n0;
     m_run[1] = n1;
-    l_run[0] *= a0;
-    l_run[1] *= a1;
+    const uint64_t r0 = f2_pack(a0, a0), r1 = f2_pack(a1, a1);
 #pragma unroll
     for (int nd = 0; nd < HD / 8; ++nd) {
-      o[nd][0] *= a0; o[nd][1] *= a0;
-      o[nd][2] *= a1; o[nd][3] *= a1;
+      f2_unpack(f2_mul(f2_pack(o[nd][0], o[nd][1]), r0), o[nd][0], o[nd][1]);
+      f2_unpack(f2_mul(f2_pack(o[nd][2], o[nd][3]), r1), o[nd][2], o[nd][3]);
     }
+    f2_unpack(f2_mul(f2_pack(lsum[0], lsum[1]), r0), lsum[0], lsum[1]);
+    f2_unpack(f2_mul(f2_pack(lsum[2], lsum[3]), r1), lsum[2], lsum[3]);
   }
-  ms0 = m_run[0] * scale_log2;
-  ms1 = m_run[1] * scale_log2;
+  const float ms0 = m_run[0] * scale_log2, ms1 = m_run[1] * scale_log2;
+  const uint64_t sl = f2_pack(scale_log2, scale_log2);
+  const uint64_t nm0 = f2_pack(-ms0, -ms0), nm1 = f2_pack(-ms1, -ms1);
+  uint32_t pw[NBLK][2];  // P as f16x2: [block][row half]
 #pragma unroll
   for (int nb = 0; nb < NBLK; ++nb) {
-    sc[nb][0] = ex2_approx(fmaf(sc[nb][0], scale_log2, -ms0));
-    sc[nb][1] = ex2_approx(fmaf(sc[nb][1], scale_log2, -ms0));
-    sc[nb][2] = ex2_approx(fmaf(sc[nb][2], scale_log2, -ms1));
-    sc[nb][3] = ex2_approx(fmaf(sc[nb][3], scale_log2, -ms1));
-    l_run[0] += sc[nb][0] + sc[nb][1];
-    l_run[1] += sc[nb][2] + sc[nb][3];
+    float t0, t1, t2, t3;
+    f2_unpack(f2_fma(f2_pack(sc[nb][0], sc[nb][1]), sl, nm0), t0, t1);
+    f2_unpack(f2_fma(f2_pack(sc[nb][2], sc[nb][3]), sl, nm1), t2, t3);
+    pw[nb][0] = ex2_f16x2(t0, t1);
+    pw[nb][1] = ex2_f16x2(t2, t3);
   }
-  if constexpr (FIRST) {
-#pragma unroll
-    for (int nd = 0; nd < HD / 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
-  }
+  const uint32_t ones[2] = {0x3C003C00u, 0x3C003C00u};  // f16 1.0 pairs
 #pragma unroll
   for (int kc = 0; kc < (NBLK + 1) / 2; ++kc) {
     uint32_t pf[4];
-    pf[0] = pack_bf16(sc[2 * kc][0], sc[2 * kc][1]);
-    pf[1] = pack_bf16(sc[2 * kc][2], sc[2 * kc][3]);
+    pf[0] = pw[2 * kc][0];
+    pf[1] = pw[2 * kc][1];
     if (2 * kc + 1 < NBLK) {
-      pf[2] = pack_bf16(sc[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][0], sc[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][1]);
-      pf[3] = pack_bf16(sc[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][2], sc[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][3]);
+      pf[2] = pw[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][0];
+      pf[3] = pw[2 * kc + 1 < NBLK ? 2 * kc + 1 : 0][1];
     } else {
       pf[2] = pf[3] = 0u;
     }
 #pragma unroll
-    for (int nd = 0; nd < HD / 8; ++nd) {
-      uint32_t vf[2];
-      ldsm_x2_t(vf, smem_u32(&vS[kc * 16 * kLds + v_off + nd * 8]));
-      mma_16816(o[nd], pf, vf);
+    for (int nd = 0; nd < HD / 8; nd += 2) {
+      uint32_t vf[4];
+      ldsm_x4_t(vf, smem_u32(&vS[kc * 16 * kLds + v_off + nd * 8]));
+      const uint32_t v0[2] = {vf[0], vf[1]}, v1[2] = {vf[2], vf[3]};
+      mma_16816_f16(o[nd], pf, v0);
+      mma_16816_f16(o[nd + 1], pf, v1);
     }
+    mma_16816_f16(lsum, pf, ones);
   }
 }
 
 template <int HD, bool FIRST>
 __device__ __forceinline__ void attn_step_dispatch(int nkeys, const __nv_bfloat16* kS,
-                                                   const __nv_bfloat16* vS, int k_off, int v_off,
+                                                   const __half* vS, int k_off, int v_off,
                                                    int lane, float scale_log2,
                                                    const uint32_t (&qf)[HD / 16][4],
                                                    float (&o)[HD / 8][4], float (&m)[2],
-                                                   float (&l)[2]) {
+                                                   float (&l)[4]) {
   const int nblk = (nkeys + 7) >> 3;
   const bool partial = (nkeys & 7) != 0;
 #define FUTON_STEP(NB)                                                                      \
@@ -456,12 +489,12 @@ __global__ void __launch_bounds__(128, 4)
 
   // Per-thread ldmatrix offsets (elements).
   const int q_off = (warp * 16 + (lane & 15)) * kLds + (lane >> 4) * 8;
-  const int k_off = (lane & 7) * kLds + ((lane >> 3) & 1) * 8;
-  const int v_off = (lane & 15) * kLds;
+  const int k_off = (lane & 7) * kLds + (lane >> 3) * 8;    // x4: two 16-column chunks
+  const int v_off = (lane & 15) * kLds + (lane >> 4) * 8;   // x4.trans: two 8-column blocks
 
   uint32_t qf[HD / 16][4];
   float o[HD / 8][4];
-  float m_run[2], l_run[2];
+  float m_run[2], l_run[4];
   issue_next();
   int step = 0;
   for (int head = 0; head < num_heads; ++head) {
@@ -471,7 +504,8 @@ __global__ void __launch_bounds__(128, 4)
       __syncthreads();
       if (warp_active) {
         const __nv_bfloat16* kS = sK + (step & 1) * kTile;
-        const __nv_bfloat16* vS = sV + (step & 1) * kTile;
+        // V columns are stored as f16 by the qkv GEMM epilogue.
+        const __half* vS = reinterpret_cast<const __half*>(sV + (step & 1) * kTile);
         const int nkeys = min(64, L - j * 64);
         if (j == 0) {
           const __nv_bfloat16* qS = sQ + (head & 1) * kTile;
@@ -484,12 +518,8 @@ __global__ void __launch_bounds__(128, 4)
                                         m_run, l_run);
         }
         if (j == nkv - 1) {
-          float l0 = l_run[0], l1 = l_run[1];
-          l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-          l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-          l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-          l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-          const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+          // Every column of the ones block holds the full row sum.
+          const float inv0 = 1.f / l_run[0], inv1 = 1.f / l_run[2];
           const int qr0 = tile.q0 + warp * 16 + (lane >> 2), qr1 = qr0 + 8;
           const size_t orow0 = cls_mode ? (size_t)tile.seq : (size_t)(s0 + qr0);
           const size_t orow1 = (size_t)(s0 + qr1);

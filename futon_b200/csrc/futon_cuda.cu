@@ -511,6 +511,7 @@ struct GemmOut {
   int rope_cols = 0;
   const int* cu = nullptr;
   int nseq = 0;
+  int f16_from = 1 << 30;
 };
 
 int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale, int M,
@@ -561,6 +562,7 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   g.ep.rope_cols = o.rope_cols;
   g.ep.cu = o.cu;
   g.ep.nseq = o.nseq;
+  g.ep.f16_from = o.f16_from;
   g.err = d.err_word;
   g.num_sms = d.num_sms;
   g.stream = st;
@@ -675,13 +677,15 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
     const bool last_cls = cls && last;
     const int rows = last_cls ? nseq : T;
 
-    // qkv = x·Wqkvᵀ + b → [T, 3h] (bf16; f32 on the int8 path)
+    // qkv = x·Wqkvᵀ + b → [T, 3h] (bf16 q, k and f16 v for the tensor-core
+    // attention; bf16 throughout for other head dims; f32 on the int8 path)
     {
       GemmOut o;
       o.epi = kEpiStore;
       o.out_f32 = q8;
       o.out = w.qkv;
       o.ldo = 3 * h;
+      if (!q8 && (m.head_dim == 32 || m.head_dim == 64)) o.f16_from = 2 * h;
       if (c.position_encoding == FUTON_POS_ROPE) {
         o.rope_cos = d.rcos;
         o.rope_sin = d.rsin;
@@ -1046,6 +1050,7 @@ int seam_gemm(SeamCtx& s, const void* A, bool s8, const float* a_scale, int m, c
   g.ep.rope_cols = 0;
   g.ep.cu = nullptr;
   g.ep.nseq = 0;
+  g.ep.f16_from = 1 << 30;
   g.err = s.err_word;
   g.num_sms = s.num_sms;
   g.stream = st;
@@ -1542,6 +1547,7 @@ extern "C" int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const
   g.ep.rope_cols = 0;
   g.ep.cu = nullptr;
   g.ep.nseq = 0;
+  g.ep.f16_from = 1 << 30;
   g.err = s->err;
   g.num_sms = s->num_sms;
   g.stream = st;

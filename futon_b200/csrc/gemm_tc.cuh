@@ -31,6 +31,8 @@
 // through L2; the weights (≤ 19 MB) stay L2-resident.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "mathf32.cuh"
 
@@ -60,6 +62,7 @@ struct EpiParams {
   int rope_cols;
   const int* cu;
   int nseq;
+  int f16_from;  // TMA-store outputs at columns ≥ f16_from are written as f16 (qkv: V)
 };
 
 template <int BN, bool S8>
@@ -92,6 +95,16 @@ template <> __device__ __forceinline__ void store32<float>(float* dst, const flo
   float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
   for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+__device__ __forceinline__ uint4 pack8_f16(const float* v) {
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __half2 p = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+    w[j] = *reinterpret_cast<uint32_t*>(&p);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 __device__ __forceinline__ uint4 pack8_bf16(const float* v) {
@@ -172,6 +185,7 @@ struct TmaSink {
   const CUtensorMap* map;
   int lane;
   int count;
+  int f16_from;              // columns ≥ f16_from are packed as f16
   __device__ __forceinline__ void put(const float (&v)[32], int col, int row0) {
     uint8_t* b = buf + (count % NBUF) * 2048;
     if (lane == 0 && count >= NBUF) {
@@ -179,9 +193,15 @@ struct TmaSink {
     }
     __syncwarp();
     const int sw = (lane >> 1) & 3;
+    if (col >= f16_from) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
-      *reinterpret_cast<uint4*>(b + lane * 64 + ((c ^ sw) << 4)) = pack8_bf16(v + 8 * c);
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(b + lane * 64 + ((c ^ sw) << 4)) = pack8_f16(v + 8 * c);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(b + lane * 64 + ((c ^ sw) << 4)) = pack8_bf16(v + 8 * c);
+    }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
@@ -694,8 +714,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     // ---------------- epilogue warps 2..9 ----------------
     const int quarter = warp & 3;        // TMEM lanes [32*quarter, 32*quarter+32)
     const int part = (warp - 2) >> 2;    // which half of the column chunks
-    TmaSink<2> tsink{extra + (warp - 2) * 4096, &tmO, lane, 0};
-    TmaSink<1> lsink{extra + 4096 + (warp - 2) * 2048, &tmO, lane, 0};
+    TmaSink<2> tsink{extra + (warp - 2) * 4096, &tmO, lane, 0, ep.f16_from};
+    TmaSink<1> lsink{extra + 4096 + (warp - 2) * 2048, &tmO, lane, 0, 1 << 30};
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int acc = it % C::kNumAcc;

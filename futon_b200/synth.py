@@ -66,6 +66,8 @@ CONFIGS: Dict[str, BenchConfig] = {
     "c2": BenchConfig("c2", "nomic", 64, ("uniform", 64, 512), out_dims=(768, 256, 64)),
     "c3": BenchConfig("c3", "arctic", 16, ("fixed", 2048), q8_modes=(False, True)),
     "c4": BenchConfig("c4", "bge", 65536, ("lognormal", 64, 0.8, 8, 512)),
+    # The throughput target's shape: bge-small at sequence length 128.
+    "bge-seq128": BenchConfig("bge-seq128", "bge", 8192, ("fixed", 128)),
 }
 
 
