@@ -263,19 +263,32 @@ def main():
     top = max(gemms, key=lambda k: gemms[k]["ms"])
     tk = gemms[top]
     per_launch_ms = tk["ms"] / tk["launches"]
-    achieved = tk["flops"] / tk["launches"] / (per_launch_ms / 1e3) / 1e12
-    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
-    # DRAM traffic of the dominant kernel from the committed ncu capture,
-    # scaled from bytes per token to this bench's average launch.
+    peak_tf = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    peak_bw = peaks.get("hbm_gbs")
+    # The bound is whichever peak makes the launch's algorithmic work take
+    # longer: FLOPs at the bf16 tensor peak or bytes at the HBM copy rate.
+    t_tensor = tk["flops"] / (peak_tf * 1e12)
+    t_hbm = tk["bytes"] / (peak_bw * 1e9) if peak_bw else 0.0
+    if t_hbm > t_tensor:
+        bound, unit, peak = "hbm", "GB/s", peak_bw
+        achieved = tk["bytes"] / tk["launches"] / (per_launch_ms / 1e3) / 1e9
+        peak_name = "hbm_gbs"
+    else:
+        bound, unit, peak = "tensor", "TFLOP/s", peak_tf
+        achieved = tk["flops"] / tk["launches"] / (per_launch_ms / 1e3) / 1e12
+        peak_name = "bf16_tflops_sustained"
+    # DRAM traffic of the dominant kernel from the committed ncu capture
+    # (DRAM bytes per algorithmic FLOP or byte of the captured launch), scaled
+    # to this bench's average launch.
     traffic, traffic_src = None, None
     tf = ROOT / "profiles" / "traffic_per_launch.txt"
     if tf.exists():
         for ln in tf.read_text().splitlines():
             f = ln.split()
             if len(f) >= 4 and f[0] == top and not ln.startswith("#"):
-                tokens_per_launch = tk["flops"] / tk["launches"] / float(f[2])
-                traffic = round(float(f[1]) * tokens_per_launch)
-                traffic_src = f"profiles/{f[3]} (scaled per token)"
+                basis = {"flop": "flops", "byte": "bytes"}[f[2]]
+                traffic = round(float(f[1]) * tk[basis] / tk["launches"])
+                traffic_src = f"profiles/{f[3]} (DRAM bytes per algorithmic {f[2]}, scaled)"
     total_ms = sum(v["ms"] for v in prof.values()) / args.steps
     breakdown = {k: {"ms_per_step": round(v["ms"] / args.steps, 3),
                      "share": round(v["ms"] / args.steps / total_ms, 4),
@@ -322,7 +335,7 @@ def main():
               "tokens_per_sec": round(world * int(cu128[-1]) / (ms128 / 1e3), 1),
               "tflops_per_gpu": round(tf128, 1),
               "frac_of_bf16_peak": round(tf128 / peaks["bf16_tflops"], 4),
-              "frac_of_bf16_peak_sustained": round(tf128 / peak, 4)}
+              "frac_of_bf16_peak_sustained": round(tf128 / peak_tf, 4)}
     del d_ids128, d_out128
 
     # ---- p50 latency of one c0 batch through the host-buffer ABI ----
@@ -361,9 +374,9 @@ def main():
             "e2e": {"value": round(world * nseq / (e2e_ms / 1e3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "ms_per_step": round(e2e_ms, 3)},
-            "roofline": {"kernel": top, "bound": "tensor", "achieved": round(achieved, 1),
-                         "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                         "peak_source": f"{peak_src} bf16_tflops_sustained",
+            "roofline": {"kernel": top, "bound": bound, "achieved": round(achieved, 1),
+                         "peak": peak, "unit": unit, "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_src} {peak_name}",
                          "traffic": traffic, "traffic_source": traffic_src,
                          "launches_per_step": tk["launches"] // args.steps,
                          "avg_launch_ms": round(per_launch_ms, 4),

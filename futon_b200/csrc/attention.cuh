@@ -62,6 +62,16 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
+// D = A·B (no accumulator input).
+__device__ __forceinline__ void mma_16816_z(float (&d)[4], const uint32_t (&a)[4],
+                                            const uint32_t (&b)[2]) {
+  const float z = 0.f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(z));
+}
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&p);
@@ -246,12 +256,7 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---------------------------------------------------------------------------
-// attn_heads_kernel: one CTA per 64-query tile of one sequence, looping over
-// every head. q, k, v arrive pre-rotated (RoPE is applied in the qkv GEMM
-// epilogue). Per (head, 64-key tile) step the CTA stages q (first step of a
-// head), k and v with cp.async into a two-slot ring, so the next step's
-// loads overlap this step's tensor-core work. cls_mode: CTA s computes only
-// query row 0 of sequence s (the CLS-pruned last layer) into row s of out.
+// cp.async staging (the int8 path's split-precision kernel).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
@@ -260,6 +265,10 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
 }
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait1() {
   asm volatile("cp.async.wait_group 1;" ::: "memory");
@@ -278,8 +287,35 @@ __device__ __forceinline__ void stage_async(__nv_bfloat16* dst, const __nv_bfloa
   }
 }
 
+// ---------------------------------------------------------------------------
+// attn_heads_kernel staging. Per (head, 64-key tile) step one thread loads
+// q (first tile of a head), k and v as 64 × HD tiles of the [T, 3h] qkv
+// buffer with TMA into a kAttnRing-slot shared-memory ring; each slot's
+// mbarrier completes when its bytes land, so the next step's loads overlap
+// this step's tensor-core work. Tiles are dense with the TMA swizzle whose
+// span is one row (64 B for HD 32, 128 B for HD 64), which keeps every
+// ldmatrix phase (8 rows × 16 B) free of bank conflicts.
+// ---------------------------------------------------------------------------
+constexpr int kAttnRing = 2;
+
 template <int HD>
-constexpr int attn_heads_smem_bytes() { return 6 * 64 * (HD + 8) * 2; }
+struct AttnSmem {
+  static constexpr int kRowBytes = HD * 2;
+  static constexpr int kTileBytes = 64 * kRowBytes;
+  static constexpr int kBarOffset = 3 * kAttnRing * kTileBytes;
+  static constexpr int kBytes = kBarOffset + 64 + 1024;  // + barriers + alignment slack
+};
+
+template <int HD>
+constexpr int attn_heads_smem_bytes() { return AttnSmem<HD>::kBytes; }
+
+// The swizzle's XOR term for a tile row: 16-byte chunk c of row r sits at
+// chunk c ^ attn_swz(r). Every fragment row used below is a lane-dependent
+// row plus a multiple of 8, which leaves the term unchanged.
+template <int HD>
+__device__ __forceinline__ int attn_swz(int r) {
+  return HD == 32 ? (r >> 1) & 3 : r & 7;
+}
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -294,6 +330,29 @@ __device__ __forceinline__ void mma_16816_f16(float (&d)[4], const uint32_t (&a)
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// D = A·B (+ D unless ZERO_C), f16 operands.
+template <bool ZERO_C>
+__device__ __forceinline__ void mma_16816_f16c(float (&d)[4], const uint32_t (&a)[4],
+                                               const uint32_t (&b)[2]) {
+  if constexpr (ZERO_C) {
+    const float z = 0.f;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(z));
+  } else {
+    mma_16816_f16(d, a, b);
+  }
+}
+
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // 2^lo, 2^hi as one f16x2 word (lo in the low half): the exponents are
@@ -313,23 +372,42 @@ __device__ __forceinline__ uint32_t ex2_f16x2(float lo, float hi) {
 // O += P V with P and V in f16. The softmax denominators come out of the
 // same MMAs: a ninth (fifth) B block of ones sums each row of P exactly as
 // it is multiplied. FIRST: the head's first key tile (no rescale of O).
+// Per-lane byte offsets of the ldmatrix rows inside a swizzled 64 × HD tile:
+// k_off[i] for key chunks 4i..4i+3 (x4: rows nb·8 + lane%8), v_off[i] for
+// value columns 16i..16i+15 (x4.trans: rows kc·16 + lane%16).
+template <int HD>
+struct AttnLane {
+  uint32_t k_off[HD / 32];
+  uint32_t v_off[HD / 16];
+  __device__ __forceinline__ explicit AttnLane(int lane) {
+    constexpr int RB = HD * 2;
+    const int kr = lane & 7, vr = lane & 15;
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i)
+      k_off[i] = kr * RB + ((((lane >> 3) + 4 * i) ^ attn_swz<HD>(kr)) << 4);
+#pragma unroll
+    for (int i = 0; i < HD / 16; ++i)
+      v_off[i] = vr * RB + ((((lane >> 4) + 2 * i) ^ attn_swz<HD>(vr)) << 4);
+  }
+};
+
 template <int HD, int NBLK, bool PARTIAL, bool FIRST>
-__device__ __forceinline__ void attn_step(const __nv_bfloat16* kS, const __half* vS,
-                                          int k_off, int v_off, int lane, int nkeys,
-                                          float scale_log2, const uint32_t (&qf)[HD / 16][4],
+__device__ __forceinline__ void attn_step(uint32_t kS, uint32_t vS, const AttnLane<HD>& al,
+                                          int lane, int nkeys, float scale_log2,
+                                          const uint32_t (&qf)[HD / 16][4],
                                           float (&o)[HD / 8][4], float (&m_run)[2],
                                           float (&lsum)[4]) {
-  constexpr int kLds = HD + 8;
+  constexpr int RB = HD * 2;
   float sc[NBLK][4];
 #pragma unroll
   for (int nb = 0; nb < NBLK; ++nb) {
-    sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
 #pragma unroll
     for (int kc = 0; kc < HD / 16; kc += 2) {
       uint32_t kf[4];
-      ldsm_x4(kf, smem_u32(&kS[nb * 8 * kLds + k_off + kc * 16]));
+      ldsm_x4(kf, kS + nb * 8 * RB + al.k_off[kc / 2]);
       const uint32_t k0[2] = {kf[0], kf[1]}, k1[2] = {kf[2], kf[3]};
-      mma_16816(sc[nb], qf[kc], k0);
+      if (kc == 0) mma_16816_z(sc[nb], qf[kc], k0);
+      else mma_16816(sc[nb], qf[kc], k0);
       mma_16816(sc[nb], qf[kc + 1], k1);
     }
   }
@@ -338,11 +416,11 @@ __device__ __forceinline__ void attn_step(const __nv_bfloat16* kS, const __half*
     if (key0 >= nkeys) { sc[NBLK - 1][0] = -INFINITY; sc[NBLK - 1][2] = -INFINITY; }
     if (key0 + 1 >= nkeys) { sc[NBLK - 1][1] = -INFINITY; sc[NBLK - 1][3] = -INFINITY; }
   }
-  float mx0 = -INFINITY, mx1 = -INFINITY;
+  float mx0 = fmaxf(sc[0][0], sc[0][1]), mx1 = fmaxf(sc[0][2], sc[0][3]);
 #pragma unroll
-  for (int nb = 0; nb < NBLK; ++nb) {
-    mx0 = fmaxf(mx0, fmaxf(sc[nb][0], sc[nb][1]));
-    mx1 = fmaxf(mx1, fmaxf(sc[nb][2], sc[nb][3]));
+  for (int nb = 1; nb < NBLK; ++nb) {
+    mx0 = fmax3(mx0, sc[nb][0], sc[nb][1]);
+    mx1 = fmax3(mx1, sc[nb][2], sc[nb][3]);
   }
   mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
   mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
@@ -351,9 +429,6 @@ __device__ __forceinline__ void attn_step(const __nv_bfloat16* kS, const __half*
   if constexpr (FIRST) {
     m_run[0] = mx0;
     m_run[1] = mx1;
-#pragma unroll
-    for (int nd = 0; nd < HD / 8; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
-    lsum[0] = lsum[1] = lsum[2] = lsum[3] = 0.f;
   } else {
     const float n0 = fmaxf(m_run[0], mx0), n1 = fmaxf(m_run[1], mx1);
     const float a0 = ex2_approx((m_run[0] - n0) * scale_log2);
@@ -393,33 +468,40 @@ __device__ __forceinline__ void attn_step(const __nv_bfloat16* kS, const __half*
     } else {
       pf[2] = pf[3] = 0u;
     }
+    // The head's first tile starts O and the sums from zero.
 #pragma unroll
     for (int nd = 0; nd < HD / 8; nd += 2) {
       uint32_t vf[4];
-      ldsm_x4_t(vf, smem_u32(&vS[kc * 16 * kLds + v_off + nd * 8]));
+      ldsm_x4_t(vf, vS + kc * 16 * RB + al.v_off[nd / 2]);
       const uint32_t v0[2] = {vf[0], vf[1]}, v1[2] = {vf[2], vf[3]};
-      mma_16816_f16(o[nd], pf, v0);
-      mma_16816_f16(o[nd + 1], pf, v1);
+      if (FIRST && kc == 0) {
+        mma_16816_f16c<true>(o[nd], pf, v0);
+        mma_16816_f16c<true>(o[nd + 1], pf, v1);
+      } else {
+        mma_16816_f16c<false>(o[nd], pf, v0);
+        mma_16816_f16c<false>(o[nd + 1], pf, v1);
+      }
     }
-    mma_16816_f16(lsum, pf, ones);
+    if (FIRST && kc == 0) mma_16816_f16c<true>(lsum, pf, ones);
+    else mma_16816_f16c<false>(lsum, pf, ones);
   }
 }
 
 template <int HD, bool FIRST>
-__device__ __forceinline__ void attn_step_dispatch(int nkeys, const __nv_bfloat16* kS,
-                                                   const __half* vS, int k_off, int v_off,
-                                                   int lane, float scale_log2,
+__device__ __forceinline__ void attn_step_dispatch(int nkeys, uint32_t kS, uint32_t vS,
+                                                   const AttnLane<HD>& al, int lane,
+                                                   float scale_log2,
                                                    const uint32_t (&qf)[HD / 16][4],
                                                    float (&o)[HD / 8][4], float (&m)[2],
                                                    float (&l)[4]) {
   const int nblk = (nkeys + 7) >> 3;
   const bool partial = (nkeys & 7) != 0;
-#define FUTON_STEP(NB)                                                                      \
-  case NB:                                                                                  \
-    if (partial)                                                                            \
-      attn_step<HD, NB, true, FIRST>(kS, vS, k_off, v_off, lane, nkeys, scale_log2, qf, o, m, l); \
-    else                                                                                    \
-      attn_step<HD, NB, false, FIRST>(kS, vS, k_off, v_off, lane, nkeys, scale_log2, qf, o, m, l); \
+#define FUTON_STEP(NB)                                                                 \
+  case NB:                                                                             \
+    if (partial)                                                                       \
+      attn_step<HD, NB, true, FIRST>(kS, vS, al, lane, nkeys, scale_log2, qf, o, m, l);  \
+    else                                                                               \
+      attn_step<HD, NB, false, FIRST>(kS, vS, al, lane, nkeys, scale_log2, qf, o, m, l); \
     break;
   switch (nblk) {
     FUTON_STEP(1) FUTON_STEP(2) FUTON_STEP(3) FUTON_STEP(4)
@@ -429,105 +511,111 @@ __device__ __forceinline__ void attn_step_dispatch(int nkeys, const __nv_bfloat1
 }
 
 // grid = ntiles (or nseq in cls_mode), block = 128 (4 warps × 16 query rows).
-// Work stops where a sequence ends: warps whose 16 query rows all lie past
-// the sequence idle, and a step multiplies only the 8-key blocks that hold
-// keys (most benchmark sequences are shorter than one 64 × 64 tile).
+// One CTA per 64-query tile of one sequence, looping over every head; q, k,
+// v arrive pre-rotated (RoPE runs in the qkv GEMM epilogue). Work stops where
+// a sequence ends: warps whose 16 query rows all lie past the sequence idle,
+// and a step multiplies only the 8-key blocks that hold keys (most benchmark
+// sequences are shorter than one 64 × 64 tile). Tile rows past the sequence
+// hold the next sequence's (finite) values or TMA's zero fill past T: their
+// keys are masked, their probabilities are 0 and their query rows are not
+// stored. cls_mode: CTA s computes only query row 0 of sequence s (the
+// CLS-pruned last layer) into row s of out. A load that does not land within
+// the wait limit sets *err (kDevTimeoutAttn) and the CTA stops.
 template <int HD, typename OutT>
 __global__ void __launch_bounds__(128, 4)
-    attn_heads_kernel(const __nv_bfloat16* __restrict__ qkv, int hidden, int num_heads,
+    attn_heads_kernel(const __grid_constant__ CUtensorMap tm_qkv, int hidden, int num_heads,
                       const int* __restrict__ cu_seqlens, const AttnTile* __restrict__ tiles,
-                      int cls_mode, float scale_log2, OutT* __restrict__ out, int ldo) {
-  constexpr int kLds = HD + 8, kTile = 64 * kLds;
-  constexpr int kChunks = HD / 8;                 // 16-byte chunks per row
-  constexpr int kPerThread = 64 * kChunks / 128;  // staged chunks per thread per matrix
-  extern __shared__ __align__(16) __nv_bfloat16 sm_heads[];
-  __nv_bfloat16* sQ = sm_heads;             // [2][kTile], slot = head parity
-  __nv_bfloat16* sK = sm_heads + 2 * kTile; // [2][kTile], slot = step parity
-  __nv_bfloat16* sV = sm_heads + 4 * kTile;
+                      int cls_mode, float scale_log2, OutT* __restrict__ out, int ldo,
+                      int* __restrict__ err) {
+  using SM = AttnSmem<HD>;
+  constexpr int RB = SM::kRowBytes, kTile = SM::kTileBytes;
+  extern __shared__ uint8_t sm_raw[];
+  const uint32_t sbase = (smem_u32(sm_raw) + 1023u) & ~1023u;
+  const uint32_t sQ = sbase;                              // slot = head % ring
+  const uint32_t sK = sbase + kAttnRing * kTile;          // slot = step % ring
+  const uint32_t sV = sbase + 2 * kAttnRing * kTile;
+  const uint32_t full = sbase + SM::kBarOffset;           // kAttnRing mbarriers
+  __shared__ int abort_flag;
 
   const AttnTile tile = cls_mode ? AttnTile{(int)blockIdx.x, 0} : tiles[blockIdx.x];
   const int s0 = cu_seqlens[tile.seq];
   const int L = cu_seqlens[tile.seq + 1] - s0;
   const int qlim = cls_mode ? 1 : L;  // query positions < qlim are real
-  const int ld = 3 * hidden;
-  const __nv_bfloat16* base = qkv + (size_t)s0 * ld;
   const int nkv = (L + 63) / 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool warp_active = tile.q0 + warp * 16 < qlim;
 
-  // This thread's staged (row, chunk) pairs: the same for every matrix/step.
-  int st_row[kPerThread], st_goff[kPerThread], st_soff[kPerThread];
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    tma_prefetch_desc(&tm_qkv);
 #pragma unroll
-  for (int i = 0; i < kPerThread; ++i) {
-    const int w = threadIdx.x + i * 128;
-    st_row[i] = w / kChunks;
-    st_goff[i] = st_row[i] * ld + (w % kChunks) * 8;
-    st_soff[i] = st_row[i] * kLds + (w % kChunks) * 8;
+    for (int i = 0; i < kAttnRing; ++i) mbar_init(full + 8 * i, 1);
+    fence_barrier_init();
   }
-  auto stage = [&](__nv_bfloat16* dst, const __nv_bfloat16* src, int r0, int lim) {
-    const __nv_bfloat16* g = src + (size_t)r0 * ld;
-#pragma unroll
-    for (int i = 0; i < kPerThread; ++i) {
-      const bool ok = r0 + st_row[i] < lim;
-      cp_async16(smem_u32(dst + st_soff[i]), ok ? g + st_goff[i] : src, ok);
-    }
-  };
+  __syncthreads();
 
-  // Next (head, key tile) to stage; one commit group per step (possibly empty).
+  // Next (head, key tile) to load (thread 0 only).
   int nh = 0, nj = 0, issued = 0;
   auto issue_next = [&]() {
-    if (nh < num_heads) {
-      const int slot = issued & 1;
-      if (nj == 0) stage(sQ + (nh & 1) * kTile, base + nh * HD, tile.q0, qlim);
-      stage(sK + slot * kTile, base + hidden + nh * HD, nj * 64, L);
-      stage(sV + slot * kTile, base + 2 * hidden + nh * HD, nj * 64, L);
-      if (++nj == nkv) { nj = 0; ++nh; }
-      ++issued;
-    }
-    cp_async_commit();
+    if (nh >= num_heads) return;
+    const int slot = issued % kAttnRing;
+    const uint32_t bar = full + 8 * slot;
+    mbar_arrive_expect_tx(bar, (nj == 0 ? 3 : 2) * kTile);
+    if (nj == 0) tma_load_2d(sQ + (nh % kAttnRing) * kTile, &tm_qkv, bar, nh * HD, s0 + tile.q0);
+    tma_load_2d(sK + slot * kTile, &tm_qkv, bar, hidden + nh * HD, s0 + nj * 64);
+    tma_load_2d(sV + slot * kTile, &tm_qkv, bar, 2 * hidden + nh * HD, s0 + nj * 64);
+    if (++nj == nkv) { nj = 0; ++nh; }
+    ++issued;
   };
 
-  // Per-thread ldmatrix offsets (elements).
-  const int q_off = (warp * 16 + (lane & 15)) * kLds + (lane >> 4) * 8;
-  const int k_off = (lane & 7) * kLds + (lane >> 3) * 8;    // x4: two 16-column chunks
-  const int v_off = (lane & 15) * kLds + (lane >> 4) * 8;   // x4.trans: two 8-column blocks
+  const AttnLane<HD> al(lane);
+  const int qr = warp * 16 + (lane & 15);
+  const uint32_t q_row = qr * RB, q_swz = attn_swz<HD>(qr), q_hi = lane >> 4;
 
   uint32_t qf[HD / 16][4];
   float o[HD / 8][4];
   float m_run[2], l_run[4];
-  issue_next();
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < kAttnRing - 1; ++i) issue_next();
+  }
   int step = 0;
   for (int head = 0; head < num_heads; ++head) {
     for (int j = 0; j < nkv; ++j, ++step) {
-      issue_next();
-      cp_async_wait1();
-      __syncthreads();
+      if (threadIdx.x == 0) issue_next();
+      const int slot = step % kAttnRing;
+      if (!mbar_wait_bounded(full + 8 * slot, (step / kAttnRing) & 1, err, kDevTimeoutAttn,
+                             &abort_flag))
+        return;
       if (warp_active) {
-        const __nv_bfloat16* kS = sK + (step & 1) * kTile;
+        const uint32_t kS = sK + slot * kTile;
         // V columns are stored as f16 by the qkv GEMM epilogue.
-        const __half* vS = reinterpret_cast<const __half*>(sV + (step & 1) * kTile);
+        const uint32_t vS = sV + slot * kTile;
         const int nkeys = min(64, L - j * 64);
         if (j == 0) {
-          const __nv_bfloat16* qS = sQ + (head & 1) * kTile;
+          const uint32_t qS = sQ + (head % kAttnRing) * kTile + q_row;
 #pragma unroll
-          for (int kc = 0; kc < HD / 16; ++kc) ldsm_x4(qf[kc], smem_u32(&qS[q_off + kc * 16]));
-          attn_step_dispatch<HD, true>(nkeys, kS, vS, k_off, v_off, lane, scale_log2, qf, o,
-                                       m_run, l_run);
+          for (int kc = 0; kc < HD / 16; ++kc)
+            ldsm_x4(qf[kc], qS + (((2 * kc + q_hi) ^ q_swz) << 4));
+          attn_step_dispatch<HD, true>(nkeys, kS, vS, al, lane, scale_log2, qf, o, m_run, l_run);
         } else {
-          attn_step_dispatch<HD, false>(nkeys, kS, vS, k_off, v_off, lane, scale_log2, qf, o,
-                                        m_run, l_run);
+          attn_step_dispatch<HD, false>(nkeys, kS, vS, al, lane, scale_log2, qf, o, m_run,
+                                        l_run);
         }
         if (j == nkv - 1) {
-          // Every column of the ones block holds the full row sum.
-          const float inv0 = 1.f / l_run[0], inv1 = 1.f / l_run[2];
+          // Every column of the ones block holds the full row sum; l ≥ 1
+          // (the row maximum contributes 2^0), so the approximate
+          // reciprocal (≤ 1 ulp) is safe.
+          const float inv0 = rcp_approx(l_run[0]), inv1 = rcp_approx(l_run[2]);
           const int qr0 = tile.q0 + warp * 16 + (lane >> 2), qr1 = qr0 + 8;
           const size_t orow0 = cls_mode ? (size_t)tile.seq : (size_t)(s0 + qr0);
-          const size_t orow1 = (size_t)(s0 + qr1);
+          OutT* const out0 = out + orow0 * ldo + (lane & 3) * 2;
+          OutT* const out1 = out + (size_t)(s0 + qr1) * ldo + (lane & 3) * 2;
 #pragma unroll
           for (int nd = 0; nd < HD / 8; ++nd) {
-            const int col = head * HD + nd * 8 + (lane & 3) * 2;
-            if (qr0 < qlim) store2<OutT>(out + orow0 * ldo + col, o[nd][0] * inv0, o[nd][1] * inv0);
-            if (qr1 < qlim) store2<OutT>(out + orow1 * ldo + col, o[nd][2] * inv1, o[nd][3] * inv1);
+            const int col = head * HD + nd * 8;
+            if (qr0 < qlim) store2<OutT>(out0 + col, o[nd][0] * inv0, o[nd][1] * inv0);
+            if (qr1 < qlim) store2<OutT>(out1 + col, o[nd][2] * inv1, o[nd][3] * inv1);
           }
         }
       }

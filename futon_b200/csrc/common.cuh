@@ -24,6 +24,7 @@ enum DeviceError : int {
   kDevTimeoutAccEmpty = 4,    // MMA warp waited too long for the epilogue
   kDevBadShape = 5,           // a kernel was launched with an unsupported shape
   kDevBadInput = 6,           // a token id outside [0, vocab) reached the device
+  kDevTimeoutAttn = 7,        // attention waited too long for a TMA stage
 };
 
 // Wall-clock limit for any single barrier wait (nanoseconds). A healthy

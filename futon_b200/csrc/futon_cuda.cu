@@ -112,6 +112,23 @@ bool make_output_map(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols,
   return r == CUDA_SUCCESS;
 }
 
+// The attention kernel's view of the [T, 3h] qkv buffer (bf16 q, k; f16 v):
+// 64-row × hd-column tiles with the swizzle spanning one tile row (64 B for
+// hd 32, 128 B for hd 64). Rows past T read as 0.
+bool make_qkv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, int hd) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)hd, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  hd == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // N tile for a GEMM with N output columns: the widest of 256/192/128 that
 // divides N, else 64 (partial last tile, masked in the epilogue).
 int pick_bn(int n) {
@@ -597,10 +614,15 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
     if (tc_hd) {
       const int grid = cls_only ? nseq : ntiles;
       if (grid == 0) return FUTON_OK;
+      // q, k, v tiles of one head: 64 rows × hd columns, swizzled over one row.
+      CUtensorMap tm;
+      if (!make_qkv_map(&tm, qkv, (uint64_t)T, (uint64_t)(3 * h), hd))
+        return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
       auto launch = [&](auto kern, int smem) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        kern<<<grid, 128, smem, st>>>(qkv, h, H, cu, tiles, cls_only ? 1 : 0, scale_log2, out, h);
+        kern<<<grid, 128, smem, st>>>(tm, h, H, cu, tiles, cls_only ? 1 : 0, scale_log2, out, h,
+                                      d.err_word);
         return cudaGetLastError();
       };
       CU_TRY(hd == 32 ? launch(attn_heads_kernel<32, OutT>, attn_heads_smem_bytes<32>())

@@ -97,13 +97,13 @@ template <> __device__ __forceinline__ void store32<float>(float* dst, const flo
   for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
+// f16 with saturation: values beyond ±65504 clamp instead of becoming inf,
+// so a probability of 0 times any stored value stays 0.
 __device__ __forceinline__ uint4 pack8_f16(const float* v) {
   uint32_t w[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    __half2 p = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-    w[j] = *reinterpret_cast<uint32_t*>(&p);
-  }
+  for (int j = 0; j < 4; ++j)
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(w[j]) : "f"(v[2 * j + 1]), "f"(v[2 * j]));
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
