@@ -1,0 +1,416 @@
+// attention_tc.cuh — variable-length self-attention on the 5th-generation
+// tensor cores (tcgen05), restating native/model.go:646-739 (attendHead,
+// softmaxScaled) for every head and sequence of a micro-batch at once.
+//
+// Work unit: a window of ≤ 128 query rows. Sequences of ≤ 128 tokens are
+// packed whole into windows, each at a 16-row-aligned offset of the window
+// (loaded as 16-row boxes); a window's keys are its own rows, masked so a
+// query sees only its own sequence. Because every sequence starts on a
+// 16-key boundary, the P·V MMAs (K = 16 keys each) group its keys exactly as
+// they would alone: a sequence's vector does not depend on what it is packed
+// with. Longer sequences get one window per 128 queries whose keys are the
+// whole sequence in 128-key blocks. One CTA takes one window and loops over
+// every head and key block ("unit" = head × key block):
+//
+//   warp 4 (one thread)  TMA: q, k, v tiles (128 rows × hd) of the unit into
+//                        a two-slot shared-memory ring
+//   warp 5 (one thread)  tcgen05.mma: S = Q·Kᵀ (bf16, M = 128, N = keys
+//                        rounded to 16) into TMEM; after the softmax, O += P·V
+//                        (f16, V read MN-major straight from its row-major
+//                        tile) and L += P·1 (row sums) into TMEM
+//   warps 0-3            softmax, one thread per query row (TMEM lane): two
+//                        passes over its S row (max, then exp2 in f16x2 of the
+//                        scaled, shifted scores), P (f16) into a 128-byte-
+//                        swizzled K-major shared tile; online-softmax
+//                        rescaling of O and L between key blocks; the
+//                        normalised O row of each head to global memory
+//
+// Probability precision matches the mma.sync kernel: exponents rounded to
+// f16 before ex2.approx.f16x2, P and V in f16, f32 accumulation.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "mathf32.cuh"
+
+namespace futon {
+
+// A sequence placed in a packed window: tokens [t0, t0 + len) at window
+// rows [row, row + len), row a multiple of 16.
+struct AttnSeg {
+  int t0, len, row;
+};
+
+// nseg = 0: query rows [q0, q0 + nq) of one long sequence whose keys are
+// [k0, k0 + nk) (micro-batch-local token indices), nq ≤ 128.
+// nseg > 0: segments [seg0, seg0 + nseg) packed into rows [0, nq), nq = nk =
+// the rows they occupy rounded to 16 (≤ 128).
+struct AttnWindow {
+  int q0, nq;
+  int k0, nk;
+  int seg0, nseg;
+};
+
+template <int HD>
+struct AttnTcCfg {
+  static constexpr int kRowBytes = HD * 2;
+  static constexpr int kTileBytes = 128 * kRowBytes;       // one q, k or v tile
+  static constexpr int kSlotBytes = 3 * kTileBytes;
+  static constexpr int kSlots = 2;
+  static constexpr int kPOffset = kSlots * kSlotBytes;     // multiple of 1024
+  static constexpr int kPBytes = 2 * 128 * 128;            // two 64-key regions, 128 B rows
+  static constexpr int kOnesOffset = kPOffset + kPBytes;
+  static constexpr int kOnesBytes = 16 * 128;              // B operand of the row sums
+  static constexpr int kBarOffset = kOnesOffset + kOnesBytes;
+  static constexpr int kBytes = kBarOffset + 128 + 1024;   // + barriers + alignment slack
+  static constexpr uint32_t kTmemCols = 256;
+  static constexpr uint32_t kColO = 128;                   // S: columns 0-127
+  static constexpr uint32_t kColL = 128 + HD;
+  static constexpr int kThreads = 192;
+};
+
+template <int HD>
+constexpr int attn_tc_smem_bytes() { return AttnTcCfg<HD>::kBytes; }
+
+// Descriptor of a tile of 128 rows × HD 16-bit values as TMA writes it with
+// the swizzle spanning one row (64 B for HD 32, 128 B for HD 64): 8-row
+// atoms stacked at 8 · row bytes. Used K-major for q and k and MN-major
+// (idesc bit 16) for v, whose one swizzle atom spans all HD columns.
+template <int HD>
+__device__ __forceinline__ uint64_t desc_rows(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1u << 16;                               // leading byte offset (unused)
+  d |= (uint64_t)((8u * HD * 2u) >> 4) << 32;            // stride byte offset: 8 rows
+  d |= (uint64_t)1u << 46;                               // version
+  d |= (uint64_t)(HD == 32 ? 4u : 2u) << 61;             // SWIZZLE_64B / SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  return r;
+}
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+// 2^lo, 2^hi as one f16x2 word (exponents rounded to f16 first).
+__device__ __forceinline__ uint32_t ex2_h2(float lo, float hi) {
+  uint32_t t, r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(t) : "f"(hi), "f"(lo));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(t));
+  return r;
+}
+
+// grid = number of windows, block = 192. qkv: [T, 3h] (bf16 q, k; f16 v)
+// read through tm_qkv (box hd × 128, long-sequence windows) and tm_qkv16
+// (box hd × 16, packed windows).
+template <int HD, typename OutT>
+__global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                   const __grid_constant__ CUtensorMap tm_qkv16, int hidden, int num_heads,
+                   const AttnWindow* __restrict__ windows, const AttnSeg* __restrict__ segs,
+                   float scale_log2, OutT* __restrict__ out, int ldo, int* __restrict__ err) {
+  using C = AttnTcCfg<HD>;
+  extern __shared__ uint8_t sm_raw[];
+  const uint32_t sbase = (smem_u32(sm_raw) + 1023u) & ~1023u;
+  const uint32_t sP = sbase + C::kPOffset;
+  const uint32_t sOnes = sbase + C::kOnesOffset;
+  const uint32_t bars = sbase + C::kBarOffset;
+  const uint32_t full_b = bars;            // [2] TMA → MMA
+  const uint32_t empty_b = bars + 16;      // [2] MMA → TMA
+  const uint32_t sfull_b = bars + 32;      // S ready (MMA → softmax)
+  const uint32_t sfree_b = bars + 40;      // S read (softmax → MMA)
+  const uint32_t pfull_b = bars + 48;      // P written, O corrected (softmax → MMA)
+  const uint32_t ofull_b = bars + 56;      // P·V done (MMA → softmax)
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const AttnWindow win = windows[blockIdx.x];
+  const int nkb = (win.nk + 127) / 128;    // key blocks per head
+  const int units = num_heads * nkb;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(full_b + 8 * i, 1);
+      mbar_init(empty_b + 8 * i, 1);
+    }
+    mbar_init(sfull_b, 1);
+    mbar_init(sfree_b, 4);
+    mbar_init(pfull_b, 4);
+    mbar_init(ofull_b, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_qkv16);
+  }
+  // The row-sum operand: 16 rows × 128 bytes of f16 ones (layout-independent).
+  for (int i = threadIdx.x; i < C::kOnesBytes / 16; i += blockDim.x)
+    st_shared_v4(sOnes + 16 * i, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+  fence_proxy_async_smem();
+  if (warp == 5) {
+    tmem_alloc(smem_u32(&tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      for (int u = 0; u < units; ++u) {
+        const int head = u / nkb, j = u % nkb, slot = u & 1;
+        if (u >= 2 && !mbar_wait_bounded(empty_b + 8 * slot, ((u >> 1) - 1) & 1, err,
+                                         kDevTimeoutAttn, &abort_flag))
+          break;
+        const uint32_t fb = full_b + 8 * slot;
+        const uint32_t dst = sbase + slot * C::kSlotBytes;
+        const int xq = head * HD, xk = hidden + head * HD, xv = 2 * hidden + head * HD;
+        if (win.nseg == 0) {
+          mbar_arrive_expect_tx(fb, C::kSlotBytes);
+          tma_load_2d(dst, &tm_qkv, fb, xq, win.q0);
+          tma_load_2d(dst + C::kTileBytes, &tm_qkv, fb, xk, win.k0 + 128 * j);
+          tma_load_2d(dst + 2 * C::kTileBytes, &tm_qkv, fb, xv, win.k0 + 128 * j);
+        } else {
+          // Rows [0, nq) in 16-row boxes, each segment from its own tokens.
+          mbar_arrive_expect_tx(fb, 3 * win.nq * C::kRowBytes);
+          for (int sg = 0; sg < win.nseg; ++sg) {
+            const AttnSeg sq = segs[win.seg0 + sg];
+            for (int m = 0; m < sq.len; m += 16) {
+              const uint32_t o = (uint32_t)(sq.row + m) * C::kRowBytes;
+              tma_load_2d(dst + o, &tm_qkv16, fb, xq, sq.t0 + m);
+              tma_load_2d(dst + C::kTileBytes + o, &tm_qkv16, fb, xk, sq.t0 + m);
+              tma_load_2d(dst + 2 * C::kTileBytes + o, &tm_qkv16, fb, xv, sq.t0 + m);
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      auto keys16 = [&](int j) { return (min(128, win.nk - 128 * j) + 15) & ~15; };
+      auto issue_s = [&](int u) -> bool {
+        const int slot = u & 1;
+        if (!mbar_wait_bounded(full_b + 8 * slot, (u >> 1) & 1, err, kDevTimeoutAttn, &abort_flag))
+          return false;
+        tc_fence_after();
+        const uint32_t q = sbase + slot * C::kSlotBytes, k = q + C::kTileBytes;
+        const uint32_t n = (uint32_t)keys16(u % nkb);
+        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (8u << 24);
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks)
+          mma_bf16(tmem, desc_rows<HD>(q) + 2 * ks, desc_rows<HD>(k) + 2 * ks, idesc,
+                   ks ? 1u : 0u);
+        mma_commit(sfull_b);
+        return true;
+      };
+      constexpr uint32_t idesc_pv = (1u << 4) | (1u << 16) | ((uint32_t)(HD >> 3) << 17) | (8u << 24);
+      constexpr uint32_t idesc_l = (1u << 4) | (2u << 17) | (8u << 24);
+      bool ok = units > 0 && issue_s(0);
+      for (int u = 0; ok && u < units; ++u) {
+        // S(u + 1) as soon as the softmax has read S(u).
+        if (!mbar_wait_bounded(sfree_b, u & 1, err, kDevTimeoutAttn, &abort_flag)) break;
+        if (u + 1 < units && !issue_s(u + 1)) break;
+        if (!mbar_wait_bounded(pfull_b, u & 1, err, kDevTimeoutAttn, &abort_flag)) break;
+        tc_fence_after();
+        const int j = u % nkb, slot = u & 1;
+        const uint32_t v = sbase + slot * C::kSlotBytes + 2 * C::kTileBytes;
+        const int nks = keys16(j) / 16;
+        for (int ks = 0; ks < nks; ++ks) {
+          const uint64_t pd = smem_desc_k_sw128(sP + (ks >> 2) * 16384) + 2 * (ks & 3);
+          const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+          mma_bf16(tmem + C::kColO, pd, desc_rows<HD>(v + ks * 16 * C::kRowBytes), idesc_pv, acc);
+          mma_bf16(tmem + C::kColL, pd, smem_desc_k_sw128(sOnes) + 2 * (ks & 3), idesc_l, acc);
+        }
+        mma_commit(ofull_b);
+        mma_commit(empty_b + 8 * slot);
+      }
+    }
+  } else {
+    // ---------------- softmax warps 0-3: thread = query row ----------------
+    const int r = warp * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    // This row's token (−1: padding) and its valid key rows [klo, khi):
+    // relative to the window for packed windows, to the sequence start for
+    // long ones.
+    int tok = -1, klo = 0, khi = 0;
+    if (win.nseg == 0) {
+      if (r < win.nq) {
+        tok = win.q0 + r;
+        khi = win.nk;
+      }
+    } else {
+      for (int sg = 0; sg < win.nseg; ++sg) {
+        const AttnSeg sq = segs[win.seg0 + sg];
+        if (r >= sq.row && r < sq.row + sq.len) {
+          tok = sq.t0 + (r - sq.row);
+          klo = sq.row;
+          khi = sq.row + sq.len;
+        }
+      }
+    }
+    const uint32_t prow = sP + (uint32_t)r * 128u;
+    const int swz = r & 7;
+    float m_run = -INFINITY;
+    bool ok = true;
+
+    // Normalised O row of `head` to global memory (rows inside the window).
+    auto store_head = [&](int head) {
+      uint32_t ov[HD];
+#pragma unroll
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t t[32];
+        tmem_ld32(trow + C::kColO + c, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ov[c + i] = t[i];
+      }
+      const float l = __uint_as_float(tmem_ld1(trow + C::kColL));
+      tmem_ld_wait();
+      if (tok >= 0) {
+        const float inv = rcp_approx(l);  // l ≥ 1: the row maximum contributes 2^0
+        OutT* dst = out + (size_t)tok * ldo + head * HD;
+        float y[32];
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) y[i] = __uint_as_float(ov[c + i]) * inv;
+          store32<OutT>(dst + c, y);
+        }
+      }
+    };
+
+    for (int u = 0; u < units && ok; ++u) {
+      const int head = u / nkb, j = u % nkb;
+      if (j == 0) m_run = -INFINITY;  // a new head
+      const int nkeys = min(128, win.nk - 128 * j);
+      const int nchunk = (((nkeys + 15) & ~15) + 31) / 32;  // 32-key chunks the MMA reads
+      // Valid keys of this row in the block: [lo, hi).
+      const int lo = max(klo - 128 * j, 0), hi = min(khi - 128 * j, nkeys);
+      const bool any = tok >= 0 && hi > lo;
+      // Chunks any row of the warp needs; the rest of [0, nchunk) is zero.
+      int clo = any ? lo >> 5 : 4, chi = any ? (hi + 31) >> 5 : 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        clo = min(clo, __shfl_xor_sync(0xffffffffu, clo, o));
+        chi = max(chi, __shfl_xor_sync(0xffffffffu, chi, o));
+      }
+      if (!mbar_wait_bounded(sfull_b, u & 1, err, kDevTimeoutAttn, &abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      // Pass 1: the row maximum over valid keys.
+      float mx = -INFINITY;
+      for (int c = clo; c < chi; ++c) {
+        uint32_t t[32];
+        tmem_ld32(trow + 32 * c, t);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = 32 * c + i;
+          if (key >= lo && key < hi) mx = fmaxf(mx, __uint_as_float(t[i]));
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;  // rows without keys: P = 0
+      const float alpha = ex2_approx((m_run == -INFINITY ? m_use : m_run) * scale_log2 -
+                                     m_use * scale_log2);
+      m_run = m_new;
+      // Pass 2: P = 2^(s·c − m·c) in f16 (0 for masked keys), kept in registers
+      // until the previous unit's P·V has released the P tile.
+      uint32_t pw[4][16];
+      const float ms = m_use * scale_log2;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c >= clo && c < chi) {
+          uint32_t t[32];
+          tmem_ld32(trow + 32 * c, t);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int k0 = 32 * c + 2 * i;
+            const float a = (k0 >= lo && k0 < hi) ? fmaf(__uint_as_float(t[2 * i]), scale_log2, -ms)
+                                                 : -INFINITY;
+            const float b = (k0 + 1 >= lo && k0 + 1 < hi)
+                                ? fmaf(__uint_as_float(t[2 * i + 1]), scale_log2, -ms)
+                                : -INFINITY;
+            pw[c][i] = ex2_h2(a, b);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sfree_b);
+      if (u > 0) {
+        // The previous unit's P·V has finished: P may be overwritten, and O
+        // holds either a finished head (store it) or this head's running sum.
+        if (!mbar_wait_bounded(ofull_b, (u - 1) & 1, err, kDevTimeoutAttn, &abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        if (j == 0) {
+          store_head(head - 1);
+        } else if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t t[32];
+            tmem_ld32(trow + C::kColO + c, t);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
+            tmem_st32(trow + C::kColO + c, t);
+          }
+          const float l = __uint_as_float(tmem_ld1(trow + C::kColL));
+          tmem_ld_wait();
+          tmem_st1(trow + C::kColL, __float_as_uint(l * alpha));
+          tmem_st_wait();
+        }
+      }
+      // P row → the 128-byte-swizzled K-major tile (keys 0-63 | 64-127).
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c < nchunk) {
+          const uint32_t base = prow + (uint32_t)(c >> 1) * 16384u;
+          const bool live = c >= clo && c < chi;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t addr = base + (uint32_t)((((c & 1) * 4 + i) ^ swz) << 4);
+            if (live)
+              st_shared_v4(addr, pw[c][4 * i], pw[c][4 * i + 1], pw[c][4 * i + 2], pw[c][4 * i + 3]);
+            else
+              st_shared_v4(addr, 0u, 0u, 0u, 0u);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pfull_b);
+    }
+    if (ok && units > 0 &&
+        mbar_wait_bounded(ofull_b, (units - 1) & 1, err, kDevTimeoutAttn, &abort_flag)) {
+      tc_fence_after();
+      store_head(num_heads - 1);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+}  // namespace futon

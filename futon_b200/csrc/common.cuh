@@ -25,6 +25,7 @@ enum DeviceError : int {
   kDevBadShape = 5,           // a kernel was launched with an unsupported shape
   kDevBadInput = 6,           // a token id outside [0, vocab) reached the device
   kDevTimeoutAttn = 7,        // attention waited too long for a TMA stage
+  kDevTimeoutLnPeer = 8,      // LayerNorm epilogue waited too long for a peer CTA's sums
 };
 
 // Wall-clock limit for any single barrier wait (nanoseconds). A healthy
@@ -92,6 +93,72 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
       }
     }
   }
+}
+
+// ----------------------------------------------------------------------------
+// Thread-block clusters: distributed shared memory and remote mbarriers
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of `saddr` (a shared::cta address of this CTA)
+// in the CTA with cluster rank `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void st_cluster_f64x2(uint32_t caddr, double a, double b) {
+  asm volatile("st.shared::cluster.v2.f64 [%0], {%1, %2};" ::"r"(caddr), "d"(a), "d"(b)
+               : "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster, releasing this
+// thread's earlier writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait_bounded for phases completed by other CTAs of the cluster.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint32_t bar, uint32_t parity, int* err,
+                                                          int code, volatile int* abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicCAS(err, 0, code);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Every thread of every CTA of the cluster; orders earlier shared-memory
+// initialisation (mbarrier.init) before any remote access.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
 }
 
 // ----------------------------------------------------------------------------

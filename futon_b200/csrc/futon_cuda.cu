@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "common.cuh"
 #include "gemm_launch.cuh"
 #include "rowops.cuh"
@@ -112,15 +113,16 @@ bool make_output_map(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols,
   return r == CUDA_SUCCESS;
 }
 
-// The attention kernel's view of the [T, 3h] qkv buffer (bf16 q, k; f16 v):
-// 64-row × hd-column tiles with the swizzle spanning one tile row (64 B for
-// hd 32, 128 B for hd 64). Rows past T read as 0.
-bool make_qkv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, int hd) {
+// The attention kernels' view of the [T, 3h] qkv buffer (bf16 q, k; f16 v):
+// box_rows × hd tiles with the swizzle spanning one tile row (64 B for hd 32,
+// 128 B for hd 64). Rows past T read as 0.
+bool make_qkv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, int hd,
+                  uint32_t box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {cols * 2};
-  cuuint32_t box[2] = {(cuuint32_t)hd, 64};
+  cuuint32_t box[2] = {(cuuint32_t)hd, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -231,7 +233,9 @@ struct DevCtx {
 struct futon_model {
   futon_cfg cfg;
   int q8 = 0;
-  bool fuse_ln = false;  // residual + LayerNorm fused into the out/fc2 GEMMs (hidden == 384)
+  // Residual + LayerNorm fused into the out/fc2 GEMMs: hidden = 192·P with
+  // 2 ≤ P ≤ 4 (P CTAs of a cluster share each row tile).
+  bool fuse_ln = false;
   int head_dim = 0;
   int eff_max = 0;
   int swiglu_half = 0;
@@ -381,8 +385,10 @@ int upload_f32(DevCtx& d, float** dst, const float* src, size_t count, char* err
 
 // Uploads a GEMM weight (optionally two interleaved halves for SwiGLU) as
 // bf16 or int8 + per-row scales, builds its bias and its TMA descriptor.
+// ln_slices: the GEMM feeds the fused LayerNorm epilogue, which splits each
+// row into 192-column slices held by the CTAs of one cluster.
 int upload_gemm(DevCtx& d, GemmWeight& g, const float* w1, const float* b1, const float* w2,
-                const float* b2, int n1, int k, int half, bool q8, bool full_row, float* staging,
+                const float* b2, int n1, int k, int half, bool q8, bool ln_slices, float* staging,
                 char* err, size_t errlen) {
   const int n = w2 ? 2 * n1 : n1;
   g.n = n;
@@ -427,7 +433,7 @@ int upload_gemm(DevCtx& d, GemmWeight& g, const float* w1, const float* b1, cons
     }
     if ((rc = upload_f32(d, &g.bias, hb.data(), (size_t)n, err, errlen))) return rc;
   }
-  g.bn = w2 ? 2 * half : (full_row ? n : pick_bn(n));
+  g.bn = w2 ? 2 * half : (ln_slices ? 192 : pick_bn(n));
   const uint32_t box = g.bn <= 256 ? (uint32_t)g.bn : (uint32_t)g.bn / 2;
   if (!make_operand_map(&g.map, g.w, q8, (uint64_t)n, (uint64_t)k, box))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed for a weight");
@@ -551,10 +557,15 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
     if (!make_output_map(&to, o.out, (uint64_t)M, ncols, (uint64_t)o.ldo))
       return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (output)");
   }
+  CUtensorMap tr;
+  if (o.epi == kEpiResidLN &&
+      !make_operand_map(&tr, o.resid, false, (uint64_t)M, (uint64_t)w.n, 128))
+    return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (residual)");
   GemmLaunch g;
   g.ta = &ta;
   g.tw = &w.map;
   g.to = bf16_out ? &to : nullptr;
+  g.tr = o.epi == kEpiResidLN ? &tr : nullptr;
   g.M = M;
   g.N = w.n;
   g.K = w.k;
@@ -597,26 +608,63 @@ inline int grid_rows(int rows, int per_block, int sms) {
 }
 
 // ---- attention dispatch --------------------------------------------------
+// attn_tc_kernel (tcgen05, packed 128-row windows) is parity-correct but, as
+// measured on the c4 workload, 1.9× slower than attn_heads_kernel: each CTA
+// runs its heads' S → softmax → P·V chain one unit at a time and the SM sits
+// on the latencies. It stays off until that chain is pipelined.
+constexpr bool kAttnTcgen05 = false;
+
+// A micro-batch's attention work lists (device memory): 64-query tiles per
+// sequence and ≤ 128-row windows of packed sequences.
+struct AttnPlan {
+  const AttnTile* tiles;
+  int ntiles;
+  const AttnWindow* wins;
+  int nwin;
+  const AttnSeg* segs;
+};
+
 // q and k arrive already rotated (RoPE runs in the qkv GEMM epilogue).
-// Float path: bf16 qkv, attn_heads_kernel (all heads per CTA) for regular
-// and CLS-only layers. Int8 path: f32 qkv and split-precision attention, so
-// the per-row quantisation that follows sees float32-accurate values.
+// Float path: bf16 qkv, attn_heads_kernel (one CTA per 64-query tile, or per
+// sequence for the CLS-only last layer). Int8 path: f32 qkv and split-precision attention,
+// so the per-row quantisation that follows sees float32-accurate values.
 // Head dims other than 32/64 use the per-query kernel.
 template <typename InT, typename OutT>
 int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* cu,
-                  const AttnTile* tiles, int ntiles, bool cls_only, const InT* qkv, OutT* out,
+                  const AttnPlan& plan, bool cls_only, const InT* qkv, OutT* out,
                   cudaStream_t st, char* err, size_t errlen) {
   const int h = m.cfg.hidden_size, H = m.cfg.num_heads, hd = m.head_dim;
   const float scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
   constexpr bool kSplit = sizeof(InT) == 4;
   const bool tc_hd = hd == 32 || hd == 64;
+  const AttnTile* tiles = plan.tiles;
+  const int ntiles = plan.ntiles;
   if constexpr (!kSplit) {
+    if (kAttnTcgen05 && tc_hd && !cls_only) {
+      if (plan.nwin == 0) return FUTON_OK;
+      // q, k, v tiles of one head: 128 rows × hd columns, swizzled over one row.
+      CUtensorMap tm, tm16;
+      if (!make_qkv_map(&tm, qkv, (uint64_t)T, (uint64_t)(3 * h), hd, 128) ||
+          !make_qkv_map(&tm16, qkv, (uint64_t)T, (uint64_t)(3 * h), hd, 16))
+        return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
+      auto launch = [&](auto kern, int smem) -> cudaError_t {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        kern<<<plan.nwin, 192, smem, st>>>(tm, tm16, h, H, plan.wins, plan.segs, scale_log2, out,
+                                           h, d.err_word);
+        return cudaGetLastError();
+      };
+      CU_TRY(hd == 32 ? launch(attn_tc_kernel<32, OutT>, attn_tc_smem_bytes<32>())
+                      : launch(attn_tc_kernel<64, OutT>, attn_tc_smem_bytes<64>()));
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+      return FUTON_OK;
+    }
     if (tc_hd) {
       const int grid = cls_only ? nseq : ntiles;
       if (grid == 0) return FUTON_OK;
       // q, k, v tiles of one head: 64 rows × hd columns, swizzled over one row.
       CUtensorMap tm;
-      if (!make_qkv_map(&tm, qkv, (uint64_t)T, (uint64_t)(3 * h), hd))
+      if (!make_qkv_map(&tm, qkv, (uint64_t)T, (uint64_t)(3 * h), hd, 64))
         return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
       auto launch = [&](auto kern, int smem) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -671,7 +719,7 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
 // ids: device [T]; cu: device [nseq+1] (local offsets); tiles: device.
 // sum_l2 = Σ L² over the micro-batch's sequences (attention work, profiler only).
 int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, int nseq, int T,
-               double sum_l2, const AttnTile* tiles, int ntiles, int out_dim, float* out,
+               double sum_l2, const AttnPlan& plan, int out_dim, float* out,
                cudaStream_t st, volatile const int* cancel, char* err, size_t errlen) {
   const futon_cfg& c = m.cfg;
   const int h = c.hidden_size, I = c.intermediate_size;
@@ -728,10 +776,10 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       const double by = (double)T * 3.0 * h * esz + (double)rows * h * esz;
       ProfScope prof(d, st, last_cls ? kStAttnCls : kStAttn, fl, by);
       if (q8)
-        rc = run_attention<float, float>(m, d, T, nseq, cu, tiles, ntiles, last_cls,
+        rc = run_attention<float, float>(m, d, T, nseq, cu, plan, last_cls,
                                          (const float*)w.qkv, (float*)w.attn, st, err, errlen);
       else
-        rc = run_attention<bf16, bf16>(m, d, T, nseq, cu, tiles, ntiles, last_cls,
+        rc = run_attention<bf16, bf16>(m, d, T, nseq, cu, plan, last_cls,
                                        (const bf16*)w.qkv, (bf16*)w.attn, st, err, errlen);
       if (rc) return rc;
     }
@@ -845,10 +893,49 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
 struct MicroBatch {
   int s0, s1;   // sequences [s0, s1)
   int t0, t1;   // tokens [t0, t1)
-  size_t cu_off, tile_off;  // int offsets into the meta buffer
-  int ntiles;
+  size_t cu_off, tile_off, win_off, seg_off;  // int offsets into the meta buffer
+  int ntiles, nwin, nseg;
   double sum_l2;            // Σ L² (profiler)
 };
+
+// Attention windows of sequences [s0, s1) (token offsets relative to t0):
+// sequences of ≤ 128 tokens are packed whole, in order, into windows, each
+// at the next 16-row boundary, while the rows fit in 128; a longer sequence
+// gets one window per 128 queries, keyed by the whole sequence. Writes
+// `wins` / `segs` when given; returns the window count and adds the segment
+// count to *nsegs.
+int plan_windows(const int32_t* cu, int s0, int s1, int t0, AttnWindow* wins, AttnSeg* segs,
+                 int* nsegs) {
+  int n = 0, ns = 0;
+  int open = -1;  // window still accepting short sequences
+  int used = 0;   // its rows
+  for (int s = s0; s < s1; ++s) {
+    const int a = cu[s] - t0, L = cu[s + 1] - cu[s];
+    if (L <= 128) {
+      const int pad = (L + 15) & ~15;
+      if (open < 0 || used + pad > 128) {
+        if (wins) wins[n] = AttnWindow{0, 0, 0, 0, ns, 0};
+        open = n++;
+        used = 0;
+      }
+      if (segs) segs[ns] = AttnSeg{a, L, used};
+      ++ns;
+      used += pad;
+      if (wins) {
+        wins[open].nq = wins[open].nk = used;
+        wins[open].nseg += 1;
+      }
+    } else {
+      open = -1;
+      for (int q = a; q < a + L; q += 128) {
+        if (wins) wins[n] = AttnWindow{q, std::min(128, a + L - q), a, L, 0, 0};
+        ++n;
+      }
+    }
+  }
+  *nsegs += ns;
+  return n;
+}
 
 int validate_input(const futon_model& m, const int32_t* cu, int nseq, int out_dim, char* err,
                    size_t errlen) {
@@ -905,10 +992,16 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, std::vector<MicroBat
     mb.s1 = s;
     mb.t1 = cu[s];
     mb.ntiles = ntiles;
+    mb.nseg = 0;
+    mb.nwin = plan_windows(cu, mb.s0, mb.s1, mb.t0, nullptr, nullptr, &mb.nseg);
     mb.cu_off = meta;
     meta += align_up((size_t)(mb.s1 - mb.s0 + 1), 4);
     mb.tile_off = meta;
     meta += align_up((size_t)ntiles * 2, 4);
+    mb.win_off = meta;
+    meta += align_up((size_t)mb.nwin * 6, 4);
+    mb.seg_off = meta;
+    meta += align_up((size_t)mb.nseg * 3, 4);
     mbs.push_back(mb);
   }
   if (mbs.empty()) return FUTON_OK;
@@ -924,6 +1017,9 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, std::vector<MicroBat
     int k = 0;
     for (int s = mb.s0; s < mb.s1; ++s)
       for (int q0 = 0; q0 < cu[s + 1] - cu[s]; q0 += 64) ht[k++] = AttnTile{s - mb.s0, q0};
+    int nseg = 0;
+    plan_windows(cu, mb.s0, mb.s1, mb.t0, reinterpret_cast<AttnWindow*>(d.h_meta + mb.win_off),
+                 reinterpret_cast<AttnSeg*>(d.h_meta + mb.seg_off), &nseg);
   }
   CU_TRY(cudaMemcpyAsync(d.d_meta, d.h_meta, meta * sizeof(int), cudaMemcpyHostToDevice, st));
   CU_TRY(cudaEventRecord(d.meta_evt, st));
@@ -943,9 +1039,12 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
   for (const MicroBatch& mb : mbs) {
     if (cancel && *cancel)
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
+    const AttnPlan plan{reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
+                        reinterpret_cast<const AttnWindow*>(d.d_meta + mb.win_off), mb.nwin,
+                        reinterpret_cast<const AttnSeg*>(d.d_meta + mb.seg_off)};
     if ((rc = forward_mb(m, d, d_ids + mb.t0, d.d_meta + mb.cu_off, mb.s1 - mb.s0, mb.t1 - mb.t0,
-                         mb.sum_l2, reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
-                         out_dim, d_out + (size_t)mb.s0 * dim, st, cancel, err, errlen)))
+                         mb.sum_l2, plan, out_dim, d_out + (size_t)mb.s0 * dim, st, cancel, err,
+                         errlen)))
       return rc;
   }
   return FUTON_OK;
@@ -1048,6 +1147,7 @@ int seam_gemm(SeamCtx& s, const void* A, bool s8, const float* a_scale, int m, c
   g.ta = &ta;
   g.tw = &tw;
   g.to = nullptr;
+  g.tr = nullptr;
   g.M = m;
   g.N = n;
   g.K = k;
@@ -1203,7 +1303,7 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
   model->head_dim = hd;
   model->eff_max = effective_max(c);
   model->swiglu_half = half;
-  model->fuse_ln = !q8 && h == 384;
+  model->fuse_ln = !q8 && h % 192 == 0 && h / 192 >= 2 && h / 192 <= kLnPeerSlots;
 
   // RoPE tables (precomputeRoPE, model.go:306-318): f64 angles, f32 storage.
   std::vector<float> rc_tab, rs_tab;
@@ -1545,6 +1645,7 @@ extern "C" int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const
   g.ta = &ta;
   g.tw = &tw;
   g.to = nullptr;
+  g.tr = nullptr;
   g.M = m;
   g.N = n;
   g.K = k;

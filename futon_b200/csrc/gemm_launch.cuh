@@ -11,6 +11,7 @@ struct GemmLaunch {
   const CUtensorMap* ta;  // A [M, K] (bf16 or s8), box 128 × 128 bytes
   const CUtensorMap* tw;  // W [N, K], box bn × 128 bytes
   const CUtensorMap* to;  // bf16 output [M, ncols], box 32 × 32, 64B swizzle (TMA-store epilogues)
+  const CUtensorMap* tr;  // kEpiResidLN: bf16 residual [M, N], box 64 × 128, 128B swizzle
   int M, N, K;
   int bn;                 // 64, 128, 192 or 256
   int epi;                // EpiKind
@@ -27,7 +28,7 @@ cudaError_t launch_gemm_s8(const GemmLaunch& g);
 
 template <int BN, int EPI, bool S8, typename OutT>
 cudaError_t launch_gemm_inst(const GemmLaunch& g) {
-  using C = GemmCfg<BN, S8>;
+  using C = GemmCfg<BN, S8, EPI == kEpiResidLN>;
   auto kern = gemm_tc_kernel<BN, EPI, S8, OutT>;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -40,22 +41,50 @@ cudaError_t launch_gemm_inst(const GemmLaunch& g) {
   }
   constexpr bool kTmaStore = sizeof(OutT) == 2;
   if (kTmaStore && !g.to) return cudaErrorInvalidValue;  // bf16 outputs need an output map
-  const long tiles = (long)((g.M + C::kBM - 1) / C::kBM) * ((g.N + BN - 1) / BN);
-  if (tiles == 0) return cudaSuccess;
-  const int grid = (int)(tiles < g.num_sms ? tiles : g.num_sms);
-  kern<<<grid, C::kThreads, C::kSmemBytes, g.stream>>>(*g.ta, *g.tw, g.to ? *g.to : *g.ta, g.M,
-                                                       g.N, g.K, g.ep, g.err);
-  return cudaGetLastError();
+  const long num_m = (g.M + C::kBM - 1) / C::kBM;
+  if (num_m == 0) return cudaSuccess;
+  if constexpr (EPI == kEpiResidLN) {
+    // Clusters of N / BN CTAs, one per column slice of a row tile.
+    if (g.N % BN != 0 || g.N / BN < 2 || g.N / BN > kLnPeerSlots || !g.tr)
+      return cudaErrorInvalidValue;
+    const int peers = g.N / BN;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)peers;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = g.stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // Clusters that fit at once (per device and cluster size, queried once).
+    static std::atomic<int> fit_cache[64][kLnPeerSlots + 1];
+    int fit = fit_cache[dev & 63][peers].load();
+    if (fit == 0) {
+      cfg.gridDim = dim3((unsigned)(peers * (g.num_sms / peers)));
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&fit, kern, &cfg);
+      if (e != cudaSuccess) return e;
+      if (fit <= 0) return cudaErrorInvalidConfiguration;
+      fit_cache[dev & 63][peers].store(fit);
+    }
+    const int clusters = (int)(num_m < fit ? num_m : fit);
+    cfg.gridDim = dim3((unsigned)(clusters * peers));
+    return cudaLaunchKernelEx(&cfg, kern, *g.ta, *g.tw, *g.to, *g.tr, g.M, g.N, g.K, g.ep, g.err);
+  } else {
+    const long tiles = num_m * ((g.N + BN - 1) / BN);
+    const int grid = (int)(tiles < g.num_sms ? tiles : g.num_sms);
+    kern<<<grid, C::kThreads, C::kSmemBytes, g.stream>>>(*g.ta, *g.tw, g.to ? *g.to : *g.ta,
+                                                         *g.ta, g.M, g.N, g.K, g.ep, g.err);
+    return cudaGetLastError();
+  }
 }
 
 template <bool S8, int BN>
 cudaError_t launch_gemm_bn(const GemmLaunch& g) {
   using Bf = __nv_bfloat16;
-  if constexpr (BN == 384) {
-    // Full-row tiles exist for the fused residual + LayerNorm epilogue only.
-    if (!S8 && g.epi == kEpiResidLN && g.N == 384) return launch_gemm_inst<384, kEpiResidLN, false, Bf>(g);
-    return cudaErrorInvalidValue;
-  } else if constexpr (!S8) {
+  if constexpr (!S8) {
     switch (g.epi) {
       case kEpiStore:
         return g.out_f32 ? launch_gemm_inst<BN, kEpiStore, false, float>(g)
@@ -65,6 +94,9 @@ cudaError_t launch_gemm_bn(const GemmLaunch& g) {
         if constexpr (BN != 192) return launch_gemm_inst<BN, kEpiSwiglu, false, Bf>(g);
         else return cudaErrorInvalidValue;
       case kEpiResid: return launch_gemm_inst<BN, kEpiResid, false, float>(g);
+      case kEpiResidLN:
+        if constexpr (BN == 192) return launch_gemm_inst<BN, kEpiResidLN, false, Bf>(g);
+        else return cudaErrorInvalidValue;
     }
   } else {
     switch (g.epi) {
@@ -88,7 +120,6 @@ cudaError_t launch_gemm_any(const GemmLaunch& g) {
     case 128: return launch_gemm_bn<S8, 128>(g);
     case 192: return launch_gemm_bn<S8, 192>(g);
     case 256: return launch_gemm_bn<S8, 256>(g);
-    case 384: return launch_gemm_bn<S8, 384>(g);
   }
   return cudaErrorInvalidValue;
 }

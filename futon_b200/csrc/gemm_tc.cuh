@@ -65,7 +65,15 @@ struct EpiParams {
   int f16_from;  // TMA-store outputs at columns ≥ f16_from are written as f16 (qkv: V)
 };
 
-template <int BN, bool S8>
+// Peer slots per tile parity in the LayerNorm row-statistics exchange: at
+// most 4 CTAs (N ≤ 4 · 192 columns) share a row tile.
+constexpr int kLnPeerSlots = 4;
+
+// LNS: the fused residual + LayerNorm configuration (BN = 192 column slices
+// in clusters): three stages, the row-statistics exchange buffer and the
+// residual tile (TMA-loaded, 128 rows × BN bf16 as BN/64 swizzled 16 KB
+// sub-tiles) in shared memory.
+template <int BN, bool S8, bool LNS = false>
 struct GemmCfg {
   static constexpr int kBM = 128;
   static constexpr int kRowBytes = 128;                       // one swizzle row
@@ -73,20 +81,26 @@ struct GemmCfg {
   static constexpr int kABytes = kBM * kRowBytes;
   static constexpr int kBBytes = BN * kRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN == 384) ? 3 : (BN >= 192) ? 4 : (BN == 128) ? 5 : 7;
-  static constexpr int kMmaN = BN <= 256 ? BN : BN / 2;       // N of one tcgen05.mma (≤ 256)
-  static constexpr int kNSplit = BN / kMmaN;                  // MMAs per k-step
-  static constexpr int kNumAcc = BN <= 256 ? 2 : 1;           // TMEM accumulators
-  static constexpr uint32_t kAccStride = (BN <= 64) ? 64 : (BN <= 128) ? 128 : (BN <= 256) ? 256 : 512;
+  static constexpr int kStages = LNS ? 3 : (BN >= 192) ? 4 : (BN == 128) ? 5 : 7;
+  static constexpr int kMmaN = BN;                            // N of one tcgen05.mma (≤ 256)
+  static constexpr int kNumAcc = 2;                           // TMEM accumulators
+  static constexpr uint32_t kAccStride = (BN <= 64) ? 64 : (BN <= 128) ? 128 : 256;
   static constexpr uint32_t kTmemCols = kNumAcc * kAccStride; // power of two, ≤ 512
   static constexpr int kEpiWarps = 8;                         // two per TMEM lane quarter
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  // After the stage ring: barriers (256 B), then either the LayerNorm
-  // partial sums (2 × 128 double2) or the TMA-store staging (per epilogue
-  // warp two 32 × 64-byte buffers).
+  // After the stage ring: barriers (≤ 1 KB), then either the LayerNorm
+  // partial sums (2 × 128 double2) and one 2 KB staging buffer per epilogue
+  // warp, or the TMA-store staging (per epilogue warp two 32 × 64-byte
+  // buffers).
   static constexpr int kStagingBytes = kEpiWarps * 2 * 2048;
   static constexpr int kExtraOffset = kStages * kStageBytes + 1024;  // 1024-aligned
-  static constexpr int kSmemBytes = kExtraOffset + kStagingBytes + 1024 /*align*/;
+  static constexpr int kXchOffset = kExtraOffset + kStagingBytes;
+  static constexpr int kXchBytes = LNS ? 2 * kLnPeerSlots * 128 * 16 : 0;
+  static constexpr int kResidOffset = kXchOffset + kXchBytes;       // 1024-aligned
+  static constexpr int kResidBytes = LNS ? kBM * BN * 2 : 0;
+  static constexpr int kSmemBytes = kResidOffset + kResidBytes + 1024 /*align*/;
+  static_assert(BN <= 256, "one tcgen05.mma covers the tile's N");
+  static_assert(!LNS || BN % 64 == 0, "residual sub-tiles are 64 columns wide");
 };
 
 template <typename T> __device__ __forceinline__ void store32(T* dst, const float (&v)[32]);
@@ -454,116 +468,162 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
   }
 }
 
-// kEpiResidLN for one thread (= one row) and one column half (part): v =
-// (D + bias) + residual is written back over the accumulator, the row's
-// f64 Σv and Σv² are combined with the other half's through shared memory,
-// then y = (v − mean)·inv·γ + β goes out as bf16 (and f32 when asked), with
-// inv = float32(1/sqrt(var + eps)) as in layerNormRows (model.go:743-769).
-// Tiles span the whole row (N = BN), so the output may overwrite the
-// residual in place: a warp reads its residual columns before it stores
-// them (TMA tile stores of the warp's 32-row slab), and the two warps of a
-// lane quarter own disjoint column halves. The bf16 residual is read two
-// chunks ahead; the first two loads are issued before the accumulator is
-// ready (ln_prefetch), so they overlap the tile's MMAs.
-struct LnResid {
-  uint4 buf[2][4];  // two chunks of 32 bf16
+// Row-statistics exchange between the CTAs of a cluster that hold the column
+// slices of one row tile (peers = N / BN; 1 = no exchange).
+struct LnPeers {
+  int peers;
+  uint32_t rank;
+  uint32_t xbuf;     // shared::cta address of this CTA's [2][kLnPeerSlots][128] double2
+  uint32_t xfull;    // shared::cta address of this CTA's two exchange mbarriers
+  int* err;
+  volatile int* abort_flag;
 };
 
-template <int BN>
-__device__ __forceinline__ void ln_load_chunk(const EpiParams& ep, int row, bool row_ok, int col,
-                                              uint4 (&dst)[4]) {
-  if (row_ok) {
-    const uint4* rp = reinterpret_cast<const uint4*>(
-        reinterpret_cast<const __nv_bfloat16*>(ep.resid) + (size_t)row * ep.ldr + col);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dst[i] = rp[i];
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(0, 0, 0, 0);
-  }
-}
-
-template <int BN>
-__device__ __forceinline__ void ln_prefetch(const EpiParams& ep, int row, int M, int part,
-                                            LnResid& rs) {
-  const int c0 = part * (BN / 2);
-  ln_load_chunk<BN>(ep, row, row < M, c0, rs.buf[0]);
-  ln_load_chunk<BN>(ep, row, row < M, c0 + 32, rs.buf[1]);
-}
-
-template <int BN, typename Sink>
-__device__ __forceinline__ void epilogue_resid_ln(uint32_t taddr, int row, int row0, int M,
-                                                  int part, int quarter, int lane,
+// Fused residual + LayerNorm (model.go:743-769) over the BN-column slice
+// [n0, n0 + BN) of a row whose full length is N: v = acc + bias + resid (the
+// residual tile is already in shared memory) is written back to TMEM while
+// Σv and Σv² accumulate in f64; the two warps of a lane quarter (one per
+// column half) combine their sums through shared memory, the CTAs holding
+// the row's other slices add theirs through distributed shared memory (in
+// rank order, so every slice normalises with bit-identical statistics), then
+// y = (v − mean)·inv·γ + β leaves through the TMA sink. `rrow` is this row's
+// line in residual sub-tile 0 (128-byte swizzled rows); `resid_done` is
+// called once the residual has been read. Returns false if a peer's sums did
+// not arrive in time.
+template <int BN, typename Sink, typename Done>
+__device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int row0, int M, int N,
+                                                  int n0, int part, int quarter, int lane,
                                                   const EpiParams& ep, double2* red, Sink& sink,
-                                                  LnResid& rs) {
+                                                  uint32_t rrow, Done&& resid_done,
+                                                  const LnPeers& px, int it) {
   constexpr int kCols = BN / 2, kChunks = kCols / 32;
   const bool row_ok = row < M;
   const int c0 = part * kCols;
+  const int swz = lane & 7;  // row & 7 (rows of a quarter start at multiples of 32)
+  // Σv, Σv²: f32 over each 32-column chunk (paired lanes), then f64.
   double s1 = 0.0, s2 = 0.0;
 #pragma unroll
   for (int k = 0; k < kChunks; ++k) {
     const int c = c0 + 32 * k;
     uint32_t u[32];
     tmem_ld32(taddr + c, u);
-    float r[32], b[32];
+    const uint32_t sub = rrow + (uint32_t)(c / 64) * (128u * 128u);
+    const int cc0 = (c % 64) / 8;
+    uint32_t w[16];  // 32 residual bf16
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t w[4] = {rs.buf[k & 1][i].x, rs.buf[k & 1][i].y, rs.buf[k & 1][i].z,
-                             rs.buf[k & 1][i].w};
+    for (int i = 0; i < 4; ++i)
+      asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(w[4 * i]), "=r"(w[4 * i + 1]), "=r"(w[4 * i + 2]), "=r"(w[4 * i + 3])
+                   : "r"(sub + (uint32_t)(((cc0 + i) ^ swz) << 4)));
+    const float4* b4 = ep.bias ? reinterpret_cast<const float4*>(ep.bias + n0 + c) : nullptr;
+    tmem_ld_wait();
+    uint64_t a1 = 0, a2 = 0;  // (0.f, 0.f)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
-        r[8 * i + 2 * j] = f.x;
-        r[8 * i + 2 * j + 1] = f.y;
+    for (int q = 0; q < 8; ++q) {
+      const float4 bq = ep.bias ? b4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = 2 * q + h;
+        // bf16 pair → f32 pair: the low half moves up, the high half is masked.
+        const uint64_t r2 =
+            f2_pack(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+        uint64_t v2 = f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
+        v2 = f2_add(v2, h ? f2_pack(bq.z, bq.w) : f2_pack(bq.x, bq.y));
+        v2 = f2_add(v2, r2);
+        a1 = f2_add(a1, v2);
+        a2 = f2_fma(v2, v2, a2);
+        float x, y;
+        f2_unpack(v2, x, y);
+        u[2 * i] = __float_as_uint(x);
+        u[2 * i + 1] = __float_as_uint(y);
       }
     }
-    if (k + 2 < kChunks) ln_load_chunk<BN>(ep, row, row_ok, c + 64, rs.buf[k & 1]);
-    load_col32(ep.bias, c, BN, b);
-    tmem_ld_wait();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float v = __uint_as_float(u[i]);
-      if (ep.bias) v = fadd(v, b[i]);
-      v = fadd(v, r[i]);
-      u[i] = __float_as_uint(v);
-      s1 += (double)v;
-      s2 += (double)v * (double)v;
-    }
+    float p0, p1, q0, q1;
+    f2_unpack(a1, p0, p1);
+    f2_unpack(a2, q0, q1);
+    s1 += (double)p0 + (double)p1;
+    s2 += (double)q0 + (double)q1;
     tmem_st32(taddr + c, u);
   }
+  resid_done();
   tmem_st_wait();
   const int slot = quarter * 32 + lane;
   red[part * 128 + slot] = make_double2(s1, s2);
   named_bar_sync(1 + quarter, 64);
   const double2 o = red[(1 - part) * 128 + slot];
-  const double mean = (s1 + o.x) / (double)BN;
-  double var = (s2 + o.y) / (double)BN - mean * mean;
+  // This slice's sums, identical in both warps (two-term sums commute).
+  double t1 = s1 + o.x, t2 = s2 + o.y;
+  if (px.peers > 1) {
+    const uint32_t par = (uint32_t)(it & 1);
+    const uint32_t cell = px.xbuf + ((par * kLnPeerSlots + px.rank) * 128 + slot) * 16;
+    if (part == 0) {
+      for (int r = 0; r < px.peers; ++r) {
+        if (r == (int)px.rank) continue;
+        st_cluster_f64x2(mapa_shared(cell, r), t1, t2);
+        mbar_arrive_cluster(mapa_shared(px.xfull + 8 * par, r));
+      }
+    }
+    if (!mbar_wait_cluster_bounded(px.xfull + 8 * par, (uint32_t)(it >> 1) & 1u, px.err,
+                                   kDevTimeoutLnPeer, px.abort_flag))
+      return false;
+    double a1 = 0.0, a2 = 0.0;
+    const double2* xb = reinterpret_cast<const double2*>(__cvta_shared_to_generic(px.xbuf)) +
+                        (size_t)par * kLnPeerSlots * 128 + slot;
+    for (int r = 0; r < px.peers; ++r) {
+      const double2 q = r == (int)px.rank ? make_double2(t1, t2) : xb[r * 128];
+      a1 += q.x;
+      a2 += q.y;
+    }
+    t1 = a1;
+    t2 = a2;
+  }
+  const double mean = t1 / (double)N;
+  double var = t2 / (double)N - mean * mean;
   var = var > 0.0 ? var : 0.0;
   const float inv = (float)(1.0 / sqrt(var + (double)ep.eps));
   const float mf = (float)mean;
+  const uint64_t nm2 = f2_pack(-mf, -mf), inv2 = f2_pack(inv, inv);
 #pragma unroll 1
   for (int c = c0; c < c0 + kCols; c += 32) {
     uint32_t u[32];
     tmem_ld32(taddr + c, u);
-    float g[32], be[32];
-    load_col32(ep.ln_w, c, BN, g);
-    load_col32(ep.ln_b, c, BN, be);
+    const float4* g4 = reinterpret_cast<const float4*>(ep.ln_w + n0 + c);
+    const float4* e4 = reinterpret_cast<const float4*>(ep.ln_b + n0 + c);
     tmem_ld_wait();
     float y[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      y[i] = fadd(fmul(fmul(fsub(__uint_as_float(u[i]), mf), inv), g[i]), be[i]);
-    sink.put(y, c, row0);
-    if (row_ok && ep.out_f32) store32<float>(ep.out_f32 + (size_t)row * BN + c, y);
+    for (int q = 0; q < 8; ++q) {
+      const float4 gq = g4[q], eq = e4[q];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = 2 * q + h;
+        // ((v − mean)·inv)·γ + β, two columns per instruction.
+        uint64_t t =
+            f2_add(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])), nm2);
+        t = f2_mul(t, inv2);
+        t = f2_fma(t, h ? f2_pack(gq.z, gq.w) : f2_pack(gq.x, gq.y),
+                   h ? f2_pack(eq.z, eq.w) : f2_pack(eq.x, eq.y));
+        f2_unpack(t, y[2 * i], y[2 * i + 1]);
+      }
+    }
+    sink.put(y, n0 + c, row0);
+    if (row_ok && ep.out_f32) store32<float>(ep.out_f32 + (size_t)row * N + n0 + c, y);
   }
+  return true;
 }
 
 template <int BN, int EPI, bool S8, typename OutT>
 __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                   const __grid_constant__ CUtensorMap tmO, int M, int N, int K, EpiParams ep,
-                   int* err) {
-  using C = GemmCfg<BN, S8>;
+                   const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
+                   int M, int N, int K, EpiParams ep, int* err) {
+  // LayerNorm over rows wider than one tile: the grid is made of clusters of
+  // N / BN CTAs, CTA rank r of a cluster computes column slice r of every
+  // row tile the cluster takes, and the slices exchange row statistics. The
+  // producer loads each tile's residual slice (tmR) next to the operands.
+  constexpr bool kLnSlices = EPI == kEpiResidLN;
+  static_assert(!kLnSlices || (BN == 192 && !S8), "LayerNorm slices are 192 bf16 columns");
+  using C = GemmCfg<BN, S8, kLnSlices>;
   // bf16 outputs leave through TMA tile stores; f32 outputs store directly.
   constexpr bool kTmaStore = sizeof(OutT) == 2;
   extern __shared__ uint8_t smem_raw[];
@@ -576,6 +636,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   uint64_t* acce_bar = accf_bar + 2;               // [kNumAcc] epilogue → MMA
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* xfull_bar = acce_bar + 3;              // [2] peers → LayerNorm epilogue
+  uint64_t* rfull_bar = acce_bar + 5;              // residual tile: TMA → epilogue
+  uint64_t* rempty_bar = acce_bar + 6;             // residual tile: epilogue → TMA
   // Extra region: LayerNorm kernels keep 4 KB of partial sums, then one
   // 2 KB staging buffer per epilogue warp; other kernels two per warp.
   uint8_t* extra = smem + C::kExtraOffset;
@@ -586,7 +649,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   const int num_m = (M + C::kBM - 1) / C::kBM;
   const int num_n = (N + BN - 1) / BN;
   const int num_k = (K + C::kBK - 1) / C::kBK;
-  const int num_tiles = num_m * num_n;
+  // Tile loop: tiles first, first + stride, ... < num_tiles; tile → (mb, nb).
+  const int peers = kLnSlices ? num_n : 1;
+  const uint32_t rank = kLnSlices ? cluster_ctarank() : 0u;
+  const int num_tiles = kLnSlices ? num_m : num_m * num_n;
+  const int first = kLnSlices ? (int)blockIdx.x / peers : (int)blockIdx.x;
+  const int stride = kLnSlices ? (int)gridDim.x / peers : (int)gridDim.x;
+  auto tile_mb = [&](int t) { return kLnSlices ? t : t / num_n; };
+  auto tile_nb = [&](int t) { return kLnSlices ? (int)rank : t % num_n; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -596,6 +666,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&accf_bar[a]), 1);
       mbar_init(smem_u32(&acce_bar[a]), C::kEpiWarps);  // one arrive per epilogue warp
+      // One arrive per row from every other slice of the row tile.
+      if (kLnSlices) mbar_init(smem_u32(&xfull_bar[a]), (uint32_t)(128 * (peers - 1)));
+    }
+    if (kLnSlices) {
+      mbar_init(smem_u32(rfull_bar), 1);
+      mbar_init(smem_u32(rempty_bar), C::kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -604,13 +680,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
     if constexpr (kTmaStore) tma_prefetch_desc(&tmO);
+    if constexpr (kLnSlices) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kLnSlices) cluster_sync_all();  // peers' barriers exist before any remote arrive
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -619,9 +697,22 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
       // ---------------- TMA producer ----------------
       int stage = 0;
       uint32_t phase = 0;
-      int issued = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int mb = tile / num_n, nb = tile % num_n;
+      int issued = 0, rtiles = 0;
+      for (int tile = first; tile < num_tiles; tile += stride) {
+        const int mb = tile_mb(tile), nb = tile_nb(tile);
+        if constexpr (kLnSlices) {
+          // The residual slice of this tile, once the epilogue has read the last one.
+          if (!mbar_wait_bounded(smem_u32(rempty_bar), ((uint32_t)rtiles & 1u) ^ 1u, err,
+                                 kDevTimeoutSmemEmpty, abort_flag))
+            goto producer_done;
+          const uint32_t rb = smem_u32(rfull_bar);
+          mbar_arrive_expect_tx(rb, C::kResidBytes);
+#pragma unroll
+          for (int g = 0; g < BN / 64; ++g)
+            tma_load_2d(smem_u32(smem + C::kResidOffset + g * C::kBM * 128), &tmR, rb,
+                        nb * BN + g * 64, mb * C::kBM);
+          ++rtiles;
+        }
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u, err, kDevTimeoutSmemEmpty,
                                  abort_flag))
@@ -631,16 +722,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
           const uint32_t fb = smem_u32(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, C::kStageBytes);
           tma_load_2d(smem_u32(sa), &tmA, fb, kb * C::kBK, mb * C::kBM);
-#pragma unroll
-          for (int j = 0; j < C::kNSplit; ++j)
-            tma_load_2d(smem_u32(sb + j * C::kMmaN * C::kRowBytes), &tmW, fb, kb * C::kBK,
-                        nb * BN + j * C::kMmaN);
+          tma_load_2d(smem_u32(sb), &tmW, fb, kb * C::kBK, nb * BN);
           ++issued;
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
         }
       }
     producer_done:
       // Drain: make sure this thread's own copies have landed before exit.
+      if (kLnSlices && rtiles > 0) {
+        uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(smem_u32(rfull_bar), (uint32_t)(rtiles - 1) & 1u)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        }
+      }
       {
         int n = issued < C::kStages ? issued : C::kStages;
         int s = stage;
@@ -661,7 +755,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      for (int tile = first; tile < num_tiles; tile += stride, ++it) {
         const int acc = it % C::kNumAcc;
         const uint32_t acc_phase = (uint32_t)(it / C::kNumAcc) & 1u;
         if (!mbar_wait_bounded(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, err, kDevTimeoutAccEmpty,
@@ -679,20 +773,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
           tc_fence_after();
           const uint8_t* sa = smem + stage * C::kStageBytes;
           const uint64_t adesc = smem_desc_k_sw128(smem_u32(sa));
+          const uint64_t bdesc = smem_desc_k_sw128(smem_u32(sa + C::kABytes));
 #pragma unroll
-          for (int j = 0; j < C::kNSplit; ++j) {
-            const uint64_t bdesc =
-                smem_desc_k_sw128(smem_u32(sa + C::kABytes + j * C::kMmaN * C::kRowBytes));
-            const uint32_t dj = d_tmem + (uint32_t)(j * C::kMmaN);
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              // +32 bytes along K inside the 128-byte swizzle row (encoded >> 4).
-              const uint64_t koff = (uint64_t)(ks * 2);
-              if constexpr (S8)
-                mma_s8(dj, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
-              else
-                mma_bf16(dj, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
-            }
+          for (int ks = 0; ks < 4; ++ks) {
+            // +32 bytes along K inside the 128-byte swizzle row (encoded >> 4).
+            const uint64_t koff = (uint64_t)(ks * 2);
+            if constexpr (S8)
+              mma_s8(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
+            else
+              mma_bf16(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
           }
           mma_commit(smem_u32(&empty_bar[stage]));
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
@@ -716,22 +805,32 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
     const int part = (warp - 2) >> 2;    // which half of the column chunks
     TmaSink<2> tsink{extra + (warp - 2) * 4096, &tmO, lane, 0, ep.f16_from};
     TmaSink<1> lsink{extra + 4096 + (warp - 2) * 2048, &tmO, lane, 0, 1 << 30};
+    const LnPeers px{peers, rank, smem_u32(smem + C::kXchOffset), smem_u32(xfull_bar), err,
+                     abort_flag};
     int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+    for (int tile = first; tile < num_tiles; tile += stride, ++it) {
       const int acc = it % C::kNumAcc;
       const uint32_t acc_phase = (uint32_t)(it / C::kNumAcc) & 1u;
-      const int mb = tile / num_n, nb = tile % num_n;
+      const int mb = tile_mb(tile), nb = tile_nb(tile);
       const int row0 = mb * C::kBM + quarter * 32;
       const int row = row0 + lane;
-      LnResid rs;
-      if constexpr (EPI == kEpiResidLN) ln_prefetch<BN>(ep, row, M, part, rs);
       if (!mbar_wait_bounded(smem_u32(&accf_bar[acc]), acc_phase, err, kDevTimeoutAccFull,
                              abort_flag))
         break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * C::kAccStride + ((uint32_t)(quarter * 32) << 16);
-      if constexpr (EPI == kEpiResidLN) {
-        epilogue_resid_ln<BN>(taddr, row, row0, M, part, quarter, lane, ep, red, lsink, rs);
+      if constexpr (kLnSlices) {
+        if (!mbar_wait_bounded(smem_u32(rfull_bar), (uint32_t)it & 1u, err, kDevTimeoutTmaFull,
+                               abort_flag))
+          break;
+        const uint32_t rrow = smem_u32(smem + C::kResidOffset) + (uint32_t)(quarter * 32 + lane) * 128u;
+        auto resid_done = [&]() {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(rempty_bar));
+        };
+        if (!epilogue_resid_ln<BN>(taddr, row, row0, M, N, nb * BN, part, quarter, lane, ep, red,
+                                   lsink, rrow, resid_done, px, it))
+          break;
       } else if constexpr (kTmaStore) {
         epilogue_row<BN, EPI, S8>(taddr, row, row0, M, N, nb, part, ep, tsink);
       } else {
