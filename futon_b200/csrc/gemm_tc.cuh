@@ -313,13 +313,20 @@ __device__ __forceinline__ void acc_values(const uint32_t (&u)[32], float a_s, c
     load_col32(ep.w_scale, col, N, ws);
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = fmul((float)(int32_t)u[i], fmul(a_s, ws[i]));
+    if (ep.bias) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fadd(v[i], b[i]);
+    }
+  } else if (ep.bias) {
+    // f32 sum + bias, two columns per instruction.
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      f2_unpack(f2_add(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])),
+                       f2_pack(b[2 * i], b[2 * i + 1])),
+                v[2 * i], v[2 * i + 1]);
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(u[i]);
-  }
-  if (ep.bias) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = fadd(v[i], b[i]);
   }
 }
 
