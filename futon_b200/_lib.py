@@ -25,7 +25,7 @@ EXPORTED = (
     "futon_cuda_sync", "futon_cuda_launch_count", "futon_cuda_matmul_t",
     "futon_cuda_matmul_t_q8", "futon_cuda_quantize_rows_q8", "futon_cuda_profile",
     "futon_cuda_profile_read", "futon_cuda_profile_stage_count", "futon_cuda_profile_stage_name",
-    "futon_cuda_matmul_t_q8_noalloc",
+    "futon_cuda_matmul_t_q8_noalloc", "futon_cuda_selftest_wait_timeout",
 )
 
 
@@ -118,6 +118,8 @@ def lib() -> C.CDLL:
         L.futon_cuda_matmul_t_q8_noalloc.argtypes = [ip, vp, vp, vp, vp, ip, ip, ip, vp, vp, cp, sz]
         L.futon_cuda_quantize_rows_q8.restype = ip
         L.futon_cuda_quantize_rows_q8.argtypes = [ip, vp, vp, vp, ip, ip, vp, cp, sz]
+        L.futon_cuda_selftest_wait_timeout.restype = ip
+        L.futon_cuda_selftest_wait_timeout.argtypes = [ip, cp, sz]
         _lib = L
         return L
 

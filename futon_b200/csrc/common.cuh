@@ -26,6 +26,7 @@ enum DeviceError : int {
   kDevBadInput = 6,           // a token id outside [0, vocab) reached the device
   kDevTimeoutAttn = 7,        // attention waited too long for a TMA stage
   kDevTimeoutLnPeer = 8,      // LayerNorm epilogue waited too long for a peer CTA's sums
+  kDevTimeoutSelfTest = 9,    // futon_cuda_selftest_wait_timeout's deliberately unmet wait
 };
 
 // Wall-clock limit for any single barrier wait (nanoseconds). A healthy

@@ -1683,3 +1683,39 @@ extern "C" int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const
   if (code) return set_err(err, errlen, FUTON_EDEVICE, "native: device-side error %d", code);
   return FUTON_OK;
 }
+
+// ---- failure-detection self-test -------------------------------------------
+namespace {
+__global__ void selftest_wait_kernel(int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // Phase 0 never completes: nothing arrives on the barrier.
+  if (threadIdx.x == 0) mbar_wait_bounded(smem_u32(&bar), 0u, err, kDevTimeoutSelfTest, &abort_flag);
+}
+}  // namespace
+
+extern "C" int futon_cuda_selftest_wait_timeout(int cuda_device, char* err, size_t errlen) {
+  SeamCtx* s = nullptr;
+  int rc;
+  if ((rc = seam_begin(cuda_device, 0, &s, err, errlen))) return rc;
+  std::lock_guard<std::mutex> lk(s->mu);
+  CU_TRY(cudaMemset(s->err_word, 0, sizeof(int)));
+  selftest_wait_kernel<<<1, 32>>>(s->err_word);
+  CU_TRY(cudaGetLastError());
+  CU_TRY(cudaDeviceSynchronize());
+  int code = 0;
+  CU_TRY(cudaMemcpy(&code, s->err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  CU_TRY(cudaMemset(s->err_word, 0, sizeof(int)));
+  if (code != kDevTimeoutSelfTest)
+    return set_err(err, errlen, FUTON_ECUDA,
+                   "native: failure self-test: expected device code %d, read %d", kDevTimeoutSelfTest,
+                   code);
+  return set_err(err, errlen, FUTON_EDEVICE, "native: device wait timed out (self-test, code %d)",
+                 code);
+}

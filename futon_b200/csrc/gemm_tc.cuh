@@ -98,7 +98,10 @@ struct GemmCfg {
   static constexpr int kXchBytes = LNS ? 2 * kLnPeerSlots * 128 * 16 : 0;
   static constexpr int kResidOffset = kXchOffset + kXchBytes;       // 1024-aligned
   static constexpr int kResidBytes = LNS ? kBM * BN * 2 : 0;
-  static constexpr int kSmemBytes = kResidOffset + kResidBytes + 1024 /*align*/;
+  // LNS: the slice's bias, γ and β (3 × BN f32), read by every tile.
+  static constexpr int kColsOffset = kResidOffset + kResidBytes;
+  static constexpr int kColsBytes = LNS ? 3 * BN * 4 : 0;
+  static constexpr int kSmemBytes = kColsOffset + kColsBytes + 1024 /*align*/;
   static_assert(BN <= 256, "one tcgen05.mma covers the tile's N");
   static_assert(!LNS || BN % 64 == 0, "residual sub-tiles are 64 columns wide");
 };
@@ -302,27 +305,37 @@ __device__ __forceinline__ void load_col32(const float* p, int col, int limit, f
 }
 
 // Accumulator chunk → f32 values before the activation: f32 sum + bias, or
-// the int8 rescale float32(sum) * (sA * sW) + bias (quant.go:132-135).
+// the int8 rescale float32(sum) * (sA * sW) + bias (quant.go:132-135). The
+// column vectors are fetched (acc_fetch) before the epilogue waits for its
+// TMEM load, so the two latencies overlap, then applied (acc_apply).
 template <bool S8>
-__device__ __forceinline__ void acc_values(const uint32_t (&u)[32], float a_s, const EpiParams& ep,
-                                           int col, int N, float (&v)[32]) {
+struct AccCols {
   float b[32];
-  load_col32(ep.bias, col, N, b);
+  float ws[S8 ? 32 : 1];
+};
+
+template <bool S8>
+__device__ __forceinline__ void acc_fetch(const EpiParams& ep, int col, int N, AccCols<S8>& k) {
+  load_col32(ep.bias, col, N, k.b);
+  if constexpr (S8) load_col32(ep.w_scale, col, N, k.ws);
+}
+
+template <bool S8>
+__device__ __forceinline__ void acc_apply(const uint32_t (&u)[32], float a_s, const EpiParams& ep,
+                                          const AccCols<S8>& k, float (&v)[32]) {
   if constexpr (S8) {
-    float ws[32];
-    load_col32(ep.w_scale, col, N, ws);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = fmul((float)(int32_t)u[i], fmul(a_s, ws[i]));
+    for (int i = 0; i < 32; ++i) v[i] = fmul((float)(int32_t)u[i], fmul(a_s, k.ws[i]));
     if (ep.bias) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = fadd(v[i], b[i]);
+      for (int i = 0; i < 32; ++i) v[i] = fadd(v[i], k.b[i]);
     }
   } else if (ep.bias) {
     // f32 sum + bias, two columns per instruction.
 #pragma unroll
     for (int i = 0; i < 16; ++i)
       f2_unpack(f2_add(f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1])),
-                       f2_pack(b[2 * i], b[2 * i + 1])),
+                       f2_pack(k.b[2 * i], k.b[2 * i + 1])),
                 v[2 * i], v[2 * i + 1]);
   } else {
 #pragma unroll
@@ -382,10 +395,18 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
       uint32_t u[32], g[32];
       tmem_ld32(taddr + c, u);
       tmem_ld32(taddr + kHalf + c, g);
-      tmem_ld_wait();
       float hv[32], gv[32], v[32];
-      acc_values<S8>(u, a_s, ep, wcol0 + c, N, hv);
-      acc_values<S8>(g, a_s, ep, wcol0 + kHalf + c, N, gv);
+      {
+        AccCols<S8> k;
+        acc_fetch<S8>(ep, wcol0 + c, N, k);
+        tmem_ld_wait();
+        acc_apply<S8>(u, a_s, ep, k, hv);
+      }
+      {
+        AccCols<S8> k;
+        acc_fetch<S8>(ep, wcol0 + kHalf + c, N, k);
+        acc_apply<S8>(g, a_s, ep, k, gv);
+      }
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = fmul(hv[i], act_silu<S8>(gv[i]));
       sink.put(v, ocol0 + c, row0);
@@ -405,14 +426,18 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
         {
           uint32_t u[32];
           tmem_ld32(taddr + c, u);
+          AccCols<S8> k;
+          acc_fetch<S8>(ep, col0 + c, N, k);
           tmem_ld_wait();
-          acc_values<S8>(u, a_s, ep, col0 + c, N, a);
+          acc_apply<S8>(u, a_s, ep, k, a);
         }
         {
           uint32_t u[32];
           tmem_ld32(taddr + c + 32, u);
+          AccCols<S8> k;
+          acc_fetch<S8>(ep, col0 + c + 32, N, k);
           tmem_ld_wait();
-          acc_values<S8>(u, a_s, ep, col0 + c + 32, N, b);
+          acc_apply<S8>(u, a_s, ep, k, b);
         }
         if (col0 + c < ep.rope_cols) {
 #pragma unroll
@@ -430,9 +455,11 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
       for (int c = 32 * part; c < BN; c += 64) {
         uint32_t u[32];
         tmem_ld32(taddr + c, u);
+        AccCols<S8> k;
+        acc_fetch<S8>(ep, col0 + c, N, k);
         tmem_ld_wait();
         float v[32];
-        acc_values<S8>(u, a_s, ep, col0 + c, N, v);
+        acc_apply<S8>(u, a_s, ep, k, v);
         if (rope && col0 + c < ep.rope_cols) {
           if (hd == 32) rope_in_chunk<32>(v, cr, sr);
           else if (hd == 16) rope_in_chunk<16>(v, cr, sr);
@@ -457,9 +484,11 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
           for (int i = 0; i < 32; ++i) r[i] = 0.0f;
         }
       }
+      AccCols<S8> k;
+      acc_fetch<S8>(ep, col, N, k);
       tmem_ld_wait();
       float v[32];
-      acc_values<S8>(u, a_s, ep, col, N, v);
+      acc_apply<S8>(u, a_s, ep, k, v);
       if constexpr (EPI == kEpiGelu && !S8) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) gelu_fast2(v[2 * i], v[2 * i + 1]);
@@ -473,6 +502,14 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
       sink.put(v, col, row0);
     }
   }
+}
+
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
 }
 
 // Row-statistics exchange between the CTAs of a cluster that hold the column
@@ -494,15 +531,16 @@ struct LnPeers {
 // the row's other slices add theirs through distributed shared memory (in
 // rank order, so every slice normalises with bit-identical statistics), then
 // y = (v − mean)·inv·γ + β leaves through the TMA sink. `rrow` is this row's
-// line in residual sub-tile 0 (128-byte swizzled rows); `resid_done` is
-// called once the residual has been read. Returns false if a peer's sums did
-// not arrive in time.
+// line in residual sub-tile 0 (128-byte swizzled rows); `cols` holds the
+// slice's bias, γ and β (shared memory, BN f32 each); `resid_done` is called
+// once the residual has been read. Returns false if a peer's sums did not
+// arrive in time.
 template <int BN, typename Sink, typename Done>
 __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int row0, int M, int N,
                                                   int n0, int part, int quarter, int lane,
                                                   const EpiParams& ep, double2* red, Sink& sink,
-                                                  uint32_t rrow, Done&& resid_done,
-                                                  const LnPeers& px, int it) {
+                                                  uint32_t rrow, uint32_t cols,
+                                                  Done&& resid_done, const LnPeers& px, int it) {
   constexpr int kCols = BN / 2, kChunks = kCols / 32;
   const bool row_ok = row < M;
   const int c0 = part * kCols;
@@ -522,12 +560,11 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
       asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
                    : "=r"(w[4 * i]), "=r"(w[4 * i + 1]), "=r"(w[4 * i + 2]), "=r"(w[4 * i + 3])
                    : "r"(sub + (uint32_t)(((cc0 + i) ^ swz) << 4)));
-    const float4* b4 = ep.bias ? reinterpret_cast<const float4*>(ep.bias + n0 + c) : nullptr;
     tmem_ld_wait();
     uint64_t a1 = 0, a2 = 0;  // (0.f, 0.f)
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const float4 bq = ep.bias ? b4[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 bq = ld_shared_f4(cols + (uint32_t)(c + 4 * q) * 4u);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int i = 2 * q + h;
@@ -594,13 +631,12 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
   for (int c = c0; c < c0 + kCols; c += 32) {
     uint32_t u[32];
     tmem_ld32(taddr + c, u);
-    const float4* g4 = reinterpret_cast<const float4*>(ep.ln_w + n0 + c);
-    const float4* e4 = reinterpret_cast<const float4*>(ep.ln_b + n0 + c);
     tmem_ld_wait();
     float y[32];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const float4 gq = g4[q], eq = e4[q];
+      const float4 gq = ld_shared_f4(cols + (uint32_t)(BN + c + 4 * q) * 4u);
+      const float4 eq = ld_shared_f4(cols + (uint32_t)(2 * BN + c + 4 * q) * 4u);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int i = 2 * q + h;
@@ -692,6 +728,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
     tmem_relinquish();
+  }
+  if constexpr (kLnSlices) {
+    // The slice's bias, γ and β, read by every tile's epilogue.
+    float* cs = reinterpret_cast<float*>(smem + C::kColsOffset);
+    const int n0 = (int)rank * BN;
+    for (int i = threadIdx.x; i < BN; i += blockDim.x) {
+      cs[i] = ep.bias ? ep.bias[n0 + i] : 0.0f;
+      cs[BN + i] = ep.ln_w[n0 + i];
+      cs[2 * BN + i] = ep.ln_b[n0 + i];
+    }
   }
   tc_fence_before();
   if constexpr (kLnSlices) cluster_sync_all();  // peers' barriers exist before any remote arrive
@@ -836,7 +882,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
           if (lane == 0) mbar_arrive(smem_u32(rempty_bar));
         };
         if (!epilogue_resid_ln<BN>(taddr, row, row0, M, N, nb * BN, part, quarter, lane, ep, red,
-                                   lsink, rrow, resid_done, px, it))
+                                   lsink, rrow, smem_u32(smem + C::kColsOffset), resid_done, px,
+                                   it))
           break;
       } else if constexpr (kTmaStore) {
         epilogue_row<BN, EPI, S8>(taddr, row, row0, M, N, nb, part, ep, tsink);

@@ -179,6 +179,15 @@ int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const float* a, 
                                    const float* scales, int m, int n, int k, const float* bias,
                                    void* stream, char* err, size_t errlen);
 
+/* Failure-detection self-test (no counterpart in the reference): launches
+ * one CTA that waits, through the same bounded-wait routine every pipeline
+ * kernel uses, on an mbarrier phase that nothing completes. The wait gives up
+ * after its 1 s limit, records its code in the device error word and the
+ * kernel returns, so the call returns FUTON_EDEVICE ("device wait timed out")
+ * with the context still usable. Any other outcome is an error of the
+ * library's failure detection on this device (FUTON_ECUDA). */
+int futon_cuda_selftest_wait_timeout(int cuda_device, char* err, size_t errlen);
+
 #ifdef __cplusplus
 }
 #endif
