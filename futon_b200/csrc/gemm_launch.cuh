@@ -28,7 +28,7 @@ cudaError_t launch_gemm_s8(const GemmLaunch& g);
 
 template <int BN, int EPI, bool S8, typename OutT>
 cudaError_t launch_gemm_inst(const GemmLaunch& g) {
-  using C = GemmCfg<BN, S8, EPI == kEpiResidLN>;
+  using C = GemmCfg<BN, S8, EPI == kEpiResidLN, gemm_epi_warps<BN, EPI, S8>()>;
   auto kern = gemm_tc_kernel<BN, EPI, S8, OutT>;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -73,7 +73,10 @@ constexpr int kLnPeerSlots = 4;
 // in clusters): three stages, the row-statistics exchange buffer and the
 // residual tile (TMA-loaded, 128 rows × BN bf16 as BN/64 swizzled 16 KB
 // sub-tiles) in shared memory.
-template <int BN, bool S8, bool LNS = false>
+// EW: epilogue warps (a multiple of 4; EW / 4 of them share each TMEM lane
+// quarter, splitting its 32-column chunks). The stage count is what the
+// shared-memory budget leaves after the epilogue's buffers.
+template <int BN, bool S8, bool LNS = false, int EW = 8>
 struct GemmCfg {
   static constexpr int kBM = 128;
   static constexpr int kRowBytes = 128;                       // one swizzle row
@@ -81,30 +84,44 @@ struct GemmCfg {
   static constexpr int kABytes = kBM * kRowBytes;
   static constexpr int kBBytes = BN * kRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = LNS ? 3 : (BN >= 192) ? 4 : (BN == 128) ? 5 : 7;
   static constexpr int kMmaN = BN;                            // N of one tcgen05.mma (≤ 256)
   static constexpr int kNumAcc = 2;                           // TMEM accumulators
   static constexpr uint32_t kAccStride = (BN <= 64) ? 64 : (BN <= 128) ? 128 : 256;
   static constexpr uint32_t kTmemCols = kNumAcc * kAccStride; // power of two, ≤ 512
-  static constexpr int kEpiWarps = 8;                         // two per TMEM lane quarter
+  static constexpr int kEpiWarps = EW;
+  static constexpr int kParts = EW / 4;                       // epilogue warps per lane quarter
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   // After the stage ring: barriers (≤ 1 KB), then either the LayerNorm
   // partial sums (2 × 128 double2) and one 2 KB staging buffer per epilogue
   // warp, or the TMA-store staging (per epilogue warp two 32 × 64-byte
   // buffers).
   static constexpr int kStagingBytes = kEpiWarps * 2 * 2048;
+  static constexpr int kXchBytes = LNS ? 2 * kLnPeerSlots * 128 * 16 : 0;
+  static constexpr int kResidBytes = LNS ? kBM * BN * 2 : 0;
+  static constexpr int kColsBytes = LNS ? 3 * BN * 4 : 0;
+  static constexpr int kFixedBytes =
+      1024 /*barriers*/ + kStagingBytes + kXchBytes + kResidBytes + kColsBytes + 1024 /*align*/;
+  static constexpr int kBudget = 227 * 1024;
+  static constexpr int kFit = (kBudget - kFixedBytes) / kStageBytes;
+  static constexpr int kStages = kFit > 7 ? 7 : kFit;
   static constexpr int kExtraOffset = kStages * kStageBytes + 1024;  // 1024-aligned
   static constexpr int kXchOffset = kExtraOffset + kStagingBytes;
-  static constexpr int kXchBytes = LNS ? 2 * kLnPeerSlots * 128 * 16 : 0;
   static constexpr int kResidOffset = kXchOffset + kXchBytes;       // 1024-aligned
-  static constexpr int kResidBytes = LNS ? kBM * BN * 2 : 0;
   // LNS: the slice's bias, γ and β (3 × BN f32), read by every tile.
   static constexpr int kColsOffset = kResidOffset + kResidBytes;
-  static constexpr int kColsBytes = LNS ? 3 * BN * 4 : 0;
   static constexpr int kSmemBytes = kColsOffset + kColsBytes + 1024 /*align*/;
   static_assert(BN <= 256, "one tcgen05.mma covers the tile's N");
   static_assert(!LNS || BN % 64 == 0, "residual sub-tiles are 64 columns wide");
+  static_assert(!LNS || EW == 8, "the LayerNorm epilogue pairs two warps per lane quarter");
+  static_assert(kStages >= 3 && kSmemBytes <= kBudget, "shared-memory budget");
 };
+
+// Epilogue warps of an instantiation: 16 for the GELU tiles (the heaviest
+// per-element epilogue), 8 otherwise.
+template <int BN, int EPI, bool S8>
+__host__ __device__ constexpr int gemm_epi_warps() {
+  return (EPI == 1 /*kEpiGelu*/ && !S8 && BN == 256) ? 16 : 8;
+}
 
 template <typename T> __device__ __forceinline__ void store32(T* dst, const float (&v)[32]);
 
@@ -381,7 +398,7 @@ __device__ __forceinline__ void rope_in_chunk(float (&v)[32], const float* cr, c
 // kEpiStore / kEpiGelu / kEpiSwiglu / kEpiResid for one thread (= one row).
 // The two warps sharing a TMEM lane quarter split the 32-column chunks
 // (part = 0/1; whole heads per thread when RoPE is on).
-template <int BN, int EPI, bool S8, typename Sink>
+template <int BN, int EPI, bool S8, int kParts, typename Sink>
 __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, int M, int N,
                                              int nb, int part, const EpiParams& ep, Sink& sink) {
   const bool row_ok = row < M;
@@ -391,7 +408,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
     const int wcol0 = nb * BN;            // interleaved weight/bias column of this tile
     const int ocol0 = nb * kHalf;         // output column of this tile
 #pragma unroll 1
-    for (int c = 32 * part; c < kHalf; c += 64) {
+    for (int c = 32 * part; c < kHalf; c += 32 * kParts) {
       uint32_t u[32], g[32];
       tmem_ld32(taddr + c, u);
       tmem_ld32(taddr + kHalf + c, g);
@@ -421,7 +438,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
     if (rope && hd == 64) {
       // A head's two halves are two 32-column chunks: heads alternate by part.
 #pragma unroll 1
-      for (int c = 64 * part; c < BN; c += 128) {
+      for (int c = 64 * part; c < BN; c += 64 * kParts) {
         float a[32], b[32];
         {
           uint32_t u[32];
@@ -452,7 +469,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
       }
     } else {
 #pragma unroll 1
-      for (int c = 32 * part; c < BN; c += 64) {
+      for (int c = 32 * part; c < BN; c += 32 * kParts) {
         uint32_t u[32];
         tmem_ld32(taddr + c, u);
         AccCols<S8> k;
@@ -471,7 +488,7 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
   } else {
     const int col0 = nb * BN;
 #pragma unroll 1
-    for (int c = 32 * part; c < BN; c += 64) {
+    for (int c = 32 * part; c < BN; c += 32 * kParts) {
       uint32_t u[32];
       tmem_ld32(taddr + c, u);
       const int col = col0 + c;
@@ -656,7 +673,7 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
 }
 
 template <int BN, int EPI, bool S8, typename OutT>
-__global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
+__global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    int M, int N, int K, EpiParams ep, int* err) {
@@ -666,7 +683,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   // producer loads each tile's residual slice (tmR) next to the operands.
   constexpr bool kLnSlices = EPI == kEpiResidLN;
   static_assert(!kLnSlices || (BN == 192 && !S8), "LayerNorm slices are 192 bf16 columns");
-  using C = GemmCfg<BN, S8, kLnSlices>;
+  using C = GemmCfg<BN, S8, kLnSlices, gemm_epi_warps<BN, EPI, S8>()>;
   // bf16 outputs leave through TMA tile stores; f32 outputs store directly.
   constexpr bool kTmaStore = sizeof(OutT) == 2;
   extern __shared__ uint8_t smem_raw[];
@@ -855,7 +872,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
   } else {
     // ---------------- epilogue warps 2..9 ----------------
     const int quarter = warp & 3;        // TMEM lanes [32*quarter, 32*quarter+32)
-    const int part = (warp - 2) >> 2;    // which half of the column chunks
+    const int part = (warp - 2) >> 2;    // which share of the column chunks
     TmaSink<2> tsink{extra + (warp - 2) * 4096, &tmO, lane, 0, ep.f16_from};
     TmaSink<1> lsink{extra + 4096 + (warp - 2) * 2048, &tmO, lane, 0, 1 << 30};
     const LnPeers px{peers, rank, smem_u32(smem + C::kXchOffset), smem_u32(xfull_bar), err,
@@ -886,11 +903,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, S8>::kThreads, 1)
                                    it))
           break;
       } else if constexpr (kTmaStore) {
-        epilogue_row<BN, EPI, S8>(taddr, row, row0, M, N, nb, part, ep, tsink);
+        epilogue_row<BN, EPI, S8, C::kParts>(taddr, row, row0, M, N, nb, part, ep, tsink);
       } else {
         DirectSink<OutT> dsink{reinterpret_cast<OutT*>(ep.out), ep.ldo, row, row < M,
                                EPI == kEpiSwiglu ? N / 2 : N};
-        epilogue_row<BN, EPI, S8>(taddr, row, row0, M, N, nb, part, ep, dsink);
+        epilogue_row<BN, EPI, S8, C::kParts>(taddr, row, row0, M, N, nb, part, ep, dsink);
       }
       tc_fence_before();
       __syncwarp();
