@@ -59,8 +59,9 @@ struct AttnTcCfg {
   static constexpr int kRowBytes = HD * 2;
   static constexpr int kTileBytes = 128 * kRowBytes;       // one q, k or v tile
   static constexpr int kSlotBytes = 3 * kTileBytes;
-  static constexpr int kSlots = 2;
+  static constexpr int kSlots = 3;
   static constexpr int kPOffset = kSlots * kSlotBytes;     // multiple of 1024
+  static constexpr int kMaxSegs = 8;                       // 128 rows / 16-row alignment
   static constexpr int kPBytes = 2 * 128 * 128;            // two 64-key regions, 128 B rows
   static constexpr int kOnesOffset = kPOffset + kPBytes;
   static constexpr int kOnesBytes = 16 * 128;              // B operand of the row sums
@@ -130,14 +131,16 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
   const uint32_t sP = sbase + C::kPOffset;
   const uint32_t sOnes = sbase + C::kOnesOffset;
   const uint32_t bars = sbase + C::kBarOffset;
-  const uint32_t full_b = bars;            // [2] TMA → MMA
-  const uint32_t empty_b = bars + 16;      // [2] MMA → TMA
-  const uint32_t sfull_b = bars + 32;      // S ready (MMA → softmax)
-  const uint32_t sfree_b = bars + 40;      // S read (softmax → MMA)
-  const uint32_t pfull_b = bars + 48;      // P written, O corrected (softmax → MMA)
-  const uint32_t ofull_b = bars + 56;      // P·V done (MMA → softmax)
+  constexpr int kS = C::kSlots;
+  const uint32_t full_b = bars;            // [kSlots] TMA → MMA
+  const uint32_t empty_b = bars + 8 * kS;  // [kSlots] MMA → TMA
+  const uint32_t sfull_b = bars + 16 * kS; // S ready (MMA → softmax)
+  const uint32_t sfree_b = sfull_b + 8;    // S read (softmax → MMA)
+  const uint32_t pfull_b = sfull_b + 16;   // P written, O corrected (softmax → MMA)
+  const uint32_t ofull_b = sfull_b + 24;   // P·V done (MMA → softmax)
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
+  __shared__ AttnSeg seg_sm[C::kMaxSegs];  // the window's segments
 
   const AttnWindow win = windows[blockIdx.x];
   const int nkb = (win.nk + 127) / 128;    // key blocks per head
@@ -146,7 +149,7 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kS; ++i) {
       mbar_init(full_b + 8 * i, 1);
       mbar_init(empty_b + 8 * i, 1);
     }
@@ -158,6 +161,7 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_qkv16);
   }
+  if (threadIdx.x < win.nseg) seg_sm[threadIdx.x] = segs[win.seg0 + threadIdx.x];
   // The row-sum operand: 16 rows × 128 bytes of f16 ones (layout-independent).
   for (int i = threadIdx.x; i < C::kOnesBytes / 16; i += blockDim.x)
     st_shared_v4(sOnes + 16 * i, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
@@ -175,9 +179,9 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       for (int u = 0; u < units; ++u) {
-        const int head = u / nkb, j = u % nkb, slot = u & 1;
-        if (u >= 2 && !mbar_wait_bounded(empty_b + 8 * slot, ((u >> 1) - 1) & 1, err,
-                                         kDevTimeoutAttn, &abort_flag))
+        const int head = u / nkb, j = u % nkb, slot = u % kS;
+        if (u >= kS && !mbar_wait_bounded(empty_b + 8 * slot, ((u / kS) - 1) & 1, err,
+                                          kDevTimeoutAttn, &abort_flag))
           break;
         const uint32_t fb = full_b + 8 * slot;
         const uint32_t dst = sbase + slot * C::kSlotBytes;
@@ -191,7 +195,7 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
           // Rows [0, nq) in 16-row boxes, each segment from its own tokens.
           mbar_arrive_expect_tx(fb, 3 * win.nq * C::kRowBytes);
           for (int sg = 0; sg < win.nseg; ++sg) {
-            const AttnSeg sq = segs[win.seg0 + sg];
+            const AttnSeg sq = seg_sm[sg];
             for (int m = 0; m < sq.len; m += 16) {
               const uint32_t o = (uint32_t)(sq.row + m) * C::kRowBytes;
               tma_load_2d(dst + o, &tm_qkv16, fb, xq, sq.t0 + m);
@@ -207,8 +211,8 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
       // ---------------- MMA issuer ----------------
       auto keys16 = [&](int j) { return (min(128, win.nk - 128 * j) + 15) & ~15; };
       auto issue_s = [&](int u) -> bool {
-        const int slot = u & 1;
-        if (!mbar_wait_bounded(full_b + 8 * slot, (u >> 1) & 1, err, kDevTimeoutAttn, &abort_flag))
+        const int slot = u % kS;
+        if (!mbar_wait_bounded(full_b + 8 * slot, (u / kS) & 1, err, kDevTimeoutAttn, &abort_flag))
           return false;
         tc_fence_after();
         const uint32_t q = sbase + slot * C::kSlotBytes, k = q + C::kTileBytes;
@@ -230,7 +234,7 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
         if (u + 1 < units && !issue_s(u + 1)) break;
         if (!mbar_wait_bounded(pfull_b, u & 1, err, kDevTimeoutAttn, &abort_flag)) break;
         tc_fence_after();
-        const int j = u % nkb, slot = u & 1;
+        const int j = u % nkb, slot = u % kS;
         const uint32_t v = sbase + slot * C::kSlotBytes + 2 * C::kTileBytes;
         const int nks = keys16(j) / 16;
         for (int ks = 0; ks < nks; ++ks) {
@@ -258,7 +262,7 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
       }
     } else {
       for (int sg = 0; sg < win.nseg; ++sg) {
-        const AttnSeg sq = segs[win.seg0 + sg];
+        const AttnSeg sq = seg_sm[sg];
         if (r >= sq.row && r < sq.row + sq.len) {
           tok = sq.t0 + (r - sq.row);
           klo = sq.row;

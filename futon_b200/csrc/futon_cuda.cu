@@ -542,7 +542,8 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   if (M == 0) return FUTON_OK;
   const double esz = s8 ? 1.0 : 2.0;
   const double out_cols = o.epi == kEpiSwiglu ? w.n / 2 : w.n;
-  const double osz = (o.out_f32 || (s8 && o.epi != kEpiStore)) ? 4.0 : 2.0;
+  const bool plain = o.epi == kEpiStore || o.epi == kEpiRope;
+  const double osz = (o.out_f32 || (s8 && !plain)) ? 4.0 : 2.0;
   const double rsz = o.resid ? (o.resid_bf16 ? 2.0 : 4.0) : 0.0;
   const double bytes = (double)M * w.k * esz + (double)w.n * w.k * esz + (double)M * out_cols * osz +
                        (double)M * w.n * rsz + (o.out_f32_copy ? (double)M * w.n * 4.0 : 0.0);
@@ -551,7 +552,7 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   if (!make_operand_map(&ta, A, s8, (uint64_t)M, (uint64_t)w.k, 128))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (activation)");
   // bf16 outputs leave through TMA tile stores.
-  const bool bf16_out = o.epi == kEpiResidLN || !(o.out_f32 || (s8 && o.epi != kEpiStore));
+  const bool bf16_out = o.epi == kEpiResidLN || !(o.out_f32 || (s8 && !plain));
   if (bf16_out) {
     const uint64_t ncols = o.epi == kEpiSwiglu ? (uint64_t)w.n / 2 : (uint64_t)w.n;
     if (!make_output_map(&to, o.out, (uint64_t)M, ncols, (uint64_t)o.ldo))
@@ -757,6 +758,7 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       o.ldo = 3 * h;
       if (!q8 && (m.head_dim == 32 || m.head_dim == 64)) o.f16_from = 2 * h;
       if (c.position_encoding == FUTON_POS_ROPE) {
+        o.epi = kEpiRope;
         o.rope_cos = d.rcos;
         o.rope_sin = d.rsin;
         o.rope_hd = m.head_dim;

@@ -89,6 +89,9 @@ cudaError_t launch_gemm_bn(const GemmLaunch& g) {
       case kEpiStore:
         return g.out_f32 ? launch_gemm_inst<BN, kEpiStore, false, float>(g)
                          : launch_gemm_inst<BN, kEpiStore, false, Bf>(g);
+      case kEpiRope:
+        return g.out_f32 ? launch_gemm_inst<BN, kEpiRope, false, float>(g)
+                         : launch_gemm_inst<BN, kEpiRope, false, Bf>(g);
       case kEpiGelu: return launch_gemm_inst<BN, kEpiGelu, false, Bf>(g);
       case kEpiSwiglu:
         if constexpr (BN != 192) return launch_gemm_inst<BN, kEpiSwiglu, false, Bf>(g);
@@ -103,6 +106,9 @@ cudaError_t launch_gemm_bn(const GemmLaunch& g) {
       case kEpiStore:
         return g.out_f32 ? launch_gemm_inst<BN, kEpiStore, true, float>(g)
                          : launch_gemm_inst<BN, kEpiStore, true, Bf>(g);
+      case kEpiRope:
+        return g.out_f32 ? launch_gemm_inst<BN, kEpiRope, true, float>(g)
+                         : launch_gemm_inst<BN, kEpiRope, true, Bf>(g);
       case kEpiGelu: return launch_gemm_inst<BN, kEpiGelu, true, float>(g);
       case kEpiSwiglu:
         if constexpr (BN != 192) return launch_gemm_inst<BN, kEpiSwiglu, true, float>(g);

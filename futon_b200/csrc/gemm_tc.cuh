@@ -5,12 +5,13 @@
 // with A row-major [M, K] (activations) and W row-major [N, K] (nn.Linear
 // layout, exactly how pack weights are stored), then applies one of the
 // layer epilogues of native/model.go:550-635 before the single store:
-//   kEpiStore   D + bias, optionally RoPE on q/k     (qkv projection)
+//   kEpiStore   D + bias                               (qkv projection)
+//   kEpiRope    D + bias, NeoX RoPE on the q/k columns (qkv of a RoPE pack)
 //   kEpiGelu    gelu(D + bias)                         (fc1, model.go:610-616)
 //   kEpiSwiglu  (D_fc1 + b1) * silu(D_gate + b2)       (fc1‖gate, model.go:617-627)
 //   kEpiResid   (D + bias) + residual                  (out / fc2 before LayerNorm)
 //   kEpiResidLN LayerNorm((D + bias) + residual)       (out / fc2 + norm1 / norm2,
-//               full-row tiles: BN = N = hidden ≤ 384, model.go:596-599, 628-633)
+//               192-column row slices in clusters, model.go:596-599, 628-633)
 // and, for the int8 path (native/quant.go:99-137), the exact rescale
 //   float32(sum_s32) * (scale_a[m] * scale_w[n]) + bias[n].
 //
@@ -38,7 +39,9 @@
 
 namespace futon {
 
-enum EpiKind : int { kEpiStore = 0, kEpiGelu = 1, kEpiSwiglu = 2, kEpiResid = 3, kEpiResidLN = 4 };
+enum EpiKind : int {
+  kEpiStore = 0, kEpiGelu = 1, kEpiSwiglu = 2, kEpiResid = 3, kEpiResidLN = 4, kEpiRope = 5
+};
 
 struct EpiParams {
   void* out;             // bf16 or f32 output, row stride ldo elements
@@ -53,7 +56,7 @@ struct EpiParams {
   const float* ln_b;
   float eps;
   float* out_f32;        // kEpiResidLN: optional f32 copy of the normalised rows
-  // kEpiStore on the qkv projection of a RoPE pack: NeoX rotation of the q
+  // kEpiRope (the qkv projection of a RoPE pack): NeoX rotation of the q
   // and k columns (< rope_cols) per head of rope_hd, at each row's position
   // in its sequence (cu_seqlens[nseq+1]), before the store (model.go:674-685).
   const float* rope_cos;  // [positions, rope_hd/2]
@@ -95,7 +98,10 @@ struct GemmCfg {
   // partial sums (2 × 128 double2) and one 2 KB staging buffer per epilogue
   // warp, or the TMA-store staging (per epilogue warp two 32 × 64-byte
   // buffers).
-  static constexpr int kStagingBytes = kEpiWarps * 2 * 2048;
+  // LayerNorm: [2 tile parities][kParts][128 rows] double2 partial sums,
+  // then one 2 KB staging buffer per epilogue warp.
+  static constexpr int kRedBytes = LNS ? 2 * kParts * 128 * 16 : 0;
+  static constexpr int kStagingBytes = LNS ? kRedBytes + kEpiWarps * 2048 : kEpiWarps * 2 * 2048;
   static constexpr int kXchBytes = LNS ? 2 * kLnPeerSlots * 128 * 16 : 0;
   static constexpr int kResidBytes = LNS ? kBM * BN * 2 : 0;
   static constexpr int kColsBytes = LNS ? 3 * BN * 4 : 0;
@@ -112,15 +118,17 @@ struct GemmCfg {
   static constexpr int kSmemBytes = kColsOffset + kColsBytes + 1024 /*align*/;
   static_assert(BN <= 256, "one tcgen05.mma covers the tile's N");
   static_assert(!LNS || BN % 64 == 0, "residual sub-tiles are 64 columns wide");
-  static_assert(!LNS || EW == 8, "the LayerNorm epilogue pairs two warps per lane quarter");
+  static_assert(!LNS || (BN / 32) % kParts == 0, "LayerNorm column shares are whole chunks");
   static_assert(kStages >= 3 && kSmemBytes <= kBudget, "shared-memory budget");
 };
 
-// Epilogue warps of an instantiation: 16 for the GELU tiles (the heaviest
-// per-element epilogue), 8 otherwise.
+// Epilogue warps of an instantiation: 16 (two 32-column chunks each) for the
+// bf16 GELU and plain-store tiles at BN 256, whose epilogues set the pace,
+// and 8 otherwise (12 measured slower for the LayerNorm slices and no faster
+// for the BN 192 qkv tiles).
 template <int BN, int EPI, bool S8>
 __host__ __device__ constexpr int gemm_epi_warps() {
-  return (EPI == 1 /*kEpiGelu*/ && !S8 && BN == 256) ? 16 : 8;
+  return ((EPI == kEpiGelu || EPI == kEpiStore) && !S8 && BN == 256) ? 16 : 8;
 }
 
 template <typename T> __device__ __forceinline__ void store32(T* dst, const float (&v)[32]);
@@ -395,7 +403,7 @@ __device__ __forceinline__ void rope_in_chunk(float (&v)[32], const float* cr, c
   }
 }
 
-// kEpiStore / kEpiGelu / kEpiSwiglu / kEpiResid for one thread (= one row).
+// kEpiStore / kEpiRope / kEpiGelu / kEpiSwiglu / kEpiResid for one thread (= one row).
 // The two warps sharing a TMEM lane quarter split the 32-column chunks
 // (part = 0/1; whole heads per thread when RoPE is on).
 template <int BN, int EPI, bool S8, int kParts, typename Sink>
@@ -428,9 +436,9 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
       for (int i = 0; i < 32; ++i) v[i] = fmul(hv[i], act_silu<S8>(gv[i]));
       sink.put(v, ocol0 + c, row0);
     }
-  } else if constexpr (EPI == kEpiStore) {
+  } else if constexpr (EPI == kEpiStore || EPI == kEpiRope) {
     const int col0 = nb * BN;
-    const bool rope = ep.rope_cos != nullptr;
+    constexpr bool rope = EPI == kEpiRope;
     const int hd = ep.rope_hd, half = hd >> 1;
     const int pos = (rope && row_ok) ? seq_position(ep.cu, ep.nseq, row) : 0;
     const float* cr = rope ? ep.rope_cos + (size_t)pos * half : nullptr;
@@ -543,8 +551,8 @@ struct LnPeers {
 // Fused residual + LayerNorm (model.go:743-769) over the BN-column slice
 // [n0, n0 + BN) of a row whose full length is N: v = acc + bias + resid (the
 // residual tile is already in shared memory) is written back to TMEM while
-// Σv and Σv² accumulate in f64; the two warps of a lane quarter (one per
-// column half) combine their sums through shared memory, the CTAs holding
+// Σv and Σv² accumulate in f64; the kParts warps of a lane quarter (one per
+// column share) combine their sums through shared memory, the CTAs holding
 // the row's other slices add theirs through distributed shared memory (in
 // rank order, so every slice normalises with bit-identical statistics), then
 // y = (v − mean)·inv·γ + β leaves through the TMA sink. `rrow` is this row's
@@ -552,13 +560,13 @@ struct LnPeers {
 // slice's bias, γ and β (shared memory, BN f32 each); `resid_done` is called
 // once the residual has been read. Returns false if a peer's sums did not
 // arrive in time.
-template <int BN, typename Sink, typename Done>
+template <int BN, int kParts, typename Sink, typename Done>
 __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int row0, int M, int N,
                                                   int n0, int part, int quarter, int lane,
                                                   const EpiParams& ep, double2* red, Sink& sink,
                                                   uint32_t rrow, uint32_t cols,
                                                   Done&& resid_done, const LnPeers& px, int it) {
-  constexpr int kCols = BN / 2, kChunks = kCols / 32;
+  constexpr int kCols = BN / kParts, kChunks = kCols / 32;
   const bool row_ok = row < M;
   const int c0 = part * kCols;
   const int swz = lane & 7;  // row & 7 (rows of a quarter start at multiples of 32)
@@ -609,11 +617,18 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
   resid_done();
   tmem_st_wait();
   const int slot = quarter * 32 + lane;
-  red[part * 128 + slot] = make_double2(s1, s2);
-  named_bar_sync(1 + quarter, 64);
-  const double2 o = red[(1 - part) * 128 + slot];
-  // This slice's sums, identical in both warps (two-term sums commute).
-  double t1 = s1 + o.x, t2 = s2 + o.y;
+  double2* rp = red + (size_t)(it & 1) * kParts * 128;  // this tile's parity
+  rp[part * 128 + slot] = make_double2(s1, s2);
+  named_bar_sync(1 + quarter, 32 * kParts);
+  // This slice's sums, added in part order: identical in every warp of the
+  // quarter.
+  double t1 = 0.0, t2 = 0.0;
+#pragma unroll
+  for (int q = 0; q < kParts; ++q) {
+    const double2 o = rp[q * 128 + slot];
+    t1 += o.x;
+    t2 += o.y;
+  }
   if (px.peers > 1) {
     const uint32_t par = (uint32_t)(it & 1);
     const uint32_t cell = px.xbuf + ((par * kLnPeerSlots + px.rank) * 128 + slot) * 16;
@@ -699,8 +714,8 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
   uint64_t* xfull_bar = acce_bar + 3;              // [2] peers → LayerNorm epilogue
   uint64_t* rfull_bar = acce_bar + 5;              // residual tile: TMA → epilogue
   uint64_t* rempty_bar = acce_bar + 6;             // residual tile: epilogue → TMA
-  // Extra region: LayerNorm kernels keep 4 KB of partial sums, then one
-  // 2 KB staging buffer per epilogue warp; other kernels two per warp.
+  // Extra region: LayerNorm kernels keep their partial sums (kRedBytes),
+  // then one 2 KB staging buffer per epilogue warp; other kernels two per warp.
   uint8_t* extra = smem + C::kExtraOffset;
   double2* red = reinterpret_cast<double2*>(extra);
 
@@ -874,7 +889,7 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     const int quarter = warp & 3;        // TMEM lanes [32*quarter, 32*quarter+32)
     const int part = (warp - 2) >> 2;    // which share of the column chunks
     TmaSink<2> tsink{extra + (warp - 2) * 4096, &tmO, lane, 0, ep.f16_from};
-    TmaSink<1> lsink{extra + 4096 + (warp - 2) * 2048, &tmO, lane, 0, 1 << 30};
+    TmaSink<1> lsink{extra + C::kRedBytes + (warp - 2) * 2048, &tmO, lane, 0, 1 << 30};
     const LnPeers px{peers, rank, smem_u32(smem + C::kXchOffset), smem_u32(xfull_bar), err,
                      abort_flag};
     int it = 0;
@@ -898,7 +913,7 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(rempty_bar));
         };
-        if (!epilogue_resid_ln<BN>(taddr, row, row0, M, N, nb * BN, part, quarter, lane, ep, red,
+        if (!epilogue_resid_ln<BN, C::kParts>(taddr, row, row0, M, N, nb * BN, part, quarter, lane, ep, red,
                                    lsink, rrow, smem_u32(smem + C::kColsOffset), resid_done, px,
                                    it))
           break;
