@@ -131,6 +131,11 @@ bool make_qkv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
   return r == CUDA_SUCCESS;
 }
 
+// Column-slice width of the fused LayerNorm GEMMs (128-column slices, which
+// leave room for a fourth pipeline stage, measured 25 % slower on the bge
+// shape: three-CTA clusters and a third copy of every A tile).
+int ln_slice_cols(int) { return 192; }
+
 // N tile for a GEMM with N output columns: the widest of 256/192/128 that
 // divides N, else 64 (partial last tile, masked in the epilogue).
 int pick_bn(int n) {
@@ -233,8 +238,9 @@ struct DevCtx {
 struct futon_model {
   futon_cfg cfg;
   int q8 = 0;
-  // Residual + LayerNorm fused into the out/fc2 GEMMs: hidden = 192·P with
-  // 2 ≤ P ≤ 4 (P CTAs of a cluster share each row tile).
+  // Residual + LayerNorm fused into the out/fc2 GEMMs: hidden = w·P with
+  // slice width w = ln_slice_cols(hidden) and 2 ≤ P ≤ 4 (P CTAs of a
+  // cluster share each row tile).
   bool fuse_ln = false;
   int head_dim = 0;
   int eff_max = 0;
@@ -433,7 +439,7 @@ int upload_gemm(DevCtx& d, GemmWeight& g, const float* w1, const float* b1, cons
     }
     if ((rc = upload_f32(d, &g.bias, hb.data(), (size_t)n, err, errlen))) return rc;
   }
-  g.bn = w2 ? 2 * half : (ln_slices ? 192 : pick_bn(n));
+  g.bn = w2 ? 2 * half : (ln_slices ? ln_slice_cols(n) : pick_bn(n));
   const uint32_t box = g.bn <= 256 ? (uint32_t)g.bn : (uint32_t)g.bn / 2;
   if (!make_operand_map(&g.map, g.w, q8, (uint64_t)n, (uint64_t)k, box))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed for a weight");
@@ -1305,7 +1311,8 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
   model->head_dim = hd;
   model->eff_max = effective_max(c);
   model->swiglu_half = half;
-  model->fuse_ln = !q8 && h % 192 == 0 && h / 192 >= 2 && h / 192 <= kLnPeerSlots;
+  model->fuse_ln = !q8 && h % ln_slice_cols(h) == 0 && h / ln_slice_cols(h) >= 2 &&
+                   h / ln_slice_cols(h) <= kLnPeerSlots;
 
   // RoPE tables (precomputeRoPE, model.go:306-318): f64 angles, f32 storage.
   std::vector<float> rc_tab, rs_tab;

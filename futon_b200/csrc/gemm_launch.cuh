@@ -98,7 +98,7 @@ cudaError_t launch_gemm_bn(const GemmLaunch& g) {
         else return cudaErrorInvalidValue;
       case kEpiResid: return launch_gemm_inst<BN, kEpiResid, false, float>(g);
       case kEpiResidLN:
-        if constexpr (BN == 192) return launch_gemm_inst<BN, kEpiResidLN, false, Bf>(g);
+        if constexpr (BN == 128 || BN == 192) return launch_gemm_inst<BN, kEpiResidLN, false, Bf>(g);
         else return cudaErrorInvalidValue;
     }
   } else {

@@ -697,7 +697,8 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
   // row tile the cluster takes, and the slices exchange row statistics. The
   // producer loads each tile's residual slice (tmR) next to the operands.
   constexpr bool kLnSlices = EPI == kEpiResidLN;
-  static_assert(!kLnSlices || (BN == 192 && !S8), "LayerNorm slices are 192 bf16 columns");
+  static_assert(!kLnSlices || ((BN == 128 || BN == 192) && !S8),
+                "LayerNorm slices are 128 or 192 bf16 columns");
   using C = GemmCfg<BN, S8, kLnSlices, gemm_epi_warps<BN, EPI, S8>()>;
   // bf16 outputs leave through TMA tile stores; f32 outputs store directly.
   constexpr bool kTmaStore = sizeof(OutT) == 2;
