@@ -162,8 +162,28 @@ def run_reference(args, rank, world):
         "note": ("the reference is a pure-Go CPU library; no Go toolchain exists on this image, "
                  "so its algorithm runs as the repository's C restatement (oracle/)"),
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
+
+
+# The JSON line goes to the process's original stdout; everything else that
+# writes to file descriptor 1 (NCCL's version banner, library messages) is
+# sent to stderr so stdout carries exactly one line.
+_RESULT = None
+
+
+def emit(line: dict) -> None:
+    global _RESULT
+    if _RESULT is None:
+        _RESULT = sys.stdout
+    print(json.dumps(line), file=_RESULT, flush=True)
+
+
+def route_stdout_to_stderr() -> None:
+    global _RESULT
+    sys.stdout.flush()
+    _RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
 
 
 def main():
@@ -175,6 +195,7 @@ def main():
     ap.add_argument("--nseq", type=int, default=None, help="override sequences per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    route_stdout_to_stderr()
 
     rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
     local = env_int("LOCAL_RANK", 0)
@@ -387,7 +408,7 @@ def main():
             "clocks": clk,
             "cpu_baseline": cb,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     model.close()
     if world > 1:
         dist.destroy_process_group()
