@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <functional>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -207,6 +208,7 @@ struct DevCtx {
   float* h_out = nullptr; // pinned
   size_t h_out_cap = 0;
   cudaEvent_t meta_evt = nullptr;
+  std::vector<cudaEvent_t> out_evts;  // host-buffer calls: one per micro-batch's D2H
   std::atomic<long long> launches{0};
   // Optional per-stage profiler (CUDA events around each launch).
   bool prof_on = false;
@@ -219,6 +221,7 @@ struct DevCtx {
   ~DevCtx() {
     cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
+    for (cudaEvent_t e : out_evts) cudaEventDestroy(e);
     for (void* p : allocs) cudaFree(p);
     if (ws.base) cudaFree(ws.base);
     if (d_ids) cudaFree(d_ids);
@@ -1034,9 +1037,13 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, std::vector<MicroBat
   return FUTON_OK;
 }
 
+// after_mb (optional) runs after each micro-batch's forward is queued, with
+// the micro-batch's index and its sequences [s0, s1).
+using MbHook = std::function<int(int, int, int)>;
+
 int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* cu, int nseq,
              int out_dim, float* d_out, cudaStream_t st, volatile const int* cancel, char* err,
-             size_t errlen) {
+             size_t errlen, const MbHook& after_mb = nullptr) {
   std::vector<MicroBatch> mbs;
   int rc;
   if ((rc = plan_and_upload(d, cu, nseq, mbs, st, err, errlen))) return rc;
@@ -1044,7 +1051,8 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
   for (const MicroBatch& mb : mbs) max_t = std::max<size_t>(max_t, (size_t)(mb.t1 - mb.t0));
   if ((rc = ensure_workspace(m, d, max_t, err, errlen))) return rc;
   const int dim = out_dim ? out_dim : m.cfg.hidden_size;
-  for (const MicroBatch& mb : mbs) {
+  for (size_t i = 0; i < mbs.size(); ++i) {
+    const MicroBatch& mb = mbs[i];
     if (cancel && *cancel)
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
     const AttnPlan plan{reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
@@ -1054,6 +1062,7 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
                          mb.sum_l2, plan, out_dim, d_out + (size_t)mb.s0 * dim, st, cancel, err,
                          errlen)))
       return rc;
+    if (after_mb && (rc = after_mb((int)i, mb.s0, mb.s1))) return rc;
   }
   return FUTON_OK;
 }
@@ -1086,17 +1095,36 @@ int encode_host(futon_model* m, DevCtx& d, const int32_t* ids, const int32_t* cu
   if ((rc = ensure_dev(&d.d_out, &d.d_out_cap, (size_t)nseq * dim, err, errlen))) return rc;
   memcpy(d.h_ids, ids, T * sizeof(int));
   CU_TRY(cudaMemcpyAsync(d.d_ids, d.h_ids, T * sizeof(int), cudaMemcpyHostToDevice, d.stream));
-  rc = run_call(*m, d, d.d_ids, cu, nseq, out_dim, d.d_out, d.stream, cancel, err, errlen);
+  // Each micro-batch's vectors go to pinned memory as soon as it is done
+  // (event per micro-batch); this thread copies them out to `out` while the
+  // GPU works on the next micro-batches.
+  struct Done { int s0, s1; };
+  std::vector<Done> done;
+  auto after_mb = [&](int i, int s0, int s1) -> int {
+    while ((int)d.out_evts.size() <= i) {
+      cudaEvent_t e = nullptr;
+      CU_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      d.out_evts.push_back(e);
+    }
+    CU_TRY(cudaMemcpyAsync(d.h_out + (size_t)s0 * dim, d.d_out + (size_t)s0 * dim,
+                           (size_t)(s1 - s0) * dim * sizeof(float), cudaMemcpyDeviceToHost,
+                           d.stream));
+    CU_TRY(cudaEventRecord(d.out_evts[i], d.stream));
+    done.push_back(Done{s0, s1});
+    return FUTON_OK;
+  };
+  rc = run_call(*m, d, d.d_ids, cu, nseq, out_dim, d.d_out, d.stream, cancel, err, errlen, after_mb);
   if (rc) {
     cudaStreamSynchronize(d.stream);  // leave nothing in flight
     return rc;
   }
-  CU_TRY(cudaMemcpyAsync(d.h_out, d.d_out, (size_t)nseq * dim * sizeof(float),
-                         cudaMemcpyDeviceToHost, d.stream));
+  for (size_t i = 0; i < done.size(); ++i) {
+    CU_TRY(cudaEventSynchronize(d.out_evts[i]));
+    const size_t off = (size_t)done[i].s0 * dim, n = (size_t)(done[i].s1 - done[i].s0) * dim;
+    memcpy(out + off, d.h_out + off, n * sizeof(float));
+  }
   CU_TRY(cudaStreamSynchronize(d.stream));
-  if ((rc = read_device_error(d, err, errlen))) return rc;
-  memcpy(out, d.h_out, (size_t)nseq * dim * sizeof(float));
-  return FUTON_OK;
+  return read_device_error(d, err, errlen);
 }
 
 // ---- kernel-seam context (per CUDA device) ------------------------------

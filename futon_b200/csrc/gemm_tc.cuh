@@ -15,21 +15,25 @@
 // and, for the int8 path (native/quant.go:99-137), the exact rescale
 //   float32(sum_s32) * (scale_a[m] * scale_w[n]) + bias[n].
 //
-// Structure: one persistent CTA per SM, 10 warps.
+// Structure: one persistent CTA per SM, 2 + EW warps (EW = 8, or 16 for the
+// bf16 GELU / plain-store tiles of width 256).
 //   warp 0     TMA producer: 128-byte-swizzled K-major tiles of A (128 rows)
-//              and W (BN rows) into a STAGES-deep shared-memory ring.
+//              and W (BN rows) into a shared-memory ring whose depth is what
+//              the shared-memory budget leaves after the epilogue's buffers.
 //   warp 1     allocates tensor memory; lane 0 issues tcgen05.mma
 //              (M=128, N≤256, K=16 bf16 / 32 s8 per instruction) into one of
 //              two TMEM accumulators and commits completion to mbarriers.
-//   warps 2-9  epilogue: tcgen05.ld of the accumulator lane quarter the warp
-//              may access (one output row per thread; the two warps of a
-//              quarter split the 32-column chunks), fused math, then either
-//              a TMA tile store through a per-warp 64B-swizzled staging ring
-//              (bf16 outputs: full-sector writes, no per-thread stores) or
-//              direct vector stores (f32 outputs).
+//   warps 2-   epilogue: tcgen05.ld of the accumulator lane quarter the warp
+//              may access (one output row per thread; the EW/4 warps of a
+//              quarter split the 32-column chunks), fused math (paired f32
+//              lanes), then either a TMA tile store through a per-warp
+//              64B-swizzled staging ring (bf16 outputs: full-sector writes,
+//              no per-thread stores) or direct vector stores (f32 outputs).
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile
 // i+1. Tiles are visited n-fastest so CTAs running together share A tiles
-// through L2; the weights (≤ 19 MB) stay L2-resident.
+// through L2; the weights (≤ 19 MB) stay L2-resident. The fused LayerNorm
+// GEMMs run as clusters of hidden/192 CTAs, one 192-column slice each, which
+// exchange per-row statistics through distributed shared memory.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -475,6 +479,22 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
         sink.put(a, col0 + c, row0);
         sink.put(b, col0 + c + 32, row0);
       }
+    } else if constexpr (!rope && !S8 && BN % (32 * kParts) == 0) {
+      // The next chunk's TMEM load is in flight while this one is processed.
+      constexpr int kPer = BN / (32 * kParts);
+      uint32_t ub[2][32];
+      tmem_ld32(taddr + 32 * part, ub[0]);
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) {
+        const int c = 32 * (part + q * kParts);
+        AccCols<S8> k;
+        acc_fetch<S8>(ep, col0 + c, N, k);
+        tmem_ld_wait();
+        if (q + 1 < kPer) tmem_ld32(taddr + c + 32 * kParts, ub[(q + 1) & 1]);
+        float v[32];
+        acc_apply<S8>(ub[q & 1], a_s, ep, k, v);
+        sink.put(v, col0 + c, row0);
+      }
     } else {
 #pragma unroll 1
       for (int c = 32 * part; c < BN; c += 32 * kParts) {
@@ -572,11 +592,12 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
   const int swz = lane & 7;  // row & 7 (rows of a quarter start at multiples of 32)
   // Σv, Σv²: f32 over each 32-column chunk (paired lanes), then f64.
   double s1 = 0.0, s2 = 0.0;
+  uint32_t ub[2][32];  // chunk k + 1's TMEM load is in flight while k is processed
+  tmem_ld32(taddr + c0, ub[0]);
 #pragma unroll
   for (int k = 0; k < kChunks; ++k) {
     const int c = c0 + 32 * k;
-    uint32_t u[32];
-    tmem_ld32(taddr + c, u);
+    uint32_t (&u)[32] = ub[k & 1];
     const uint32_t sub = rrow + (uint32_t)(c / 64) * (128u * 128u);
     const int cc0 = (c % 64) / 8;
     uint32_t w[16];  // 32 residual bf16
@@ -586,6 +607,10 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
                    : "=r"(w[4 * i]), "=r"(w[4 * i + 1]), "=r"(w[4 * i + 2]), "=r"(w[4 * i + 3])
                    : "r"(sub + (uint32_t)(((cc0 + i) ^ swz) << 4)));
     tmem_ld_wait();
+    if (k + 1 < kChunks) {
+      if (k > 0) tmem_st_wait();  // that buffer was chunk k − 1's store source
+      tmem_ld32(taddr + c + 32, ub[(k + 1) & 1]);
+    }
     uint64_t a1 = 0, a2 = 0;  // (0.f, 0.f)
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -659,11 +684,13 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
   const float inv = (float)(1.0 / sqrt(var + (double)ep.eps));
   const float mf = (float)mean;
   const uint64_t nm2 = f2_pack(-mf, -mf), inv2 = f2_pack(inv, inv);
-#pragma unroll 1
-  for (int c = c0; c < c0 + kCols; c += 32) {
-    uint32_t u[32];
-    tmem_ld32(taddr + c, u);
+  tmem_ld32(taddr + c0, ub[0]);
+#pragma unroll
+  for (int k = 0; k < kChunks; ++k) {
+    const int c = c0 + 32 * k;
+    const uint32_t (&u)[32] = ub[k & 1];
     tmem_ld_wait();
+    if (k + 1 < kChunks) tmem_ld32(taddr + c + 32, ub[(k + 1) & 1]);
     float y[32];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
