@@ -8,7 +8,7 @@ pinned nomic-bert code) byte for byte, so the parity tests run where the
 reference tree is absent. Also records the oracle's vectors for the same
 cases (oracle_vectors.json) as a regression pin.
 
-Usage: python tests/golden/make_golden.py [/path/to/futon]
+Usage: python tests/golden/make_golden.py /path/to/futon-checkout
 """
 from __future__ import annotations
 
@@ -59,4 +59,6 @@ def main(ref: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/futon-checkout")
+    main(Path(sys.argv[1]))

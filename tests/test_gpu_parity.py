@@ -93,6 +93,23 @@ def test_c0_full_vs_oracle(gpu):
     print(f"c0 min cos {cs.min():.7f} mean {cs.mean():.7f}")
 
 
+@pytest.mark.parametrize("arch", ["bge", "nomic"])
+def test_f16_pack_vs_oracle(gpu, arch):
+    """Shipped packs store F16 tensors (safetensors.go:266-289; the reference
+    expands them to f32 for MatMulTF16). The library takes them as F16 over
+    the ABI; the oracle runs on their exact f32 expansion."""
+    cfg = synth.arch(arch)
+    cfg.num_layers = 3
+    w16 = {k: v.astype(np.float16) for k, v in synth.make_weights(cfg).items()}
+    m = Model(cfg, w16, devices=[0])
+    ids, cu = synth.make_inputs("c0" if arch == "bge" else "c2", nseq=12, vocab=cfg.vocab_size)
+    got = m.encode_packed(ids, cu)
+    m.close()
+    w32 = {k: v.astype(np.float32) for k, v in w16.items()}
+    want = OracleModel(cfg, w32, gemm=oracle_mode()).encode_batch(ids, cu)
+    assert_parity(got, want, f"f16 pack {arch}")
+
+
 def test_c1_subset_vs_oracle(gpu):
     cfg, w, m = synth_model("minilm6")
     ids, cu = synth.make_inputs("c1", nseq=32)
