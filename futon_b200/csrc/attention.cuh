@@ -522,7 +522,7 @@ __device__ __forceinline__ void attn_step_dispatch(int nkeys, uint32_t kS, uint3
 // CLS-pruned last layer) into row s of out. A load that does not land within
 // the wait limit sets *err (kDevTimeoutAttn) and the CTA stops.
 template <int HD, typename OutT>
-__global__ void __launch_bounds__(128, 4)
+__global__ void __launch_bounds__(128, HD == 32 ? 5 : 4)
     attn_heads_kernel(const __grid_constant__ CUtensorMap tm_qkv, int hidden, int num_heads,
                       const int* __restrict__ cu_seqlens, const AttnTile* __restrict__ tiles,
                       int cls_mode, float scale_log2, OutT* __restrict__ out, int ldo,
