@@ -28,7 +28,8 @@ cudaError_t launch_gemm_s8(const GemmLaunch& g);
 
 template <int BN, int EPI, bool S8, typename OutT>
 cudaError_t launch_gemm_inst(const GemmLaunch& g) {
-  using C = GemmCfg<BN, S8, EPI == kEpiResidLN, gemm_epi_warps<BN, EPI, S8>()>;
+  constexpr bool kLn = EPI == kEpiResidLN || EPI == kEpiResidLNG;
+  using C = GemmCfg<BN, S8, kLn, gemm_epi_warps<BN, EPI, S8>(), EPI == kEpiResidLN>;
   auto kern = gemm_tc_kernel<BN, EPI, S8, OutT>;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -43,7 +44,7 @@ cudaError_t launch_gemm_inst(const GemmLaunch& g) {
   if (kTmaStore && !g.to) return cudaErrorInvalidValue;  // bf16 outputs need an output map
   const long num_m = (g.M + C::kBM - 1) / C::kBM;
   if (num_m == 0) return cudaSuccess;
-  if constexpr (EPI == kEpiResidLN) {
+  if constexpr (kLn) {
     // Clusters of N / BN CTAs, one per column slice of a row tile.
     if (g.N % BN != 0 || g.N / BN < 2 || g.N / BN > kLnPeerSlots || !g.tr)
       return cudaErrorInvalidValue;
@@ -98,7 +99,11 @@ cudaError_t launch_gemm_bn(const GemmLaunch& g) {
         else return cudaErrorInvalidValue;
       case kEpiResid: return launch_gemm_inst<BN, kEpiResid, false, float>(g);
       case kEpiResidLN:
-        if constexpr (BN == 128 || BN == 192) return launch_gemm_inst<BN, kEpiResidLN, false, Bf>(g);
+        // Long-K GEMMs (fc2) take the global-residual variant and its extra
+        // pipeline stage; short ones (out) the TMA-loaded residual tile.
+        if constexpr (BN == 128 || BN == 192)
+          return g.K >= 1024 ? launch_gemm_inst<BN, kEpiResidLNG, false, Bf>(g)
+                             : launch_gemm_inst<BN, kEpiResidLN, false, Bf>(g);
         else return cudaErrorInvalidValue;
     }
   } else {

@@ -44,7 +44,11 @@
 namespace futon {
 
 enum EpiKind : int {
-  kEpiStore = 0, kEpiGelu = 1, kEpiSwiglu = 2, kEpiResid = 3, kEpiResidLN = 4, kEpiRope = 5
+  kEpiStore = 0, kEpiGelu = 1, kEpiSwiglu = 2, kEpiResid = 3, kEpiResidLN = 4, kEpiRope = 5,
+  // kEpiResidLN reading the residual from global memory (prefetched two
+  // chunks ahead) instead of a TMA-loaded shared tile: the freed 48 KB buy a
+  // fourth pipeline stage for long-K GEMMs (chosen by the launcher).
+  kEpiResidLNG = 6
 };
 
 struct EpiParams {
@@ -83,7 +87,7 @@ constexpr int kLnPeerSlots = 4;
 // EW: epilogue warps (a multiple of 4; EW / 4 of them share each TMEM lane
 // quarter, splitting its 32-column chunks). The stage count is what the
 // shared-memory budget leaves after the epilogue's buffers.
-template <int BN, bool S8, bool LNS = false, int EW = 8>
+template <int BN, bool S8, bool LNS = false, int EW = 8, bool RSM = true>
 struct GemmCfg {
   static constexpr int kBM = 128;
   static constexpr int kRowBytes = 128;                       // one swizzle row
@@ -107,7 +111,7 @@ struct GemmCfg {
   static constexpr int kRedBytes = LNS ? 2 * kParts * 128 * 16 : 0;
   static constexpr int kStagingBytes = LNS ? kRedBytes + kEpiWarps * 2048 : kEpiWarps * 2 * 2048;
   static constexpr int kXchBytes = LNS ? 2 * kLnPeerSlots * 128 * 16 : 0;
-  static constexpr int kResidBytes = LNS ? kBM * BN * 2 : 0;
+  static constexpr int kResidBytes = (LNS && RSM) ? kBM * BN * 2 : 0;
   static constexpr int kColsBytes = LNS ? 3 * BN * 4 : 0;
   static constexpr int kFixedBytes =
       1024 /*barriers*/ + kStagingBytes + kXchBytes + kResidBytes + kColsBytes + 1024 /*align*/;
@@ -580,12 +584,20 @@ struct LnPeers {
 // slice's bias, γ and β (shared memory, BN f32 each); `resid_done` is called
 // once the residual has been read. Returns false if a peer's sums did not
 // arrive in time.
-template <int BN, int kParts, typename Sink, typename Done>
+// Residual chunk (32 bf16 of one row) from global memory; zeros past M.
+__device__ __forceinline__ void resid_fetch(const __nv_bfloat16* p, bool ok, uint4 (&dst)[4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    dst[i] = ok ? reinterpret_cast<const uint4*>(p)[i] : make_uint4(0u, 0u, 0u, 0u);
+}
+
+template <int BN, int kParts, bool kSmemResid, typename Sink, typename Done>
 __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int row0, int M, int N,
                                                   int n0, int part, int quarter, int lane,
                                                   const EpiParams& ep, double2* red, Sink& sink,
-                                                  uint32_t rrow, uint32_t cols,
-                                                  Done&& resid_done, const LnPeers& px, int it) {
+                                                  uint32_t rrow, uint4 (&rg)[2][4],
+                                                  uint32_t cols, Done&& resid_done,
+                                                  const LnPeers& px, int it) {
   constexpr int kCols = BN / kParts, kChunks = kCols / 32;
   const bool row_ok = row < M;
   const int c0 = part * kCols;
@@ -598,14 +610,29 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
   for (int k = 0; k < kChunks; ++k) {
     const int c = c0 + 32 * k;
     uint32_t (&u)[32] = ub[k & 1];
-    const uint32_t sub = rrow + (uint32_t)(c / 64) * (128u * 128u);
-    const int cc0 = (c % 64) / 8;
     uint32_t w[16];  // 32 residual bf16
+    if constexpr (kSmemResid) {
+      const uint32_t sub = rrow + (uint32_t)(c / 64) * (128u * 128u);
+      const int cc0 = (c % 64) / 8;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(w[4 * i]), "=r"(w[4 * i + 1]), "=r"(w[4 * i + 2]), "=r"(w[4 * i + 3])
-                   : "r"(sub + (uint32_t)(((cc0 + i) ^ swz) << 4)));
+      for (int i = 0; i < 4; ++i)
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w[4 * i]), "=r"(w[4 * i + 1]), "=r"(w[4 * i + 2]), "=r"(w[4 * i + 3])
+                     : "r"(sub + (uint32_t)(((cc0 + i) ^ swz) << 4)));
+    } else {
+      // Chunks k and k + 1 were fetched ahead; fetch k + 2 into k's buffer.
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        w[4 * i] = rg[k & 1][i].x;
+        w[4 * i + 1] = rg[k & 1][i].y;
+        w[4 * i + 2] = rg[k & 1][i].z;
+        w[4 * i + 3] = rg[k & 1][i].w;
+      }
+      if (k + 2 < kChunks)
+        resid_fetch(reinterpret_cast<const __nv_bfloat16*>(ep.resid) + (size_t)row * ep.ldr + n0 +
+                        c + 64,
+                    row_ok, rg[k & 1]);
+    }
     tmem_ld_wait();
     if (k + 1 < kChunks) {
       if (k > 0) tmem_st_wait();  // that buffer was chunk k − 1's store source
@@ -723,10 +750,11 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
   // N / BN CTAs, CTA rank r of a cluster computes column slice r of every
   // row tile the cluster takes, and the slices exchange row statistics. The
   // producer loads each tile's residual slice (tmR) next to the operands.
-  constexpr bool kLnSlices = EPI == kEpiResidLN;
+  constexpr bool kLnSlices = EPI == kEpiResidLN || EPI == kEpiResidLNG;
+  constexpr bool kResidTma = EPI == kEpiResidLN;  // residual tile via TMA into shared memory
   static_assert(!kLnSlices || ((BN == 128 || BN == 192) && !S8),
                 "LayerNorm slices are 128 or 192 bf16 columns");
-  using C = GemmCfg<BN, S8, kLnSlices, gemm_epi_warps<BN, EPI, S8>()>;
+  using C = GemmCfg<BN, S8, kLnSlices, gemm_epi_warps<BN, EPI, S8>(), kResidTma>;
   // bf16 outputs leave through TMA tile stores; f32 outputs store directly.
   constexpr bool kTmaStore = sizeof(OutT) == 2;
   extern __shared__ uint8_t smem_raw[];
@@ -772,7 +800,7 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
       // One arrive per row from every other slice of the row tile.
       if (kLnSlices) mbar_init(smem_u32(&xfull_bar[a]), (uint32_t)(128 * (peers - 1)));
     }
-    if (kLnSlices) {
+    if (kResidTma) {
       mbar_init(smem_u32(rfull_bar), 1);
       mbar_init(smem_u32(rempty_bar), C::kEpiWarps);
     }
@@ -783,7 +811,7 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
     if constexpr (kTmaStore) tma_prefetch_desc(&tmO);
-    if constexpr (kLnSlices) tma_prefetch_desc(&tmR);
+    if constexpr (kResidTma) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
@@ -813,7 +841,7 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
       int issued = 0, rtiles = 0;
       for (int tile = first; tile < num_tiles; tile += stride) {
         const int mb = tile_mb(tile), nb = tile_nb(tile);
-        if constexpr (kLnSlices) {
+        if constexpr (kResidTma) {
           // The residual slice of this tile, once the epilogue has read the last one.
           if (!mbar_wait_bounded(smem_u32(rempty_bar), ((uint32_t)rtiles & 1u) ^ 1u, err,
                                  kDevTimeoutSmemEmpty, abort_flag))
@@ -842,7 +870,7 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
       }
     producer_done:
       // Drain: make sure this thread's own copies have landed before exit.
-      if (kLnSlices && rtiles > 0) {
+      if (kResidTma && rtiles > 0) {
         uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(smem_u32(rfull_bar), (uint32_t)(rtiles - 1) & 1u)) {
           if (globaltimer_ns() - t0 > kWaitLimitNs) break;
@@ -927,23 +955,34 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
       const int mb = tile_mb(tile), nb = tile_nb(tile);
       const int row0 = mb * C::kBM + quarter * 32;
       const int row = row0 + lane;
+      // Global-residual LayerNorm: the first two chunks are fetched while the
+      // tile's MMAs finish.
+      uint4 rg[2][4];
+      if constexpr (kLnSlices && !kResidTma) {
+        const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(ep.resid) +
+                                  (size_t)row * ep.ldr + nb * BN + part * (BN / C::kParts);
+        resid_fetch(rp, row < M, rg[0]);
+        resid_fetch(rp + 32, row < M, rg[1]);
+      }
       if (!mbar_wait_bounded(smem_u32(&accf_bar[acc]), acc_phase, err, kDevTimeoutAccFull,
                              abort_flag))
         break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * C::kAccStride + ((uint32_t)(quarter * 32) << 16);
       if constexpr (kLnSlices) {
-        if (!mbar_wait_bounded(smem_u32(rfull_bar), (uint32_t)it & 1u, err, kDevTimeoutTmaFull,
-                               abort_flag))
+        if (kResidTma && !mbar_wait_bounded(smem_u32(rfull_bar), (uint32_t)it & 1u, err,
+                                            kDevTimeoutTmaFull, abort_flag))
           break;
         const uint32_t rrow = smem_u32(smem + C::kResidOffset) + (uint32_t)(quarter * 32 + lane) * 128u;
         auto resid_done = [&]() {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(rempty_bar));
+          if constexpr (kResidTma) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(rempty_bar));
+          }
         };
-        if (!epilogue_resid_ln<BN, C::kParts>(taddr, row, row0, M, N, nb * BN, part, quarter, lane, ep, red,
-                                   lsink, rrow, smem_u32(smem + C::kColsOffset), resid_done, px,
-                                   it))
+        if (!epilogue_resid_ln<BN, C::kParts, kResidTma>(
+                taddr, row, row0, M, N, nb * BN, part, quarter, lane, ep, red, lsink, rrow, rg,
+                smem_u32(smem + C::kColsOffset), resid_done, px, it))
           break;
       } else if constexpr (kTmaStore) {
         epilogue_row<BN, EPI, S8, C::kParts>(taddr, row, row0, M, N, nb, part, ep, tsink);
