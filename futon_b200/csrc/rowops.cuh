@@ -114,17 +114,9 @@ __device__ __forceinline__ void warp_layernorm_store(float4 (&v)[kMaxRowVec], in
   if (xq) warp_quant_row(v, n4, lane, xq, xs);
 }
 
-// Position of packed row t within its sequence (cu non-decreasing, binary search).
-__device__ __forceinline__ int row_position(const int* cu, int nseq, int t) {
-  int lo = 0, hi = nseq;
-  while (hi - lo > 1) {
-    int mid = (lo + hi) >> 1;
-    if (cu[mid] <= t) lo = mid; else hi = mid;
-  }
-  return t - cu[lo];
-}
-
-// grid-stride over tokens, one warp per token row.
+// One warp per token row; each warp takes a contiguous run of tokens, so the
+// sequence (for the position row) is found by one binary search per run and
+// then advanced token by token.
 __global__ void __launch_bounds__(256)
     embed_ln_kernel(const int* __restrict__ ids, const int* __restrict__ cu, int nseq, int T,
                     int h, int vocab, int* __restrict__ err, const float* __restrict__ word, const float* __restrict__ type0,
@@ -135,14 +127,30 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int n4 = h >> 2;
-  for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += warps) {
+  const int per = (T + warps - 1) / warps;
+  const int t0 = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * per;
+  const int t1 = min(T, t0 + per);
+  int s = 0;
+  if (pos && t0 < t1) {
+    int lo = 0, hi = nseq;  // cu[lo] ≤ t0 < cu[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (cu[mid] <= t0) lo = mid; else hi = mid;
+    }
+    s = lo;
+  }
+  for (int t = t0; t < t1; ++t) {
     int id = ids[t];
     if ((unsigned)id >= (unsigned)vocab) {  // device-resident ids are not host-checked
       if (lane == 0) atomicCAS(err, 0, (int)kDevBadInput);
       id = 0;
     }
     const float* wr = word + (size_t)id * h;
-    const float* pr = pos ? pos + (size_t)row_position(cu, nseq, t) * h : nullptr;
+    const float* pr = nullptr;
+    if (pos) {
+      while (t >= cu[s + 1]) ++s;
+      pr = pos + (size_t)(t - cu[s]) * h;
+    }
     float4 v[kMaxRowVec];
 #pragma unroll
     for (int j = 0; j < kMaxRowVec; ++j) {

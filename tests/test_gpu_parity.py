@@ -205,6 +205,34 @@ def test_deterministic_runs(gpu):
     assert np.array_equal(a, b)
 
 
+def test_concurrent_callers(gpu):
+    """Model is safe for concurrent use (native/model.go:14-15): host threads
+    calling into one model at once get exactly their serial results (calls on
+    a device are serialised inside the library)."""
+    import threading
+    cfg, w, m = synth_model("bge")
+    batches = [synth.make_inputs("c4", nseq=64 + 16 * i, seed=20 + i) for i in range(4)]
+    want = [m.encode_packed(ids, cu) for ids, cu in batches]
+    got = [None] * len(batches)
+    errors = []
+
+    def run(i):
+        try:
+            for _ in range(3):
+                got[i] = m.encode_packed(*batches[i])
+        except Exception as e:  # surfaced below
+            errors.append(e)
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(len(batches))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for g, w_ in zip(got, want):
+        assert np.array_equal(g, w_)
+
+
 def test_encode_device_matches_host(gpu):
     import torch
     cfg, w, m = synth_model("bge")
