@@ -116,13 +116,17 @@ __device__ __forceinline__ uint32_t ex2_h2(float lo, float hi) {
   return r;
 }
 
-// grid = number of windows, block = 192. qkv: [T, 3h] (bf16 q, k; f16 v)
-// read through tm_qkv (box hd × 128, long-sequence windows) and tm_qkv16
-// (box hd × 16, packed windows).
+// Views of the [T, 3h] qkv buffer: m[n] has boxes of 16·n rows × hd columns
+// (n = 1..8), so a packed sequence of up to 16·n rows arrives in one load
+// per matrix; m[8] (128 rows) also serves the long-sequence windows.
+struct AttnMaps {
+  CUtensorMap m[9];  // m[0] unused
+};
+
+// grid = number of windows, block = 192. qkv: [T, 3h] (bf16 q, k; f16 v).
 template <int HD, typename OutT>
 __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv,
-                   const __grid_constant__ CUtensorMap tm_qkv16, int hidden, int num_heads,
+    attn_tc_kernel(const __grid_constant__ AttnMaps maps, int hidden, int num_heads,
                    const AttnWindow* __restrict__ windows, const AttnSeg* __restrict__ segs,
                    float scale_log2, OutT* __restrict__ out, int ldo, int* __restrict__ err) {
   using C = AttnTcCfg<HD>;
@@ -158,8 +162,7 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
     mbar_init(pfull_b, 4);
     mbar_init(ofull_b, 1);
     fence_barrier_init();
-    tma_prefetch_desc(&tm_qkv);
-    tma_prefetch_desc(&tm_qkv16);
+    for (int n = 1; n <= 8; ++n) tma_prefetch_desc(&maps.m[n]);
   }
   if (threadIdx.x < win.nseg) seg_sm[threadIdx.x] = segs[win.seg0 + threadIdx.x];
   // The row-sum operand: 16 rows × 128 bytes of f16 ones (layout-independent).
@@ -188,20 +191,20 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
         const int xq = head * HD, xk = hidden + head * HD, xv = 2 * hidden + head * HD;
         if (win.nseg == 0) {
           mbar_arrive_expect_tx(fb, C::kSlotBytes);
-          tma_load_2d(dst, &tm_qkv, fb, xq, win.q0);
-          tma_load_2d(dst + C::kTileBytes, &tm_qkv, fb, xk, win.k0 + 128 * j);
-          tma_load_2d(dst + 2 * C::kTileBytes, &tm_qkv, fb, xv, win.k0 + 128 * j);
+          tma_load_2d(dst, &maps.m[8], fb, xq, win.q0);
+          tma_load_2d(dst + C::kTileBytes, &maps.m[8], fb, xk, win.k0 + 128 * j);
+          tma_load_2d(dst + 2 * C::kTileBytes, &maps.m[8], fb, xv, win.k0 + 128 * j);
         } else {
-          // Rows [0, nq) in 16-row boxes, each segment from its own tokens.
+          // Rows [0, nq): each segment from its own tokens in one box of its
+          // 16-rounded length.
           mbar_arrive_expect_tx(fb, 3 * win.nq * C::kRowBytes);
           for (int sg = 0; sg < win.nseg; ++sg) {
             const AttnSeg sq = seg_sm[sg];
-            for (int m = 0; m < sq.len; m += 16) {
-              const uint32_t o = (uint32_t)(sq.row + m) * C::kRowBytes;
-              tma_load_2d(dst + o, &tm_qkv16, fb, xq, sq.t0 + m);
-              tma_load_2d(dst + C::kTileBytes + o, &tm_qkv16, fb, xk, sq.t0 + m);
-              tma_load_2d(dst + 2 * C::kTileBytes + o, &tm_qkv16, fb, xv, sq.t0 + m);
-            }
+            const CUtensorMap* mp = &maps.m[(sq.len + 15) >> 4];
+            const uint32_t o = (uint32_t)sq.row * C::kRowBytes;
+            tma_load_2d(dst + o, mp, fb, xq, sq.t0);
+            tma_load_2d(dst + C::kTileBytes + o, mp, fb, xk, sq.t0);
+            tma_load_2d(dst + 2 * C::kTileBytes + o, mp, fb, xv, sq.t0);
           }
         }
       }

@@ -653,14 +653,14 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
     if (kAttnTcgen05 && tc_hd && !cls_only) {
       if (plan.nwin == 0) return FUTON_OK;
       // q, k, v tiles of one head: 128 rows × hd columns, swizzled over one row.
-      CUtensorMap tm, tm16;
-      if (!make_qkv_map(&tm, qkv, (uint64_t)T, (uint64_t)(3 * h), hd, 128) ||
-          !make_qkv_map(&tm16, qkv, (uint64_t)T, (uint64_t)(3 * h), hd, 16))
-        return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
+      AttnMaps maps{};
+      for (int n = 1; n <= 8; ++n)
+        if (!make_qkv_map(&maps.m[n], qkv, (uint64_t)T, (uint64_t)(3 * h), hd, 16u * n))
+          return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
       auto launch = [&](auto kern, int smem) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        kern<<<plan.nwin, 192, smem, st>>>(tm, tm16, h, H, plan.wins, plan.segs, scale_log2, out,
+        kern<<<plan.nwin, 192, smem, st>>>(maps, h, H, plan.wins, plan.segs, scale_log2, out,
                                            h, d.err_word);
         return cudaGetLastError();
       };
