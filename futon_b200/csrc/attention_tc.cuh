@@ -26,7 +26,9 @@
 //                        normalised O row of each head to global memory
 //
 // Probability precision matches the mma.sync kernel: exponents rounded to
-// f16 before ex2.approx.f16x2, P and V in f16, f32 accumulation.
+// f16 before ex2.approx.f16x2, P and V in f16, f32 accumulation. Packed
+// windows fold the sequence mask into S = Q·Kᵀ as an extra K = 16 step
+// (exact zeros inside a sequence), so the softmax never tests key indices.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -54,18 +56,26 @@ struct AttnWindow {
   int seg0, nseg;
 };
 
+struct AttnMaps {
+  CUtensorMap m[9];  // m[n]: boxes of 16·n rows × hd columns
+};
+
 template <int HD>
 struct AttnTcCfg {
   static constexpr int kRowBytes = HD * 2;
   static constexpr int kTileBytes = 128 * kRowBytes;       // one q, k or v tile
   static constexpr int kSlotBytes = 3 * kTileBytes;
-  static constexpr int kSlots = 3;
+  static constexpr int kSlots = 2;
   static constexpr int kPOffset = kSlots * kSlotBytes;     // multiple of 1024
-  static constexpr int kMaxSegs = 8;                       // 128 rows / 16-row alignment
   static constexpr int kPBytes = 2 * 128 * 128;            // two 64-key regions, 128 B rows
   static constexpr int kOnesOffset = kPOffset + kPBytes;
   static constexpr int kOnesBytes = 16 * 128;              // B operand of the row sums
-  static constexpr int kBarOffset = kOnesOffset + kOnesBytes;
+  // Packed windows: the sequence mask as one more K = 16 step of S = Q·Kᵀ —
+  // row r of the q side holds onehot(segment(r)), row k of the k side holds
+  // −30000·(1 − onehot(segment(k))), both bf16 in 64-byte swizzled rows.
+  static constexpr int kAugOffset = kOnesOffset + 2048;    // 1024-aligned
+  static constexpr int kAugBytes = 2 * 128 * 64;
+  static constexpr int kBarOffset = kAugOffset + kAugBytes;
   static constexpr int kBytes = kBarOffset + 128 + 1024;   // + barriers + alignment slack
   static constexpr uint32_t kTmemCols = 256;
   static constexpr uint32_t kColO = 128;                   // S: columns 0-127
@@ -116,14 +126,9 @@ __device__ __forceinline__ uint32_t ex2_h2(float lo, float hi) {
   return r;
 }
 
-// Views of the [T, 3h] qkv buffer: m[n] has boxes of 16·n rows × hd columns
-// (n = 1..8), so a packed sequence of up to 16·n rows arrives in one load
-// per matrix; m[8] (128 rows) also serves the long-sequence windows.
-struct AttnMaps {
-  CUtensorMap m[9];  // m[0] unused
-};
-
-// grid = number of windows, block = 192. qkv: [T, 3h] (bf16 q, k; f16 v).
+// grid = number of windows, block = 192. qkv: [T, 3h] (bf16 q, k; f16 v)
+// read through tm_qkv (box hd × 128, long-sequence windows) and tm_qkv16
+// (box hd × 16, packed windows).
 template <int HD, typename OutT>
 __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
     attn_tc_kernel(const __grid_constant__ AttnMaps maps, int hidden, int num_heads,
@@ -134,26 +139,26 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
   const uint32_t sbase = (smem_u32(sm_raw) + 1023u) & ~1023u;
   const uint32_t sP = sbase + C::kPOffset;
   const uint32_t sOnes = sbase + C::kOnesOffset;
+  const uint32_t sQa = sbase + C::kAugOffset, sKa = sQa + 128 * 64;
   const uint32_t bars = sbase + C::kBarOffset;
-  constexpr int kS = C::kSlots;
-  const uint32_t full_b = bars;            // [kSlots] TMA → MMA
-  const uint32_t empty_b = bars + 8 * kS;  // [kSlots] MMA → TMA
-  const uint32_t sfull_b = bars + 16 * kS; // S ready (MMA → softmax)
-  const uint32_t sfree_b = sfull_b + 8;    // S read (softmax → MMA)
-  const uint32_t pfull_b = sfull_b + 16;   // P written, O corrected (softmax → MMA)
-  const uint32_t ofull_b = sfull_b + 24;   // P·V done (MMA → softmax)
+  const uint32_t full_b = bars;            // [2] TMA → MMA
+  const uint32_t empty_b = bars + 16;      // [2] MMA → TMA
+  const uint32_t sfull_b = bars + 32;      // S ready (MMA → softmax)
+  const uint32_t sfree_b = bars + 40;      // S read (softmax → MMA)
+  const uint32_t pfull_b = bars + 48;      // P written, O corrected (softmax → MMA)
+  const uint32_t ofull_b = bars + 56;      // P·V done (MMA → softmax)
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
-  __shared__ AttnSeg seg_sm[C::kMaxSegs];  // the window's segments
 
   const AttnWindow win = windows[blockIdx.x];
+  const bool packed = win.nseg > 0;
   const int nkb = (win.nk + 127) / 128;    // key blocks per head
   const int units = num_heads * nkb;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int i = 0; i < kS; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(full_b + 8 * i, 1);
       mbar_init(empty_b + 8 * i, 1);
     }
@@ -164,10 +169,50 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
     fence_barrier_init();
     for (int n = 1; n <= 8; ++n) tma_prefetch_desc(&maps.m[n]);
   }
-  if (threadIdx.x < win.nseg) seg_sm[threadIdx.x] = segs[win.seg0 + threadIdx.x];
   // The row-sum operand: 16 rows × 128 bytes of f16 ones (layout-independent).
   for (int i = threadIdx.x; i < C::kOnesBytes / 16; i += blockDim.x)
     st_shared_v4(sOnes + 16 * i, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+
+  // Softmax thread = query row r: its token (−1: padding row) and, for
+  // packed windows, its segment's rows [klo, khi) and the mask rows.
+  const int r = warp * 32 + lane;
+  int tok = -1, klo = 0, khi = 0;
+  if (warp < 4) {
+    int sidx = -1;
+    if (!packed) {
+      if (r < win.nq) {
+        tok = win.q0 + r;
+        khi = win.nk;
+      }
+    } else {
+      for (int sg = 0; sg < win.nseg; ++sg) {
+        const AttnSeg sq = segs[win.seg0 + sg];
+        if (r >= sq.row && r < sq.row + sq.len) {
+          tok = sq.t0 + (r - sq.row);
+          klo = sq.row;
+          khi = sq.row + sq.len;
+          sidx = sg;
+        }
+      }
+      // q side: onehot(segment); k side: −30000 off the own segment (bf16
+      // 0xC6EA = −29952), so S gains 0 inside a sequence and about −3e4
+      // across sequences or on padding keys.
+      uint32_t qa[8], ka[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t lo = (2 * i == sidx) ? 0x3F80u : 0u, hi = (2 * i + 1 == sidx) ? 0x3F80u : 0u;
+        qa[i] = lo | (hi << 16);
+        const uint32_t klo16 = (2 * i == sidx) ? 0u : 0xC6EAu;
+        const uint32_t khi16 = (2 * i + 1 == sidx) ? 0u : 0xC6EAu;
+        ka[i] = klo16 | (khi16 << 16);
+      }
+      const int sw = (r >> 1) & 3;  // 64-byte swizzle: 16-byte chunk c at c ^ sw
+      st_shared_v4(sQa + r * 64 + ((0 ^ sw) << 4), qa[0], qa[1], qa[2], qa[3]);
+      st_shared_v4(sQa + r * 64 + ((1 ^ sw) << 4), qa[4], qa[5], qa[6], qa[7]);
+      st_shared_v4(sKa + r * 64 + ((0 ^ sw) << 4), ka[0], ka[1], ka[2], ka[3]);
+      st_shared_v4(sKa + r * 64 + ((1 ^ sw) << 4), ka[4], ka[5], ka[6], ka[7]);
+    }
+  }
   fence_proxy_async_smem();
   if (warp == 5) {
     tmem_alloc(smem_u32(&tmem_slot), C::kTmemCols);
@@ -182,24 +227,23 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       for (int u = 0; u < units; ++u) {
-        const int head = u / nkb, j = u % nkb, slot = u % kS;
-        if (u >= kS && !mbar_wait_bounded(empty_b + 8 * slot, ((u / kS) - 1) & 1, err,
-                                          kDevTimeoutAttn, &abort_flag))
+        const int head = u / nkb, j = u % nkb, slot = u & 1;
+        if (u >= 2 && !mbar_wait_bounded(empty_b + 8 * slot, ((u >> 1) - 1) & 1, err,
+                                         kDevTimeoutAttn, &abort_flag))
           break;
         const uint32_t fb = full_b + 8 * slot;
         const uint32_t dst = sbase + slot * C::kSlotBytes;
         const int xq = head * HD, xk = hidden + head * HD, xv = 2 * hidden + head * HD;
-        if (win.nseg == 0) {
+        if (!packed) {
           mbar_arrive_expect_tx(fb, C::kSlotBytes);
           tma_load_2d(dst, &maps.m[8], fb, xq, win.q0);
           tma_load_2d(dst + C::kTileBytes, &maps.m[8], fb, xk, win.k0 + 128 * j);
           tma_load_2d(dst + 2 * C::kTileBytes, &maps.m[8], fb, xv, win.k0 + 128 * j);
         } else {
-          // Rows [0, nq): each segment from its own tokens in one box of its
-          // 16-rounded length.
+          // Rows [0, nq) in 16-row boxes, each segment from its own tokens.
           mbar_arrive_expect_tx(fb, 3 * win.nq * C::kRowBytes);
           for (int sg = 0; sg < win.nseg; ++sg) {
-            const AttnSeg sq = seg_sm[sg];
+            const AttnSeg sq = segs[win.seg0 + sg];
             const CUtensorMap* mp = &maps.m[(sq.len + 15) >> 4];
             const uint32_t o = (uint32_t)sq.row * C::kRowBytes;
             tma_load_2d(dst + o, mp, fb, xq, sq.t0);
@@ -214,8 +258,8 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
       // ---------------- MMA issuer ----------------
       auto keys16 = [&](int j) { return (min(128, win.nk - 128 * j) + 15) & ~15; };
       auto issue_s = [&](int u) -> bool {
-        const int slot = u % kS;
-        if (!mbar_wait_bounded(full_b + 8 * slot, (u / kS) & 1, err, kDevTimeoutAttn, &abort_flag))
+        const int slot = u & 1;
+        if (!mbar_wait_bounded(full_b + 8 * slot, (u >> 1) & 1, err, kDevTimeoutAttn, &abort_flag))
           return false;
         tc_fence_after();
         const uint32_t q = sbase + slot * C::kSlotBytes, k = q + C::kTileBytes;
@@ -225,6 +269,7 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
         for (int ks = 0; ks < HD / 16; ++ks)
           mma_bf16(tmem, desc_rows<HD>(q) + 2 * ks, desc_rows<HD>(k) + 2 * ks, idesc,
                    ks ? 1u : 0u);
+        if (packed) mma_bf16(tmem, desc_rows<32>(sQa), desc_rows<32>(sKa), idesc, 1u);
         mma_commit(sfull_b);
         return true;
       };
@@ -237,7 +282,7 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
         if (u + 1 < units && !issue_s(u + 1)) break;
         if (!mbar_wait_bounded(pfull_b, u & 1, err, kDevTimeoutAttn, &abort_flag)) break;
         tc_fence_after();
-        const int j = u % nkb, slot = u % kS;
+        const int j = u % nkb, slot = u & 1;
         const uint32_t v = sbase + slot * C::kSlotBytes + 2 * C::kTileBytes;
         const int nks = keys16(j) / 16;
         for (int ks = 0; ks < nks; ++ks) {
@@ -252,33 +297,21 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
     }
   } else {
     // ---------------- softmax warps 0-3: thread = query row ----------------
-    const int r = warp * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    // This row's token (−1: padding) and its valid key rows [klo, khi):
-    // relative to the window for packed windows, to the sequence start for
-    // long ones.
-    int tok = -1, klo = 0, khi = 0;
-    if (win.nseg == 0) {
-      if (r < win.nq) {
-        tok = win.q0 + r;
-        khi = win.nk;
-      }
-    } else {
-      for (int sg = 0; sg < win.nseg; ++sg) {
-        const AttnSeg sq = seg_sm[sg];
-        if (r >= sq.row && r < sq.row + sq.len) {
-          tok = sq.t0 + (r - sq.row);
-          klo = sq.row;
-          khi = sq.row + sq.len;
-        }
-      }
-    }
     const uint32_t prow = sP + (uint32_t)r * 128u;
     const int swz = r & 7;
+    // 32-key chunks any row of this warp needs (packed windows: its rows'
+    // segments; long windows: the whole block); other chunks of P are zero.
+    int clo = tok >= 0 ? klo >> 5 : 4, chi = tok >= 0 ? (khi + 31) >> 5 : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      clo = min(clo, __shfl_xor_sync(0xffffffffu, clo, o));
+      chi = max(chi, __shfl_xor_sync(0xffffffffu, chi, o));
+    }
     float m_run = -INFINITY;
     bool ok = true;
 
-    // Normalised O row of `head` to global memory (rows inside the window).
+    // Normalised O row of `head` to global memory.
     auto store_head = [&](int head) {
       uint32_t ov[HD];
 #pragma unroll
@@ -307,61 +340,46 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
       const int head = u / nkb, j = u % nkb;
       if (j == 0) m_run = -INFINITY;  // a new head
       const int nkeys = min(128, win.nk - 128 * j);
-      const int nchunk = (((nkeys + 15) & ~15) + 31) / 32;  // 32-key chunks the MMA reads
-      // Valid keys of this row in the block: [lo, hi).
-      const int lo = max(klo - 128 * j, 0), hi = min(khi - 128 * j, nkeys);
-      const bool any = tok >= 0 && hi > lo;
-      // Chunks any row of the warp needs; the rest of [0, nchunk) is zero.
-      int clo = any ? lo >> 5 : 4, chi = any ? (hi + 31) >> 5 : 0;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        clo = min(clo, __shfl_xor_sync(0xffffffffu, clo, o));
-        chi = max(chi, __shfl_xor_sync(0xffffffffu, chi, o));
-      }
+      const int nchunk = (((nkeys + 15) & ~15) + 31) / 32;  // chunks the P·V MMAs read
+      const int c0 = packed ? clo : 0;
+      const int c1 = packed ? chi : (nkeys + 31) >> 5;
       if (!mbar_wait_bounded(sfull_b, u & 1, err, kDevTimeoutAttn, &abort_flag)) { ok = false; break; }
       tc_fence_after();
-      // Pass 1: the row maximum over valid keys.
-      float mx = -INFINITY;
-      for (int c = clo; c < chi; ++c) {
-        uint32_t t[32];
-        tmem_ld32(trow + 32 * c, t);
-        tmem_ld_wait();
+      // The row's scores of the live chunks, one TMEM wait for all.
+      uint32_t sv[4][32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = 32 * c + i;
-          if (key >= lo && key < hi) mx = fmaxf(mx, __uint_as_float(t[i]));
-        }
-      }
-      const float m_new = fmaxf(m_run, mx);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;  // rows without keys: P = 0
-      const float alpha = ex2_approx((m_run == -INFINITY ? m_use : m_run) * scale_log2 -
-                                     m_use * scale_log2);
-      m_run = m_new;
-      // Pass 2: P = 2^(s·c − m·c) in f16 (0 for masked keys), kept in registers
-      // until the previous unit's P·V has released the P tile.
-      uint32_t pw[4][16];
-      const float ms = m_use * scale_log2;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (c >= clo && c < chi) {
-          uint32_t t[32];
-          tmem_ld32(trow + 32 * c, t);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int k0 = 32 * c + 2 * i;
-            const float a = (k0 >= lo && k0 < hi) ? fmaf(__uint_as_float(t[2 * i]), scale_log2, -ms)
-                                                 : -INFINITY;
-            const float b = (k0 + 1 >= lo && k0 + 1 < hi)
-                                ? fmaf(__uint_as_float(t[2 * i + 1]), scale_log2, -ms)
-                                : -INFINITY;
-            pw[c][i] = ex2_h2(a, b);
-          }
-        }
-      }
+      for (int c = 0; c < 4; ++c)
+        if (c >= c0 && c < c1) tmem_ld32(trow + 32 * c, sv[c]);
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(sfree_b);
+      // Long windows: keys past the sequence in the last block (the same for
+      // every row) leave the softmax.
+      if (nkeys & 31) {
+        const int c = (nkeys - 1) >> 5;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          if (cc == c) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * cc + i >= nkeys) sv[cc][i] = __float_as_uint(-INFINITY);
+          }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c >= c0 && c < c1) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            mx = fmax3(mx, __uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1]));
+        }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;  // rows without keys: P = 0
+      const float alpha = ex2_approx(((m_run == -INFINITY ? m_use : m_run) - m_use) * scale_log2);
+      m_run = m_new;
+      const float ms = m_use * scale_log2;
+      const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nms2 = f2_pack(-ms, -ms);
       if (u > 0) {
         // The previous unit's P·V has finished: P may be overwritten, and O
         // holds either a finished head (store it) or this head's running sum.
@@ -385,19 +403,31 @@ __global__ void __launch_bounds__(192, HD == 32 ? 2 : 1)
           tmem_st_wait();
         }
       }
-      // P row → the 128-byte-swizzled K-major tile (keys 0-63 | 64-127).
+      // P = 2^(s·c − m·c) in f16 → the 128-byte-swizzled K-major tile
+      // (keys 0-63 | 64-127); chunks no row of the warp needs are zero.
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         if (c < nchunk) {
           const uint32_t base = prow + (uint32_t)(c >> 1) * 16384u;
-          const bool live = c >= clo && c < chi;
+          if (c >= c0 && c < c1) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t addr = base + (uint32_t)((((c & 1) * 4 + i) ^ swz) << 4);
-            if (live)
-              st_shared_v4(addr, pw[c][4 * i], pw[c][4 * i + 1], pw[c][4 * i + 2], pw[c][4 * i + 3]);
-            else
-              st_shared_v4(addr, 0u, 0u, 0u, 0u);
+            for (int i = 0; i < 4; ++i) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int k = 8 * i + 2 * e;
+                float a, b;
+                f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[c][k]), __uint_as_float(sv[c][k + 1])),
+                                 sl2, nms2),
+                          a, b);
+                w[e] = ex2_h2(a, b);
+              }
+              st_shared_v4(base + (uint32_t)((((c & 1) * 4 + i) ^ swz) << 4), w[0], w[1], w[2], w[3]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              st_shared_v4(base + (uint32_t)((((c & 1) * 4 + i) ^ swz) << 4), 0u, 0u, 0u, 0u);
           }
         }
       }

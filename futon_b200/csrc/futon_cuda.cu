@@ -618,10 +618,9 @@ inline int grid_rows(int rows, int per_block, int sms) {
 }
 
 // ---- attention dispatch --------------------------------------------------
-// attn_tc_kernel (tcgen05, packed 128-row windows) is parity-correct but, as
-// measured on the c4 workload, 1.9× slower than attn_heads_kernel: each CTA
-// runs its heads' S → softmax → P·V chain one unit at a time and the SM sits
-// on the latencies. It stays off until that chain is pipelined.
+// attn_tc_kernel (tcgen05, packed 128-row windows) is parity-correct and
+// batch-invariant but, as measured on the c4 workload, 1.5× slower than
+// attn_heads_kernel; it stays off until it is the faster one.
 constexpr bool kAttnTcgen05 = false;
 
 // A micro-batch's attention work lists (device memory): 64-query tiles per
