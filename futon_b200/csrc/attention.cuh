@@ -11,8 +11,9 @@
 //
 // Kernels:
 //   attn_heads_kernel  one 64-query tile of one sequence per CTA, all heads
-//                      in turn, 64-key tiles staged by cp.async in a two-slot
-//                      ring, m16n8k16 tensor-core MMAs with f32 accumulation
+//                      in turn (two per step for head_dim 32), 64-key tiles
+//                      staged by TMA in a two-slot mbarrier ring, m16n8k16
+//                      tensor-core MMAs with f32 accumulation
 //                      (Q·Kᵀ in bf16, P·V in f16 — v is stored as f16) and
 //                      online softmax (head_dim 32 or 64); also the CLS-only
 //                      last layer (model.go:403-410).
@@ -288,33 +289,40 @@ __device__ __forceinline__ void stage_async(__nv_bfloat16* dst, const __nv_bfloa
 }
 
 // ---------------------------------------------------------------------------
-// attn_heads_kernel staging. Per (head, 64-key tile) step one thread loads
-// q (first tile of a head), k and v as 64 × HD tiles of the [T, 3h] qkv
-// buffer with TMA into a kAttnRing-slot shared-memory ring; each slot's
-// mbarrier completes when its bytes land, so the next step's loads overlap
-// this step's tensor-core work. Tiles are dense with the TMA swizzle whose
-// span is one row (64 B for HD 32, 128 B for HD 64), which keeps every
-// ldmatrix phase (8 rows × 16 B) free of bank conflicts.
+// attn_heads_kernel staging. Per (head group, 64-key tile) step one thread
+// loads q (first tile of a group), k and v as 64 × (NH·HD) tiles of the
+// [T, 3h] qkv buffer with TMA into a kAttnRing-slot shared-memory ring; each
+// slot's mbarrier completes when its bytes land, so the next step's loads
+// overlap this step's tensor-core work. Tiles are dense with the TMA swizzle
+// whose span is one row (64 B for 32 columns, 128 B for 64), which keeps
+// every ldmatrix phase (8 rows × 16 B) free of bank conflicts.
 // ---------------------------------------------------------------------------
 constexpr int kAttnRing = 2;
 
-template <int HD>
+template <int W>  // tile width in elements (head_dim × heads per step)
 struct AttnSmem {
-  static constexpr int kRowBytes = HD * 2;
+  static constexpr int kRowBytes = W * 2;
   static constexpr int kTileBytes = 64 * kRowBytes;
   static constexpr int kBarOffset = 3 * kAttnRing * kTileBytes;
   static constexpr int kBytes = kBarOffset + 64 + 1024;  // + barriers + alignment slack
 };
 
-template <int HD>
-constexpr int attn_heads_smem_bytes() { return AttnSmem<HD>::kBytes; }
+// Heads per (key tile) step: two for head_dim 32 (one 64-column TMA box
+// holds both, so every barrier, wait and load serves twice the work), else one.
+__host__ __device__ constexpr int attn_heads_per_step(int hd, int num_heads) {
+  return hd == 32 && num_heads % 2 == 0 ? 2 : 1;
+}
 
-// The swizzle's XOR term for a tile row: 16-byte chunk c of row r sits at
-// chunk c ^ attn_swz(r). Every fragment row used below is a lane-dependent
-// row plus a multiple of 8, which leaves the term unchanged.
-template <int HD>
+template <int HD, int NH>
+constexpr int attn_heads_smem_bytes() { return AttnSmem<HD * NH>::kBytes; }
+
+// The swizzle's XOR term for a tile row of RB bytes (64-byte swizzle for
+// 64-byte rows, 128-byte swizzle for 128-byte rows): 16-byte chunk c of row r
+// sits at chunk c ^ attn_swz(r). Every fragment row used below is a
+// lane-dependent row plus a multiple of 8, which leaves the term unchanged.
+template <int RB>
 __device__ __forceinline__ int attn_swz(int r) {
-  return HD == 32 ? (r >> 1) & 3 : r & 7;
+  return RB == 64 ? (r >> 1) & 3 : r & 7;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -372,32 +380,32 @@ __device__ __forceinline__ uint32_t ex2_f16x2(float lo, float hi) {
 // O += P V with P and V in f16. The softmax denominators come out of the
 // same MMAs: a ninth (fifth) B block of ones sums each row of P exactly as
 // it is multiplied. FIRST: the head's first key tile (no rescale of O).
-// Per-lane byte offsets of the ldmatrix rows inside a swizzled 64 × HD tile:
+// Per-lane byte offsets of the ldmatrix rows of head e inside a swizzled
+// 64-row tile of RB-byte rows (head e holds 16-byte chunks e·HD/8 onward):
 // k_off[i] for key chunks 4i..4i+3 (x4: rows nb·8 + lane%8), v_off[i] for
 // value columns 16i..16i+15 (x4.trans: rows kc·16 + lane%16).
-template <int HD>
+template <int HD, int RB>
 struct AttnLane {
   uint32_t k_off[HD / 32];
   uint32_t v_off[HD / 16];
-  __device__ __forceinline__ explicit AttnLane(int lane) {
-    constexpr int RB = HD * 2;
-    const int kr = lane & 7, vr = lane & 15;
+  AttnLane() = default;
+  __device__ __forceinline__ AttnLane(int lane, int e) {
+    const int kr = lane & 7, vr = lane & 15, c0 = e * (HD / 8);
 #pragma unroll
     for (int i = 0; i < HD / 32; ++i)
-      k_off[i] = kr * RB + ((((lane >> 3) + 4 * i) ^ attn_swz<HD>(kr)) << 4);
+      k_off[i] = kr * RB + (((c0 + (lane >> 3) + 4 * i) ^ attn_swz<RB>(kr)) << 4);
 #pragma unroll
     for (int i = 0; i < HD / 16; ++i)
-      v_off[i] = vr * RB + ((((lane >> 4) + 2 * i) ^ attn_swz<HD>(vr)) << 4);
+      v_off[i] = vr * RB + (((c0 + (lane >> 4) + 2 * i) ^ attn_swz<RB>(vr)) << 4);
   }
 };
 
-template <int HD, int NBLK, bool PARTIAL, bool FIRST>
-__device__ __forceinline__ void attn_step(uint32_t kS, uint32_t vS, const AttnLane<HD>& al,
+template <int HD, int RB, int NBLK, bool PARTIAL, bool FIRST>
+__device__ __forceinline__ void attn_step(uint32_t kS, uint32_t vS, const AttnLane<HD, RB>& al,
                                           int lane, int nkeys, float scale_log2,
                                           const uint32_t (&qf)[HD / 16][4],
                                           float (&o)[HD / 8][4], float (&m_run)[2],
                                           float (&lsum)[4]) {
-  constexpr int RB = HD * 2;
   float sc[NBLK][4];
 #pragma unroll
   for (int nb = 0; nb < NBLK; ++nb) {
@@ -487,21 +495,29 @@ __device__ __forceinline__ void attn_step(uint32_t kS, uint32_t vS, const AttnLa
   }
 }
 
-template <int HD, bool FIRST>
+// One key tile of the NH heads held by a tile row block: the 8-key block
+// count is resolved once, then each head's step runs in the same basic
+// block (independent chains the scheduler can interleave).
+template <int HD, int RB, int NH, bool FIRST>
 __device__ __forceinline__ void attn_step_dispatch(int nkeys, uint32_t kS, uint32_t vS,
-                                                   const AttnLane<HD>& al, int lane,
+                                                   const AttnLane<HD, RB> (&al)[NH], int lane,
                                                    float scale_log2,
-                                                   const uint32_t (&qf)[HD / 16][4],
-                                                   float (&o)[HD / 8][4], float (&m)[2],
-                                                   float (&l)[4]) {
+                                                   const uint32_t (&qf)[NH][HD / 16][4],
+                                                   float (&o)[NH][HD / 8][4], float (&m)[NH][2],
+                                                   float (&l)[NH][4]) {
   const int nblk = (nkeys + 7) >> 3;
   const bool partial = (nkeys & 7) != 0;
-#define FUTON_STEP(NB)                                                                 \
-  case NB:                                                                             \
-    if (partial)                                                                       \
-      attn_step<HD, NB, true, FIRST>(kS, vS, al, lane, nkeys, scale_log2, qf, o, m, l);  \
-    else                                                                               \
-      attn_step<HD, NB, false, FIRST>(kS, vS, al, lane, nkeys, scale_log2, qf, o, m, l); \
+#define FUTON_STEP(NB)                                                                      \
+  case NB:                                                                                  \
+    if (partial) {                                                                          \
+      _Pragma("unroll") for (int e = 0; e < NH; ++e)                                        \
+        attn_step<HD, RB, NB, true, FIRST>(kS, vS, al[e], lane, nkeys, scale_log2, qf[e],    \
+                                           o[e], m[e], l[e]);                               \
+    } else {                                                                                \
+      _Pragma("unroll") for (int e = 0; e < NH; ++e)                                        \
+        attn_step<HD, RB, NB, false, FIRST>(kS, vS, al[e], lane, nkeys, scale_log2, qf[e],   \
+                                            o[e], m[e], l[e]);                              \
+    }                                                                                       \
     break;
   switch (nblk) {
     FUTON_STEP(1) FUTON_STEP(2) FUTON_STEP(3) FUTON_STEP(4)
@@ -511,27 +527,36 @@ __device__ __forceinline__ void attn_step_dispatch(int nkeys, uint32_t kS, uint3
 }
 
 // grid = ntiles (or nseq in cls_mode), block = 128 (4 warps × 16 query rows).
-// One CTA per 64-query tile of one sequence, looping over every head; q, k,
-// v arrive pre-rotated (RoPE runs in the qkv GEMM epilogue). Work stops where
-// a sequence ends: warps whose 16 query rows all lie past the sequence idle,
-// and a step multiplies only the 8-key blocks that hold keys (most benchmark
-// sequences are shorter than one 64 × 64 tile). Tile rows past the sequence
-// hold the next sequence's (finite) values or TMA's zero fill past T: their
-// keys are masked, their probabilities are 0 and their query rows are not
-// stored. cls_mode: CTA s computes only query row 0 of sequence s (the
-// CLS-pruned last layer) into row s of out. A load that does not land within
-// the wait limit sets *err (kDevTimeoutAttn) and the CTA stops.
-template <int HD, typename OutT>
-__global__ void __launch_bounds__(128, HD == 32 ? 5 : 4)
+// One CTA per 64-query tile of one sequence, looping over every head, NH
+// heads per step (their q, k, v columns are adjacent in qkv, so one TMA box
+// of NH·HD columns carries them); q, k, v arrive pre-rotated (RoPE runs in
+// the qkv GEMM epilogue). Work stops where a sequence ends: warps whose 16
+// query rows all lie past the sequence idle, and a step multiplies only the
+// 8-key blocks that hold keys (most benchmark sequences are shorter than one
+// 64 × 64 tile). Tile rows past the sequence hold the next sequence's
+// (finite) values or TMA's zero fill past T: their keys are masked, their
+// probabilities are 0 and their query rows are not stored. cls_mode: CTA s
+// computes only query row 0 of sequence s (the CLS-pruned last layer) into
+// row s of out. A load that does not land within the wait limit sets *err
+// (kDevTimeoutAttn) and the CTA stops.
+// CTAs per SM the register budget is cut for. Measured on the bge shape:
+// two heads per step at 3 CTAs (168 registers) beat one head at 5 (96) by
+// 2 %, and two heads at 4 (128, with spills) or one head at 6-8 were slower.
+template <int HD, int NH>
+constexpr int attn_heads_min_ctas() { return NH == 2 ? 3 : HD == 32 ? 5 : 4; }
+
+template <int HD, int NH, typename OutT>
+__global__ void __launch_bounds__(128, attn_heads_min_ctas<HD, NH>())
     attn_heads_kernel(const __grid_constant__ CUtensorMap tm_qkv, int hidden, int num_heads,
                       const int* __restrict__ cu_seqlens, const AttnTile* __restrict__ tiles,
                       int cls_mode, float scale_log2, OutT* __restrict__ out, int ldo,
                       int* __restrict__ err) {
-  using SM = AttnSmem<HD>;
+  constexpr int W = HD * NH;  // tile width in elements
+  using SM = AttnSmem<W>;
   constexpr int RB = SM::kRowBytes, kTile = SM::kTileBytes;
   extern __shared__ uint8_t sm_raw[];
   const uint32_t sbase = (smem_u32(sm_raw) + 1023u) & ~1023u;
-  const uint32_t sQ = sbase;                              // slot = head % ring
+  const uint32_t sQ = sbase;                              // slot = head group % ring
   const uint32_t sK = sbase + kAttnRing * kTile;          // slot = step % ring
   const uint32_t sV = sbase + 2 * kAttnRing * kTile;
   const uint32_t full = sbase + SM::kBarOffset;           // kAttnRing mbarriers
@@ -542,6 +567,7 @@ __global__ void __launch_bounds__(128, HD == 32 ? 5 : 4)
   const int L = cu_seqlens[tile.seq + 1] - s0;
   const int qlim = cls_mode ? 1 : L;  // query positions < qlim are real
   const int nkv = (L + 63) / 64;
+  const int ngroups = num_heads / NH;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool warp_active = tile.q0 + warp * 16 < qlim;
 
@@ -554,33 +580,35 @@ __global__ void __launch_bounds__(128, HD == 32 ? 5 : 4)
   }
   __syncthreads();
 
-  // Next (head, key tile) to load (thread 0 only).
-  int nh = 0, nj = 0, issued = 0;
+  // Next (head group, key tile) to load (thread 0 only).
+  int ng = 0, nj = 0, issued = 0;
   auto issue_next = [&]() {
-    if (nh >= num_heads) return;
+    if (ng >= ngroups) return;
     const int slot = issued % kAttnRing;
     const uint32_t bar = full + 8 * slot;
     mbar_arrive_expect_tx(bar, (nj == 0 ? 3 : 2) * kTile);
-    if (nj == 0) tma_load_2d(sQ + (nh % kAttnRing) * kTile, &tm_qkv, bar, nh * HD, s0 + tile.q0);
-    tma_load_2d(sK + slot * kTile, &tm_qkv, bar, hidden + nh * HD, s0 + nj * 64);
-    tma_load_2d(sV + slot * kTile, &tm_qkv, bar, 2 * hidden + nh * HD, s0 + nj * 64);
-    if (++nj == nkv) { nj = 0; ++nh; }
+    if (nj == 0) tma_load_2d(sQ + (ng % kAttnRing) * kTile, &tm_qkv, bar, ng * W, s0 + tile.q0);
+    tma_load_2d(sK + slot * kTile, &tm_qkv, bar, hidden + ng * W, s0 + nj * 64);
+    tma_load_2d(sV + slot * kTile, &tm_qkv, bar, 2 * hidden + ng * W, s0 + nj * 64);
+    if (++nj == nkv) { nj = 0; ++ng; }
     ++issued;
   };
 
-  const AttnLane<HD> al(lane);
+  AttnLane<HD, RB> al[NH];
+#pragma unroll
+  for (int e = 0; e < NH; ++e) al[e] = AttnLane<HD, RB>(lane, e);
   const int qr = warp * 16 + (lane & 15);
-  const uint32_t q_row = qr * RB, q_swz = attn_swz<HD>(qr), q_hi = lane >> 4;
+  const uint32_t q_row = qr * RB, q_swz = attn_swz<RB>(qr), q_hi = lane >> 4;
 
-  uint32_t qf[HD / 16][4];
-  float o[HD / 8][4];
-  float m_run[2], l_run[4];
+  uint32_t qf[NH][HD / 16][4];
+  float o[NH][HD / 8][4];
+  float m_run[NH][2], l_run[NH][4];
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int i = 0; i < kAttnRing - 1; ++i) issue_next();
   }
   int step = 0;
-  for (int head = 0; head < num_heads; ++head) {
+  for (int g = 0; g < ngroups; ++g) {
     for (int j = 0; j < nkv; ++j, ++step) {
       if (threadIdx.x == 0) issue_next();
       const int slot = step % kAttnRing;
@@ -593,29 +621,35 @@ __global__ void __launch_bounds__(128, HD == 32 ? 5 : 4)
         const uint32_t vS = sV + slot * kTile;
         const int nkeys = min(64, L - j * 64);
         if (j == 0) {
-          const uint32_t qS = sQ + (head % kAttnRing) * kTile + q_row;
+          const uint32_t qS = sQ + (g % kAttnRing) * kTile + q_row;
 #pragma unroll
-          for (int kc = 0; kc < HD / 16; ++kc)
-            ldsm_x4(qf[kc], qS + (((2 * kc + q_hi) ^ q_swz) << 4));
-          attn_step_dispatch<HD, true>(nkeys, kS, vS, al, lane, scale_log2, qf, o, m_run, l_run);
+          for (int e = 0; e < NH; ++e)
+#pragma unroll
+            for (int kc = 0; kc < HD / 16; ++kc)
+              ldsm_x4(qf[e][kc], qS + (((e * (HD / 8) + 2 * kc + q_hi) ^ q_swz) << 4));
+          attn_step_dispatch<HD, RB, NH, true>(nkeys, kS, vS, al, lane, scale_log2, qf, o, m_run,
+                                               l_run);
         } else {
-          attn_step_dispatch<HD, false>(nkeys, kS, vS, al, lane, scale_log2, qf, o, m_run,
-                                        l_run);
+          attn_step_dispatch<HD, RB, NH, false>(nkeys, kS, vS, al, lane, scale_log2, qf, o,
+                                                m_run, l_run);
         }
         if (j == nkv - 1) {
-          // Every column of the ones block holds the full row sum; l ≥ 1
-          // (the row maximum contributes 2^0), so the approximate
-          // reciprocal (≤ 1 ulp) is safe.
-          const float inv0 = rcp_approx(l_run[0]), inv1 = rcp_approx(l_run[2]);
           const int qr0 = tile.q0 + warp * 16 + (lane >> 2), qr1 = qr0 + 8;
           const size_t orow0 = cls_mode ? (size_t)tile.seq : (size_t)(s0 + qr0);
           OutT* const out0 = out + orow0 * ldo + (lane & 3) * 2;
           OutT* const out1 = out + (size_t)(s0 + qr1) * ldo + (lane & 3) * 2;
 #pragma unroll
-          for (int nd = 0; nd < HD / 8; ++nd) {
-            const int col = head * HD + nd * 8;
-            if (qr0 < qlim) store2<OutT>(out0 + col, o[nd][0] * inv0, o[nd][1] * inv0);
-            if (qr1 < qlim) store2<OutT>(out1 + col, o[nd][2] * inv1, o[nd][3] * inv1);
+          for (int e = 0; e < NH; ++e) {
+            // Every column of the ones block holds the full row sum; l ≥ 1
+            // (the row maximum contributes 2^0), so the approximate
+            // reciprocal (≤ 1 ulp) is safe.
+            const float inv0 = rcp_approx(l_run[e][0]), inv1 = rcp_approx(l_run[e][2]);
+#pragma unroll
+            for (int nd = 0; nd < HD / 8; ++nd) {
+              const int col = (g * NH + e) * HD + nd * 8;
+              if (qr0 < qlim) store2<OutT>(out0 + col, o[e][nd][0] * inv0, o[e][nd][1] * inv0);
+              if (qr1 < qlim) store2<OutT>(out1 + col, o[e][nd][2] * inv1, o[e][nd][3] * inv1);
+            }
           }
         }
       }

@@ -671,9 +671,11 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
     if (tc_hd) {
       const int grid = cls_only ? nseq : ntiles;
       if (grid == 0) return FUTON_OK;
-      // q, k, v tiles of one head: 64 rows × hd columns, swizzled over one row.
+      // q, k, v tiles of nh adjacent heads: 64 rows × nh·hd columns, swizzled
+      // over one row.
+      const int nh = attn_heads_per_step(hd, H);
       CUtensorMap tm;
-      if (!make_qkv_map(&tm, qkv, (uint64_t)T, (uint64_t)(3 * h), hd, 64))
+      if (!make_qkv_map(&tm, qkv, (uint64_t)T, (uint64_t)(3 * h), nh * hd, 64))
         return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
       auto launch = [&](auto kern, int smem) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -682,8 +684,9 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
                                       d.err_word);
         return cudaGetLastError();
       };
-      CU_TRY(hd == 32 ? launch(attn_heads_kernel<32, OutT>, attn_heads_smem_bytes<32>())
-                      : launch(attn_heads_kernel<64, OutT>, attn_heads_smem_bytes<64>()));
+      CU_TRY(hd == 64   ? launch(attn_heads_kernel<64, 1, OutT>, attn_heads_smem_bytes<64, 1>())
+             : nh == 2 ? launch(attn_heads_kernel<32, 2, OutT>, attn_heads_smem_bytes<32, 2>())
+                       : launch(attn_heads_kernel<32, 1, OutT>, attn_heads_smem_bytes<32, 1>()));
       d.launches.fetch_add(1, std::memory_order_relaxed);
       return FUTON_OK;
     }
