@@ -110,6 +110,23 @@ def test_f16_pack_vs_oracle(gpu, arch):
     assert_parity(got, want, f"f16 pack {arch}")
 
 
+@pytest.mark.parametrize("heads", [3, 6])
+def test_head_dim32_head_counts_vs_oracle(gpu, heads):
+    """head_dim 32 with an odd head count (one head per attention step) and
+    an even one (two heads per step), at widths the fused LayerNorm slices do
+    not divide (standalone LayerNorm kernel), sequences up to 128 tokens (two
+    key tiles)."""
+    cfg = synth.arch("bge")
+    cfg.hidden_size, cfg.num_heads, cfg.intermediate_size, cfg.num_layers = 32 * heads, heads, 128 * heads, 2
+    w = synth.make_weights(cfg)
+    m = Model(cfg, w, devices=[0])
+    ids, cu = synth.make_inputs("c0", nseq=16, vocab=cfg.vocab_size)
+    got = m.encode_packed(ids, cu)
+    m.close()
+    want = OracleModel(cfg, w, gemm=oracle_mode()).encode_batch(ids, cu)
+    assert_parity(got, want, f"hd32 × {heads} heads")
+
+
 def test_c1_subset_vs_oracle(gpu):
     cfg, w, m = synth_model("minilm6")
     ids, cu = synth.make_inputs("c1", nseq=32)
