@@ -22,7 +22,7 @@ from __future__ import annotations
 import ctypes as C
 import dataclasses
 import threading
-from typing import Dict, Iterable, List, Optional, Sequence
+from typing import Dict, List, Optional, Sequence
 
 import numpy as np
 
@@ -262,9 +262,6 @@ class Provider:
         with self._mu:
             if self._closed:
                 raise FutonError(_lib.FUTON_EINVAL, "native: provider is closed")
-
-    def _clamp(self, ids: Sequence[int]) -> List[int]:
-        return list(ids)
 
     def embed_ids(self, ids: Sequence[int], cancel: Optional[CancelFlag] = None) -> np.ndarray:
         """Embed for pre-tokenised input (provider.go:115-121)."""

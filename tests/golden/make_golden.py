@@ -35,7 +35,6 @@ def main(ref: Path) -> None:
     shutil.copyfile(src / "expected.json", dst / "expected.json")
 
     sys.path.insert(0, str(ROOT))
-    import numpy as np
     from futon_b200.pack import load_pack
     from oracle.oracle import OracleModel
 

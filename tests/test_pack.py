@@ -12,7 +12,7 @@ import pytest
 
 from conftest import GOLDEN
 from futon_b200 import synth
-from futon_b200.pack import (PackConfig, PackError, expected_tensor_shapes, load_pack,
+from futon_b200.pack import (PackError, expected_tensor_shapes, load_pack,
                              load_pack_config, parse_safetensors, safetensors_bytes, sha256_file,
                              write_pack)
 

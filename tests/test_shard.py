@@ -8,7 +8,6 @@ import os
 import socket
 
 import numpy as np
-import pytest
 import torch.multiprocessing as mp
 
 from conftest import GOLDEN
