@@ -954,6 +954,7 @@ int validate_input(const futon_model& m, const int32_t* cu, int nseq, int out_di
                    size_t errlen) {
   const futon_cfg& c = m.cfg;
   if (nseq < 0) return set_err(err, errlen, FUTON_EINVAL, "native: negative sequence count");
+  if (nseq > 0 && !cu) return set_err(err, errlen, FUTON_EINVAL, "native: null cu_seqlens");
   if (out_dim < 0 || out_dim > c.hidden_size)
     return set_err(err, errlen, FUTON_EINVAL, "native: requested dim %d outside [1,%d]", out_dim,
                    c.hidden_size);
@@ -1481,6 +1482,8 @@ int futon_cuda_encode_device(futon_model* model, int device, const int32_t* d_id
   if (!model) return set_err(err, errlen, FUTON_EINVAL, "native: null model");
   if (device < 0 || device >= (int)model->devs.size())
     return set_err(err, errlen, FUTON_EINVAL, "native: device index %d out of range", device);
+  if (nseq > 0 && (!d_ids || !d_out))
+    return set_err(err, errlen, FUTON_EINVAL, "native: null buffer");
   int rc;
   if ((rc = validate_input(*model, cu_seqlens, nseq, out_dim, err, errlen))) return rc;
   DevCtx& d = *model->devs[device];
@@ -1552,6 +1555,7 @@ int futon_cuda_matmul_t(int cuda_device, float* dst, const float* a, const float
   if (m < 0 || n <= 0 || k <= 0 || k % 8)
     return set_err(err, errlen, FUTON_EINVAL, "native: matmul shape m=%d n=%d k=%d (k %% 8 == 0)", m, n, k);
   if (m == 0) return FUTON_OK;
+  if (!dst || !a || !b) return set_err(err, errlen, FUTON_EINVAL, "native: null buffer");
   const size_t abytes = align_up((size_t)m * k * 2, 256), bbytes = align_up((size_t)n * k * 2, 256);
   SeamCtx* s;
   int rc;
@@ -1573,6 +1577,7 @@ int futon_cuda_matmul_t_q8(int cuda_device, float* dst, const float* a, const in
   if (m < 0 || n <= 0 || k <= 0 || k % 16)
     return set_err(err, errlen, FUTON_EINVAL, "native: q8 matmul shape m=%d n=%d k=%d (k %% 16 == 0)", m, n, k);
   if (m == 0) return FUTON_OK;
+  if (!dst || !a || !qb || !scales) return set_err(err, errlen, FUTON_EINVAL, "native: null buffer");
   const size_t qbytes = align_up((size_t)m * k, 256), sbytes = align_up((size_t)m * 4, 256);
   SeamCtx* s;
   int rc;
@@ -1592,6 +1597,7 @@ int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, con
   if (rows < 0 || k <= 0 || k % 4)
     return set_err(err, errlen, FUTON_EINVAL, "native: quantize shape rows=%d k=%d (k %% 4 == 0)", rows, k);
   if (rows == 0) return FUTON_OK;
+  if (!dst || !scales || !src) return set_err(err, errlen, FUTON_EINVAL, "native: null buffer");
   SeamCtx* s;
   int rc;
   if ((rc = seam_begin(cuda_device, 256, &s, err, errlen))) return rc;
@@ -1665,6 +1671,7 @@ extern "C" int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const
                    "native: q8 no-alloc scratch needs %zu bytes for m=%d k=%d; the fixed "
                    "scratch holds %zu (m·k + 4·m, rounded)", need, m, k, kNoAllocScratchBytes);
   if (m == 0) return FUTON_OK;
+  if (!dst || !a || !qb || !scales) return set_err(err, errlen, FUTON_EINVAL, "native: null buffer");
   CU_TRY(cudaSetDevice(cuda_device));
   NoAllocDev* s;
   int rc;

@@ -116,7 +116,8 @@ int futon_cuda_encode_batch(futon_model* model, const int32_t* ids, const int32_
  * d_ids and d_out are device pointers on that device, cu_seqlens is host
  * memory (it plans the micro-batches). Work is queued on `stream`
  * (cudaStream_t, NULL = the library's stream for that device) and the call
- * returns without waiting; futon_cuda_sync reports completion and errors. */
+ * returns without waiting; futon_cuda_sync reports completion and errors.
+ * NULL buffers with nseq > 0 are refused (FUTON_EINVAL) before any launch. */
 int futon_cuda_encode_device(futon_model* model, int device, const int32_t* d_ids,
                              const int32_t* cu_seqlens, int nseq, int out_dim, float* d_out,
                              void* stream, char* err, size_t errlen);

@@ -96,3 +96,10 @@ def test_seam_rejects_bad_shapes(gpu):
         _lib.call("futon_cuda_matmul_t", 0, None, None, None, 4, 4, 7, None, None)
     with pytest.raises(_lib.FutonError):
         _lib.call("futon_cuda_matmul_t_q8", 0, None, None, None, None, 4, 4, 8, None, None)
+    # Well-formed shapes with null buffers are refused on the host.
+    with pytest.raises(_lib.FutonError, match="null buffer"):
+        _lib.call("futon_cuda_matmul_t", 0, None, None, None, 4, 4, 8, None, None)
+    with pytest.raises(_lib.FutonError, match="null buffer"):
+        _lib.call("futon_cuda_matmul_t_q8", 0, None, None, None, None, 4, 4, 16, None, None)
+    with pytest.raises(_lib.FutonError, match="null buffer"):
+        _lib.call("futon_cuda_quantize_rows_q8", 0, None, None, None, 4, 16, None)

@@ -297,6 +297,8 @@ def test_rejects(gpu):
         m.encode_tokens([2, 3], p.cfg.hidden_size + 1)
     with pytest.raises(FutonError, match="empty"):
         m.encode_packed(np.array([2, 3], np.int32), np.array([0, 2, 2], np.int32))
+    with pytest.raises(FutonError, match="null buffer"):  # caught on the host, nothing launched
+        m.encode_device(0, np.array([0, 2], np.int32), 0, 0)
     m.close()
 
 
