@@ -70,3 +70,22 @@ def test_null_model_calls_return_errors():
     with pytest.raises(FutonError, match="null model"):
         _lib.call("futon_cuda_sync", None, 0, None)
     assert _lib.lib().futon_cuda_launch_count(None, 0) == -1
+
+
+@pytest.mark.parametrize("call", [
+    ("futon_cuda_matmul_t", 0, None, None, None, 4, 4, 8, None, None),
+    ("futon_cuda_matmul_t_q8", 0, None, None, None, None, 4, 4, 16, None, None),
+    ("futon_cuda_matmul_t_q8_noalloc", 0, None, None, None, None, 4, 4, 16, None, None),
+    ("futon_cuda_quantize_rows_q8", 0, None, None, None, 4, 16, None),
+])
+def test_kernel_seams_refuse_null_buffers(call):
+    """Well-formed shapes with null buffers are refused before any device work."""
+    with pytest.raises(FutonError, match="null buffer"):
+        _lib.call(*call)
+
+
+def test_kernel_seams_accept_empty_shapes():
+    """m = 0 (or rows = 0) is a no-op that returns success without a device."""
+    _lib.call("futon_cuda_matmul_t", 0, None, None, None, 0, 4, 8, None, None)
+    _lib.call("futon_cuda_matmul_t_q8", 0, None, None, None, None, 0, 4, 16, None, None)
+    _lib.call("futon_cuda_quantize_rows_q8", 0, None, None, None, 0, 16, None)
