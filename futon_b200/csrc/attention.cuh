@@ -545,7 +545,10 @@ __device__ __forceinline__ void attn_step_dispatch(int nkeys, uint32_t kS, uint3
 template <int HD, int NH>
 constexpr int attn_heads_min_ctas() { return NH == 2 ? 3 : HD == 32 ? 5 : 4; }
 
-template <int HD, int NH, typename OutT>
+// SPLIT: blockIdx.y takes an equal share of the head groups instead of all
+// of them (grid.y CTAs per tile), for micro-batches whose tile count alone
+// leaves most SMs idle.
+template <int HD, int NH, typename OutT, bool SPLIT = false>
 __global__ void __launch_bounds__(128, attn_heads_min_ctas<HD, NH>())
     attn_heads_kernel(const __grid_constant__ CUtensorMap tm_qkv, int hidden, int num_heads,
                       const int* __restrict__ cu_seqlens, const AttnTile* __restrict__ tiles,
@@ -567,7 +570,13 @@ __global__ void __launch_bounds__(128, attn_heads_min_ctas<HD, NH>())
   const int L = cu_seqlens[tile.seq + 1] - s0;
   const int qlim = cls_mode ? 1 : L;  // query positions < qlim are real
   const int nkv = (L + 63) / 64;
-  const int ngroups = num_heads / NH;
+  int g_begin = 0, g_end = num_heads / NH;
+  if constexpr (SPLIT) {
+    const int per = (g_end + (int)gridDim.y - 1) / (int)gridDim.y;
+    g_begin = (int)blockIdx.y * per;
+    g_end = min(g_end, g_begin + per);
+    if (g_begin >= g_end) return;  // uniform over the CTA, before any barrier
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool warp_active = tile.q0 + warp * 16 < qlim;
 
@@ -581,9 +590,9 @@ __global__ void __launch_bounds__(128, attn_heads_min_ctas<HD, NH>())
   __syncthreads();
 
   // Next (head group, key tile) to load (thread 0 only).
-  int ng = 0, nj = 0, issued = 0;
+  int ng = g_begin, nj = 0, issued = 0;
   auto issue_next = [&]() {
-    if (ng >= ngroups) return;
+    if (ng >= g_end) return;
     const int slot = issued % kAttnRing;
     const uint32_t bar = full + 8 * slot;
     mbar_arrive_expect_tx(bar, (nj == 0 ? 3 : 2) * kTile);
@@ -608,7 +617,7 @@ __global__ void __launch_bounds__(128, attn_heads_min_ctas<HD, NH>())
     for (int i = 0; i < kAttnRing - 1; ++i) issue_next();
   }
   int step = 0;
-  for (int g = 0; g < ngroups; ++g) {
+  for (int g = g_begin; g < g_end; ++g) {
     for (int j = 0; j < nkv; ++j, ++step) {
       if (threadIdx.x == 0) issue_next();
       const int slot = step % kAttnRing;

@@ -27,6 +27,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -248,6 +249,12 @@ struct futon_model {
   int head_dim = 0;
   int eff_max = 0;
   int swiglu_half = 0;
+  // Attention kernel of the float path (read from FUTON_CUDA_ATTN when the
+  // model is created): 0 = attn_heads_kernel, 1 = attn_tc_kernel.
+  int attn_kind = 0;
+  // FUTON_CUDA_ATTN_SPLIT=1: attn_heads_kernel launches with the head groups
+  // shared among grid.y CTAs when the tiles alone would leave SMs idle.
+  bool attn_split = false;
   std::vector<std::unique_ptr<DevCtx>> devs;
 };
 
@@ -620,8 +627,26 @@ inline int grid_rows(int rows, int per_block, int sms) {
 // ---- attention dispatch --------------------------------------------------
 // attn_tc_kernel (tcgen05, packed 128-row windows) is parity-correct and
 // batch-invariant but, as measured on the c4 workload, 1.5× slower than
-// attn_heads_kernel; it stays off until it is the faster one.
-constexpr bool kAttnTcgen05 = false;
+// attn_heads_kernel; it runs only when FUTON_CUDA_ATTN=tc.
+enum AttnKind : int { kAttnHeads = 0, kAttnTc = 1 };
+
+// Model-creation-time attention options from the environment; unknown
+// values leave the defaults.
+void read_attn_env(futon_model& m) {
+  if (const char* v = std::getenv("FUTON_CUDA_ATTN")) {
+    if (!strcmp(v, "tc")) m.attn_kind = kAttnTc;
+    else if (!strcmp(v, "heads")) m.attn_kind = kAttnHeads;
+  }
+  if (const char* v = std::getenv("FUTON_CUDA_ATTN_SPLIT")) m.attn_split = !strcmp(v, "1");
+}
+
+// CTAs per tile (grid.y) for attn_heads_kernel's head-group split: enough to
+// give every SM about two CTAs, at most one per head group.
+int attn_split_ways(const futon_model& m, const DevCtx& d, int tiles, int ngroups) {
+  if (!m.attn_split || tiles <= 0 || ngroups <= 1) return 1;
+  const int want = (2 * d.num_sms + tiles - 1) / tiles;
+  return std::max(1, std::min(ngroups, want));
+}
 
 // A micro-batch's attention work lists (device memory): 64-query tiles per
 // sequence and ≤ 128-row windows of packed sequences.
@@ -649,7 +674,7 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
   const AttnTile* tiles = plan.tiles;
   const int ntiles = plan.ntiles;
   if constexpr (!kSplit) {
-    if (kAttnTcgen05 && tc_hd && !cls_only) {
+    if (m.attn_kind == kAttnTc && tc_hd && !cls_only) {
       if (plan.nwin == 0) return FUTON_OK;
       // q, k, v tiles of one head: 128 rows × hd columns, swizzled over one row.
       AttnMaps maps{};
@@ -677,16 +702,22 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
       CUtensorMap tm;
       if (!make_qkv_map(&tm, qkv, (uint64_t)T, (uint64_t)(3 * h), nh * hd, 64))
         return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
+      const int ways = attn_split_ways(m, d, grid, H / nh);
       auto launch = [&](auto kern, int smem) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        kern<<<grid, 128, smem, st>>>(tm, h, H, cu, tiles, cls_only ? 1 : 0, scale_log2, out, h,
-                                      d.err_word);
+        kern<<<dim3(grid, ways), 128, smem, st>>>(tm, h, H, cu, tiles, cls_only ? 1 : 0,
+                                                  scale_log2, out, h, d.err_word);
         return cudaGetLastError();
       };
-      CU_TRY(hd == 64   ? launch(attn_heads_kernel<64, 1, OutT>, attn_heads_smem_bytes<64, 1>())
-             : nh == 2 ? launch(attn_heads_kernel<32, 2, OutT>, attn_heads_smem_bytes<32, 2>())
-                       : launch(attn_heads_kernel<32, 1, OutT>, attn_heads_smem_bytes<32, 1>()));
+      if (ways > 1)
+        CU_TRY(hd == 64   ? launch(attn_heads_kernel<64, 1, OutT, true>, attn_heads_smem_bytes<64, 1>())
+               : nh == 2 ? launch(attn_heads_kernel<32, 2, OutT, true>, attn_heads_smem_bytes<32, 2>())
+                         : launch(attn_heads_kernel<32, 1, OutT, true>, attn_heads_smem_bytes<32, 1>()));
+      else
+        CU_TRY(hd == 64   ? launch(attn_heads_kernel<64, 1, OutT>, attn_heads_smem_bytes<64, 1>())
+               : nh == 2 ? launch(attn_heads_kernel<32, 2, OutT>, attn_heads_smem_bytes<32, 2>())
+                         : launch(attn_heads_kernel<32, 1, OutT>, attn_heads_smem_bytes<32, 1>()));
       d.launches.fetch_add(1, std::memory_order_relaxed);
       return FUTON_OK;
     }
@@ -1344,6 +1375,7 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
   model->swiglu_half = half;
   model->fuse_ln = !q8 && h % ln_slice_cols(h) == 0 && h / ln_slice_cols(h) >= 2 &&
                    h / ln_slice_cols(h) <= kLnPeerSlots;
+  read_attn_env(*model);
 
   // RoPE tables (precomputeRoPE, model.go:306-318): f64 angles, f32 storage.
   std::vector<float> rc_tab, rs_tab;

@@ -1,8 +1,9 @@
 """Shared fixtures for the futon_b200 test suite.
 
 Markers: `gpu` tests need a CUDA device and call libfuton_cuda through its
-C ABI; everything else runs on the CPU (oracle, pack host logic, ABI
-loading, gloo multi-process planning).
+C ABI; `gpu_variant` tests check opt-in kernel variants on a GPU and run only
+when FUTON_TEST_ATTN_VARIANTS=1; everything else runs on the CPU (oracle,
+pack host logic, ABI loading, gloo multi-process planning).
 """
 from __future__ import annotations
 
@@ -28,6 +29,8 @@ GPU_COSINE_MIN = 0.9999
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and libfuton_cuda")
+    config.addinivalue_line(
+        "markers", "gpu_variant: GPU checks of opt-in kernel variants (FUTON_TEST_ATTN_VARIANTS=1)")
 
 
 def cosine(a, b) -> float:

@@ -1,0 +1,92 @@
+"""GPU checks of the opt-in attention variants, selected when a model is
+created by FUTON_CUDA_ATTN / FUTON_CUDA_ATTN_SPLIT.
+
+These run only on request (`FUTON_TEST_ATTN_VARIANTS=1 pytest -m
+gpu_variant`): the default configuration never reaches the variants, so the
+default `-m gpu` suite does not select them.
+
+- split: attn_heads_kernel with the head groups shared among grid.y CTAs.
+  Every head is computed by the same code in the same order as without the
+  split, so the vectors must be bitwise equal to the default kernel's.
+- tc: the tcgen05 attention kernel; parity with the oracle (cosine gate)
+  and batch invariance (a sequence's vector does not depend on what it is
+  packed with).
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GPU_COSINE_MIN, row_cosines
+from futon_b200 import Model, pack_ids, synth
+from oracle.oracle import GEMM_AVX2, GEMM_GO, OracleModel, has_avx2
+
+pytestmark = [
+    pytest.mark.gpu_variant,
+    pytest.mark.skipif(os.environ.get("FUTON_TEST_ATTN_VARIANTS") != "1",
+                       reason="opt-in: FUTON_TEST_ATTN_VARIANTS=1"),
+]
+
+_weights = {}
+
+
+def weights(arch, layers=None):
+    key = (arch, layers)
+    if key not in _weights:
+        cfg = synth.arch(arch)
+        if layers:
+            cfg.num_layers = layers
+        _weights[key] = (cfg, synth.make_weights(cfg))
+    return _weights[key]
+
+
+def encode(monkeypatch, env, cfg, w, ids, cu, out_dim=0):
+    for k in ("FUTON_CUDA_ATTN", "FUTON_CUDA_ATTN_SPLIT"):
+        monkeypatch.delenv(k, raising=False)
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    m = Model(cfg, w, devices=[0])
+    try:
+        return m.encode_packed(ids, cu, out_dim=out_dim)
+    finally:
+        m.close()
+
+
+CASES = [
+    ("bge", "c0", 32, None),       # CLS pooling: the pruned last layer splits too
+    ("minilm6", "c1", 16, None),   # mean pooling, 128-token sequences (two key tiles)
+    ("nomic", "c2", 4, 3),         # head_dim 64, one head per step, up to 512 tokens
+]
+
+
+@pytest.mark.parametrize("arch,inputs,nseq,layers", CASES)
+def test_split_bitwise_equals_default(gpu, monkeypatch, arch, inputs, nseq, layers):
+    cfg, w = weights(arch, layers)
+    ids, cu = synth.make_inputs(inputs, nseq=nseq, vocab=cfg.vocab_size)
+    base = encode(monkeypatch, {}, cfg, w, ids, cu)
+    split = encode(monkeypatch, {"FUTON_CUDA_ATTN_SPLIT": "1"}, cfg, w, ids, cu)
+    assert np.array_equal(base, split), f"{arch}: split attention differs from the default"
+
+
+@pytest.mark.parametrize("arch,inputs,nseq,layers", CASES)
+def test_tc_vs_oracle(gpu, monkeypatch, arch, inputs, nseq, layers):
+    cfg, w = weights(arch, layers)
+    ids, cu = synth.make_inputs(inputs, nseq=nseq, vocab=cfg.vocab_size)
+    got = encode(monkeypatch, {"FUTON_CUDA_ATTN": "tc"}, cfg, w, ids, cu)
+    gemm = GEMM_AVX2 if has_avx2() else GEMM_GO
+    want = OracleModel(cfg, w, gemm=gemm).encode_batch(ids, cu)
+    cs = row_cosines(got, want)
+    assert cs.min() >= GPU_COSINE_MIN, f"{arch}: tc attention min cosine {cs.min():.7f}"
+
+
+def test_tc_batch_invariance(gpu, monkeypatch):
+    cfg, w = weights("bge", 2)
+    ids, cu = synth.make_inputs("c4", nseq=24, vocab=cfg.vocab_size)
+    seqs = [ids[cu[i]:cu[i + 1]] for i in range(len(cu) - 1)]
+    env = {"FUTON_CUDA_ATTN": "tc"}
+    packed = encode(monkeypatch, env, cfg, w, ids, cu)
+    rev_ids, rev_cu = pack_ids(seqs[::-1])
+    rev = encode(monkeypatch, env, cfg, w, rev_ids, rev_cu)[::-1]
+    assert np.array_equal(packed, rev), "tc attention: a vector depends on its batch neighbours"
