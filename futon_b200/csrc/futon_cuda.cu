@@ -1172,9 +1172,15 @@ struct SeamCtx {
 };
 SeamCtx g_seam[64];
 
-int seam_begin(int dev, size_t bytes, SeamCtx** out, char* err, size_t errlen) {
+// Takes the device's seam lock (handed to the caller in *lk, held until the
+// call returns: the scratch, its capacity and the error word are shared by
+// every seam call on the device), then initialises the context and grows
+// the scratch to `bytes`.
+int seam_begin(int dev, size_t bytes, SeamCtx** out, std::unique_lock<std::mutex>* lk, char* err,
+               size_t errlen) {
   if (dev < 0 || dev >= 64) return set_err(err, errlen, FUTON_EINVAL, "native: bad device %d", dev);
   SeamCtx& s = g_seam[dev];
+  std::unique_lock<std::mutex> held(s.mu);
   CU_TRY(cudaSetDevice(dev));
   if (!s.init) {
     CU_TRY(cudaMalloc(&s.err_word, sizeof(int)));
@@ -1191,6 +1197,7 @@ int seam_begin(int dev, size_t bytes, SeamCtx** out, char* err, size_t errlen) {
     s.cap = bytes;
   }
   *out = &s;
+  *lk = std::move(held);
   return FUTON_OK;
 }
 
@@ -1591,8 +1598,8 @@ int futon_cuda_matmul_t(int cuda_device, float* dst, const float* a, const float
   const size_t abytes = align_up((size_t)m * k * 2, 256), bbytes = align_up((size_t)n * k * 2, 256);
   SeamCtx* s;
   int rc;
-  if ((rc = seam_begin(cuda_device, abytes + bbytes, &s, err, errlen))) return rc;
-  std::lock_guard<std::mutex> lock(s->mu);
+  std::unique_lock<std::mutex> lock;
+  if ((rc = seam_begin(cuda_device, abytes + bbytes, &s, &lock, err, errlen))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   bf16* ab = (bf16*)s->scratch;
   bf16* bb = (bf16*)((uint8_t*)s->scratch + abytes);
@@ -1613,8 +1620,8 @@ int futon_cuda_matmul_t_q8(int cuda_device, float* dst, const float* a, const in
   const size_t qbytes = align_up((size_t)m * k, 256), sbytes = align_up((size_t)m * 4, 256);
   SeamCtx* s;
   int rc;
-  if ((rc = seam_begin(cuda_device, qbytes + sbytes, &s, err, errlen))) return rc;
-  std::lock_guard<std::mutex> lock(s->mu);
+  std::unique_lock<std::mutex> lock;
+  if ((rc = seam_begin(cuda_device, qbytes + sbytes, &s, &lock, err, errlen))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int8_t* qa = (int8_t*)s->scratch;
   float* sa = (float*)((uint8_t*)s->scratch + qbytes);
@@ -1632,7 +1639,8 @@ int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, con
   if (!dst || !scales || !src) return set_err(err, errlen, FUTON_EINVAL, "native: null buffer");
   SeamCtx* s;
   int rc;
-  if ((rc = seam_begin(cuda_device, 256, &s, err, errlen))) return rc;
+  std::unique_lock<std::mutex> lock;
+  if ((rc = seam_begin(cuda_device, 256, &s, &lock, err, errlen))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   quant_rows_kernel<<<grid_rows(rows, 8, s->num_sms), 256, 0, st>>>(src, rows, k, dst, scales);
   CU_TRY(cudaGetLastError());
@@ -1781,8 +1789,8 @@ __global__ void selftest_wait_kernel(int* err) {
 extern "C" int futon_cuda_selftest_wait_timeout(int cuda_device, char* err, size_t errlen) {
   SeamCtx* s = nullptr;
   int rc;
-  if ((rc = seam_begin(cuda_device, 0, &s, err, errlen))) return rc;
-  std::lock_guard<std::mutex> lk(s->mu);
+  std::unique_lock<std::mutex> lk;
+  if ((rc = seam_begin(cuda_device, 0, &s, &lk, err, errlen))) return rc;
   CU_TRY(cudaMemset(s->err_word, 0, sizeof(int)));
   selftest_wait_kernel<<<1, 32>>>(s->err_word);
   CU_TRY(cudaGetLastError());

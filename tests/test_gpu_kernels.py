@@ -103,3 +103,59 @@ def test_seam_rejects_bad_shapes(gpu):
         _lib.call("futon_cuda_matmul_t_q8", 0, None, None, None, None, 4, 4, 16, None, None)
     with pytest.raises(_lib.FutonError, match="null buffer"):
         _lib.call("futon_cuda_quantize_rows_q8", 0, None, None, None, 4, 16, None)
+
+
+def test_seam_concurrent_callers(gpu):
+    """Kernel-seam calls from several host threads on one device (the Kernel
+    interface is safe for concurrent use): the calls share the device's
+    scratch, which grows while they run (the last shape needs more than any
+    earlier test), and every result equals the single-threaded one bit for
+    bit."""
+    import threading
+
+    import torch
+    shapes = [(64, 128, 128), (512, 384, 384), (2048, 1152, 384), (8192, 2304, 768)]
+    rng = np.random.default_rng(99)
+    cases = []
+    for m, n, k in shapes:
+        a = _dev(rng.standard_normal((m, k)).astype(np.float32))
+        b = _dev(rng.standard_normal((n, k)).astype(np.float32))
+        cases.append((a, b, m, n, k))
+
+    def run(i, out):
+        a, b, m, n, k = cases[i]
+        _lib.call("futon_cuda_matmul_t", 0, out.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k,
+                  None, None)
+
+    nthreads, rounds = 4, 2
+    outs = [[torch.empty((c[2], c[3]), dtype=torch.float32, device="cuda") for c in cases]
+            for _ in range(nthreads)]
+    got = [[[] for _ in cases] for _ in range(nthreads)]
+    errors = []
+
+    def worker(t):
+        try:
+            for r in range(rounds):
+                order = list(range(len(cases)))
+                if (t + r) % 2:
+                    order.reverse()
+                for i in order:
+                    run(i, outs[t][i])
+                    got[t][i].append(outs[t][i].cpu().numpy())
+        except Exception as e:  # noqa: BLE001 - reported below
+            errors.append(f"thread {t}: {e!r}")
+
+    threads = [threading.Thread(target=worker, args=(t,)) for t in range(nthreads)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=120)
+    assert not any(th.is_alive() for th in threads), "seam calls did not finish"
+    assert not errors, errors[:4]
+    for i, (a, b, m, n, k) in enumerate(cases):
+        ref = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        run(i, ref)
+        want = ref.cpu().numpy()
+        for t in range(nthreads):
+            for r, g in enumerate(got[t][i]):
+                assert np.array_equal(g, want), f"thread {t} round {r} shape {(m, n, k)}: mismatch"
