@@ -209,6 +209,10 @@ struct DevCtx {
   float* h_out = nullptr; // pinned
   size_t h_out_cap = 0;
   cudaEvent_t meta_evt = nullptr;
+  // Recorded on a call's stream after its last launch; the next call's stream
+  // waits on it first. Calls may use different streams (encode_device takes
+  // the caller's), and they share the workspace and the meta buffer.
+  cudaEvent_t done_evt = nullptr;
   std::vector<cudaEvent_t> out_evts;  // host-buffer calls: one per micro-batch's D2H
   std::atomic<long long> launches{0};
   // Optional per-stage profiler (CUDA events around each launch).
@@ -232,6 +236,7 @@ struct DevCtx {
     if (h_ids) cudaFreeHost(h_ids);
     if (h_out) cudaFreeHost(h_out);
     if (meta_evt) cudaEventDestroy(meta_evt);
+    if (done_evt) cudaEventDestroy(done_evt);
     for (cudaEvent_t e : ev_all) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
   }
@@ -1078,6 +1083,15 @@ using MbHook = std::function<int(int, int, int)>;
 int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* cu, int nseq,
              int out_dim, float* d_out, cudaStream_t st, volatile const int* cancel, char* err,
              size_t errlen, const MbHook& after_mb = nullptr) {
+  // Work of earlier calls (possibly on other streams) finishes before this
+  // call's uploads and kernels touch the shared buffers; this call's end is
+  // recorded for the next one on every return path.
+  CU_TRY(cudaStreamWaitEvent(st, d.done_evt, 0));
+  struct RecordDone {
+    DevCtx& d;
+    cudaStream_t st;
+    ~RecordDone() { cudaEventRecord(d.done_evt, st); }
+  } record_done{d, st};
   std::vector<MicroBatch> mbs;
   int rc;
   if ((rc = plan_and_upload(d, cu, nseq, mbs, st, err, errlen))) return rc;
@@ -1408,6 +1422,8 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
     CU_TRY(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
     CU_TRY(cudaEventCreateWithFlags(&d->meta_evt, cudaEventDisableTiming));
     CU_TRY(cudaEventRecord(d->meta_evt, d->stream));
+    CU_TRY(cudaEventCreateWithFlags(&d->done_evt, cudaEventDisableTiming));
+    CU_TRY(cudaEventRecord(d->done_evt, d->stream));
     if ((rc = dev_alloc(*d, &d->err_word, 1, err, errlen))) return rc;
     CU_TRY(cudaMemset(d->err_word, 0, sizeof(int)));
     if ((rc = upload_f32(*d, &d->word, word, (size_t)c.vocab_size * h, err, errlen))) return rc;

@@ -265,6 +265,27 @@ def test_encode_device_matches_host(gpu):
     assert m.launch_count() > 0
 
 
+def test_encode_device_two_streams(gpu):
+    """Back-to-back device-resident calls on two different caller streams,
+    queued without waiting, share the device's workspace: the library orders
+    the second after the first, so both match the host-buffer path."""
+    import torch
+    cfg, w, m = synth_model("bge")
+    batches = [synth.make_inputs("c4", nseq=400, seed=11), synth.make_inputs("c0", seed=12)]
+    want = [m.encode_packed(ids, cu) for ids, cu in batches]
+    d_ids = [torch.from_numpy(ids).cuda() for ids, _ in batches]
+    d_out = [torch.empty((len(cu) - 1, cfg.hidden_size), dtype=torch.float32, device="cuda")
+             for _, cu in batches]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for (ids, cu), di, do, s in zip(batches, d_ids, d_out, streams):
+        m.encode_device(di.data_ptr(), cu, 0, do.data_ptr(), stream=s.cuda_stream)
+    for s in streams:
+        m.sync(stream=s.cuda_stream)
+    for do, wv in zip(d_out, want):
+        assert np.array_equal(do.cpu().numpy(), wv)
+
+
 def test_micro_batching_large_call(gpu):
     """A call larger than one micro-batch (131,072 tokens) splits without
     changing any vector."""
