@@ -225,6 +225,7 @@ struct DevCtx {
 
   ~DevCtx() {
     cudaSetDevice(device);
+    if (done_evt) cudaEventSynchronize(done_evt);  // the last call, whatever its stream
     if (stream) cudaStreamSynchronize(stream);
     for (cudaEvent_t e : out_evts) cudaEventDestroy(e);
     for (void* p : allocs) cudaFree(p);

@@ -19,6 +19,7 @@ CUDA kernels in libfuton_cuda.so.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 import dataclasses
 import threading
@@ -124,9 +125,13 @@ class Model:
         cs = _cfg_struct(cfg)
         _lib.call("futon_cuda_model_create", C.byref(cs), arr, len(tensors), devs, len(devices),
                   1 if self.q8 else 0, C.byref(handle))
+        self._init_handle(handle)
+
+    def _init_handle(self, handle: C.c_void_p) -> None:
         self._h = handle
         self._closed = False
-        self._mu = threading.Lock()
+        self._cv = threading.Condition()
+        self._inflight = 0
 
     @classmethod
     def load(cls, pack_dir, devices=None, q8=None) -> "Model":
@@ -135,10 +140,15 @@ class Model:
 
     # -- lifecycle --------------------------------------------------------
     def close(self) -> None:
-        with self._mu:
-            if not self._closed and self._h:
-                _lib.lib().futon_cuda_model_destroy(self._h)
+        """Refuses new calls, waits for the calls in flight on other threads
+        (like Provider.Close, provider.go:274-281, which lets in-flight
+        forwards finish), then releases every device buffer."""
+        with self._cv:
             self._closed = True
+            while self._inflight:
+                self._cv.wait()
+            if self._h:
+                _lib.lib().futon_cuda_model_destroy(self._h)
             self._h = C.c_void_p()
 
     def __del__(self):
@@ -152,6 +162,22 @@ class Model:
         if self._closed:
             raise FutonError(_lib.FUTON_EINVAL, "native: model is closed")
         return self._h
+
+    @contextlib.contextmanager
+    def _call(self):
+        """The native handle for one call; close() waits until it returns."""
+        with self._cv:
+            if self._closed:
+                raise FutonError(_lib.FUTON_EINVAL, "native: model is closed")
+            self._inflight += 1
+            h = self._h
+        try:
+            yield h
+        finally:
+            with self._cv:
+                self._inflight -= 1
+                if not self._inflight:
+                    self._cv.notify_all()
 
     def effective_max_seq_len(self) -> int:
         return self.cfg.effective_max_seq_len()
@@ -167,8 +193,9 @@ class Model:
         cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
         nseq = len(cu) - 1
         out = np.empty((max(nseq, 0), self.out_width(out_dim)), dtype=np.float32)
-        _lib.call("futon_cuda_encode", self.handle, device, ids.ctypes.data, cu.ctypes.data, nseq,
-                  out_dim, out.ctypes.data, cancel.ptr if cancel else None)
+        with self._call() as h:
+            _lib.call("futon_cuda_encode", h, device, ids.ctypes.data, cu.ctypes.data, nseq,
+                      out_dim, out.ctypes.data, cancel.ptr if cancel else None)
         return out
 
     def encode_batch(self, ids: np.ndarray, cu_seqlens: np.ndarray, out_dim: int = 0,
@@ -178,8 +205,9 @@ class Model:
         cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
         nseq = len(cu) - 1
         out = np.empty((max(nseq, 0), self.out_width(out_dim)), dtype=np.float32)
-        _lib.call("futon_cuda_encode_batch", self.handle, ids.ctypes.data, cu.ctypes.data, nseq,
-                  out_dim, out.ctypes.data, cancel.ptr if cancel else None)
+        with self._call() as h:
+            _lib.call("futon_cuda_encode_batch", h, ids.ctypes.data, cu.ctypes.data, nseq,
+                      out_dim, out.ctypes.data, cancel.ptr if cancel else None)
         return out
 
     def encode_tokens(self, ids: Sequence[int], out_dim: int = 0, device: int = 0,
@@ -197,31 +225,36 @@ class Model:
                       device: int = 0, stream: Optional[int] = None) -> None:
         """Queues a forward over ids already in HBM (returns without waiting)."""
         cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
-        _lib.call("futon_cuda_encode_device", self.handle, device, C.c_void_p(d_ids),
-                  cu.ctypes.data, len(cu) - 1, out_dim, C.c_void_p(d_out),
-                  C.c_void_p(stream) if stream else None)
+        with self._call() as h:
+            _lib.call("futon_cuda_encode_device", h, device, C.c_void_p(d_ids),
+                      cu.ctypes.data, len(cu) - 1, out_dim, C.c_void_p(d_out),
+                      C.c_void_p(stream) if stream else None)
 
     def sync(self, device: int = 0, stream: Optional[int] = None) -> None:
-        _lib.call("futon_cuda_sync", self.handle, device, C.c_void_p(stream) if stream else None)
+        with self._call() as h:
+            _lib.call("futon_cuda_sync", h, device, C.c_void_p(stream) if stream else None)
 
     def launch_count(self, device: int = 0) -> int:
-        return int(_lib.lib().futon_cuda_launch_count(self.handle, device))
+        with self._call() as h:
+            return int(_lib.lib().futon_cuda_launch_count(h, device))
 
     def profile(self, enable: bool, device: int = 0) -> None:
         """Resets the per-stage profiler and turns it on or off."""
-        _lib.call("futon_cuda_profile", self.handle, device, 1 if enable else 0)
+        with self._call() as h:
+            _lib.call("futon_cuda_profile", h, device, 1 if enable else 0)
 
     def profile_read(self, device: int = 0) -> Dict[str, dict]:
         """{stage: {ms, launches, flops, bytes}} accumulated since profile(True)."""
         L = _lib.lib()
         out = {}
-        for st in range(L.futon_cuda_profile_stage_count()):
-            ms, n, fl, by = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
-            _lib.call("futon_cuda_profile_read", self.handle, device, st, C.byref(ms), C.byref(n),
-                      C.byref(fl), C.byref(by))
-            if n.value:
-                out[L.futon_cuda_profile_stage_name(st).decode()] = {
-                    "ms": ms.value, "launches": n.value, "flops": fl.value, "bytes": by.value}
+        with self._call() as h:
+            for st in range(L.futon_cuda_profile_stage_count()):
+                ms, n, fl, by = C.c_double(), C.c_longlong(), C.c_double(), C.c_double()
+                _lib.call("futon_cuda_profile_read", h, device, st, C.byref(ms), C.byref(n),
+                          C.byref(fl), C.byref(by))
+                if n.value:
+                    out[L.futon_cuda_profile_stage_name(st).decode()] = {
+                        "ms": ms.value, "launches": n.value, "flops": fl.value, "bytes": by.value}
         return out
 
 
