@@ -34,6 +34,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <unordered_map>
 #include <vector>
 
 #include "attention.cuh"
@@ -149,6 +150,48 @@ int pick_bn(int n) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Tensor maps of activation buffers, memoised per device: a map is a pure
+// function of its encode arguments (kind, base address, extents, box), so a
+// hit returns exactly what encoding again would. Calls with the same batch
+// shape (a serving loop, benchmark repeats) then encode nothing on the host.
+struct MapKey {
+  int kind;
+  const void* base;
+  uint64_t a, b, c, d;
+  bool operator==(const MapKey& o) const {
+    return kind == o.kind && base == o.base && a == o.a && b == o.b && c == o.c && d == o.d;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&](uint64_t v) { h = (h ^ v) * 1099511628211ull; };
+    mix((uint64_t)k.kind);
+    mix((uint64_t)(uintptr_t)k.base);
+    mix(k.a);
+    mix(k.b);
+    mix(k.c);
+    mix(k.d);
+    return (size_t)h;
+  }
+};
+struct MapCache {
+  std::unordered_map<MapKey, CUtensorMap, MapKeyHash> maps;
+  template <typename Make>
+  bool get(const MapKey& k, CUtensorMap* out, Make&& make) {
+    auto it = maps.find(k);
+    if (it != maps.end()) {
+      *out = it->second;
+      return true;
+    }
+    if (!make(out)) return false;
+    if (maps.size() >= 4096) maps.clear();  // many distinct batch shapes: start over
+    maps.emplace(k, *out);
+    return true;
+  }
+};
+enum MapKind : int { kMapOperand = 1, kMapOutput = 2, kMapQkv = 3 };
+
 // ---------------------------------------------------------------------------
 // Model state
 // ---------------------------------------------------------------------------
@@ -213,6 +256,7 @@ struct DevCtx {
   // waits on it first. Calls may use different streams (encode_device takes
   // the caller's), and they share the workspace and the meta buffer.
   cudaEvent_t done_evt = nullptr;
+  MapCache map_cache;  // activation tensor maps (guarded by mu)
   std::vector<cudaEvent_t> out_evts;  // host-buffer calls: one per micro-batch's D2H
   std::atomic<long long> launches{0};
   // Optional per-stage profiler (CUDA events around each launch).
@@ -571,18 +615,27 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
                        (double)M * w.n * rsz + (o.out_f32_copy ? (double)M * w.n * 4.0 : 0.0);
   ProfScope prof(d, st, stage, 2.0 * M * w.n * w.k, bytes);
   CUtensorMap ta, to;
-  if (!make_operand_map(&ta, A, s8, (uint64_t)M, (uint64_t)w.k, 128))
+  auto operand_map = [&](CUtensorMap* map, const void* base, bool is_s8, uint64_t rows,
+                         uint64_t cols) {
+    return d.map_cache.get(MapKey{kMapOperand, base, rows, cols, is_s8 ? 1u : 0u, 128}, map,
+                           [&](CUtensorMap* mm) {
+                             return make_operand_map(mm, base, is_s8, rows, cols, 128);
+                           });
+  };
+  if (!operand_map(&ta, A, s8, (uint64_t)M, (uint64_t)w.k))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (activation)");
   // bf16 outputs leave through TMA tile stores.
   const bool bf16_out = o.epi == kEpiResidLN || !(o.out_f32 || (s8 && !plain));
   if (bf16_out) {
     const uint64_t ncols = o.epi == kEpiSwiglu ? (uint64_t)w.n / 2 : (uint64_t)w.n;
-    if (!make_output_map(&to, o.out, (uint64_t)M, ncols, (uint64_t)o.ldo))
+    const MapKey key{kMapOutput, o.out, (uint64_t)M, ncols, (uint64_t)o.ldo, 0};
+    if (!d.map_cache.get(key, &to, [&](CUtensorMap* mm) {
+          return make_output_map(mm, o.out, (uint64_t)M, ncols, (uint64_t)o.ldo);
+        }))
       return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (output)");
   }
   CUtensorMap tr;
-  if (o.epi == kEpiResidLN &&
-      !make_operand_map(&tr, o.resid, false, (uint64_t)M, (uint64_t)w.n, 128))
+  if (o.epi == kEpiResidLN && !operand_map(&tr, o.resid, false, (uint64_t)M, (uint64_t)w.n))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (residual)");
   GemmLaunch g;
   g.ta = &ta;
@@ -685,7 +738,12 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
       // q, k, v tiles of one head: 128 rows × hd columns, swizzled over one row.
       AttnMaps maps{};
       for (int n = 1; n <= 8; ++n)
-        if (!make_qkv_map(&maps.m[n], qkv, (uint64_t)T, (uint64_t)(3 * h), hd, 16u * n))
+        if (!d.map_cache.get(MapKey{kMapQkv, qkv, (uint64_t)T, (uint64_t)(3 * h), (uint64_t)hd,
+                                    16u * n},
+                             &maps.m[n], [&](CUtensorMap* mm) {
+                               return make_qkv_map(mm, qkv, (uint64_t)T, (uint64_t)(3 * h), hd,
+                                                   16u * n);
+                             }))
           return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
       auto launch = [&](auto kern, int smem) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -706,7 +764,12 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
       // over one row.
       const int nh = attn_heads_per_step(hd, H);
       CUtensorMap tm;
-      if (!make_qkv_map(&tm, qkv, (uint64_t)T, (uint64_t)(3 * h), nh * hd, 64))
+      if (!d.map_cache.get(MapKey{kMapQkv, qkv, (uint64_t)T, (uint64_t)(3 * h),
+                                  (uint64_t)(nh * hd), 64},
+                           &tm, [&](CUtensorMap* mm) {
+                             return make_qkv_map(mm, qkv, (uint64_t)T, (uint64_t)(3 * h), nh * hd,
+                                                 64);
+                           }))
         return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
       const int ways = attn_split_ways(m, d, grid, H / nh);
       auto launch = [&](auto kern, int smem) -> cudaError_t {
