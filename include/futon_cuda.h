@@ -90,7 +90,9 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
                             const int* devices, int ndev, int q8, futon_model** out, char* err,
                             size_t errlen);
 
-/* Releases every device buffer. Callers must not race it with encode. */
+/* Waits for the model's last queued call on every device, then releases
+ * every device buffer. Callers must not race it with encode: a host binding
+ * refuses new calls and waits for calls in flight first (Provider.Close). */
 void futon_cuda_model_destroy(futon_model* model);
 
 /* Encodes nseq packed sequences on the model's device number `device`
@@ -117,6 +119,9 @@ int futon_cuda_encode_batch(futon_model* model, const int32_t* ids, const int32_
  * memory (it plans the micro-batches). Work is queued on `stream`
  * (cudaStream_t, NULL = the library's stream for that device) and the call
  * returns without waiting; futon_cuda_sync reports completion and errors.
+ * Calls on one device run on the GPU in the order they were made, whatever
+ * their streams (each call's stream first waits for the previous call's
+ * end: they share the device's activation workspace).
  * NULL buffers with nseq > 0 are refused (FUTON_EINVAL) before any launch. */
 int futon_cuda_encode_device(futon_model* model, int device, const int32_t* d_ids,
                              const int32_t* cu_seqlens, int nseq, int out_dim, float* d_out,
@@ -143,7 +148,10 @@ int futon_cuda_profile_read(futon_model* model, int device, int stage, double* m
 int futon_cuda_profile_stage_count(void);
 const char* futon_cuda_profile_stage_name(int stage);
 
-/* ---- Kernel seam (device pointers, CUDA device `cuda_device`) ---- */
+/* ---- Kernel seam (device pointers, CUDA device `cuda_device`) ----
+ * Safe to call from several host threads: calls on one device take turns
+ * (they share that device's scratch and error word) and each waits for its
+ * stream before returning. */
 
 /* dst[m×n] = a[m×k] · b[n×k]ᵀ (+ bias[n]) on the tcgen05 tensor cores with
  * bf16 operands and f32 accumulation. k % 8 == 0. Uses library-managed
