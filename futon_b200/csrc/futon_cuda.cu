@@ -9,9 +9,12 @@
 //     (the pack's nn.Linear layout), or int8 + per-row f32 scales on the Q8
 //     path; biases and LayerNorm parameters f32;
 //   rotary cos/sin tables [max_trained, hd/2] f32 (RoPE packs).
-// Activations of one micro-batch of T packed tokens: x [T, h] f32 (residual
-// stream), xb [T, h] bf16 (GEMM operand), qkv [T, 3h] bf16, attn [T, h],
-// ffn [T, inter], tmp [T, h] f32 (pre-LayerNorm sums), int8 copies on Q8.
+// Activations of one micro-batch of T packed tokens: the residual stream —
+// xb [T, h] bf16 on the float path (also the GEMMs' A operand, updated in
+// place by the fused residual + LayerNorm epilogues), x [T, h] f32 plus its
+// int8 codes on the Q8 path — qkv [T, 3h], attn [T, h], ffn [T, inter],
+// xf [T, h] f32 (final hidden rows for pooling), tmp [T, h] f32
+// (pre-LayerNorm sums where LayerNorm is not fused).
 //
 // One forward = embed+LN, then per layer: qkv GEMM, attention, out GEMM with
 // residual, LN, fc1 GEMM with GELU or SwiGLU, fc2 GEMM with residual, LN;
