@@ -28,7 +28,7 @@ from typing import Dict, List, Optional, Sequence
 import numpy as np
 
 from . import _lib
-from ._lib import CanceledError, FutonError
+from ._lib import FutonError
 from .pack import (ACT_SWIGLU, POOL_MEAN, POS_ROPE, PackConfig, PackError, load_pack)
 
 NATIVE_MODEL_NAME_PREFIX = "native/"

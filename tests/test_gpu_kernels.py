@@ -3,8 +3,6 @@ quantizeRowQ8) through the C ABI, mirroring native/kernel_test.go and
 native/quant_test.go."""
 from __future__ import annotations
 
-import ctypes as C
-
 import numpy as np
 import pytest
 
