@@ -387,7 +387,9 @@ def main():
                        "12 heads, FFN 1536, GELU, CLS)", "seqs_per_rank": nseq,
                        "tokens_per_rank": ntok, "global_batch": nseq * world,
                        "parallelism": f"dp{world}",
-                       "l2": "working set > L2 (per micro-batch activations ~1.3 GB)"},
+                       "l2": "working set > L2 (per micro-batch activations ~1.3 GB)",
+                       "attention": {"kernel": os.environ.get("FUTON_CUDA_ATTN") or "heads",
+                                     "split": os.environ.get("FUTON_CUDA_ATTN_SPLIT") == "1"}},
             "tokens_per_sec": round(world * ntok / (ms / 1e3), 1),
             "tflops": round(world * flops / (ms / 1e3) / 1e12, 1),
             "frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
