@@ -42,6 +42,7 @@
 
 #include "attention.cuh"
 #include "attention_tc.cuh"
+#include "attn_exact.cuh"
 #include "common.cuh"
 #include "gemm_launch.cuh"
 #include "rowops.cuh"
@@ -248,6 +249,8 @@ struct DevCtx {
   size_t d_meta_cap = 0;
   float* d_out = nullptr;
   size_t d_out_cap = 0;
+  float* d_pscr = nullptr;  // exact int8-path attention: rows of P for a head group
+  size_t d_pscr_cap = 0;
   int* h_meta = nullptr;  // pinned
   size_t h_meta_cap = 0;
   int* h_ids = nullptr;   // pinned
@@ -280,6 +283,7 @@ struct DevCtx {
     if (d_ids) cudaFree(d_ids);
     if (d_meta) cudaFree(d_meta);
     if (d_out) cudaFree(d_out);
+    if (d_pscr) cudaFree(d_pscr);
     if (h_meta) cudaFreeHost(h_meta);
     if (h_ids) cudaFreeHost(h_ids);
     if (h_out) cudaFreeHost(h_out);
@@ -308,6 +312,9 @@ struct futon_model {
   // FUTON_CUDA_ATTN_SPLIT=1: attn_heads_kernel launches with the head groups
   // shared among grid.y CTAs when the tiles alone would leave SMs idle.
   bool attn_split = false;
+  // FUTON_CUDA_Q8_ATTN=exact: the int8 path's attention runs in the
+  // reference's exact float32 operation order (attn_exact.cuh).
+  bool q8_exact_attn = false;
   std::vector<std::unique_ptr<DevCtx>> devs;
 };
 
@@ -700,6 +707,7 @@ void read_attn_env(futon_model& m) {
     else if (!strcmp(v, "heads")) m.attn_kind = kAttnHeads;
   }
   if (const char* v = std::getenv("FUTON_CUDA_ATTN_SPLIT")) m.attn_split = !strcmp(v, "1");
+  if (const char* v = std::getenv("FUTON_CUDA_Q8_ATTN")) m.q8_exact_attn = !strcmp(v, "exact");
 }
 
 // CTAs per tile (grid.y) for attn_heads_kernel's head-group split: enough to
@@ -718,6 +726,13 @@ struct AttnPlan {
   const AttnWindow* wins;
   int nwin;
   const AttnSeg* segs;
+  // Exact int8-path attention: per-sequence offsets of P (all query rows /
+  // the CLS row only), their totals, the scratch and heads per launch.
+  const int* poff = nullptr;
+  const int* pcls = nullptr;
+  size_t ptot = 0, ptot_cls = 0;
+  float* pscr = nullptr;
+  int head_group = 0;
 };
 
 // q and k arrive already rotated (RoPE runs in the qkv GEMM epilogue).
@@ -794,6 +809,32 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
       return FUTON_OK;
     }
   } else {
+    if (plan.pscr && tc_hd) {
+      // Exact operation order (attn_exact.cuh), head groups of plan.head_group.
+      const int grid = cls_only ? nseq : ntiles;
+      if (grid == 0) return FUTON_OK;
+      const int* poff = cls_only ? plan.pcls : plan.poff;
+      const size_t pstride = cls_only ? plan.ptot_cls : plan.ptot;
+      const float scale = (float)(1.0 / std::sqrt((double)hd));
+      const int cls = cls_only ? 1 : 0;
+      for (int h0 = 0; h0 < H; h0 += plan.head_group) {
+        const unsigned nh = (unsigned)std::min(plan.head_group, H - h0);
+        if (hd == 32) {
+          attn_exact_softmax_kernel<32><<<dim3(grid, nh), 64, 0, st>>>(
+              qkv, h, h0, cu, tiles, cls, poff, pstride, scale, plan.pscr);
+          attn_exact_pv_kernel<32><<<dim3(grid, 4, nh), 256, 0, st>>>(
+              qkv, h, h0, cu, tiles, cls, poff, pstride, plan.pscr, out, h);
+        } else {
+          attn_exact_softmax_kernel<64><<<dim3(grid, nh), 64, 0, st>>>(
+              qkv, h, h0, cu, tiles, cls, poff, pstride, scale, plan.pscr);
+          attn_exact_pv_kernel<64><<<dim3(grid, 4, nh), 256, 0, st>>>(
+              qkv, h, h0, cu, tiles, cls, poff, pstride, plan.pscr, out, h);
+        }
+        CU_TRY(cudaGetLastError());
+        d.launches.fetch_add(2, std::memory_order_relaxed);
+      }
+      return FUTON_OK;
+    }
     if (tc_hd && !cls_only && ntiles > 0) {
       dim3 grid(ntiles, H);
       const int smem = 6 * 64 * (hd + 8) * 2;
@@ -1012,6 +1053,9 @@ struct MicroBatch {
   size_t cu_off, tile_off, win_off, seg_off;  // int offsets into the meta buffer
   int ntiles, nwin, nseg;
   double sum_l2;            // Σ L² (profiler)
+  // Exact int8-path attention: offsets of the P row blocks (meta) and totals.
+  size_t poff_off = 0, pcls_off = 0;
+  size_t ptot = 0, ptot_cls = 0;
 };
 
 // Attention windows of sequences [s0, s1) (token offsets relative to t0):
@@ -1089,8 +1133,8 @@ int check_ids(const futon_model& m, const int32_t* ids, const int32_t* cu, int n
 }
 
 // Plans micro-batches, fills the pinned meta buffer, uploads it (one copy).
-int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, std::vector<MicroBatch>& mbs,
-                    cudaStream_t st, char* err, size_t errlen) {
+int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, bool exact_p,
+                    std::vector<MicroBatch>& mbs, cudaStream_t st, char* err, size_t errlen) {
   mbs.clear();
   size_t meta = 0;
   for (int s = 0; s < nseq;) {
@@ -1119,6 +1163,22 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, std::vector<MicroBat
     meta += align_up((size_t)mb.nwin * 6, 4);
     mb.seg_off = meta;
     meta += align_up((size_t)mb.nseg * 3, 4);
+    if (exact_p) {
+      // P holds pad8(L) keys × L query rows per sequence (1 row for the CLS
+      // layer); offsets are int, so a micro-batch's total must fit in one.
+      for (int q = mb.s0; q < mb.s1; ++q) {
+        const size_t L = (size_t)(cu[q + 1] - cu[q]), kp = (L + 7) & ~(size_t)7;
+        mb.ptot += kp * L;
+        mb.ptot_cls += kp;
+      }
+      if (mb.ptot > (size_t)INT32_MAX)
+        return set_err(err, errlen, FUTON_EINVAL,
+                       "native: micro-batch too large for the exact int8 attention");
+      mb.poff_off = meta;
+      meta += align_up((size_t)(mb.s1 - mb.s0 + 1), 4);
+      mb.pcls_off = meta;
+      meta += align_up((size_t)(mb.s1 - mb.s0 + 1), 4);
+    }
     mbs.push_back(mb);
   }
   if (mbs.empty()) return FUTON_OK;
@@ -1137,6 +1197,16 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, std::vector<MicroBat
     int nseg = 0;
     plan_windows(cu, mb.s0, mb.s1, mb.t0, reinterpret_cast<AttnWindow*>(d.h_meta + mb.win_off),
                  reinterpret_cast<AttnSeg*>(d.h_meta + mb.seg_off), &nseg);
+    if (exact_p) {
+      int* po = d.h_meta + mb.poff_off;
+      int* pc = d.h_meta + mb.pcls_off;
+      po[0] = pc[0] = 0;
+      for (int q = mb.s0; q < mb.s1; ++q) {
+        const int L = cu[q + 1] - cu[q], kp = (L + 7) & ~7;
+        po[q - mb.s0 + 1] = po[q - mb.s0] + kp * L;
+        pc[q - mb.s0 + 1] = pc[q - mb.s0] + kp;
+      }
+    }
   }
   CU_TRY(cudaMemcpyAsync(d.d_meta, d.h_meta, meta * sizeof(int), cudaMemcpyHostToDevice, st));
   CU_TRY(cudaEventRecord(d.meta_evt, st));
@@ -1161,18 +1231,38 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
   } record_done{d, st};
   std::vector<MicroBatch> mbs;
   int rc;
-  if ((rc = plan_and_upload(d, cu, nseq, mbs, st, err, errlen))) return rc;
-  size_t max_t = 0;
-  for (const MicroBatch& mb : mbs) max_t = std::max<size_t>(max_t, (size_t)(mb.t1 - mb.t0));
+  const bool exact_p = m.q8 && m.q8_exact_attn && (m.head_dim == 32 || m.head_dim == 64);
+  if ((rc = plan_and_upload(d, cu, nseq, exact_p, mbs, st, err, errlen))) return rc;
+  size_t max_t = 0, max_p = 0;
+  for (const MicroBatch& mb : mbs) {
+    max_t = std::max<size_t>(max_t, (size_t)(mb.t1 - mb.t0));
+    max_p = std::max(max_p, mb.ptot);
+  }
   if ((rc = ensure_workspace(m, d, max_t, err, errlen))) return rc;
+  // Exact attention scratch: as many heads per launch as fit in 4 GiB.
+  int head_group = 0;
+  if (exact_p && max_p > 0) {
+    const size_t budget = (size_t)1 << 30;  // floats
+    head_group = (int)std::max<size_t>(1, std::min<size_t>((size_t)m.cfg.num_heads, budget / max_p));
+    if ((rc = ensure_dev(&d.d_pscr, &d.d_pscr_cap, (size_t)head_group * max_p, err, errlen)))
+      return rc;
+  }
   const int dim = out_dim ? out_dim : m.cfg.hidden_size;
   for (size_t i = 0; i < mbs.size(); ++i) {
     const MicroBatch& mb = mbs[i];
     if (cancel && *cancel)
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
-    const AttnPlan plan{reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
-                        reinterpret_cast<const AttnWindow*>(d.d_meta + mb.win_off), mb.nwin,
-                        reinterpret_cast<const AttnSeg*>(d.d_meta + mb.seg_off)};
+    AttnPlan plan{reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
+                  reinterpret_cast<const AttnWindow*>(d.d_meta + mb.win_off), mb.nwin,
+                  reinterpret_cast<const AttnSeg*>(d.d_meta + mb.seg_off)};
+    if (head_group > 0) {
+      plan.poff = d.d_meta + mb.poff_off;
+      plan.pcls = d.d_meta + mb.pcls_off;
+      plan.ptot = mb.ptot;
+      plan.ptot_cls = mb.ptot_cls;
+      plan.pscr = d.d_pscr;
+      plan.head_group = head_group;
+    }
     if ((rc = forward_mb(m, d, d_ids + mb.t0, d.d_meta + mb.cu_off, mb.s1 - mb.s0, mb.t1 - mb.t0,
                          mb.sum_l2, plan, out_dim, d_out + (size_t)mb.s0 * dim, st, cancel, err,
                          errlen)))

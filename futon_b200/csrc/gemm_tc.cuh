@@ -395,18 +395,30 @@ __device__ __forceinline__ int seq_position(const int* cu, int nseq, int row) {
   return row - cu[lo];
 }
 
+// One NeoX rotation pair of the int8 path (rotateHalf, model.go:703-712):
+// each product and sum rounded separately, as the reference does.
+__device__ __forceinline__ void rope_pair_exact(float& x1, float& x2, float c, float sn) {
+  const float a = x1, b = x2;
+  x1 = fsub(fmul(a, c), fmul(b, sn));
+  x2 = fadd(fmul(b, c), fmul(a, sn));
+}
+
 // Rotates the 32 values of one chunk in place: heads of HD ≤ 32 lie inside
-// the chunk (pairs i, i + HD/2 of each head).
-template <int HD>
+// the chunk (pairs i, i + HD/2 of each head). EXACT: rope_pair_exact.
+template <int HD, bool EXACT>
 __device__ __forceinline__ void rope_in_chunk(float (&v)[32], const float* cr, const float* sr) {
   constexpr int kHalf = HD / 2;
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     if ((i % HD) < kHalf) {
-      const float c = cr[i % HD], sn = sr[i % HD];
-      const float x1 = v[i], x2 = v[i + kHalf];
-      v[i] = x1 * c - x2 * sn;
-      v[i + kHalf] = x2 * c + x1 * sn;
+      if constexpr (EXACT) {
+        rope_pair_exact(v[i], v[i + kHalf], cr[i % HD], sr[i % HD]);
+      } else {
+        const float c = cr[i % HD], sn = sr[i % HD];
+        const float x1 = v[i], x2 = v[i + kHalf];
+        v[i] = x1 * c - x2 * sn;
+        v[i + kHalf] = x2 * c + x1 * sn;
+      }
     }
   }
 }
@@ -475,9 +487,13 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
         if (col0 + c < ep.rope_cols) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            const float x1 = a[i], x2 = b[i], cc = cr[i], sn = sr[i];
-            a[i] = x1 * cc - x2 * sn;
-            b[i] = x2 * cc + x1 * sn;
+            if constexpr (S8) {
+              rope_pair_exact(a[i], b[i], cr[i], sr[i]);
+            } else {
+              const float x1 = a[i], x2 = b[i], cc = cr[i], sn = sr[i];
+              a[i] = x1 * cc - x2 * sn;
+              b[i] = x2 * cc + x1 * sn;
+            }
           }
         }
         sink.put(a, col0 + c, row0);
@@ -510,9 +526,9 @@ __device__ __forceinline__ void epilogue_row(uint32_t taddr, int row, int row0, 
         float v[32];
         acc_apply<S8>(u, a_s, ep, k, v);
         if (rope && col0 + c < ep.rope_cols) {
-          if (hd == 32) rope_in_chunk<32>(v, cr, sr);
-          else if (hd == 16) rope_in_chunk<16>(v, cr, sr);
-          else rope_in_chunk<8>(v, cr, sr);
+          if (hd == 32) rope_in_chunk<32, S8>(v, cr, sr);
+          else if (hd == 16) rope_in_chunk<16, S8>(v, cr, sr);
+          else rope_in_chunk<8, S8>(v, cr, sr);
         }
         sink.put(v, col0 + c, row0);
       }

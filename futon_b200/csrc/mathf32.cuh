@@ -12,18 +12,55 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <cstdint>
+#include <cstring>
+
+// FUTON_HD marks the exact-order f32 primitives that host code can call too
+// (CPU unit tests of the device arithmetic compile them with a host C++
+// compiler and -ffp-contract=off); device code is unchanged by it.
+#if defined(__CUDACC__)
+#define FUTON_HD __host__ __device__
+#else
+#define FUTON_HD
+#endif
 
 namespace futon {
 
-__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
-__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
-__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+FUTON_HD __forceinline__ float fmul(float a, float b) {
+#ifdef __CUDA_ARCH__
+  return __fmul_rn(a, b);
+#else
+  return a * b;
+#endif
+}
+FUTON_HD __forceinline__ float fadd(float a, float b) {
+#ifdef __CUDA_ARCH__
+  return __fadd_rn(a, b);
+#else
+  return a + b;
+#endif
+}
+FUTON_HD __forceinline__ float fsub(float a, float b) {
+#ifdef __CUDA_ARCH__
+  return __fsub_rn(a, b);
+#else
+  return a - b;
+#endif
+}
+FUTON_HD __forceinline__ float f32_from_bits(int32_t b) {
+#ifdef __CUDA_ARCH__
+  return __int_as_float(b);
+#else
+  float f;
+  std::memcpy(&f, &b, sizeof f);
+  return f;
+#endif
+}
 
 constexpr float kExpOverflowF32 = 88.72283f;   // ln(MaxFloat32)
 constexpr float kExpUnderflowF32 = -87.33654f; // ln(2^-126)
 constexpr float kExpClampLo = -104.0f;
 
-__device__ __forceinline__ float exp_f32(float x) {
+FUTON_HD __forceinline__ float exp_f32(float x) {
   if (x < kExpUnderflowF32) return 0.0f;
   float kf = fsub(fadd(fmul(x, 1.4426950408889634f), 12582912.0f), 12582912.0f);
   int32_t k = (int32_t)kf;
@@ -38,8 +75,8 @@ __device__ __forceinline__ float exp_f32(float x) {
   p = fadd(fmul(fadd(fmul(p, r), 1.0f), r), 1.0f);
   int32_t e = k + 127;
   if (e <= 0) return 0.0f;
-  if (e >= 255) return fmul(fmul(p, __int_as_float((e - 1) << 23)), 2.0f);
-  return fmul(p, __int_as_float(e << 23));
+  if (e >= 255) return fmul(fmul(p, f32_from_bits((e - 1) << 23)), 2.0f);
+  return fmul(p, f32_from_bits(e << 23));
 }
 
 __device__ __forceinline__ float erfc_pos_f32(float a) {

@@ -447,12 +447,6 @@ static void mmt(const fo_model *m, float *dst, const float *a, int li, int slot,
     else fo_matmul_t(dst, a, w, rows, n, k, bias);
 }
 
-static void kmm(const fo_model *m, float *dst, const float *a, const float *b, int rows, int n,
-                int k) {
-    if (m->gemm_mode == FO_GEMM_AVX2) fo_matmul_t_avx2(dst, a, b, rows, n, k, NULL);
-    else fo_matmul_t(dst, a, b, rows, n, k, NULL);
-}
-
 typedef struct {
     float *x, *pooled, *qkv, *q, *k, *vT, *scores, *head_out, *attn_cat, *attn_out, *ffn_h,
         *ffn_gate, *ffn_out;
@@ -460,38 +454,68 @@ typedef struct {
 
 static int pad_seq(int seq) { return (seq + 7) & ~7; } /* model.go:532 */
 
-/* attendHead, model.go:646-701. */
-static void attend_head(const fo_model *m, scratch_t *s, int head, int seq, int rows) {
-    int h = m->cfg.hidden, hd = m->head_dim, half = hd / 2;
+/* attendHead, model.go:646-701, for one head of one sequence: qkv holds the
+ * sequence's [seq, 3h] rows; the first `rows` queries (seq, or 1 for the
+ * CLS-pruned last layer, model.go:403-410) attend over all seq keys (padded
+ * to a multiple of 8 with zeros, model.go:532); head_out receives [rows, hd].
+ * rope_cos/rope_sin ([positions, hd/2]) are NULL for absolute-position packs.
+ * q [seq, hd], k [kp, hd], vT [hd, kp] and scores [rows, kp] are scratch. */
+static void attend_head_core(int gemm_mode, const float *qkv, int seq, int rows, int h, int hd,
+                             int head, const float *rope_cos, const float *rope_sin, float *q,
+                             float *k, float *vT, float *scores, float *head_out) {
+    int half = hd / 2;
     float scale = (float)(1.0 / sqrt((double)hd));
     int kp = pad_seq(seq);
-    memset(s->k + (size_t)seq * hd, 0, sizeof(float) * (size_t)(kp - seq) * hd);
+    memset(k + (size_t)seq * hd, 0, sizeof(float) * (size_t)(kp - seq) * hd);
     for (int d = 0; d < hd; d++)
-        memset(s->vT + (size_t)d * kp + seq, 0, sizeof(float) * (size_t)(kp - seq));
+        memset(vT + (size_t)d * kp + seq, 0, sizeof(float) * (size_t)(kp - seq));
     int qo = head * hd, ko = h + head * hd, vo = 2 * h + head * hd;
     for (int t = 0; t < seq; t++) {
-        const float *row = s->qkv + (size_t)t * 3 * h;
-        if (t < rows) memcpy(s->q + (size_t)t * hd, row + qo, sizeof(float) * hd);
-        memcpy(s->k + (size_t)t * hd, row + ko, sizeof(float) * hd);
-        for (int d = 0; d < hd; d++) s->vT[(size_t)d * kp + t] = row[vo + d];
+        const float *row = qkv + (size_t)t * 3 * h;
+        if (t < rows) memcpy(q + (size_t)t * hd, row + qo, sizeof(float) * hd);
+        memcpy(k + (size_t)t * hd, row + ko, sizeof(float) * hd);
+        for (int d = 0; d < hd; d++) vT[(size_t)d * kp + t] = row[vo + d];
     }
-    if (m->cfg.rope) {
+    if (rope_cos) {
         for (int t = 0; t < seq; t++) {
-            const float *c = m->rope_cos + (size_t)t * half, *sn = m->rope_sin + (size_t)t * half;
-            if (t < rows) rotate_half(s->q + (size_t)t * hd, c, sn, half);
-            rotate_half(s->k + (size_t)t * hd, c, sn, half);
+            const float *c = rope_cos + (size_t)t * half, *sn = rope_sin + (size_t)t * half;
+            if (t < rows) rotate_half(q + (size_t)t * hd, c, sn, half);
+            rotate_half(k + (size_t)t * hd, c, sn, half);
         }
     }
-    kmm(m, s->scores, s->q, s->k, rows, kp, hd);
+    if (gemm_mode == FO_GEMM_AVX2) fo_matmul_t_avx2(scores, q, k, rows, kp, hd, NULL);
+    else fo_matmul_t(scores, q, k, rows, kp, hd, NULL);
     for (int t = 0; t < rows; t++) {
-        float *row = s->scores + (size_t)t * kp;
+        float *row = scores + (size_t)t * kp;
         fo_softmax_scaled(row, seq, scale);
         memset(row + seq, 0, sizeof(float) * (size_t)(kp - seq));
     }
-    kmm(m, s->head_out, s->scores, s->vT, rows, hd, kp);
+    if (gemm_mode == FO_GEMM_AVX2) fo_matmul_t_avx2(head_out, scores, vT, rows, hd, kp, NULL);
+    else fo_matmul_t(head_out, scores, vT, rows, hd, kp, NULL);
+}
+
+static void attend_head(const fo_model *m, scratch_t *s, int head, int seq, int rows) {
+    int h = m->cfg.hidden, hd = m->head_dim;
+    attend_head_core(m->gemm_mode, s->qkv, seq, rows, h, hd, head,
+                     m->cfg.rope ? m->rope_cos : NULL, m->cfg.rope ? m->rope_sin : NULL, s->q,
+                     s->k, s->vT, s->scores, s->head_out);
     for (int t = 0; t < rows; t++)
         memcpy(s->attn_cat + (size_t)t * h + head * hd, s->head_out + (size_t)t * hd,
                sizeof(float) * hd);
+}
+
+int fo_attend_head(const float *qkv, int seq, int rows, int h, int hd, int head,
+                   const float *rope_cos, const float *rope_sin, int gemm_mode, float *out) {
+    if (seq <= 0 || rows <= 0 || rows > seq || hd <= 0 || h % hd || head < 0 || head >= h / hd)
+        return -1;
+    int kp = pad_seq(seq);
+    size_t n = (size_t)seq * hd + (size_t)kp * hd + (size_t)hd * kp + (size_t)rows * kp;
+    float *buf = (float *)calloc(n, sizeof(float));
+    if (!buf) return -1;
+    float *q = buf, *k = q + (size_t)seq * hd, *vT = k + (size_t)kp * hd, *sc = vT + (size_t)hd * kp;
+    attend_head_core(gemm_mode, qkv, seq, rows, h, hd, head, rope_cos, rope_sin, q, k, vT, sc, out);
+    free(buf);
+    return 0;
 }
 
 static void add_into(float *dst, const float *src, size_t n) {

@@ -118,6 +118,12 @@ float fo_exp(float x);
 float fo_gelu(float x);
 float fo_sigmoid(float x);
 void fo_rope_tables(int max_seq, int head_dim, double theta, float *cos_out, float *sin_out);
+/* attendHead (model.go:646-701) for head `head` of one sequence: qkv is its
+ * [seq, 3h] float32 block, the first `rows` queries attend over all seq keys,
+ * out receives [rows, hd]. rope_cos/rope_sin ([seq or more, hd/2]) are NULL
+ * for absolute-position packs. Returns 0, or -1 on a bad shape. */
+int fo_attend_head(const float *qkv, int seq, int rows, int h, int hd, int head,
+                   const float *rope_cos, const float *rope_sin, int gemm_mode, float *out);
 int fo_has_avx2(void);
 
 #ifdef __cplusplus

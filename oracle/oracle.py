@@ -83,6 +83,8 @@ def lib() -> C.CDLL:
             getattr(L, name).argtypes = [fp]
         L.fo_rope_tables.argtypes = [ip, ip, C.c_double, vp, vp]
         L.fo_has_avx2.restype = ip
+        L.fo_attend_head.restype = ip
+        L.fo_attend_head.argtypes = [vp, ip, ip, ip, ip, ip, vp, vp, ip, vp]
         _lib = L
     return _lib
 
@@ -249,6 +251,23 @@ def rope_tables(max_seq: int, head_dim: int, theta: float):
     s = np.zeros((max_seq, half), dtype=np.float32)
     lib().fo_rope_tables(max_seq, head_dim, theta, c.ctypes.data, s.ctypes.data)
     return c, s
+
+
+def attend_head(qkv, hd: int, head: int, rows: Optional[int] = None, rope=None,
+                gemm: int = GEMM_GO) -> np.ndarray:
+    """attendHead (model.go:646-701) for one head of one sequence: qkv is its
+    [seq, 3h] float32 block; the first `rows` queries (default: all) attend
+    over every key; rope = (cos, sin) tables [positions, hd/2] or None.
+    Returns [rows, hd]."""
+    qkv = _f32(qkv)
+    seq, h = qkv.shape[0], qkv.shape[1] // 3
+    rows = seq if rows is None else rows
+    out = np.zeros((rows, hd), dtype=np.float32)
+    rc, rs = (None, None) if rope is None else (_f32(rope[0]), _f32(rope[1]))
+    if lib().fo_attend_head(qkv.ctypes.data, seq, rows, h, hd, head, _ptr(rc), _ptr(rs), gemm,
+                            out.ctypes.data):
+        raise OracleError("fo_attend_head: bad shape")
+    return out
 
 
 def has_avx2() -> bool:

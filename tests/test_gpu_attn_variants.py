@@ -11,6 +11,11 @@ default `-m gpu` suite does not select them.
 - tc: the tcgen05 attention kernel; parity with the oracle (cosine gate)
   and batch invariance (a sequence's vector does not depend on what it is
   packed with).
+- FUTON_CUDA_Q8_ATTN=exact: the int8 path's attention in the reference's
+  exact float32 operation order (avx2Kernel MatMulT, softmaxScaled); its
+  arithmetic is checked bit for bit on the CPU by test_attn_exact_host.py.
+  On the GPU the int8 forward must then sit within float32 noise of the
+  oracle's int8 forward (avx2Kernel order), far inside the 0.9999 gate.
 """
 from __future__ import annotations
 
@@ -42,12 +47,12 @@ def weights(arch, layers=None):
     return _weights[key]
 
 
-def encode(monkeypatch, env, cfg, w, ids, cu, out_dim=0):
-    for k in ("FUTON_CUDA_ATTN", "FUTON_CUDA_ATTN_SPLIT"):
+def encode(monkeypatch, env, cfg, w, ids, cu, out_dim=0, q8=False):
+    for k in ("FUTON_CUDA_ATTN", "FUTON_CUDA_ATTN_SPLIT", "FUTON_CUDA_Q8_ATTN"):
         monkeypatch.delenv(k, raising=False)
     for k, v in env.items():
         monkeypatch.setenv(k, v)
-    m = Model(cfg, w, devices=[0])
+    m = Model(cfg, w, devices=[0], q8=q8)
     try:
         return m.encode_packed(ids, cu, out_dim=out_dim)
     finally:
@@ -90,3 +95,21 @@ def test_tc_batch_invariance(gpu, monkeypatch):
     rev_ids, rev_cu = pack_ids(seqs[::-1])
     rev = encode(monkeypatch, env, cfg, w, rev_ids, rev_cu)[::-1]
     assert np.array_equal(packed, rev), "tc attention: a vector depends on its batch neighbours"
+
+
+@pytest.mark.parametrize("arch,inputs,nseq,layers", [
+    ("arctic", "c3", 2, 3),   # RoPE, SwiGLU, CLS, head_dim 64, 2048 tokens
+    ("bge", "c0", 16, None),  # absolute positions, GELU, CLS, head_dim 32
+    ("nomic", "c2", 4, 2),    # mean pooling: every layer attends over all rows
+])
+def test_q8_exact_attention_vs_oracle(gpu, monkeypatch, arch, inputs, nseq, layers):
+    if not has_avx2():
+        pytest.skip("the oracle's avx2Kernel order needs an AVX2 host")
+    cfg, w = weights(arch, layers)
+    ids, cu = synth.make_inputs(inputs, nseq=nseq, vocab=cfg.vocab_size)
+    got = encode(monkeypatch, {"FUTON_CUDA_Q8_ATTN": "exact"}, cfg, w, ids, cu, q8=True)
+    want = OracleModel(cfg, w, q8=True, gemm=GEMM_AVX2).encode_batch(ids, cu)
+    cs = row_cosines(got, want)
+    same = int(np.sum(np.all(got == want, axis=1)))
+    print(f"[q8 exact] {arch}: min cos {cs.min():.9f}, {same}/{len(cs)} vectors bit-identical")
+    assert cs.min() >= 0.99999, f"{arch}: exact int8 attention min cosine {cs.min():.9f}"
