@@ -888,9 +888,14 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
     const double pos_bytes = c.position_encoding == FUTON_POS_ABSOLUTE ? 4.0 * h : 0.0;
     const double out_bytes = q8 ? 5.0 * h : 2.0 * h;
     ProfScope prof(d, st, kStEmbed, 0.0, (double)T * (4.0 + 4.0 * h + pos_bytes + out_bytes));
-    embed_ln_kernel<<<grid_rows(T, 8, d.num_sms), 256, 0, st>>>(
-        ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0, d.pos, d.embw, d.embb, eps,
-        w.x, w.xb, w.xq, w.xs);
+    if (q8 && m.q8_exact_attn)
+      embed_ln_kernel<true><<<grid_rows(T, 8, d.num_sms), 256, 0, st>>>(
+          ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0, d.pos, d.embw, d.embb,
+          eps, w.x, w.xb, w.xq, w.xs);
+    else
+      embed_ln_kernel<<<grid_rows(T, 8, d.num_sms), 256, 0, st>>>(
+          ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0, d.pos, d.embw, d.embb,
+          eps, w.x, w.xb, w.xq, w.xs);
     CU_TRY(cudaGetLastError());
     d.launches.fetch_add(1, std::memory_order_relaxed);
   }
@@ -983,8 +988,12 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       if (r2) return r2;
       ProfScope prof(d, st, kStLayerNorm, 0.0, (double)rows * h * (q8 ? 9.0 : (f32_copy ? 10.0 : 6.0)));
       float* xo = q8 ? w.x : (f32_copy ? w.xf : nullptr);
-      layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(
-          w.tmp, rows, h, lnw, lnb, eps, xo, q8 ? nullptr : w.xb, w.xq, w.xs);
+      if (q8 && m.q8_exact_attn)
+        layernorm_kernel<true><<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(
+            w.tmp, rows, h, lnw, lnb, eps, xo, nullptr, w.xq, w.xs);
+      else
+        layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(
+            w.tmp, rows, h, lnw, lnb, eps, xo, q8 ? nullptr : w.xb, w.xq, w.xs);
       CU_TRY(cudaGetLastError());
       d.launches.fetch_add(1, std::memory_order_relaxed);
       return FUTON_OK;

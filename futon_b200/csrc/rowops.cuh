@@ -62,32 +62,69 @@ __device__ __forceinline__ void warp_quant_row(const float4 (&v)[kMaxRowVec], in
   if (lane == 0) *scale_out = amax == 0.f ? 0.f : __fdiv_rn(amax, 127.0f);
 }
 
+// Row statistics in layerNormRows' exact order (model.go:743-769): one
+// lane sums the row (staged in this warp's shared-memory row `srow`) in
+// element order in float64, mean = Σx / h, then Σ (x − mean)² with every
+// product and sum rounded separately, / h. For the int8 path's exact mode,
+// whose per-row quantisation turns any float32 difference in a row's mean or
+// 1/σ into whole code steps.
+__device__ __forceinline__ void warp_row_stats_seq(const float4 (&v)[kMaxRowVec], int h, int lane,
+                                                   float* srow, double* mean_out,
+                                                   double* var_out) {
+  const int n4 = h >> 2;
+#pragma unroll
+  for (int j = 0; j < kMaxRowVec; ++j)
+    if (lane + 32 * j < n4) reinterpret_cast<float4*>(srow)[lane + 32 * j] = v[j];
+  __syncwarp();
+  double mean = 0.0, var = 0.0;
+  if (lane == 0) {
+    for (int i = 0; i < h; ++i) mean = __dadd_rn(mean, (double)srow[i]);
+    mean = __ddiv_rn(mean, (double)h);
+    for (int i = 0; i < h; ++i) {
+      const double d = __dsub_rn((double)srow[i], mean);
+      var = __dadd_rn(var, __dmul_rn(d, d));
+    }
+    var = __ddiv_rn(var, (double)h);
+  }
+  *mean_out = __shfl_sync(0xffffffffu, mean, 0);
+  *var_out = __shfl_sync(0xffffffffu, var, 0);
+  __syncwarp();  // srow is free for the warp's next row
+}
+
 // LayerNorm of a row held as float4 registers; writes f32, bf16 and
-// optionally int8 outputs.
+// optionally int8 outputs. SEQ: statistics by warp_row_stats_seq (srow: this
+// warp's h floats of shared memory); otherwise a warp-parallel float64 sum.
+template <bool SEQ = false>
 __device__ __forceinline__ void warp_layernorm_store(float4 (&v)[kMaxRowVec], int h, int lane,
                                                      const float* __restrict__ w,
                                                      const float* __restrict__ b, float eps,
                                                      float* __restrict__ xo,
                                                      __nv_bfloat16* __restrict__ xbo,
                                                      int8_t* __restrict__ xq,
-                                                     float* __restrict__ xs) {
+                                                     float* __restrict__ xs,
+                                                     float* srow = nullptr) {
   const int n4 = h >> 2;
-  double sum = 0.0;
+  double mean, var;
+  if constexpr (SEQ) {
+    warp_row_stats_seq(v, h, lane, srow, &mean, &var);
+  } else {
+    double sum = 0.0;
 #pragma unroll
-  for (int j = 0; j < kMaxRowVec; ++j)
-    if (lane + 32 * j < n4)
-      sum += ((double)v[j].x + (double)v[j].y) + ((double)v[j].z + (double)v[j].w);
-  const double mean = warp_sum_d(sum) / (double)h;
-  double var = 0.0;
+    for (int j = 0; j < kMaxRowVec; ++j)
+      if (lane + 32 * j < n4)
+        sum += ((double)v[j].x + (double)v[j].y) + ((double)v[j].z + (double)v[j].w);
+    mean = warp_sum_d(sum) / (double)h;
+    var = 0.0;
 #pragma unroll
-  for (int j = 0; j < kMaxRowVec; ++j) {
-    if (lane + 32 * j < n4) {
-      double a = (double)v[j].x - mean, bb = (double)v[j].y - mean;
-      double c = (double)v[j].z - mean, d = (double)v[j].w - mean;
-      var += (a * a + bb * bb) + (c * c + d * d);
+    for (int j = 0; j < kMaxRowVec; ++j) {
+      if (lane + 32 * j < n4) {
+        double a = (double)v[j].x - mean, bb = (double)v[j].y - mean;
+        double c = (double)v[j].z - mean, d = (double)v[j].w - mean;
+        var += (a * a + bb * bb) + (c * c + d * d);
+      }
     }
+    var = warp_sum_d(var) / (double)h;
   }
-  var = warp_sum_d(var) / (double)h;
   const float inv = (float)(1.0 / sqrt(var + (double)eps));
   const float mf = (float)mean;
 #pragma unroll
@@ -117,6 +154,8 @@ __device__ __forceinline__ void warp_layernorm_store(float4 (&v)[kMaxRowVec], in
 // One warp per token row; each warp takes a contiguous run of tokens, so the
 // sequence (for the position row) is found by one binary search per run and
 // then advanced token by token.
+// SEQ: LayerNorm statistics in the reference's exact order (int8 exact mode).
+template <bool SEQ = false>
 __global__ void __launch_bounds__(256)
     embed_ln_kernel(const int* __restrict__ ids, const int* __restrict__ cu, int nseq, int T,
                     int h, int vocab, int* __restrict__ err, const float* __restrict__ word, const float* __restrict__ type0,
@@ -170,12 +209,21 @@ __global__ void __launch_bounds__(256)
         v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
-    warp_layernorm_store(v, h, lane, w, b, eps, x ? x + (size_t)t * h : nullptr,
-                         xb ? xb + (size_t)t * h : nullptr, xq ? xq + (size_t)t * h : nullptr,
-                         xq ? xs + t : nullptr);
+    if constexpr (SEQ) {
+      __shared__ __align__(16) float srows[8][kMaxRowVec * 128];
+      warp_layernorm_store<true>(v, h, lane, w, b, eps, x ? x + (size_t)t * h : nullptr,
+                                 xb ? xb + (size_t)t * h : nullptr,
+                                 xq ? xq + (size_t)t * h : nullptr, xq ? xs + t : nullptr,
+                                 srows[threadIdx.x >> 5]);
+    } else {
+      warp_layernorm_store(v, h, lane, w, b, eps, x ? x + (size_t)t * h : nullptr,
+                           xb ? xb + (size_t)t * h : nullptr, xq ? xq + (size_t)t * h : nullptr,
+                           xq ? xs + t : nullptr);
+    }
   }
 }
 
+template <bool SEQ = false>
 __global__ void __launch_bounds__(256)
     layernorm_kernel(const float* __restrict__ in, int rows, int h, const float* __restrict__ w,
                      const float* __restrict__ b, float eps, float* __restrict__ x,
@@ -192,9 +240,17 @@ __global__ void __launch_bounds__(256)
       const int c4 = lane + 32 * j;
       v[j] = c4 < n4 ? src[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    warp_layernorm_store(v, h, lane, w, b, eps, x ? x + (size_t)r * h : nullptr,
-                         xb ? xb + (size_t)r * h : nullptr, xq ? xq + (size_t)r * h : nullptr,
-                         xq ? xs + r : nullptr);
+    if constexpr (SEQ) {
+      __shared__ __align__(16) float srows[8][kMaxRowVec * 128];
+      warp_layernorm_store<true>(v, h, lane, w, b, eps, x ? x + (size_t)r * h : nullptr,
+                                 xb ? xb + (size_t)r * h : nullptr,
+                                 xq ? xq + (size_t)r * h : nullptr, xq ? xs + r : nullptr,
+                                 srows[threadIdx.x >> 5]);
+    } else {
+      warp_layernorm_store(v, h, lane, w, b, eps, x ? x + (size_t)r * h : nullptr,
+                           xb ? xb + (size_t)r * h : nullptr, xq ? xq + (size_t)r * h : nullptr,
+                           xq ? xs + r : nullptr);
+    }
   }
 }
 
