@@ -21,6 +21,8 @@ barrier and the max-over-ranks of the timings).
          GPU, ids in HBM, CUDA events — with its fraction of the bf16 peak
   p50_batch_latency  median over 50 calls of one c0 batch (32 sequences,
          L ~ U[8, 128]) through the host-buffer C ABI, wall clock per call
+  nomic  the metric's second model: the nomic-bert-shaped encoder on 1,024
+         sequences per GPU with c2's lengths (U[64, 512]), ids in HBM
 
 `--impl reference` times that CPU port alone (the reference is Go and has no
 GPU path; it cannot be built on this image) and prints its own line.
@@ -194,6 +196,8 @@ def main():
     ap.add_argument("--impl", default="futon_b200", choices=["futon_b200", "reference"])
     ap.add_argument("--nseq", type=int, default=None, help="override sequences per rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nomic-nseq", type=int, default=1024,
+                    help="sequences per rank of the nomic-shaped throughput run (0 = skip)")
     args = ap.parse_args()
     route_stdout_to_stderr()
 
@@ -359,6 +363,55 @@ def main():
               "frac_of_bf16_peak_sustained": round(tf128 / peak_tf, 4)}
     del d_ids128, d_out128
 
+    # ---- nomic-bert-shaped encoder: c2 lengths (U[64, 512]), mean pooling ----
+    # Every rank takes the same collective steps whatever happens here: the
+    # timing is local, its max over ranks follows outside the try.
+    nomic_ms, nomic_info = float("nan"), None
+    if args.nomic_nseq > 0:
+        try:
+            ncfg = synth.arch("nomic")
+            nmodel = Model(ncfg, synth.make_weights(ncfg), devices=[local], q8=False)
+            nids, ncu = synth.make_inputs("c2", seed=21 + rank, nseq=args.nomic_nseq)
+            nflops = synth.total_flops(ncfg, ncu)
+            d_nids = torch.from_numpy(nids).cuda()
+            d_nout = torch.empty((len(ncu) - 1, ncfg.hidden_size), dtype=torch.float32,
+                                 device="cuda")
+            for _ in range(args.warmup):
+                nmodel.encode_device(d_nids.data_ptr(), ncu, 0, d_nout.data_ptr(), stream=sh)
+            nmodel.sync(stream=sh)
+            n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n0.record(stream)
+            for _ in range(args.steps):
+                nmodel.encode_device(d_nids.data_ptr(), ncu, 0, d_nout.data_ptr(), stream=sh)
+            n1.record(stream)
+            n1.synchronize()
+            nmodel.sync(stream=sh)
+            nomic_ms = n0.elapsed_time(n1) / args.steps
+            nn = torch.linalg.vector_norm(d_nout, dim=1)
+            if float((nn - 1).abs().max()) >= 1e-4:
+                raise RuntimeError("nomic outputs are not unit-norm")
+            nomic_info = {"seqs": len(ncu) - 1, "tokens": int(ncu[-1]), "flops": nflops}
+            del d_nids, d_nout
+            nmodel.close()
+        except Exception as e:  # noqa: BLE001 - reported in the JSON line
+            nomic_ms, nomic_info = float("nan"), {"error": repr(e)[:300]}
+    barrier()
+    nomic_ms = max_over_ranks(nomic_ms)
+    nomic = None
+    if nomic_info is not None and "error" not in nomic_info and nomic_ms == nomic_ms:
+        ntf = nomic_info["flops"] / (nomic_ms / 1e3) / 1e12
+        nomic = {"model": "nomic-bert-shaped (12 layers, hidden 768, 12 heads, RoPE, SwiGLU 3072, "
+                          "mean pooling)",
+                 "workload": "c2 lengths U[64, 512], ids in HBM, CUDA events",
+                 "seqs_per_rank": nomic_info["seqs"], "tokens_per_rank": nomic_info["tokens"],
+                 "ms_per_step": round(nomic_ms, 3),
+                 "embeddings_per_sec": round(world * nomic_info["seqs"] / (nomic_ms / 1e3), 1),
+                 "tokens_per_sec": round(world * nomic_info["tokens"] / (nomic_ms / 1e3), 1),
+                 "tflops_per_gpu": round(ntf, 1),
+                 "frac_of_bf16_peak": round(ntf / peaks["bf16_tflops"], 4)}
+    elif nomic_info is not None:
+        nomic = nomic_info if "error" in nomic_info else {"error": "a rank failed"}
+
     # ---- p50 latency of one c0 batch through the host-buffer ABI ----
     ids0, cu0 = synth.make_inputs("c0", seed=1 + rank)
     for _ in range(5):
@@ -406,6 +459,7 @@ def main():
                          "profiled_ms_per_step": round(prof_ms, 3)},
             "stages": breakdown,
             "seq128": seq128,
+            "nomic": nomic,
             "p50_batch_latency": latency,
             "clocks": clk,
             "cpu_baseline": cb,
