@@ -25,7 +25,7 @@ EXPORTED = (
     "futon_cuda_sync", "futon_cuda_launch_count", "futon_cuda_matmul_t",
     "futon_cuda_matmul_t_q8", "futon_cuda_quantize_rows_q8", "futon_cuda_profile",
     "futon_cuda_profile_read", "futon_cuda_profile_stage_count", "futon_cuda_profile_stage_name",
-    "futon_cuda_matmul_t_q8_noalloc", "futon_cuda_selftest_wait_timeout",
+    "futon_cuda_matmul_t_q8_noalloc", "futon_cuda_selftest_wait_timeout", "futon_cuda_io_bytes",
 )
 
 
@@ -100,6 +100,9 @@ def lib() -> C.CDLL:
         L.futon_cuda_sync.argtypes = [vp, ip, vp, cp, sz]
         L.futon_cuda_launch_count.restype = C.c_longlong
         L.futon_cuda_launch_count.argtypes = [vp, ip]
+        L.futon_cuda_io_bytes.restype = ip
+        L.futon_cuda_io_bytes.argtypes = [vp, ip, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong),
+                                          cp, sz]
         L.futon_cuda_profile.restype = ip
         L.futon_cuda_profile.argtypes = [vp, ip, ip, cp, sz]
         L.futon_cuda_profile_read.restype = ip

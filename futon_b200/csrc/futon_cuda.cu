@@ -265,6 +265,9 @@ struct DevCtx {
   MapCache map_cache;  // activation tensor maps (guarded by mu)
   std::vector<cudaEvent_t> out_evts;  // host-buffer calls: one per micro-batch's D2H
   std::atomic<long long> launches{0};
+  // Bytes this device's calls copied host→device and device→host (ids,
+  // micro-batch metadata, vectors, the device error word).
+  std::atomic<long long> h2d_bytes{0}, d2h_bytes{0};
   // Optional per-stage profiler (CUDA events around each launch).
   bool prof_on = false;
   struct ProfRec { cudaEvent_t a, b; int stage; double flops, bytes; };
@@ -1218,6 +1221,7 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, bool exact_p,
     }
   }
   CU_TRY(cudaMemcpyAsync(d.d_meta, d.h_meta, meta * sizeof(int), cudaMemcpyHostToDevice, st));
+  d.h2d_bytes.fetch_add((long long)(meta * sizeof(int)), std::memory_order_relaxed);
   CU_TRY(cudaEventRecord(d.meta_evt, st));
   return FUTON_OK;
 }
@@ -1284,6 +1288,7 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
 int read_device_error(DevCtx& d, char* err, size_t errlen) {
   int code = 0;
   CU_TRY(cudaMemcpy(&code, d.err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  d.d2h_bytes.fetch_add((long long)sizeof(int), std::memory_order_relaxed);
   if (code != 0) {
     CU_TRY(cudaMemset(d.err_word, 0, sizeof(int)));
     return set_err(err, errlen, code == kDevBadInput ? FUTON_EINVAL : FUTON_EDEVICE,
@@ -1309,6 +1314,7 @@ int encode_host(futon_model* m, DevCtx& d, const int32_t* ids, const int32_t* cu
   if ((rc = ensure_dev(&d.d_out, &d.d_out_cap, (size_t)nseq * dim, err, errlen))) return rc;
   memcpy(d.h_ids, ids, T * sizeof(int));
   CU_TRY(cudaMemcpyAsync(d.d_ids, d.h_ids, T * sizeof(int), cudaMemcpyHostToDevice, d.stream));
+  d.h2d_bytes.fetch_add((long long)(T * sizeof(int)), std::memory_order_relaxed);
   // Each micro-batch's vectors go to pinned memory as soon as it is done
   // (event per micro-batch); this thread copies them out to `out` while the
   // GPU works on the next micro-batches.
@@ -1323,6 +1329,8 @@ int encode_host(futon_model* m, DevCtx& d, const int32_t* ids, const int32_t* cu
     CU_TRY(cudaMemcpyAsync(d.h_out + (size_t)s0 * dim, d.d_out + (size_t)s0 * dim,
                            (size_t)(s1 - s0) * dim * sizeof(float), cudaMemcpyDeviceToHost,
                            d.stream));
+    d.d2h_bytes.fetch_add((long long)((size_t)(s1 - s0) * dim * sizeof(float)),
+                          std::memory_order_relaxed);
     CU_TRY(cudaEventRecord(d.out_evts[i], d.stream));
     done.push_back(Done{s0, s1});
     return FUTON_OK;
@@ -1730,6 +1738,15 @@ int futon_cuda_sync(futon_model* model, int device, void* stream, char* err, siz
 long long futon_cuda_launch_count(futon_model* model, int device) {
   if (!model || device < 0 || device >= (int)model->devs.size()) return -1;
   return model->devs[device]->launches.load();
+}
+
+int futon_cuda_io_bytes(futon_model* model, int device, long long* h2d, long long* d2h, char* err,
+                        size_t errlen) {
+  if (!model || device < 0 || device >= (int)model->devs.size())
+    return set_err(err, errlen, FUTON_EINVAL, "native: bad model or device index");
+  if (h2d) *h2d = model->devs[device]->h2d_bytes.load();
+  if (d2h) *d2h = model->devs[device]->d2h_bytes.load();
+  return FUTON_OK;
 }
 
 int futon_cuda_profile(futon_model* model, int device, int enable, char* err, size_t errlen) {

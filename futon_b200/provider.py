@@ -234,6 +234,13 @@ class Model:
         with self._call() as h:
             _lib.call("futon_cuda_sync", h, device, C.c_void_p(stream) if stream else None)
 
+    def io_bytes(self, device: int = 0) -> tuple:
+        """(host→device, device→host) bytes the calls on `device` copied since create."""
+        h2d, d2h = C.c_longlong(), C.c_longlong()
+        with self._call() as h:
+            _lib.call("futon_cuda_io_bytes", h, device, C.byref(h2d), C.byref(d2h))
+        return int(h2d.value), int(d2h.value)
+
     def launch_count(self, device: int = 0) -> int:
         with self._call() as h:
             return int(_lib.lib().futon_cuda_launch_count(h, device))

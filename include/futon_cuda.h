@@ -135,6 +135,12 @@ int futon_cuda_sync(futon_model* model, int device, void* stream, char* err, siz
  * (counts every launch of this library's own kernels). */
 long long futon_cuda_launch_count(futon_model* model, int device);
 
+/* Bytes the model's calls on `device` copied host→device (*h2d: token ids,
+ * micro-batch metadata) and device→host (*d2h: vectors, the device error
+ * word) since create (no counterpart in the reference: measurement). */
+int futon_cuda_io_bytes(futon_model* model, int device, long long* h2d, long long* d2h, char* err,
+                        size_t errlen);
+
 /* ---- Per-stage profiler (no counterpart in the reference: measurement) ----
  * When enabled, every launch on `device` is bracketed by CUDA events and
  * attributed to a stage (embed_ln, gemm_qkv, attention, …) together with its

@@ -265,6 +265,18 @@ def test_encode_device_matches_host(gpu):
     assert m.launch_count() > 0
 
 
+def test_io_bytes_counts_the_copies(gpu):
+    """futon_cuda_io_bytes: a host-buffer call copies at least the ids in and
+    exactly the vectors plus the 4-byte device error word out."""
+    cfg, w, m = synth_model("bge")
+    ids, cu = synth.make_inputs("c0", seed=13)
+    h0, d0 = m.io_bytes()
+    m.encode_packed(ids, cu)
+    h1, d1 = m.io_bytes()
+    assert h1 - h0 >= ids.nbytes + cu.nbytes
+    assert d1 - d0 == (len(cu) - 1) * cfg.hidden_size * 4 + 4
+
+
 def test_encode_device_two_streams(gpu):
     """Back-to-back device-resident calls on two different caller streams,
     queued without waiting, share the device's workspace: the library orders
