@@ -46,6 +46,13 @@ FUTON_HD __forceinline__ float fsub(float a, float b) {
   return a - b;
 #endif
 }
+FUTON_HD __forceinline__ float fdiv(float a, float b) {
+#ifdef __CUDA_ARCH__
+  return __fdiv_rn(a, b);
+#else
+  return a / b;
+#endif
+}
 FUTON_HD __forceinline__ float f32_from_bits(int32_t b) {
 #ifdef __CUDA_ARCH__
   return __int_as_float(b);
@@ -79,8 +86,8 @@ FUTON_HD __forceinline__ float exp_f32(float x) {
   return fmul(p, f32_from_bits(e << 23));
 }
 
-__device__ __forceinline__ float erfc_pos_f32(float a) {
-  float t = __fdiv_rn(1.0f, fadd(1.0f, fmul(0.5f, a)));
+FUTON_HD __forceinline__ float erfc_pos_f32(float a) {
+  float t = fdiv(1.0f, fadd(1.0f, fmul(0.5f, a)));
   float p = 0.17087277f;
   p = fsub(fmul(p, t), 0.82215223f);
   p = fadd(fmul(p, t), 1.48851587f);
@@ -96,7 +103,7 @@ __device__ __forceinline__ float erfc_pos_f32(float a) {
   return fmul(t, exp_f32(e));
 }
 
-__device__ __forceinline__ float gelu_f32(float x) {
+FUTON_HD __forceinline__ float gelu_f32(float x) {
   float a = fmul(x, 0.7071067811865476f);
   if (a < 0) a = -a;
   float c = erfc_pos_f32(a);
@@ -104,11 +111,11 @@ __device__ __forceinline__ float gelu_f32(float x) {
   return fmul(fmul(0.5f, x), fsub(2.0f, c));
 }
 
-__device__ __forceinline__ float sigmoid_f32(float x) {
+FUTON_HD __forceinline__ float sigmoid_f32(float x) {
   float e = -x;
   if (e < kExpClampLo) e = kExpClampLo;
   if (e > kExpOverflowF32) return 0.0f;
-  return __fdiv_rn(1.0f, fadd(1.0f, exp_f32(e)));
+  return fdiv(1.0f, fadd(1.0f, exp_f32(e)));
 }
 
 // Fast variants for the bf16 path, whose outputs are rounded to bf16 (2^-9

@@ -1,8 +1,9 @@
-// Host build of the int8 path's exact-order attention arithmetic
-// (futon_b200/csrc/attn_exact.cuh), for CPU tests against the oracle. It
-// runs the same per-row and per-column routines as attn_exact_softmax_kernel
-// and attn_exact_pv_kernel, over the same 64-key tiles, in the same order.
-// Built by tests/test_attn_exact_host.py with nvcc (host code,
+// Host build of the int8 path's exact-order arithmetic, for CPU tests
+// against the oracle: the attention (futon_b200/csrc/attn_exact.cuh: the
+// same per-row and per-column routines as attn_exact_softmax_kernel and
+// attn_exact_pv_kernel, over the same 64-key tiles, in the same order) and
+// the activations of futon_b200/csrc/mathf32.cuh.
+// Built by tests/test_exact_host.py with nvcc (host code,
 // -ffp-contract=off); test infrastructure only.
 #include <cmath>
 #include <vector>
@@ -67,3 +68,8 @@ extern "C" int fx_attend_head(const float* qkv, int seq, int rows, int h, int hd
 
 // exp_f32 on the host (the device restatement of the reference's expF32).
 extern "C" float fx_exp_f32(float x) { return exp_f32(x); }
+
+// The int8 path's activations on the host (the device restatements of the
+// reference's geluF32 and sigmoidF32, mathf32.go:40-120).
+extern "C" float fx_gelu_f32(float x) { return gelu_f32(x); }
+extern "C" float fx_sigmoid_f32(float x) { return sigmoid_f32(x); }

@@ -1,8 +1,10 @@
-"""CPU check of the int8 path's exact-order attention arithmetic
-(futon_b200/csrc/attn_exact.cuh) against the oracle's attendHead
-(native/model.go:646-739) in the avx2Kernel summation order, bit for bit.
+"""CPU check of the int8 path's exact-order arithmetic against the oracle,
+bit for bit: the attention (futon_b200/csrc/attn_exact.cuh) against the
+oracle's attendHead (native/model.go:646-739) in the avx2Kernel summation
+order, and the activations (futon_b200/csrc/mathf32.cuh: expF32, geluF32,
+sigmoidF32, native/mathf32.go:40-120).
 
-tests/host/attn_exact_host.cu runs the routines the device kernels call,
+tests/host/exact_host.cu runs the routines the device kernels call,
 over the same 64-key tiles in the same order, as host code built with nvcc
 (-ffp-contract=off). The device kernels add only the staging of those tiles.
 """
@@ -29,15 +31,16 @@ def fx(tmp_path_factory):
     out = tmp_path_factory.mktemp("fx") / "libfx.so"
     cmd = [nvcc, "-O2", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-shared",
            "-Xcompiler", "-fPIC,-ffp-contract=off", "-I", str(ROOT / "futon_b200" / "csrc"),
-           "-I", str(ROOT / "include"), "-o", str(out), str(ROOT / "tests" / "host" / "attn_exact_host.cu")]
+           "-I", str(ROOT / "include"), "-o", str(out), str(ROOT / "tests" / "host" / "exact_host.cu")]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     lib = C.CDLL(str(out))
     lib.fx_attend_head.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                    C.c_void_p]
     lib.fx_attend_head.restype = C.c_int
-    lib.fx_exp_f32.argtypes = [C.c_float]
-    lib.fx_exp_f32.restype = C.c_float
+    for name in ("fx_exp_f32", "fx_gelu_f32", "fx_sigmoid_f32"):
+        getattr(lib, name).argtypes = [C.c_float]
+        getattr(lib, name).restype = C.c_float
     return lib
 
 
@@ -79,3 +82,20 @@ def test_exp_f32_host_matches_oracle(fx):
     got = np.array([fx.fx_exp_f32(float(x)) for x in xs], np.float32)
     want = np.array([O.exp_f32(float(x)) for x in xs], np.float32)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def _sweep():
+    rng = np.random.default_rng(7)
+    return np.concatenate([np.linspace(-12, 12, 60001, dtype=np.float32),
+                           rng.standard_normal(60000).astype(np.float32) * 3,
+                           np.float32([0.0, -0.0, 1e-30, -1e-30, 87.0, -87.0, 110.0, -110.0])])
+
+
+@pytest.mark.parametrize("name,ref", [("fx_gelu_f32", "gelu_f32"), ("fx_sigmoid_f32", "sigmoid_f32")])
+def test_activation_host_matches_oracle(fx, name, ref):
+    xs = _sweep()
+    f, r = getattr(fx, name), getattr(O, ref)
+    got = np.array([f(float(x)) for x in xs], np.float32)
+    want = np.array([r(float(x)) for x in xs], np.float32)
+    bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
+    assert bad.size == 0, f"{name}: {bad.size} mismatches, first at x={xs[bad[0]]!r}"

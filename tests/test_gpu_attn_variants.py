@@ -13,7 +13,7 @@ default `-m gpu` suite does not select them.
   packed with).
 - FUTON_CUDA_Q8_ATTN=exact: the int8 path's attention in the reference's
   exact float32 operation order (avx2Kernel MatMulT, softmaxScaled); its
-  arithmetic is checked bit for bit on the CPU by test_attn_exact_host.py.
+  arithmetic is checked bit for bit on the CPU by test_exact_host.py.
   On the GPU the int8 forward must then sit within float32 noise of the
   oracle's int8 forward (avx2Kernel order), far inside the 0.9999 gate.
 """
