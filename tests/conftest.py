@@ -28,6 +28,11 @@ GPU_COSINE_MIN = 0.9999
 
 
 def pytest_configure(config):
+    # A checkout without the built library (it is not committed) builds it
+    # once here; nvcc cross-compiles sm_100a without a GPU.
+    from futon_b200 import build as fb_build
+    if not fb_build.LIB.exists():
+        fb_build.build()
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and libfuton_cuda")
     config.addinivalue_line(
         "markers", "gpu_variant: GPU checks of opt-in kernel variants (FUTON_TEST_ATTN_VARIANTS=1)")
