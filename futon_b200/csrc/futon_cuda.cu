@@ -418,6 +418,41 @@ float f16_to_f32(uint16_t h) {
   return f;
 }
 
+// Expands n binary16 values to binary32 (exact): through a 65,536-entry
+// table of f16_to_f32, on up to 16 host threads for large tensors (a real
+// pack's weights are F16, so this is most of a cold start's host work).
+void f16_expand(const uint16_t* src, size_t n, float* dst) {
+  static std::vector<float> table;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    table.resize(65536);
+    for (uint32_t h = 0; h < 65536; ++h) table[h] = f16_to_f32((uint16_t)h);
+  });
+  const float* tb = table.data();
+  auto run = [&](size_t lo, size_t hi) {
+    for (size_t k = lo; k < hi; ++k) dst[k] = tb[src[k]];
+  };
+  constexpr size_t kPerThread = size_t(1) << 22;
+  const size_t hw = std::max<size_t>(1, std::thread::hardware_concurrency());
+  const size_t nt = std::min<size_t>({hw, size_t(16), (n + kPerThread - 1) / kPerThread});
+  if (nt <= 1) {
+    run(0, n);
+    return;
+  }
+  std::vector<std::thread> th;
+  const size_t per = (n + nt - 1) / nt;
+  size_t launched = 0;  // chunks [0, launched) run on threads, the rest here
+  try {
+    for (; launched < nt; ++launched) {
+      const size_t lo = launched * per, hi = std::min(n, lo + per);
+      if (lo < hi) th.emplace_back(run, lo, hi);
+    }
+  } catch (...) {  // no thread available: finish on this one
+  }
+  for (size_t i = launched; i < nt; ++i) run(std::min(n, i * per), std::min(n, i * per + per));
+  for (auto& x : th) x.join();
+}
+
 struct TensorSet {
   std::map<std::string, HostTensor> byname;
   std::map<std::string, bool> used;
@@ -1515,8 +1550,7 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
       size_t n = 1;
       for (int k = 0; k < t.ndim; ++k) n *= (size_t)t.shape[k];
       ht.f32.resize(n);
-      const uint16_t* src = (const uint16_t*)t.data;
-      for (size_t k = 0; k < n; ++k) ht.f32[k] = f16_to_f32(src[k]);
+      f16_expand((const uint16_t*)t.data, n, ht.f32.data());
     }
     if (ts.byname.count(t.name))
       return set_err(err, errlen, FUTON_EINVAL, "native: duplicate tensor %s", t.name);
