@@ -70,6 +70,14 @@ def test_null_model_calls_return_errors():
     with pytest.raises(FutonError, match="null model"):
         _lib.call("futon_cuda_sync", None, 0, None)
     assert _lib.lib().futon_cuda_launch_count(None, 0) == -1
+    h2d, d2h = C.c_longlong(), C.c_longlong()
+    with pytest.raises(FutonError, match="bad model"):
+        _lib.call("futon_cuda_io_bytes", None, 0, C.byref(h2d), C.byref(d2h))
+    with pytest.raises(FutonError, match="null model"):
+        _lib.call("futon_cuda_encode_device", None, 0, None, cu.ctypes.data, 1, 0, None, None)
+    with pytest.raises(FutonError, match="null model"):
+        _lib.call("futon_cuda_encode_batch", None, ids.ctypes.data, cu.ctypes.data, 1, 0,
+                  out.ctypes.data, None)
 
 
 @pytest.mark.parametrize("call", [
