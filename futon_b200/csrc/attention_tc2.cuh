@@ -1,0 +1,410 @@
+// attention_tc2.cuh — tcgen05 attention for head_dim 32 with head-pair
+// stages and two softmax warpgroups (opt-in, FUTON_CUDA_ATTN=tc2), restating
+// native/model.go:646-739 (attendHead, softmaxScaled) for every head and
+// sequence of a micro-batch.
+//
+// Same work decomposition and numerics as attn_tc_kernel (attention_tc.cuh):
+// a CTA takes one window of ≤ 128 query rows (sequences of ≤ 128 tokens
+// packed at 16-row-aligned offsets with the sequence mask folded into S as
+// one more K = 16 MMA step, or 128 queries of a longer sequence with its
+// keys in 128-key blocks); exponents rounded to f16 before ex2.approx.f16x2,
+// P and V in f16, f32 accumulation in TMEM. What changes is the pipeline:
+//
+//   stage u       q, k and v of one head PAIR (adjacent qkv columns: one
+//                 64-column box, 128-byte rows, 128-byte swizzle) and one
+//                 key block; a two-stage ring, so a pair's loads are in
+//                 flight while the previous pair is computed;
+//   warps 0-3     softmax warpgroup 0: the pair's first head
+//   warps 4-7     softmax warpgroup 1: the pair's second head. Each group
+//                 owns its S (128 TMEM columns), O (64: P·V runs over both
+//                 heads' 64 value columns, the group reads its own 32), row
+//                 sums (16) and P tile (32 KB), so the two heads of a stage
+//                 proceed side by side and neither waits on the other's P·V;
+//   warp 8        TMA producer (one thread);
+//   warp 9        MMA issuer (one thread) and TMEM owner (512 columns).
+//
+// q·kᵀ of head e reads its 32 columns at byte 64·e of each 128-byte row (the
+// start-address advance inside a swizzle atom that the GEMM's K steps use).
+// Unit u of warpgroup e: the MMA thread issues S(u, e) once the stage has
+// landed and the group has handed in P(u − 1, e) (so S_e has been read), and
+// P·V(u, e) once P(u, e) is written; the stage is released after both P·Vs.
+// Every wait is bounded (kDevTimeoutAttn).
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "attention_tc.cuh"
+#include "common.cuh"
+#include "gemm_tc.cuh"
+
+namespace futon {
+
+struct AttnTc2Cfg {
+  static constexpr int kRowBytes = 128;                    // two heads × 32 × 2 B
+  static constexpr int kTileBytes = 128 * kRowBytes;       // one q, k or v tile
+  static constexpr int kStageBytes = 3 * kTileBytes;       // 48 KB
+  static constexpr int kStages = 2;
+  static constexpr int kPOffset = kStages * kStageBytes;   // 1024-aligned
+  static constexpr int kPBytes = 2 * 128 * 128;            // per group: two 64-key regions
+  static constexpr int kOnesOffset = kPOffset + 2 * kPBytes;
+  static constexpr int kOnesBytes = 16 * 128;
+  static constexpr int kAugOffset = kOnesOffset + 2048;    // 1024-aligned
+  static constexpr int kAugBytes = 2 * 128 * 64;
+  static constexpr int kBarOffset = kAugOffset + kAugBytes;
+  static constexpr int kBytes = kBarOffset + 128 + 1024;   // + barriers + alignment slack
+  static constexpr uint32_t kTmemCols = 512;
+  // TMEM columns of group e: S at 128·e, O at 256 + 64·e, row sums at 384 + 32·e.
+  static constexpr uint32_t kColS = 0, kColO = 256, kColL = 384;
+  static constexpr int kThreads = 320;
+};
+
+constexpr int attn_tc2_smem_bytes() { return AttnTc2Cfg::kBytes; }
+
+// grid = number of windows, block = 320; num_heads even; qkv [T, 3h] (bf16
+// q, k; f16 v) through maps.m[n] (boxes of 16·n rows × 64 columns).
+template <typename OutT>
+__global__ void __launch_bounds__(320, 1)
+    attn_tc2_kernel(const __grid_constant__ AttnMaps maps, int hidden, int num_heads,
+                    const AttnWindow* __restrict__ windows, const AttnSeg* __restrict__ segs,
+                    float scale_log2, OutT* __restrict__ out, int ldo, int* __restrict__ err) {
+  using C = AttnTc2Cfg;
+  constexpr int HD = 32;
+  extern __shared__ uint8_t sm_raw[];
+  const uint32_t sbase = (smem_u32(sm_raw) + 1023u) & ~1023u;
+  const uint32_t sOnes = sbase + C::kOnesOffset;
+  const uint32_t sQa = sbase + C::kAugOffset, sKa = sQa + 128 * 64;
+  const uint32_t bars = sbase + C::kBarOffset;
+  const uint32_t full_b = bars;            // [2] TMA → MMA
+  const uint32_t empty_b = bars + 16;      // [2] MMA → TMA (both heads' P·V done)
+  const uint32_t sfull_b = bars + 32;      // [2] S(u, e) ready (MMA → group e)
+  const uint32_t pfull_b = bars + 48;      // [2] P(u, e) written, O corrected (group e → MMA)
+  const uint32_t ofull_b = bars + 64;      // [2] P·V(u, e) done (MMA → group e)
+  const uint32_t drain_b = bars + 80;      // the MMA thread's last MMAs are done
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const AttnWindow win = windows[blockIdx.x];
+  const bool packed = win.nseg > 0;
+  const int nkb = (win.nk + 127) / 128;     // key blocks per head pair
+  const int units = (num_heads / 2) * nkb;  // stages; each serves both groups
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(full_b + 8 * i, 1);
+      mbar_init(empty_b + 8 * i, 1);
+      mbar_init(sfull_b + 8 * i, 1);
+      mbar_init(pfull_b + 8 * i, 4);
+      mbar_init(ofull_b + 8 * i, 1);
+    }
+    mbar_init(drain_b, 1);
+    fence_barrier_init();
+    for (int n = 1; n <= 8; ++n) tma_prefetch_desc(&maps.m[n]);
+  }
+  for (int i = threadIdx.x; i < C::kOnesBytes / 16; i += blockDim.x)
+    st_shared_v4(sOnes + 16 * i, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
+
+  // Softmax thread: query row r of the window (both groups cover rows
+  // 0-127); its token (−1: padding row) and its keys [klo, khi).
+  const int grp = warp >> 2;               // 0, 1 for warps 0-7
+  const int r = (warp & 3) * 32 + lane;
+  int tok = -1, klo = 0, khi = 0;
+  if (warp < 8) {
+    int sidx = -1;
+    if (!packed) {
+      if (r < win.nq) {
+        tok = win.q0 + r;
+        khi = win.nk;
+      }
+    } else {
+      for (int sg = 0; sg < win.nseg; ++sg) {
+        const AttnSeg sq = segs[win.seg0 + sg];
+        if (r >= sq.row && r < sq.row + sq.len) {
+          tok = sq.t0 + (r - sq.row);
+          klo = sq.row;
+          khi = sq.row + sq.len;
+          sidx = sg;
+        }
+      }
+      if (grp == 0) {
+        // Mask rows (as in attn_tc_kernel): q side onehot(segment), k side
+        // −29952 (bf16 0xC6EA) off the own segment.
+        uint32_t qa[8], ka[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t lo = (2 * i == sidx) ? 0x3F80u : 0u, hi = (2 * i + 1 == sidx) ? 0x3F80u : 0u;
+          qa[i] = lo | (hi << 16);
+          const uint32_t klo16 = (2 * i == sidx) ? 0u : 0xC6EAu;
+          const uint32_t khi16 = (2 * i + 1 == sidx) ? 0u : 0xC6EAu;
+          ka[i] = klo16 | (khi16 << 16);
+        }
+        const int sw = (r >> 1) & 3;
+        st_shared_v4(sQa + r * 64 + ((0 ^ sw) << 4), qa[0], qa[1], qa[2], qa[3]);
+        st_shared_v4(sQa + r * 64 + ((1 ^ sw) << 4), qa[4], qa[5], qa[6], qa[7]);
+        st_shared_v4(sKa + r * 64 + ((0 ^ sw) << 4), ka[0], ka[1], ka[2], ka[3]);
+        st_shared_v4(sKa + r * 64 + ((1 ^ sw) << 4), ka[4], ka[5], ka[6], ka[7]);
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  if (warp == 9) {
+    tmem_alloc(smem_u32(&tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      // ---------------- TMA producer: one stage per (head pair, key block) ----------------
+      int issued = 0;
+      for (int u = 0; u < units; ++u, ++issued) {
+        const int pair = u / nkb, j = u % nkb, slot = u & 1;
+        if (u >= 2 && !mbar_wait_bounded(empty_b + 8 * slot, ((u >> 1) - 1) & 1, err,
+                                         kDevTimeoutAttn, &abort_flag))
+          break;
+        const uint32_t fb = full_b + 8 * slot;
+        const uint32_t dst = sbase + slot * C::kStageBytes;
+        const int xq = pair * 2 * HD, xk = hidden + pair * 2 * HD, xv = 2 * hidden + pair * 2 * HD;
+        if (!packed) {
+          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          tma_load_2d(dst, &maps.m[8], fb, xq, win.q0);
+          tma_load_2d(dst + C::kTileBytes, &maps.m[8], fb, xk, win.k0 + 128 * j);
+          tma_load_2d(dst + 2 * C::kTileBytes, &maps.m[8], fb, xv, win.k0 + 128 * j);
+        } else {
+          // Rows [0, nq) in 16-row boxes, each segment from its own tokens.
+          mbar_arrive_expect_tx(fb, 3 * win.nq * C::kRowBytes);
+          for (int sg = 0; sg < win.nseg; ++sg) {
+            const AttnSeg sq = segs[win.seg0 + sg];
+            const CUtensorMap* mp = &maps.m[(sq.len + 15) >> 4];
+            const uint32_t o = (uint32_t)sq.row * C::kRowBytes;
+            tma_load_2d(dst + o, mp, fb, xq, sq.t0);
+            tma_load_2d(dst + C::kTileBytes + o, mp, fb, xk, sq.t0);
+            tma_load_2d(dst + 2 * C::kTileBytes + o, mp, fb, xv, sq.t0);
+          }
+        }
+      }
+      // Drain (time-bounded, also after an abort): this thread's last copies
+      // land before the CTA can exit.
+      for (int u = issued - 1; u >= 0 && u >= issued - 2; --u) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(full_b + 8 * (u & 1), (uint32_t)(u >> 1) & 1u))
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      auto keys16 = [&](int j) { return (min(128, win.nk - 128 * j) + 15) & ~15; };
+      // S(u, e) = q_e · k_eᵀ (+ the mask step) into group e's S columns.
+      auto issue_s = [&](int u, int e) {
+        const int slot = u & 1;
+        const uint32_t q = sbase + slot * C::kStageBytes, k = q + C::kTileBytes;
+        const uint32_t n = (uint32_t)keys16(u % nkb);
+        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (8u << 24);
+        const uint32_t d = tmem + C::kColS + 128u * (uint32_t)e;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks)
+          mma_bf16(d, smem_desc_k_sw128(q) + 4 * e + 2 * ks, smem_desc_k_sw128(k) + 4 * e + 2 * ks,
+                   idesc, ks ? 1u : 0u);
+        if (packed) mma_bf16(d, desc_rows<32>(sQa), desc_rows<32>(sKa), idesc, 1u);
+        mma_commit(sfull_b + 8 * e);
+      };
+      constexpr uint32_t idesc_pv = (1u << 4) | (1u << 16) | ((uint32_t)(64 >> 3) << 17) | (8u << 24);
+      constexpr uint32_t idesc_l = (1u << 4) | (2u << 17) | (8u << 24);
+      bool ok = units > 0 &&
+                mbar_wait_bounded(full_b, 0, err, kDevTimeoutAttn, &abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(0, 1);
+      }
+      for (int u = 0; ok && u < units; ++u) {
+        const int j = u % nkb, slot = u & 1;
+        const uint32_t v = sbase + slot * C::kStageBytes + 2 * C::kTileBytes;
+        const int nks = keys16(j) / 16;
+        for (int e = 0; e < 2 && ok; ++e) {
+          if (!mbar_wait_bounded(pfull_b + 8 * e, u & 1, err, kDevTimeoutAttn, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sp = sbase + C::kPOffset + (uint32_t)e * C::kPBytes;
+          for (int ks = 0; ks < nks; ++ks) {
+            const uint64_t pd = smem_desc_k_sw128(sp + (ks >> 2) * 16384) + 2 * (ks & 3);
+            const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+            mma_bf16(tmem + C::kColO + 64u * (uint32_t)e, pd,
+                     desc_rows<64>(v + ks * 16 * C::kRowBytes), idesc_pv, acc);
+            mma_bf16(tmem + C::kColL + 32u * (uint32_t)e, pd,
+                     smem_desc_k_sw128(sOnes) + 2 * (ks & 3), idesc_l, acc);
+          }
+          mma_commit(ofull_b + 8 * e);
+          if (u + 1 < units) {
+            // Group e has handed in P(u, e), so it has read S(u, e).
+            if (e == 0 && !mbar_wait_bounded(full_b + 8 * ((u + 1) & 1), ((u + 1) >> 1) & 1, err,
+                                              kDevTimeoutAttn, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(u + 1, e);
+          }
+        }
+        if (ok) mma_commit(empty_b + 8 * slot);
+      }
+      // Drain (time-bounded): every MMA issued above completes before TMEM
+      // is freed.
+      mma_commit(drain_b);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain_b, 0u))
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+  } else {
+    // ---------------- softmax groups: warps 0-3 (e = 0), 4-7 (e = 1) ----------------
+    const int e = grp;
+    const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t srow = tmem + lanes + C::kColS + 128u * (uint32_t)e;
+    const uint32_t orow = tmem + lanes + C::kColO + 64u * (uint32_t)e + 32u * (uint32_t)e;
+    const uint32_t lrow = tmem + lanes + C::kColL + 32u * (uint32_t)e;
+    const uint32_t prow = sbase + C::kPOffset + (uint32_t)e * C::kPBytes + (uint32_t)r * 128u;
+    const int swz = r & 7;
+    int clo = tok >= 0 ? klo >> 5 : 4, chi = tok >= 0 ? (khi + 31) >> 5 : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      clo = min(clo, __shfl_xor_sync(0xffffffffu, clo, o));
+      chi = max(chi, __shfl_xor_sync(0xffffffffu, chi, o));
+    }
+    float m_run = -INFINITY;
+    bool ok = true;
+
+    // Normalised O row of head `head` (this group's 32 columns) to global memory.
+    auto store_head = [&](int head) {
+      uint32_t t[32];
+      tmem_ld32(orow, t);
+      const float l = __uint_as_float(tmem_ld1(lrow));
+      tmem_ld_wait();
+      if (tok >= 0) {
+        const float inv = rcp_approx(l);  // l ≥ 1: the row maximum contributes 2^0
+        float y[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) y[i] = __uint_as_float(t[i]) * inv;
+        store32<OutT>(out + (size_t)tok * ldo + head * HD, y);
+      }
+    };
+
+    for (int u = 0; u < units && ok; ++u) {
+      const int j = u % nkb;
+      if (j == 0) m_run = -INFINITY;  // a new head
+      const int nkeys = min(128, win.nk - 128 * j);
+      const int nchunk = (((nkeys + 15) & ~15) + 31) / 32;  // chunks the P·V MMAs read
+      const int c0 = packed ? clo : 0;
+      const int c1 = packed ? chi : (nkeys + 31) >> 5;
+      if (!mbar_wait_bounded(sfull_b + 8 * e, u & 1, err, kDevTimeoutAttn, &abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c >= c0 && c < c1) tmem_ld32(srow + 32 * c, sv[c]);
+      tmem_ld_wait();
+      if (nkeys & 31) {
+        const int c = (nkeys - 1) >> 5;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+          if (cc == c) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * cc + i >= nkeys) sv[cc][i] = __float_as_uint(-INFINITY);
+          }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        if (c >= c0 && c < c1) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2)
+            mx = fmax3(mx, __uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1]));
+        }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;  // rows without keys: P = 0
+      const float alpha = ex2_approx(((m_run == -INFINITY ? m_use : m_run) - m_use) * scale_log2);
+      m_run = m_new;
+      const float ms = m_use * scale_log2;
+      const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nms2 = f2_pack(-ms, -ms);
+      if (u > 0) {
+        // P·V(u − 1, e) has finished: P_e may be overwritten, and O_e holds
+        // either a finished head (store it) or this head's running sum.
+        if (!mbar_wait_bounded(ofull_b + 8 * e, (u - 1) & 1, err, kDevTimeoutAttn, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (j == 0) {
+          store_head(2 * ((u - 1) / nkb) + e);
+        } else if (__any_sync(0xffffffffu, alpha != 1.f)) {
+          uint32_t t[32];
+          tmem_ld32(orow, t);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
+          tmem_st32(orow, t);
+          const float l = __uint_as_float(tmem_ld1(lrow));
+          tmem_ld_wait();
+          tmem_st1(lrow, __float_as_uint(l * alpha));
+          tmem_st_wait();
+        }
+      }
+      // P = 2^(s·c − m·c) in f16 → this group's 128-byte-swizzled K-major
+      // tile (keys 0-63 | 64-127); chunks no row of the warp needs are zero.
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c < nchunk) {
+          const uint32_t base = prow + (uint32_t)(c >> 1) * 16384u;
+          if (c >= c0 && c < c1) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t w[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int k = 8 * i + 2 * q;
+                float a, b;
+                f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[c][k]), __uint_as_float(sv[c][k + 1])),
+                                 sl2, nms2),
+                          a, b);
+                w[q] = ex2_h2(a, b);
+              }
+              st_shared_v4(base + (uint32_t)((((c & 1) * 4 + i) ^ swz) << 4), w[0], w[1], w[2], w[3]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              st_shared_v4(base + (uint32_t)((((c & 1) * 4 + i) ^ swz) << 4), 0u, 0u, 0u, 0u);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pfull_b + 8 * e);
+    }
+    if (ok && units > 0 &&
+        mbar_wait_bounded(ofull_b + 8 * e, (units - 1) & 1, err, kDevTimeoutAttn, &abort_flag)) {
+      tc_fence_after();
+      store_head(2 * ((units - 1) / nkb) + e);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+}  // namespace futon

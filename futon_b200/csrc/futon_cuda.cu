@@ -42,6 +42,7 @@
 
 #include "attention.cuh"
 #include "attention_tc.cuh"
+#include "attention_tc2.cuh"
 #include "attn_exact.cuh"
 #include "common.cuh"
 #include "gemm_launch.cuh"
@@ -310,7 +311,8 @@ struct futon_model {
   int eff_max = 0;
   int swiglu_half = 0;
   // Attention kernel of the float path (read from FUTON_CUDA_ATTN when the
-  // model is created): 0 = attn_heads_kernel, 1 = attn_tc_kernel.
+  // model is created): 0 = attn_heads_kernel, 1 = attn_tc_kernel,
+  // 2 = attn_tc2_kernel (head_dim 32, even head count; others keep 0).
   int attn_kind = 0;
   // FUTON_CUDA_ATTN_SPLIT=1: attn_heads_kernel launches with the head groups
   // shared among grid.y CTAs when the tiles alone would leave SMs idle.
@@ -735,13 +737,14 @@ inline int grid_rows(int rows, int per_block, int sms) {
 // attn_tc_kernel (tcgen05, packed 128-row windows) is parity-correct and
 // batch-invariant but, as measured on the c4 workload, 1.5× slower than
 // attn_heads_kernel; it runs only when FUTON_CUDA_ATTN=tc.
-enum AttnKind : int { kAttnHeads = 0, kAttnTc = 1 };
+enum AttnKind : int { kAttnHeads = 0, kAttnTc = 1, kAttnTc2 = 2 };
 
 // Model-creation-time attention options from the environment; unknown
 // values leave the defaults.
 void read_attn_env(futon_model& m) {
   if (const char* v = std::getenv("FUTON_CUDA_ATTN")) {
     if (!strcmp(v, "tc")) m.attn_kind = kAttnTc;
+    else if (!strcmp(v, "tc2")) m.attn_kind = kAttnTc2;
     else if (!strcmp(v, "heads")) m.attn_kind = kAttnHeads;
   }
   if (const char* v = std::getenv("FUTON_CUDA_ATTN_SPLIT")) m.attn_split = !strcmp(v, "1");
@@ -789,6 +792,26 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
   const AttnTile* tiles = plan.tiles;
   const int ntiles = plan.ntiles;
   if constexpr (!kSplit) {
+    if (m.attn_kind == kAttnTc2 && hd == 32 && H % 2 == 0 && !cls_only) {
+      if (plan.nwin == 0) return FUTON_OK;
+      // q, k, v tiles of one head pair: 16·n rows × 64 columns, 128-byte swizzle.
+      AttnMaps maps{};
+      for (int n = 1; n <= 8; ++n)
+        if (!d.map_cache.get(MapKey{kMapQkv, qkv, (uint64_t)T, (uint64_t)(3 * h), 64u, 16u * n},
+                             &maps.m[n], [&](CUtensorMap* mm) {
+                               return make_qkv_map(mm, qkv, (uint64_t)T, (uint64_t)(3 * h), 64,
+                                                   16u * n);
+                             }))
+          return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
+      const int smem = attn_tc2_smem_bytes();
+      CU_TRY(cudaFuncSetAttribute(attn_tc2_kernel<OutT>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attn_tc2_kernel<OutT><<<plan.nwin, AttnTc2Cfg::kThreads, smem, st>>>(
+          maps, h, H, plan.wins, plan.segs, scale_log2, out, h, d.err_word);
+      CU_TRY(cudaGetLastError());
+      d.launches.fetch_add(1, std::memory_order_relaxed);
+      return FUTON_OK;
+    }
     if (m.attn_kind == kAttnTc && tc_hd && !cls_only) {
       if (plan.nwin == 0) return FUTON_OK;
       // q, k, v tiles of one head: 128 rows × hd columns, swizzled over one row.

@@ -8,9 +8,10 @@ default `-m gpu` suite does not select them.
 - split: attn_heads_kernel with the head groups shared among grid.y CTAs.
   Every head is computed by the same code in the same order as without the
   split, so the vectors must be bitwise equal to the default kernel's.
-- tc: the tcgen05 attention kernel; parity with the oracle (cosine gate)
-  and batch invariance (a sequence's vector does not depend on what it is
-  packed with).
+- tc, tc2: the tcgen05 attention kernels (tc2: head-pair stages and two
+  softmax warpgroups, head_dim 32 only; other shapes keep the default);
+  parity with the oracle (cosine gate) and batch invariance (a sequence's
+  vector does not depend on what it is packed with).
 - FUTON_CUDA_Q8_ATTN=exact: the int8 path's attention in the reference's
   exact float32 operation order (avx2Kernel MatMulT, softmaxScaled); its
   arithmetic is checked bit for bit on the CPU by test_exact_host.py.
@@ -75,26 +76,28 @@ def test_split_bitwise_equals_default(gpu, monkeypatch, arch, inputs, nseq, laye
     assert np.array_equal(base, split), f"{arch}: split attention differs from the default"
 
 
+@pytest.mark.parametrize("kernel", ["tc", "tc2"])
 @pytest.mark.parametrize("arch,inputs,nseq,layers", CASES)
-def test_tc_vs_oracle(gpu, monkeypatch, arch, inputs, nseq, layers):
+def test_tc_vs_oracle(gpu, monkeypatch, kernel, arch, inputs, nseq, layers):
     cfg, w = weights(arch, layers)
     ids, cu = synth.make_inputs(inputs, nseq=nseq, vocab=cfg.vocab_size)
-    got = encode(monkeypatch, {"FUTON_CUDA_ATTN": "tc"}, cfg, w, ids, cu)
+    got = encode(monkeypatch, {"FUTON_CUDA_ATTN": kernel}, cfg, w, ids, cu)
     gemm = GEMM_AVX2 if has_avx2() else GEMM_GO
     want = OracleModel(cfg, w, gemm=gemm).encode_batch(ids, cu)
     cs = row_cosines(got, want)
-    assert cs.min() >= GPU_COSINE_MIN, f"{arch}: tc attention min cosine {cs.min():.7f}"
+    assert cs.min() >= GPU_COSINE_MIN, f"{arch}: {kernel} attention min cosine {cs.min():.7f}"
 
 
-def test_tc_batch_invariance(gpu, monkeypatch):
+@pytest.mark.parametrize("kernel", ["tc", "tc2"])
+def test_tc_batch_invariance(gpu, monkeypatch, kernel):
     cfg, w = weights("bge", 2)
     ids, cu = synth.make_inputs("c4", nseq=24, vocab=cfg.vocab_size)
     seqs = [ids[cu[i]:cu[i + 1]] for i in range(len(cu) - 1)]
-    env = {"FUTON_CUDA_ATTN": "tc"}
+    env = {"FUTON_CUDA_ATTN": kernel}
     packed = encode(monkeypatch, env, cfg, w, ids, cu)
     rev_ids, rev_cu = pack_ids(seqs[::-1])
     rev = encode(monkeypatch, env, cfg, w, rev_ids, rev_cu)[::-1]
-    assert np.array_equal(packed, rev), "tc attention: a vector depends on its batch neighbours"
+    assert np.array_equal(packed, rev), f"{kernel} attention: a vector depends on its batch neighbours"
 
 
 @pytest.mark.parametrize("arch,inputs,nseq,layers", [
