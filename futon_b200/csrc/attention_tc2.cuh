@@ -8,27 +8,31 @@
 // packed at 16-row-aligned offsets with the sequence mask folded into S as
 // one more K = 16 MMA step, or 128 queries of a longer sequence with its
 // keys in 128-key blocks); exponents rounded to f16 before ex2.approx.f16x2,
-// P and V in f16, f32 accumulation in TMEM. What changes is the pipeline:
+// P and V in f16, f32 accumulation in TMEM. What changes is the pipeline.
+// A unit u is one head PAIR (adjacent qkv columns: one 64-column box,
+// 128-byte rows, 128-byte swizzle) and one key block:
 //
-//   stage u       q, k and v of one head PAIR (adjacent qkv columns: one
-//                 64-column box, 128-byte rows, 128-byte swizzle) and one
-//                 key block; a two-stage ring, so a pair's loads are in
-//                 flight while the previous pair is computed;
-//   warps 0-3     softmax warpgroup 0: the pair's first head
-//   warps 4-7     softmax warpgroup 1: the pair's second head. Each group
-//                 owns its S (128 TMEM columns), O (64: P·V runs over both
-//                 heads' 64 value columns, the group reads its own 32), row
-//                 sums (16) and P tile (32 KB), so the two heads of a stage
-//                 proceed side by side and neither waits on the other's P·V;
-//   warp 8        TMA producer (one thread);
-//   warp 9        MMA issuer (one thread) and TMEM owner (512 columns).
+//   warp 8 (one thread)  TMA: q and k of unit u into a three-stage ring,
+//                        v into a separate two-stage ring, so the next
+//                        units' q·k tiles are in flight two units ahead and
+//                        a v tile is released as soon as its P·V is done;
+//   warp 9 (one thread)  MMA, TMEM owner (512 columns): S(u + 1, e) as soon
+//                        as group e has read S(u, e); P·V(u, e) once P(u, e)
+//                        is written;
+//   warps 0-3, 4-7       softmax groups e = 0, 1, one per head of the pair,
+//                        thread = query row. Each group owns its S (128 TMEM
+//                        columns), O (64: P·V runs over both heads' value
+//                        columns, the group reads its own 32), row sums (16)
+//                        and P tile (32 KB). A group reads S(u) and frees it
+//                        at once, so S(u + 1) is computed while the group
+//                        waits for P·V(u − 1) (which frees its P tile and
+//                        settles O) and writes P(u); the other group's work
+//                        fills this group's waits.
 //
 // q·kᵀ of head e reads its 32 columns at byte 64·e of each 128-byte row (the
 // start-address advance inside a swizzle atom that the GEMM's K steps use).
-// Unit u of warpgroup e: the MMA thread issues S(u, e) once the stage has
-// landed and the group has handed in P(u − 1, e) (so S_e has been read), and
-// P·V(u, e) once P(u, e) is written; the stage is released after both P·Vs.
-// Every wait is bounded (kDevTimeoutAttn).
+// Every wait is bounded (kDevTimeoutAttn); before exit the producer waits
+// (time-bounded) for its last copies and the MMA thread for its last MMAs.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -41,17 +45,19 @@ namespace futon {
 
 struct AttnTc2Cfg {
   static constexpr int kRowBytes = 128;                    // two heads × 32 × 2 B
-  static constexpr int kTileBytes = 128 * kRowBytes;       // one q, k or v tile
-  static constexpr int kStageBytes = 3 * kTileBytes;       // 48 KB
-  static constexpr int kStages = 2;
-  static constexpr int kPOffset = kStages * kStageBytes;   // 1024-aligned
+  static constexpr int kTileBytes = 128 * kRowBytes;       // one q, k or v tile (16 KB)
+  static constexpr int kQkStages = 3, kVStages = 2;
+  static constexpr int kQkOffset = 0;                      // [3] q tile, k tile
+  static constexpr int kVOffset = kQkStages * 2 * kTileBytes;
+  static constexpr int kPOffset = kVOffset + kVStages * kTileBytes;
   static constexpr int kPBytes = 2 * 128 * 128;            // per group: two 64-key regions
   static constexpr int kOnesOffset = kPOffset + 2 * kPBytes;
   static constexpr int kOnesBytes = 16 * 128;
   static constexpr int kAugOffset = kOnesOffset + 2048;    // 1024-aligned
   static constexpr int kAugBytes = 2 * 128 * 64;
   static constexpr int kBarOffset = kAugOffset + kAugBytes;
-  static constexpr int kBytes = kBarOffset + 128 + 1024;   // + barriers + alignment slack
+  static constexpr int kBarBytes = 256;
+  static constexpr int kBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
   static constexpr uint32_t kTmemCols = 512;
   // TMEM columns of group e: S at 128·e, O at 256 + 64·e, row sums at 384 + 32·e.
   static constexpr uint32_t kColS = 0, kColO = 256, kColL = 384;
@@ -74,27 +80,35 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t sOnes = sbase + C::kOnesOffset;
   const uint32_t sQa = sbase + C::kAugOffset, sKa = sQa + 128 * 64;
   const uint32_t bars = sbase + C::kBarOffset;
-  const uint32_t full_b = bars;            // [2] TMA → MMA
-  const uint32_t empty_b = bars + 16;      // [2] MMA → TMA (both heads' P·V done)
-  const uint32_t sfull_b = bars + 32;      // [2] S(u, e) ready (MMA → group e)
-  const uint32_t pfull_b = bars + 48;      // [2] P(u, e) written, O corrected (group e → MMA)
-  const uint32_t ofull_b = bars + 64;      // [2] P·V(u, e) done (MMA → group e)
-  const uint32_t drain_b = bars + 80;      // the MMA thread's last MMAs are done
+  const uint32_t qkfull_b = bars;          // [3] q, k landed (TMA → MMA)
+  const uint32_t qkempty_b = bars + 24;    // [3] both S of the unit done (MMA → TMA)
+  const uint32_t vfull_b = bars + 48;      // [2] v landed
+  const uint32_t vempty_b = bars + 64;     // [2] both P·V of the unit done
+  const uint32_t sfull_b = bars + 80;      // [2] S(u, e) ready (MMA → group e)
+  const uint32_t sfree_b = bars + 96;      // [2] group e has read S(u, e) (4 warps)
+  const uint32_t pfull_b = bars + 112;     // [2] P(u, e) written, O settled (4 warps)
+  const uint32_t ofull_b = bars + 128;     // [2] P·V(u, e) done (MMA → group e)
+  const uint32_t drain_b = bars + 144;     // the MMA thread's last MMAs are done
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
   const AttnWindow win = windows[blockIdx.x];
   const bool packed = win.nseg > 0;
   const int nkb = (win.nk + 127) / 128;     // key blocks per head pair
-  const int units = (num_heads / 2) * nkb;  // stages; each serves both groups
+  const int units = (num_heads / 2) * nkb;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
+    for (int i = 0; i < C::kQkStages; ++i) {
+      mbar_init(qkfull_b + 8 * i, 1);
+      mbar_init(qkempty_b + 8 * i, 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(full_b + 8 * i, 1);
-      mbar_init(empty_b + 8 * i, 1);
+      mbar_init(vfull_b + 8 * i, 1);
+      mbar_init(vempty_b + 8 * i, 1);
       mbar_init(sfull_b + 8 * i, 1);
+      mbar_init(sfree_b + 8 * i, 4);
       mbar_init(pfull_b + 8 * i, 4);
       mbar_init(ofull_b + 8 * i, 1);
     }
@@ -159,39 +173,67 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 8) {
     if (lane == 0) {
-      // ---------------- TMA producer: one stage per (head pair, key block) ----------------
-      int issued = 0;
-      for (int u = 0; u < units; ++u, ++issued) {
-        const int pair = u / nkb, j = u % nkb, slot = u & 1;
-        if (u >= 2 && !mbar_wait_bounded(empty_b + 8 * slot, ((u >> 1) - 1) & 1, err,
-                                         kDevTimeoutAttn, &abort_flag))
-          break;
-        const uint32_t fb = full_b + 8 * slot;
-        const uint32_t dst = sbase + slot * C::kStageBytes;
-        const int xq = pair * 2 * HD, xk = hidden + pair * 2 * HD, xv = 2 * hidden + pair * 2 * HD;
+      // ---------------- TMA producer ----------------
+      // Loads rows [0, nq) of column block x into dst: one 128-row box for
+      // a long window (rows from `row0`), one 16·n-row box per packed segment.
+      auto load_rows = [&](uint32_t dst, uint32_t bar, int x, int row0) {
         if (!packed) {
-          mbar_arrive_expect_tx(fb, C::kStageBytes);
-          tma_load_2d(dst, &maps.m[8], fb, xq, win.q0);
-          tma_load_2d(dst + C::kTileBytes, &maps.m[8], fb, xk, win.k0 + 128 * j);
-          tma_load_2d(dst + 2 * C::kTileBytes, &maps.m[8], fb, xv, win.k0 + 128 * j);
+          tma_load_2d(dst, &maps.m[8], bar, x, row0);
         } else {
-          // Rows [0, nq) in 16-row boxes, each segment from its own tokens.
-          mbar_arrive_expect_tx(fb, 3 * win.nq * C::kRowBytes);
           for (int sg = 0; sg < win.nseg; ++sg) {
             const AttnSeg sq = segs[win.seg0 + sg];
-            const CUtensorMap* mp = &maps.m[(sq.len + 15) >> 4];
-            const uint32_t o = (uint32_t)sq.row * C::kRowBytes;
-            tma_load_2d(dst + o, mp, fb, xq, sq.t0);
-            tma_load_2d(dst + C::kTileBytes + o, mp, fb, xk, sq.t0);
-            tma_load_2d(dst + 2 * C::kTileBytes + o, mp, fb, xv, sq.t0);
+            tma_load_2d(dst + (uint32_t)sq.row * C::kRowBytes, &maps.m[(sq.len + 15) >> 4], bar, x,
+                        sq.t0);
           }
         }
+      };
+      const uint32_t tile_tx = packed ? (uint32_t)win.nq * C::kRowBytes : (uint32_t)C::kTileBytes;
+      int qk_issued = 0, v_issued = 0;
+      auto issue_qk = [&](int u) -> bool {
+        const int slot = u % C::kQkStages;
+        if (u >= C::kQkStages &&
+            !mbar_wait_bounded(qkempty_b + 8 * slot, (uint32_t)(u / C::kQkStages - 1) & 1u, err,
+                               kDevTimeoutAttn, &abort_flag))
+          return false;
+        const int pair = u / nkb, j = u % nkb;
+        const uint32_t fb = qkfull_b + 8 * slot;
+        const uint32_t dst = sbase + C::kQkOffset + (uint32_t)slot * 2u * C::kTileBytes;
+        mbar_arrive_expect_tx(fb, 2 * tile_tx);
+        load_rows(dst, fb, pair * 2 * HD, win.q0);
+        load_rows(dst + C::kTileBytes, fb, hidden + pair * 2 * HD, win.k0 + 128 * j);
+        ++qk_issued;
+        return true;
+      };
+      auto issue_v = [&](int u) -> bool {
+        const int slot = u & 1;
+        if (u >= 2 && !mbar_wait_bounded(vempty_b + 8 * slot, (uint32_t)((u >> 1) - 1) & 1u, err,
+                                         kDevTimeoutAttn, &abort_flag))
+          return false;
+        const int pair = u / nkb, j = u % nkb;
+        const uint32_t fb = vfull_b + 8 * slot;
+        mbar_arrive_expect_tx(fb, tile_tx);
+        load_rows(sbase + C::kVOffset + (uint32_t)slot * C::kTileBytes, fb,
+                  2 * hidden + pair * 2 * HD, win.k0 + 128 * j);
+        ++v_issued;
+        return true;
+      };
+      // q·k two units ahead of v: QK(0), QK(1), V(0), QK(2), V(1), QK(3), …
+      bool ok = true;
+      for (int u = 0; ok && u < units && u < 2; ++u) ok = issue_qk(u);
+      for (int u = 0; ok && u < units; ++u) {
+        ok = issue_v(u);
+        if (ok && u + 2 < units) ok = issue_qk(u + 2);
       }
       // Drain (time-bounded, also after an abort): this thread's last copies
       // land before the CTA can exit.
-      for (int u = issued - 1; u >= 0 && u >= issued - 2; --u) {
+      for (int u = qk_issued - 1; u >= 0 && u >= qk_issued - C::kQkStages; --u) {
         const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(full_b + 8 * (u & 1), (uint32_t)(u >> 1) & 1u))
+        while (!mbar_try_wait(qkfull_b + 8 * (u % C::kQkStages), (uint32_t)(u / C::kQkStages) & 1u))
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+      for (int u = v_issued - 1; u >= 0 && u >= v_issued - 2; --u) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(vfull_b + 8 * (u & 1), (uint32_t)(u >> 1) & 1u))
           if (globaltimer_ns() - t0 > kWaitLimitNs) break;
       }
     }
@@ -201,8 +243,8 @@ __global__ void __launch_bounds__(320, 1)
       auto keys16 = [&](int j) { return (min(128, win.nk - 128 * j) + 15) & ~15; };
       // S(u, e) = q_e · k_eᵀ (+ the mask step) into group e's S columns.
       auto issue_s = [&](int u, int e) {
-        const int slot = u & 1;
-        const uint32_t q = sbase + slot * C::kStageBytes, k = q + C::kTileBytes;
+        const uint32_t q = sbase + C::kQkOffset + (uint32_t)(u % C::kQkStages) * 2u * C::kTileBytes;
+        const uint32_t k = q + C::kTileBytes;
         const uint32_t n = (uint32_t)keys16(u % nkb);
         const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (8u << 24);
         const uint32_t d = tmem + C::kColS + 128u * (uint32_t)e;
@@ -215,19 +257,42 @@ __global__ void __launch_bounds__(320, 1)
       };
       constexpr uint32_t idesc_pv = (1u << 4) | (1u << 16) | ((uint32_t)(64 >> 3) << 17) | (8u << 24);
       constexpr uint32_t idesc_l = (1u << 4) | (2u << 17) | (8u << 24);
-      bool ok = units > 0 &&
-                mbar_wait_bounded(full_b, 0, err, kDevTimeoutAttn, &abort_flag);
+      bool ok = units > 0 && mbar_wait_bounded(qkfull_b, 0u, err, kDevTimeoutAttn, &abort_flag);
       if (ok) {
         tc_fence_after();
         issue_s(0, 0);
         issue_s(0, 1);
+        mma_commit(qkempty_b);
       }
       for (int u = 0; ok && u < units; ++u) {
-        const int j = u % nkb, slot = u & 1;
-        const uint32_t v = sbase + slot * C::kStageBytes + 2 * C::kTileBytes;
+        // S(u + 1, ·) as soon as its q·k tiles are in and each group has read S(u).
+        if (u + 1 < units) {
+          const int nu = u + 1, qs = nu % C::kQkStages;
+          if (!mbar_wait_bounded(qkfull_b + 8 * qs, (uint32_t)(nu / C::kQkStages) & 1u, err,
+                                 kDevTimeoutAttn, &abort_flag))
+            break;
+          for (int e = 0; e < 2 && ok; ++e) {
+            if (!mbar_wait_bounded(sfree_b + 8 * e, (uint32_t)u & 1u, err, kDevTimeoutAttn,
+                                   &abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(nu, e);
+          }
+          if (!ok) break;
+          mma_commit(qkempty_b + 8 * qs);
+        }
+        // P·V(u, ·) once its v tile is in and each group has written P(u).
+        const int j = u % nkb, vs = u & 1;
+        if (!mbar_wait_bounded(vfull_b + 8 * vs, (uint32_t)(u >> 1) & 1u, err, kDevTimeoutAttn,
+                               &abort_flag))
+          break;
+        const uint32_t v = sbase + C::kVOffset + (uint32_t)vs * C::kTileBytes;
         const int nks = keys16(j) / 16;
         for (int e = 0; e < 2 && ok; ++e) {
-          if (!mbar_wait_bounded(pfull_b + 8 * e, u & 1, err, kDevTimeoutAttn, &abort_flag)) {
+          if (!mbar_wait_bounded(pfull_b + 8 * e, (uint32_t)u & 1u, err, kDevTimeoutAttn,
+                                 &abort_flag)) {
             ok = false;
             break;
           }
@@ -242,18 +307,9 @@ __global__ void __launch_bounds__(320, 1)
                      smem_desc_k_sw128(sOnes) + 2 * (ks & 3), idesc_l, acc);
           }
           mma_commit(ofull_b + 8 * e);
-          if (u + 1 < units) {
-            // Group e has handed in P(u, e), so it has read S(u, e).
-            if (e == 0 && !mbar_wait_bounded(full_b + 8 * ((u + 1) & 1), ((u + 1) >> 1) & 1, err,
-                                              kDevTimeoutAttn, &abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(u + 1, e);
-          }
         }
-        if (ok) mma_commit(empty_b + 8 * slot);
+        if (!ok) break;
+        mma_commit(vempty_b + 8 * vs);
       }
       // Drain (time-bounded): every MMA issued above completes before TMEM
       // is freed.
@@ -302,7 +358,8 @@ __global__ void __launch_bounds__(320, 1)
       const int nchunk = (((nkeys + 15) & ~15) + 31) / 32;  // chunks the P·V MMAs read
       const int c0 = packed ? clo : 0;
       const int c1 = packed ? chi : (nkeys + 31) >> 5;
-      if (!mbar_wait_bounded(sfull_b + 8 * e, u & 1, err, kDevTimeoutAttn, &abort_flag)) {
+      if (!mbar_wait_bounded(sfull_b + 8 * e, (uint32_t)u & 1u, err, kDevTimeoutAttn,
+                             &abort_flag)) {
         ok = false;
         break;
       }
@@ -312,6 +369,10 @@ __global__ void __launch_bounds__(320, 1)
       for (int c = 0; c < 4; ++c)
         if (c >= c0 && c < c1) tmem_ld32(srow + 32 * c, sv[c]);
       tmem_ld_wait();
+      // S(u) is in registers: the MMA thread may write S(u + 1).
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sfree_b + 8 * e);
       if (nkeys & 31) {
         const int c = (nkeys - 1) >> 5;
 #pragma unroll
@@ -339,7 +400,8 @@ __global__ void __launch_bounds__(320, 1)
       if (u > 0) {
         // P·V(u − 1, e) has finished: P_e may be overwritten, and O_e holds
         // either a finished head (store it) or this head's running sum.
-        if (!mbar_wait_bounded(ofull_b + 8 * e, (u - 1) & 1, err, kDevTimeoutAttn, &abort_flag)) {
+        if (!mbar_wait_bounded(ofull_b + 8 * e, (uint32_t)(u - 1) & 1u, err, kDevTimeoutAttn,
+                               &abort_flag)) {
           ok = false;
           break;
         }
@@ -359,8 +421,11 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st_wait();
         }
       }
-      // P = 2^(s·c − m·c) in f16 → this group's 128-byte-swizzled K-major
+      // P(u) = 2^(s·c − m·c) in f16 → this group's 128-byte-swizzled K-major
       // tile (keys 0-63 | 64-127); chunks no row of the warp needs are zero.
+      // (Forming P before the wait above would hide P·V(u − 1) behind the
+      // exponentials, but S and P together need more than the 168 registers
+      // a 10-warp CTA leaves each thread.)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         if (c < nchunk) {
@@ -393,7 +458,8 @@ __global__ void __launch_bounds__(320, 1)
       if (lane == 0) mbar_arrive(pfull_b + 8 * e);
     }
     if (ok && units > 0 &&
-        mbar_wait_bounded(ofull_b + 8 * e, (units - 1) & 1, err, kDevTimeoutAttn, &abort_flag)) {
+        mbar_wait_bounded(ofull_b + 8 * e, (uint32_t)(units - 1) & 1u, err, kDevTimeoutAttn,
+                          &abort_flag)) {
       tc_fence_after();
       store_head(2 * ((units - 1) / nkb) + e);
     }
