@@ -26,6 +26,30 @@ def test_bounds_tile_and_balance():
         assert per.max() <= per.sum() / world + costs.max() + 1e-6
 
 
+def test_bounds_properties_random():
+    """Any lengths and world size (more ranks than sequences included): the
+    ranges are contiguous, cover every sequence once, and no rank carries
+    more than its even share plus one sequence's cost."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    @settings(max_examples=200, deadline=None)
+    @given(st.lists(st.integers(1, 2048), min_size=0, max_size=64), st.integers(1, 12))
+    def check(lens, world):
+        cu = np.zeros(len(lens) + 1, np.int32)
+        np.cumsum(lens, out=cu[1:])
+        b = shard_bounds(cu, world)
+        assert len(b) == world and b[0][0] == 0 and b[-1][1] == len(lens)
+        assert all(b[k][1] == b[k + 1][0] for k in range(world - 1))
+        assert all(s0 <= s1 for s0, s1 in b)
+        if lens:
+            costs = sequence_costs(cu, 384)
+            per = np.array([costs[s0:s1].sum() for s0, s1 in b])
+            assert per.max() <= per.sum() / world + costs.max() * (1 + 1e-9) + 1e-6
+
+    check()
+
+
 def test_shard_for_rank_local_offsets():
     ids, cu = synth.make_inputs("c4", nseq=50)
     got = []
