@@ -1,5 +1,5 @@
-// attention_tc2.cuh — tcgen05 attention for head_dim 32 with head-pair
-// stages and two softmax warpgroups (opt-in, FUTON_CUDA_ATTN=tc2), restating
+// attention_tc2.cuh — tcgen05 attention with two softmax warpgroups and
+// separate q·k and v rings (opt-in, FUTON_CUDA_ATTN=tc2), restating
 // native/model.go:646-739 (attendHead, softmaxScaled) for every head and
 // sequence of a micro-batch.
 //
@@ -9,28 +9,32 @@
 // one more K = 16 MMA step, or 128 queries of a longer sequence with its
 // keys in 128-key blocks); exponents rounded to f16 before ex2.approx.f16x2,
 // P and V in f16, f32 accumulation in TMEM. What changes is the pipeline.
-// A unit u is one head PAIR (adjacent qkv columns: one 64-column box,
-// 128-byte rows, 128-byte swizzle) and one key block:
+// A unit u is one key block of 64 qkv columns (one box, 128-byte rows,
+// 128-byte swizzle): for head_dim 32 a head PAIR, whose two heads go to the
+// two softmax groups; for head_dim 64 one head, units alternating between
+// the groups (head pairs in order, each pair's key blocks interleaved, so a
+// group meets its head's key blocks in order):
 //
 //   warp 8 (one thread)  TMA: q and k of unit u into a three-stage ring,
 //                        v into a separate two-stage ring, so the next
 //                        units' q·k tiles are in flight two units ahead and
 //                        a v tile is released as soon as its P·V is done;
-//   warp 9 (one thread)  MMA, TMEM owner (512 columns): S(u + 1, e) as soon
-//                        as group e has read S(u, e); P·V(u, e) once P(u, e)
-//                        is written;
-//   warps 0-3, 4-7       softmax groups e = 0, 1, one per head of the pair,
-//                        thread = query row. Each group owns its S (128 TMEM
-//                        columns), O (64: P·V runs over both heads' value
-//                        columns, the group reads its own 32), row sums (16)
+//   warp 9 (one thread)  MMA, TMEM owner (512 columns): a group's next S as
+//                        soon as it has read its current one; P·V once P is
+//                        written;
+//   warps 0-3, 4-7       softmax groups e = 0, 1, thread = query row. Each
+//                        group owns its S (128 TMEM columns), O (64: for
+//                        head_dim 32 P·V runs over both heads' value columns
+//                        and the group reads its own 32), row sums (16)
 //                        and P tile (32 KB). A group reads S(u) and frees it
 //                        at once, so S(u + 1) is computed while the group
 //                        waits for P·V(u − 1) (which frees its P tile and
 //                        settles O) and writes P(u); the other group's work
 //                        fills this group's waits.
 //
-// q·kᵀ of head e reads its 32 columns at byte 64·e of each 128-byte row (the
-// start-address advance inside a swizzle atom that the GEMM's K steps use).
+// For head_dim 32, q·kᵀ of head e reads its 32 columns at byte 64·e of each
+// 128-byte row (the start-address advance inside a swizzle atom that the
+// GEMM's K steps use).
 // Every wait is bounded (kDevTimeoutAttn); before exit the producer waits
 // (time-bounded) for its last copies and the MMA thread for its last MMAs.
 #pragma once
@@ -66,15 +70,17 @@ struct AttnTc2Cfg {
 
 constexpr int attn_tc2_smem_bytes() { return AttnTc2Cfg::kBytes; }
 
-// grid = number of windows, block = 320; num_heads even; qkv [T, 3h] (bf16
-// q, k; f16 v) through maps.m[n] (boxes of 16·n rows × 64 columns).
-template <typename OutT>
+// grid = number of windows, block = 320; HD = 32 or 64, num_heads even; qkv
+// [T, 3h] (bf16 q, k; f16 v) through maps.m[n] (boxes of 16·n rows × 64
+// columns).
+template <int HD, typename OutT>
 __global__ void __launch_bounds__(320, 1)
     attn_tc2_kernel(const __grid_constant__ AttnMaps maps, int hidden, int num_heads,
                     const AttnWindow* __restrict__ windows, const AttnSeg* __restrict__ segs,
                     float scale_log2, OutT* __restrict__ out, int ldo, int* __restrict__ err) {
+  static_assert(HD == 32 || HD == 64, "head_dim 32 or 64");
   using C = AttnTc2Cfg;
-  constexpr int HD = 32;
+  constexpr bool kPair = HD == 32;          // a unit = a head pair (both groups)
   extern __shared__ uint8_t sm_raw[];
   const uint32_t sbase = (smem_u32(sm_raw) + 1023u) & ~1023u;
   const uint32_t sOnes = sbase + C::kOnesOffset;
@@ -94,8 +100,13 @@ __global__ void __launch_bounds__(320, 1)
 
   const AttnWindow win = windows[blockIdx.x];
   const bool packed = win.nseg > 0;
-  const int nkb = (win.nk + 127) / 128;     // key blocks per head pair
-  const int units = (num_heads / 2) * nkb;
+  const int nkb = (win.nk + 127) / 128;     // key blocks per head
+  const int units = (kPair ? num_heads / 2 : num_heads) * nkb;
+  // Unit u's 64-column block and key block.
+  auto unit_col = [&](int u) {
+    return kPair ? (u / nkb) * 64 : (2 * (u / (2 * nkb)) + (u & 1)) * 64;
+  };
+  auto unit_kb = [&](int u) { return kPair ? u % nkb : (u % (2 * nkb)) >> 1; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -195,12 +206,12 @@ __global__ void __launch_bounds__(320, 1)
             !mbar_wait_bounded(qkempty_b + 8 * slot, (uint32_t)(u / C::kQkStages - 1) & 1u, err,
                                kDevTimeoutAttn, &abort_flag))
           return false;
-        const int pair = u / nkb, j = u % nkb;
+        const int col = unit_col(u), j = unit_kb(u);
         const uint32_t fb = qkfull_b + 8 * slot;
         const uint32_t dst = sbase + C::kQkOffset + (uint32_t)slot * 2u * C::kTileBytes;
         mbar_arrive_expect_tx(fb, 2 * tile_tx);
-        load_rows(dst, fb, pair * 2 * HD, win.q0);
-        load_rows(dst + C::kTileBytes, fb, hidden + pair * 2 * HD, win.k0 + 128 * j);
+        load_rows(dst, fb, col, win.q0);
+        load_rows(dst + C::kTileBytes, fb, hidden + col, win.k0 + 128 * j);
         ++qk_issued;
         return true;
       };
@@ -209,20 +220,22 @@ __global__ void __launch_bounds__(320, 1)
         if (u >= 2 && !mbar_wait_bounded(vempty_b + 8 * slot, (uint32_t)((u >> 1) - 1) & 1u, err,
                                          kDevTimeoutAttn, &abort_flag))
           return false;
-        const int pair = u / nkb, j = u % nkb;
+        const int col = unit_col(u), j = unit_kb(u);
         const uint32_t fb = vfull_b + 8 * slot;
         mbar_arrive_expect_tx(fb, tile_tx);
-        load_rows(sbase + C::kVOffset + (uint32_t)slot * C::kTileBytes, fb,
-                  2 * hidden + pair * 2 * HD, win.k0 + 128 * j);
+        load_rows(sbase + C::kVOffset + (uint32_t)slot * C::kTileBytes, fb, 2 * hidden + col,
+                  win.k0 + 128 * j);
         ++v_issued;
         return true;
       };
-      // q·k two units ahead of v: QK(0), QK(1), V(0), QK(2), V(1), QK(3), …
+      // q·k two units ahead of v: QK(0), QK(1), QK(2), V(0), QK(3), V(1), …
+      // (QK(u + 2) needs only the S of unit u − 1 to be done, V(u) the P·V
+      // of unit u − 2).
       bool ok = true;
       for (int u = 0; ok && u < units && u < 2; ++u) ok = issue_qk(u);
       for (int u = 0; ok && u < units; ++u) {
-        ok = issue_v(u);
-        if (ok && u + 2 < units) ok = issue_qk(u + 2);
+        if (u + 2 < units) ok = issue_qk(u + 2);
+        if (ok) ok = issue_v(u);
       }
       // Drain (time-bounded, also after an abort): this thread's last copies
       // land before the CTA can exit.
@@ -241,30 +254,89 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       auto keys16 = [&](int j) { return (min(128, win.nk - 128 * j) + 15) & ~15; };
-      // S(u, e) = q_e · k_eᵀ (+ the mask step) into group e's S columns.
+      // S of unit u for group e = q · kᵀ (+ the mask step) into the group's S
+      // columns; head_dim 32: head e's columns start 64 bytes into each row.
       auto issue_s = [&](int u, int e) {
         const uint32_t q = sbase + C::kQkOffset + (uint32_t)(u % C::kQkStages) * 2u * C::kTileBytes;
         const uint32_t k = q + C::kTileBytes;
-        const uint32_t n = (uint32_t)keys16(u % nkb);
+        const uint32_t n = (uint32_t)keys16(unit_kb(u));
         const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (8u << 24);
         const uint32_t d = tmem + C::kColS + 128u * (uint32_t)e;
+        const uint64_t hoff = kPair ? 4u * (uint32_t)e : 0u;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks)
-          mma_bf16(d, smem_desc_k_sw128(q) + 4 * e + 2 * ks, smem_desc_k_sw128(k) + 4 * e + 2 * ks,
+          mma_bf16(d, smem_desc_k_sw128(q) + hoff + 2 * ks, smem_desc_k_sw128(k) + hoff + 2 * ks,
                    idesc, ks ? 1u : 0u);
         if (packed) mma_bf16(d, desc_rows<32>(sQa), desc_rows<32>(sKa), idesc, 1u);
         mma_commit(sfull_b + 8 * e);
       };
       constexpr uint32_t idesc_pv = (1u << 4) | (1u << 16) | ((uint32_t)(64 >> 3) << 17) | (8u << 24);
       constexpr uint32_t idesc_l = (1u << 4) | (2u << 17) | (8u << 24);
-      bool ok = units > 0 && mbar_wait_bounded(qkfull_b, 0u, err, kDevTimeoutAttn, &abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        issue_s(0, 1);
-        mma_commit(qkempty_b);
+      // P·V of unit u for group e into the group's O and row-sum columns.
+      auto issue_pv = [&](int u, int e) {
+        const int j = unit_kb(u);
+        const uint32_t v = sbase + C::kVOffset + (uint32_t)(u & 1) * C::kTileBytes;
+        const uint32_t sp = sbase + C::kPOffset + (uint32_t)e * C::kPBytes;
+        const int nks = keys16(j) / 16;
+        for (int ks = 0; ks < nks; ++ks) {
+          const uint64_t pd = smem_desc_k_sw128(sp + (ks >> 2) * 16384) + 2 * (ks & 3);
+          const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+          mma_bf16(tmem + C::kColO + 64u * (uint32_t)e, pd,
+                   desc_rows<64>(v + ks * 16 * C::kRowBytes), idesc_pv, acc);
+          mma_bf16(tmem + C::kColL + 32u * (uint32_t)e, pd,
+                   smem_desc_k_sw128(sOnes) + 2 * (ks & 3), idesc_l, acc);
+        }
+        mma_commit(ofull_b + 8 * e);
+      };
+      bool ok = units > 0;
+      if constexpr (kPair) {
+        if (ok) ok = mbar_wait_bounded(qkfull_b, 0u, err, kDevTimeoutAttn, &abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0, 0);
+          issue_s(0, 1);
+          mma_commit(qkempty_b);
+        }
+      } else {
+        // Units 0 and 1 start the two groups.
+        for (int u = 0; ok && u < 2 && u < units; ++u) {
+          ok = mbar_wait_bounded(qkfull_b + 8 * u, 0u, err, kDevTimeoutAttn, &abort_flag);
+          if (ok) {
+            tc_fence_after();
+            issue_s(u, u & 1);
+            mma_commit(qkempty_b + 8 * u);
+          }
+        }
       }
-      for (int u = 0; ok && u < units; ++u) {
+      for (int u = 0; ok && !kPair && u < units; ++u) {
+        // Unit u belongs to group e = u mod 2 as its i-th; the group's next
+        // unit is u + 2.
+        const int e = u & 1, i = u >> 1;
+        if (u + 2 < units) {
+          const int w = u + 2, qs = w % C::kQkStages;
+          if (!mbar_wait_bounded(qkfull_b + 8 * qs, (uint32_t)(w / C::kQkStages) & 1u, err,
+                                 kDevTimeoutAttn, &abort_flag) ||
+              !mbar_wait_bounded(sfree_b + 8 * e, (uint32_t)i & 1u, err, kDevTimeoutAttn,
+                                 &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(w, e);
+          mma_commit(qkempty_b + 8 * qs);
+        }
+        if (!mbar_wait_bounded(vfull_b + 8 * (u & 1), (uint32_t)(u >> 1) & 1u, err, kDevTimeoutAttn,
+                               &abort_flag) ||
+            !mbar_wait_bounded(pfull_b + 8 * e, (uint32_t)i & 1u, err, kDevTimeoutAttn,
+                               &abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(u, e);
+        mma_commit(vempty_b + 8 * (u & 1));
+      }
+      for (int u = 0; ok && kPair && u < units; ++u) {
         // S(u + 1, ·) as soon as its q·k tiles are in and each group has read S(u).
         if (u + 1 < units) {
           const int nu = u + 1, qs = nu % C::kQkStages;
@@ -284,12 +356,10 @@ __global__ void __launch_bounds__(320, 1)
           mma_commit(qkempty_b + 8 * qs);
         }
         // P·V(u, ·) once its v tile is in and each group has written P(u).
-        const int j = u % nkb, vs = u & 1;
+        const int vs = u & 1;
         if (!mbar_wait_bounded(vfull_b + 8 * vs, (uint32_t)(u >> 1) & 1u, err, kDevTimeoutAttn,
                                &abort_flag))
           break;
-        const uint32_t v = sbase + C::kVOffset + (uint32_t)vs * C::kTileBytes;
-        const int nks = keys16(j) / 16;
         for (int e = 0; e < 2 && ok; ++e) {
           if (!mbar_wait_bounded(pfull_b + 8 * e, (uint32_t)u & 1u, err, kDevTimeoutAttn,
                                  &abort_flag)) {
@@ -297,16 +367,7 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sp = sbase + C::kPOffset + (uint32_t)e * C::kPBytes;
-          for (int ks = 0; ks < nks; ++ks) {
-            const uint64_t pd = smem_desc_k_sw128(sp + (ks >> 2) * 16384) + 2 * (ks & 3);
-            const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
-            mma_bf16(tmem + C::kColO + 64u * (uint32_t)e, pd,
-                     desc_rows<64>(v + ks * 16 * C::kRowBytes), idesc_pv, acc);
-            mma_bf16(tmem + C::kColL + 32u * (uint32_t)e, pd,
-                     smem_desc_k_sw128(sOnes) + 2 * (ks & 3), idesc_l, acc);
-          }
-          mma_commit(ofull_b + 8 * e);
+          issue_pv(u, e);
         }
         if (!ok) break;
         mma_commit(vempty_b + 8 * vs);
@@ -323,7 +384,9 @@ __global__ void __launch_bounds__(320, 1)
     const int e = grp;
     const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t srow = tmem + lanes + C::kColS + 128u * (uint32_t)e;
-    const uint32_t orow = tmem + lanes + C::kColO + 64u * (uint32_t)e + 32u * (uint32_t)e;
+    // This group's O columns: head_dim 32 its head's 32 of the pair's 64.
+    constexpr int kOCols = kPair ? 32 : 64;
+    const uint32_t orow = tmem + lanes + C::kColO + 64u * (uint32_t)e + (kPair ? 32u * (uint32_t)e : 0u);
     const uint32_t lrow = tmem + lanes + C::kColL + 32u * (uint32_t)e;
     const uint32_t prow = sbase + C::kPOffset + (uint32_t)e * C::kPBytes + (uint32_t)r * 128u;
     const int swz = r & 7;
@@ -336,29 +399,38 @@ __global__ void __launch_bounds__(320, 1)
     float m_run = -INFINITY;
     bool ok = true;
 
-    // Normalised O row of head `head` (this group's 32 columns) to global memory.
+    // The head of unit u (this group's).
+    auto head_of = [&](int u) { return kPair ? 2 * (u / nkb) + e : unit_col(u) / 64; };
+    // Normalised O row of head `head` to global memory.
     auto store_head = [&](int head) {
-      uint32_t t[32];
-      tmem_ld32(orow, t);
       const float l = __uint_as_float(tmem_ld1(lrow));
       tmem_ld_wait();
-      if (tok >= 0) {
-        const float inv = rcp_approx(l);  // l ≥ 1: the row maximum contributes 2^0
-        float y[32];
+      const float inv = rcp_approx(l);  // l ≥ 1: the row maximum contributes 2^0
 #pragma unroll
-        for (int i = 0; i < 32; ++i) y[i] = __uint_as_float(t[i]) * inv;
-        store32<OutT>(out + (size_t)tok * ldo + head * HD, y);
+      for (int c = 0; c < kOCols; c += 32) {
+        uint32_t t[32];
+        tmem_ld32(orow + c, t);
+        tmem_ld_wait();
+        if (tok >= 0) {
+          float y[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) y[i] = __uint_as_float(t[i]) * inv;
+          store32<OutT>(out + (size_t)tok * ldo + head * HD + c, y);
+        }
       }
     };
 
-    for (int u = 0; u < units && ok; ++u) {
-      const int j = u % nkb;
+    // This group's units: every unit (head pairs) or every other one.
+    const int ustep = kPair ? 1 : 2;
+    const int mine = kPair ? units : units / 2;
+    for (int i = 0, u = kPair ? 0 : e; i < mine && ok; ++i, u += ustep) {
+      const int j = unit_kb(u);
       if (j == 0) m_run = -INFINITY;  // a new head
       const int nkeys = min(128, win.nk - 128 * j);
       const int nchunk = (((nkeys + 15) & ~15) + 31) / 32;  // chunks the P·V MMAs read
       const int c0 = packed ? clo : 0;
       const int c1 = packed ? chi : (nkeys + 31) >> 5;
-      if (!mbar_wait_bounded(sfull_b + 8 * e, (uint32_t)u & 1u, err, kDevTimeoutAttn,
+      if (!mbar_wait_bounded(sfull_b + 8 * e, (uint32_t)i & 1u, err, kDevTimeoutAttn,
                              &abort_flag)) {
         ok = false;
         break;
@@ -397,24 +469,27 @@ __global__ void __launch_bounds__(320, 1)
       m_run = m_new;
       const float ms = m_use * scale_log2;
       const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nms2 = f2_pack(-ms, -ms);
-      if (u > 0) {
-        // P·V(u − 1, e) has finished: P_e may be overwritten, and O_e holds
-        // either a finished head (store it) or this head's running sum.
-        if (!mbar_wait_bounded(ofull_b + 8 * e, (uint32_t)(u - 1) & 1u, err, kDevTimeoutAttn,
+      if (i > 0) {
+        // The group's previous P·V has finished: P_e may be overwritten, and
+        // O_e holds either a finished head (store it) or this head's running sum.
+        if (!mbar_wait_bounded(ofull_b + 8 * e, (uint32_t)(i - 1) & 1u, err, kDevTimeoutAttn,
                                &abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (j == 0) {
-          store_head(2 * ((u - 1) / nkb) + e);
+          store_head(head_of(u - ustep));
         } else if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          uint32_t t[32];
-          tmem_ld32(orow, t);
-          tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
-          tmem_st32(orow, t);
+          for (int c = 0; c < kOCols; c += 32) {
+            uint32_t t[32];
+            tmem_ld32(orow + c, t);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 32; ++q) t[q] = __float_as_uint(__uint_as_float(t[q]) * alpha);
+            tmem_st32(orow + c, t);
+          }
           const float l = __uint_as_float(tmem_ld1(lrow));
           tmem_ld_wait();
           tmem_st1(lrow, __float_as_uint(l * alpha));
@@ -457,11 +532,11 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(pfull_b + 8 * e);
     }
-    if (ok && units > 0 &&
-        mbar_wait_bounded(ofull_b + 8 * e, (uint32_t)(units - 1) & 1u, err, kDevTimeoutAttn,
+    if (ok && mine > 0 &&
+        mbar_wait_bounded(ofull_b + 8 * e, (uint32_t)(mine - 1) & 1u, err, kDevTimeoutAttn,
                           &abort_flag)) {
       tc_fence_after();
-      store_head(2 * ((units - 1) / nkb) + e);
+      store_head(head_of(kPair ? units - 1 : units - 2 + e));
     }
   }
 

@@ -312,7 +312,7 @@ struct futon_model {
   int swiglu_half = 0;
   // Attention kernel of the float path (read from FUTON_CUDA_ATTN when the
   // model is created): 0 = attn_heads_kernel, 1 = attn_tc_kernel,
-  // 2 = attn_tc2_kernel (head_dim 32, even head count; others keep 0).
+  // 2 = attn_tc2_kernel (head_dim 32 or 64, even head count; others keep 0).
   int attn_kind = 0;
   // FUTON_CUDA_ATTN_SPLIT=1: attn_heads_kernel launches with the head groups
   // shared among grid.y CTAs when the tiles alone would leave SMs idle.
@@ -792,9 +792,10 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
   const AttnTile* tiles = plan.tiles;
   const int ntiles = plan.ntiles;
   if constexpr (!kSplit) {
-    if (m.attn_kind == kAttnTc2 && hd == 32 && H % 2 == 0 && !cls_only) {
+    if (m.attn_kind == kAttnTc2 && tc_hd && H % 2 == 0 && !cls_only) {
       if (plan.nwin == 0) return FUTON_OK;
-      // q, k, v tiles of one head pair: 16·n rows × 64 columns, 128-byte swizzle.
+      // 64-column q, k, v tiles (a head pair for head_dim 32, a head for 64):
+      // 16·n rows, 128-byte swizzle.
       AttnMaps maps{};
       for (int n = 1; n <= 8; ++n)
         if (!d.map_cache.get(MapKey{kMapQkv, qkv, (uint64_t)T, (uint64_t)(3 * h), 64u, 16u * n},
@@ -804,11 +805,14 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
                              }))
           return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
       const int smem = attn_tc2_smem_bytes();
-      CU_TRY(cudaFuncSetAttribute(attn_tc2_kernel<OutT>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      attn_tc2_kernel<OutT><<<plan.nwin, AttnTc2Cfg::kThreads, smem, st>>>(
-          maps, h, H, plan.wins, plan.segs, scale_log2, out, h, d.err_word);
-      CU_TRY(cudaGetLastError());
+      auto launch = [&](auto kern) -> cudaError_t {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        kern<<<plan.nwin, AttnTc2Cfg::kThreads, smem, st>>>(maps, h, H, plan.wins, plan.segs,
+                                                             scale_log2, out, h, d.err_word);
+        return cudaGetLastError();
+      };
+      CU_TRY(hd == 32 ? launch(attn_tc2_kernel<32, OutT>) : launch(attn_tc2_kernel<64, OutT>));
       d.launches.fetch_add(1, std::memory_order_relaxed);
       return FUTON_OK;
     }

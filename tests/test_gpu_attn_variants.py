@@ -8,8 +8,8 @@ default `-m gpu` suite does not select them.
 - split: attn_heads_kernel with the head groups shared among grid.y CTAs.
   Every head is computed by the same code in the same order as without the
   split, so the vectors must be bitwise equal to the default kernel's.
-- tc, tc2: the tcgen05 attention kernels (tc2: head-pair stages and two
-  softmax warpgroups, head_dim 32 only; other shapes keep the default);
+- tc, tc2: the tcgen05 attention kernels (tc2: separate q·k and v rings
+  and two softmax warpgroups; head_dim 32 or 64 with an even head count);
   parity with the oracle (cosine gate) and batch invariance (a sequence's
   vector does not depend on what it is packed with).
 - FUTON_CUDA_Q8_ATTN=exact: the int8 path's attention in the reference's

@@ -1,5 +1,7 @@
 """Model check of attn_tc2_kernel's barrier protocol (futon_b200/csrc/
-attention_tc2.cuh), on the CPU.
+attention_tc2.cuh), on the CPU, for both of its forms: head_dim 32 (a unit
+is a head pair and serves both softmax groups) and head_dim 64 (a unit is
+one head; units alternate between the groups).
 
 The kernel's four roles — TMA producer, MMA thread, and the two softmax
 groups (four warps each) — are restated as coroutines that wait on and
@@ -37,7 +39,7 @@ class Bar:
         return (self.phase & 1) != parity
 
 
-def simulate(units: int, seed: int) -> None:
+def simulate(units: int, seed: int, pair: bool) -> None:
     rng = random.Random(seed)
     qkfull = [Bar(f"qkfull{i}", 1) for i in range(QK_STAGES)]
     qkempty = [Bar(f"qkempty{i}", 1) for i in range(QK_STAGES)]
@@ -84,9 +86,9 @@ def simulate(units: int, seed: int) -> None:
         for u in range(min(2, units)):
             yield from issue_qk(u)
         for u in range(units):
-            yield from issue_v(u)
             if u + 2 < units:
                 yield from issue_qk(u + 2)
+            yield from issue_v(u)
 
     def mma_thread():
         def issue_s(u, e):
@@ -96,7 +98,32 @@ def simulate(units: int, seed: int) -> None:
             mma([f"QK{u % QK_STAGES}"], [f"S{e}"])
             mma_queue.append(("commit", sfull[e]))
 
+        def issue_pv(u, e):
+            vs = u & 1
+            assert content.get(f"V{vs}") == u, ("P·V reads a stale v slot", u)
+            assert p_unit[e] == u, ("P·V reads a stale P", e, u)
+            mma([f"P{e}", f"V{vs}"], [f"O{e}"])
+            mma_queue.append(("commit", ofull[e]))
+
         if units == 0:
+            return
+        if not pair:
+            for u in range(min(2, units)):
+                yield ("wait", qkfull[u], 0)
+                issue_s(u, u & 1)
+                mma_queue.append(("commit", qkempty[u]))
+            for u in range(units):
+                e, i = u & 1, u >> 1
+                if u + 2 < units:
+                    w = u + 2
+                    yield ("wait", qkfull[w % QK_STAGES], (w // QK_STAGES) & 1)
+                    yield ("wait", sfree[e], i & 1)
+                    issue_s(w, e)
+                    mma_queue.append(("commit", qkempty[w % QK_STAGES]))
+                yield ("wait", vfull[u & 1], (u >> 1) & 1)
+                yield ("wait", pfull[e], i & 1)
+                issue_pv(u, e)
+                mma_queue.append(("commit", vempty[u & 1]))
             return
         yield ("wait", qkfull[0], 0)
         issue_s(0, 0)
@@ -114,31 +141,29 @@ def simulate(units: int, seed: int) -> None:
             yield ("wait", vfull[vs], (u >> 1) & 1)
             for e in range(2):
                 yield ("wait", pfull[e], u & 1)
-                assert content.get(f"V{vs}") == u, ("P·V reads a stale v slot", u)
-                assert p_unit[e] == u, ("P·V reads a stale P", e, u)
-                mma([f"P{e}", f"V{vs}"], [f"O{e}"])
-                mma_queue.append(("commit", ofull[e]))
+                issue_pv(u, e)
             mma_queue.append(("commit", vempty[vs]))
 
     def group_warp(e):
-        for u in range(units):
-            yield ("wait", sfull[e], u & 1)
+        mine = list(range(units)) if pair else list(range(e, units, 2))
+        for i, u in enumerate(mine):
+            yield ("wait", sfull[e], i & 1)
             assert writes_pending.get(f"S{e}", 0) == 0 and s_state[e] == ("pending", u), \
                 ("group reads the wrong S", e, u)
             s_reads[e] += 1
             if s_reads[e] == 4:
                 s_state[e], s_reads[e] = "read", 0
             yield ("act", sfree[e].arrive)
-            if u > 0:
-                yield ("wait", ofull[e], (u - 1) & 1)
+            if i > 0:
+                yield ("wait", ofull[e], (i - 1) & 1)
                 assert writes_pending.get(f"O{e}", 0) == 0, "O read while a P·V writes it"
                 assert reads_pending.get(f"P{e}", 0) == 0, "P written while a P·V reads it"
             p_writes[e] += 1
             if p_writes[e] == 4:
                 p_unit[e], p_writes[e] = u, 0
             yield ("act", pfull[e].arrive)
-        if units:
-            yield ("wait", ofull[e], (units - 1) & 1)
+        if mine:
+            yield ("wait", ofull[e], (len(mine) - 1) & 1)
             assert writes_pending.get(f"O{e}", 0) == 0
 
     roles = [producer(), mma_thread()] + [group_warp(e) for e in range(2) for _ in range(4)]
@@ -185,6 +210,12 @@ def simulate(units: int, seed: int) -> None:
 
 
 @pytest.mark.parametrize("units", [1, 2, 3, 4, 5, 6, 7, 12, 24])
-def test_tc2_protocol_random_schedules(units):
+def test_tc2_pair_protocol_random_schedules(units):
     for seed in range(200):
-        simulate(units, seed)
+        simulate(units, seed, pair=True)
+
+
+@pytest.mark.parametrize("units", [2, 4, 6, 8, 12, 24, 48])
+def test_tc2_single_head_protocol_random_schedules(units):
+    for seed in range(200):
+        simulate(units, seed, pair=False)
