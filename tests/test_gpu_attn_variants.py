@@ -64,6 +64,7 @@ CASES = [
     ("bge", "c0", 32, None),       # CLS pooling: the pruned last layer splits too
     ("minilm6", "c1", 16, None),   # mean pooling, 128-token sequences (two key tiles)
     ("nomic", "c2", 4, 3),         # head_dim 64, one head per step, up to 512 tokens
+    ("bge", "c4", 64, 2),          # head_dim 32 with sequences past 128 tokens (key blocks)
 ]
 
 
