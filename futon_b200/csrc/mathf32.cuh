@@ -163,16 +163,40 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
 // GELU of two values. With z = |x| and the 7.1.28 coefficients a_k scaled
 // by (1/√2)^k · 2^(1/16), P'(z)^16 = 2 · P(z/√2)^16, so q = 1/P'(z)^16 =
 // 0.5 · erfc(|x|/√2) and gelu(x) = max(x, 0) − |x| · q for either sign.
+// gelu_p(k): P' coefficient k, from z^6 (k = 0) down to z^0 (k = 6).
+FUTON_HD constexpr float gelu_p(int k) {
+  return k == 0   ? 5.6212996640e-06f
+         : k == 1 ? 5.1055209009e-05f
+         : k == 2 ? 3.9686137011e-05f
+         : k == 3 ? 3.4227392389e-03f
+         : k == 4 ? 2.2076998457e-02f
+         : k == 5 ? 5.2075163037e-02f
+                  : 1.0442737824e+00f;
+}
+
+// The same evaluation on one value with an exactly rounded reciprocal
+// (gelu_fast2 uses rcp.approx, within 1 ulp of it): the host's check of the
+// formula's accuracy.
+FUTON_HD __forceinline__ float gelu_fast_ref(float x) {
+  const float z = x < 0.0f ? -x : x;
+  float p = gelu_p(0);
+  for (int k = 1; k < 7; ++k) p = fmaf(p, z, gelu_p(k));
+  p = p * p;
+  p = p * p;
+  p = p * p;
+  p = p * p;
+  return fmaf(-z, 1.0f / p, x > 0.0f ? x : 0.0f);
+}
+
 __device__ __forceinline__ void gelu_fast2(float& x0, float& x1) {
   const float z0 = fabsf(x0), z1 = fabsf(x1);
   const uint64_t z = f2_pack(z0, z1);
-  uint64_t p = f2_fma(f2_pack(5.6212996640e-06f, 5.6212996640e-06f), z,
-                      f2_pack(5.1055209009e-05f, 5.1055209009e-05f));
-  p = f2_fma(p, z, f2_pack(3.9686137011e-05f, 3.9686137011e-05f));
-  p = f2_fma(p, z, f2_pack(3.4227392389e-03f, 3.4227392389e-03f));
-  p = f2_fma(p, z, f2_pack(2.2076998457e-02f, 2.2076998457e-02f));
-  p = f2_fma(p, z, f2_pack(5.2075163037e-02f, 5.2075163037e-02f));
-  p = f2_fma(p, z, f2_pack(1.0442737824e+00f, 1.0442737824e+00f));
+  uint64_t p = f2_fma(f2_pack(gelu_p(0), gelu_p(0)), z, f2_pack(gelu_p(1), gelu_p(1)));
+  p = f2_fma(p, z, f2_pack(gelu_p(2), gelu_p(2)));
+  p = f2_fma(p, z, f2_pack(gelu_p(3), gelu_p(3)));
+  p = f2_fma(p, z, f2_pack(gelu_p(4), gelu_p(4)));
+  p = f2_fma(p, z, f2_pack(gelu_p(5), gelu_p(5)));
+  p = f2_fma(p, z, f2_pack(gelu_p(6), gelu_p(6)));
   p = f2_mul(p, p);
   p = f2_mul(p, p);
   p = f2_mul(p, p);

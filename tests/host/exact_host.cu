@@ -73,3 +73,7 @@ extern "C" float fx_exp_f32(float x) { return exp_f32(x); }
 // reference's geluF32 and sigmoidF32, mathf32.go:40-120).
 extern "C" float fx_gelu_f32(float x) { return gelu_f32(x); }
 extern "C" float fx_sigmoid_f32(float x) { return sigmoid_f32(x); }
+
+// The bf16 path's fast GELU formula (gelu_fast2's evaluation with an exactly
+// rounded reciprocal), for the accuracy bound the design states.
+extern "C" float fx_gelu_fast_ref(float x) { return gelu_fast_ref(x); }

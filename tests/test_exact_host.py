@@ -2,7 +2,8 @@
 bit for bit: the attention (futon_b200/csrc/attn_exact.cuh) against the
 oracle's attendHead (native/model.go:646-739) in the avx2Kernel summation
 order, and the activations (futon_b200/csrc/mathf32.cuh: expF32, geluF32,
-sigmoidF32, native/mathf32.go:40-120).
+sigmoidF32, native/mathf32.go:40-120). Also the accuracy of the bf16 path's
+fast GELU formula against the exact-erf GELU.
 
 tests/host/exact_host.cu runs the routines the device kernels call,
 over the same 64-key tiles in the same order, as host code built with nvcc
@@ -38,7 +39,7 @@ def fx(tmp_path_factory):
     lib.fx_attend_head.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                    C.c_void_p]
     lib.fx_attend_head.restype = C.c_int
-    for name in ("fx_exp_f32", "fx_gelu_f32", "fx_sigmoid_f32"):
+    for name in ("fx_exp_f32", "fx_gelu_f32", "fx_sigmoid_f32", "fx_gelu_fast_ref"):
         getattr(lib, name).argtypes = [C.c_float]
         getattr(lib, name).restype = C.c_float
     return lib
@@ -99,3 +100,19 @@ def test_activation_host_matches_oracle(fx, name, ref):
     want = np.array([r(float(x)) for x in xs], np.float32)
     bad = np.flatnonzero(got.view(np.uint32) != want.view(np.uint32))
     assert bad.size == 0, f"{name}: {bad.size} mismatches, first at x={xs[bad[0]]!r}"
+
+
+def test_fast_gelu_formula_error_bound(fx):
+    """The bf16 path's GELU (Abramowitz & Stegun 7.1.28 in gelu_fast2) stays
+    within 7.1e-7 of the exact-erf GELU over [−12, 12] (float64 reference).
+    The device evaluates the same formula with rcp.approx (within 1 ulp of
+    the exact reciprocal used here), far below that bound."""
+    import math
+    xs = np.concatenate([np.linspace(-12, 12, 96001, dtype=np.float32),
+                         np.linspace(3.9, 4.1, 20001, dtype=np.float32)])
+    worst = 0.0
+    for x in xs:
+        x = float(x)
+        exact = 0.5 * x * math.erfc(-x / math.sqrt(2.0))
+        worst = max(worst, abs(fx.fx_gelu_fast_ref(x) - exact))
+    assert worst <= 7.1e-7, worst
