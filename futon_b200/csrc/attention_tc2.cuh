@@ -471,13 +471,47 @@ __global__ void __launch_bounds__(320, 1)
       const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nms2 = f2_pack(-ms, -ms);
       if (i > 0) {
         // The group's previous P·V has finished: P_e may be overwritten, and
-        // O_e holds either a finished head (store it) or this head's running sum.
+        // O_e holds either a finished head or this head's running sum (dealt
+        // with after the P write, once S is out of registers).
         if (!mbar_wait_bounded(ofull_b + 8 * e, (uint32_t)(i - 1) & 1u, err, kDevTimeoutAttn,
                                &abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
+      }
+      // P(u) = 2^(s·c − m·c) in f16 → this group's 128-byte-swizzled K-major
+      // tile (keys 0-63 | 64-127); chunks no row of the warp needs are zero.
+      // (Forming P before the wait above would hide P·V(u − 1) behind the
+      // exponentials, but S and P together need more than the 168 registers
+      // a 10-warp CTA leaves each thread.)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c < nchunk) {
+          const uint32_t base = prow + (uint32_t)(c >> 1) * 16384u;
+          if (c >= c0 && c < c1) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {  // 16-byte granule g of the chunk's 64 bytes
+              uint32_t w[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int k = 8 * g + 2 * q;
+                float a, b;
+                f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[c][k]), __uint_as_float(sv[c][k + 1])),
+                                 sl2, nms2),
+                          a, b);
+                w[q] = ex2_h2(a, b);
+              }
+              st_shared_v4(base + (uint32_t)((((c & 1) * 4 + g) ^ swz) << 4), w[0], w[1], w[2], w[3]);
+            }
+          } else {
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              st_shared_v4(base + (uint32_t)((((c & 1) * 4 + g) ^ swz) << 4), 0u, 0u, 0u, 0u);
+          }
+        }
+      }
+      if (i > 0) {
         if (j == 0) {
           store_head(head_of(u - ustep));
         } else if (__any_sync(0xffffffffu, alpha != 1.f)) {
@@ -494,37 +528,6 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld_wait();
           tmem_st1(lrow, __float_as_uint(l * alpha));
           tmem_st_wait();
-        }
-      }
-      // P(u) = 2^(s·c − m·c) in f16 → this group's 128-byte-swizzled K-major
-      // tile (keys 0-63 | 64-127); chunks no row of the warp needs are zero.
-      // (Forming P before the wait above would hide P·V(u − 1) behind the
-      // exponentials, but S and P together need more than the 168 registers
-      // a 10-warp CTA leaves each thread.)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (c < nchunk) {
-          const uint32_t base = prow + (uint32_t)(c >> 1) * 16384u;
-          if (c >= c0 && c < c1) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint32_t w[4];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int k = 8 * i + 2 * q;
-                float a, b;
-                f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[c][k]), __uint_as_float(sv[c][k + 1])),
-                                 sl2, nms2),
-                          a, b);
-                w[q] = ex2_h2(a, b);
-              }
-              st_shared_v4(base + (uint32_t)((((c & 1) * 4 + i) ^ swz) << 4), w[0], w[1], w[2], w[3]);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              st_shared_v4(base + (uint32_t)((((c & 1) * 4 + i) ^ swz) << 4), 0u, 0u, 0u, 0u);
-          }
         }
       }
       fence_proxy_async_smem();
