@@ -451,8 +451,8 @@ __global__ void __launch_bounds__(320, 1)
         for (int cc = 0; cc < 4; ++cc)
           if (cc == c) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (32 * cc + i >= nkeys) sv[cc][i] = __float_as_uint(-INFINITY);
+            for (int x = 0; x < 32; ++x)
+              if (32 * cc + x >= nkeys) sv[cc][x] = __float_as_uint(-INFINITY);
           }
       }
       float mx = -INFINITY;
@@ -460,8 +460,8 @@ __global__ void __launch_bounds__(320, 1)
       for (int c = 0; c < 4; ++c)
         if (c >= c0 && c < c1) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 2)
-            mx = fmax3(mx, __uint_as_float(sv[c][i]), __uint_as_float(sv[c][i + 1]));
+          for (int x = 0; x < 32; x += 2)
+            mx = fmax3(mx, __uint_as_float(sv[c][x]), __uint_as_float(sv[c][x + 1]));
         }
       const float m_new = fmaxf(m_run, mx);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;  // rows without keys: P = 0
