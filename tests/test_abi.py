@@ -97,3 +97,17 @@ def test_kernel_seams_accept_empty_shapes():
     _lib.call("futon_cuda_matmul_t", 0, None, None, None, 0, 4, 8, None, None)
     _lib.call("futon_cuda_matmul_t_q8", 0, None, None, None, None, 0, 4, 16, None, None)
     _lib.call("futon_cuda_quantize_rows_q8", 0, None, None, None, 0, 16, None)
+
+
+def test_runtime_options_documented():
+    """Every environment variable the library reads is in INTEGRATION.md's
+    runtime-option table, and every documented value is one it accepts."""
+    src = (ROOT / "futon_b200" / "csrc" / "futon_cuda.cu").read_text()
+    doc = (ROOT / "INTEGRATION.md").read_text()
+    names = set(re.findall(r'getenv\("(FUTON_\w+)"\)', src))
+    assert names, "no environment options found"
+    for n in names:
+        assert f"`{n}=" in doc, f"{n} is read by the library but not documented"
+    for n, v in re.findall(r"`(FUTON_CUDA_\w+)=(\w+)`", doc):
+        assert n in names, f"{n} is documented but not read"
+        assert f'"{v}"' in src, f"{n}={v} is documented but not accepted"
