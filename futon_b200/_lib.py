@@ -26,7 +26,16 @@ EXPORTED = (
     "futon_cuda_matmul_t_q8", "futon_cuda_quantize_rows_q8", "futon_cuda_profile",
     "futon_cuda_profile_read", "futon_cuda_profile_stage_count", "futon_cuda_profile_stage_name",
     "futon_cuda_matmul_t_q8_noalloc", "futon_cuda_selftest_wait_timeout", "futon_cuda_io_bytes",
+    "futon_cuda_debug_cancel_after",
 )
+
+# Environment options the library reads when a model is created, with the
+# values it accepts (any other value leaves the default, listed first).
+RUNTIME_OPTIONS = {
+    "FUTON_CUDA_ATTN": ("heads", "tc", "tc2"),
+    "FUTON_CUDA_ATTN_SPLIT": ("0", "1"),
+    "FUTON_CUDA_Q8_ATTN": ("split", "exact"),
+}
 
 
 class FutonLibraryError(RuntimeError):
@@ -123,6 +132,8 @@ def lib() -> C.CDLL:
         L.futon_cuda_quantize_rows_q8.argtypes = [ip, vp, vp, vp, ip, ip, vp, cp, sz]
         L.futon_cuda_selftest_wait_timeout.restype = ip
         L.futon_cuda_selftest_wait_timeout.argtypes = [ip, cp, sz]
+        L.futon_cuda_debug_cancel_after.restype = None
+        L.futon_cuda_debug_cancel_after.argtypes = [C.c_longlong]
         _lib = L
         return L
 

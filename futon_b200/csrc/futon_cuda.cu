@@ -327,6 +327,22 @@ namespace {
 
 constexpr int kTokenBudget = 131072;  // tokens per micro-batch
 
+// Cancellation checkpoint: entry, every micro-batch, every layer and every
+// layer's FFN (the points where native/model.go checks ctx.Err()). The
+// countdown, armed per host thread by futon_cuda_debug_cancel_after, makes
+// the checkpoint that follows `n` passed ones report cancellation, as the
+// reference's tests do with a context canceled after N Err() checks.
+thread_local long long t_cancel_after = -1;
+
+bool canceled(volatile const int* cancel) {
+  if (t_cancel_after == 0) {
+    t_cancel_after = -1;
+    return true;
+  }
+  if (t_cancel_after > 0) --t_cancel_after;
+  return cancel && *cancel;
+}
+
 // Profiler stages (futon_cuda_profile_read's `stage` argument).
 enum Stage : int {
   kStEmbed = 0, kStGemmQkv, kStAttn, kStAttnCls, kStGather, kStQuant, kStGemmOut, kStLayerNorm,
@@ -966,7 +982,7 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
   }
 
   for (int li = 0; li < c.num_layers; ++li) {
-    if (cancel && *cancel)
+    if (canceled(cancel))
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
     const LayerDev& L = d.layers[li];
     const bool last = li == c.num_layers - 1;
@@ -1078,7 +1094,7 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
     }
     if ((rc = resid_ln(kStGemmOut, a_out, a_out_s, L.out, resid, L.n1w, L.n1b, false))) return rc;
 
-    if (cancel && *cancel)
+    if (canceled(cancel))
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
 
     // FFN
@@ -1325,7 +1341,7 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
   const int dim = out_dim ? out_dim : m.cfg.hidden_size;
   for (size_t i = 0; i < mbs.size(); ++i) {
     const MicroBatch& mb = mbs[i];
-    if (cancel && *cancel)
+    if (canceled(cancel))
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
     AttnPlan plan{reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
                   reinterpret_cast<const AttnWindow*>(d.d_meta + mb.win_off), mb.nwin,
@@ -1462,9 +1478,12 @@ int seam_finish(SeamCtx& s, cudaStream_t st, char* err, size_t errlen) {
   return FUTON_OK;
 }
 
-int seam_gemm(SeamCtx& s, const void* A, bool s8, const float* a_scale, int m, const void* W,
-              const float* w_scale, int n, int k, const float* bias, float* dst, cudaStream_t st,
-              char* err, size_t errlen) {
+// The kernel seam's GEMM launch (f32 output, bias, optional int8 rescale),
+// shared by the allocating seam calls and the no-allocation Q8 entry point:
+// err_word is the device error word the kernel's bounded waits report into.
+int seam_gemm(int* err_word, int num_sms, const void* A, bool s8, const float* a_scale, int m,
+              const void* W, const float* w_scale, int n, int k, const float* bias, float* dst,
+              cudaStream_t st, char* err, size_t errlen) {
   CUtensorMap ta, tw;
   const int bn = pick_bn(n);
   if (!make_operand_map(&ta, A, s8, (uint64_t)m, (uint64_t)k, 128) ||
@@ -1500,8 +1519,8 @@ int seam_gemm(SeamCtx& s, const void* A, bool s8, const float* a_scale, int m, c
   g.ep.cu = nullptr;
   g.ep.nseq = 0;
   g.ep.f16_from = 1 << 30;
-  g.err = s.err_word;
-  g.num_sms = s.num_sms;
+  g.err = err_word;
+  g.num_sms = num_sms;
   g.stream = st;
   cudaError_t e = s8 ? launch_gemm_s8(g) : launch_gemm_bf16(g);
   if (e != cudaSuccess)
@@ -1713,7 +1732,7 @@ int futon_cuda_encode(futon_model* model, int device, const int32_t* ids,
   int rc;
   if ((rc = validate_input(*model, cu_seqlens, nseq, out_dim, err, errlen))) return rc;
   if ((rc = check_ids(*model, ids, cu_seqlens, nseq, err, errlen))) return rc;
-  if (cancel && *cancel) return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
+  if (canceled(cancel)) return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
   return encode_host(model, *model->devs[device], ids, cu_seqlens, nseq, out_dim, out, cancel, err,
                      errlen);
 }
@@ -1727,7 +1746,7 @@ int futon_cuda_encode_batch(futon_model* model, const int32_t* ids, const int32_
   int rc;
   if ((rc = validate_input(*model, cu_seqlens, nseq, out_dim, err, errlen))) return rc;
   if ((rc = check_ids(*model, ids, cu_seqlens, nseq, err, errlen))) return rc;
-  if (cancel && *cancel) return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
+  if (canceled(cancel)) return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
   const int ndev = (int)model->devs.size();
   const int dim = out_dim ? out_dim : model->cfg.hidden_size;
   if (nseq == 0) return FUTON_OK;
@@ -1866,7 +1885,9 @@ int futon_cuda_matmul_t(int cuda_device, float* dst, const float* a, const float
   f32_to_bf16_kernel<<<1024, 256, 0, st>>>(a, (size_t)m * k, ab);
   f32_to_bf16_kernel<<<1024, 256, 0, st>>>(b, (size_t)n * k, bb);
   CU_TRY(cudaGetLastError());
-  if ((rc = seam_gemm(*s, ab, false, nullptr, m, bb, nullptr, n, k, bias, dst, st, err, errlen))) return rc;
+  if ((rc = seam_gemm(s->err_word, s->num_sms, ab, false, nullptr, m, bb, nullptr, n, k, bias, dst,
+                      st, err, errlen)))
+    return rc;
   return seam_finish(*s, st, err, errlen);
 }
 
@@ -1887,7 +1908,9 @@ int futon_cuda_matmul_t_q8(int cuda_device, float* dst, const float* a, const in
   float* sa = (float*)((uint8_t*)s->scratch + qbytes);
   quant_rows_kernel<<<grid_rows(m, 8, s->num_sms), 256, 0, st>>>(a, m, k, qa, sa);
   CU_TRY(cudaGetLastError());
-  if ((rc = seam_gemm(*s, qa, true, sa, m, qb, scales, n, k, bias, dst, st, err, errlen))) return rc;
+  if ((rc = seam_gemm(s->err_word, s->num_sms, qa, true, sa, m, qb, scales, n, k, bias, dst, st,
+                      err, errlen)))
+    return rc;
   return seam_finish(*s, st, err, errlen);
 }
 
@@ -1920,6 +1943,14 @@ int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, con
 // their scales go to a fixed array in this library's device image instead of
 // allocated scratch. The array (kNoAllocScratchBytes) is resident on every
 // GPU that loads the library, until the process exits.
+//
+// The array is part of this file's device code, which the CUDA runtime loads
+// onto a device lazily (CUDA_MODULE_LOADING=LAZY is the default): the first
+// call on a device, or any earlier call into the library that launches one of
+// this file's kernels there, loads it and so reserves the array and the code
+// in device memory. A caller that hands the free HBM to another allocator
+// therefore makes its first call before doing so; from then on the calls
+// allocate nothing.
 // ===========================================================================
 namespace {
 
@@ -1969,7 +2000,7 @@ extern "C" int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const
   if (need > kNoAllocScratchBytes)
     return set_err(err, errlen, FUTON_EINVAL,
                    "native: q8 no-alloc scratch needs %zu bytes for m=%d k=%d; the fixed "
-                   "scratch holds %zu (m·k + 4·m, rounded)", need, m, k, kNoAllocScratchBytes);
+                   "scratch holds %zu (m·k rounded up to 256, plus 4·m)", need, m, k, kNoAllocScratchBytes);
   if (m == 0) return FUTON_OK;
   if (!dst || !a || !qb || !scales) return set_err(err, errlen, FUTON_EINVAL, "native: null buffer");
   CU_TRY(cudaSetDevice(cuda_device));
@@ -1982,47 +2013,9 @@ extern "C" int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const
   CU_TRY(cudaMemsetAsync(s->err, 0, sizeof(int), st));
   quant_rows_kernel<<<grid_rows(m, 8, s->num_sms), 256, 0, st>>>(a, m, k, qa, sa);
   CU_TRY(cudaGetLastError());
-  CUtensorMap ta, tw;
-  const int bn = pick_bn(n);
-  if (!make_operand_map(&ta, qa, true, (uint64_t)m, (uint64_t)k, 128) ||
-      !make_operand_map(&tw, qb, true, (uint64_t)n, (uint64_t)k, (uint32_t)bn))
-    return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed");
-  GemmLaunch g;
-  g.ta = &ta;
-  g.tw = &tw;
-  g.to = nullptr;
-  g.tr = nullptr;
-  g.M = m;
-  g.N = n;
-  g.K = k;
-  g.bn = bn;
-  g.epi = kEpiStore;
-  g.out_f32 = true;
-  g.ep.out = dst;
-  g.ep.ldo = n;
-  g.ep.bias = bias;
-  g.ep.resid = nullptr;
-  g.ep.ldr = 0;
-  g.ep.resid_bf16 = 0;
-  g.ep.a_scale = sa;
-  g.ep.w_scale = scales;
-  g.ep.ln_w = nullptr;
-  g.ep.ln_b = nullptr;
-  g.ep.eps = 0.f;
-  g.ep.out_f32 = nullptr;
-  g.ep.rope_cos = nullptr;
-  g.ep.rope_sin = nullptr;
-  g.ep.rope_hd = 0;
-  g.ep.rope_cols = 0;
-  g.ep.cu = nullptr;
-  g.ep.nseq = 0;
-  g.ep.f16_from = 1 << 30;
-  g.err = s->err;
-  g.num_sms = s->num_sms;
-  g.stream = st;
-  cudaError_t e = launch_gemm_s8(g);
-  if (e != cudaSuccess)
-    return set_err(err, errlen, FUTON_ECUDA, "native: gemm launch: %s", cudaGetErrorString(e));
+  if ((rc = seam_gemm(s->err, s->num_sms, qa, true, sa, m, qb, scales, n, k, bias, dst, st, err,
+                      errlen)))
+    return rc;
   CU_TRY(cudaStreamSynchronize(st));
   int code = 0;
   CU_TRY(cudaMemcpy(&code, s->err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -2045,6 +2038,10 @@ __global__ void selftest_wait_kernel(int* err) {
   if (threadIdx.x == 0) mbar_wait_bounded(smem_u32(&bar), 0u, err, kDevTimeoutSelfTest, &abort_flag);
 }
 }  // namespace
+
+extern "C" void futon_cuda_debug_cancel_after(long long polls) {
+  t_cancel_after = polls < 0 ? -1 : polls;
+}
 
 extern "C" int futon_cuda_selftest_wait_timeout(int cuda_device, char* err, size_t errlen) {
   SeamCtx* s = nullptr;

@@ -183,16 +183,30 @@ int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, con
  * outputs and bit-exact results as futon_cuda_matmul_t_q8, but the quantised
  * activations and scales go to a fixed 4 MiB array in the library's device
  * image (resident on every GPU that loads the library until exit), so
- * m·k + 4·m bytes (each part rounded up to 256) must fit in 4 MiB; larger
- * shapes are rejected with FUTON_EINVAL. The first call on a device resolves
- * that array's device address; make it before any stream capture. The call
- * allocates nothing, zeroes its device error word, and waits for its stream.
+ * align_up(m·k, 256) + 4·m bytes must fit in 4 MiB; larger shapes are
+ * rejected with FUTON_EINVAL. The first call on a device resolves that
+ * array's device address; make it before any stream capture. That first
+ * call (or any earlier library call that launches a kernel on the device)
+ * also loads the library's device code there, which is when the array and
+ * the code take their device memory (CUDA loads modules lazily by default):
+ * make it before another allocator takes the free HBM. After it, calls
+ * allocate nothing; each zeroes its device error word and waits for its
+ * stream.
  * All calls on a device share the one array: calls whose GPU work overlaps
  * (other host threads, other streams) race and must be serialised by the
  * caller. */
 int futon_cuda_matmul_t_q8_noalloc(int cuda_device, float* dst, const float* a, const int8_t* qb,
                                    const float* scales, int m, int n, int k, const float* bias,
                                    void* stream, char* err, size_t errlen);
+
+/* Cancellation test hook, the library-side form of the reference's
+ * cancelAfterN test context (native/model_test.go:203-244): the next
+ * futon_cuda_encode / futon_cuda_encode_device call made from this host
+ * thread passes `polls` cancellation checkpoints (the entry check, then one
+ * per micro-batch, one before each layer and one before each layer's FFN)
+ * and reports FUTON_ECANCELED at the next, as if *cancel had been raised
+ * there. The countdown then disarms; polls < 0 disarms it at once. */
+void futon_cuda_debug_cancel_after(long long polls);
 
 /* Failure-detection self-test (no counterpart in the reference): launches
  * one CTA that waits, through the same bounded-wait routine every pipeline

@@ -99,15 +99,14 @@ def test_kernel_seams_accept_empty_shapes():
     _lib.call("futon_cuda_quantize_rows_q8", 0, None, None, None, 0, 16, None)
 
 
-def test_runtime_options_documented():
-    """Every environment variable the library reads is in INTEGRATION.md's
-    runtime-option table, and every documented value is one it accepts."""
+def test_runtime_options_match_library():
+    """Every environment variable the library reads is in the package's
+    RUNTIME_OPTIONS table, and every non-default value listed there is one
+    the library compares against."""
     src = (ROOT / "futon_b200" / "csrc" / "futon_cuda.cu").read_text()
-    doc = (ROOT / "INTEGRATION.md").read_text()
     names = set(re.findall(r'getenv\("(FUTON_\w+)"\)', src))
     assert names, "no environment options found"
-    for n in names:
-        assert f"`{n}=" in doc, f"{n} is read by the library but not documented"
-    for n, v in re.findall(r"`(FUTON_CUDA_\w+)=(\w+)`", doc):
-        assert n in names, f"{n} is documented but not read"
-        assert f'"{v}"' in src, f"{n}={v} is documented but not accepted"
+    assert names == set(_lib.RUNTIME_OPTIONS), names ^ set(_lib.RUNTIME_OPTIONS)
+    for n, values in _lib.RUNTIME_OPTIONS.items():
+        for v in values[1:]:
+            assert f'"{v}"' in src, f"{n}={v} is listed but not accepted"

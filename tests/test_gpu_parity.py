@@ -127,22 +127,28 @@ def test_head_dim32_head_counts_vs_oracle(gpu, heads):
     assert_parity(got, want, f"hd32 × {heads} heads")
 
 
-def test_c1_subset_vs_oracle(gpu):
+def test_c1_full_vs_oracle(gpu):
+    """c1 at full size: all 256 MiniLM-6 sequences of 128 tokens (mean
+    pooling) against the oracle on every host core."""
     cfg, w, m = synth_model("minilm6")
-    ids, cu = synth.make_inputs("c1", nseq=32)
+    ids, cu = synth.make_inputs("c1")
+    assert len(cu) - 1 == 256 and ids.size == 256 * 128
     got = m.encode_packed(ids, cu)
     want = OracleModel(cfg, w, gemm=oracle_mode()).encode_batch(ids, cu)
-    assert_parity(got, want, "c1")
+    assert_parity(got, want, "c1-full")
 
 
 @pytest.mark.parametrize("dim", [768, 256, 64])
-def test_c2_subset_vs_oracle(gpu, dim):
+def test_c2_full_vs_oracle(gpu, dim):
+    """c2 at full size: all 64 nomic-shaped sequences (lengths U[64, 512],
+    RoPE, SwiGLU, mean pooling) at each matryoshka width."""
     cfg, w, m = synth_model("nomic")
-    ids, cu = synth.make_inputs("c2", nseq=6)
+    ids, cu = synth.make_inputs("c2")
+    assert len(cu) - 1 == 64
     got = m.encode_packed(ids, cu, out_dim=dim)
-    assert got.shape == (6, dim)
+    assert got.shape == (64, dim)
     want = OracleModel(cfg, w, gemm=oracle_mode()).encode_batch(ids, cu, out_dim=dim)
-    assert_parity(got, want, f"c2/{dim}")
+    assert_parity(got, want, f"c2-full/{dim}")
 
 
 # Q8 path gates. The reference's Q8 forward amplifies float32-rounding-level
@@ -345,6 +351,41 @@ def test_cancellation(gpu):
     # The model stays usable after a canceled call.
     out = m.encode_packed(ids, cu)
     assert np.abs(np.linalg.norm(out, axis=1) - 1).max() <= NORM_TOL
+
+
+def test_cancellation_at_every_checkpoint(gpu):
+    """Cancellation at each checkpoint of a two-micro-batch call, like the
+    reference's cancelAfterN context (model_test.go:203-244): the call
+    returns the cancel error, writes no vector, and the next call is
+    bit-identical to a clean run."""
+    from futon_b200 import _lib, pack_ids
+    cfg = synth.arch("bge")
+    cfg.num_layers = 2
+    w = synth.make_weights(cfg)
+    m = Model(cfg, w, devices=[0])
+    seqs = [np.full(128, 1000 + i % 7, np.int32) for i in range(1100)]  # 140,800 tokens
+    ids, cu = pack_ids(seqs)
+    clean = m.encode_packed(ids, cu)
+    # Checkpoints: the entry check, then per micro-batch (two of ≤ 131,072
+    # tokens) one before it, and one before each layer and each layer's FFN.
+    checkpoints = 1 + 2 * (1 + 2 * cfg.num_layers)
+    lib = _lib.lib()
+    try:
+        for k in range(checkpoints):
+            out = np.full((len(seqs), cfg.hidden_size), np.nan, np.float32)
+            lib.futon_cuda_debug_cancel_after(k)
+            with m._call() as h, pytest.raises(CanceledError):
+                _lib.call("futon_cuda_encode", h, 0, ids.ctypes.data, cu.ctypes.data, len(seqs), 0,
+                          out.ctypes.data, None)
+            assert np.isnan(out).all(), f"checkpoint {k}: a partial vector was written"
+            again = m.encode_packed(ids, cu)
+            assert np.array_equal(again, clean), f"checkpoint {k}: the next call differs"
+        # With as many passes as checkpoints the call completes.
+        lib.futon_cuda_debug_cancel_after(checkpoints)
+        assert np.array_equal(m.encode_packed(ids, cu), clean)
+    finally:
+        lib.futon_cuda_debug_cancel_after(-1)
+        m.close()
 
 
 def test_trained_context_clamp(gpu):
