@@ -1,17 +1,21 @@
 #!/usr/bin/env python3
 """Benchmark: embeddings/s of the bge-small-shaped encoder on the c4 workload.
 
-A step is one forward over one c4 batch per GPU: 65,536 sequences with
-log-normal lengths (median 64, sigma 0.8, clipped to [8, 512]), CLS pooled,
+A step is one forward over THE c4 batch: 65,536 sequences with log-normal
+lengths (median 64, sigma 0.8, clipped to [8, 512]), CLS pooled,
 L2-normalised 384-d vectors, random-init weights (synthetic data of the
-benchmark's shape; see futon_b200/synth.py). Each rank encodes its own batch
-(weak scaling, no collective on the data path; NCCL is used only for the
-barrier and the max-over-ranks of the timings).
+benchmark's shape; see futon_b200/synth.py). With N GPUs (one process per
+GPU) the one batch is split into N contiguous cost-balanced shards, one per
+rank (strong scaling, futon_b200/shard.py); there is no collective on the data
+path — NCCL carries only barriers and the max-over-ranks of the timings.
 
   value  whole-job embeddings/s with ids already in HBM (device-resident
          entry point), timed with CUDA events on the launch stream, max over ranks
-  e2e    the same through the host-buffer C ABI (futon_cuda_encode): ids
-         copied host→device and vectors device→host inside the timed region
+  e2e    the same through the host-buffer C ABI (futon_cuda_encode): each rank
+         copies its shard's ids host→device and writes its vectors
+         device→host straight into one index-aligned host buffer shared by
+         all ranks (/dev/shm); a step ends when the last rank's vectors are
+         in it (barrier)
   roofline  the dominant kernel's achieved TFLOP/s (its algorithmic FLOPs per
          launch ÷ its CUDA-event-timed average launch duration, from the
          library's per-stage profiler over a second timed pass)
@@ -23,6 +27,10 @@ barrier and the max-over-ranks of the timings).
          L ~ U[8, 128]) through the host-buffer C ABI, wall clock per call
   nomic  the metric's second model: the nomic-bert-shaped encoder on 1,024
          sequences per GPU with c2's lengths (U[64, 512]), ids in HBM
+  c1, c3, c3_q8  the other benchmark configurations per GPU, ids in HBM:
+         MiniLM-6 on 256 × 128 tokens; the arctic-shaped long-context encoder
+         on 16 × 2048 tokens with bf16 tensor-core GEMMs, and with the int8
+         weight path (int8 tensor-core GEMMs, exact-order attention)
 
 `--impl reference` times that CPU port alone (the reference is Go and has no
 GPU path; it cannot be built on this image) and prints its own line.
@@ -154,10 +162,12 @@ def run_reference(args, rank, world):
     line = {
         "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": cb["ms_per_sample"], "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": cb["ms_per_sample"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "model": "bge-small-shaped (12 layers, hidden 384)",
-                   "sample_seqs": CPU_SAMPLE_SEQS, "parallelism": "host threads"},
+        "config": {"workload": WORKLOAD, "model": "bge-small-shaped (12 layers, hidden 384, "
+                   "12 heads, FFN 1536, GELU, CLS)", "global_batch": 65536,
+                   "sample_seqs": CPU_SAMPLE_SEQS,
+                   "parallelism": "host threads (a bounded sample of the c4 batch per step)"},
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -194,10 +204,12 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="futon_b200", choices=["futon_b200", "reference"])
-    ap.add_argument("--nseq", type=int, default=None, help="override sequences per rank")
+    ap.add_argument("--nseq", type=int, default=None, help="override the c4 batch size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--nomic-nseq", type=int, default=1024,
                     help="sequences per rank of the nomic-shaped throughput run (0 = skip)")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the c1 / c3 / c3-int8 per-GPU throughput keys")
     args = ap.parse_args()
     route_stdout_to_stderr()
 
@@ -209,6 +221,7 @@ def main():
     import torch
     import torch.distributed as dist
     from futon_b200 import Model, synth
+    from futon_b200.shard import SharedRows, shard_for_rank
 
     torch.cuda.set_device(local)
     if world > 1:
@@ -221,20 +234,29 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
+    def reduce(x: float, op) -> float:
         if world == 1:
             return x
         t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=op)
         return float(t.item())
+
+    def max_over_ranks(x: float) -> float:
+        return reduce(x, dist.ReduceOp.MAX if world > 1 else None)
+
+    def sum_over_ranks(x: float) -> float:
+        return reduce(x, dist.ReduceOp.SUM if world > 1 else None)
 
     cfg = synth.arch("bge")
     weights = synth.make_weights(cfg)
     model = Model(cfg, weights, devices=[local], q8=False)
-    ids, cu = synth.make_inputs(WORKLOAD, seed=1 + rank, nseq=args.nseq)
-    nseq, ntok = len(cu) - 1, int(cu[-1])
-    flops = synth.total_flops(cfg, cu)
     dim = cfg.hidden_size
+    # The one c4 batch (same seed on every rank) and this rank's shard of it.
+    ids_all, cu_all = synth.make_inputs(WORKLOAD, seed=1, nseq=args.nseq)
+    nseq_all, ntok_all = len(cu_all) - 1, int(cu_all[-1])
+    flops_all = synth.total_flops(cfg, cu_all)
+    ids, cu, s0, s1 = shard_for_rank(ids_all, cu_all, rank, world, hidden=dim)
+    nseq = len(cu) - 1
 
     # A dedicated stream: the library queues its kernels on the stream handle it
     # is given, and the legacy default stream's handle (0) means "library stream".
@@ -264,12 +286,12 @@ def main():
     e1.synchronize()
     model.sync(stream=sh)
     barrier()
-    launches = model.launch_count() - l0
+    launches = int(sum_over_ranks(float(model.launch_count() - l0)))
     clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
     norms = torch.linalg.vector_norm(d_out, dim=1)
     assert float((norms - 1).abs().max()) < 1e-4, "outputs are not unit-norm"
-    value = world * nseq / (ms / 1e3)
+    value = nseq_all / (ms / 1e3)
 
     # ---- roofline: second pass with the per-stage profiler on ----
     model.profile(True)
@@ -321,50 +343,85 @@ def main():
                      "tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1) if v["flops"] else None,
                      "gbs": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1)}
                  for k, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])}
+    del d_ids, d_out
 
-    # ---- e2e: host buffers through the C ABI ----
+    # ---- e2e: host buffers through the C ABI into one shared result ----
+    rows = SharedRows(nseq_all, dim)
+    mine = rows.array[s0:s1]
     for _ in range(max(1, args.warmup)):
-        model.encode_packed(ids, cu)
+        model.encode_packed(ids, cu, out=mine)
     barrier()
     io0 = model.io_bytes()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        out = model.encode_packed(ids, cu)
+        model.encode_packed(ids, cu, out=mine)
+        rows.barrier()  # the step ends with the last rank's vectors in the buffer
     t1 = time.perf_counter()
     io1 = model.io_bytes()
     barrier()
     e2e_ms = max_over_ranks((t1 - t0) * 1e3) / args.steps
-    assert np.abs(np.linalg.norm(out, axis=1) - 1).max() < 1e-4
-    # Bytes the library copied per call (ids and micro-batch metadata in;
-    # vectors and the device error word out), counted by the library.
-    h2d = (io1[0] - io0[0]) // args.steps
-    d2h = (io1[1] - io0[1]) // args.steps
+    full = np.asarray(rows.array)
+    assert np.abs(np.linalg.norm(full, axis=1) - 1).max() < 1e-4, "a shard's vectors are missing"
+    del full
+    rows.close()
+    # Bytes the library copied per step on all ranks (ids and micro-batch
+    # metadata in; vectors and the device error words out), counted by the
+    # library.
+    h2d = sum_over_ranks(float(io1[0] - io0[0])) / args.steps
+    d2h = sum_over_ranks(float(io1[1] - io0[1])) / args.steps
+
+    def per_gpu_run(key, arch, q8=False, nseq_=None, seed=11, out_dim=0, label=None):
+        """Throughput of one configuration per GPU (ids in HBM, CUDA events),
+        max over ranks. Every rank takes the same collective steps whatever
+        happens: a failure is reported in the key."""
+        ms_, info = float("nan"), None
+        try:
+            acfg = synth.arch(arch)
+            m = model if (arch == "bge" and not q8) else \
+                Model(acfg, synth.make_weights(acfg), devices=[local], q8=q8)
+            xi, xc = synth.make_inputs(key, seed=seed + rank, nseq=nseq_)
+            di = torch.from_numpy(xi).cuda()
+            width = out_dim or acfg.hidden_size
+            do = torch.empty((len(xc) - 1, width), dtype=torch.float32, device="cuda")
+            for _ in range(args.warmup):
+                m.encode_device(di.data_ptr(), xc, out_dim, do.data_ptr(), stream=sh)
+            m.sync(stream=sh)
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for _ in range(args.steps):
+                m.encode_device(di.data_ptr(), xc, out_dim, do.data_ptr(), stream=sh)
+            a1.record(stream)
+            a1.synchronize()
+            m.sync(stream=sh)
+            ms_ = a0.elapsed_time(a1) / args.steps
+            nn = torch.linalg.vector_norm(do, dim=1)
+            if float((nn - 1).abs().max()) >= 1e-4:
+                raise RuntimeError("outputs are not unit-norm")
+            info = {"seqs": len(xc) - 1, "tokens": int(xc[-1]),
+                    "flops": synth.total_flops(acfg, xc)}
+            del di, do
+            if m is not model:
+                m.close()
+        except Exception as e:  # noqa: BLE001 - reported in the JSON line
+            ms_, info = float("nan"), {"error": repr(e)[:300]}
+        if world > 1:
+            barrier()
+            ms_ = max_over_ranks(ms_)
+        if info is None or "error" in info or ms_ != ms_:
+            return info if info and "error" in info else {"error": "a rank failed"}
+        xtf = info["flops"] / (ms_ / 1e3) / 1e12
+        return {"model": label or arch, "seqs_per_gpu": info["seqs"],
+                "tokens_per_gpu": info["tokens"], "ms_per_step": round(ms_, 3),
+                "embeddings_per_sec": round(world * info["seqs"] / (ms_ / 1e3), 1),
+                "tokens_per_sec": round(world * info["tokens"] / (ms_ / 1e3), 1),
+                "tflops_per_gpu": round(xtf, 1),
+                "frac_of_bf16_peak": round(xtf / peaks["bf16_tflops"], 4)}
 
     # ---- the target shape: bge at sequence length 128 ----
-    ids128, cu128 = synth.make_inputs("bge-seq128", seed=11 + rank)
-    n128 = len(cu128) - 1
-    flops128 = synth.total_flops(cfg, cu128)
-    d_ids128 = torch.from_numpy(ids128).cuda()
-    d_out128 = torch.empty((n128, dim), dtype=torch.float32, device="cuda")
-    for _ in range(args.warmup):
-        model.encode_device(d_ids128.data_ptr(), cu128, 0, d_out128.data_ptr(), stream=sh)
-    barrier()
-    q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    q0.record(stream)
-    for _ in range(args.steps):
-        model.encode_device(d_ids128.data_ptr(), cu128, 0, d_out128.data_ptr(), stream=sh)
-    q1.record(stream)
-    q1.synchronize()
-    barrier()
-    ms128 = max_over_ranks(q0.elapsed_time(q1)) / args.steps
-    tf128 = flops128 / (ms128 / 1e3) / 1e12
-    seq128 = {"seqs_per_rank": n128, "seq_len": 128, "ms_per_step": round(ms128, 3),
-              "embeddings_per_sec": round(world * n128 / (ms128 / 1e3), 1),
-              "tokens_per_sec": round(world * int(cu128[-1]) / (ms128 / 1e3), 1),
-              "tflops_per_gpu": round(tf128, 1),
-              "frac_of_bf16_peak": round(tf128 / peaks["bf16_tflops"], 4),
-              "frac_of_bf16_peak_sustained": round(tf128 / peak_tf, 4)}
-    del d_ids128, d_out128
+    seq128 = per_gpu_run("bge-seq128", "bge", seed=11,
+                         label="bge-small-shaped, 8,192 × 128 tokens per GPU")
+    if "tflops_per_gpu" in seq128:
+        seq128["frac_of_bf16_peak_sustained"] = round(seq128["tflops_per_gpu"] / peak_tf, 4)
 
     # ---- p50 latency of one c0 batch through the host-buffer ABI ----
     ids0, cu0 = synth.make_inputs("c0", seed=1 + rank)
@@ -379,55 +436,22 @@ def main():
     latency = {"config": "c0: 32 bge sequences, L ~ U[8, 128], host buffers", "repeats": 50,
                "p50_ms": round(p50, 3)}
 
-    # ---- nomic-bert-shaped encoder: c2 lengths (U[64, 512]), mean pooling ----
-    # Every rank takes the same collective steps whatever happens here: the
-    # timing is local, its max over ranks follows outside the try.
-    nomic_ms, nomic_info = float("nan"), None
-    if args.nomic_nseq > 0:
-        try:
-            ncfg = synth.arch("nomic")
-            nmodel = Model(ncfg, synth.make_weights(ncfg), devices=[local], q8=False)
-            nids, ncu = synth.make_inputs("c2", seed=21 + rank, nseq=args.nomic_nseq)
-            nflops = synth.total_flops(ncfg, ncu)
-            d_nids = torch.from_numpy(nids).cuda()
-            d_nout = torch.empty((len(ncu) - 1, ncfg.hidden_size), dtype=torch.float32,
-                                 device="cuda")
-            for _ in range(args.warmup):
-                nmodel.encode_device(d_nids.data_ptr(), ncu, 0, d_nout.data_ptr(), stream=sh)
-            nmodel.sync(stream=sh)
-            n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            n0.record(stream)
-            for _ in range(args.steps):
-                nmodel.encode_device(d_nids.data_ptr(), ncu, 0, d_nout.data_ptr(), stream=sh)
-            n1.record(stream)
-            n1.synchronize()
-            nmodel.sync(stream=sh)
-            nomic_ms = n0.elapsed_time(n1) / args.steps
-            nn = torch.linalg.vector_norm(d_nout, dim=1)
-            if float((nn - 1).abs().max()) >= 1e-4:
-                raise RuntimeError("nomic outputs are not unit-norm")
-            nomic_info = {"seqs": len(ncu) - 1, "tokens": int(ncu[-1]), "flops": nflops}
-            del d_nids, d_nout
-            nmodel.close()
-        except Exception as e:  # noqa: BLE001 - reported in the JSON line
-            nomic_ms, nomic_info = float("nan"), {"error": repr(e)[:300]}
-    if world > 1:  # single-GPU runs make no CUDA call outside the try
-        barrier()
-        nomic_ms = max_over_ranks(nomic_ms)
     nomic = None
-    if nomic_info is not None and "error" not in nomic_info and nomic_ms == nomic_ms:
-        ntf = nomic_info["flops"] / (nomic_ms / 1e3) / 1e12
-        nomic = {"model": "nomic-bert-shaped (12 layers, hidden 768, 12 heads, RoPE, SwiGLU 3072, "
-                          "mean pooling)",
-                 "workload": "c2 lengths U[64, 512], ids in HBM, CUDA events",
-                 "seqs_per_rank": nomic_info["seqs"], "tokens_per_rank": nomic_info["tokens"],
-                 "ms_per_step": round(nomic_ms, 3),
-                 "embeddings_per_sec": round(world * nomic_info["seqs"] / (nomic_ms / 1e3), 1),
-                 "tokens_per_sec": round(world * nomic_info["tokens"] / (nomic_ms / 1e3), 1),
-                 "tflops_per_gpu": round(ntf, 1),
-                 "frac_of_bf16_peak": round(ntf / peaks["bf16_tflops"], 4)}
-    elif nomic_info is not None:
-        nomic = nomic_info if "error" in nomic_info else {"error": "a rank failed"}
+    if args.nomic_nseq > 0:
+        nomic = per_gpu_run("c2", "nomic", nseq_=args.nomic_nseq, seed=21,
+                            label="nomic-bert-shaped (12 layers, hidden 768, RoPE, SwiGLU 3072, "
+                                  "mean pooling), c2 lengths U[64, 512]")
+    extra = {}
+    if not args.no_extra:
+        extra["c1"] = per_gpu_run("c1", "minilm6", seed=31,
+                                  label="MiniLM-L6-shaped, 256 × 128 tokens, mean pooling")
+        extra["c3"] = per_gpu_run("c3", "arctic", seed=41,
+                                  label="arctic-embed-m-long-shaped, 16 × 2048 tokens, "
+                                        "bf16 tensor-core GEMMs")
+        extra["c3_q8"] = per_gpu_run("c3", "arctic", q8=True, seed=41,
+                                     label="arctic-embed-m-long-shaped, 16 × 2048 tokens, int8 "
+                                           "weight path (int8 tensor-core GEMMs, exact-order "
+                                           "attention)")
 
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -438,20 +462,21 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init weights N(0,0.02), seeded c4 lengths and ids)",
             "config": {"workload": WORKLOAD, "model": "bge-small-shaped (12 layers, hidden 384, "
-                       "12 heads, FFN 1536, GELU, CLS)", "seqs_per_rank": nseq,
-                       "tokens_per_rank": ntok, "global_batch": nseq * world,
-                       "parallelism": f"dp{world}",
+                       "12 heads, FFN 1536, GELU, CLS)", "global_batch": nseq_all,
+                       "tokens": ntok_all, "seqs_on_rank0": nseq,
+                       "parallelism": f"dp{world} (contiguous cost-balanced shards of one batch)",
                        "l2": "working set > L2 (per micro-batch activations ~1.3 GB)",
                        "attention": {"kernel": os.environ.get("FUTON_CUDA_ATTN") or "heads",
-                                     "split": os.environ.get("FUTON_CUDA_ATTN_SPLIT") == "1"}},
-            "tokens_per_sec": round(world * ntok / (ms / 1e3), 1),
-            "tflops": round(world * flops / (ms / 1e3) / 1e12, 1),
-            "frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"], 4),
+                                     "split": os.environ.get("FUTON_CUDA_ATTN_SPLIT") != "0"}},
+            "tokens_per_sec": round(ntok_all / (ms / 1e3), 1),
+            "tflops": round(flops_all / (ms / 1e3) / 1e12, 1),
+            "frac_of_bf16_peak": round(flops_all / world / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                                       4),
             "gpu_launches": launches,
-            "e2e": {"value": round(world * nseq / (e2e_ms / 1e3), 1), "unit": UNIT,
+            "e2e": {"value": round(nseq_all / (e2e_ms / 1e3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "ms_per_step": round(e2e_ms, 3)},
             "roofline": {"kernel": top, "bound": bound, "achieved": round(achieved, 1),
@@ -464,6 +489,7 @@ def main():
             "stages": breakdown,
             "seq128": seq128,
             "nomic": nomic,
+            **extra,
             "p50_batch_latency": latency,
             "clocks": clk,
             "cpu_baseline": cb,

@@ -33,8 +33,8 @@ EXPORTED = (
 # values it accepts (any other value leaves the default, listed first).
 RUNTIME_OPTIONS = {
     "FUTON_CUDA_ATTN": ("heads", "tc", "tc2"),
-    "FUTON_CUDA_ATTN_SPLIT": ("0", "1"),
-    "FUTON_CUDA_Q8_ATTN": ("split", "exact"),
+    "FUTON_CUDA_ATTN_SPLIT": ("1", "0"),
+    "FUTON_CUDA_Q8_ATTN": ("exact", "split"),
 }
 
 

@@ -316,10 +316,10 @@ struct futon_model {
   int attn_kind = 0;
   // FUTON_CUDA_ATTN_SPLIT=1: attn_heads_kernel launches with the head groups
   // shared among grid.y CTAs when the tiles alone would leave SMs idle.
-  bool attn_split = false;
+  bool attn_split = true;
   // FUTON_CUDA_Q8_ATTN=exact: the int8 path's attention runs in the
   // reference's exact float32 operation order (attn_exact.cuh).
-  bool q8_exact_attn = false;
+  bool q8_exact_attn = true;
   std::vector<std::unique_ptr<DevCtx>> devs;
 };
 
@@ -763,8 +763,14 @@ void read_attn_env(futon_model& m) {
     else if (!strcmp(v, "tc2")) m.attn_kind = kAttnTc2;
     else if (!strcmp(v, "heads")) m.attn_kind = kAttnHeads;
   }
-  if (const char* v = std::getenv("FUTON_CUDA_ATTN_SPLIT")) m.attn_split = !strcmp(v, "1");
-  if (const char* v = std::getenv("FUTON_CUDA_Q8_ATTN")) m.q8_exact_attn = !strcmp(v, "exact");
+  if (const char* v = std::getenv("FUTON_CUDA_ATTN_SPLIT")) {
+    if (!strcmp(v, "0")) m.attn_split = false;
+    else if (!strcmp(v, "1")) m.attn_split = true;
+  }
+  if (const char* v = std::getenv("FUTON_CUDA_Q8_ATTN")) {
+    if (!strcmp(v, "split")) m.q8_exact_attn = false;
+    else if (!strcmp(v, "exact")) m.q8_exact_attn = true;
+  }
 }
 
 // CTAs per tile (grid.y) for attn_heads_kernel's head-group split: enough to

@@ -187,12 +187,21 @@ class Model:
 
     # -- forward ----------------------------------------------------------
     def encode_packed(self, ids: np.ndarray, cu_seqlens: np.ndarray, out_dim: int = 0,
-                      device: int = 0, cancel: Optional[CancelFlag] = None) -> np.ndarray:
-        """[nseq, dim] vectors for packed sequences on device index `device`."""
+                      device: int = 0, cancel: Optional[CancelFlag] = None,
+                      out: Optional[np.ndarray] = None) -> np.ndarray:
+        """[nseq, dim] vectors for packed sequences on device index `device`,
+        written to `out` when given (a C-contiguous float32 [nseq, dim] host
+        array, e.g. rows of a caller's index-aligned result buffer)."""
         ids = np.ascontiguousarray(ids, dtype=np.int32)
         cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
         nseq = len(cu) - 1
-        out = np.empty((max(nseq, 0), self.out_width(out_dim)), dtype=np.float32)
+        shape = (max(nseq, 0), self.out_width(out_dim))
+        if out is None:
+            out = np.empty(shape, dtype=np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise FutonError(_lib.FUTON_EINVAL,
+                             f"native: out must be C-contiguous float32 {shape}, got "
+                             f"{out.dtype} {out.shape}")
         with self._call() as h:
             _lib.call("futon_cuda_encode", h, device, ids.ctypes.data, cu.ctypes.data, nseq,
                       out_dim, out.ctypes.data, cancel.ptr if cancel else None)

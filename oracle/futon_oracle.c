@@ -223,11 +223,38 @@ float fo_quantize_row_q8(int8_t *dst, const float *src, int n) {
     return scale;
 }
 
+#if defined(__x86_64__)
+/* The exact int32 dot of two int8 rows with AVX2: products widened to int16
+ * pairs summed into int32 lanes (|q| <= 127, so a pair is at most 32,258
+ * and no lane can overflow for k < 2^17). Integer addition is associative,
+ * so the sum is the scalar loop's sum bit for bit, in any order. */
+__attribute__((target("avx2"))) static int32_t dot_q8_avx2(const int8_t *a, const int8_t *b, int k) {
+    __m256i acc = _mm256_setzero_si256();
+    int p = 0;
+    for (; p + 16 <= k; p += 16) {
+        __m256i va = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(a + p)));
+        __m256i vb = _mm256_cvtepi8_epi16(_mm_loadu_si128((const __m128i *)(b + p)));
+        acc = _mm256_add_epi32(acc, _mm256_madd_epi16(va, vb));
+    }
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(acc), _mm256_extracti128_si256(acc, 1));
+    s = _mm_hadd_epi32(s, s);
+    s = _mm_hadd_epi32(s, s);
+    int32_t sum = _mm_cvtsi128_si32(s);
+    for (; p < k; p++) sum += (int32_t)a[p] * (int32_t)b[p];
+    return sum;
+}
+#endif
+
 /* matMulTQ8 inner loop, quant.go:114-136, over already-quantised operands:
- * exact int32 dot, then float32(sum) * (sA * sB) + bias. */
-void fo_matmul_t_q8_prequant(float *dst, const int8_t *qa, const float *a_scale,
-                             const int8_t *qb, const float *b_scale, int m, int n, int k,
-                             const float *bias) {
+ * exact int32 dot, then float32(sum) * (sA * sB) + bias. The reference's
+ * loop is scalar (quant_amd64.go:5-8); fo_matmul_t_q8_prequant_scalar
+ * restates it, and fo_matmul_t_q8_prequant computes the same exact integer
+ * sums with AVX2 where the host has it (the CPU suite checks the two agree
+ * bit for bit), which makes full-length (2048-token) Q8 forwards practical
+ * as a parity check. */
+void fo_matmul_t_q8_prequant_scalar(float *dst, const int8_t *qa, const float *a_scale,
+                                    const int8_t *qb, const float *b_scale, int m, int n, int k,
+                                    const float *bias) {
     for (int i = 0; i < m; i++) {
         const int8_t *ai = qa + (size_t)i * k;
         float sA = a_scale[i];
@@ -240,6 +267,27 @@ void fo_matmul_t_q8_prequant(float *dst, const int8_t *qa, const float *a_scale,
             dst[(size_t)i * n + j] = s;
         }
     }
+}
+
+void fo_matmul_t_q8_prequant(float *dst, const int8_t *qa, const float *a_scale,
+                             const int8_t *qb, const float *b_scale, int m, int n, int k,
+                             const float *bias) {
+#if defined(__x86_64__)
+    if (fo_has_avx2()) {
+        for (int i = 0; i < m; i++) {
+            const int8_t *ai = qa + (size_t)i * k;
+            float sA = a_scale[i];
+            for (int j = 0; j < n; j++) {
+                int32_t sum = dot_q8_avx2(ai, qb + (size_t)j * k, k);
+                float s = (float)sum * (sA * b_scale[j]);
+                if (bias) s += bias[j];
+                dst[(size_t)i * n + j] = s;
+            }
+        }
+        return;
+    }
+#endif
+    fo_matmul_t_q8_prequant_scalar(dst, qa, a_scale, qb, b_scale, m, n, k, bias);
 }
 
 /* matMulTQ8, quant.go:99-137: dynamic per-row activation quantisation, then

@@ -110,6 +110,9 @@ float fo_quantize_row_q8(int8_t *dst, const float *src, int n);
 void fo_matmul_t_q8_prequant(float *dst, const int8_t *qa, const float *a_scale,
                              const int8_t *qb, const float *b_scale, int m, int n, int k,
                              const float *bias);
+void fo_matmul_t_q8_prequant_scalar(float *dst, const int8_t *qa, const float *a_scale,
+                                    const int8_t *qb, const float *b_scale, int m, int n, int k,
+                                    const float *bias);
 void fo_matmul_t_q8(float *dst, const float *a, const int8_t *qb, const float *scales,
                     int m, int n, int k, const float *bias);
 void fo_layernorm_rows(float *x, int rows, int h, const float *w, const float *b, float eps);

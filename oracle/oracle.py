@@ -76,6 +76,7 @@ def lib() -> C.CDLL:
         L.fo_quantize_row_q8.argtypes = [vp, vp, ip]
         L.fo_matmul_t_q8.argtypes = [vp, vp, vp, vp, ip, ip, ip, vp]
         L.fo_matmul_t_q8_prequant.argtypes = [vp, vp, vp, vp, vp, ip, ip, ip, vp]
+        L.fo_matmul_t_q8_prequant_scalar.argtypes = [vp, vp, vp, vp, vp, ip, ip, ip, vp]
         L.fo_layernorm_rows.argtypes = [vp, ip, ip, vp, vp, fp]
         L.fo_softmax_scaled.argtypes = [vp, ip, fp]
         for name in ("fo_exp", "fo_gelu", "fo_sigmoid"):

@@ -1,22 +1,21 @@
 """GPU checks of the opt-in attention variants, selected when a model is
-created by FUTON_CUDA_ATTN / FUTON_CUDA_ATTN_SPLIT.
+created by FUTON_CUDA_ATTN / FUTON_CUDA_Q8_ATTN.
 
 These run only on request (`FUTON_TEST_ATTN_VARIANTS=1 pytest -m
 gpu_variant`): the default configuration never reaches the variants, so the
 default `-m gpu` suite does not select them.
 
-- split: attn_heads_kernel with the head groups shared among grid.y CTAs.
-  Every head is computed by the same code in the same order as without the
-  split, so the vectors must be bitwise equal to the default kernel's.
 - tc, tc2: the tcgen05 attention kernels (tc2: separate q·k and v rings
   and two softmax warpgroups; head_dim 32 or 64 with an even head count);
   parity with the oracle (cosine gate) and batch invariance (a sequence's
   vector does not depend on what it is packed with).
-- FUTON_CUDA_Q8_ATTN=exact: the int8 path's attention in the reference's
-  exact float32 operation order (avx2Kernel MatMulT, softmaxScaled); its
-  arithmetic is checked bit for bit on the CPU by test_exact_host.py.
-  On the GPU the int8 forward must then sit within float32 noise of the
-  oracle's int8 forward (avx2Kernel order), far inside the 0.9999 gate.
+- FUTON_CUDA_Q8_ATTN=split: the int8 path's split-precision tensor-core
+  attention (bf16 hi + lo parts) instead of the default exact-order one.
+  Not bit-identical to the reference's float32 order, so the per-row
+  quantisations that follow amplify its float32-level differences: it is
+  held to the reference's own Q8 acceptance rule against the float path
+  (cos ≥ 0.999, native/quant.go:27-29) and to cos ≥ 0.9998 against the
+  oracle's Q8 forward.
 """
 from __future__ import annotations
 
@@ -68,15 +67,6 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("arch,inputs,nseq,layers", CASES)
-def test_split_bitwise_equals_default(gpu, monkeypatch, arch, inputs, nseq, layers):
-    cfg, w = weights(arch, layers)
-    ids, cu = synth.make_inputs(inputs, nseq=nseq, vocab=cfg.vocab_size)
-    base = encode(monkeypatch, {}, cfg, w, ids, cu)
-    split = encode(monkeypatch, {"FUTON_CUDA_ATTN_SPLIT": "1"}, cfg, w, ids, cu)
-    assert np.array_equal(base, split), f"{arch}: split attention differs from the default"
-
-
 @pytest.mark.parametrize("kernel", ["tc", "tc2"])
 @pytest.mark.parametrize("arch,inputs,nseq,layers", CASES)
 def test_tc_vs_oracle(gpu, monkeypatch, kernel, arch, inputs, nseq, layers):
@@ -104,16 +94,16 @@ def test_tc_batch_invariance(gpu, monkeypatch, kernel):
 @pytest.mark.parametrize("arch,inputs,nseq,layers", [
     ("arctic", "c3", 2, 3),   # RoPE, SwiGLU, CLS, head_dim 64, 2048 tokens
     ("bge", "c0", 16, None),  # absolute positions, GELU, CLS, head_dim 32
-    ("nomic", "c2", 4, 2),    # mean pooling: every layer attends over all rows
 ])
-def test_q8_exact_attention_vs_oracle(gpu, monkeypatch, arch, inputs, nseq, layers):
+def test_q8_split_attention_vs_oracle(gpu, monkeypatch, arch, inputs, nseq, layers):
     if not has_avx2():
         pytest.skip("the oracle's avx2Kernel order needs an AVX2 host")
     cfg, w = weights(arch, layers)
     ids, cu = synth.make_inputs(inputs, nseq=nseq, vocab=cfg.vocab_size)
-    got = encode(monkeypatch, {"FUTON_CUDA_Q8_ATTN": "exact"}, cfg, w, ids, cu, q8=True)
+    got = encode(monkeypatch, {"FUTON_CUDA_Q8_ATTN": "split"}, cfg, w, ids, cu, q8=True)
     want = OracleModel(cfg, w, q8=True, gemm=GEMM_AVX2).encode_batch(ids, cu)
-    cs = row_cosines(got, want)
-    same = int(np.sum(np.all(got == want, axis=1)))
-    print(f"[q8 exact] {arch}: min cos {cs.min():.9f}, {same}/{len(cs)} vectors bit-identical")
-    assert cs.min() >= 0.99999, f"{arch}: exact int8 attention min cosine {cs.min():.9f}"
+    flt = OracleModel(cfg, w, q8=False, gemm=GEMM_AVX2).encode_batch(ids, cu)
+    cs, cf = row_cosines(got, want), row_cosines(got, flt)
+    print(f"[q8 split] {arch}: min cos {cs.min():.9f} vs Q8 oracle, {cf.min():.9f} vs float")
+    assert cs.min() >= 0.9998, f"{arch}: split int8 attention min cosine {cs.min():.9f}"
+    assert cf.min() >= 0.999, f"{arch}: split int8 vs float min cosine {cf.min():.9f}"

@@ -180,6 +180,30 @@ def test_q8_matmul_exact(m, n, k):
     assert np.array_equal(got, want.astype(np.float32))
 
 
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (3, 5, 15), (4, 7, 16), (9, 33, 100), (64, 96, 768),
+                                   (17, 40, 3072)])
+def test_q8_prequant_avx2_equals_scalar(m, n, k):
+    """The oracle's AVX2 int8 dot gives the reference loop's exact sums: the
+    two prequantised GEMMs agree bit for bit, extremes (±127 everywhere,
+    the largest possible sums) included."""
+    rng = np.random.default_rng(m * 1000 + n + k)
+    qa = rng.integers(-127, 128, size=(m, k), dtype=np.int64).astype(np.int8)
+    qb = rng.integers(-127, 128, size=(n, k), dtype=np.int64).astype(np.int8)
+    qa[0, :] = -127
+    qb[0, :] = -127
+    sa = rng.random(m).astype(np.float32)
+    sb = rng.random(n).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    out = {}
+    for name in ("fo_matmul_t_q8_prequant", "fo_matmul_t_q8_prequant_scalar"):
+        o = np.zeros((m, n), np.float32)
+        getattr(O.lib(), name)(o.ctypes.data, qa.ctypes.data, sa.ctypes.data, qb.ctypes.data,
+                               sb.ctypes.data, m, n, k, bias.ctypes.data)
+        out[name] = o
+    a, b = out.values()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
 def test_q8_toy_forward(toy_expected):
     """TestQ8ToyForward (quant_test.go:152-183): Q8 tracks the goldens ≥ 0.98."""
     for pack, pexp in toy_expected["packs"].items():
