@@ -32,7 +32,7 @@ EXPORTED = (
 # Environment options the library reads when a model is created, with the
 # values it accepts (any other value leaves the default, listed first).
 RUNTIME_OPTIONS = {
-    "FUTON_CUDA_ATTN": ("heads", "tc", "tc2"),
+    "FUTON_CUDA_ATTN": ("heads", "tc2"),
     "FUTON_CUDA_ATTN_SPLIT": ("1", "0"),
     "FUTON_CUDA_Q8_ATTN": ("exact", "split"),
 }

@@ -20,7 +20,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libfuton_cuda.so"
-SOURCES = ["futon_cuda.cu", "gemm_bf16.cu", "gemm_s8.cu"]
+SOURCES = ["futon_cuda.cu", "gemm_f16.cu", "gemm_bf16.cu", "gemm_s8.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -25,6 +25,8 @@
 
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "mathf32.cuh"
 
@@ -85,6 +87,11 @@ template <> __device__ __forceinline__ void store2<float>(float* dst, float a, f
 template <> __device__ __forceinline__ void store2<__nv_bfloat16>(__nv_bfloat16* dst, float a,
                                                                   float b) {
   *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(a, b);
+}
+template <> __device__ __forceinline__ void store2<__half>(__half* dst, float a, float b) {
+  uint32_t w;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(b), "f"(a));
+  *reinterpret_cast<uint32_t*>(dst) = w;
 }
 
 // ---------------------------------------------------------------------------
@@ -400,7 +407,8 @@ struct AttnLane {
   }
 };
 
-template <int HD, int RB, int NBLK, bool PARTIAL, bool FIRST>
+// QF16: q and k are f16 (else bf16).
+template <int HD, int RB, int NBLK, bool PARTIAL, bool FIRST, bool QF16>
 __device__ __forceinline__ void attn_step(uint32_t kS, uint32_t vS, const AttnLane<HD, RB>& al,
                                           int lane, int nkeys, float scale_log2,
                                           const uint32_t (&qf)[HD / 16][4],
@@ -414,9 +422,15 @@ __device__ __forceinline__ void attn_step(uint32_t kS, uint32_t vS, const AttnLa
       uint32_t kf[4];
       ldsm_x4(kf, kS + nb * 8 * RB + al.k_off[kc / 2]);
       const uint32_t k0[2] = {kf[0], kf[1]}, k1[2] = {kf[2], kf[3]};
-      if (kc == 0) mma_16816_z(sc[nb], qf[kc], k0);
-      else mma_16816(sc[nb], qf[kc], k0);
-      mma_16816(sc[nb], qf[kc + 1], k1);
+      if constexpr (QF16) {
+        if (kc == 0) mma_16816_f16c<true>(sc[nb], qf[kc], k0);
+        else mma_16816_f16c<false>(sc[nb], qf[kc], k0);
+        mma_16816_f16c<false>(sc[nb], qf[kc + 1], k1);
+      } else {
+        if (kc == 0) mma_16816_z(sc[nb], qf[kc], k0);
+        else mma_16816(sc[nb], qf[kc], k0);
+        mma_16816(sc[nb], qf[kc + 1], k1);
+      }
     }
   }
   if constexpr (PARTIAL) {
@@ -498,7 +512,7 @@ __device__ __forceinline__ void attn_step(uint32_t kS, uint32_t vS, const AttnLa
 // One key tile of the NH heads held by a tile row block: the 8-key block
 // count is resolved once, then each head's step runs in the same basic
 // block (independent chains the scheduler can interleave).
-template <int HD, int RB, int NH, bool FIRST>
+template <int HD, int RB, int NH, bool FIRST, bool QF16>
 __device__ __forceinline__ void attn_step_dispatch(int nkeys, uint32_t kS, uint32_t vS,
                                                    const AttnLane<HD, RB> (&al)[NH], int lane,
                                                    float scale_log2,
@@ -511,12 +525,12 @@ __device__ __forceinline__ void attn_step_dispatch(int nkeys, uint32_t kS, uint3
   case NB:                                                                                  \
     if (partial) {                                                                          \
       _Pragma("unroll") for (int e = 0; e < NH; ++e)                                        \
-        attn_step<HD, RB, NB, true, FIRST>(kS, vS, al[e], lane, nkeys, scale_log2, qf[e],    \
-                                           o[e], m[e], l[e]);                               \
+        attn_step<HD, RB, NB, true, FIRST, QF16>(kS, vS, al[e], lane, nkeys, scale_log2,     \
+                                                 qf[e], o[e], m[e], l[e]);                  \
     } else {                                                                                \
       _Pragma("unroll") for (int e = 0; e < NH; ++e)                                        \
-        attn_step<HD, RB, NB, false, FIRST>(kS, vS, al[e], lane, nkeys, scale_log2, qf[e],   \
-                                            o[e], m[e], l[e]);                              \
+        attn_step<HD, RB, NB, false, FIRST, QF16>(kS, vS, al[e], lane, nkeys, scale_log2,    \
+                                                  qf[e], o[e], m[e], l[e]);                 \
     }                                                                                       \
     break;
   switch (nblk) {
@@ -555,6 +569,8 @@ __global__ void __launch_bounds__(128, attn_heads_min_ctas<HD, NH>())
                       int cls_mode, float scale_log2, OutT* __restrict__ out, int ldo,
                       int* __restrict__ err) {
   constexpr int W = HD * NH;  // tile width in elements
+  // f16 outputs: the qkv buffer holds f16 q and k too (else bf16 q, k).
+  constexpr bool kQF16 = std::is_same<OutT, __half>::value;
   using SM = AttnSmem<W>;
   constexpr int RB = SM::kRowBytes, kTile = SM::kTileBytes;
   extern __shared__ uint8_t sm_raw[];
@@ -636,11 +652,11 @@ __global__ void __launch_bounds__(128, attn_heads_min_ctas<HD, NH>())
 #pragma unroll
             for (int kc = 0; kc < HD / 16; ++kc)
               ldsm_x4(qf[e][kc], qS + (((e * (HD / 8) + 2 * kc + q_hi) ^ q_swz) << 4));
-          attn_step_dispatch<HD, RB, NH, true>(nkeys, kS, vS, al, lane, scale_log2, qf, o, m_run,
-                                               l_run);
+          attn_step_dispatch<HD, RB, NH, true, kQF16>(nkeys, kS, vS, al, lane, scale_log2, qf, o,
+                                                      m_run, l_run);
         } else {
-          attn_step_dispatch<HD, RB, NH, false>(nkeys, kS, vS, al, lane, scale_log2, qf, o,
-                                                m_run, l_run);
+          attn_step_dispatch<HD, RB, NH, false, kQF16>(nkeys, kS, vS, al, lane, scale_log2, qf, o,
+                                                       m_run, l_run);
         }
         if (j == nkv - 1) {
           const int qr0 = tile.q0 + warp * 16 + (lane >> 2), qr1 = qr0 + 8;
@@ -682,8 +698,17 @@ __device__ __forceinline__ int find_seq(const int* cu, int nseq, int row) {
 // sequence i; output row i of a compact [nseq, ldo] buffer.
 template <typename T> __device__ __forceinline__ float to_f32(T v);
 template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
 template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
   return __bfloat162float(v);
+}
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) {
+  return __float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f));
+}
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
 }
 
 template <int HD, typename InT, typename OutT>
@@ -764,10 +789,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int d = 0; d < HD; ++d) {
     const float v = warp_sum(o[d] * a);
-    if (lane == (d & 31)) {
-      if constexpr (sizeof(OutT) == 4) dst[d] = v * inv;
-      else dst[d] = __float2bfloat16_rn(v * inv);
-    }
+    if (lane == (d & 31)) dst[d] = from_f32<OutT>(v * inv);
   }
 }
 

@@ -3,8 +3,7 @@
 // native/model.go:646-739 (attendHead, softmaxScaled) for every head and
 // sequence of a micro-batch.
 //
-// Same work decomposition and numerics as attn_tc_kernel (attention_tc.cuh):
-// a CTA takes one window of ≤ 128 query rows (sequences of ≤ 128 tokens
+// A CTA takes one window of ≤ 128 query rows (sequences of ≤ 128 tokens
 // packed at 16-row-aligned offsets with the sequence mask folded into S as
 // one more K = 16 MMA step, or 128 queries of a longer sequence with its
 // keys in 128-key blocks); exponents rounded to f16 before ex2.approx.f16x2,
@@ -41,11 +40,75 @@
 
 #include <cuda_fp16.h>
 
-#include "attention_tc.cuh"
+#include <type_traits>
+
+#include "attention.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
+#include "mathf32.cuh"
 
 namespace futon {
+
+// A sequence placed in a packed window: tokens [t0, t0 + len) at window
+// rows [row, row + len), row a multiple of 16.
+struct AttnSeg {
+  int t0, len, row;
+};
+
+// nseg = 0: query rows [q0, q0 + nq) of one long sequence whose keys are
+// [k0, k0 + nk) (micro-batch-local token indices), nq ≤ 128.
+// nseg > 0: segments [seg0, seg0 + nseg) packed into rows [0, nq), nq = nk =
+// the rows they occupy rounded to 16 (≤ 128).
+struct AttnWindow {
+  int q0, nq;
+  int k0, nk;
+  int seg0, nseg;
+};
+
+struct AttnMaps {
+  CUtensorMap m[9];  // m[n]: boxes of 16·n rows × hd columns
+};
+
+// Descriptor of a tile of 128 rows × HD 16-bit values as TMA writes it with
+// the swizzle spanning one row (64 B for HD 32, 128 B for HD 64): 8-row
+// atoms stacked at 8 · row bytes. Used K-major for q and k and MN-major
+// (idesc bit 16) for v, whose one swizzle atom spans all HD columns.
+template <int HD>
+__device__ __forceinline__ uint64_t desc_rows(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1u << 16;                               // leading byte offset (unused)
+  d |= (uint64_t)((8u * HD * 2u) >> 4) << 32;            // stride byte offset: 8 rows
+  d |= (uint64_t)1u << 46;                               // version
+  d |= (uint64_t)(HD == 32 ? 4u : 2u) << 61;             // SWIZZLE_64B / SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  return r;
+}
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+// 2^lo, 2^hi as one f16x2 word (exponents rounded to f16 first).
+__device__ __forceinline__ uint32_t ex2_h2(float lo, float hi) {
+  uint32_t t, r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(t) : "f"(hi), "f"(lo));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(t));
+  return r;
+}
+
 
 struct AttnTc2Cfg {
   static constexpr int kRowBytes = 128;                    // two heads × 32 × 2 B
@@ -81,6 +144,11 @@ __global__ void __launch_bounds__(320, 1)
   static_assert(HD == 32 || HD == 64, "head_dim 32 or 64");
   using C = AttnTc2Cfg;
   constexpr bool kPair = HD == 32;          // a unit = a head pair (both groups)
+  // f16 outputs: q and k are f16 too (else bf16); the mask rows' 1 and
+  // −29952 in that format.
+  constexpr bool kQF16 = std::is_same<OutT, __half>::value;
+  constexpr uint32_t kOne16 = kQF16 ? 0x3C00u : 0x3F80u;
+  constexpr uint32_t kOff16 = kQF16 ? 0xF750u : 0xC6EAu;
   extern __shared__ uint8_t sm_raw[];
   const uint32_t sbase = (smem_u32(sm_raw) + 1023u) & ~1023u;
   const uint32_t sOnes = sbase + C::kOnesOffset;
@@ -153,15 +221,15 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       if (grp == 0) {
-        // Mask rows (as in attn_tc_kernel): q side onehot(segment), k side
-        // −29952 (bf16 0xC6EA) off the own segment.
+        // Mask rows: q side onehot(segment), k side
+        // −29952 off the own segment.
         uint32_t qa[8], ka[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const uint32_t lo = (2 * i == sidx) ? 0x3F80u : 0u, hi = (2 * i + 1 == sidx) ? 0x3F80u : 0u;
+          const uint32_t lo = (2 * i == sidx) ? kOne16 : 0u, hi = (2 * i + 1 == sidx) ? kOne16 : 0u;
           qa[i] = lo | (hi << 16);
-          const uint32_t klo16 = (2 * i == sidx) ? 0u : 0xC6EAu;
-          const uint32_t khi16 = (2 * i + 1 == sidx) ? 0u : 0xC6EAu;
+          const uint32_t klo16 = (2 * i == sidx) ? 0u : kOff16;
+          const uint32_t khi16 = (2 * i + 1 == sidx) ? 0u : kOff16;
           ka[i] = klo16 | (khi16 << 16);
         }
         const int sw = (r >> 1) & 3;
@@ -260,14 +328,15 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t q = sbase + C::kQkOffset + (uint32_t)(u % C::kQkStages) * 2u * C::kTileBytes;
         const uint32_t k = q + C::kTileBytes;
         const uint32_t n = (uint32_t)keys16(unit_kb(u));
-        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (8u << 24);
+        const uint32_t ab = kQF16 ? 0u : 1u;  // operand format: f16 0, bf16 1
+        const uint32_t idesc = (1u << 4) | (ab << 7) | (ab << 10) | ((n >> 3) << 17) | (8u << 24);
         const uint32_t d = tmem + C::kColS + 128u * (uint32_t)e;
         const uint64_t hoff = kPair ? 4u * (uint32_t)e : 0u;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks)
-          mma_bf16(d, smem_desc_k_sw128(q) + hoff + 2 * ks, smem_desc_k_sw128(k) + hoff + 2 * ks,
+          mma_f16kind(d, smem_desc_k_sw128(q) + hoff + 2 * ks, smem_desc_k_sw128(k) + hoff + 2 * ks,
                    idesc, ks ? 1u : 0u);
-        if (packed) mma_bf16(d, desc_rows<32>(sQa), desc_rows<32>(sKa), idesc, 1u);
+        if (packed) mma_f16kind(d, desc_rows<32>(sQa), desc_rows<32>(sKa), idesc, 1u);
         mma_commit(sfull_b + 8 * e);
       };
       constexpr uint32_t idesc_pv = (1u << 4) | (1u << 16) | ((uint32_t)(64 >> 3) << 17) | (8u << 24);
@@ -281,9 +350,9 @@ __global__ void __launch_bounds__(320, 1)
         for (int ks = 0; ks < nks; ++ks) {
           const uint64_t pd = smem_desc_k_sw128(sp + (ks >> 2) * 16384) + 2 * (ks & 3);
           const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
-          mma_bf16(tmem + C::kColO + 64u * (uint32_t)e, pd,
+          mma_f16kind(tmem + C::kColO + 64u * (uint32_t)e, pd,
                    desc_rows<64>(v + ks * 16 * C::kRowBytes), idesc_pv, acc);
-          mma_bf16(tmem + C::kColL + 32u * (uint32_t)e, pd,
+          mma_f16kind(tmem + C::kColL + 32u * (uint32_t)e, pd,
                    smem_desc_k_sw128(sOnes) + 2 * (ks & 3), idesc_l, acc);
         }
         mma_commit(ofull_b + 8 * e);

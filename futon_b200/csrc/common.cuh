@@ -118,6 +118,18 @@ __device__ __forceinline__ void st_cluster_f64x2(uint32_t caddr, double a, doubl
                : "memory");
 }
 
+// Asynchronous 16-byte store into another CTA's shared memory (both
+// addresses shared::cluster): completes `bytes` of the transaction count of
+// that CTA's mbarrier `cbar` once the data has landed, with no fence on the
+// sending side (the receiver's acquire wait on the mbarrier orders it).
+__device__ __forceinline__ void st_async_f64x2(uint32_t caddr, double a, double b, uint32_t cbar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f64 [%0], {%1, %2}, [%3];" ::"r"(
+          caddr),
+      "d"(a), "d"(b), "r"(cbar)
+      : "memory");
+}
+
 // Arrive on an mbarrier of another CTA of the cluster, releasing this
 // thread's earlier writes at cluster scope.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
@@ -203,9 +215,9 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem] · B[smem]ᵀ, both operands K-major, kind::f16 (bf16 in,
-// f32 accumulate). One thread issues.
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+// D[tmem] (+)= A[smem] · B[smem]ᵀ, kind::f16: f16 or bf16 operands (both the
+// same, as idesc says), f32 accumulate. One thread issues.
+__device__ __forceinline__ void mma_f16kind(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -269,7 +281,7 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
 // Instruction descriptor (kind::f16 / kind::i8): dense, K-major A and B,
 // M = 128, N = n.
 //   c_format (bits 4-5):  1 = F32, 2 = S32
-//   a/b_format (7-9, 10-12): 1 = BF16 (kind::f16) or S8 (kind::i8)
+//   a/b_format (7-9, 10-12): kind::f16 0 = F16, 1 = BF16; kind::i8 1 = S8
 //   n_dim (17-22) = N >> 3, m_dim (24-28) = M >> 4
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_format, uint32_t ab_format,
                                                   uint32_t m, uint32_t n) {

@@ -5,12 +5,12 @@
 //   embeddings: word [vocab, h] f32, position [max_seq, h] f32 (absolute
 //     packs), token-type row 0 [h] f32, embedding LayerNorm γ/β f32;
 //   per layer: qkv W [3h, h], out W [h, h], fc1 W [inter, h] (or fc1‖gate
-//     interleaved [2·inter, h] for SwiGLU), fc2 W [h, inter] — bf16, K-major
+//     interleaved [2·inter, h] for SwiGLU), fc2 W [h, inter] — f16, K-major
 //     (the pack's nn.Linear layout), or int8 + per-row f32 scales on the Q8
 //     path; biases and LayerNorm parameters f32;
 //   rotary cos/sin tables [max_trained, hd/2] f32 (RoPE packs).
 // Activations of one micro-batch of T packed tokens: the residual stream —
-// xb [T, h] bf16 on the float path (also the GEMMs' A operand, updated in
+// xb [T, h] f16 on the float path (also the GEMMs' A operand, updated in
 // place by the fused residual + LayerNorm epilogues), x [T, h] f32 plus its
 // int8 codes on the Q8 path — qkv [T, 3h], attn [T, h], ffn [T, inter],
 // xf [T, h] f32 (final hidden rows for pooling), tmp [T, h] f32
@@ -41,7 +41,6 @@
 #include <vector>
 
 #include "attention.cuh"
-#include "attention_tc.cuh"
 #include "attention_tc2.cuh"
 #include "attn_exact.cuh"
 #include "common.cuh"
@@ -49,7 +48,11 @@
 #include "rowops.cuh"
 
 using namespace futon;
-using bf16 = __nv_bfloat16;
+using bf16 = __nv_bfloat16;  // the MatMulT seam's operands
+using f16 = __half;          // the float path's operands and activations
+
+// Element type of a 2-D TMA operand.
+enum Elem : uint32_t { kElemS8 = 1, kElemBf16 = 2, kElemF16 = 3 };
 
 namespace {
 
@@ -88,25 +91,30 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D row-major [rows, cols] operand (bf16 or int8) read in 128-byte-wide,
-// box_rows-high swizzled tiles. Rows and columns past the extent read as 0.
-bool make_operand_map(CUtensorMap* map, const void* base, bool s8, uint64_t rows, uint64_t cols,
+// 2-D row-major [rows, cols] operand (int8, bf16 or f16) read in
+// 128-byte-wide, box_rows-high swizzled tiles. Rows and columns past the
+// extent read as 0.
+bool make_operand_map(CUtensorMap* map, const void* base, Elem e, uint64_t rows, uint64_t cols,
                       uint32_t box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
+  const bool s8 = e == kElemS8;
   const uint32_t esz = s8 ? 1 : 2;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {cols * esz};
   cuuint32_t box[2] = {128u / esz, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, s8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const CUtensorMapDataType dt = s8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : e == kElemF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-// bf16 [rows, cols] GEMM output (row stride ld) written by TMA tile stores:
+// f16 [rows, cols] GEMM output (row stride ld) written by TMA tile stores:
 // 32 × 32 boxes with the 64-byte swizzle the epilogue staging uses.
 bool make_output_map(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols, uint64_t ld) {
   auto fn = encode_fn();
@@ -115,13 +123,13 @@ bool make_output_map(CUtensorMap* map, void* base, uint64_t rows, uint64_t cols,
   cuuint64_t strides[1] = {ld * 2};
   cuuint32_t box[2] = {32, 32};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-// The attention kernels' view of the [T, 3h] qkv buffer (bf16 q, k; f16 v):
+// The attention kernels' view of the [T, 3h] f16 qkv buffer:
 // box_rows × hd tiles with the swizzle spanning one tile row (64 B for hd 32,
 // 128 B for hd 64). Rows past T read as 0.
 bool make_qkv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, int hd,
@@ -132,7 +140,7 @@ bool make_qkv_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
   cuuint64_t strides[1] = {cols * 2};
   cuuint32_t box[2] = {(cuuint32_t)hd, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   hd == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -201,7 +209,7 @@ enum MapKind : int { kMapOperand = 1, kMapOutput = 2, kMapQkv = 3 };
 // Model state
 // ---------------------------------------------------------------------------
 struct GemmWeight {
-  void* w = nullptr;        // bf16 [n, k] or int8 [n, k]
+  void* w = nullptr;        // f16 [n, k] or int8 [n, k]
   float* scale = nullptr;   // int8 only: [n]
   float* bias = nullptr;    // [n] or null
   int n = 0, k = 0, bn = 64;
@@ -213,7 +221,7 @@ struct LayerDev {
   float *n1w, *n1b, *n2w, *n2b;
 };
 
-// Float path: the residual stream is xb (bf16), updated in place by the
+// Float path: the residual stream is xb (f16), updated in place by the
 // fused residual + LayerNorm epilogues; xf receives the f32 final hidden
 // state for pooling. Int8 path: the residual stream is x (f32) plus its int8
 // codes xq/xs; xb is unused.
@@ -221,13 +229,13 @@ struct Workspace {
   size_t tokens = 0;  // capacity
   void* base = nullptr;
   float* x;          // int8 path: residual stream (f32)
-  bf16* xb;          // float path: residual stream / GEMM operand (bf16)
+  f16* xb;           // float path: residual stream / GEMM operand (f16)
   float* xf;         // float path: final hidden rows (f32) for pooling
-  void* qkv;         // bf16 (float path) or f32 (q8 path)
-  void* attn;        // bf16 (float path) or f32 (q8 path)
-  void* ffn;         // bf16 or f32
+  void* qkv;         // f16 (float path) or f32 (q8 path)
+  void* attn;        // f16 (float path) or f32 (q8 path)
+  void* ffn;         // f16 or f32
   float* tmp;        // pre-LayerNorm sums when LayerNorm is not fused
-  void* xc;          // CLS rows of the residual stream (bf16 or f32)
+  void* xc;          // CLS rows of the residual stream (f16 or f32)
   int8_t *xq, *attnq, *ffnq;
   float *xs, *attns, *ffns;
 };
@@ -311,8 +319,8 @@ struct futon_model {
   int eff_max = 0;
   int swiglu_half = 0;
   // Attention kernel of the float path (read from FUTON_CUDA_ATTN when the
-  // model is created): 0 = attn_heads_kernel, 1 = attn_tc_kernel,
-  // 2 = attn_tc2_kernel (head_dim 32 or 64, even head count; others keep 0).
+  // model is created): 0 = attn_heads_kernel, 2 = attn_tc2_kernel
+  // (head_dim 32 or 64, even head count; others keep 0).
   int attn_kind = 0;
   // FUTON_CUDA_ATTN_SPLIT=1: attn_heads_kernel launches with the head groups
   // shared among grid.y CTAs when the tiles alone would leave SMs idle.
@@ -411,8 +419,15 @@ int effective_max(const futon_cfg& c) {
 // ---- tensor lookup -------------------------------------------------------
 struct HostTensor {
   const futon_tensor* t = nullptr;
-  std::vector<float> f32;  // converted copy for F16 inputs
-  const float* data() const { return t->dtype == FUTON_DTYPE_F32 ? (const float*)t->data : f32.data(); }
+  std::vector<float> f32;  // f32 copy of an F16 tensor, made when first asked for as f32
+  const float* data();
+};
+
+// A GEMM weight as the caller holds it: F32 or F16 (uploaded without an
+// f32 copy on the host).
+struct HostMat {
+  const void* p = nullptr;
+  int dtype = FUTON_DTYPE_F32;
 };
 
 float f16_to_f32(uint16_t h) {
@@ -471,14 +486,27 @@ void f16_expand(const uint16_t* src, size_t n, float* dst) {
   for (auto& x : th) x.join();
 }
 
+const float* HostTensor::data() {
+  if (t->dtype == FUTON_DTYPE_F32) return (const float*)t->data;
+  if (f32.empty()) {
+    size_t n = 1;
+    for (int k = 0; k < t->ndim; ++k) n *= (size_t)t->shape[k];
+    f32.resize(n);
+    f16_expand((const uint16_t*)t->data, n, f32.data());
+  }
+  return f32.data();
+}
+
 struct TensorSet {
   std::map<std::string, HostTensor> byname;
   std::map<std::string, bool> used;
 };
 
-int need(TensorSet& ts, const std::string& name, std::vector<int64_t> shape, bool optional,
-         const float** out, char* err, size_t errlen) {
-  *out = nullptr;
+// Looks up `name` with shape `shape`; on success *ht is its entry (null if
+// optional and absent).
+int find_tensor(TensorSet& ts, const std::string& name, const std::vector<int64_t>& shape,
+                bool optional, HostTensor** ht, char* err, size_t errlen) {
+  *ht = nullptr;
   auto it = ts.byname.find(name);
   if (it == ts.byname.end()) {
     if (optional) return FUTON_OK;
@@ -493,7 +521,26 @@ int need(TensorSet& ts, const std::string& name, std::vector<int64_t> shape, boo
       return set_err(err, errlen, FUTON_EINVAL, "native: tensor %s dim %zu is %lld, want %lld",
                      name.c_str(), i, (long long)t->shape[i], (long long)shape[i]);
   ts.used[name] = true;
-  *out = it->second.data();
+  *ht = &it->second;
+  return FUTON_OK;
+}
+
+int need(TensorSet& ts, const std::string& name, std::vector<int64_t> shape, bool optional,
+         const float** out, char* err, size_t errlen) {
+  HostTensor* ht;
+  int rc = find_tensor(ts, name, shape, optional, &ht, err, errlen);
+  *out = ht ? ht->data() : nullptr;
+  return rc;
+}
+
+// A GEMM weight in the caller's dtype (no f32 copy of F16 data).
+int need_mat(TensorSet& ts, const std::string& name, std::vector<int64_t> shape, HostMat* out,
+             char* err, size_t errlen) {
+  HostTensor* ht;
+  int rc = find_tensor(ts, name, shape, false, &ht, err, errlen);
+  if (rc) return rc;
+  out->p = ht->t->data;
+  out->dtype = ht->t->dtype;
   return FUTON_OK;
 }
 
@@ -507,54 +554,75 @@ int dev_alloc(DevCtx& d, T** p, size_t count, char* err, size_t errlen) {
   return FUTON_OK;
 }
 
+// Uploads go through d.stream, in order with the kernels that convert them
+// (a plain cudaMemcpy from pageable memory may return before its DMA has
+// landed, and d.stream does not wait for the legacy stream). The caller
+// synchronises d.stream before the source memory goes away.
 int upload_f32(DevCtx& d, float** dst, const float* src, size_t count, char* err, size_t errlen) {
   if (!src) { *dst = nullptr; return FUTON_OK; }
   int rc = dev_alloc(d, dst, count, err, errlen);
   if (rc) return rc;
-  CU_TRY(cudaMemcpy(*dst, src, count * sizeof(float), cudaMemcpyHostToDevice));
+  CU_TRY(cudaMemcpyAsync(*dst, src, count * sizeof(float), cudaMemcpyHostToDevice, d.stream));
   return FUTON_OK;
 }
 
 // Uploads a GEMM weight (optionally two interleaved halves for SwiGLU) as
-// bf16 or int8 + per-row scales, builds its bias and its TMA descriptor.
+// f16 or int8 + per-row scales, builds its bias and its TMA descriptor.
+// F16 weights of the float path go to the device as they are (exact: no
+// rounding and no host f32 copy); F32 weights are rounded to f16 on the
+// device; the int8 path quantises f32 rows (F16 weights are widened on the
+// device first). staging: device scratch of ≥ 6 bytes per weight element.
 // ln_slices: the GEMM feeds the fused LayerNorm epilogue, which splits each
 // row into 192-column slices held by the CTAs of one cluster.
-int upload_gemm(DevCtx& d, GemmWeight& g, const float* w1, const float* b1, const float* w2,
-                const float* b2, int n1, int k, int half, bool q8, bool ln_slices, float* staging,
+int upload_gemm(DevCtx& d, GemmWeight& g, HostMat w1, const float* b1, HostMat w2,
+                const float* b2, int n1, int k, int half, bool q8, bool ln_slices, void* staging,
                 char* err, size_t errlen) {
-  const int n = w2 ? 2 * n1 : n1;
+  const bool two = w2.p != nullptr;
+  const int n = two ? 2 * n1 : n1;
   g.n = n;
   g.k = k;
-  // Stage the f32 matrix on the device (interleaving fc1/gate blocks of `half` rows).
-  if (!w2) {
-    CU_TRY(cudaMemcpy(staging, w1, (size_t)n * k * sizeof(float), cudaMemcpyHostToDevice));
+  if (two && w2.dtype != w1.dtype)
+    return set_err(err, errlen, FUTON_EINVAL, "native: fc1 and gate weights differ in dtype");
+  const bool in16 = w1.dtype == FUTON_DTYPE_F16;
+  const size_t esz = in16 ? 2 : 4, count = (size_t)n * k;
+  float* st32 = static_cast<float*>(staging);
+  uint8_t* st16 = static_cast<uint8_t*>(staging) + count * 4;
+  int rc;
+  f16* w16 = nullptr;
+  if (!q8 && (rc = dev_alloc(d, &w16, count, err, errlen))) return rc;
+  // The matrix as given (interleaving fc1/gate blocks of `half` rows): F16
+  // straight into the float path's weight, else into staging.
+  uint8_t* dst = (!q8 && in16) ? reinterpret_cast<uint8_t*>(w16)
+                               : (in16 ? st16 : reinterpret_cast<uint8_t*>(st32));
+  if (!two) {
+    CU_TRY(cudaMemcpyAsync(dst, w1.p, count * esz, cudaMemcpyHostToDevice, d.stream));
   } else {
+    const size_t blk = (size_t)half * k * esz;
     for (int j = 0; j * half < n1; ++j) {
-      CU_TRY(cudaMemcpy(staging + (size_t)(2 * j) * half * k, w1 + (size_t)j * half * k,
-                        (size_t)half * k * sizeof(float), cudaMemcpyHostToDevice));
-      CU_TRY(cudaMemcpy(staging + (size_t)(2 * j + 1) * half * k, w2 + (size_t)j * half * k,
-                        (size_t)half * k * sizeof(float), cudaMemcpyHostToDevice));
+      CU_TRY(cudaMemcpyAsync(dst + (size_t)(2 * j) * blk, (const uint8_t*)w1.p + (size_t)j * blk,
+                             blk, cudaMemcpyHostToDevice, d.stream));
+      CU_TRY(cudaMemcpyAsync(dst + (size_t)(2 * j + 1) * blk,
+                             (const uint8_t*)w2.p + (size_t)j * blk, blk, cudaMemcpyHostToDevice,
+                             d.stream));
     }
   }
-  int rc;
   if (q8) {
+    if (in16) f16_to_f32_kernel<<<1024, 256, 0, d.stream>>>((const f16*)st16, count, st32);
     int8_t* q = nullptr;
-    if ((rc = dev_alloc(d, &q, (size_t)n * k, err, errlen))) return rc;
+    if ((rc = dev_alloc(d, &q, count, err, errlen))) return rc;
     if ((rc = dev_alloc(d, &g.scale, (size_t)n, err, errlen))) return rc;
-    quant_rows_kernel<<<std::min(4096, (n + 7) / 8), 256, 0, d.stream>>>(staging, n, k, q, g.scale);
+    quant_rows_kernel<<<std::min(4096, (n + 7) / 8), 256, 0, d.stream>>>(st32, n, k, q, g.scale);
     g.w = q;
   } else {
-    bf16* w = nullptr;
-    if ((rc = dev_alloc(d, &w, (size_t)n * k, err, errlen))) return rc;
-    f32_to_bf16_kernel<<<1024, 256, 0, d.stream>>>(staging, (size_t)n * k, w);
-    g.w = w;
+    if (!in16) f32_to_f16_kernel<<<1024, 256, 0, d.stream>>>(st32, count, w16);
+    g.w = w16;
   }
   CU_TRY(cudaGetLastError());
   CU_TRY(cudaStreamSynchronize(d.stream));
   // Bias (interleaved like the weight for SwiGLU; an absent half is zero).
   if (b1 || b2) {
     std::vector<float> hb((size_t)n, 0.0f);
-    if (!w2) {
+    if (!two) {
       memcpy(hb.data(), b1, sizeof(float) * n);
     } else {
       for (int j = 0; j * half < n1; ++j)
@@ -564,10 +632,11 @@ int upload_gemm(DevCtx& d, GemmWeight& g, const float* w1, const float* b1, cons
         }
     }
     if ((rc = upload_f32(d, &g.bias, hb.data(), (size_t)n, err, errlen))) return rc;
+    CU_TRY(cudaStreamSynchronize(d.stream));  // hb is released on return
   }
-  g.bn = w2 ? 2 * half : (ln_slices ? ln_slice_cols(n) : pick_bn(n));
+  g.bn = two ? 2 * half : (ln_slices ? ln_slice_cols(n) : pick_bn(n));
   const uint32_t box = g.bn <= 256 ? (uint32_t)g.bn : (uint32_t)g.bn / 2;
-  if (!make_operand_map(&g.map, g.w, q8, (uint64_t)n, (uint64_t)k, box))
+  if (!make_operand_map(&g.map, g.w, q8 ? kElemS8 : kElemF16, (uint64_t)n, (uint64_t)k, box))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed for a weight");
   return FUTON_OK;
 }
@@ -602,7 +671,7 @@ int ensure_workspace(const futon_model& m, DevCtx& d, size_t tokens, char* err, 
   w.base = base;
   w.tokens = tokens;
   w.x = q8 ? (float*)(b + o_x) : nullptr;
-  w.xb = q8 ? nullptr : (bf16*)(b + o_xb);
+  w.xb = q8 ? nullptr : (f16*)(b + o_xb);
   w.xf = q8 ? nullptr : (float*)(b + o_xf);
   w.qkv = b + o_qkv;
   w.attn = b + o_attn;
@@ -655,7 +724,7 @@ struct GemmOut {
   int ldo = 0;
   const void* resid = nullptr;
   int ldr = 0;
-  bool resid_bf16 = false;
+  bool resid_16 = false;  // the residual is f16 (else f32)
   const float* ln_w = nullptr;
   const float* ln_b = nullptr;
   float eps = 0.f;
@@ -676,23 +745,24 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   const double out_cols = o.epi == kEpiSwiglu ? w.n / 2 : w.n;
   const bool plain = o.epi == kEpiStore || o.epi == kEpiRope;
   const double osz = (o.out_f32 || (s8 && !plain)) ? 4.0 : 2.0;
-  const double rsz = o.resid ? (o.resid_bf16 ? 2.0 : 4.0) : 0.0;
+  const double rsz = o.resid ? (o.resid_16 ? 2.0 : 4.0) : 0.0;
   const double bytes = (double)M * w.k * esz + (double)w.n * w.k * esz + (double)M * out_cols * osz +
                        (double)M * w.n * rsz + (o.out_f32_copy ? (double)M * w.n * 4.0 : 0.0);
   ProfScope prof(d, st, stage, 2.0 * M * w.n * w.k, bytes);
   CUtensorMap ta, to;
   auto operand_map = [&](CUtensorMap* map, const void* base, bool is_s8, uint64_t rows,
                          uint64_t cols) {
-    return d.map_cache.get(MapKey{kMapOperand, base, rows, cols, is_s8 ? 1u : 0u, 128}, map,
+    const Elem e = is_s8 ? kElemS8 : kElemF16;
+    return d.map_cache.get(MapKey{kMapOperand, base, rows, cols, (uint64_t)e, 128}, map,
                            [&](CUtensorMap* mm) {
-                             return make_operand_map(mm, base, is_s8, rows, cols, 128);
+                             return make_operand_map(mm, base, e, rows, cols, 128);
                            });
   };
   if (!operand_map(&ta, A, s8, (uint64_t)M, (uint64_t)w.k))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (activation)");
-  // bf16 outputs leave through TMA tile stores.
-  const bool bf16_out = o.epi == kEpiResidLN || !(o.out_f32 || (s8 && !plain));
-  if (bf16_out) {
+  // 16-bit outputs leave through TMA tile stores.
+  const bool out16 = o.epi == kEpiResidLN || !(o.out_f32 || (s8 && !plain));
+  if (out16) {
     const uint64_t ncols = o.epi == kEpiSwiglu ? (uint64_t)w.n / 2 : (uint64_t)w.n;
     const MapKey key{kMapOutput, o.out, (uint64_t)M, ncols, (uint64_t)o.ldo, 0};
     if (!d.map_cache.get(key, &to, [&](CUtensorMap* mm) {
@@ -706,7 +776,7 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   GemmLaunch g;
   g.ta = &ta;
   g.tw = &w.map;
-  g.to = bf16_out ? &to : nullptr;
+  g.to = out16 ? &to : nullptr;
   g.tr = o.epi == kEpiResidLN ? &tr : nullptr;
   g.M = M;
   g.N = w.n;
@@ -714,12 +784,13 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   g.bn = w.bn;
   g.epi = o.epi;
   g.out_f32 = o.out_f32;
+  g.f16 = !s8;
   g.ep.out = o.out;
   g.ep.ldo = o.ldo;
   g.ep.bias = w.bias;
   g.ep.resid = o.resid;
   g.ep.ldr = o.ldr;
-  g.ep.resid_bf16 = o.resid_bf16 ? 1 : 0;
+  g.ep.resid_kind = o.resid_16 ? kResidF16 : kResidF32;
   g.ep.a_scale = a_scale;
   g.ep.w_scale = w.scale;
   g.ep.ln_w = o.ln_w;
@@ -736,7 +807,7 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   g.err = d.err_word;
   g.num_sms = d.num_sms;
   g.stream = st;
-  cudaError_t e = s8 ? launch_gemm_s8(g) : launch_gemm_bf16(g);
+  cudaError_t e = s8 ? launch_gemm_s8(g) : launch_gemm_f16(g);
   if (e != cudaSuccess)
     return set_err(err, errlen, FUTON_ECUDA, "native: gemm launch: %s", cudaGetErrorString(e));
   d.launches.fetch_add(1, std::memory_order_relaxed);
@@ -750,17 +821,16 @@ inline int grid_rows(int rows, int per_block, int sms) {
 }
 
 // ---- attention dispatch --------------------------------------------------
-// attn_tc_kernel (tcgen05, packed 128-row windows) is parity-correct and
-// batch-invariant but, as measured on the c4 workload, 1.5× slower than
-// attn_heads_kernel; it runs only when FUTON_CUDA_ATTN=tc.
-enum AttnKind : int { kAttnHeads = 0, kAttnTc = 1, kAttnTc2 = 2 };
+// attn_tc2_kernel (tcgen05, packed 128-row windows) is parity-correct and
+// batch-invariant but, as measured on the c4 workload, 1.4× slower than
+// attn_heads_kernel; it runs only when FUTON_CUDA_ATTN=tc2.
+enum AttnKind : int { kAttnHeads = 0, kAttnTc2 = 2 };
 
 // Model-creation-time attention options from the environment; unknown
 // values leave the defaults.
 void read_attn_env(futon_model& m) {
   if (const char* v = std::getenv("FUTON_CUDA_ATTN")) {
-    if (!strcmp(v, "tc")) m.attn_kind = kAttnTc;
-    else if (!strcmp(v, "tc2")) m.attn_kind = kAttnTc2;
+    if (!strcmp(v, "tc2")) m.attn_kind = kAttnTc2;
     else if (!strcmp(v, "heads")) m.attn_kind = kAttnHeads;
   }
   if (const char* v = std::getenv("FUTON_CUDA_ATTN_SPLIT")) {
@@ -796,10 +866,13 @@ struct AttnPlan {
   size_t ptot = 0, ptot_cls = 0;
   float* pscr = nullptr;
   int head_group = 0;
+  // float32(1/Σe) per (head of the group, query row or CLS sequence).
+  float* pinv = nullptr;
+  int pinv_ld = 0;
 };
 
 // q and k arrive already rotated (RoPE runs in the qkv GEMM epilogue).
-// Float path: bf16 qkv, attn_heads_kernel (one CTA per 64-query tile, or per
+// Float path: f16 qkv, attn_heads_kernel (one CTA per 64-query tile, or per
 // sequence for the CLS-only last layer). Int8 path: f32 qkv and split-precision attention,
 // so the per-row quantisation that follows sees float32-accurate values.
 // Head dims other than 32/64 use the per-query kernel.
@@ -835,30 +908,6 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
         return cudaGetLastError();
       };
       CU_TRY(hd == 32 ? launch(attn_tc2_kernel<32, OutT>) : launch(attn_tc2_kernel<64, OutT>));
-      d.launches.fetch_add(1, std::memory_order_relaxed);
-      return FUTON_OK;
-    }
-    if (m.attn_kind == kAttnTc && tc_hd && !cls_only) {
-      if (plan.nwin == 0) return FUTON_OK;
-      // q, k, v tiles of one head: 128 rows × hd columns, swizzled over one row.
-      AttnMaps maps{};
-      for (int n = 1; n <= 8; ++n)
-        if (!d.map_cache.get(MapKey{kMapQkv, qkv, (uint64_t)T, (uint64_t)(3 * h), (uint64_t)hd,
-                                    16u * n},
-                             &maps.m[n], [&](CUtensorMap* mm) {
-                               return make_qkv_map(mm, qkv, (uint64_t)T, (uint64_t)(3 * h), hd,
-                                                   16u * n);
-                             }))
-          return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed (qkv)");
-      auto launch = [&](auto kern, int smem) -> cudaError_t {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        kern<<<plan.nwin, 192, smem, st>>>(maps, h, H, plan.wins, plan.segs, scale_log2, out,
-                                           h, d.err_word);
-        return cudaGetLastError();
-      };
-      CU_TRY(hd == 32 ? launch(attn_tc_kernel<32, OutT>, attn_tc_smem_bytes<32>())
-                      : launch(attn_tc_kernel<64, OutT>, attn_tc_smem_bytes<64>()));
       d.launches.fetch_add(1, std::memory_order_relaxed);
       return FUTON_OK;
     }
@@ -908,14 +957,14 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
         const unsigned nh = (unsigned)std::min(plan.head_group, H - h0);
         if (hd == 32) {
           attn_exact_softmax_kernel<32><<<dim3(grid, nh), 64, 0, st>>>(
-              qkv, h, h0, cu, tiles, cls, poff, pstride, scale, plan.pscr);
-          attn_exact_pv_kernel<32><<<dim3(grid, 4, nh), 256, 0, st>>>(
-              qkv, h, h0, cu, tiles, cls, poff, pstride, plan.pscr, out, h);
+              qkv, h, h0, cu, tiles, cls, poff, pstride, scale, plan.pscr, plan.pinv, plan.pinv_ld);
+          attn_exact_pv_kernel<32><<<dim3(grid, 2, nh), 4 * 32, 0, st>>>(
+              qkv, h, h0, cu, tiles, cls, poff, pstride, plan.pscr, plan.pinv, plan.pinv_ld, out, h);
         } else {
           attn_exact_softmax_kernel<64><<<dim3(grid, nh), 64, 0, st>>>(
-              qkv, h, h0, cu, tiles, cls, poff, pstride, scale, plan.pscr);
-          attn_exact_pv_kernel<64><<<dim3(grid, 4, nh), 256, 0, st>>>(
-              qkv, h, h0, cu, tiles, cls, poff, pstride, plan.pscr, out, h);
+              qkv, h, h0, cu, tiles, cls, poff, pstride, scale, plan.pscr, plan.pinv, plan.pinv_ld);
+          attn_exact_pv_kernel<64><<<dim3(grid, 2, nh), 4 * 64, 0, st>>>(
+              qkv, h, h0, cu, tiles, cls, poff, pstride, plan.pscr, plan.pinv, plan.pinv_ld, out, h);
         }
         CU_TRY(cudaGetLastError());
         d.launches.fetch_add(2, std::memory_order_relaxed);
@@ -995,15 +1044,14 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
     const bool last_cls = cls && last;
     const int rows = last_cls ? nseq : T;
 
-    // qkv = x·Wqkvᵀ + b → [T, 3h] (bf16 q, k and f16 v for the tensor-core
-    // attention; bf16 throughout for other head dims; f32 on the int8 path)
+    // qkv = x·Wqkvᵀ + b → [T, 3h] (f16 on the float path, f32 on the int8
+    // path)
     {
       GemmOut o;
       o.epi = kEpiStore;
       o.out_f32 = q8;
       o.out = w.qkv;
       o.ldo = 3 * h;
-      if (!q8 && (m.head_dim == 32 || m.head_dim == 64)) o.f16_from = 2 * h;
       if (c.position_encoding == FUTON_POS_ROPE) {
         o.epi = kEpiRope;
         o.rope_cos = d.rcos;
@@ -1028,8 +1076,8 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
         rc = run_attention<float, float>(m, d, T, nseq, cu, plan, last_cls,
                                          (const float*)w.qkv, (float*)w.attn, st, err, errlen);
       else
-        rc = run_attention<bf16, bf16>(m, d, T, nseq, cu, plan, last_cls,
-                                       (const bf16*)w.qkv, (bf16*)w.attn, st, err, errlen);
+        rc = run_attention<f16, f16>(m, d, T, nseq, cu, plan, last_cls,
+                                     (const f16*)w.qkv, (f16*)w.attn, st, err, errlen);
       if (rc) return rc;
     }
 
@@ -1040,7 +1088,7 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       ProfScope prof(d, st, kStGather, 0.0, (double)nseq * 2.0 * h * esz);
       const int blocks = grid_rows((int)((size_t)nseq * h * esz / 16), 256, d.num_sms);
       if (q8) gather_rows_kernel<float><<<blocks, 256, 0, st>>>(w.x, cu, nseq, h, (float*)w.xc);
-      else gather_rows_kernel<bf16><<<blocks, 256, 0, st>>>(w.xb, cu, nseq, h, (bf16*)w.xc);
+      else gather_rows_kernel<f16><<<blocks, 256, 0, st>>>(w.xb, cu, nseq, h, (f16*)w.xc);
       CU_TRY(cudaGetLastError());
       d.launches.fetch_add(1, std::memory_order_relaxed);
       resid = w.xc;
@@ -1057,7 +1105,7 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
         o.ldo = h;
         o.resid = res;
         o.ldr = h;
-        o.resid_bf16 = true;
+        o.resid_16 = true;
         o.ln_w = lnw;
         o.ln_b = lnb;
         o.eps = eps;
@@ -1070,7 +1118,7 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       o.ldo = h;
       o.resid = res;
       o.ldr = h;
-      o.resid_bf16 = !q8;
+      o.resid_16 = !q8;
       int r2 = run_gemm(d, stage, A, q8, a_scale, rows, W, o, st, err, errlen);
       if (r2) return r2;
       ProfScope prof(d, st, kStLayerNorm, 0.0, (double)rows * h * (q8 ? 9.0 : (f32_copy ? 10.0 : 6.0)));
@@ -1336,12 +1384,15 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
     max_p = std::max(max_p, mb.ptot);
   }
   if ((rc = ensure_workspace(m, d, max_t, err, errlen))) return rc;
-  // Exact attention scratch: as many heads per launch as fit in 4 GiB.
+  // Exact attention scratch: as many heads per launch as fit in 4 GiB of P,
+  // then each head's per-row 1/Σe (max_t rows: every micro-batch's query
+  // rows and CLS sequences fit).
   int head_group = 0;
   if (exact_p && max_p > 0) {
     const size_t budget = (size_t)1 << 30;  // floats
     head_group = (int)std::max<size_t>(1, std::min<size_t>((size_t)m.cfg.num_heads, budget / max_p));
-    if ((rc = ensure_dev(&d.d_pscr, &d.d_pscr_cap, (size_t)head_group * max_p, err, errlen)))
+    if ((rc = ensure_dev(&d.d_pscr, &d.d_pscr_cap, (size_t)head_group * (max_p + max_t), err,
+                         errlen)))
       return rc;
   }
   const int dim = out_dim ? out_dim : m.cfg.hidden_size;
@@ -1359,6 +1410,8 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
       plan.ptot_cls = mb.ptot_cls;
       plan.pscr = d.d_pscr;
       plan.head_group = head_group;
+      plan.pinv = d.d_pscr + (size_t)head_group * max_p;
+      plan.pinv_ld = (int)max_t;
     }
     if ((rc = forward_mb(m, d, d_ids + mb.t0, d.d_meta + mb.cu_off, mb.s1 - mb.s0, mb.t1 - mb.t0,
                          mb.sum_l2, plan, out_dim, d_out + (size_t)mb.s0 * dim, st, cancel, err,
@@ -1374,7 +1427,9 @@ int read_device_error(DevCtx& d, char* err, size_t errlen) {
   CU_TRY(cudaMemcpy(&code, d.err_word, sizeof(int), cudaMemcpyDeviceToHost));
   d.d2h_bytes.fetch_add((long long)sizeof(int), std::memory_order_relaxed);
   if (code != 0) {
-    CU_TRY(cudaMemset(d.err_word, 0, sizeof(int)));
+    // Cleared on the device's stream (ordered with the next call's kernels).
+    CU_TRY(cudaMemsetAsync(d.err_word, 0, sizeof(int), d.stream));
+    CU_TRY(cudaStreamSynchronize(d.stream));
     return set_err(err, errlen, code == kDevBadInput ? FUTON_EINVAL : FUTON_EDEVICE,
                    code == kDevBadInput ? "native: token id outside vocab (device-side check)"
                                         : "native: device-side error %d (a bounded pipeline wait expired)",
@@ -1457,6 +1512,7 @@ int seam_begin(int dev, size_t bytes, SeamCtx** out, std::unique_lock<std::mutex
   if (!s.init) {
     CU_TRY(cudaMalloc(&s.err_word, sizeof(int)));
     CU_TRY(cudaMemset(s.err_word, 0, sizeof(int)));
+    CU_TRY(cudaDeviceSynchronize());  // zero before kernels on any stream read it
     CU_TRY(cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev));
     s.init = true;
   }
@@ -1478,7 +1534,8 @@ int seam_finish(SeamCtx& s, cudaStream_t st, char* err, size_t errlen) {
   int code = 0;
   CU_TRY(cudaMemcpy(&code, s.err_word, sizeof(int), cudaMemcpyDeviceToHost));
   if (code) {
-    CU_TRY(cudaMemset(s.err_word, 0, sizeof(int)));
+    CU_TRY(cudaMemsetAsync(s.err_word, 0, sizeof(int), st));
+    CU_TRY(cudaStreamSynchronize(st));
     return set_err(err, errlen, FUTON_EDEVICE, "native: device-side error %d", code);
   }
   return FUTON_OK;
@@ -1492,8 +1549,9 @@ int seam_gemm(int* err_word, int num_sms, const void* A, bool s8, const float* a
               cudaStream_t st, char* err, size_t errlen) {
   CUtensorMap ta, tw;
   const int bn = pick_bn(n);
-  if (!make_operand_map(&ta, A, s8, (uint64_t)m, (uint64_t)k, 128) ||
-      !make_operand_map(&tw, W, s8, (uint64_t)n, (uint64_t)k, (uint32_t)bn))
+  const Elem el = s8 ? kElemS8 : kElemBf16;
+  if (!make_operand_map(&ta, A, el, (uint64_t)m, (uint64_t)k, 128) ||
+      !make_operand_map(&tw, W, el, (uint64_t)n, (uint64_t)k, (uint32_t)bn))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed");
   GemmLaunch g;
   g.ta = &ta;
@@ -1506,12 +1564,13 @@ int seam_gemm(int* err_word, int num_sms, const void* A, bool s8, const float* a
   g.bn = bn;
   g.epi = kEpiStore;
   g.out_f32 = true;
+  g.f16 = false;
   g.ep.out = dst;
   g.ep.ldo = n;
   g.ep.bias = bias;
   g.ep.resid = nullptr;
   g.ep.ldr = 0;
-  g.ep.resid_bf16 = 0;
+  g.ep.resid_kind = kResidF32;
   g.ep.a_scale = a_scale;
   g.ep.w_scale = w_scale;
   g.ep.ln_w = nullptr;
@@ -1598,12 +1657,6 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
       return set_err(err, errlen, FUTON_EINVAL, "native: tensor %s has rank %d", t.name, t.ndim);
     HostTensor ht;
     ht.t = &t;
-    if (t.dtype == FUTON_DTYPE_F16) {
-      size_t n = 1;
-      for (int k = 0; k < t.ndim; ++k) n *= (size_t)t.shape[k];
-      ht.f32.resize(n);
-      f16_expand((const uint16_t*)t.data, n, ht.f32.data());
-    }
     if (ts.byname.count(t.name))
       return set_err(err, errlen, FUTON_EINVAL, "native: duplicate tensor %s", t.name);
     ts.byname.emplace(t.name, std::move(ht));
@@ -1618,27 +1671,27 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
   if ((rc = need(ts, "embeddings.norm.weight", {h}, false, &embw, err, errlen))) return rc;
   if ((rc = need(ts, "embeddings.norm.bias", {h}, false, &embb, err, errlen))) return rc;
   struct LW {
-    const float *qkvw, *qkvb, *outw, *outb, *n1w, *n1b, *fc1w, *fc1b, *gatew, *gateb, *fc2w, *fc2b,
-        *n2w, *n2b;
+    HostMat qkvw, outw, fc1w, gatew, fc2w;
+    const float *qkvb, *outb, *n1w, *n1b, *fc1b, *gateb, *fc2b, *n2w, *n2b;
   };
   std::vector<LW> lw(c.num_layers);
   for (int i = 0; i < c.num_layers; ++i) {
     auto p = [&](const char* s) { return "layers." + std::to_string(i) + "." + s; };
     LW& l = lw[i];
-    l.gatew = l.gateb = nullptr;
-    if ((rc = need(ts, p("attn.qkv.weight"), {3 * h, h}, false, &l.qkvw, err, errlen))) return rc;
+    l.gateb = nullptr;
+    if ((rc = need_mat(ts, p("attn.qkv.weight"), {3 * h, h}, &l.qkvw, err, errlen))) return rc;
     if ((rc = need(ts, p("attn.qkv.bias"), {3 * h}, true, &l.qkvb, err, errlen))) return rc;
-    if ((rc = need(ts, p("attn.out.weight"), {h, h}, false, &l.outw, err, errlen))) return rc;
+    if ((rc = need_mat(ts, p("attn.out.weight"), {h, h}, &l.outw, err, errlen))) return rc;
     if ((rc = need(ts, p("attn.out.bias"), {h}, true, &l.outb, err, errlen))) return rc;
     if ((rc = need(ts, p("norm1.weight"), {h}, false, &l.n1w, err, errlen))) return rc;
     if ((rc = need(ts, p("norm1.bias"), {h}, false, &l.n1b, err, errlen))) return rc;
-    if ((rc = need(ts, p("mlp.fc1.weight"), {I, h}, false, &l.fc1w, err, errlen))) return rc;
+    if ((rc = need_mat(ts, p("mlp.fc1.weight"), {I, h}, &l.fc1w, err, errlen))) return rc;
     if ((rc = need(ts, p("mlp.fc1.bias"), {I}, true, &l.fc1b, err, errlen))) return rc;
     if (swiglu) {
-      if ((rc = need(ts, p("mlp.gate.weight"), {I, h}, false, &l.gatew, err, errlen))) return rc;
+      if ((rc = need_mat(ts, p("mlp.gate.weight"), {I, h}, &l.gatew, err, errlen))) return rc;
       if ((rc = need(ts, p("mlp.gate.bias"), {I}, true, &l.gateb, err, errlen))) return rc;
     }
-    if ((rc = need(ts, p("mlp.fc2.weight"), {h, I}, false, &l.fc2w, err, errlen))) return rc;
+    if ((rc = need_mat(ts, p("mlp.fc2.weight"), {h, I}, &l.fc2w, err, errlen))) return rc;
     if ((rc = need(ts, p("mlp.fc2.bias"), {h}, true, &l.fc2b, err, errlen))) return rc;
     if ((rc = need(ts, p("norm2.weight"), {h}, false, &l.n2w, err, errlen))) return rc;
     if ((rc = need(ts, p("norm2.bias"), {h}, false, &l.n2b, err, errlen))) return rc;
@@ -1673,10 +1726,15 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
       }
   }
 
+  // One weight replica per device, uploaded by one host thread per device
+  // (each GPU's copies run over its own link at the same time).
   const size_t max_mat = std::max<size_t>((size_t)3 * h * h, (size_t)2 * I * h);
-  for (int di = 0; di < ndev; ++di) {
+  auto upload_device = [&](int dev, std::unique_ptr<DevCtx>* slot, char* e, size_t el) -> int {
     auto d = std::make_unique<DevCtx>();
-    d->device = devices[di];
+    d->device = dev;
+    char* err = e;
+    size_t errlen = el;
+    int rc;
     CU_TRY(cudaSetDevice(d->device));
     CU_TRY(cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, d->device));
     CU_TRY(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
@@ -1685,7 +1743,7 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
     CU_TRY(cudaEventCreateWithFlags(&d->done_evt, cudaEventDisableTiming));
     CU_TRY(cudaEventRecord(d->done_evt, d->stream));
     if ((rc = dev_alloc(*d, &d->err_word, 1, err, errlen))) return rc;
-    CU_TRY(cudaMemset(d->err_word, 0, sizeof(int)));
+    CU_TRY(cudaMemsetAsync(d->err_word, 0, sizeof(int), d->stream));
     if ((rc = upload_f32(*d, &d->word, word, (size_t)c.vocab_size * h, err, errlen))) return rc;
     if ((rc = upload_f32(*d, &d->pos, pos, pos ? (size_t)c.max_seq_len * h : 0, err, errlen))) return rc;
     if ((rc = upload_f32(*d, &d->type0, type, type ? (size_t)h : 0, err, errlen))) return rc;
@@ -1695,19 +1753,21 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
       if ((rc = upload_f32(*d, &d->rcos, rc_tab.data(), rc_tab.size(), err, errlen))) return rc;
       if ((rc = upload_f32(*d, &d->rsin, rs_tab.data(), rs_tab.size(), err, errlen))) return rc;
     }
-    float* staging = nullptr;
-    CU_TRY(cudaMalloc(&staging, max_mat * sizeof(float)));
+    void* staging = nullptr;
+    CU_TRY(cudaMalloc(&staging, max_mat * 6));
     d->layers.resize(c.num_layers);
+    const HostMat none;
+    rc = FUTON_OK;
     for (int i = 0; i < c.num_layers && rc == FUTON_OK; ++i) {
       const LW& l = lw[i];
       LayerDev& L = d->layers[i];
       const bool fr = model->fuse_ln;
-      if ((rc = upload_gemm(*d, L.qkv, l.qkvw, l.qkvb, nullptr, nullptr, 3 * h, h, 0, q8, false, staging, err, errlen))) break;
-      if ((rc = upload_gemm(*d, L.out, l.outw, l.outb, nullptr, nullptr, h, h, 0, q8, fr, staging, err, errlen))) break;
+      if ((rc = upload_gemm(*d, L.qkv, l.qkvw, l.qkvb, none, nullptr, 3 * h, h, 0, q8, false, staging, err, errlen))) break;
+      if ((rc = upload_gemm(*d, L.out, l.outw, l.outb, none, nullptr, h, h, 0, q8, fr, staging, err, errlen))) break;
       if (swiglu) rc = upload_gemm(*d, L.fc1, l.fc1w, l.fc1b, l.gatew, l.gateb, I, h, half, q8, false, staging, err, errlen);
-      else rc = upload_gemm(*d, L.fc1, l.fc1w, l.fc1b, nullptr, nullptr, I, h, 0, q8, false, staging, err, errlen);
+      else rc = upload_gemm(*d, L.fc1, l.fc1w, l.fc1b, none, nullptr, I, h, 0, q8, false, staging, err, errlen);
       if (rc) break;
-      if ((rc = upload_gemm(*d, L.fc2, l.fc2w, l.fc2b, nullptr, nullptr, h, I, 0, q8, fr, staging, err, errlen))) break;
+      if ((rc = upload_gemm(*d, L.fc2, l.fc2w, l.fc2b, none, nullptr, h, I, 0, q8, fr, staging, err, errlen))) break;
       if ((rc = upload_f32(*d, &L.n1w, l.n1w, h, err, errlen))) break;
       if ((rc = upload_f32(*d, &L.n1b, l.n1b, h, err, errlen))) break;
       if ((rc = upload_f32(*d, &L.n2w, l.n2w, h, err, errlen))) break;
@@ -1716,8 +1776,27 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
     cudaFree(staging);
     if (rc) return rc;
     CU_TRY(cudaStreamSynchronize(d->stream));
-    model->devs.push_back(std::move(d));
+    *slot = std::move(d);
+    return FUTON_OK;
+  };
+  std::vector<std::unique_ptr<DevCtx>> devs(ndev);
+  std::vector<int> rcs(ndev, FUTON_OK);
+  std::vector<std::string> msgs(ndev);
+  auto run_one = [&](int di) {
+    char e[512] = {0};
+    rcs[di] = upload_device(devices[di], &devs[di], e, sizeof e);
+    msgs[di] = e;
+  };
+  if (ndev == 1) {
+    run_one(0);
+  } else {
+    std::vector<std::thread> th;
+    for (int di = 0; di < ndev; ++di) th.emplace_back(run_one, di);
+    for (auto& t : th) t.join();
   }
+  for (int di = 0; di < ndev; ++di)
+    if (rcs[di]) return set_err(err, errlen, rcs[di], "%s", msgs[di].c_str());
+  for (auto& d : devs) model->devs.push_back(std::move(d));
   *out = model.release();
   return FUTON_OK;
 }

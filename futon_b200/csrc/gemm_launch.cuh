@@ -15,22 +15,26 @@ struct GemmLaunch {
   int M, N, K;
   int bn;                 // 64, 128, 192 or 256
   int epi;                // EpiKind
-  bool out_f32;           // output element type: f32 (true) or bf16
+  bool out_f32;           // output element type: f32 (true) or 16-bit (bf16, or f16 with f16)
+  bool f16;               // 16-bit operands, outputs and residuals are f16 (else bf16)
   EpiParams ep;
   int* err;               // device error word
   int num_sms;
   cudaStream_t stream;
 };
 
-// Defined in gemm_bf16.cu / gemm_s8.cu.
+// Defined in gemm_f16.cu (the forward's f16 GEMMs, every epilogue),
+// gemm_bf16.cu (the MatMulT seam: bf16 operands, f32 output, bias only) and
+// gemm_s8.cu (the int8 path).
+cudaError_t launch_gemm_f16(const GemmLaunch& g);
 cudaError_t launch_gemm_bf16(const GemmLaunch& g);
 cudaError_t launch_gemm_s8(const GemmLaunch& g);
 
-template <int BN, int EPI, bool S8, typename OutT>
+template <int BN, int EPI, bool S8, typename OutT, bool F16 = false>
 cudaError_t launch_gemm_inst(const GemmLaunch& g) {
   constexpr bool kLn = EPI == kEpiResidLN || EPI == kEpiResidLNG;
   using C = GemmCfg<BN, S8, kLn, gemm_epi_warps<BN, EPI, S8>(), EPI == kEpiResidLN>;
-  auto kern = gemm_tc_kernel<BN, EPI, S8, OutT>;
+  auto kern = gemm_tc_kernel<BN, EPI, S8, OutT, F16>;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<uint64_t> attr_done{0};  // one bit per device
@@ -82,38 +86,41 @@ cudaError_t launch_gemm_inst(const GemmLaunch& g) {
   }
 }
 
-template <bool S8, int BN>
+template <bool S8, int BN, bool F16>
 cudaError_t launch_gemm_bn(const GemmLaunch& g) {
-  using Bf = __nv_bfloat16;
-  if constexpr (!S8) {
+  using H = __half;
+  if constexpr (!S8 && F16) {
     switch (g.epi) {
       case kEpiStore:
-        return g.out_f32 ? launch_gemm_inst<BN, kEpiStore, false, float>(g)
-                         : launch_gemm_inst<BN, kEpiStore, false, Bf>(g);
+        return g.out_f32 ? launch_gemm_inst<BN, kEpiStore, false, float, true>(g)
+                         : launch_gemm_inst<BN, kEpiStore, false, H, true>(g);
       case kEpiRope:
-        return g.out_f32 ? launch_gemm_inst<BN, kEpiRope, false, float>(g)
-                         : launch_gemm_inst<BN, kEpiRope, false, Bf>(g);
-      case kEpiGelu: return launch_gemm_inst<BN, kEpiGelu, false, Bf>(g);
+        return g.out_f32 ? launch_gemm_inst<BN, kEpiRope, false, float, true>(g)
+                         : launch_gemm_inst<BN, kEpiRope, false, H, true>(g);
+      case kEpiGelu: return launch_gemm_inst<BN, kEpiGelu, false, H, true>(g);
       case kEpiSwiglu:
-        if constexpr (BN != 192) return launch_gemm_inst<BN, kEpiSwiglu, false, Bf>(g);
+        if constexpr (BN != 192) return launch_gemm_inst<BN, kEpiSwiglu, false, H, true>(g);
         else return cudaErrorInvalidValue;
-      case kEpiResid: return launch_gemm_inst<BN, kEpiResid, false, float>(g);
+      case kEpiResid: return launch_gemm_inst<BN, kEpiResid, false, float, true>(g);
       case kEpiResidLN:
         // Long-K GEMMs (fc2) take the global-residual variant and its extra
         // pipeline stage; short ones (out) the TMA-loaded residual tile.
         if constexpr (BN == 128 || BN == 192)
-          return g.K >= 1024 ? launch_gemm_inst<BN, kEpiResidLNG, false, Bf>(g)
-                             : launch_gemm_inst<BN, kEpiResidLN, false, Bf>(g);
+          return g.K >= 1024 ? launch_gemm_inst<BN, kEpiResidLNG, false, H, true>(g)
+                             : launch_gemm_inst<BN, kEpiResidLN, false, H, true>(g);
         else return cudaErrorInvalidValue;
     }
+  } else if constexpr (!S8) {
+    // The MatMulT seam: f32 output, bias only.
+    if (g.epi == kEpiStore && g.out_f32) return launch_gemm_inst<BN, kEpiStore, false, float>(g);
   } else {
     switch (g.epi) {
       case kEpiStore:
         return g.out_f32 ? launch_gemm_inst<BN, kEpiStore, true, float>(g)
-                         : launch_gemm_inst<BN, kEpiStore, true, Bf>(g);
+                         : launch_gemm_inst<BN, kEpiStore, true, __nv_bfloat16>(g);
       case kEpiRope:
         return g.out_f32 ? launch_gemm_inst<BN, kEpiRope, true, float>(g)
-                         : launch_gemm_inst<BN, kEpiRope, true, Bf>(g);
+                         : launch_gemm_inst<BN, kEpiRope, true, __nv_bfloat16>(g);
       case kEpiGelu: return launch_gemm_inst<BN, kEpiGelu, true, float>(g);
       case kEpiSwiglu:
         if constexpr (BN != 192) return launch_gemm_inst<BN, kEpiSwiglu, true, float>(g);
@@ -124,13 +131,13 @@ cudaError_t launch_gemm_bn(const GemmLaunch& g) {
   return cudaErrorInvalidValue;
 }
 
-template <bool S8>
+template <bool S8, bool F16>
 cudaError_t launch_gemm_any(const GemmLaunch& g) {
   switch (g.bn) {
-    case 64: return launch_gemm_bn<S8, 64>(g);
-    case 128: return launch_gemm_bn<S8, 128>(g);
-    case 192: return launch_gemm_bn<S8, 192>(g);
-    case 256: return launch_gemm_bn<S8, 256>(g);
+    case 64: return launch_gemm_bn<S8, 64, F16>(g);
+    case 128: return launch_gemm_bn<S8, 128, F16>(g);
+    case 192: return launch_gemm_bn<S8, 192, F16>(g);
+    case 256: return launch_gemm_bn<S8, 256, F16>(g);
   }
   return cudaErrorInvalidValue;
 }

@@ -2,5 +2,5 @@
 #include "gemm_launch.cuh"
 
 namespace futon {
-cudaError_t launch_gemm_s8(const GemmLaunch& g) { return launch_gemm_any<true>(g); }
+cudaError_t launch_gemm_s8(const GemmLaunch& g) { return launch_gemm_any<true, false>(g); }
 }  // namespace futon

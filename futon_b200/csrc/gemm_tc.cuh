@@ -55,9 +55,9 @@ struct EpiParams {
   void* out;             // bf16 or f32 output, row stride ldo elements
   int ldo;
   const float* bias;     // [N] (interleaved like W for kEpiSwiglu) or null
-  const void* resid;     // kEpiResid / kEpiResidLN: [M, ldr], f32 or bf16 (resid_bf16)
+  const void* resid;     // kEpiResid / kEpiResidLN: [M, ldr], f32, bf16 or f16 (resid_kind)
   int ldr;
-  int resid_bf16;
+  int resid_kind;        // kResidF32, kResidBf16 or kResidF16
   const float* a_scale;  // int8 path: per-row activation scales [M]
   const float* w_scale;  // int8 path: per-row weight scales [N]
   const float* ln_w;     // kEpiResidLN: LayerNorm γ, β [N], eps
@@ -75,6 +75,8 @@ struct EpiParams {
   int nseq;
   int f16_from;  // TMA-store outputs at columns ≥ f16_from are written as f16 (qkv: V)
 };
+
+enum ResidKind : int { kResidF32 = 0, kResidBf16 = 1, kResidF16 = 2 };
 
 // Peer slots per tile parity in the LayerNorm row-statistics exchange: at
 // most 4 CTAs (N ≤ 4 · 192 columns) share a row tile.
@@ -174,10 +176,33 @@ template <> __device__ __forceinline__ void store32<__nv_bfloat16>(__nv_bfloat16
   for (int i = 0; i < 4; ++i) d4[i] = pack8_bf16(v + 8 * i);
 }
 
+template <> __device__ __forceinline__ void store32<__half>(__half* dst, const float (&v)[32]) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d4[i] = pack8_f16(v + 8 * i);
+}
+
 template <typename T> __device__ __forceinline__ void store1(T* dst, float v);
 template <> __device__ __forceinline__ void store1<float>(float* dst, float v) { *dst = v; }
 template <> __device__ __forceinline__ void store1<__nv_bfloat16>(__nv_bfloat16* dst, float v) {
   *dst = __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ void store1<__half>(__half* dst, float v) {
+  *dst = __float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f));
+}
+
+// Two 16-bit values of one 32-bit word (low half first) as f32: f16 (F16)
+// or bf16.
+template <bool F16>
+__device__ __forceinline__ void unpack2_16(uint32_t w, float& lo, float& hi) {
+  if constexpr (F16) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    lo = f.x;
+    hi = f.y;
+  } else {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xFFFF0000u);
+  }
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -290,19 +315,18 @@ struct DirectSink {
 
 // 32 consecutive residual values of one row (f32 or bf16).
 __device__ __forceinline__ void load_resid32(const EpiParams& ep, int row, int col, float (&r)[32]) {
-  if (ep.resid_bf16) {
+  if (ep.resid_kind != kResidF32) {
     const uint4* rp = reinterpret_cast<const uint4*>(
-        reinterpret_cast<const __nv_bfloat16*>(ep.resid) + (size_t)row * ep.ldr + col);
+        reinterpret_cast<const uint16_t*>(ep.resid) + (size_t)row * ep.ldr + col);
+    const bool f16 = ep.resid_kind == kResidF16;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const uint4 q = rp[i];
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&w[j]);
-        const float2 f = __bfloat1622float2(b2);
-        r[8 * i + 2 * j] = f.x;
-        r[8 * i + 2 * j + 1] = f.y;
+        if (f16) unpack2_16<true>(w[j], r[8 * i + 2 * j], r[8 * i + 2 * j + 1]);
+        else unpack2_16<false>(w[j], r[8 * i + 2 * j], r[8 * i + 2 * j + 1]);
       }
     }
   } else {
@@ -601,13 +625,13 @@ struct LnPeers {
 // once the residual has been read. Returns false if a peer's sums did not
 // arrive in time.
 // Residual chunk (32 bf16 of one row) from global memory; zeros past M.
-__device__ __forceinline__ void resid_fetch(const __nv_bfloat16* p, bool ok, uint4 (&dst)[4]) {
+__device__ __forceinline__ void resid_fetch(const uint16_t* p, bool ok, uint4 (&dst)[4]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i)
     dst[i] = ok ? reinterpret_cast<const uint4*>(p)[i] : make_uint4(0u, 0u, 0u, 0u);
 }
 
-template <int BN, int kParts, bool kSmemResid, typename Sink, typename Done>
+template <int BN, int kParts, bool kSmemResid, bool F16, typename Sink, typename Done>
 __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int row0, int M, int N,
                                                   int n0, int part, int quarter, int lane,
                                                   const EpiParams& ep, double2* red, Sink& sink,
@@ -645,7 +669,7 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
         w[4 * i + 3] = rg[k & 1][i].w;
       }
       if (k + 2 < kChunks)
-        resid_fetch(reinterpret_cast<const __nv_bfloat16*>(ep.resid) + (size_t)row * ep.ldr + n0 +
+        resid_fetch(reinterpret_cast<const uint16_t*>(ep.resid) + (size_t)row * ep.ldr + n0 +
                         c + 64,
                     row_ok, rg[k & 1]);
     }
@@ -661,9 +685,9 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int i = 2 * q + h;
-        // bf16 pair → f32 pair: the low half moves up, the high half is masked.
-        const uint64_t r2 =
-            f2_pack(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+        float rlo, rhi;
+        unpack2_16<F16>(w[i], rlo, rhi);
+        const uint64_t r2 = f2_pack(rlo, rhi);
         uint64_t v2 = f2_pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
         v2 = f2_add(v2, h ? f2_pack(bq.z, bq.w) : f2_pack(bq.x, bq.y));
         v2 = f2_add(v2, r2);
@@ -700,11 +724,15 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
   if (px.peers > 1) {
     const uint32_t par = (uint32_t)(it & 1);
     const uint32_t cell = px.xbuf + ((par * kLnPeerSlots + px.rank) * 128 + slot) * 16;
+    // This tile's phase of the exchange barrier completes on one local
+    // arrival that announces the bytes the peers send (16 per row and peer;
+    // their stores may land before or after it).
+    if (part == 0 && quarter == 0 && lane == 0)
+      mbar_arrive_expect_tx(px.xfull + 8 * par, 128u * 16u * (uint32_t)(px.peers - 1));
     if (part == 0) {
       for (int r = 0; r < px.peers; ++r) {
         if (r == (int)px.rank) continue;
-        st_cluster_f64x2(mapa_shared(cell, r), t1, t2);
-        mbar_arrive_cluster(mapa_shared(px.xfull + 8 * par, r));
+        st_async_f64x2(mapa_shared(cell, r), t1, t2, mapa_shared(px.xfull + 8 * par, r));
       }
     }
     if (!mbar_wait_cluster_bounded(px.xfull + 8 * par, (uint32_t)(it >> 1) & 1u, px.err,
@@ -757,7 +785,7 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
   return true;
 }
 
-template <int BN, int EPI, bool S8, typename OutT>
+template <int BN, int EPI, bool S8, typename OutT, bool F16 = false>
 __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
@@ -813,8 +841,9 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&accf_bar[a]), 1);
       mbar_init(smem_u32(&acce_bar[a]), C::kEpiWarps);  // one arrive per epilogue warp
-      // One arrive per row from every other slice of the row tile.
-      if (kLnSlices) mbar_init(smem_u32(&xfull_bar[a]), (uint32_t)(128 * (peers - 1)));
+      // One local arrival per tile, plus the peers' asynchronous stores
+      // counted in bytes (epilogue_resid_ln).
+      if (kLnSlices) mbar_init(smem_u32(&xfull_bar[a]), 1u);
     }
     if (kResidTma) {
       mbar_init(smem_u32(rfull_bar), 1);
@@ -908,7 +937,9 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = make_idesc(S8 ? 2u : 1u, 1u, 128u, (uint32_t)C::kMmaN);
+      // Operand format: S8 (kind::i8), else F16 = 0 / BF16 = 1 (kind::f16).
+      constexpr uint32_t idesc =
+          make_idesc(S8 ? 2u : 1u, (S8 || !F16) ? 1u : 0u, 128u, (uint32_t)C::kMmaN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -938,7 +969,7 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
             if constexpr (S8)
               mma_s8(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
             else
-              mma_bf16(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
+              mma_f16kind(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
           }
           mma_commit(smem_u32(&empty_bar[stage]));
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
@@ -960,8 +991,8 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     // ---------------- epilogue warps 2..9 ----------------
     const int quarter = warp & 3;        // TMEM lanes [32*quarter, 32*quarter+32)
     const int part = (warp - 2) >> 2;    // which share of the column chunks
-    TmaSink<2> tsink{extra + (warp - 2) * 4096, &tmO, lane, 0, ep.f16_from};
-    TmaSink<1> lsink{extra + C::kRedBytes + (warp - 2) * 2048, &tmO, lane, 0, 1 << 30};
+    TmaSink<2> tsink{extra + (warp - 2) * 4096, &tmO, lane, 0, F16 ? 0 : ep.f16_from};
+    TmaSink<1> lsink{extra + C::kRedBytes + (warp - 2) * 2048, &tmO, lane, 0, F16 ? 0 : 1 << 30};
     const LnPeers px{peers, rank, smem_u32(smem + C::kXchOffset), smem_u32(xfull_bar), err,
                      abort_flag};
     int it = 0;
@@ -975,8 +1006,8 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
       // tile's MMAs finish.
       uint4 rg[2][4];
       if constexpr (kLnSlices && !kResidTma) {
-        const __nv_bfloat16* rp = reinterpret_cast<const __nv_bfloat16*>(ep.resid) +
-                                  (size_t)row * ep.ldr + nb * BN + part * (BN / C::kParts);
+        const uint16_t* rp = reinterpret_cast<const uint16_t*>(ep.resid) +
+                             (size_t)row * ep.ldr + nb * BN + part * (BN / C::kParts);
         resid_fetch(rp, row < M, rg[0]);
         resid_fetch(rp + 32, row < M, rg[1]);
       }
@@ -996,7 +1027,7 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
             if (lane == 0) mbar_arrive(smem_u32(rempty_bar));
           }
         };
-        if (!epilogue_resid_ln<BN, C::kParts, kResidTma>(
+        if (!epilogue_resid_ln<BN, C::kParts, kResidTma, F16>(
                 taddr, row, row0, M, N, nb * BN, part, quarter, lane, ep, red, lsink, rrow, rg,
                 smem_u32(smem + C::kColsOffset), resid_done, px, it))
           break;
@@ -1011,11 +1042,15 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
     }
-    if constexpr (EPI == kEpiResidLN) lsink.drain();
+    // The last tile's TMA stores read their staging before the CTA exits.
+    if constexpr (kLnSlices) lsink.drain();
     else if constexpr (kTmaStore) tsink.drain();
   }
 
   __syncthreads();
+  // No CTA of a LayerNorm cluster leaves while a peer may still store into
+  // its shared memory (every wait above is bounded, so all CTAs get here).
+  if constexpr (kLnSlices) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);

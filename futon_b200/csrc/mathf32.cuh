@@ -118,7 +118,7 @@ FUTON_HD __forceinline__ float sigmoid_f32(float x) {
   return fdiv(1.0f, fadd(1.0f, exp_f32(e)));
 }
 
-// Fast variants for the bf16 path, whose outputs are rounded to bf16 (2^-9
+// Fast variants for the float path, whose outputs are rounded to f16 (2^-11
 // relative) right after. GELU: erfc(z) = 1 / P(z)^16 with the degree-6
 // polynomial of Abramowitz & Stegun 7.1.28 (|error| ≤ 3e-7; ≤ 7.1e-7 on
 // gelu over [−12, 12] in f32), one hardware reciprocal and no exponential;

@@ -14,9 +14,11 @@
 // variance accumulate in float64, inv = float32(1/sqrt(var + eps)), and the
 // apply step (x − mean)·inv·γ + β runs as separately rounded f32 ops.
 // Each LayerNorm writes the f32 row (the residual for the next block), its
-// bf16 copy (the next GEMM's A operand) and, on the int8 path, the row's
+// f16 copy (the next GEMM's A operand) and, on the int8 path, the row's
 // int8 codes and scale.
 #pragma once
+
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "mathf32.cuh"
@@ -91,7 +93,14 @@ __device__ __forceinline__ void warp_row_stats_seq(const float4 (&v)[kMaxRowVec]
   __syncwarp();  // srow is free for the warp's next row
 }
 
-// LayerNorm of a row held as float4 registers; writes f32, bf16 and
+// Two f32 values as an f16x2 word (low half first), saturating at ±65504.
+__device__ __forceinline__ uint32_t pack2_f16_sat(float lo, float hi) {
+  uint32_t w;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(w) : "f"(hi), "f"(lo));
+  return w;
+}
+
+// LayerNorm of a row held as float4 registers; writes f32, f16 and
 // optionally int8 outputs. SEQ: statistics by warp_row_stats_seq (srow: this
 // warp's h floats of shared memory); otherwise a warp-parallel float64 sum.
 template <bool SEQ = false>
@@ -99,7 +108,7 @@ __device__ __forceinline__ void warp_layernorm_store(float4 (&v)[kMaxRowVec], in
                                                      const float* __restrict__ w,
                                                      const float* __restrict__ b, float eps,
                                                      float* __restrict__ xo,
-                                                     __nv_bfloat16* __restrict__ xbo,
+                                                     __half* __restrict__ xbo,
                                                      int8_t* __restrict__ xq,
                                                      float* __restrict__ xs,
                                                      float* srow = nullptr) {
@@ -140,12 +149,9 @@ __device__ __forceinline__ void warp_layernorm_store(float4 (&v)[kMaxRowVec], in
       y.w = fadd(fmul(fmul(fsub(v[j].w, mf), inv), g.w), be.w);
       v[j] = y;
       if (xo) reinterpret_cast<float4*>(xo)[c4] = y;
-      if (xbo) {
-        __nv_bfloat162 p0 = __floats2bfloat162_rn(y.x, y.y);
-        __nv_bfloat162 p1 = __floats2bfloat162_rn(y.z, y.w);
-        uint2 pk = make_uint2(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1));
-        reinterpret_cast<uint2*>(xbo)[c4] = pk;
-      }
+      if (xbo)
+        reinterpret_cast<uint2*>(xbo)[c4] = make_uint2(pack2_f16_sat(y.x, y.y),
+                                                       pack2_f16_sat(y.z, y.w));
     }
   }
   if (xq) warp_quant_row(v, n4, lane, xq, xs);
@@ -161,7 +167,7 @@ __global__ void __launch_bounds__(256)
                     int h, int vocab, int* __restrict__ err, const float* __restrict__ word, const float* __restrict__ type0,
                     const float* __restrict__ pos, const float* __restrict__ w,
                     const float* __restrict__ b, float eps, float* __restrict__ x,
-                    __nv_bfloat16* __restrict__ xb, int8_t* __restrict__ xq,
+                    __half* __restrict__ xb, int8_t* __restrict__ xq,
                     float* __restrict__ xs) {
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
@@ -227,7 +233,7 @@ template <bool SEQ = false>
 __global__ void __launch_bounds__(256)
     layernorm_kernel(const float* __restrict__ in, int rows, int h, const float* __restrict__ w,
                      const float* __restrict__ b, float eps, float* __restrict__ x,
-                     __nv_bfloat16* __restrict__ xb, int8_t* __restrict__ xq,
+                     __half* __restrict__ xb, int8_t* __restrict__ xq,
                      float* __restrict__ xs) {
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
@@ -290,7 +296,7 @@ __global__ void __launch_bounds__(256)
 }
 
 // Copies the CLS row (first token) of every sequence into a compact buffer
-// (f32 or bf16 rows; 16-byte vectors).
+// (f32 or f16 rows; 16-byte vectors).
 template <typename T>
 __global__ void gather_rows_kernel(const T* __restrict__ x, const int* __restrict__ cu, int nseq,
                                    int h, T* __restrict__ xc) {
@@ -366,6 +372,21 @@ __global__ void __launch_bounds__(256)
   }
   for (int c = threadIdx.x; c < d; c += blockDim.x)
     out[(size_t)s * d + c] = normalize ? fmul(pooled[c], scale) : pooled[c];
+}
+
+// f32 → f16 (round to nearest, saturating at ±65504): GEMM weights of the
+// float path.
+__global__ void f32_to_f16_kernel(const float* __restrict__ in, size_t n, __half* __restrict__ out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    out[i] = __float2half_rn(fminf(fmaxf(in[i], -65504.0f), 65504.0f));
+}
+
+// f16 → f32 (exact): F16 weights the int8 path quantises as f32 rows.
+__global__ void f16_to_f32_kernel(const __half* __restrict__ in, size_t n, float* __restrict__ out) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    out[i] = __half2float(in[i]);
 }
 
 __global__ void f32_to_bf16_kernel(const float* __restrict__ in, size_t n,

@@ -21,7 +21,7 @@ if str(ROOT) not in sys.path:
 GOLDEN = ROOT / "tests" / "golden" / "toy"
 
 # Reference gates (native/model_test.go:19-22) for the CPU oracle, and the
-# north-star gate for the bf16 tensor-core path.
+# north-star gate for the f16 tensor-core path.
 TOY_COSINE_MIN = 0.99999
 TOY_ABS_TOL = 2e-4
 GPU_COSINE_MIN = 0.9999

@@ -2,8 +2,8 @@
 bit for bit: the attention (futon_b200/csrc/attn_exact.cuh) against the
 oracle's attendHead (native/model.go:646-739) in the avx2Kernel summation
 order, and the activations (futon_b200/csrc/mathf32.cuh: expF32, geluF32,
-sigmoidF32, native/mathf32.go:40-120). Also the accuracy of the bf16 path's
-fast GELU formula against the exact-erf GELU.
+sigmoidF32, native/mathf32.go:40-120). Also the accuracy of the float
+path's fast GELU formula against the exact-erf GELU.
 
 tests/host/exact_host.cu runs the routines the device kernels call,
 over the same 64-key tiles in the same order, as host code built with nvcc
@@ -103,7 +103,7 @@ def test_activation_host_matches_oracle(fx, name, ref):
 
 
 def test_fast_gelu_formula_error_bound(fx):
-    """The bf16 path's GELU (Abramowitz & Stegun 7.1.28 in gelu_fast2) stays
+    """The float path's GELU (Abramowitz & Stegun 7.1.28 in gelu_fast2) stays
     within 7.1e-7 of the exact-erf GELU over [−12, 12] (float64 reference).
     The device evaluates the same formula with rcp.approx (within 1 ulp of
     the exact reciprocal used here), far below that bound."""

@@ -5,8 +5,8 @@ These run only on request (`FUTON_TEST_ATTN_VARIANTS=1 pytest -m
 gpu_variant`): the default configuration never reaches the variants, so the
 default `-m gpu` suite does not select them.
 
-- tc, tc2: the tcgen05 attention kernels (tc2: separate q·k and v rings
-  and two softmax warpgroups; head_dim 32 or 64 with an even head count);
+- tc2: the tcgen05 attention kernel (separate q·k and v rings and two
+  softmax warpgroups; head_dim 32 or 64 with an even head count);
   parity with the oracle (cosine gate) and batch invariance (a sequence's
   vector does not depend on what it is packed with).
 - FUTON_CUDA_Q8_ATTN=split: the int8 path's split-precision tensor-core
@@ -67,7 +67,7 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("kernel", ["tc", "tc2"])
+@pytest.mark.parametrize("kernel", ["tc2"])
 @pytest.mark.parametrize("arch,inputs,nseq,layers", CASES)
 def test_tc_vs_oracle(gpu, monkeypatch, kernel, arch, inputs, nseq, layers):
     cfg, w = weights(arch, layers)
@@ -79,7 +79,7 @@ def test_tc_vs_oracle(gpu, monkeypatch, kernel, arch, inputs, nseq, layers):
     assert cs.min() >= GPU_COSINE_MIN, f"{arch}: {kernel} attention min cosine {cs.min():.7f}"
 
 
-@pytest.mark.parametrize("kernel", ["tc", "tc2"])
+@pytest.mark.parametrize("kernel", ["tc2"])
 def test_tc_batch_invariance(gpu, monkeypatch, kernel):
     cfg, w = weights("bge", 2)
     ids, cu = synth.make_inputs("c4", nseq=24, vocab=cfg.vocab_size)
