@@ -205,17 +205,36 @@ __global__ void __launch_bounds__(64)
     }
   }
   if (!live) return;
-  // softmaxScaled up to the sum (exact_softmax_row without its final scaling).
+  // softmaxScaled up to the sum (exact_softmax_row without its final
+  // scaling), eight scores in flight: every load of a group is issued
+  // before the group's first store (the row's scores in key order, the f64
+  // sum still taken one key after another).
   const float ms = fmul(mx, scale);
   double sum = 0.0;
-  for (int j = 0; j < L; ++j) {
+  constexpr int kG = 8;
+  int j = 0;
+  for (; j + kG <= L; j += kG) {
+    float v[kG];
+#pragma unroll
+    for (int u = 0; u < kG; ++u) v[u] = prow[(size_t)(j + u) * nq];
+#pragma unroll
+    for (int u = 0; u < kG; ++u) {
+      float dd = fsub(fmul(v[u], scale), ms);
+      if (dd < kExpClampLo) dd = kExpClampLo;
+      v[u] = exp_f32(dd);
+      sum += (double)v[u];
+    }
+#pragma unroll
+    for (int u = 0; u < kG; ++u) prow[(size_t)(j + u) * nq] = v[u];
+  }
+  for (; j < L; ++j) {
     float dd = fsub(fmul(prow[(size_t)j * nq], scale), ms);
     if (dd < kExpClampLo) dd = kExpClampLo;
     const float e = exp_f32(dd);
     prow[(size_t)j * nq] = e;
     sum += (double)e;
   }
-  for (int j = L; j < kp; ++j) prow[(size_t)j * nq] = 0.0f;
+  for (j = L; j < kp; ++j) prow[(size_t)j * nq] = 0.0f;
   const size_t irow = cls_mode ? (size_t)tile.seq : (size_t)(s0 + r);
   pinv[(size_t)blockIdx.y * pinv_ld + irow] = (float)(1.0 / sum);
 }
@@ -263,18 +282,36 @@ __global__ void __launch_bounds__(4 * HD)
   for (int k0 = 0; k0 < kp; k0 += kT) {
     const int n = min(kT, kp - k0);  // a multiple of 8
     __syncthreads();
-    for (int i = threadIdx.x; i < n * (HD / 4); i += blockDim.x) {
-      const int jj = i / (HD / 4), c = i % (HD / 4);
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + jj < L)
-        v = reinterpret_cast<const float4*>(qkv + (size_t)(s0 + k0 + jj) * ld + 2 * hidden +
-                                            head * HD)[c];
-      reinterpret_cast<float4*>(sV)[i] = v;
-    }
-    for (int i = threadIdx.x; i < 32 * n; i += blockDim.x) {
-      const int jj = i >> 5, qi = i & 31;
-      const int rr = rbase + qi;
-      sP[jj * 32 + qi] = rr < nq ? fmul(pblk[(size_t)(k0 + jj) * nq + rr], sInv[qi]) : 0.0f;
+    // V (n × HD) and P (n × 32) of the tile: every thread's loads are
+    // issued before its stores (n·HD/4 and 32·n are multiples of blockDim).
+    {
+      constexpr int kVI = kT * (HD / 4) / (4 * HD), kPI = kT * 32 / (4 * HD);
+      float4 vv[kVI];
+      float pp[kPI];
+#pragma unroll
+      for (int u = 0; u < kVI; ++u) {
+        const int i = (int)threadIdx.x + u * (int)blockDim.x;
+        const int jj = i / (HD / 4), c = i % (HD / 4);
+        vv[u] = (jj < n && k0 + jj < L)
+                    ? reinterpret_cast<const float4*>(qkv + (size_t)(s0 + k0 + jj) * ld +
+                                                      2 * hidden + head * HD)[c]
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kPI; ++u) {
+        const int i = (int)threadIdx.x + u * (int)blockDim.x;
+        const int jj = i >> 5, qi = i & 31;
+        const int rr = rbase + qi;
+        pp[u] = (jj < n && rr < nq) ? pblk[(size_t)(k0 + jj) * nq + rr] : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kVI; ++u)
+        reinterpret_cast<float4*>(sV)[(int)threadIdx.x + u * (int)blockDim.x] = vv[u];
+#pragma unroll
+      for (int u = 0; u < kPI; ++u) {
+        const int i = (int)threadIdx.x + u * (int)blockDim.x;
+        sP[i] = fmul(pp[u], sInv[i & 31]);
+      }
     }
     __syncthreads();
     for (int j8 = 0; j8 < n; j8 += 8) {
