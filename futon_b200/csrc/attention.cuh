@@ -581,7 +581,7 @@ __global__ void __launch_bounds__(128, attn_heads_min_ctas<HD, NH>())
   const uint32_t full = sbase + SM::kBarOffset;           // kAttnRing mbarriers
   __shared__ int abort_flag;
 
-  const AttnTile tile = cls_mode ? AttnTile{(int)blockIdx.x, 0} : tiles[blockIdx.x];
+  const AttnTile tile = tiles[blockIdx.x];  // cls_mode: (sequence, 0)
   const int s0 = cu_seqlens[tile.seq];
   const int L = cu_seqlens[tile.seq + 1] - s0;
   const int qlim = cls_mode ? 1 : L;  // query positions < qlim are real

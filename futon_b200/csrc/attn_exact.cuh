@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(64)
                               int pinv_ld) {
   static_assert(HD % 8 == 0, "head_dim must be a multiple of 8");
   __shared__ __align__(16) float sK[kExactKeyTile * HD];
-  const AttnTile tile = cls_mode ? AttnTile{(int)blockIdx.x, 0} : tiles[blockIdx.x];
+  const AttnTile tile = tiles[blockIdx.x];  // cls_mode: (sequence, 0)
   const int head = head0 + (int)blockIdx.y;
   const int s0 = cu[tile.seq], L = cu[tile.seq + 1] - s0;
   const int nq = cls_mode ? 1 : L, kp = (L + 7) & ~7;
@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(4 * HD)
   __shared__ __align__(16) float sV[kT * HD];
   __shared__ __align__(16) float sP[kT * 32];  // [key][row of the half]
   __shared__ float sInv[32];
-  const AttnTile tile = cls_mode ? AttnTile{(int)blockIdx.x, 0} : tiles[blockIdx.x];
+  const AttnTile tile = tiles[blockIdx.x];  // cls_mode: (sequence, 0)
   const int head = head0 + (int)blockIdx.z;
   const int s0 = cu[tile.seq], L = cu[tile.seq + 1] - s0;
   const int nq = cls_mode ? 1 : L, kp = (L + 7) & ~7;

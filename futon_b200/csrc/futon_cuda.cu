@@ -856,6 +856,7 @@ int attn_split_ways(const futon_model& m, const DevCtx& d, int tiles, int ngroup
 struct AttnPlan {
   const AttnTile* tiles;
   int ntiles;
+  const AttnTile* cls_tiles;  // one (sequence, 0) per sequence, longest first
   const AttnWindow* wins;
   int nwin;
   const AttnSeg* segs;
@@ -884,7 +885,8 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
   const float scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
   constexpr bool kSplit = sizeof(InT) == 4;
   const bool tc_hd = hd == 32 || hd == 64;
-  const AttnTile* tiles = plan.tiles;
+  // The CLS-only layer walks its own list: (sequence, query 0), longest first.
+  const AttnTile* tiles = cls_only ? plan.cls_tiles : plan.tiles;
   const int ntiles = plan.ntiles;
   if constexpr (!kSplit) {
     if (m.attn_kind == kAttnTc2 && tc_hd && H % 2 == 0 && !cls_only) {
@@ -1124,7 +1126,7 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       ProfScope prof(d, st, kStLayerNorm, 0.0, (double)rows * h * (q8 ? 9.0 : (f32_copy ? 10.0 : 6.0)));
       float* xo = q8 ? w.x : (f32_copy ? w.xf : nullptr);
       if (q8 && m.q8_exact_attn)
-        layernorm_kernel<true><<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(
+        layernorm_kernel<true><<<grid_rows(rows, 256, d.num_sms), 256, 0, st>>>(
             w.tmp, rows, h, lnw, lnb, eps, xo, nullptr, w.xq, w.xs);
       else
         layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(
@@ -1194,7 +1196,7 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
 struct MicroBatch {
   int s0, s1;   // sequences [s0, s1)
   int t0, t1;   // tokens [t0, t1)
-  size_t cu_off, tile_off, win_off, seg_off;  // int offsets into the meta buffer
+  size_t cu_off, tile_off, cls_off, win_off, seg_off;  // int offsets into the meta buffer
   int ntiles, nwin, nseg;
   double sum_l2;            // Σ L² (profiler)
   // Exact int8-path attention: offsets of the P row blocks (meta) and totals.
@@ -1303,6 +1305,8 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, bool exact_p,
     meta += align_up((size_t)(mb.s1 - mb.s0 + 1), 4);
     mb.tile_off = meta;
     meta += align_up((size_t)ntiles * 2, 4);
+    mb.cls_off = meta;
+    meta += align_up((size_t)(mb.s1 - mb.s0) * 2, 4);
     mb.win_off = meta;
     meta += align_up((size_t)mb.nwin * 6, 4);
     mb.seg_off = meta;
@@ -1334,13 +1338,29 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, bool exact_p,
   for (const MicroBatch& mb : mbs) {
     int* hc = d.h_meta + mb.cu_off;
     for (int s = mb.s0; s <= mb.s1; ++s) hc[s - mb.s0] = cu[s] - mb.t0;
+    // Tiles longest sequence first (the CTAs launch in list order, so the
+    // tiles with the most key blocks start early instead of trailing the
+    // launch); every tile is computed the same way in any order.
     AttnTile* ht = reinterpret_cast<AttnTile*>(d.h_meta + mb.tile_off);
     int k = 0;
     for (int s = mb.s0; s < mb.s1; ++s)
       for (int q0 = 0; q0 < cu[s + 1] - cu[s]; q0 += 64) ht[k++] = AttnTile{s - mb.s0, q0};
+    const int* cl = cu + mb.s0;
+    auto longer = [cl](const AttnTile& a, const AttnTile& b) {
+      return cl[a.seq + 1] - cl[a.seq] > cl[b.seq + 1] - cl[b.seq];
+    };
+    std::stable_sort(ht, ht + k, longer);
+    // The CLS-only last layer: one query row per sequence, same order.
+    AttnTile* hc2 = reinterpret_cast<AttnTile*>(d.h_meta + mb.cls_off);
+    for (int s = mb.s0; s < mb.s1; ++s) hc2[s - mb.s0] = AttnTile{s - mb.s0, 0};
+    std::stable_sort(hc2, hc2 + (mb.s1 - mb.s0), longer);
     int nseg = 0;
-    plan_windows(cu, mb.s0, mb.s1, mb.t0, reinterpret_cast<AttnWindow*>(d.h_meta + mb.win_off),
-                 reinterpret_cast<AttnSeg*>(d.h_meta + mb.seg_off), &nseg);
+    AttnWindow* hw = reinterpret_cast<AttnWindow*>(d.h_meta + mb.win_off);
+    plan_windows(cu, mb.s0, mb.s1, mb.t0, hw, reinterpret_cast<AttnSeg*>(d.h_meta + mb.seg_off),
+                 &nseg);
+    // tcgen05 windows most keys first (each keeps its own segment range).
+    std::stable_sort(hw, hw + mb.nwin,
+                     [](const AttnWindow& a, const AttnWindow& b) { return a.nk > b.nk; });
     if (exact_p) {
       int* po = d.h_meta + mb.poff_off;
       int* pc = d.h_meta + mb.pcls_off;
@@ -1401,6 +1421,7 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
     if (canceled(cancel))
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
     AttnPlan plan{reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
+                  reinterpret_cast<const AttnTile*>(d.d_meta + mb.cls_off),
                   reinterpret_cast<const AttnWindow*>(d.d_meta + mb.win_off), mb.nwin,
                   reinterpret_cast<const AttnSeg*>(d.d_meta + mb.seg_off)};
     if (head_group > 0) {

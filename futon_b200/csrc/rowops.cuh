@@ -100,6 +100,15 @@ __device__ __forceinline__ uint32_t pack2_f16_sat(float lo, float hi) {
   return w;
 }
 
+__device__ __forceinline__ void warp_layernorm_apply(float4 (&v)[kMaxRowVec], int h, int lane,
+                                                     const float* __restrict__ w,
+                                                     const float* __restrict__ b, float eps,
+                                                     double mean, double var,
+                                                     float* __restrict__ xo,
+                                                     __half* __restrict__ xbo,
+                                                     int8_t* __restrict__ xq,
+                                                     float* __restrict__ xs);
+
 // LayerNorm of a row held as float4 registers; writes f32, f16 and
 // optionally int8 outputs. SEQ: statistics by warp_row_stats_seq (srow: this
 // warp's h floats of shared memory); otherwise a warp-parallel float64 sum.
@@ -134,6 +143,56 @@ __device__ __forceinline__ void warp_layernorm_store(float4 (&v)[kMaxRowVec], in
     }
     var = warp_sum_d(var) / (double)h;
   }
+  warp_layernorm_apply(v, h, lane, w, b, eps, mean, var, xo, xbo, xq, xs);
+}
+
+// Row statistics of 32 rows at once in layerNormRows' exact order
+// (model.go:743-769): lane l takes row x + l·h (rows past `n` give 0) and
+// sums it in element order in float64 — mean = Σx / h, then Σ (x − mean)²
+// with every product and sum rounded separately, / h — the same operations,
+// in the same order, as warp_row_stats_seq, one row per lane.
+__device__ __forceinline__ void warp_rows_stats_seq32(const float* __restrict__ x, int n, int h,
+                                                      int lane, double* mean_out,
+                                                      double* var_out) {
+  double mean = 0.0, var = 0.0;
+  if (lane < n) {
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)lane * h);
+    const int n4 = h >> 2;
+    for (int c = 0; c < n4; ++c) {
+      const float4 a = xr[c];
+      mean = __dadd_rn(mean, (double)a.x);
+      mean = __dadd_rn(mean, (double)a.y);
+      mean = __dadd_rn(mean, (double)a.z);
+      mean = __dadd_rn(mean, (double)a.w);
+    }
+    mean = __ddiv_rn(mean, (double)h);
+    for (int c = 0; c < n4; ++c) {
+      const float4 a = xr[c];
+      const float e[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const double d = __dsub_rn((double)e[t], mean);
+        var = __dadd_rn(var, __dmul_rn(d, d));
+      }
+    }
+    var = __ddiv_rn(var, (double)h);
+  }
+  *mean_out = mean;
+  *var_out = var;
+}
+
+// The apply step of a LayerNorm whose statistics are known:
+// y = (x − mean)·inv·γ + β with inv = float32(1/sqrt(var + eps)), then the
+// f32 / f16 / int8 outputs.
+__device__ __forceinline__ void warp_layernorm_apply(float4 (&v)[kMaxRowVec], int h, int lane,
+                                                     const float* __restrict__ w,
+                                                     const float* __restrict__ b, float eps,
+                                                     double mean, double var,
+                                                     float* __restrict__ xo,
+                                                     __half* __restrict__ xbo,
+                                                     int8_t* __restrict__ xq,
+                                                     float* __restrict__ xs) {
+  const int n4 = h >> 2;
   const float inv = (float)(1.0 / sqrt(var + (double)eps));
   const float mf = (float)mean;
 #pragma unroll
@@ -238,21 +297,39 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int n4 = h >> 2;
-  for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
-    const float4* src = reinterpret_cast<const float4*>(in + (size_t)r * h);
-    float4 v[kMaxRowVec];
+  if constexpr (SEQ) {
+    // 32 rows per warp: each lane takes one row's statistics in the
+    // reference's order, then the warp normalises the rows one by one.
+    const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    for (int base = wid * 32; base < rows; base += warps * 32) {
+      const int nr = min(32, rows - base);
+      double mean, var;
+      warp_rows_stats_seq32(in + (size_t)base * h, nr, h, lane, &mean, &var);
+      for (int k = 0; k < nr; ++k) {
+        const int r = base + k;
+        const double mk = __shfl_sync(0xffffffffu, mean, k);
+        const double vk = __shfl_sync(0xffffffffu, var, k);
+        const float4* src = reinterpret_cast<const float4*>(in + (size_t)r * h);
+        float4 v[kMaxRowVec];
 #pragma unroll
-    for (int j = 0; j < kMaxRowVec; ++j) {
-      const int c4 = lane + 32 * j;
-      v[j] = c4 < n4 ? src[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < kMaxRowVec; ++j) {
+          const int c4 = lane + 32 * j;
+          v[j] = c4 < n4 ? src[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        warp_layernorm_apply(v, h, lane, w, b, eps, mk, vk, x ? x + (size_t)r * h : nullptr,
+                             xb ? xb + (size_t)r * h : nullptr, xq ? xq + (size_t)r * h : nullptr,
+                             xq ? xs + r : nullptr);
+      }
     }
-    if constexpr (SEQ) {
-      __shared__ __align__(16) float srows[8][kMaxRowVec * 128];
-      warp_layernorm_store<true>(v, h, lane, w, b, eps, x ? x + (size_t)r * h : nullptr,
-                                 xb ? xb + (size_t)r * h : nullptr,
-                                 xq ? xq + (size_t)r * h : nullptr, xq ? xs + r : nullptr,
-                                 srows[threadIdx.x >> 5]);
-    } else {
+  } else {
+    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+      const float4* src = reinterpret_cast<const float4*>(in + (size_t)r * h);
+      float4 v[kMaxRowVec];
+#pragma unroll
+      for (int j = 0; j < kMaxRowVec; ++j) {
+        const int c4 = lane + 32 * j;
+        v[j] = c4 < n4 ? src[c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
       warp_layernorm_store(v, h, lane, w, b, eps, x ? x + (size_t)r * h : nullptr,
                            xb ? xb + (size_t)r * h : nullptr, xq ? xq + (size_t)r * h : nullptr,
                            xq ? xs + r : nullptr);
