@@ -35,6 +35,7 @@ RUNTIME_OPTIONS = {
     "FUTON_CUDA_ATTN": ("heads", "tc2"),
     "FUTON_CUDA_ATTN_SPLIT": ("1", "0"),
     "FUTON_CUDA_Q8_ATTN": ("exact", "split"),
+    "FUTON_CUDA_GEMM_PAIR": ("0", "1"),
 }
 
 

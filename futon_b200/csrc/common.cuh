@@ -193,6 +193,20 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// The same load issued by either CTA of a CTA pair (cluster ranks 2i, 2i + 1)
+// that feeds one cta_group::2 MMA: the data lands in this CTA's shared memory
+// and the byte count completes `cbar`, a shared::cluster address of an
+// mbarrier in either CTA of the pair (the pair's leader, even rank, counts
+// both CTAs' bytes). No multicast: each CTA fetches its own tile.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map,
+                                                 uint32_t cbar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(cbar), "r"(x), "r"(y)
+      : "memory");
+}
+
 // ----------------------------------------------------------------------------
 // tcgen05: tensor memory and 5th-generation tensor-core MMA
 // ----------------------------------------------------------------------------
@@ -245,6 +259,48 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
       : "memory");
 }
 
+// cta_group::2 forms, for kernels whose MMAs span a CTA pair. A kernel uses
+// one cta_group throughout: allocation, MMA, commit and deallocation. The
+// allocation and deallocation are issued by the same warp of both CTAs (the
+// pair gets the same TMEM address, written to `dst_smem` in each CTA).
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D (+)= A·Bᵀ over a CTA pair, issued by the even CTA only: M = 256 rows, A's
+// rows 0-127 and B's first N/2 rows in the issuing CTA's shared memory, A's
+// rows 128-255 and B's other N/2 rows at the same addresses in its peer; D
+// rows 0-127 land in the issuing CTA's TMEM, rows 128-255 in the peer's,
+// every one of the N columns in both.
+__device__ __forceinline__ void mma_f16kind_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier at shared::cta address `bar` of every CTA in
+// `cta_mask` (the pair) when the pair MMAs issued so far are done.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
 // Loads 32 consecutive f32/s32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -279,7 +335,7 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
 }
 
 // Instruction descriptor (kind::f16 / kind::i8): dense, K-major A and B,
-// M = 128, N = n.
+// M = m (128, or 256 for a CTA pair), N = n.
 //   c_format (bits 4-5):  1 = F32, 2 = S32
 //   a/b_format (7-9, 10-12): kind::f16 0 = F16, 1 = BF16; kind::i8 1 = S8
 //   n_dim (17-22) = N >> 3, m_dim (24-28) = M >> 4

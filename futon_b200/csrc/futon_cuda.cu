@@ -213,6 +213,10 @@ struct GemmWeight {
   float* scale = nullptr;   // int8 only: [n]
   float* bias = nullptr;    // [n] or null
   int n = 0, k = 0, bn = 64;
+  // pair: the f16 forward runs this weight's GEMMs as CTA-pair tiles
+  // (gemm_tc_kernel<..., PAIR>), whose CTAs each stage bn / 2 rows: the
+  // map's box is bn / 2 rows then, else bn (bn / 2 above 256).
+  bool pair = false;
   CUtensorMap map;
 };
 
@@ -243,6 +247,7 @@ struct Workspace {
 struct DevCtx {
   int device = 0;
   int num_sms = 148;
+  bool gemm_pair = false;  // the model's gemm_pair option, read by upload_gemm
   cudaStream_t stream = nullptr;
   std::mutex mu;
   std::vector<void*> allocs;
@@ -328,12 +333,23 @@ struct futon_model {
   // FUTON_CUDA_Q8_ATTN=exact: the int8 path's attention runs in the
   // reference's exact float32 operation order (attn_exact.cuh).
   bool q8_exact_attn = true;
+  // FUTON_CUDA_GEMM_PAIR=1: the float path's GEMMs run as CTA-pair tiles
+  // (M = 256 over two SMs, each staging half of every weight tile).
+  bool gemm_pair = false;
   std::vector<std::unique_ptr<DevCtx>> devs;
 };
 
 namespace {
 
-constexpr int kTokenBudget = 131072;  // tokens per micro-batch
+// Tokens per micro-batch. Measured on the c4 workload (one B200): 131,072 →
+// 524,288 tokens is 3.8 % more embeddings/s (a quarter of the launches, each
+// with its prologue, pipeline fill and drain, and a quarter of the tails);
+// the activations then take ≈ 4.4 GB of workspace for bge-small.
+constexpr int kTokenBudget = 524288;
+// The exact int8 attention's probability scratch per micro-batch (floats):
+// a micro-batch also closes before its Σ pad8(L)·L would pass this, so
+// long-sequence batches stay within int offsets and 4 GiB of scratch.
+constexpr size_t kExactPBudget = (size_t)1 << 30;
 
 // Cancellation checkpoint: entry, every micro-batch, every layer and every
 // layer's FFN (the points where native/model.go checks ctx.Err()). The
@@ -635,7 +651,8 @@ int upload_gemm(DevCtx& d, GemmWeight& g, HostMat w1, const float* b1, HostMat w
     CU_TRY(cudaStreamSynchronize(d.stream));  // hb is released on return
   }
   g.bn = two ? 2 * half : (ln_slices ? ln_slice_cols(n) : pick_bn(n));
-  const uint32_t box = g.bn <= 256 ? (uint32_t)g.bn : (uint32_t)g.bn / 2;
+  g.pair = !q8 && d.gemm_pair && g.bn <= 256;
+  const uint32_t box = (g.pair || g.bn > 256) ? (uint32_t)g.bn / 2 : (uint32_t)g.bn;
   if (!make_operand_map(&g.map, g.w, q8 ? kElemS8 : kElemF16, (uint64_t)n, (uint64_t)k, box))
     return set_err(err, errlen, FUTON_ECUDA, "native: cuTensorMapEncodeTiled failed for a weight");
   return FUTON_OK;
@@ -785,6 +802,7 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   g.epi = o.epi;
   g.out_f32 = o.out_f32;
   g.f16 = !s8;
+  g.pair = w.pair;
   g.ep.out = o.out;
   g.ep.ldo = o.ldo;
   g.ep.bias = w.bias;
@@ -840,6 +858,10 @@ void read_attn_env(futon_model& m) {
   if (const char* v = std::getenv("FUTON_CUDA_Q8_ATTN")) {
     if (!strcmp(v, "split")) m.q8_exact_attn = false;
     else if (!strcmp(v, "exact")) m.q8_exact_attn = true;
+  }
+  if (const char* v = std::getenv("FUTON_CUDA_GEMM_PAIR")) {
+    if (!strcmp(v, "1")) m.gemm_pair = true;
+    else if (!strcmp(v, "0")) m.gemm_pair = false;
   }
 }
 
@@ -1289,7 +1311,11 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, bool exact_p,
     mb.t0 = cu[s];
     int ntiles = 0;
     double l2 = 0.0;
+    size_t pacc = 0;  // exact_p: Σ pad8(L)·L so far
     while (s < nseq && (s == mb.s0 || cu[s + 1] - mb.t0 <= kTokenBudget)) {
+      const size_t Lz = (size_t)(cu[s + 1] - cu[s]);
+      if (exact_p && s > mb.s0 && pacc + ((Lz + 7) & ~(size_t)7) * Lz > kExactPBudget) break;
+      pacc += ((Lz + 7) & ~(size_t)7) * Lz;
       const double Ls = cu[s + 1] - cu[s];
       ntiles += (cu[s + 1] - cu[s] + 63) / 64;
       l2 += Ls * Ls;
@@ -1409,7 +1435,7 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
   // rows and CLS sequences fit).
   int head_group = 0;
   if (exact_p && max_p > 0) {
-    const size_t budget = (size_t)1 << 30;  // floats
+    const size_t budget = kExactPBudget;  // floats
     head_group = (int)std::max<size_t>(1, std::min<size_t>((size_t)m.cfg.num_heads, budget / max_p));
     if ((rc = ensure_dev(&d.d_pscr, &d.d_pscr_cap, (size_t)head_group * (max_p + max_t), err,
                          errlen)))
@@ -1586,6 +1612,7 @@ int seam_gemm(int* err_word, int num_sms, const void* A, bool s8, const float* a
   g.epi = kEpiStore;
   g.out_f32 = true;
   g.f16 = false;
+  g.pair = false;
   g.ep.out = dst;
   g.ep.ldo = n;
   g.ep.bias = bias;
@@ -1758,6 +1785,7 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
     int rc;
     CU_TRY(cudaSetDevice(d->device));
     CU_TRY(cudaDeviceGetAttribute(&d->num_sms, cudaDevAttrMultiProcessorCount, d->device));
+    d->gemm_pair = model->gemm_pair;
     CU_TRY(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
     CU_TRY(cudaEventCreateWithFlags(&d->meta_evt, cudaEventDisableTiming));
     CU_TRY(cudaEventRecord(d->meta_evt, d->stream));

@@ -17,6 +17,7 @@ struct GemmLaunch {
   int epi;                // EpiKind
   bool out_f32;           // output element type: f32 (true) or 16-bit (bf16, or f16 with f16)
   bool f16;               // 16-bit operands, outputs and residuals are f16 (else bf16)
+  bool pair;              // f16 only: CTA-pair tiles (M = 256, cta_group::2); tw's box is bn / 2 rows
   EpiParams ep;
   int* err;               // device error word
   int num_sms;
@@ -30,11 +31,11 @@ cudaError_t launch_gemm_f16(const GemmLaunch& g);
 cudaError_t launch_gemm_bf16(const GemmLaunch& g);
 cudaError_t launch_gemm_s8(const GemmLaunch& g);
 
-template <int BN, int EPI, bool S8, typename OutT, bool F16 = false>
-cudaError_t launch_gemm_inst(const GemmLaunch& g) {
+template <int BN, int EPI, bool S8, typename OutT, bool F16, bool PAIR>
+cudaError_t launch_gemm_inst_p(const GemmLaunch& g) {
   constexpr bool kLn = EPI == kEpiResidLN || EPI == kEpiResidLNG;
-  using C = GemmCfg<BN, S8, kLn, gemm_epi_warps<BN, EPI, S8>(), EPI == kEpiResidLN>;
-  auto kern = gemm_tc_kernel<BN, EPI, S8, OutT, F16>;
+  using C = GemmCfg<BN, S8, kLn, gemm_epi_warps<BN, EPI, S8>(), EPI == kEpiResidLN, PAIR>;
+  auto kern = gemm_tc_kernel<BN, EPI, S8, OutT, F16, PAIR>;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<uint64_t> attr_done{0};  // one bit per device
@@ -46,44 +47,58 @@ cudaError_t launch_gemm_inst(const GemmLaunch& g) {
   }
   constexpr bool kTmaStore = sizeof(OutT) == 2;
   if (kTmaStore && !g.to) return cudaErrorInvalidValue;  // bf16 outputs need an output map
-  const long num_m = (g.M + C::kBM - 1) / C::kBM;
+  const long num_m = (g.M + C::kTileM - 1) / C::kTileM;
   if (num_m == 0) return cudaSuccess;
   if constexpr (kLn) {
-    // Clusters of N / BN CTAs, one per column slice of a row tile.
+    // N / BN column slices of a row tile per cluster.
     if (g.N % BN != 0 || g.N / BN < 2 || g.N / BN > kLnPeerSlots || !g.tr)
       return cudaErrorInvalidValue;
-    const int peers = g.N / BN;
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)peers;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(C::kThreads);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    cfg.stream = g.stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    // Clusters that fit at once (per device and cluster size, queried once).
-    static std::atomic<int> fit_cache[64][kLnPeerSlots + 1];
-    int fit = fit_cache[dev & 63][peers].load();
-    if (fit == 0) {
-      cfg.gridDim = dim3((unsigned)(peers * (g.num_sms / peers)));
-      cudaError_t e = cudaOccupancyMaxActiveClusters(&fit, kern, &cfg);
-      if (e != cudaSuccess) return e;
-      if (fit <= 0) return cudaErrorInvalidConfiguration;
-      fit_cache[dev & 63][peers].store(fit);
-    }
-    const int clusters = (int)(num_m < fit ? num_m : fit);
-    cfg.gridDim = dim3((unsigned)(clusters * peers));
-    return cudaLaunchKernelEx(&cfg, kern, *g.ta, *g.tw, *g.to, *g.tr, g.M, g.N, g.K, g.ep, g.err);
-  } else {
-    const long tiles = num_m * ((g.N + BN - 1) / BN);
+  }
+  const int peers = kLn ? g.N / BN : 1;
+  const int csize = peers * (PAIR ? 2 : 1);  // CTAs per cluster
+  const long tiles = kLn ? num_m : num_m * ((g.N + BN - 1) / BN);
+  if (csize == 1) {
     const int grid = (int)(tiles < g.num_sms ? tiles : g.num_sms);
     kern<<<grid, C::kThreads, C::kSmemBytes, g.stream>>>(*g.ta, *g.tw, g.to ? *g.to : *g.ta,
                                                          *g.ta, g.M, g.N, g.K, g.ep, g.err);
     return cudaGetLastError();
   }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = g.stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Clusters that fit at once (per device and cluster size, queried once).
+  static std::atomic<int> fit_cache[64][2 * kLnPeerSlots + 1];
+  int fit = fit_cache[dev & 63][csize].load();
+  if (fit == 0) {
+    cfg.gridDim = dim3((unsigned)(csize * (g.num_sms / csize)));
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&fit, kern, &cfg);
+    if (e != cudaSuccess) return e;
+    if (fit <= 0) return cudaErrorInvalidConfiguration;
+    fit_cache[dev & 63][csize].store(fit);
+  }
+  const int clusters = (int)(tiles < fit ? tiles : fit);
+  cfg.gridDim = dim3((unsigned)(clusters * csize));
+  return cudaLaunchKernelEx(&cfg, kern, *g.ta, *g.tw, g.to ? *g.to : *g.ta, g.tr ? *g.tr : *g.ta,
+                            g.M, g.N, g.K, g.ep, g.err);
+}
+
+// The CTA-pair form for the f16 forward (g.pair), else one CTA per tile.
+template <int BN, int EPI, bool S8, typename OutT, bool F16 = false>
+cudaError_t launch_gemm_inst(const GemmLaunch& g) {
+  if constexpr (F16 && !S8) {
+    if (g.pair) return launch_gemm_inst_p<BN, EPI, S8, OutT, F16, true>(g);
+  } else {
+    if (g.pair) return cudaErrorInvalidValue;
+  }
+  return launch_gemm_inst_p<BN, EPI, S8, OutT, F16, false>(g);
 }
 
 template <bool S8, int BN, bool F16>

@@ -89,13 +89,17 @@ constexpr int kLnPeerSlots = 4;
 // EW: epilogue warps (a multiple of 4; EW / 4 of them share each TMEM lane
 // quarter, splitting its 32-column chunks). The stage count is what the
 // shared-memory budget leaves after the epilogue's buffers.
-template <int BN, bool S8, bool LNS = false, int EW = 8, bool RSM = true>
+// PAIR: the tile's MMAs span a CTA pair (cta_group::2, M = 256): each CTA
+// stages its own 128 rows of A and half (BN / 2 rows) of the tile's W.
+template <int BN, bool S8, bool LNS = false, int EW = 8, bool RSM = true, bool PAIR = false>
 struct GemmCfg {
-  static constexpr int kBM = 128;
+  static constexpr int kBM = 128;                             // rows per CTA
+  static constexpr int kTileM = PAIR ? 256 : 128;             // rows per tile
   static constexpr int kRowBytes = 128;                       // one swizzle row
   static constexpr int kBK = S8 ? 128 : 64;                   // elements per k-block
   static constexpr int kABytes = kBM * kRowBytes;
-  static constexpr int kBBytes = BN * kRowBytes;
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;           // W rows staged per CTA
+  static constexpr int kBBytes = kBRows * kRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kMmaN = BN;                            // N of one tcgen05.mma (≤ 256)
   static constexpr int kNumAcc = 2;                           // TMEM accumulators
@@ -119,7 +123,7 @@ struct GemmCfg {
       1024 /*barriers*/ + kStagingBytes + kXchBytes + kResidBytes + kColsBytes + 1024 /*align*/;
   static constexpr int kBudget = 227 * 1024;
   static constexpr int kFit = (kBudget - kFixedBytes) / kStageBytes;
-  static constexpr int kStages = kFit > 7 ? 7 : kFit;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr int kExtraOffset = kStages * kStageBytes + 1024;  // 1024-aligned
   static constexpr int kXchOffset = kExtraOffset + kStagingBytes;
   static constexpr int kResidOffset = kXchOffset + kXchBytes;       // 1024-aligned
@@ -127,6 +131,7 @@ struct GemmCfg {
   static constexpr int kColsOffset = kResidOffset + kResidBytes;
   static constexpr int kSmemBytes = kColsOffset + kColsBytes + 1024 /*align*/;
   static_assert(BN <= 256, "one tcgen05.mma covers the tile's N");
+  static_assert(!PAIR || (!S8 && (BN / 2) % 16 == 0), "pair tiles: 16-bit operands, N / 2 in 16s");
   static_assert(!LNS || BN % 64 == 0, "residual sub-tiles are 64 columns wide");
   static_assert(!LNS || (BN / 32) % kParts == 0, "LayerNorm column shares are whole chunks");
   static_assert(kStages >= 3 && kSmemBytes <= kBudget, "shared-memory budget");
@@ -605,7 +610,8 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
 // slices of one row tile (peers = N / BN; 1 = no exchange).
 struct LnPeers {
   int peers;
-  uint32_t rank;
+  uint32_t rank;     // this CTA's slice; slice r of the same rows is cluster rank r·rstride + rhalf
+  uint32_t rstride, rhalf;
   uint32_t xbuf;     // shared::cta address of this CTA's [2][kLnPeerSlots][128] double2
   uint32_t xfull;    // shared::cta address of this CTA's two exchange mbarriers
   int* err;
@@ -732,7 +738,8 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
     if (part == 0) {
       for (int r = 0; r < px.peers; ++r) {
         if (r == (int)px.rank) continue;
-        st_async_f64x2(mapa_shared(cell, r), t1, t2, mapa_shared(px.xfull + 8 * par, r));
+        const uint32_t cr = (uint32_t)r * px.rstride + px.rhalf;
+        st_async_f64x2(mapa_shared(cell, cr), t1, t2, mapa_shared(px.xfull + 8 * par, cr));
       }
     }
     if (!mbar_wait_cluster_bounded(px.xfull + 8 * par, (uint32_t)(it >> 1) & 1u, px.err,
@@ -785,20 +792,21 @@ __device__ __forceinline__ bool epilogue_resid_ln(uint32_t taddr, int row, int r
   return true;
 }
 
-template <int BN, int EPI, bool S8, typename OutT, bool F16 = false>
+template <int BN, int EPI, bool S8, typename OutT, bool F16 = false, bool PAIR = false>
 __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    int M, int N, int K, EpiParams ep, int* err) {
   // LayerNorm over rows wider than one tile: the grid is made of clusters of
-  // N / BN CTAs, CTA rank r of a cluster computes column slice r of every
-  // row tile the cluster takes, and the slices exchange row statistics. The
-  // producer loads each tile's residual slice (tmR) next to the operands.
+  // N / BN column slices (CTA pairs with PAIR), the CTAs of slice r compute
+  // columns [r·BN, r·BN + BN) of every row tile the cluster takes, and the
+  // slices exchange row statistics. The producer loads each tile's residual
+  // slice (tmR) next to the operands.
   constexpr bool kLnSlices = EPI == kEpiResidLN || EPI == kEpiResidLNG;
   constexpr bool kResidTma = EPI == kEpiResidLN;  // residual tile via TMA into shared memory
   static_assert(!kLnSlices || ((BN == 128 || BN == 192) && !S8),
                 "LayerNorm slices are 128 or 192 bf16 columns");
-  using C = GemmCfg<BN, S8, kLnSlices, gemm_epi_warps<BN, EPI, S8>(), kResidTma>;
+  using C = GemmCfg<BN, S8, kLnSlices, gemm_epi_warps<BN, EPI, S8>(), kResidTma, PAIR>;
   // bf16 outputs leave through TMA tile stores; f32 outputs store directly.
   constexpr bool kTmaStore = sizeof(OutT) == 2;
   extern __shared__ uint8_t smem_raw[];
@@ -821,17 +829,29 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (M + C::kBM - 1) / C::kBM;
+  const int num_m = (M + C::kTileM - 1) / C::kTileM;
   const int num_n = (N + BN - 1) / BN;
   const int num_k = (K + C::kBK - 1) / C::kBK;
+  // Cluster layout: rank = slice · (PAIR ? 2 : 1) + half. With PAIR the even
+  // CTA of a pair (the leader) issues the pair's MMAs, waits for both CTAs'
+  // operand bytes on its full barriers and for both CTAs' epilogues on its
+  // accumulator-empty barriers; commits arrive in both CTAs.
+  const uint32_t crank = (kLnSlices || PAIR) ? cluster_ctarank() : 0u;
+  const uint32_t half = PAIR ? (crank & 1u) : 0u;
+  const uint32_t leader = crank & ~1u;  // the pair's even rank (PAIR)
+  const bool is_leader = !PAIR || half == 0;
+  const uint16_t pair_mask = (uint16_t)(3u << leader);
   // Tile loop: tiles first, first + stride, ... < num_tiles; tile → (mb, nb).
   const int peers = kLnSlices ? num_n : 1;
-  const uint32_t rank = kLnSlices ? cluster_ctarank() : 0u;
+  const int csize = peers * (PAIR ? 2 : 1);  // CTAs per cluster
+  const uint32_t rank = PAIR ? crank >> 1 : crank;  // this CTA's column slice (kLnSlices)
   const int num_tiles = kLnSlices ? num_m : num_m * num_n;
-  const int first = kLnSlices ? (int)blockIdx.x / peers : (int)blockIdx.x;
-  const int stride = kLnSlices ? (int)gridDim.x / peers : (int)gridDim.x;
+  const int first = (int)blockIdx.x / csize;
+  const int stride = (int)gridDim.x / csize;
   auto tile_mb = [&](int t) { return kLnSlices ? t : t / num_n; };
   auto tile_nb = [&](int t) { return kLnSlices ? (int)rank : t % num_n; };
+  // This CTA's first row of a tile's rows.
+  auto tile_row0 = [&](int mb) { return mb * C::kTileM + (int)half * C::kBM; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -840,7 +860,8 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&accf_bar[a]), 1);
-      mbar_init(smem_u32(&acce_bar[a]), C::kEpiWarps);  // one arrive per epilogue warp
+      // One arrive per epilogue warp (of both CTAs of a pair).
+      mbar_init(smem_u32(&acce_bar[a]), (PAIR ? 2 : 1) * C::kEpiWarps);
       // One local arrival per tile, plus the peers' asynchronous stores
       // counted in bytes (epilogue_resid_ln).
       if (kLnSlices) mbar_init(smem_u32(&xfull_bar[a]), 1u);
@@ -859,8 +880,13 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     if constexpr (kResidTma) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), C::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   if constexpr (kLnSlices) {
     // The slice's bias, γ and β, read by every tile's epilogue.
@@ -873,7 +899,8 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     }
   }
   tc_fence_before();
-  if constexpr (kLnSlices) cluster_sync_all();  // peers' barriers exist before any remote arrive
+  // Peers' barriers exist before any remote arrive.
+  if constexpr (kLnSlices || PAIR) cluster_sync_all();
   else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
@@ -896,7 +923,7 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
 #pragma unroll
           for (int g = 0; g < BN / 64; ++g)
             tma_load_2d(smem_u32(smem + C::kResidOffset + g * C::kBM * 128), &tmR, rb,
-                        nb * BN + g * 64, mb * C::kBM);
+                        nb * BN + g * 64, tile_row0(mb));
           ++rtiles;
         }
         for (int kb = 0; kb < num_k; ++kb) {
@@ -906,9 +933,19 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
           uint8_t* sa = smem + stage * C::kStageBytes;
           uint8_t* sb = sa + C::kABytes;
           const uint32_t fb = smem_u32(&full_bar[stage]);
-          mbar_arrive_expect_tx(fb, C::kStageBytes);
-          tma_load_2d(smem_u32(sa), &tmA, fb, kb * C::kBK, mb * C::kBM);
-          tma_load_2d(smem_u32(sb), &tmW, fb, kb * C::kBK, nb * BN);
+          if constexpr (PAIR) {
+            // Both CTAs' bytes complete the leader's barrier; the leader
+            // announces them (a peer's bytes may land first: the phase cannot
+            // complete before the leader's arrival).
+            if (is_leader) mbar_arrive_expect_tx(fb, 2 * C::kStageBytes);
+            const uint32_t cfb = mapa_shared(fb, leader);
+            tma_load_2d_pair(smem_u32(sa), &tmA, cfb, kb * C::kBK, tile_row0(mb));
+            tma_load_2d_pair(smem_u32(sb), &tmW, cfb, kb * C::kBK, nb * BN + (int)half * C::kBRows);
+          } else {
+            mbar_arrive_expect_tx(fb, C::kStageBytes);
+            tma_load_2d(smem_u32(sa), &tmA, fb, kb * C::kBK, mb * C::kBM);
+            tma_load_2d(smem_u32(sb), &tmW, fb, kb * C::kBK, nb * BN);
+          }
           ++issued;
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
         }
@@ -921,7 +958,10 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
           if (globaltimer_ns() - t0 > kWaitLimitNs) break;
         }
       }
-      {
+      // A pair's operand bytes all complete the leader's full barriers, so the
+      // leader drains for both (the peer cannot leave before it: the kernel
+      // ends with a cluster barrier).
+      if (is_leader) {
         int n = issued < C::kStages ? issued : C::kStages;
         int s = stage;
         uint32_t ph = phase;
@@ -935,20 +975,24 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && is_leader) {
       // ---------------- MMA issuer ----------------
       // Operand format: S8 (kind::i8), else F16 = 0 / BF16 = 1 (kind::f16).
-      constexpr uint32_t idesc =
-          make_idesc(S8 ? 2u : 1u, (S8 || !F16) ? 1u : 0u, 128u, (uint32_t)C::kMmaN);
+      constexpr uint32_t idesc = make_idesc(S8 ? 2u : 1u, (S8 || !F16) ? 1u : 0u,
+                                            (uint32_t)C::kTileM, (uint32_t)C::kMmaN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       for (int tile = first; tile < num_tiles; tile += stride, ++it) {
         const int acc = it % C::kNumAcc;
         const uint32_t acc_phase = (uint32_t)(it / C::kNumAcc) & 1u;
-        if (!mbar_wait_bounded(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, err, kDevTimeoutAccEmpty,
-                               abort_flag))
-          break;
+        // A pair's accumulator is free once both CTAs' epilogues have read it.
+        const bool freed =
+            PAIR ? mbar_wait_cluster_bounded(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, err,
+                                             kDevTimeoutAccEmpty, abort_flag)
+                 : mbar_wait_bounded(smem_u32(&acce_bar[acc]), acc_phase ^ 1u, err,
+                                     kDevTimeoutAccEmpty, abort_flag);
+        if (!freed) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * C::kAccStride;
         bool ok = true;
@@ -968,13 +1012,17 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
             const uint64_t koff = (uint64_t)(ks * 2);
             if constexpr (S8)
               mma_s8(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
+            else if constexpr (PAIR)
+              mma_f16kind_pair(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
             else
               mma_f16kind(d_tmem, adesc + koff, bdesc + koff, idesc, (kb | ks) ? 1u : 0u);
           }
-          mma_commit(smem_u32(&empty_bar[stage]));
+          if constexpr (PAIR) mma_commit_pair(smem_u32(&empty_bar[stage]), pair_mask);
+          else mma_commit(smem_u32(&empty_bar[stage]));
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
         }
-        mma_commit(smem_u32(&accf_bar[acc]));
+        if constexpr (PAIR) mma_commit_pair(smem_u32(&accf_bar[acc]), pair_mask);
+        else mma_commit(smem_u32(&accf_bar[acc]));
         if (!ok) break;
       }
       // Drain: wait (bounded) for the last committed MMAs before TMEM is freed.
@@ -993,14 +1041,17 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
     const int part = (warp - 2) >> 2;    // which share of the column chunks
     TmaSink<2> tsink{extra + (warp - 2) * 4096, &tmO, lane, 0, F16 ? 0 : ep.f16_from};
     TmaSink<1> lsink{extra + C::kRedBytes + (warp - 2) * 2048, &tmO, lane, 0, F16 ? 0 : 1 << 30};
-    const LnPeers px{peers, rank, smem_u32(smem + C::kXchOffset), smem_u32(xfull_bar), err,
-                     abort_flag};
+    const LnPeers px{peers, rank, PAIR ? 2u : 1u, half, smem_u32(smem + C::kXchOffset),
+                     smem_u32(xfull_bar), err, abort_flag};
+    // The accumulator-empty barrier this CTA's epilogue arrives on: its own,
+    // or the pair leader's.
+    const uint32_t acce_dst = PAIR ? mapa_shared(smem_u32(acce_bar), leader) : smem_u32(acce_bar);
     int it = 0;
     for (int tile = first; tile < num_tiles; tile += stride, ++it) {
       const int acc = it % C::kNumAcc;
       const uint32_t acc_phase = (uint32_t)(it / C::kNumAcc) & 1u;
       const int mb = tile_mb(tile), nb = tile_nb(tile);
-      const int row0 = mb * C::kBM + quarter * 32;
+      const int row0 = tile_row0(mb) + quarter * 32;
       const int row = row0 + lane;
       // Global-residual LayerNorm: the first two chunks are fetched while the
       // tile's MMAs finish.
@@ -1040,7 +1091,10 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&acce_bar[acc]));
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_cluster(acce_dst + 8u * (uint32_t)acc);
+        else mbar_arrive(acce_dst + 8u * (uint32_t)acc);
+      }
     }
     // The last tile's TMA stores read their staging before the CTA exits.
     if constexpr (kLnSlices) lsink.drain();
@@ -1048,12 +1102,14 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
   }
 
   __syncthreads();
-  // No CTA of a LayerNorm cluster leaves while a peer may still store into
-  // its shared memory (every wait above is bounded, so all CTAs get here).
-  if constexpr (kLnSlices) cluster_sync_all();
+  // No CTA of a cluster leaves while a peer may still store into its shared
+  // memory or issue MMAs into its TMEM (every wait above is bounded, so all
+  // CTAs get here).
+  if constexpr (kLnSlices || PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    else tmem_dealloc(tmem_base, C::kTmemCols);
   }
 }
 

@@ -305,6 +305,30 @@ def test_attention_split_bitwise_equals_unsplit(gpu, monkeypatch, arch, inputs, 
     assert np.array_equal(out["1"], out["0"])
 
 
+@pytest.mark.parametrize("arch,inputs,nseq", [
+    ("bge", "c4", 700),      # M-tail tiles, the fused LayerNorm clusters
+    ("nomic", "c2", 24),     # SwiGLU fc1‖gate, RoPE qkv
+])
+def test_gemm_pair_tiles_match_single_cta(gpu, monkeypatch, arch, inputs, nseq):
+    """CTA-pair GEMM tiles (FUTON_CUDA_GEMM_PAIR=1: M = 256 over two SMs with
+    cta_group::2 MMAs, each CTA staging half of the weight tile) against the
+    default one CTA per 128-row tile: the same products summed over the same
+    k-blocks, so the vectors are bit-identical, and both meet the oracle gate."""
+    cfg = synth.arch(arch)
+    w = synth.make_weights(cfg)
+    ids, cu = synth.make_inputs(inputs, nseq=nseq, vocab=cfg.vocab_size)
+    out = {}
+    for v in ("1", "0"):
+        monkeypatch.setenv("FUTON_CUDA_GEMM_PAIR", v)
+        m = Model(cfg, w, devices=[0])
+        out[v] = m.encode_packed(ids, cu)
+        m.close()
+    assert np.array_equal(out["1"], out["0"])
+    n = min(nseq, 64)
+    want = OracleModel(cfg, w, gemm=oracle_mode()).encode_batch(ids[:cu[n]], cu[:n + 1])
+    assert_parity(out["1"][:n], want, f"pair tiles {arch}")
+
+
 def test_batch_matches_single_bitwise(gpu):
     """Packing never perturbs a sequence (no padding, no cross-sequence
     reduction): each vector of a packed call equals its single-sequence call."""
@@ -401,10 +425,11 @@ def test_encode_device_two_streams(gpu):
 
 
 def test_micro_batching_large_call(gpu):
-    """A call larger than one micro-batch (131,072 tokens) splits without
+    """A call larger than one micro-batch (524,288 tokens) splits without
     changing any vector."""
     cfg, w, m = synth_model("bge")
-    ids, cu = synth.make_inputs("c4", nseq=2000, seed=9)
+    ids, cu = synth.make_inputs("c4", nseq=7000, seed=9)
+    assert cu[-1] > 524288
     big = np.concatenate([ids] * 1)
     full = m.encode_packed(big, cu)
     # re-encode a slice that crosses no boundary and compare
@@ -459,10 +484,10 @@ def test_cancellation_at_every_checkpoint(gpu):
     cfg.num_layers = 2
     w = synth.make_weights(cfg)
     m = Model(cfg, w, devices=[0])
-    seqs = [np.full(128, 1000 + i % 7, np.int32) for i in range(1100)]  # 140,800 tokens
+    seqs = [np.full(128, 1000 + i % 7, np.int32) for i in range(4200)]  # 537,600 tokens
     ids, cu = pack_ids(seqs)
     clean = m.encode_packed(ids, cu)
-    # Checkpoints: the entry check, then per micro-batch (two of ≤ 131,072
+    # Checkpoints: the entry check, then per micro-batch (two of ≤ 524,288
     # tokens) one before it, and one before each layer and each layer's FFN.
     checkpoints = 1 + 2 * (1 + 2 * cfg.num_layers)
     lib = _lib.lib()
