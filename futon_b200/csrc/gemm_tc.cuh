@@ -911,21 +911,13 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0, rtiles = 0;
+      // The residual slice of a tile is loaded once the epilogue has read the
+      // previous tile's, after the tile's first ring-full of k-blocks: those
+      // loads go out while the previous tile's epilogue still holds the
+      // residual buffer, so the MMAs of this tile start on time.
+      const int resid_after = (num_k < C::kStages ? num_k : C::kStages) - 1;
       for (int tile = first; tile < num_tiles; tile += stride) {
         const int mb = tile_mb(tile), nb = tile_nb(tile);
-        if constexpr (kResidTma) {
-          // The residual slice of this tile, once the epilogue has read the last one.
-          if (!mbar_wait_bounded(smem_u32(rempty_bar), ((uint32_t)rtiles & 1u) ^ 1u, err,
-                                 kDevTimeoutSmemEmpty, abort_flag))
-            goto producer_done;
-          const uint32_t rb = smem_u32(rfull_bar);
-          mbar_arrive_expect_tx(rb, C::kResidBytes);
-#pragma unroll
-          for (int g = 0; g < BN / 64; ++g)
-            tma_load_2d(smem_u32(smem + C::kResidOffset + g * C::kBM * 128), &tmR, rb,
-                        nb * BN + g * 64, tile_row0(mb));
-          ++rtiles;
-        }
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&empty_bar[stage]), phase ^ 1u, err, kDevTimeoutSmemEmpty,
                                  abort_flag))
@@ -948,6 +940,20 @@ __global__ void __launch_bounds__(64 + 32 * gemm_epi_warps<BN, EPI, S8>(), 1)
           }
           ++issued;
           if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+          if constexpr (kResidTma) {
+            if (kb == resid_after) {
+              if (!mbar_wait_bounded(smem_u32(rempty_bar), ((uint32_t)rtiles & 1u) ^ 1u, err,
+                                     kDevTimeoutSmemEmpty, abort_flag))
+                goto producer_done;
+              const uint32_t rb = smem_u32(rfull_bar);
+              mbar_arrive_expect_tx(rb, C::kResidBytes);
+#pragma unroll
+              for (int g = 0; g < BN / 64; ++g)
+                tma_load_2d(smem_u32(smem + C::kResidOffset + g * C::kBM * 128), &tmR, rb,
+                            nb * BN + g * 64, tile_row0(mb));
+              ++rtiles;
+            }
+          }
         }
       }
     producer_done:
