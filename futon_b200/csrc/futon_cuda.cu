@@ -246,6 +246,7 @@ struct Workspace {
 
 struct DevCtx {
   int device = 0;
+  std::vector<int> plan_slots;  // upload_mb_meta's counting-sort slots
   int num_sms = 148;
   bool gemm_pair = false;  // the model's gemm_pair option, read by upload_gemm
   cudaStream_t stream = nullptr;
@@ -1289,20 +1290,29 @@ int validate_input(const futon_model& m, const int32_t* cu, int nseq, int out_di
   return FUTON_OK;
 }
 
+// Every id in [0, vocab): one branch-free pass over the packed ids (cu is
+// validated, so they are exactly [0, cu[nseq])); the first bad id and its
+// sequence are looked up only when there is one.
 int check_ids(const futon_model& m, const int32_t* ids, const int32_t* cu, int nseq, char* err,
               size_t errlen) {
-  const int V = m.cfg.vocab_size;
-  for (int s = 0; s < nseq; ++s)
-    for (int t = cu[s]; t < cu[s + 1]; ++t)
-      if (ids[t] < 0 || ids[t] >= V)
-        return set_err(err, errlen, FUTON_EINVAL, "native: batch item %d: token id %d outside vocab of %d",
-                       s, ids[t], V);
-  return FUTON_OK;
+  const uint32_t V = (uint32_t)m.cfg.vocab_size;
+  const size_t T = nseq > 0 ? (size_t)cu[nseq] : 0;
+  uint32_t bad = 0;
+  for (size_t t = 0; t < T; ++t) bad |= (uint32_t)((uint32_t)ids[t] >= V);
+  if (!bad) return FUTON_OK;
+  size_t t = 0;
+  while ((uint32_t)ids[t] < V) ++t;
+  const int s = (int)(std::upper_bound(cu, cu + nseq + 1, (int32_t)t) - cu) - 1;
+  return set_err(err, errlen, FUTON_EINVAL, "native: batch item %d: token id %d outside vocab of %d",
+                 s, ids[t], (int)V);
 }
 
-// Plans micro-batches, fills the pinned meta buffer, uploads it (one copy).
-int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, bool exact_p,
-                    std::vector<MicroBatch>& mbs, cudaStream_t st, char* err, size_t errlen) {
+// Splits a call into micro-batches and lays out their metadata in the
+// pinned meta buffer (offsets only; upload_mb_meta fills and uploads each
+// one just before its forward, so the host plans micro-batch i + 1 while the
+// GPU runs i). windows: the tcgen05 attention's window lists are planned too.
+int plan_batches(DevCtx& d, const int32_t* cu, int nseq, bool exact_p, bool windows,
+                 std::vector<MicroBatch>& mbs, char* err, size_t errlen) {
   mbs.clear();
   size_t meta = 0;
   for (int s = 0; s < nseq;) {
@@ -1326,7 +1336,7 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, bool exact_p,
     mb.t1 = cu[s];
     mb.ntiles = ntiles;
     mb.nseg = 0;
-    mb.nwin = plan_windows(cu, mb.s0, mb.s1, mb.t0, nullptr, nullptr, &mb.nseg);
+    mb.nwin = windows ? plan_windows(cu, mb.s0, mb.s1, mb.t0, nullptr, nullptr, &mb.nseg) : 0;
     mb.cu_off = meta;
     meta += align_up((size_t)(mb.s1 - mb.s0 + 1), 4);
     mb.tile_off = meta;
@@ -1356,30 +1366,53 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, bool exact_p,
     mbs.push_back(mb);
   }
   if (mbs.empty()) return FUTON_OK;
-  // The pinned staging may still feed the previous call's upload.
+  // The pinned staging may still feed the previous call's uploads.
   CU_TRY(cudaEventSynchronize(d.meta_evt));
   int rc;
   if ((rc = ensure_host(&d.h_meta, &d.h_meta_cap, meta, err, errlen))) return rc;
   if ((rc = ensure_dev(&d.d_meta, &d.d_meta_cap, meta, err, errlen))) return rc;
-  for (const MicroBatch& mb : mbs) {
-    int* hc = d.h_meta + mb.cu_off;
-    for (int s = mb.s0; s <= mb.s1; ++s) hc[s - mb.s0] = cu[s] - mb.t0;
-    // Tiles longest sequence first (the CTAs launch in list order, so the
-    // tiles with the most key blocks start early instead of trailing the
-    // launch); every tile is computed the same way in any order.
-    AttnTile* ht = reinterpret_cast<AttnTile*>(d.h_meta + mb.tile_off);
-    int k = 0;
-    for (int s = mb.s0; s < mb.s1; ++s)
-      for (int q0 = 0; q0 < cu[s + 1] - cu[s]; q0 += 64) ht[k++] = AttnTile{s - mb.s0, q0};
-    const int* cl = cu + mb.s0;
-    auto longer = [cl](const AttnTile& a, const AttnTile& b) {
-      return cl[a.seq + 1] - cl[a.seq] > cl[b.seq + 1] - cl[b.seq];
-    };
-    std::stable_sort(ht, ht + k, longer);
-    // The CLS-only last layer: one query row per sequence, same order.
-    AttnTile* hc2 = reinterpret_cast<AttnTile*>(d.h_meta + mb.cls_off);
-    for (int s = mb.s0; s < mb.s1; ++s) hc2[s - mb.s0] = AttnTile{s - mb.s0, 0};
-    std::stable_sort(hc2, hc2 + (mb.s1 - mb.s0), longer);
+  return FUTON_OK;
+}
+
+// Fills micro-batch mb's metadata (local cu_seqlens, attention tiles and
+// CLS list longest sequence first, tcgen05 windows when planned, the exact
+// int8 attention's P offsets) and uploads it on st.
+int upload_mb_meta(DevCtx& d, const int32_t* cu, const MicroBatch& mb, bool exact_p, bool windows,
+                   cudaStream_t st, char* err, size_t errlen) {
+  int* hc = d.h_meta + mb.cu_off;
+  int maxL = 0;
+  for (int s = mb.s0; s <= mb.s1; ++s) hc[s - mb.s0] = cu[s] - mb.t0;
+  for (int s = mb.s0; s < mb.s1; ++s) maxL = std::max(maxL, cu[s + 1] - cu[s]);
+  // Tiles longest sequence first (the CTAs launch in list order, so the
+  // tiles with the most key blocks start early instead of trailing the
+  // launch); every tile is computed the same way in any order. A counting
+  // sort on the length, ties in sequence order: the order a stable sort by
+  // decreasing length gives. slot[L]: next free entry for length L.
+  std::vector<int>& slot = d.plan_slots;
+  auto order = [&](int per_tile) {
+    slot.assign((size_t)maxL + 1, 0);
+    for (int s = mb.s0; s < mb.s1; ++s) {
+      const int L = cu[s + 1] - cu[s];
+      slot[L] += per_tile ? (L + 63) / 64 : 1;
+    }
+    int acc = 0;
+    for (int L = maxL; L >= 0; --L) {
+      const int c = slot[L];
+      slot[L] = acc;
+      acc += c;
+    }
+  };
+  AttnTile* ht = reinterpret_cast<AttnTile*>(d.h_meta + mb.tile_off);
+  order(1);
+  for (int s = mb.s0; s < mb.s1; ++s) {
+    const int L = cu[s + 1] - cu[s];
+    for (int q0 = 0; q0 < L; q0 += 64) ht[slot[L]++] = AttnTile{s - mb.s0, q0};
+  }
+  // The CLS-only last layer: one query row per sequence, same order.
+  AttnTile* hcl = reinterpret_cast<AttnTile*>(d.h_meta + mb.cls_off);
+  order(0);
+  for (int s = mb.s0; s < mb.s1; ++s) hcl[slot[cu[s + 1] - cu[s]]++] = AttnTile{s - mb.s0, 0};
+  if (windows) {
     int nseg = 0;
     AttnWindow* hw = reinterpret_cast<AttnWindow*>(d.h_meta + mb.win_off);
     plan_windows(cu, mb.s0, mb.s1, mb.t0, hw, reinterpret_cast<AttnSeg*>(d.h_meta + mb.seg_off),
@@ -1387,30 +1420,38 @@ int plan_and_upload(DevCtx& d, const int32_t* cu, int nseq, bool exact_p,
     // tcgen05 windows most keys first (each keeps its own segment range).
     std::stable_sort(hw, hw + mb.nwin,
                      [](const AttnWindow& a, const AttnWindow& b) { return a.nk > b.nk; });
-    if (exact_p) {
-      int* po = d.h_meta + mb.poff_off;
-      int* pc = d.h_meta + mb.pcls_off;
-      po[0] = pc[0] = 0;
-      for (int q = mb.s0; q < mb.s1; ++q) {
-        const int L = cu[q + 1] - cu[q], kp = (L + 7) & ~7;
-        po[q - mb.s0 + 1] = po[q - mb.s0] + kp * L;
-        pc[q - mb.s0 + 1] = pc[q - mb.s0] + kp;
-      }
+  }
+  if (exact_p) {
+    int* po = d.h_meta + mb.poff_off;
+    int* pc = d.h_meta + mb.pcls_off;
+    po[0] = pc[0] = 0;
+    for (int q = mb.s0; q < mb.s1; ++q) {
+      const int L = cu[q + 1] - cu[q], kp = (L + 7) & ~7;
+      po[q - mb.s0 + 1] = po[q - mb.s0] + kp * L;
+      pc[q - mb.s0 + 1] = pc[q - mb.s0] + kp;
     }
   }
-  CU_TRY(cudaMemcpyAsync(d.d_meta, d.h_meta, meta * sizeof(int), cudaMemcpyHostToDevice, st));
-  d.h2d_bytes.fetch_add((long long)(meta * sizeof(int)), std::memory_order_relaxed);
+  // The micro-batch's block of the meta buffer: from its cu list to the end
+  // of its last list (the layout is contiguous per micro-batch).
+  const size_t lo = mb.cu_off;
+  const size_t hi = exact_p ? mb.pcls_off + align_up((size_t)(mb.s1 - mb.s0 + 1), 4)
+                            : mb.seg_off + align_up((size_t)mb.nseg * 3, 4);
+  CU_TRY(cudaMemcpyAsync(d.d_meta + lo, d.h_meta + lo, (hi - lo) * sizeof(int),
+                         cudaMemcpyHostToDevice, st));
+  d.h2d_bytes.fetch_add((long long)((hi - lo) * sizeof(int)), std::memory_order_relaxed);
   CU_TRY(cudaEventRecord(d.meta_evt, st));
   return FUTON_OK;
 }
 
 // after_mb (optional) runs after each micro-batch's forward is queued, with
 // the micro-batch's index and its sequences [s0, s1).
+// before_mb (optional) runs after the micro-batch's metadata upload is
+// queued and before its forward, with its index and tokens [t0, t1).
 using MbHook = std::function<int(int, int, int)>;
 
 int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* cu, int nseq,
              int out_dim, float* d_out, cudaStream_t st, volatile const int* cancel, char* err,
-             size_t errlen, const MbHook& after_mb = nullptr) {
+             size_t errlen, const MbHook& after_mb = nullptr, const MbHook& before_mb = nullptr) {
   // Work of earlier calls (possibly on other streams) finishes before this
   // call's uploads and kernels touch the shared buffers; this call's end is
   // recorded for the next one on every return path.
@@ -1423,7 +1464,8 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
   std::vector<MicroBatch> mbs;
   int rc;
   const bool exact_p = m.q8 && m.q8_exact_attn && (m.head_dim == 32 || m.head_dim == 64);
-  if ((rc = plan_and_upload(d, cu, nseq, exact_p, mbs, st, err, errlen))) return rc;
+  const bool windows = m.attn_kind == kAttnTc2 && !m.q8;
+  if ((rc = plan_batches(d, cu, nseq, exact_p, windows, mbs, err, errlen))) return rc;
   size_t max_t = 0, max_p = 0;
   for (const MicroBatch& mb : mbs) {
     max_t = std::max<size_t>(max_t, (size_t)(mb.t1 - mb.t0));
@@ -1446,6 +1488,8 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
     const MicroBatch& mb = mbs[i];
     if (canceled(cancel))
       return set_err(err, errlen, FUTON_ECANCELED, "native: context canceled");
+    if ((rc = upload_mb_meta(d, cu, mb, exact_p, windows, st, err, errlen))) return rc;
+    if (before_mb && (rc = before_mb((int)i, mb.t0, mb.t1))) return rc;
     AttnPlan plan{reinterpret_cast<const AttnTile*>(d.d_meta + mb.tile_off), mb.ntiles,
                   reinterpret_cast<const AttnTile*>(d.d_meta + mb.cls_off),
                   reinterpret_cast<const AttnWindow*>(d.d_meta + mb.win_off), mb.nwin,
@@ -1498,9 +1542,23 @@ int encode_host(futon_model* m, DevCtx& d, const int32_t* ids, const int32_t* cu
   if ((rc = ensure_dev(&d.d_ids, &d.d_ids_cap, T, err, errlen))) return rc;
   if ((rc = ensure_host(&d.h_out, &d.h_out_cap, (size_t)nseq * dim, err, errlen))) return rc;
   if ((rc = ensure_dev(&d.d_out, &d.d_out_cap, (size_t)nseq * dim, err, errlen))) return rc;
-  memcpy(d.h_ids, ids, T * sizeof(int));
-  CU_TRY(cudaMemcpyAsync(d.d_ids, d.h_ids, T * sizeof(int), cudaMemcpyHostToDevice, d.stream));
-  d.h2d_bytes.fetch_add((long long)(T * sizeof(int)), std::memory_order_relaxed);
+  // The ids of the first micro-batch (at most kTokenBudget tokens: all of a
+  // small call) go up before planning; the rest micro-batch by micro-batch,
+  // just before each forward (the host copies micro-batch i + 1's while the
+  // GPU runs i). `sent`: tokens [0, sent) are on their way.
+  size_t sent = 0;
+  auto send_ids = [&](size_t t1) -> int {
+    if (t1 <= sent) return FUTON_OK;
+    const size_t n = t1 - sent;
+    memcpy(d.h_ids + sent, ids + sent, n * sizeof(int));
+    CU_TRY(cudaMemcpyAsync(d.d_ids + sent, d.h_ids + sent, n * sizeof(int),
+                           cudaMemcpyHostToDevice, d.stream));
+    d.h2d_bytes.fetch_add((long long)(n * sizeof(int)), std::memory_order_relaxed);
+    sent = t1;
+    return FUTON_OK;
+  };
+  if ((rc = send_ids(std::min(T, (size_t)kTokenBudget)))) return rc;
+  auto before_mb = [&](int, int, int t1) -> int { return send_ids((size_t)t1); };
   // Each micro-batch's vectors go to pinned memory as soon as it is done
   // (event per micro-batch); this thread copies them out to `out` while the
   // GPU works on the next micro-batches.
@@ -1521,7 +1579,8 @@ int encode_host(futon_model* m, DevCtx& d, const int32_t* ids, const int32_t* cu
     done.push_back(Done{s0, s1});
     return FUTON_OK;
   };
-  rc = run_call(*m, d, d.d_ids, cu, nseq, out_dim, d.d_out, d.stream, cancel, err, errlen, after_mb);
+  rc = run_call(*m, d, d.d_ids, cu, nseq, out_dim, d.d_out, d.stream, cancel, err, errlen, after_mb,
+                before_mb);
   if (rc) {
     cudaStreamSynchronize(d.stream);  // leave nothing in flight
     return rc;
