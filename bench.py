@@ -494,7 +494,7 @@ def main():
                        "12 heads, FFN 1536, GELU, CLS)", "global_batch": nseq_all,
                        "tokens": ntok_all, "seqs_on_rank0": nseq,
                        "parallelism": f"dp{world} (contiguous cost-balanced shards of one batch)",
-                       "l2": "working set > L2 (per micro-batch activations ~1.3 GB)",
+                       "l2": "working set > L2 (per micro-batch activations ~3.4 GB)",
                        "attention": {"kernel": os.environ.get("FUTON_CUDA_ATTN") or "heads",
                                      "split": os.environ.get("FUTON_CUDA_ATTN_SPLIT") != "0"}},
             "tokens_per_sec": round(ntok_all / (ms / 1e3), 1),
