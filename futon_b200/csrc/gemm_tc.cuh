@@ -34,6 +34,9 @@
 // through L2; the weights (≤ 19 MB) stay L2-resident. The fused LayerNorm
 // GEMMs run as clusters of hidden/192 CTAs, one 192-column slice each, which
 // exchange per-row statistics through distributed shared memory.
+// PAIR (opt-in): 256-row tiles over a CTA pair, tcgen05.mma.cta_group::2
+// issued by the pair's even CTA; each CTA stages its own 128 rows of A and
+// half of the tile's W rows (no multicast), commits arrive in both CTAs.
 #pragma once
 
 #include <cuda_fp16.h>
