@@ -290,11 +290,22 @@ struct DevCtx {
   std::vector<cudaEvent_t> ev_pool, ev_all;
   struct ProfAgg { double ms = 0, flops = 0, bytes = 0; long long n = 0; };
   ProfAgg prof_agg[16];
+  // CUDA graphs of small host-buffer calls: the launches of a one-micro-batch
+  // forward, keyed by every value they were captured with (shapes, metadata
+  // offsets, buffer addresses, stream), replayed when a call repeats them.
+  struct GraphEntry {
+    cudaGraphExec_t exec = nullptr;
+    long long launches = 0;  // kernels in the graph
+    unsigned long long used = 0;
+  };
+  std::map<std::vector<long long>, GraphEntry> graphs;
+  unsigned long long graph_clock = 0;
 
   ~DevCtx() {
     cudaSetDevice(device);
     if (done_evt) cudaEventSynchronize(done_evt);  // the last call, whatever its stream
     if (stream) cudaStreamSynchronize(stream);
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second.exec);
     for (cudaEvent_t e : out_evts) cudaEventDestroy(e);
     for (void* p : allocs) cudaFree(p);
     if (ws.base) cudaFree(ws.base);
@@ -1449,9 +1460,17 @@ int upload_mb_meta(DevCtx& d, const int32_t* cu, const MicroBatch& mb, bool exac
 // queued and before its forward, with its index and tokens [t0, t1).
 using MbHook = std::function<int(int, int, int)>;
 
+// Calls of one micro-batch of at most this many tokens run from a CUDA graph
+// when allow_graph is set (the host-buffer entry point, whose buffers are the
+// library's own): launch-bound sizes, where ~60 kernel launches per forward
+// cost as much as the kernels.
+constexpr int kGraphMaxTokens = 32768;
+constexpr size_t kGraphCacheSize = 32;
+
 int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* cu, int nseq,
              int out_dim, float* d_out, cudaStream_t st, volatile const int* cancel, char* err,
-             size_t errlen, const MbHook& after_mb = nullptr, const MbHook& before_mb = nullptr) {
+             size_t errlen, const MbHook& after_mb = nullptr, const MbHook& before_mb = nullptr,
+             bool allow_graph = false) {
   // Work of earlier calls (possibly on other streams) finishes before this
   // call's uploads and kernels touch the shared buffers; this call's end is
   // recorded for the next one on every return path.
@@ -1504,10 +1523,74 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
       plan.pinv = d.d_pscr + (size_t)head_group * max_p;
       plan.pinv_ld = (int)max_t;
     }
-    if ((rc = forward_mb(m, d, d_ids + mb.t0, d.d_meta + mb.cu_off, mb.s1 - mb.s0, mb.t1 - mb.t0,
-                         mb.sum_l2, plan, out_dim, d_out + (size_t)mb.s0 * dim, st, cancel, err,
-                         errlen)))
-      return rc;
+    auto forward = [&]() {
+      return forward_mb(m, d, d_ids + mb.t0, d.d_meta + mb.cu_off, mb.s1 - mb.s0, mb.t1 - mb.t0,
+                        mb.sum_l2, plan, out_dim, d_out + (size_t)mb.s0 * dim, st, cancel, err,
+                        errlen);
+    };
+    // A small one-micro-batch call replays the graph of an earlier call with
+    // the same launches (this call's ids and metadata were uploaded above, to
+    // the same addresses). Its cancellation is checked at entry and before
+    // the micro-batch; the layer checkpoints pass at capture. Profiling and
+    // the debug cancellation counter keep the direct launches.
+    const bool graph = allow_graph && mbs.size() == 1 && mb.t1 - mb.t0 <= kGraphMaxTokens &&
+                       !d.prof_on && t_cancel_after < 0;
+    if (!graph) {
+      if ((rc = forward())) return rc;
+    } else {
+      const std::vector<long long> key = {
+          mb.t1 - mb.t0, mb.s1 - mb.s0, out_dim, mb.ntiles, mb.nwin, mb.nseg,
+          (long long)mb.cu_off, (long long)mb.tile_off, (long long)mb.cls_off,
+          (long long)mb.win_off, (long long)mb.seg_off, (long long)mb.poff_off,
+          (long long)mb.pcls_off, (long long)mb.ptot, (long long)mb.ptot_cls, head_group,
+          (long long)max_p, (long long)max_t, (long long)(intptr_t)d_ids,
+          (long long)(intptr_t)d_out, (long long)(intptr_t)d.d_meta,
+          (long long)(intptr_t)d.d_pscr, (long long)(intptr_t)d.ws.base,
+          (long long)d.ws.tokens, (long long)(intptr_t)st};
+      auto it = d.graphs.find(key);
+      if (it == d.graphs.end()) {
+        // Capture this call's launches (they run when the graph is launched
+        // below); any capture failure falls back to direct launches.
+        const long long l0 = d.launches.load();
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed) != cudaSuccess) {
+          (void)cudaGetLastError();
+          if ((rc = forward())) return rc;
+        } else {
+          rc = forward();
+          const cudaError_t ce = cudaStreamEndCapture(st, &g);
+          cudaGraphExec_t ex = nullptr;
+          const bool ok = ce == cudaSuccess && g && cudaGraphInstantiate(&ex, g, 0) == cudaSuccess;
+          if (g) cudaGraphDestroy(g);
+          if (rc) {
+            if (ex) cudaGraphExecDestroy(ex);
+            return rc;
+          }
+          if (!ok) {
+            (void)cudaGetLastError();
+            if ((rc = forward())) return rc;
+          } else {
+            if (d.graphs.size() >= kGraphCacheSize) {  // drop the least recently used
+              auto lru = d.graphs.begin();
+              for (auto j = d.graphs.begin(); j != d.graphs.end(); ++j)
+                if (j->second.used < lru->second.used) lru = j;
+              cudaGraphExecDestroy(lru->second.exec);
+              d.graphs.erase(lru);
+            }
+            DevCtx::GraphEntry e;
+            e.exec = ex;
+            e.launches = d.launches.load() - l0;
+            it = d.graphs.emplace(key, e).first;
+            it->second.used = ++d.graph_clock;
+            CU_TRY(cudaGraphLaunch(ex, st));
+          }
+        }
+      } else {
+        it->second.used = ++d.graph_clock;
+        CU_TRY(cudaGraphLaunch(it->second.exec, st));
+        d.launches.fetch_add(it->second.launches, std::memory_order_relaxed);
+      }
+    }
     if (after_mb && (rc = after_mb((int)i, mb.s0, mb.s1))) return rc;
   }
   return FUTON_OK;
@@ -1580,7 +1663,7 @@ int encode_host(futon_model* m, DevCtx& d, const int32_t* ids, const int32_t* cu
     return FUTON_OK;
   };
   rc = run_call(*m, d, d.d_ids, cu, nseq, out_dim, d.d_out, d.stream, cancel, err, errlen, after_mb,
-                before_mb);
+                before_mb, /*allow_graph=*/true);
   if (rc) {
     cudaStreamSynchronize(d.stream);  // leave nothing in flight
     return rc;

@@ -391,6 +391,34 @@ def test_encode_device_matches_host(gpu):
     assert m.launch_count() > 0
 
 
+def test_graph_replay_takes_each_calls_batch(gpu):
+    """Small host-buffer calls run from a CUDA graph captured by the first call
+    with the same launches and replayed after this call's ids and tile lists
+    are uploaded: a repeated batch, the same sequences in another order (same
+    shape: same token count, sequence count and tiles) and other token ids
+    with the same lengths each give their own vectors, bit for bit the ones
+    of the device-resident entry point (which launches directly)."""
+    import torch
+    from futon_b200 import pack_ids
+    cfg, w, m = synth_model("bge")
+    ids, cu = synth.make_inputs("c0", nseq=32, seed=21)
+    a = m.encode_packed(ids, cu)
+    assert np.array_equal(m.encode_packed(ids, cu), a)
+    perm = np.arange(len(cu) - 1)[::-1]
+    ids_b, cu_b = pack_ids([ids[cu[i]:cu[i + 1]] for i in perm])
+    assert np.array_equal(m.encode_packed(ids_b, cu_b), a[perm])
+    ids_c = np.random.default_rng(3).integers(1000, cfg.vocab_size, ids.size).astype(np.int32)
+    c = m.encode_packed(ids_c, cu)
+    d_ids = torch.from_numpy(ids_c).cuda()
+    d_out = torch.empty((len(cu) - 1, cfg.hidden_size), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    m.encode_device(d_ids.data_ptr(), cu, 0, d_out.data_ptr(), stream=s.cuda_stream)
+    m.sync(stream=s.cuda_stream)
+    assert np.array_equal(d_out.cpu().numpy(), c)
+    assert not np.array_equal(c, a)
+
+
 def test_io_bytes_counts_the_copies(gpu):
     """futon_cuda_io_bytes: a host-buffer call copies at least the ids in and
     exactly the vectors plus the 4-byte device error word out."""
