@@ -102,7 +102,11 @@ void futon_cuda_model_destroy(futon_model* model);
  * Rejects like EncodeTokens (model.go:348-365): an empty sequence, a length
  * above the effective max, an id outside [0, vocab), out_dim outside
  * [0, hidden], truncation without matryoshka support. *cancel (may be NULL)
- * is polled between micro-batches and layers; non-zero → FUTON_ECANCELED. */
+ * is polled between micro-batches and layers; non-zero → FUTON_ECANCELED.
+ * A call of one micro-batch of at most 32,768 tokens replays a CUDA graph of
+ * an earlier call with the same launches (captured on the library's own
+ * stream the first time); it polls *cancel at entry and before its
+ * micro-batch only. */
 int futon_cuda_encode(futon_model* model, int device, const int32_t* ids,
                       const int32_t* cu_seqlens, int nseq, int out_dim, float* out,
                       volatile const int* cancel, char* err, size_t errlen);
