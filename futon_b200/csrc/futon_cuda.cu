@@ -1907,13 +1907,17 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
     const int ms = model->eff_max, hh = hd / 2;
     rc_tab.resize((size_t)ms * hh);
     rs_tab.resize((size_t)ms * hh);
+    // cos and sin in loops of their own: one loop with both lets the
+    // compiler fuse them into a sincos call, whose last bit may differ from
+    // the separate calls the reference (and the test oracle) make.
+    auto angle = [&](int t, int i) {
+      const double freq = 1.0 / std::pow(c.rope_theta, (double)(2 * i) / (double)hd);
+      return (double)t * freq;
+    };
     for (int t = 0; t < ms; ++t)
-      for (int i = 0; i < hh; ++i) {
-        const double freq = 1.0 / std::pow(c.rope_theta, (double)(2 * i) / (double)hd);
-        const double ang = (double)t * freq;
-        rc_tab[(size_t)t * hh + i] = (float)std::cos(ang);
-        rs_tab[(size_t)t * hh + i] = (float)std::sin(ang);
-      }
+      for (int i = 0; i < hh; ++i) rc_tab[(size_t)t * hh + i] = (float)std::cos(angle(t, i));
+    for (int t = 0; t < ms; ++t)
+      for (int i = 0; i < hh; ++i) rs_tab[(size_t)t * hh + i] = (float)std::sin(angle(t, i));
   }
 
   // One weight replica per device, uploaded by one host thread per device
