@@ -272,6 +272,8 @@ struct DevCtx {
   size_t h_ids_cap = 0;
   float* h_out = nullptr; // pinned
   size_t h_out_cap = 0;
+  int* h_err = nullptr;   // pinned: the device error word, read back after a call
+  size_t h_err_cap = 0;
   cudaEvent_t meta_evt = nullptr;
   // Recorded on a call's stream after its last launch; the next call's stream
   // waits on it first. Calls may use different streams (encode_device takes
@@ -316,6 +318,7 @@ struct DevCtx {
     if (h_meta) cudaFreeHost(h_meta);
     if (h_ids) cudaFreeHost(h_ids);
     if (h_out) cudaFreeHost(h_out);
+    if (h_err) cudaFreeHost(h_err);
     if (meta_evt) cudaEventDestroy(meta_evt);
     if (done_evt) cudaEventDestroy(done_evt);
     for (cudaEvent_t e : ev_all) cudaEventDestroy(e);
@@ -1596,9 +1599,16 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
   return FUTON_OK;
 }
 
-int read_device_error(DevCtx& d, char* err, size_t errlen) {
+// The device error word of the calls so far: read here (a blocking copy), or
+// taken from *copied, an asynchronous copy of it the caller queued after its
+// kernels and has synchronised.
+int read_device_error(DevCtx& d, char* err, size_t errlen, const int* copied = nullptr) {
   int code = 0;
-  CU_TRY(cudaMemcpy(&code, d.err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (copied) {
+    code = *copied;
+  } else {
+    CU_TRY(cudaMemcpy(&code, d.err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  }
   d.d2h_bytes.fetch_add((long long)sizeof(int), std::memory_order_relaxed);
   if (code != 0) {
     // Cleared on the device's stream (ordered with the next call's kernels).
@@ -1668,13 +1678,16 @@ int encode_host(futon_model* m, DevCtx& d, const int32_t* ids, const int32_t* cu
     cudaStreamSynchronize(d.stream);  // leave nothing in flight
     return rc;
   }
+  // The error word comes back behind the last vectors (no second round trip).
+  if ((rc = ensure_host(&d.h_err, &d.h_err_cap, 1, err, errlen))) return rc;
+  CU_TRY(cudaMemcpyAsync(d.h_err, d.err_word, sizeof(int), cudaMemcpyDeviceToHost, d.stream));
   for (size_t i = 0; i < done.size(); ++i) {
     CU_TRY(cudaEventSynchronize(d.out_evts[i]));
     const size_t off = (size_t)done[i].s0 * dim, n = (size_t)(done[i].s1 - done[i].s0) * dim;
     memcpy(out + off, d.h_out + off, n * sizeof(float));
   }
   CU_TRY(cudaStreamSynchronize(d.stream));
-  return read_device_error(d, err, errlen);
+  return read_device_error(d, err, errlen, d.h_err);
 }
 
 // ---- kernel-seam context (per CUDA device) ------------------------------
