@@ -604,6 +604,8 @@ __global__ void __launch_bounds__(128, attn_heads_min_ctas<HD, NH>())
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_wait();  // qkv and out only after the previous kernel has completed
+  pdl_trigger();
 
   // Next (head group, key tile) to load (thread 0 only).
   int ng = g_begin, nj = 0, issued = 0;
@@ -717,6 +719,8 @@ __global__ void __launch_bounds__(256)
                      const int* __restrict__ cu_seqlens, int nseq, int nq, int cls_mode,
                      const float* __restrict__ rcos, const float* __restrict__ rsin, int rope,
                      float scale_log2, OutT* __restrict__ out, int ldo) {
+  pdl_wait();
+  pdl_trigger();
   const int gw = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   const int qi = gw / num_heads, head = gw % num_heads;

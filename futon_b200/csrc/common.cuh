@@ -175,6 +175,21 @@ __device__ __forceinline__ void cluster_sync_all() {
 }
 
 // ----------------------------------------------------------------------------
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the kernel before it in the stream is still
+// running; pdl_wait returns once that kernel has completed and its memory
+// operations are visible, so every kernel of the forward calls it before it
+// reads or writes global memory that another kernel of the call touches
+// (only set-up — shared memory, TMEM, barriers, weights, the call's
+// metadata — comes before it), then pdl_trigger lets the next kernel start.
+// Both do nothing for a kernel launched without the attribute.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ----------------------------------------------------------------------------
 // TMA (tiled, no multicast)
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

@@ -246,6 +246,9 @@ struct Workspace {
 
 struct DevCtx {
   int device = 0;
+  // Set while a small float-path call's forward is captured into a graph:
+  // its launches carry programmatic stream serialization (launch_k).
+  bool pdl = false;
   std::vector<int> plan_slots;  // upload_mb_meta's counting-sort slots
   int num_sms = 148;
   bool gemm_pair = false;  // the model's gemm_pair option, read by upload_gemm
@@ -818,6 +821,7 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
   g.out_f32 = o.out_f32;
   g.f16 = !s8;
   g.pair = w.pair;
+  g.pdl = d.pdl;
   g.ep.out = o.out;
   g.ep.ldo = o.ldo;
   g.ep.bias = w.bias;
@@ -845,6 +849,30 @@ int run_gemm(DevCtx& d, int stage, const void* A, bool s8, const float* a_scale,
     return set_err(err, errlen, FUTON_ECUDA, "native: gemm launch: %s", cudaGetErrorString(e));
   d.launches.fetch_add(1, std::memory_order_relaxed);
   return FUTON_OK;
+}
+
+// Kernel launch on st; with pdl the kernel may start while the kernel before
+// it in the stream finishes (programmatic dependent launch: the kernels of
+// the forward wait for their predecessor with pdl_wait before they touch
+// global memory).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t st, Args&&... args) {
+  if (!pdl) {
+    kern<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 inline int grid_rows(int rows, int per_block, int sms) {
@@ -968,9 +996,8 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
       auto launch = [&](auto kern, int smem) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        kern<<<dim3(grid, ways), 128, smem, st>>>(tm, h, H, cu, tiles, cls_only ? 1 : 0,
-                                                  scale_log2, out, h, d.err_word);
-        return cudaGetLastError();
+        return launch_k(d.pdl, kern, dim3(grid, ways), dim3(128), (size_t)smem, st, tm, h, H, cu,
+                        tiles, cls_only ? 1 : 0, scale_log2, out, h, d.err_word);
       };
       if (ways > 1)
         CU_TRY(hd == 64   ? launch(attn_heads_kernel<64, 1, OutT, true>, attn_heads_smem_bytes<64, 1>())
@@ -1030,9 +1057,9 @@ int run_attention(const futon_model& m, DevCtx& d, int T, int nseq, const int* c
   const int blocks = (int)((warps * 32 + 255) / 256);
   if (blocks == 0) return FUTON_OK;
 #define FUTON_ROWQ(HD_)                                                                   \
-  attn_rowq_kernel<HD_, InT, OutT><<<blocks, 256, 0, st>>>(qkv, h, H, cu, nseq, nq,         \
-                                                          cls_only ? 1 : 0, nullptr, nullptr, \
-                                                          0, scale_log2, out, h)
+  launch_k(d.pdl, attn_rowq_kernel<HD_, InT, OutT>, dim3(blocks), dim3(256), 0, st, qkv, h, H, \
+           cu, nseq, nq, cls_only ? 1 : 0, (const float*)nullptr, (const float*)nullptr, 0,  \
+           scale_log2, out, h)
   switch (hd) {
     case 8: FUTON_ROWQ(8); break;
     case 16: FUTON_ROWQ(16); break;
@@ -1068,9 +1095,9 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
           ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0, d.pos, d.embw, d.embb,
           eps, w.x, w.xb, w.xq, w.xs);
     else
-      embed_ln_kernel<<<grid_rows(T, 8, d.num_sms), 256, 0, st>>>(
-          ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0, d.pos, d.embw, d.embb,
-          eps, w.x, w.xb, w.xq, w.xs);
+      CU_TRY(launch_k(d.pdl, embed_ln_kernel<false>, dim3(grid_rows(T, 8, d.num_sms)), dim3(256),
+                      0, st, ids, cu, nseq, T, h, c.vocab_size, d.err_word, d.word, d.type0,
+                      d.pos, d.embw, d.embb, eps, w.x, w.xb, w.xq, w.xs));
     CU_TRY(cudaGetLastError());
     d.launches.fetch_add(1, std::memory_order_relaxed);
   }
@@ -1127,7 +1154,8 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
       ProfScope prof(d, st, kStGather, 0.0, (double)nseq * 2.0 * h * esz);
       const int blocks = grid_rows((int)((size_t)nseq * h * esz / 16), 256, d.num_sms);
       if (q8) gather_rows_kernel<float><<<blocks, 256, 0, st>>>(w.x, cu, nseq, h, (float*)w.xc);
-      else gather_rows_kernel<f16><<<blocks, 256, 0, st>>>(w.xb, cu, nseq, h, (f16*)w.xc);
+      else CU_TRY(launch_k(d.pdl, gather_rows_kernel<f16>, dim3(blocks), dim3(256), 0, st,
+                           (const f16*)w.xb, cu, nseq, h, (f16*)w.xc));
       CU_TRY(cudaGetLastError());
       d.launches.fetch_add(1, std::memory_order_relaxed);
       resid = w.xc;
@@ -1166,8 +1194,9 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
         layernorm_kernel<true><<<grid_rows(rows, 256, d.num_sms), 256, 0, st>>>(
             w.tmp, rows, h, lnw, lnb, eps, xo, nullptr, w.xq, w.xs);
       else
-        layernorm_kernel<<<grid_rows(rows, 8, d.num_sms), 256, 0, st>>>(
-            w.tmp, rows, h, lnw, lnb, eps, xo, q8 ? nullptr : w.xb, w.xq, w.xs);
+        CU_TRY(launch_k(d.pdl, layernorm_kernel<false>, dim3(grid_rows(rows, 8, d.num_sms)),
+                        dim3(256), 0, st, (const float*)w.tmp, rows, h, lnw, lnb, eps, xo,
+                        q8 ? nullptr : w.xb, w.xq, w.xs));
       CU_TRY(cudaGetLastError());
       d.launches.fetch_add(1, std::memory_order_relaxed);
       return FUTON_OK;
@@ -1221,8 +1250,9 @@ int forward_mb(const futon_model& m, DevCtx& d, const int* ids, const int* cu, i
     const double rows_read = cls ? (double)nseq : (double)T;
     ProfScope prof(d, st, kStPool, 0.0, rows_read * h * 4.0 + (double)nseq * dim * 4.0);
     const int mat_ln = c.matryoshka_layernorm ? 1 : 0;
-    pool_kernel<<<nseq, 256, h * sizeof(float), st>>>(q8 ? w.x : w.xf, cu, h, cls ? 0 : 1, out_dim,
-                                                      mat_ln, c.normalize ? 1 : 0, out);
+    CU_TRY(launch_k(d.pdl, pool_kernel, dim3(nseq), dim3(256), h * sizeof(float), st,
+                    (const float*)(q8 ? w.x : w.xf), cu, h, cls ? 0 : 1, out_dim, mat_ln,
+                    c.normalize ? 1 : 0, out));
     CU_TRY(cudaGetLastError());
     d.launches.fetch_add(1, std::memory_order_relaxed);
   }
@@ -1560,7 +1590,12 @@ int run_call(const futon_model& m, DevCtx& d, const int* d_ids, const int32_t* c
           (void)cudaGetLastError();
           if ((rc = forward())) return rc;
         } else {
+          // The float path's kernels (and the default attention) wait for
+          // their predecessor before touching global memory, so inside its
+          // graph each may start while the previous one finishes.
+          d.pdl = !m.q8 && m.attn_kind == kAttnHeads;
           rc = forward();
+          d.pdl = false;
           const cudaError_t ce = cudaStreamEndCapture(st, &g);
           cudaGraphExec_t ex = nullptr;
           const bool ok = ce == cudaSuccess && g && cudaGraphInstantiate(&ex, g, 0) == cudaSuccess;
@@ -1768,6 +1803,7 @@ int seam_gemm(int* err_word, int num_sms, const void* A, bool s8, const float* a
   g.out_f32 = true;
   g.f16 = false;
   g.pair = false;
+  g.pdl = false;
   g.ep.out = dst;
   g.ep.ldo = n;
   g.ep.bias = bias;

@@ -18,6 +18,7 @@ struct GemmLaunch {
   bool out_f32;           // output element type: f32 (true) or 16-bit (bf16, or f16 with f16)
   bool f16;               // 16-bit operands, outputs and residuals are f16 (else bf16)
   bool pair;              // f16 only: CTA-pair tiles (M = 256, cta_group::2); tw's box is bn / 2 rows
+  bool pdl;               // programmatic dependent launch (the kernel waits with griddepcontrol.wait)
   EpiParams ep;
   int* err;               // device error word
   int num_sms;
@@ -57,23 +58,31 @@ cudaError_t launch_gemm_inst_p(const GemmLaunch& g) {
   const int peers = kLn ? g.N / BN : 1;
   const int csize = peers * (PAIR ? 2 : 1);  // CTAs per cluster
   const long tiles = kLn ? num_m : num_m * ((g.N + BN - 1) / BN);
-  if (csize == 1) {
-    const int grid = (int)(tiles < g.num_sms ? tiles : g.num_sms);
-    kern<<<grid, C::kThreads, C::kSmemBytes, g.stream>>>(*g.ta, *g.tw, g.to ? *g.to : *g.ta,
-                                                         *g.ta, g.M, g.N, g.K, g.ep, g.err);
-    return cudaGetLastError();
-  }
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)csize;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (csize > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)csize;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (g.pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.blockDim = dim3(C::kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = g.stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.attrs = na ? attr : nullptr;
+  cfg.numAttrs = (unsigned)na;
+  if (csize == 1) {
+    cfg.gridDim = dim3((unsigned)(tiles < g.num_sms ? tiles : g.num_sms));
+    return cudaLaunchKernelEx(&cfg, kern, *g.ta, *g.tw, g.to ? *g.to : *g.ta, *g.ta, g.M, g.N, g.K,
+                              g.ep, g.err);
+  }
   // Clusters that fit at once (per device and cluster size, queried once).
   static std::atomic<int> fit_cache[64][2 * kLnPeerSlots + 1];
   int fit = fit_cache[dev & 63][csize].load();

@@ -228,6 +228,8 @@ __global__ void __launch_bounds__(256)
                     const float* __restrict__ b, float eps, float* __restrict__ x,
                     __half* __restrict__ xb, int8_t* __restrict__ xq,
                     float* __restrict__ xs) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int n4 = h >> 2;
@@ -294,6 +296,8 @@ __global__ void __launch_bounds__(256)
                      const float* __restrict__ b, float eps, float* __restrict__ x,
                      __half* __restrict__ xb, int8_t* __restrict__ xq,
                      float* __restrict__ xs) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int n4 = h >> 2;
@@ -342,6 +346,8 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     quant_rows_kernel(const float* __restrict__ in, int rows, int k, int8_t* __restrict__ q,
                       float* __restrict__ scale) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int n4 = k >> 2;
@@ -377,6 +383,8 @@ __global__ void __launch_bounds__(256)
 template <typename T>
 __global__ void gather_rows_kernel(const T* __restrict__ x, const int* __restrict__ cu, int nseq,
                                    int h, T* __restrict__ xc) {
+  pdl_wait();
+  pdl_trigger();
   const int nv = h * (int)sizeof(T) / 16;
   const size_t total = (size_t)nseq * nv;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
@@ -407,6 +415,8 @@ __global__ void __launch_bounds__(256)
                 int out_dim, int mat_ln, int normalize, float* __restrict__ out) {
   extern __shared__ float pooled[];  // [h]
   __shared__ double red[32];
+  pdl_wait();
+  pdl_trigger();
   const int s = blockIdx.x;
   if (mean_pool) {
     const int s0 = cu[s], L = cu[s + 1] - s0;
