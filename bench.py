@@ -31,6 +31,12 @@ path — NCCL carries only barriers and the max-over-ranks of the timings.
   cold_start  wall time of model creation (futon_cuda_model_create) from F16
          weights, the shipped pack format, on this rank's GPU (median of
          three creations)
+  text_path  the Provider's text side on the c4 lengths as text (synthetic
+         words from the bert-base-uncased vocab, each text tokenising to its
+         c4 length): native tokenizer throughput on all host threads and on
+         one, and text → vectors end to end (embed_texts: tokenisation
+         pipelined with the GPU forward, host wall clock per batch), with the
+         tokenizer's CPU restatement on a bounded sample as its baseline
   c1, c3, c3_q8  the other benchmark configurations per GPU, ids in HBM:
          MiniLM-6 on 256 × 128 tokens; the arctic-shaped long-context encoder
          on 16 × 2048 tokens with f16 tensor-core GEMMs, and with the int8
@@ -60,6 +66,7 @@ METRIC = "embeddings/sec (bge-small-shaped encoder, c4 log-normal batch)"
 UNIT = "embeddings/s"
 WORKLOAD = "c4"
 CPU_SAMPLE_SEQS = 512
+VOCAB_PATH = ROOT / "tests" / "golden" / "tokenizer" / "vocab_bert_uncased.txt"
 
 
 def env_int(name, default):
@@ -156,6 +163,60 @@ def cpu_baseline(steps: int = 1, warmup: int = 0, seqs: int = CPU_SAMPLE_SEQS):
                    f"C restatement of the reference forward ({'AVX2' if has_avx2() else 'scalar'} "
                    f"GEMM), {threads} threads"),
         "ms_per_sample": dt * 1e3, "tokens_per_sec": int(cu[-1]) / dt,
+    }
+
+
+def text_path(model, synth, nseq=None, steps: int = 3, warmup: int = 1) -> dict:
+    """Tokenizer throughput and text → vectors on the c4 lengths (rank 0, N = 1)."""
+    from futon_b200.provider import embed_texts
+    from futon_b200.tokenizer import Tokenizer, TokenizerConfig, pack_texts
+    vocab = VOCAB_PATH.read_bytes()
+    texts, lens = synth.make_texts(WORKLOAD, vocab.decode().split("\n"), seed=1, nseq=nseq)
+    tok = Tokenizer(vocab, TokenizerConfig(**synth.TOKENIZER))
+    max_len = model.effective_max_seq_len()
+    data, offsets = pack_texts(texts)
+    ntexts, ntok = len(texts), int(lens.sum())
+
+    def timed(fn, reps, warm):
+        for _ in range(warm):
+            fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            r = fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts), r
+
+    threads = os.cpu_count() or 1
+    t_all, (ids, cu) = timed(lambda: tok.encode_packed_bytes(data, offsets, max_len), steps,
+                             warmup)
+    assert np.array_equal(np.diff(cu), lens), "synthetic texts did not tokenise to their lengths"
+    n1 = min(ntexts, 8192)
+    t_one, _ = timed(lambda: tok.encode_packed_bytes(data, offsets[:n1 + 1], max_len, 1), 1, 1)
+    t_e2e, out = timed(lambda: embed_texts(model, tok, texts), steps, warmup)
+    norms = np.linalg.norm(out, axis=1)
+    assert float(np.abs(norms - 1).max()) < 1e-4, "text path outputs are not unit-norm"
+
+    from oracle.tokenizer import Tokenizer as OracleTokenizer, TokenizerConfig as OracleCfg
+    ot = OracleTokenizer(vocab, OracleCfg(**synth.TOKENIZER))
+    ns = min(ntexts, 256)
+    t0 = time.perf_counter()
+    for t in texts[:ns]:
+        ot.encode(t, max_len)
+    t_or = time.perf_counter() - t0
+    return {
+        "config": f"{ntexts} synthetic texts, {ntok} tokens, {len(data)} bytes "
+                  "(c4 lengths, bert-base-uncased vocab words)",
+        "tokenizer": {"texts_per_sec": round(ntexts / t_all, 1),
+                      "tokens_per_sec": round(ntok / t_all, 1),
+                      "mb_per_sec": round(len(data) / t_all / 1e6, 1), "ms": round(t_all * 1e3, 2),
+                      "threads": threads,
+                      "single_thread_texts_per_sec": round(n1 / t_one, 1)},
+        "e2e": {"value": round(ntexts / t_e2e, 1), "unit": UNIT, "ms": round(t_e2e * 1e3, 2),
+                "path": "embed_texts: pack texts, tokenise (pipelined), host-buffer forward"},
+        "cpu_baseline": {"value": round(ns / t_or, 1), "unit": "texts/s", "cores": 1,
+                         "kind": "port", "sample": f"first {ns} texts through the tokenizer's "
+                         "CPU restatement (pure Python)"},
     }
 
 
@@ -479,6 +540,10 @@ def main():
             except Exception as e:  # noqa: BLE001 - reported in the JSON line
                 cold[arch] = {"error": repr(e)[:300]}
 
+    text = None
+    if rank == 0 and world == 1 and not args.no_extra:
+        text = text_path(model, synth, nseq=args.nseq)
+
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline()
@@ -517,6 +582,7 @@ def main():
             "nomic": nomic,
             **extra,
             "cold_start": cold,
+            "text_path": text,
             "p50_batch_latency": latency,
             "clocks": clk,
             "cpu_baseline": cb,

@@ -1,4 +1,5 @@
-"""ctypes binding of libfuton_cuda.so (the C ABI in include/futon_cuda.h).
+"""ctypes binding of libfuton_cuda.so (the C ABI in include/futon_cuda.h and
+include/futon_tokenizer.h).
 
 The library lives next to this file. There is no fallback: if it is missing
 or fails to load, every entry point raises FutonLibraryError.
@@ -27,6 +28,8 @@ EXPORTED = (
     "futon_cuda_profile_read", "futon_cuda_profile_stage_count", "futon_cuda_profile_stage_name",
     "futon_cuda_matmul_t_q8_noalloc", "futon_cuda_selftest_wait_timeout", "futon_cuda_io_bytes",
     "futon_cuda_debug_cancel_after",
+    "futon_tokenizer_create", "futon_tokenizer_destroy", "futon_tokenizer_vocab_size",
+    "futon_tokenizer_pad_id", "futon_tokenizer_encode", "futon_tokenizer_encode_batch",
 )
 
 # Environment options the library reads when a model is created, with the
@@ -64,6 +67,15 @@ class FutonCfg(C.Structure):
         ("position_encoding", C.c_int32), ("rope_theta", C.c_double),
         ("activation", C.c_int32), ("pooling", C.c_int32), ("normalize", C.c_int32),
         ("matryoshka", C.c_int32), ("matryoshka_layernorm", C.c_int32),
+    ]
+
+
+class FutonTokenizerCfg(C.Structure):
+    _fields_ = [
+        ("do_lower_case", C.c_int32), ("tokenize_chinese_chars", C.c_int32),
+        ("max_input_chars_per_word", C.c_int32), ("cls_token", C.c_char_p),
+        ("sep_token", C.c_char_p), ("unk_token", C.c_char_p), ("pad_token", C.c_char_p),
+        ("mask_token", C.c_char_p),
     ]
 
 
@@ -135,6 +147,20 @@ def lib() -> C.CDLL:
         L.futon_cuda_selftest_wait_timeout.argtypes = [ip, cp, sz]
         L.futon_cuda_debug_cancel_after.restype = None
         L.futon_cuda_debug_cancel_after.argtypes = [C.c_longlong]
+        L.futon_tokenizer_create.restype = ip
+        L.futon_tokenizer_create.argtypes = [vp, sz, C.POINTER(FutonTokenizerCfg), C.POINTER(vp),
+                                             cp, sz]
+        L.futon_tokenizer_destroy.restype = None
+        L.futon_tokenizer_destroy.argtypes = [vp]
+        L.futon_tokenizer_vocab_size.restype = ip
+        L.futon_tokenizer_vocab_size.argtypes = [vp]
+        L.futon_tokenizer_pad_id.restype = ip
+        L.futon_tokenizer_pad_id.argtypes = [vp]
+        L.futon_tokenizer_encode.restype = ip
+        L.futon_tokenizer_encode.argtypes = [vp, vp, sz, ip, vp, ip, C.POINTER(C.c_int), cp, sz]
+        L.futon_tokenizer_encode_batch.restype = ip
+        L.futon_tokenizer_encode_batch.argtypes = [vp, vp, vp, ip, ip, ip, vp, C.c_int64, vp, cp,
+                                                   sz]
         _lib = L
         return L
 

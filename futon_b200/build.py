@@ -2,7 +2,9 @@
 
 Each translation unit under csrc/ compiles in parallel; the objects link into
 futon_b200/libfuton_cuda.so with the CUDA runtime linked statically, so the
-library only needs the NVIDIA driver at run time. Usage:
+library only needs the NVIDIA driver at run time. The tokenizer's Unicode
+tables (unicode_tables.h) are generated into the build folder first by
+csrc/gen_unicode_tables.py. Usage:
     python -m futon_b200.build [--force] [--verbose]
 """
 from __future__ import annotations
@@ -20,7 +22,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libfuton_cuda.so"
-SOURCES = ["futon_cuda.cu", "gemm_f16.cu", "gemm_bf16.cu", "gemm_s8.cu"]
+SOURCES = ["futon_cuda.cu", "gemm_f16.cu", "gemm_bf16.cu", "gemm_s8.cu", "tokenizer.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -32,7 +34,8 @@ def nvcc() -> str:
 
 
 def _deps() -> list[Path]:
-    return sorted(CSRC.glob("*.cu*")) + sorted((ROOT / "include").glob("*.h"))
+    return (sorted(CSRC.glob("*.cu*")) + sorted(CSRC.glob("*.cpp")) + sorted(CSRC.glob("*.py"))
+            + sorted((ROOT / "include").glob("*.h")))
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:
@@ -47,10 +50,14 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not _stale(LIB, deps):
         return LIB
     BUILD.mkdir(exist_ok=True)
+    r = subprocess.run([sys.executable, str(CSRC / "gen_unicode_tables.py"),
+                        str(BUILD / "unicode_tables.h")], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"gen_unicode_tables.py failed:\n{r.stdout}\n{r.stderr}")
     cc = nvcc()
     common = ARCH + [
         "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
-        "-I", str(ROOT / "include"), "-I", str(CSRC),
+        "-I", str(ROOT / "include"), "-I", str(CSRC), "-I", str(BUILD),
     ]
     if verbose:
         common += ["-Xptxas", "-v"]

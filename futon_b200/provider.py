@@ -7,12 +7,13 @@ Same names, argument meaning and error behaviour as the Go surface
                                   uploaded once per device (one replica each)
   Model.encode_tokens(ids, dim)   EncodeTokens for one sequence
   Model.encode_packed(ids, cu)    many sequences in one call (packed, no padding)
-  Provider(Options(...))          New: pack load + Dimensions validation
-  Provider.embed_ids / embed_batch_ids / dimensions / model_name /
-  is_available / close
+  Provider(Options(...))          New: pack load, tokenizer from vocab.txt,
+                                  Dimensions validation
+  Provider.embed / embed_batch    Embed / EmbedBatch: text → native tokenizer
+                                  (tokenizer.py) → forward (embed_texts)
+  Provider.embed_ids / embed_batch_ids   the same for pre-tokenised input
+  Provider.dimensions / model_name / is_available / close
 
-Text tokenisation stays with the caller (the reference keeps its WordPiece
-tokenizer in Go on the host); these entry points take token ids.
 Errors carry the reference's "native:" messages; a raised cancel flag
 surfaces as CanceledError. There is no CPU path: every forward runs the
 CUDA kernels in libfuton_cuda.so.
@@ -23,6 +24,8 @@ import contextlib
 import ctypes as C
 import dataclasses
 import threading
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
 from typing import Dict, List, Optional, Sequence
 
 import numpy as np
@@ -30,6 +33,7 @@ import numpy as np
 from . import _lib
 from ._lib import FutonError
 from .pack import (ACT_SWIGLU, POOL_MEAN, POS_ROPE, PackConfig, PackError, load_pack)
+from .tokenizer import Text, Tokenizer, TokenizerConfig
 
 NATIVE_MODEL_NAME_PREFIX = "native/"
 ENV_NATIVE_Q8 = "FUTON_NATIVE_Q8"
@@ -72,6 +76,64 @@ def _cfg_struct(cfg: PackConfig) -> _lib.FutonCfg:
     c.matryoshka = 1 if cfg.matryoshka is not None else 0
     c.matryoshka_layernorm = 1 if (cfg.matryoshka is not None and cfg.matryoshka.layernorm) else 0
     return c
+
+
+# Text bytes of the first chunk of a pipelined embed_batch (~1M tokens of
+# English text: two full micro-batches of the forward).
+FIRST_CHUNK_BYTES = 8 << 20
+
+
+def text_chunks(texts: Sequence[Text], first_bytes: int = FIRST_CHUNK_BYTES) -> List[tuple]:
+    """[lo, hi) text ranges of a pipelined embed_batch: the first holds about
+    first_bytes of text, each next one about twice the previous, the last
+    takes the rest (a batch under 2 × first_bytes stays whole)."""
+    sizes = np.fromiter((len(t) for t in texts), dtype=np.int64, count=len(texts))
+    csum = np.cumsum(sizes)
+    total = int(csum[-1]) if len(texts) else 0
+    chunks, lo, want, done = [], 0, first_bytes, 0
+    while lo < len(texts):
+        if total - done < 2 * want:
+            chunks.append((lo, len(texts)))
+            break
+        hi = int(np.searchsorted(csum, done + want, side="left")) + 1
+        hi = min(max(hi, lo + 1), len(texts))
+        chunks.append((lo, hi))
+        done = int(csum[hi - 1])
+        lo, want = hi, 2 * want
+    return chunks
+
+
+def embed_texts(model: "Model", tokenizer: Tokenizer, texts: Sequence[Text], out_dim: int = 0,
+                threads: int = 0, cancel: Optional[CancelFlag] = None) -> np.ndarray:
+    """Texts → [n, out_dim or hidden] vectors over every device of `model`.
+    Texts are tokenised on `threads` host threads (0 = all), truncated to
+    the model's EffectiveMaxSeqLen, and encoded by packed forwards sharded
+    across the GPUs. A large batch goes in chunks that double in size
+    (text_chunks): while the GPUs encode chunk k, a host thread tokenises
+    chunk k+1 (the library call releases the GIL), so only the first
+    chunk's tokenisation is exposed. Results do not depend on the chunking."""
+    n = len(texts)
+    out = np.empty((n, model.out_width(out_dim)), dtype=np.float32)
+    if n == 0:
+        return out
+    max_len = model.effective_max_seq_len()
+    chunks = text_chunks(texts, FIRST_CHUNK_BYTES)
+
+    def tokenize(k):
+        lo, hi = chunks[k]
+        return tokenizer.encode_batch(texts[lo:hi], max_len, threads)
+
+    if len(chunks) == 1:
+        ids, cu = tokenize(0)
+        return model.encode_batch(ids, cu, out_dim, cancel=cancel, out=out)
+    with ThreadPoolExecutor(max_workers=1) as ex:
+        nxt = ex.submit(tokenize, 0)
+        for k, (lo, hi) in enumerate(chunks):
+            ids, cu = nxt.result()
+            if k + 1 < len(chunks):
+                nxt = ex.submit(tokenize, k + 1)
+            model.encode_batch(ids, cu, out_dim, cancel=cancel, out=out[lo:hi])
+    return out
 
 
 def pack_ids(seqs: Sequence[Sequence[int]]) -> tuple:
@@ -208,12 +270,20 @@ class Model:
         return out
 
     def encode_batch(self, ids: np.ndarray, cu_seqlens: np.ndarray, out_dim: int = 0,
-                     cancel: Optional[CancelFlag] = None) -> np.ndarray:
-        """Data-parallel over every device of the model (EmbedBatch's engine)."""
+                     cancel: Optional[CancelFlag] = None,
+                     out: Optional[np.ndarray] = None) -> np.ndarray:
+        """Data-parallel over every device of the model (EmbedBatch's engine),
+        written to `out` when given (as in encode_packed)."""
         ids = np.ascontiguousarray(ids, dtype=np.int32)
         cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
         nseq = len(cu) - 1
-        out = np.empty((max(nseq, 0), self.out_width(out_dim)), dtype=np.float32)
+        shape = (max(nseq, 0), self.out_width(out_dim))
+        if out is None:
+            out = np.empty(shape, dtype=np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise FutonError(_lib.FUTON_EINVAL,
+                             f"native: out must be C-contiguous float32 {shape}, got "
+                             f"{out.dtype} {out.shape}")
         with self._call() as h:
             _lib.call("futon_cuda_encode_batch", h, ids.ctypes.data, cu.ctypes.data, nseq,
                       out_dim, out.ctypes.data, cancel.ptr if cancel else None)
@@ -282,6 +352,7 @@ class Options:
     dimensions: int = 0
     devices: Optional[List[int]] = None  # None = every visible GPU
     q8: Optional[bool] = None            # None = FUTON_NATIVE_Q8 == "1"
+    threads: int = 0                     # host threads for tokenising a batch; 0 = all
 
 
 class Provider:
@@ -293,6 +364,18 @@ class Provider:
                              "native: PackDir is required (no downloading in this phase)")
         self.model = Model.load(opts.pack_dir, devices=opts.devices, q8=opts.q8)
         cfg = self.model.cfg
+        try:
+            self.tokenizer = Tokenizer.from_file(Path(opts.pack_dir) / "vocab.txt",
+                                                 TokenizerConfig.from_dict(cfg.tokenizer))
+        except FutonError:
+            self.model.close()
+            raise
+        if self.tokenizer.vocab_size() > cfg.vocab_size:
+            self.model.close()
+            raise FutonError(_lib.FUTON_EINVAL,
+                             f"native: vocab.txt has {self.tokenizer.vocab_size()} entries but "
+                             f"pack declares vocab_size {cfg.vocab_size}")
+        self._threads = opts.threads
         dims = opts.dimensions or cfg.hidden_size
         if dims != cfg.hidden_size:
             if cfg.matryoshka is None:
@@ -311,6 +394,20 @@ class Provider:
         with self._mu:
             if self._closed:
                 raise FutonError(_lib.FUTON_EINVAL, "native: provider is closed")
+
+    def embed(self, text: Text, cancel: Optional[CancelFlag] = None) -> np.ndarray:
+        """Embed (provider.go:111-121): tokenise with the pack's vocab,
+        truncated to EffectiveMaxSeqLen, then one forward."""
+        self._check_open()
+        ids = self.tokenizer.encode(text, self.model.effective_max_seq_len())
+        return self.model.encode_tokens(ids, self._dims, cancel=cancel)
+
+    def embed_batch(self, texts: Sequence[Text],
+                    cancel: Optional[CancelFlag] = None) -> np.ndarray:
+        """EmbedBatch (provider.go:152-202): index-aligned [n, dims] vectors,
+        bit-identical to embed per text (embed_texts)."""
+        self._check_open()
+        return embed_texts(self.model, self.tokenizer, texts, self._dims, self._threads, cancel)
 
     def embed_ids(self, ids: Sequence[int], cancel: Optional[CancelFlag] = None) -> np.ndarray:
         """Embed for pre-tokenised input (provider.go:115-121)."""
@@ -348,6 +445,7 @@ class Provider:
                 return
             self._closed = True
         self.model.close()
+        self.tokenizer.close()
 
 
 def new(opts: Options) -> Provider:

@@ -13,6 +13,10 @@ so a sequence's length includes both special tokens.
       matryoshka 768/256/64
   c3  arctic-embed-m-long shape, 16 × 2048, CLS pooling, fp32 and Q8
   c4  bge-small shape, 65,536 sequences, L = clip(round(exp(ln 64 + 0.8 N)), 8, 512)
+
+Text inputs (make_texts) stand in for a corpus where the tokenizer is part of
+the path: each text is L-3 words drawn from the vocab's whole-word entries
+plus a full stop, first word capitalised, so it tokenises to exactly L ids.
 """
 from __future__ import annotations
 
@@ -120,6 +124,27 @@ def make_inputs(key: str, seed: int = 1, nseq: Optional[int] = None,
     ids[cu[:-1]] = CLS_ID
     ids[cu[1:] - 1] = SEP_ID
     return ids, cu
+
+
+def make_texts(key: str, vocab_lines: List[str], seed: int = 1,
+               nseq: Optional[int] = None) -> Tuple[List[str], np.ndarray]:
+    """Synthetic texts with a configuration's lengths (in tokens, [CLS] and
+    [SEP] included) over a WordPiece vocab; returns (texts, lengths)."""
+    bc = CONFIGS[key]
+    n = bc.nseq if nseq is None else nseq
+    rng = np.random.default_rng(seed)
+    lens = np.maximum(sample_lengths(bc.lengths, n, rng), 3)
+    words = [w for w in vocab_lines if w.isascii() and w.isalpha() and w.islower()]
+    if not words:
+        raise ValueError("vocab has no whole-word entries")
+    picks = rng.integers(0, len(words), size=int((lens - 3).sum()))
+    texts, k = [], 0
+    for L in lens:
+        m = int(L) - 3
+        body = " ".join(words[i] for i in picks[k:k + m])
+        k += m
+        texts.append(body[:1].upper() + body[1:] + ".")
+    return texts, lens
 
 
 def synthetic_vocab(cfg: PackConfig) -> List[str]:

@@ -19,7 +19,9 @@ def declared(header) -> set:
 
 
 def test_header_symbols_exported():
-    names = declared(ROOT / "include" / "futon_cuda.h")
+    headers = sorted((ROOT / "include").glob("*.h"))
+    assert [h.name for h in headers] == ["futon_cuda.h", "futon_tokenizer.h"]
+    names = set().union(*(declared(h) for h in headers))
     assert names == set(_lib.EXPORTED), names ^ set(_lib.EXPORTED)
     lib = C.CDLL(str(_lib.LIB_PATH))
     for n in names:
