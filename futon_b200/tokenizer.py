@@ -121,12 +121,21 @@ class Tokenizer:
     def encode(self, text: Text, max_seq_len: int) -> List[int]:
         """Encode (tokenizer.go:143-184)."""
         b = _as_bytes(text)
-        cap = max(2, max_seq_len)
-        out = (C.c_int32 * cap)()
+        # As in encode_packed_bytes: ids ≤ bytes + 2 in practice, and a short
+        # buffer comes back with the exact count, then the call is repeated.
+        cap = min(max(2, max_seq_len), len(b) + 2)
         n = C.c_int(0)
-        _lib.call("futon_tokenizer_encode", self._h, b, len(b), int(max_seq_len), out, cap,
-                  C.byref(n))
-        return list(out[:n.value])
+        for _ in range(2):
+            out = (C.c_int32 * cap)()
+            try:
+                _lib.call("futon_tokenizer_encode", self._h, b, len(b), int(max_seq_len), out,
+                          cap, C.byref(n))
+                return list(out[:n.value])
+            except FutonError:
+                if n.value <= cap:
+                    raise
+                cap = n.value
+        raise FutonError(_lib.FUTON_EINVAL, "tokenizer: id count changed between calls")
 
     def encode_packed_bytes(self, data: bytes, offsets: np.ndarray, max_seq_len: int,
                             threads: int = 0) -> Tuple[np.ndarray, np.ndarray]:

@@ -294,3 +294,41 @@ def test_toy_pack_text_ids(toy_expected):
     tok = Tokenizer.from_file(pack / "vocab.txt", TokenizerConfig.from_dict(cfg.tokenizer))
     for c in toy_expected["packs"]["toy-absolute-gelu"]["text_cases"]:
         assert tok.encode(c["text"], cfg.effective_max_seq_len()) == c["ids"], c["text"]
+
+
+# ---- property-based: arbitrary text and bytes (FuzzTokenizerEncode's input) --
+
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+# Every Unicode category, weighted towards what the pipeline treats specially:
+# ASCII, Latin with accents, combining marks, CJK, whitespace and controls.
+_ALPHABET = st.one_of(
+    st.characters(min_codepoint=0, max_codepoint=0x7F),
+    st.characters(min_codepoint=0xC0, max_codepoint=0x24F),
+    st.characters(min_codepoint=0x300, max_codepoint=0x36F),
+    st.sampled_from(list("\u3000\u00a0\u2028\u2003\u0085\u200b\ufffd\u0130\u212a\u03a3"
+                         "\u81ea\u7136\uac00\ud55c\U0001D165\U0001D16D\u0f73\u0344")),
+    st.characters(blacklist_categories=("Cs",)),
+)
+_TEXT = st.one_of(
+    st.text(_ALPHABET, max_size=120),
+    st.binary(max_size=120),
+    st.lists(st.sampled_from(["[CLS]", "[SEP]", "[PAD]", "hello", "World", " ", "\u0301",
+                              "##", "[", "]", "\xe9t\xe9"]), max_size=20).map("".join),
+)
+
+
+@settings(max_examples=600, deadline=None, derandomize=True)
+@given(text=_TEXT, max_len=st.integers(min_value=-3, max_value=600))
+def test_native_matches_oracle_property(native, oracle, text, max_len):
+    got = native.encode(text, max_len)
+    assert got == oracle.encode(text, max_len)
+    assert 2 <= len(got) <= max(2, max_len)
+    assert got[0] == 101 and got[-1] == 102
+
+
+def test_huge_max_len_allocates_by_text(native):
+    """encode sizes its buffer by the text, not by max_seq_len."""
+    assert native.encode("hello world", 2**31 - 1) == [101, 7592, 2088, 102]
+    ids, cu = native.encode_batch(["hello world", ""], 2**31 - 1)
+    assert ids.tolist() == [101, 7592, 2088, 102, 101, 102] and cu.tolist() == [0, 4, 6]
