@@ -2,14 +2,18 @@
 // (native/tokenizer.go), producing the packed ids + cu_seqlens that the
 // encoder entry points take.
 //
-// Per text, one pass over decoded code points does what the reference does
-// in several string passes (tokenizer.go:218-266): drop NUL, U+FFFD and
-// category-C runes except TAB/LF/CR, turn whitespace (those three, space,
-// Zs) into a space, isolate CJK ideographs, lowercase (simple mapping).
-// With lowercasing on, NFD + removal of Mn follows on the code-point buffer,
+// Per text segment, one pass over the bytes does what the reference does in
+// several string passes (tokenizer.go:218-266). ASCII bytes (most of any
+// text) go through a 128-entry class table: no decoding, no Unicode tables.
+// Each run of other bytes is decoded and cleaned on its own — NUL, U+FFFD
+// and category-C runes but TAB/LF/CR dropped, whitespace (those three,
+// space, Zs) turned into a space, CJK ideographs isolated, lowercased (simple
+// mapping) — and, with lowercasing on, put through NFD + removal of Mn,
 // skipped when no code point is at or above U+00C0 (none below decomposes or
-// is a combining mark). Words are then split on Go's unicode.IsSpace and on
-// punctuation, and each word goes through greedy longest-match WordPiece
+// is a combining mark). The ASCII characters between runs are starters
+// without decompositions, so NFD never reaches across them. Words are split
+// on Go's unicode.IsSpace and on punctuation, and each word goes through
+// greedy longest-match WordPiece
 // (tokenizer.go:268-302) against two open-addressing tables: word-initial
 // keys, and "##" continuation keys stored without the prefix, so no lookup
 // builds a string. Candidate pieces longer than the table's longest key are
@@ -236,26 +240,37 @@ class VocabTable {
     return memcmp(arena_.data() + off, p, n) == 0;
   }
 
-  static uint64_t mix(uint64_t x) {
-    x ^= x >> 30;
-    x *= 0xBF58476D1CE4E5B9ull;
-    x ^= x >> 27;
-    x *= 0x94D049BB133111EBull;
-    return x ^ (x >> 31);
+  // The last n < 8 bytes as one word, from fixed-size loads (a variable-size
+  // copy would be a library call per lookup). For a given n the value
+  // determines the bytes: two overlapping 4-byte loads cover n = 4..7, and
+  // bytes 0, n/2 and n-1 cover n = 1..3.
+  static uint64_t tail(const char* p, size_t n) {
+    if (n >= 4) {
+      uint32_t a, b;
+      memcpy(&a, p, 4);
+      memcpy(&b, p + n - 4, 4);
+      return (uint64_t)a | ((uint64_t)b << 32);
+    }
+    if (n == 0) return 0;
+    return (uint64_t)(uint8_t)p[0] | ((uint64_t)(uint8_t)p[n >> 1] << 8) |
+           ((uint64_t)(uint8_t)p[n - 1] << 16);
   }
 
+  // One multiply-xorshift per 8 bytes; the final fold brings the high bits
+  // into the low ones that index the slots. Lookups compare whole keys, so
+  // the hash only has to spread them.
   static uint64_t hash(const char* p, size_t n) {
-    uint64_t h = 0x9E3779B97F4A7C15ull * (n + 1);
+    uint64_t h = 0x9E3779B97F4A7C15ull ^ ((uint64_t)n << 56);
     while (n >= 8) {
       uint64_t v;
       memcpy(&v, p, 8);
-      h = mix(h ^ v);
+      h = (h ^ v) * 0xBF58476D1CE4E5B9ull;
+      h ^= h >> 29;
       p += 8;
       n -= 8;
     }
-    uint64_t v = 0;
-    memcpy(&v, p, n);
-    return mix(h ^ v ^ ((uint64_t)n << 59));
+    h = (h ^ tail(p, n)) * 0x94D049BB133111EBull;
+    return h ^ (h >> 32);
   }
 
   std::vector<Slot> slots_;
@@ -282,6 +297,29 @@ struct Special {
   int32_t id;
 };
 
+// What the cleaning step and the split make of an ASCII byte: dropped (NUL
+// and the other C0 controls but TAB/LF/CR, and DEL), a word separator
+// (space, TAB, LF, CR), a punctuation word of its own (the four ASCII
+// symbol/punctuation ranges of isPunct), or a word character. ASCII text
+// has nothing to decompose and no combining marks, so NFD is the identity.
+enum AsciiClass : uint8_t { kDrop, kSep, kPunct, kWordChar };
+
+struct AsciiTable {
+  uint8_t cls[128];
+  char lower[128];  // unicode.ToLower on ASCII
+  constexpr AsciiTable() : cls{}, lower{} {
+    for (int c = 0; c < 128; ++c) {
+      if (c == ' ' || c == '\t' || c == '\n' || c == '\r') cls[c] = kSep;
+      else if (c < 32 || c == 127) cls[c] = kDrop;
+      else if ((c >= 33 && c <= 47) || (c >= 58 && c <= 64) || (c >= 91 && c <= 96) ||
+               (c >= 123 && c <= 126)) cls[c] = kPunct;
+      else cls[c] = kWordChar;
+      lower[c] = (char)((c >= 'A' && c <= 'Z') ? c + 32 : c);
+    }
+  }
+};
+constexpr AsciiTable kAscii;
+
 }  // namespace
 
 struct futon_tokenizer {
@@ -292,7 +330,11 @@ struct futon_tokenizer {
   std::vector<Special> specials;
 
   void nfd_strip(Scratch& sc) const;
-  void word_piece(Scratch& sc) const;
+  void word_piece(const char* w, const uint32_t* b, size_t nr,
+                  std::vector<int32_t>& pieces) const;
+  bool emit_word(const char* w, const uint32_t* b, size_t nr, Scratch& sc,
+                 std::vector<int32_t>& ids, size_t budget) const;
+  bool clean_run(const uint8_t* s, size_t n, Scratch& sc) const;
   bool encode_text(const uint8_t* s, size_t n, Scratch& sc, std::vector<int32_t>& ids,
                    size_t budget) const;
   void encode(const uint8_t* s, size_t n, int max_seq_len, Scratch& sc,
@@ -361,41 +403,58 @@ void futon_tokenizer::nfd_strip(Scratch& sc) const {
   sc.cps.swap(out);
 }
 
-// wordPiece (tokenizer.go:268-302) of sc.word into sc.pieces.
-void futon_tokenizer::word_piece(Scratch& sc) const {
-  sc.pieces.clear();
-  const size_t nr = sc.bounds.size() - 1;
+// wordPiece (tokenizer.go:268-302) of the nr-rune word w into pieces. b holds
+// the byte offset of each rune plus the word's end; b == nullptr means one
+// byte per rune (an ASCII word).
+void futon_tokenizer::word_piece(const char* w, const uint32_t* b, size_t nr,
+                                 std::vector<int32_t>& pieces) const {
+  pieces.clear();
   if (nr > (size_t)max_chars) {
-    sc.pieces.push_back(unk);
+    pieces.push_back(unk);
     return;
   }
-  const char* w = sc.word.data();
-  const uint32_t* b = sc.bounds.data();
+  auto off = [b](size_t i) -> size_t { return b ? b[i] : i; };
   size_t start = 0;
   while (start < nr) {
     const VocabTable& tab = start > 0 ? cont : initial;
     const size_t lim = tab.max_len();
     size_t end = nr;
-    while (end > start && b[end] - b[start] > lim) --end;
+    while (end > start && off(end) - off(start) > lim) --end;
     int32_t id = -1;
     for (; end > start; --end) {
-      id = tab.find(w + b[start], b[end] - b[start]);
+      id = tab.find(w + off(start), off(end) - off(start));
       if (id >= 0) break;
     }
     if (id < 0) {
-      sc.pieces.clear();
-      sc.pieces.push_back(unk);
+      pieces.clear();
+      pieces.push_back(unk);
       return;
     }
-    sc.pieces.push_back(id);
+    pieces.push_back(id);
     start = end;
   }
 }
 
-// basicTokenize + the WordPiece loop of Encode (tokenizer.go:158-178) for one
-// text segment. Returns false once the id budget is spent.
-bool futon_tokenizer::encode_text(const uint8_t* s, size_t n, Scratch& sc,
-                                  std::vector<int32_t>& ids, size_t budget) const {
+// The per-word step of Encode's loop (tokenizer.go:166-176): stop before the
+// word, or before any of its pieces, once the id budget is spent. Returns
+// false then.
+bool futon_tokenizer::emit_word(const char* w, const uint32_t* b, size_t nr, Scratch& sc,
+                                std::vector<int32_t>& ids, size_t budget) const {
+  if (ids.size() - 1 >= budget) return false;
+  word_piece(w, b, nr, sc.pieces);
+  for (int32_t p : sc.pieces) {
+    if (ids.size() - 1 >= budget) return false;
+    ids.push_back(p);
+  }
+  return true;
+}
+
+// Cleaning (tokenizer.go:224-239) and lowercasing of the code points of
+// s[0, n) into sc.cps: NUL, U+FFFD and category-C runes but TAB/LF/CR are
+// dropped, TAB/LF/CR/space/Zs become a space, CJK ideographs are isolated
+// by spaces. Returns whether a code point at or above U+00C0 was kept (none
+// below decomposes or is a combining mark, so NFD can be skipped without).
+bool futon_tokenizer::clean_run(const uint8_t* s, size_t n, Scratch& sc) const {
   std::vector<uint32_t>& cps = sc.cps;
   cps.clear();
   bool wide = false;
@@ -420,38 +479,104 @@ bool futon_tokenizer::encode_text(const uint8_t* s, size_t n, Scratch& sc,
       cps.push_back(v);
     }
   }
-  if (lower && wide) nfd_strip(sc);
+  return wide;
+}
 
+// basicTokenize + the WordPiece loop of Encode (tokenizer.go:158-178) for one
+// text segment, in one pass over its bytes. ASCII bytes go through a
+// 128-entry class table (no decoding, no Unicode tables; words are built
+// in place). A run of other bytes, together with any ASCII controls inside
+// it (the cleaning step removes those before NFD sees the text), is
+// decoded and cleaned by clean_run and, with lowercasing on, put through
+// NFD and Mn removal on its own: every ASCII character that survives
+// cleaning is a starter without a decomposition, so NFD's reordering and
+// its stream-safe count cannot reach across one. Words are then split on
+// Go's unicode.IsSpace and on punctuation. Returns false once the id budget
+// is spent.
+bool futon_tokenizer::encode_text(const uint8_t* s, size_t n, Scratch& sc,
+                                  std::vector<int32_t>& ids, size_t budget) const {
   std::string& word = sc.word;
   std::vector<uint32_t>& bounds = sc.bounds;
+  word.clear();
+  bounds.clear();
+  bool multi = false;  // the word holds a multi-byte rune: bounds are kept
   auto flush = [&]() -> bool {
     if (word.empty()) return true;
-    bounds.push_back((uint32_t)word.size());
-    if (ids.size() - 1 >= budget) return false;
-    word_piece(sc);
-    for (int32_t p : sc.pieces) {
-      if (ids.size() - 1 >= budget) return false;
-      ids.push_back(p);
+    bool ok;
+    if (multi) {
+      bounds.push_back((uint32_t)word.size());
+      ok = emit_word(word.data(), bounds.data(), bounds.size() - 1, sc, ids, budget);
+    } else {
+      ok = emit_word(word.data(), nullptr, word.size(), sc, ids, budget);
     }
     word.clear();
     bounds.clear();
-    return true;
+    multi = false;
+    return ok;
   };
-  word.clear();
-  bounds.clear();
-  for (uint32_t cp : cps) {
-    const uint8_t f = uflags(cp);
-    if (f & F_SPACE) {
-      if (!flush()) return false;
-    } else if (f & F_PUNCT) {
-      if (!flush()) return false;
-      bounds.push_back(0);
-      append_utf8(word, cp);
-      if (!flush()) return false;
-    } else {
-      bounds.push_back((uint32_t)word.size());
-      append_utf8(word, cp);
+  auto append_rune = [&](uint32_t cp) {
+    if (cp < 0x80 && !multi) {
+      word.push_back((char)cp);
+      return;
     }
+    if (!multi) {  // the ASCII prefix so far: one rune per byte
+      bounds.resize(word.size());
+      for (size_t k = 0; k < word.size(); ++k) bounds[k] = (uint32_t)k;
+      multi = true;
+    }
+    bounds.push_back((uint32_t)word.size());
+    append_utf8(word, cp);
+  };
+  for (size_t i = 0; i < n;) {
+    const uint8_t c = s[i];
+    if (c < 0x80) {
+      const uint8_t k = kAscii.cls[c];
+      if (k == kWordChar) {
+        size_t j = i + 1;
+        while (j < n && s[j] < 0x80 && kAscii.cls[s[j]] == kWordChar) ++j;
+        if (!multi) {
+          const size_t old = word.size();
+          word.resize(old + (j - i));
+          char* d = &word[old];
+          if (lower) {
+            for (size_t t = i; t < j; ++t) *d++ = kAscii.lower[s[t]];
+          } else {
+            memcpy(d, s + i, j - i);
+          }
+        } else {
+          for (size_t t = i; t < j; ++t) {
+            bounds.push_back((uint32_t)word.size());
+            word.push_back(lower ? kAscii.lower[s[t]] : (char)s[t]);
+          }
+        }
+        i = j;
+        continue;
+      }
+      ++i;
+      if (k == kDrop) continue;
+      if (!flush()) return false;
+      if (k == kPunct) {
+        word.push_back((char)c);
+        if (!flush()) return false;
+      }
+      continue;
+    }
+    size_t j = i + 1;
+    while (j < n && (s[j] >= 0x80 || kAscii.cls[s[j]] == kDrop)) ++j;
+    if (clean_run(s + i, j - i, sc) && lower) nfd_strip(sc);
+    for (uint32_t cp : sc.cps) {
+      const uint8_t f = uflags(cp);
+      if (f & F_SPACE) {
+        if (!flush()) return false;
+      } else if (f & F_PUNCT) {
+        if (!flush()) return false;
+        append_rune(cp);
+        if (!flush()) return false;
+      } else {
+        append_rune(cp);
+      }
+    }
+    i = j;
   }
   return flush();
 }

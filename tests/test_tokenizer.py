@@ -282,6 +282,12 @@ def test_stream_safe_nfd_order():
     long = "x" + b + "\u0301" * 30 + a   # the 31st starts a new segment
     assert n.encode(short, 16) == o.encode(short, 16) == [2, 5, 6, 7, 3]
     assert n.encode(long, 16) == o.encode(long, 16) == [2, 5, 7, 6, 3]
+    # An ASCII control inside the run is removed before NFD: it neither ends
+    # the run nor resets the count, while a kept ASCII character ends both.
+    ctrl = "x" + b + "\x07" + "\u0301" * 30 + "\x01" + a
+    assert n.encode(ctrl, 16) == o.encode(ctrl, 16) == [2, 5, 7, 6, 3]
+    kept = "x" + b + "\u0301" * 15 + "x" + "\u0301" * 15 + a
+    assert n.encode(kept, 16) == o.encode(kept, 16)
 
 
 def test_toy_pack_text_ids(toy_expected):
