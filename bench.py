@@ -554,7 +554,10 @@ def main():
 
     text = None
     if rank == 0 and world == 1 and not args.no_extra:
-        text = text_path(model, synth, nseq=args.nseq)
+        try:
+            text = text_path(model, synth, nseq=args.nseq)
+        except Exception as e:  # noqa: BLE001 - reported in the JSON line
+            text = {"error": repr(e)[:300]}
 
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
