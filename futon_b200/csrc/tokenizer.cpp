@@ -39,9 +39,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <exception>
 #include <limits>
 #include <string_view>
-#include <system_error>
 #include <new>
 #include <string>
 #include <thread>
@@ -774,10 +774,15 @@ int futon_tokenizer_encode_batch(const futon_tokenizer* tok, const char* text,
         next = nchunks;
       }
     };
+    // The calling thread works too, and the atomic counter hands out every
+    // chunk, so a thread that cannot be started only leaves fewer workers.
     auto run = [&](auto&& body) {
       std::vector<std::thread> pool;
-      pool.reserve(workers - 1);
-      for (int w = 1; w < workers; ++w) pool.emplace_back(body);
+      try {
+        pool.reserve(workers - 1);
+        for (int w = 1; w < workers; ++w) pool.emplace_back(body);
+      } catch (const std::exception&) {
+      }
       body();
       for (auto& th : pool) th.join();
     };
@@ -810,9 +815,6 @@ int futon_tokenizer_encode_batch(const futon_tokenizer* tok, const char* text,
     return FUTON_OK;
   } catch (const std::bad_alloc&) {
     set_err(err, errlen, "tokenizer: out of host memory");
-    return FUTON_ENOMEM;
-  } catch (const std::system_error&) {
-    set_err(err, errlen, "tokenizer: could not start host threads");
     return FUTON_ENOMEM;
   }
 }
