@@ -32,9 +32,11 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <exception>
 #include <map>
 #include <memory>
 #include <mutex>
+#include <new>
 #include <string>
 #include <thread>
 #include <unordered_map>
@@ -65,6 +67,20 @@ int set_err(char* err, size_t errlen, int code, const char* fmt, ...) {
   }
   return code;
 }
+
+// The tail of every C entry point: no C++ exception crosses the ABI (a cgo
+// or ctypes caller cannot take one); host allocation failure is
+// FUTON_ENOMEM, anything else FUTON_ECUDA with its message.
+#define FUTON_CATCH(err, errlen)                                                         \
+  catch (const std::bad_alloc&) {                                                        \
+    return set_err(err, errlen, FUTON_ENOMEM, "native: out of host memory");             \
+  }                                                                                      \
+  catch (const std::exception& ex_) {                                                    \
+    return set_err(err, errlen, FUTON_ECUDA, "native: host exception: %s", ex_.what());  \
+  }                                                                                      \
+  catch (...) {                                                                          \
+    return set_err(err, errlen, FUTON_ECUDA, "native: host exception");                  \
+  }
 
 #define CU_TRY(call)                                                                     \
   do {                                                                                   \
@@ -483,6 +499,23 @@ float f16_to_f32(uint16_t h) {
   float f;
   memcpy(&f, &bits, 4);
   return f;
+}
+
+// Runs fn(0), …, fn(n-1), each on a host thread of its own where one can be
+// started and on the calling thread otherwise, and returns when all have
+// finished. No exception escapes: a thread that cannot be started only
+// serialises its item.
+template <typename Fn>
+void run_on_threads(int n, Fn&& fn) {
+  std::vector<std::thread> th;
+  int started = 0;
+  try {
+    th.reserve(n);
+    for (; started < n; ++started) th.emplace_back(fn, started);
+  } catch (...) {
+  }
+  for (int i = started; i < n; ++i) fn(i);
+  for (auto& t : th) t.join();
 }
 
 // Expands n binary16 values to binary32 (exact): through a 65,536-entry
@@ -1848,7 +1881,7 @@ int futon_cuda_device_count(void) {
   return n;
 }
 
-int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, int ntensors,
+static int futon_cuda_model_create_impl(const futon_cfg* cfg, const futon_tensor* tensors, int ntensors,
                             const int* devices, int ndev, int q8, futon_model** out, char* err,
                             size_t errlen) {
   if (!cfg || !out || (ntensors > 0 && !tensors))
@@ -2028,15 +2061,18 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
   std::vector<std::string> msgs(ndev);
   auto run_one = [&](int di) {
     char e[512] = {0};
-    rcs[di] = upload_device(devices[di], &devs[di], e, sizeof e);
-    msgs[di] = e;
+    try {
+      rcs[di] = upload_device(devices[di], &devs[di], e, sizeof e);
+      msgs[di] = e;
+    } catch (...) {
+      rcs[di] = FUTON_ENOMEM;
+      msgs[di] = "native: host exception while uploading a device replica";
+    }
   };
   if (ndev == 1) {
     run_one(0);
   } else {
-    std::vector<std::thread> th;
-    for (int di = 0; di < ndev; ++di) th.emplace_back(run_one, di);
-    for (auto& t : th) t.join();
+    run_on_threads(ndev, run_one);
   }
   for (int di = 0; di < ndev; ++di)
     if (rcs[di]) return set_err(err, errlen, rcs[di], "%s", msgs[di].c_str());
@@ -2045,12 +2081,21 @@ int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, i
   return FUTON_OK;
 }
 
+int futon_cuda_model_create(const futon_cfg* cfg, const futon_tensor* tensors, int ntensors,
+                            const int* devices, int ndev, int q8, futon_model** out, char* err,
+                            size_t errlen) {
+  try {
+    return futon_cuda_model_create_impl(cfg, tensors, ntensors, devices, ndev, q8, out, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
 void futon_cuda_model_destroy(futon_model* model) {
   if (!model) return;
   delete model;
 }
 
-int futon_cuda_encode(futon_model* model, int device, const int32_t* ids,
+static int futon_cuda_encode_impl(futon_model* model, int device, const int32_t* ids,
                       const int32_t* cu_seqlens, int nseq, int out_dim, float* out,
                       volatile const int* cancel, char* err, size_t errlen) {
   if (!model) return set_err(err, errlen, FUTON_EINVAL, "native: null model");
@@ -2066,7 +2111,16 @@ int futon_cuda_encode(futon_model* model, int device, const int32_t* ids,
                      errlen);
 }
 
-int futon_cuda_encode_batch(futon_model* model, const int32_t* ids, const int32_t* cu_seqlens,
+int futon_cuda_encode(futon_model* model, int device, const int32_t* ids,
+                      const int32_t* cu_seqlens, int nseq, int out_dim, float* out,
+                      volatile const int* cancel, char* err, size_t errlen) {
+  try {
+    return futon_cuda_encode_impl(model, device, ids, cu_seqlens, nseq, out_dim, out, cancel, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
+static int futon_cuda_encode_batch_impl(futon_model* model, const int32_t* ids, const int32_t* cu_seqlens,
                             int nseq, int out_dim, float* out, volatile const int* cancel,
                             char* err, size_t errlen) {
   if (!model) return set_err(err, errlen, FUTON_EINVAL, "native: null model");
@@ -2095,26 +2149,36 @@ int futon_cuda_encode_batch(futon_model* model, const int32_t* ids, const int32_
   }
   std::vector<int> rcs(ndev, FUTON_OK);
   std::vector<std::string> msgs(ndev);
-  std::vector<std::thread> threads;
-  for (int k = 0; k < ndev; ++k) {
-    threads.emplace_back([&, k] {
-      const int s0 = cut[k], s1 = cut[k + 1];
-      if (s1 <= s0) return;
+  run_on_threads(ndev, [&](int k) {
+    const int s0 = cut[k], s1 = cut[k + 1];
+    if (s1 <= s0) return;
+    try {
       std::vector<int32_t> cu(s1 - s0 + 1);
       for (int s = s0; s <= s1; ++s) cu[s - s0] = cu_seqlens[s] - cu_seqlens[s0];
       char e[512] = {0};
       rcs[k] = encode_host(model, *model->devs[k], ids + cu_seqlens[s0], cu.data(), s1 - s0,
                            out_dim, out + (size_t)s0 * dim, cancel, e, sizeof e);
       msgs[k] = e;
-    });
-  }
-  for (auto& t : threads) t.join();
+    } catch (...) {
+      rcs[k] = FUTON_ENOMEM;
+      msgs[k] = "native: host exception in a device's shard";
+    }
+  });
   for (int k = 0; k < ndev; ++k)
     if (rcs[k] != FUTON_OK) return set_err(err, errlen, rcs[k], "%s", msgs[k].c_str());
   return FUTON_OK;
 }
 
-int futon_cuda_encode_device(futon_model* model, int device, const int32_t* d_ids,
+int futon_cuda_encode_batch(futon_model* model, const int32_t* ids, const int32_t* cu_seqlens,
+                            int nseq, int out_dim, float* out, volatile const int* cancel,
+                            char* err, size_t errlen) {
+  try {
+    return futon_cuda_encode_batch_impl(model, ids, cu_seqlens, nseq, out_dim, out, cancel, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
+static int futon_cuda_encode_device_impl(futon_model* model, int device, const int32_t* d_ids,
                              const int32_t* cu_seqlens, int nseq, int out_dim, float* d_out,
                              void* stream, char* err, size_t errlen) {
   if (!model) return set_err(err, errlen, FUTON_EINVAL, "native: null model");
@@ -2132,7 +2196,16 @@ int futon_cuda_encode_device(futon_model* model, int device, const int32_t* d_id
                   errlen);
 }
 
-int futon_cuda_sync(futon_model* model, int device, void* stream, char* err, size_t errlen) {
+int futon_cuda_encode_device(futon_model* model, int device, const int32_t* d_ids,
+                             const int32_t* cu_seqlens, int nseq, int out_dim, float* d_out,
+                             void* stream, char* err, size_t errlen) {
+  try {
+    return futon_cuda_encode_device_impl(model, device, d_ids, cu_seqlens, nseq, out_dim, d_out, stream, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
+static int futon_cuda_sync_impl(futon_model* model, int device, void* stream, char* err, size_t errlen) {
   if (!model) return set_err(err, errlen, FUTON_EINVAL, "native: null model");
   if (device < 0 || device >= (int)model->devs.size())
     return set_err(err, errlen, FUTON_EINVAL, "native: device index %d out of range", device);
@@ -2144,12 +2217,19 @@ int futon_cuda_sync(futon_model* model, int device, void* stream, char* err, siz
   return read_device_error(d, err, errlen);
 }
 
+int futon_cuda_sync(futon_model* model, int device, void* stream, char* err, size_t errlen) {
+  try {
+    return futon_cuda_sync_impl(model, device, stream, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
 long long futon_cuda_launch_count(futon_model* model, int device) {
   if (!model || device < 0 || device >= (int)model->devs.size()) return -1;
   return model->devs[device]->launches.load();
 }
 
-int futon_cuda_io_bytes(futon_model* model, int device, long long* h2d, long long* d2h, char* err,
+static int futon_cuda_io_bytes_impl(futon_model* model, int device, long long* h2d, long long* d2h, char* err,
                         size_t errlen) {
   if (!model || device < 0 || device >= (int)model->devs.size())
     return set_err(err, errlen, FUTON_EINVAL, "native: bad model or device index");
@@ -2158,7 +2238,15 @@ int futon_cuda_io_bytes(futon_model* model, int device, long long* h2d, long lon
   return FUTON_OK;
 }
 
-int futon_cuda_profile(futon_model* model, int device, int enable, char* err, size_t errlen) {
+int futon_cuda_io_bytes(futon_model* model, int device, long long* h2d, long long* d2h, char* err,
+                        size_t errlen) {
+  try {
+    return futon_cuda_io_bytes_impl(model, device, h2d, d2h, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
+static int futon_cuda_profile_impl(futon_model* model, int device, int enable, char* err, size_t errlen) {
   if (!model || device < 0 || device >= (int)model->devs.size())
     return set_err(err, errlen, FUTON_EINVAL, "native: bad model or device index");
   DevCtx& d = *model->devs[device];
@@ -2171,7 +2259,14 @@ int futon_cuda_profile(futon_model* model, int device, int enable, char* err, si
   return FUTON_OK;
 }
 
-int futon_cuda_profile_read(futon_model* model, int device, int stage, double* ms,
+int futon_cuda_profile(futon_model* model, int device, int enable, char* err, size_t errlen) {
+  try {
+    return futon_cuda_profile_impl(model, device, enable, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
+static int futon_cuda_profile_read_impl(futon_model* model, int device, int stage, double* ms,
                             long long* launches, double* flops, double* bytes, char* err,
                             size_t errlen) {
   if (!model || device < 0 || device >= (int)model->devs.size())
@@ -2191,13 +2286,22 @@ int futon_cuda_profile_read(futon_model* model, int device, int stage, double* m
   return FUTON_OK;
 }
 
+int futon_cuda_profile_read(futon_model* model, int device, int stage, double* ms,
+                            long long* launches, double* flops, double* bytes, char* err,
+                            size_t errlen) {
+  try {
+    return futon_cuda_profile_read_impl(model, device, stage, ms, launches, flops, bytes, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
 int futon_cuda_profile_stage_count(void) { return kNumStages; }
 
 const char* futon_cuda_profile_stage_name(int stage) {
   return (stage >= 0 && stage < kNumStages) ? kStageNames[stage] : "";
 }
 
-int futon_cuda_matmul_t(int cuda_device, float* dst, const float* a, const float* b, int m, int n,
+static int futon_cuda_matmul_t_impl(int cuda_device, float* dst, const float* a, const float* b, int m, int n,
                         int k, const float* bias, void* stream, char* err, size_t errlen) {
   if (m < 0 || n <= 0 || k <= 0 || k % 8)
     return set_err(err, errlen, FUTON_EINVAL, "native: matmul shape m=%d n=%d k=%d (k %% 8 == 0)", m, n, k);
@@ -2220,7 +2324,15 @@ int futon_cuda_matmul_t(int cuda_device, float* dst, const float* a, const float
   return seam_finish(*s, st, err, errlen);
 }
 
-int futon_cuda_matmul_t_q8(int cuda_device, float* dst, const float* a, const int8_t* qb,
+int futon_cuda_matmul_t(int cuda_device, float* dst, const float* a, const float* b, int m, int n,
+                        int k, const float* bias, void* stream, char* err, size_t errlen) {
+  try {
+    return futon_cuda_matmul_t_impl(cuda_device, dst, a, b, m, n, k, bias, stream, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
+static int futon_cuda_matmul_t_q8_impl(int cuda_device, float* dst, const float* a, const int8_t* qb,
                            const float* scales, int m, int n, int k, const float* bias,
                            void* stream, char* err, size_t errlen) {
   if (m < 0 || n <= 0 || k <= 0 || k % 16)
@@ -2243,7 +2355,16 @@ int futon_cuda_matmul_t_q8(int cuda_device, float* dst, const float* a, const in
   return seam_finish(*s, st, err, errlen);
 }
 
-int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, const float* src,
+int futon_cuda_matmul_t_q8(int cuda_device, float* dst, const float* a, const int8_t* qb,
+                           const float* scales, int m, int n, int k, const float* bias,
+                           void* stream, char* err, size_t errlen) {
+  try {
+    return futon_cuda_matmul_t_q8_impl(cuda_device, dst, a, qb, scales, m, n, k, bias, stream, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
+}
+
+static int futon_cuda_quantize_rows_q8_impl(int cuda_device, int8_t* dst, float* scales, const float* src,
                                 int rows, int k, void* stream, char* err, size_t errlen) {
   if (rows < 0 || k <= 0 || k % 4)
     return set_err(err, errlen, FUTON_EINVAL, "native: quantize shape rows=%d k=%d (k %% 4 == 0)", rows, k);
@@ -2257,6 +2378,14 @@ int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, con
   quant_rows_kernel<<<grid_rows(rows, 8, s->num_sms), 256, 0, st>>>(src, rows, k, dst, scales);
   CU_TRY(cudaGetLastError());
   return seam_finish(*s, st, err, errlen);
+}
+
+int futon_cuda_quantize_rows_q8(int cuda_device, int8_t* dst, float* scales, const float* src,
+                                int rows, int k, void* stream, char* err, size_t errlen) {
+  try {
+    return futon_cuda_quantize_rows_q8_impl(cuda_device, dst, scales, src, rows, k, stream, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
 }
 
 }  // extern "C"
@@ -2372,7 +2501,7 @@ extern "C" void futon_cuda_debug_cancel_after(long long polls) {
   t_cancel_after = polls < 0 ? -1 : polls;
 }
 
-extern "C" int futon_cuda_selftest_wait_timeout(int cuda_device, char* err, size_t errlen) {
+static int futon_cuda_selftest_wait_timeout_impl(int cuda_device, char* err, size_t errlen) {
   SeamCtx* s = nullptr;
   int rc;
   std::unique_lock<std::mutex> lk;
@@ -2390,4 +2519,11 @@ extern "C" int futon_cuda_selftest_wait_timeout(int cuda_device, char* err, size
                    code);
   return set_err(err, errlen, FUTON_EDEVICE, "native: device wait timed out (self-test, code %d)",
                  code);
+}
+
+extern "C" int futon_cuda_selftest_wait_timeout(int cuda_device, char* err, size_t errlen) {
+  try {
+    return futon_cuda_selftest_wait_timeout_impl(cuda_device, err, errlen);
+  }
+  FUTON_CATCH(err, errlen)
 }

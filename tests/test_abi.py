@@ -112,3 +112,32 @@ def test_runtime_options_match_library():
     for n, values in _lib.RUNTIME_OPTIONS.items():
         for v in values[1:]:
             assert f'"{v}"' in src, f"{n}={v} is listed but not accepted"
+
+
+def test_entry_points_forward_their_arguments():
+    """Every C entry point reaches its body with its own arguments and
+    returns that body's code and message through the exception guard at the
+    ABI (invalid arguments, rejected before any device work, so no GPU is
+    needed)."""
+    E = _lib.FUTON_EINVAL
+    d = C.c_double()
+    ll = C.c_longlong()
+    cases = [
+        ("futon_cuda_encode", (None, 0, None, None, 0, 0, None, None), "null model"),
+        ("futon_cuda_encode_batch", (None, None, None, 0, 0, None, None), "null model"),
+        ("futon_cuda_encode_device", (None, 0, None, None, 0, 0, None, None), "null model"),
+        ("futon_cuda_sync", (None, 0, None), "null model"),
+        ("futon_cuda_io_bytes", (None, 0, C.byref(ll), C.byref(ll)), "bad model or device"),
+        ("futon_cuda_profile", (None, 0, 1), "bad model or device"),
+        ("futon_cuda_profile_read", (None, 0, 0, C.byref(d), C.byref(ll), C.byref(d), C.byref(d)),
+         "bad model or device"),
+        ("futon_cuda_matmul_t", (0, None, None, None, 4, 8, 7, None, None), r"m=4 n=8 k=7"),
+        ("futon_cuda_matmul_t_q8", (0, None, None, None, None, 4, 8, 24, None, None),
+         r"m=4 n=8 k=24"),
+        ("futon_cuda_quantize_rows_q8", (0, None, None, None, 3, 6, None), r"rows=3 k=6"),
+        ("futon_cuda_selftest_wait_timeout", (-1,), "bad device -1"),
+    ]
+    for fn, args, msg in cases:
+        with pytest.raises(FutonError, match=msg) as ei:
+            _lib.call(fn, *args)
+        assert ei.value.code == E, fn
