@@ -73,7 +73,7 @@ int futon_tokenizer_encode(const futon_tokenizer* tok, const char* text, size_t 
  * `text` (offsets non-decreasing, from 0 or more). Writes cu_seqlens[0..
  * ntexts] (cu_seqlens[0] = 0) and the ids of text i into ids[cu_seqlens[i],
  * cu_seqlens[i+1]): the packed layout futon_cuda_encode takes. If the total
- * exceeds ids_cap (ntexts × max_seq_len always suffices) it fails with
+ * exceeds ids_cap (ntexts × max(max_seq_len, 2) always suffices) it fails with
  * FUTON_EINVAL after writing cu_seqlens only, so the caller can size ids
  * from cu_seqlens[ntexts] and call again. Results equal futon_tokenizer_encode
  * per text for every thread count. */

@@ -289,7 +289,7 @@ class Tokenizer:
         """Encode (tokenizer.go:143-184): [CLS] … [SEP], head-truncated so
         that len(ids) <= max(max_seq_len, 2)."""
         if isinstance(text, str):
-            text = text.encode()
+            text = text.encode("utf-8", "surrogatepass")
         if max_seq_len < 2:
             max_seq_len = 2
         ids = [self.cls_id]
