@@ -141,3 +141,33 @@ def test_entry_points_forward_their_arguments():
         with pytest.raises(FutonError, match=msg) as ei:
             _lib.call(fn, *args)
         assert ei.value.code == E, fn
+
+
+def test_headers_build_as_c_and_the_library_runs_from_c(tmp_path):
+    """cgo compiles the headers as C: a pedantic C99 program includes both,
+    links libfuton_cuda and tokenises the reference's fixture texts through
+    the batch entry point (tests/host/abi_consumer.c), giving the fixture ids."""
+    import json
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    exe = tmp_path / "abi_consumer"
+    lib_dir = _lib.LIB_PATH.parent
+    r = subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic",
+                        "-I", str(ROOT / "include"), str(ROOT / "tests" / "host" / "abi_consumer.c"),
+                        "-L", str(lib_dir), "-lfuton_cuda", f"-Wl,-rpath,{lib_dir}", "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    tokdir = ROOT / "tests" / "golden" / "tokenizer"
+    fx = json.loads((tokdir / "tokenizer_fixtures.json").read_text())
+    cases = [c for c in fx["models"]["bge-small-en-v1.5"]["cases"] if "\x00" not in c["text"]]
+    for max_len, key in ((512, "ids"), (16, "ids_max16")):
+        r = subprocess.run([str(exe), str(tokdir / "vocab_bert_uncased.txt"), str(max_len)]
+                           + [c["text"] for c in cases], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+        lines = r.stdout.split("\n")
+        assert lines[0].startswith("devices ") and lines[0].endswith(" vocab 30522 pad 0")
+        got = [[int(v) for v in ln.split()] for ln in lines[1:1 + len(cases)]]
+        assert got == [c[key] for c in cases]
