@@ -106,7 +106,8 @@ class _IdsModel:
         self.calls.append(len(cu) - 1)
         for i in range(len(cu) - 1):
             s = ids[cu[i]:cu[i + 1]].astype(np.float64)
-            out[i] = [len(s), s.sum(), (s * np.arange(1, len(s) + 1)).sum(), s[-2]]
+            out[i] = 0
+            out[i, :4] = [len(s), s.sum(), (s * np.arange(1, len(s) + 1)).sum(), s[-2]]
         return out
 
 
@@ -130,3 +131,80 @@ def test_embed_texts_chunked_equals_whole(monkeypatch):
     seqs = [tok.encode(t, 32) for t in texts]
     assert [int(v) for v in whole[:, 0]] == [len(s) for s in seqs]
     assert P.embed_texts(_IdsModel(), tok, []).shape == (0, 4)
+
+
+# ---- Provider text API over a stand-in model (host logic only) -------------
+
+class _FakePackModel(_IdsModel):
+    """Model.load's stand-in: the pack's config, vectors from _IdsModel."""
+
+    def __init__(self, cfg):
+        super().__init__()
+        self.cfg = cfg
+        self.closed = False
+
+    def effective_max_seq_len(self):
+        return self.cfg.effective_max_seq_len()
+
+    def encode_tokens(self, ids, out_dim=0, device=0, cancel=None):
+        ids = np.asarray(ids, np.int32)
+        out = np.empty((1, self.out_width(out_dim)), np.float32)
+        return self.encode_batch(ids, np.array([0, ids.size], np.int32), out_dim, cancel, out)[0]
+
+    def close(self):
+        self.closed = True
+
+
+def _provider(monkeypatch, pack_dir):
+    from futon_b200 import provider as P
+    from futon_b200.pack import load_pack_config
+    made = []
+
+    def load(d, devices=None, q8=None):
+        made.append(_FakePackModel(load_pack_config(d)))
+        return made[-1]
+
+    monkeypatch.setattr(P.Model, "load", staticmethod(load))
+    return P, made
+
+
+def test_provider_text_api(monkeypatch, toy_expected):
+    """Embed / EmbedBatch tokenise with the pack's own vocab and config (the
+    toy packs' upstream ids) and give the same rows; calls after Close fail."""
+    P, made = _provider(monkeypatch, None)
+    pack = ROOT / "tests" / "golden" / "toy" / "toy-absolute-gelu"
+    prov = P.Provider(P.Options(pack_dir=str(pack)))
+    cases = toy_expected["packs"]["toy-absolute-gelu"]["text_cases"]
+    texts = [c["text"] for c in cases]
+    batch = prov.embed_batch(texts)
+    for i, c in enumerate(cases):
+        assert prov.tokenizer.encode(c["text"], 64) == c["ids"]
+        single = prov.embed(c["text"])
+        assert np.array_equal(single, batch[i])
+        ids = np.asarray(c["ids"], np.float64)
+        assert single[0] == len(ids) and single[1] == ids.sum()
+    assert prov.embed_batch([]).shape == (0, prov.dimensions())
+    prov.close()
+    assert made[0].closed
+    with pytest.raises(FutonError, match="provider is closed"):
+        prov.embed("hello")
+
+
+def test_provider_new_checks_the_vocab(monkeypatch, tmp_path):
+    """New (provider.go:69-104): a vocab.txt larger than the pack's
+    vocab_size, or none at all, fails and releases the loaded model."""
+    from futon_b200.pack import load_pack, write_pack
+    P, made = _provider(monkeypatch, None)
+    src = load_pack(ROOT / "tests" / "golden" / "toy" / "toy-absolute-gelu", keep_f16=False)
+    vocab = [v for v in (ROOT / "tests" / "golden" / "toy" / "toy-absolute-gelu" /
+                         "vocab.txt").read_text().split("\n") if v]
+    big = write_pack(tmp_path / "big", src.cfg, src.tensors,
+                     vocab + [f"extra{i}" for i in range(src.cfg.vocab_size)])
+    with pytest.raises(FutonError, match="vocab.txt has .* entries but pack declares vocab_size"):
+        P.Provider(P.Options(pack_dir=str(big)))
+    assert made[-1].closed
+    ok = write_pack(tmp_path / "ok", src.cfg, src.tensors, vocab)
+    (ok / "vocab.txt").unlink()
+    with pytest.raises(FutonError, match="tokenizer: open vocab"):
+        P.Provider(P.Options(pack_dir=str(ok)))
+    assert made[-1].closed
