@@ -13,6 +13,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 import subprocess
+import sys
 from pathlib import Path
 from typing import Dict, Optional
 
@@ -41,10 +42,14 @@ class FoCfg(C.Structure):
 
 
 def build() -> Path:
-    """Compiles liboracle.so with the committed Makefile when it is stale."""
-    srcs = [HERE / "futon_oracle.c", HERE / "futon_oracle.h", HERE / "Makefile"]
-    if not LIB.exists() or any(s.stat().st_mtime > LIB.stat().st_mtime for s in srcs):
-        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    """Compiles liboracle.so and libtokport.so (the tokenizer port) with the
+    committed Makefile when either is stale."""
+    gen = HERE.parent / "futon_b200" / "csrc" / "gen_unicode_tables.py"
+    deps = {LIB: [HERE / "futon_oracle.c", HERE / "futon_oracle.h", HERE / "Makefile"],
+            HERE / "libtokport.so": [HERE / "tokenizer_port.cpp", HERE / "Makefile", gen]}
+    if any(not out.exists() or any(s.stat().st_mtime > out.stat().st_mtime for s in srcs)
+           for out, srcs in deps.items()):
+        subprocess.run(["make", "-s", "-C", str(HERE), f"PYTHON={sys.executable}"], check=True)
     return LIB
 
 

@@ -27,8 +27,9 @@ class _UnitModel:
 
 def test_text_path_line():
     """The text_path key: tokenizer throughput, text → vectors and the
-    tokenizer's CPU baseline, on synthetic texts that tokenise to exactly
-    their c4 lengths."""
+    tokenizer's CPU baseline (the compiled port, whose ids must equal the
+    library's), on synthetic texts that tokenise to exactly their c4
+    lengths."""
     r = bench.text_path(_UnitModel(), synth, nseq=1500, steps=1, warmup=0)
     assert set(r) == {"config", "tokenizer", "e2e", "cpu_baseline"}
     assert r["config"].startswith("1500 synthetic texts")
@@ -37,7 +38,8 @@ def test_text_path_line():
     assert tk["single_thread_texts_per_sec"] > 0 and tk["threads"] >= 1
     assert r["e2e"]["value"] > 0 and r["e2e"]["unit"] == bench.UNIT
     cb = r["cpu_baseline"]
-    assert cb["kind"] == "port" and cb["cores"] == 1 and cb["value"] > 0
+    assert cb["kind"] == "port" and cb["cores"] == tk["threads"] and cb["value"] > 0
+    assert cb["single_thread_texts_per_sec"] > 0
 
 
 def test_make_texts_tokenise_to_their_lengths():

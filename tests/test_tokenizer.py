@@ -338,3 +338,21 @@ def test_huge_max_len_allocates_by_text(native):
     assert native.encode("hello world", 2**31 - 1) == [101, 7592, 2088, 102]
     ids, cu = native.encode_batch(["hello world", ""], 2**31 - 1)
     assert ids.tolist() == [101, 7592, 2088, 102, 101, 102] and cu.tolist() == [0, 4, 6]
+
+
+# ---- the compiled port timed as the text path's CPU baseline ---------------
+
+def test_compiled_port_gives_the_reference_ids(fixtures, native, random_texts):
+    """oracle/tokenizer_port.cpp (the reference tokenizer's structure,
+    compiled; bench.py's CPU baseline) reproduces the fixtures and equals the
+    library on seeded random text, for one and several threads."""
+    from oracle.tokport import TokenizerPort
+    port = TokenizerPort(VOCAB.read_bytes())
+    for model, name, text, max_len, want in _fixture_cases(fixtures):
+        assert port.encode(text, max_len) == want, (model, name, max_len)
+    data, off = pack_texts(random_texts)
+    for threads in (1, 4):
+        for max_len in (16, 512):
+            ids, cu = port.encode_packed_bytes(data, off, max_len, threads)
+            want_ids, want_cu = native.encode_packed_bytes(data, off, max_len)
+            assert np.array_equal(cu, want_cu) and np.array_equal(ids, want_ids)
