@@ -13,11 +13,11 @@
 // is a combining mark). The ASCII characters between runs are starters
 // without decompositions, so NFD never reaches across them. Words are split
 // on Go's unicode.IsSpace and on punctuation, and each word goes through
-// greedy longest-match WordPiece
-// (tokenizer.go:268-302) against two open-addressing tables: word-initial
-// keys, and "##" continuation keys stored without the prefix, so no lookup
-// builds a string. Candidate pieces longer than the table's longest key are
-// skipped without a lookup (they cannot match).
+// greedy longest-match WordPiece (tokenizer.go:268-302) against two
+// open-addressing tables: word-initial keys, and "##" continuation keys
+// stored without the prefix, so no lookup builds a string. Candidate pieces
+// longer than the table's longest key are skipped without a lookup (they
+// cannot match).
 //
 // Unicode data (categories, lowercase, canonical decompositions, combining
 // classes; Unicode 15.0.0 as in Go 1.23 and golang.org/x/text v0.21.0) comes
