@@ -171,3 +171,23 @@ def test_headers_build_as_c_and_the_library_runs_from_c(tmp_path):
         assert lines[0].startswith("devices ") and lines[0].endswith(" vocab 30522 pad 0")
         got = [[int(v) for v in ln.split()] for ln in lines[1:1 + len(cases)]]
         assert got == [c[key] for c in cases]
+
+
+def test_tokenizer_entry_points_reject_bad_arguments():
+    """The tokenizer's C entry points answer null or negative arguments with
+    FUTON_EINVAL or -1 (as futon_tokenizer.h says), never a crash."""
+    L = _lib.lib()
+    assert L.futon_tokenizer_vocab_size(None) == -1
+    assert L.futon_tokenizer_pad_id(None) == -1
+    L.futon_tokenizer_destroy(None)
+    h = C.c_void_p()
+    with pytest.raises(FutonError, match="null argument"):
+        _lib.call("futon_tokenizer_create", None, 5, None, C.byref(h))
+    with pytest.raises(FutonError, match="null argument"):
+        _lib.call("futon_tokenizer_create", b"[CLS]", 5, None, None)
+    n = C.c_int(0)
+    with pytest.raises(FutonError, match="null or negative"):
+        _lib.call("futon_tokenizer_encode", None, b"x", 1, 8, None, 0, C.byref(n))
+    cu = (C.c_int32 * 2)()
+    with pytest.raises(FutonError, match="null or negative"):
+        _lib.call("futon_tokenizer_encode_batch", None, b"x", None, 1, 8, 1, None, 0, cu)
